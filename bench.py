@@ -1,0 +1,414 @@
+#!/usr/bin/env python3
+"""Commit throughput of the zkIE shard-commit hot path on B200.
+
+Metric: "shard prove s; commit Melem/s (NTT+Merkle) at 1/2/4/8
+B200 vs host CPU".  The value reported is commit throughput in input field
+elements per second (Melem/s) on BASELINE configuration 2 (raw commit sweep),
+case: 256 polynomials of 2^20 coefficients each, blowup 2 -- an LDE of
+2^21 x 256 Goldilocks elements, then the Poseidon2-16 Merkle tree over its
+2^21 rows.  One step = one full commit (LDE NTT + leaf hashing + tree).
+
+  value: inputs resident in HBM, device-side timing (CUDA events on the stream
+         the kernels run on), max over ranks.
+  e2e:   the same commit through the host-buffer C-ABI call zkie2_commit_host
+         (pinned coefficients in, LDE + all digest layers + root out).
+
+N > 1: one process per GPU, each commits its own independent batch (weak
+scaling); no collective touches the data path, only the timing barrier/max.
+
+--impl reference times the reference algorithm on the host cores (the C
+restatement under oracle/, OpenMP over all cores -- the reference itself is
+Rust and cannot be built in this image) on bounded samples of the same
+workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "shard prove s; commit Melem/s (NTT+Merkle) at 1/2/4/8 B200 vs host CPU"
+UNIT = "Melem/s"
+P = 0xFFFFFFFF00000001
+LG_L, W, LG_B = 20, 256, 1
+HBM_FALLBACK_GBS = 6650.0
+
+
+def workload_config(lg_l, w, lg_b, n_gpus):
+    return {
+        "workload": f"cfg2 raw commit: {w} polys x 2^{lg_l} coeffs, blowup {1 << lg_b}, LDE NTT + Poseidon2-16 Merkle over rows",
+        "polys": w, "log_size": lg_l, "blowup": 1 << lg_b,
+        "lde_rows": 1 << (lg_l + lg_b),
+        "bytes_in_per_rank": 8 * w << lg_l,
+        "l2_policy": "inputs (2 GiB) and LDE (4 GiB) per step exceed the 126 MB L2; no flush",
+        "parallelism": f"independent commit per GPU x{n_gpus}",
+    }
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="zkie_b200", choices=["zkie_b200", "reference"])
+    ap.add_argument("--lg-size", type=int, default=LG_L)
+    ap.add_argument("--polys", type=int, default=W)
+    ap.add_argument("--lg-blowup", type=int, default=LG_B)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ---- CPU side (oracle) --------------------------------------------------------------------
+def cpu_commit_rate(lg_rows, w, lg_b, seed=7):
+    """Oracle LDE + Merkle commit of a (2^lg_rows x w) sample; returns (Melem/s, seconds)."""
+    import numpy as np
+    from oracle import oracle as orc
+    consts = orc.p2_constants(1)
+    m = np.random.default_rng(seed).integers(0, P, size=(1 << lg_rows, w), dtype=np.uint64)
+    t0 = time.perf_counter()
+    lde = orc.lde(m, lg_b)
+    orc.merkle_tree(consts, lde)
+    dt = time.perf_counter() - t0
+    return m.size / dt / 1e6, dt
+
+
+def cpu_sample_rows(w, lg_b, target_s):
+    rate, _ = cpu_commit_rate(8, w, lg_b)
+    rows = max(1, int(target_s * rate * 1e6 / w))
+    return min(max(8, rows.bit_length() - 1), 18)
+
+
+def cpu_baseline(w, lg_b, target_s=10.0):
+    lg_rows = cpu_sample_rows(w, lg_b, target_s)
+    rate, dt = cpu_commit_rate(lg_rows, w, lg_b)
+    return {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle/zkie_oracle.c LDE + Merkle of {w} polys x 2^{lg_rows} coeffs (blowup {1 << lg_b}), "
+                      f"OpenMP over {os.cpu_count()} host threads, {dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    lg_rows = cpu_sample_rows(args.polys, args.lg_blowup, target_s=3.0)
+    for _ in range(args.warmup):
+        cpu_commit_rate(max(8, lg_rows - 2), args.polys, args.lg_blowup)
+    times = []
+    for s in range(args.steps):
+        _, dt = cpu_commit_rate(lg_rows, args.polys, args.lg_blowup, seed=100 + s)
+        times.append(dt)
+    elems = args.polys << lg_rows
+    value = elems * len(times) / sum(times) / 1e6
+    cfg = workload_config(args.lg_size, args.polys, args.lg_blowup, args.gpus)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Goldilocks)", "data": "synthetic",
+        "impl": "reference", "config": cfg,
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{args.polys} polys x 2^{lg_rows} coeffs per step (bounded sample of the "
+                                   f"workload), oracle/zkie_oracle.c on all host threads"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- clocks ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus = bus_id.lower()[-12:] if bus_id else ""
+        self.proc = None
+        self.rows = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.th = threading.Thread(target=self._read, daemon=True)
+        self.th.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        mine = [r for r in self.rows if not self.bus or r[0].lower().endswith(self.bus)] or self.rows
+        sm = [float(r[1]) for r in mine if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in mine for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(mine)}
+
+
+# ---- GPU side -------------------------------------------------------------------------------------
+def synth_device(n, seed, device):
+    """Uniform canonical Goldilocks elements generated on the device."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    hi = torch.randint(0, 1 << 32, (n,), generator=g, device=device, dtype=torch.int64)
+    lo = torch.randint(0, 1 << 32, (n,), generator=g, device=device, dtype=torch.int64)
+    x = (hi << 32) | lo                       # bit pattern of a u64
+    big = (x < 0) & (x >= -(1 << 32) + 1)     # u64 >= p  <=>  signed in [p - 2^64, 0)
+    x = torch.where(big, x + ((1 << 32) - 1), x)  # x - p mod 2^64
+    return x.view(torch.uint64)
+
+
+def ntt_passes(lg):
+    return 1 if lg <= 10 else (2 if lg <= 20 else 3)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    try:
+        import zkie_b200 as zk
+    except ImportError:
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_b", os.path.join(ROOT, "zkie_b200", "build.py"))
+        b = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(b)
+        b.build()
+        import zkie_b200 as zk
+    lib, check = zk.lib, zk.check
+
+    lg_l, w, lg_b = args.lg_size, args.polys, args.lg_blowup
+    L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+    lg = lg_l + lg_b
+    n_in = L * w
+    check(lib.zkie2_p2_init_default(), "init constants")
+    d_in = synth_device(n_in, 1234 + rank, dev)
+    d_lde = torch.empty(H * w, dtype=torch.uint64, device=dev)
+    total_dig = lib.zkie2_merkle_total_digests(H)
+    d_layers = torch.empty(total_dig * 8, dtype=torch.uint64, device=dev)
+    d_scr = torch.empty(max(lib.zkie2_commit_scratch_elems(lg_l, lg_b, w), 1), dtype=torch.uint64, device=dev)
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+
+    def step(evs=None):
+        if evs:
+            evs[0].record(stream)
+        check(lib.zkie2_lde(d_in.data_ptr(), d_lde.data_ptr(), d_scr.data_ptr(), lg_l, lg_b, w, sh), "lde")
+        if evs:
+            evs[1].record(stream)
+        check(lib.zkie2_merkle_leaves(d_lde.data_ptr(), H, w, d_layers.data_ptr(), sh), "leaves")
+        if evs:
+            evs[2].record(stream)
+        check(lib.zkie2_merkle_tree_from_leaves(H, d_layers.data_ptr(), sh), "tree")
+        if evs:
+            evs[3].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    bus = getattr(torch.cuda.get_device_properties(dev), "pci_bus_id", None)
+    if bus is None:
+        props = torch.cuda.get_device_properties(dev)
+        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
+                                     getattr(props, "pci_device_id", 0))
+    sampler = ClockSampler(str(bus))
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(evs[s])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    ntt_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    leaf_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    node_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * n_in / (ms_per_step / 1e3) / 1e6
+    root = d_layers[-8:].cpu().numpy()
+
+    # permutation ceiling of the same Poseidon2 code: register-resident states, no HBM traffic
+    n_states, reps = 148 * 16 * 128, 16
+    st = synth_device(n_states * 16, 99, dev)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_states, 1, sh), "permute warmup")
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pe0.record(stream)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_states, reps, sh), "permute")
+    pe1.record(stream)
+    torch.cuda.synchronize()
+    perm_ceiling = n_states * reps / (pe0.elapsed_time(pe1) / 1e3)
+
+    perms_leaf = H * ((w + 7) // 8)
+    leaf_rate = perms_leaf / (leaf_ms / 1e3)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    hbm_peak, hbm_src = HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
+    if os.path.exists(peaks_path):
+        try:
+            hbm_peak = float(json.load(open(peaks_path))["hbm_gbs"])
+            hbm_src = "MEASURED_PEAKS.json hbm_gbs (measured)"
+        except Exception:
+            pass
+    ntt_bytes = 8 * w * (L + H)
+    ntt_gbs = ntt_bytes / (ntt_ms / 1e3) / 1e9
+    del st
+
+    # ---- e2e through the host-buffer C-ABI call ----
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.empty(n_in, dtype=torch.uint64, pin_memory=True)
+        h_in.copy_(d_in)
+        h_lde = torch.empty(H * w, dtype=torch.uint64, pin_memory=True)
+        h_layers = torch.empty(total_dig * 8, dtype=torch.uint64, pin_memory=True)
+        h_root = torch.empty(8, dtype=torch.uint64, pin_memory=True)
+        for _ in range(max(1, args.warmup)):
+            check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
+                                        h_root.data_ptr()), "commit_host")
+        k_e2e = max(1, min(args.steps, 5))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(k_e2e):
+            check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
+                                        h_root.data_ptr()), "commit_host")
+        e2e_s = (time.perf_counter() - t0) / k_e2e
+        if world > 1:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        assert (h_root.numpy() == root).all(), "host-path root differs from the device-path root"
+        e2e = {"value": round(world * n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
+               "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 64 * total_dig,
+               "call": "zkie2_commit_host (pinned input; LDE + every digest layer + root back to pinned host)"}
+        del h_in, h_lde, h_layers
+
+    # ---- MatMul shard prove (inputs resident) ----
+    shard = shard_prove_ms(zk, dev) if rank == 0 else None
+
+    launches_per_step = ntt_passes(lg) + 1 + (lib.zkie2_merkle_num_layers(H) - 1)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Goldilocks mod-p integer)", "data": "synthetic",
+        "config": workload_config(lg_l, w, lg_b, world),
+        "roofline": {
+            "bound": "int", "kernel": "k_leaf_rows (Poseidon2 leaf sponge, 32 permutations per row)",
+            "achieved": round(leaf_rate / 1e9, 4), "peak": round(perm_ceiling / 1e9, 4), "unit": "Gperm/s",
+            "frac": round(leaf_rate / perm_ceiling, 4), "traffic": None,
+            "peak_source": "measured live: the same permutation code with register-resident states and no memory "
+                           "traffic (zkie2_p2_permute), i.e. the integer-pipe ceiling of this implementation",
+            "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
+        },
+        "roofline_ntt": {
+            "bound": "hbm", "kernel": f"k_ntt_pass x{ntt_passes(lg)} (LDE 2^{lg_l} -> 2^{lg})",
+            "achieved": round(ntt_gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(ntt_gbs / hbm_peak, 4),
+            "traffic": None, "algorithmic_bytes": ntt_bytes, "peak_source": hbm_src,
+            "ms_per_step": round(ntt_ms, 4), "share_of_step": round(ntt_ms / ms_per_step, 4),
+        },
+        "nodes_ms_per_step": round(node_ms, 4),
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "root_rank0": [hex(int(x)) for x in root[:2]],
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if shard:
+        line["shard_prove"] = shard
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(w, lg_b)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def shard_prove_ms(zk, dev, iters=5):
+    """A 16x768 and W 768x768 (entries uniform in [-2^15, 2^15),
+    zero-padded to 16x1024 / 1024x1024), forward C = A @ W, WHIR commits of W
+    (n = 20) and of the shard boundary A, C (n = 14), and the MatMul GKR proof
+    with challenges from the shard-DAG child transcript."""
+    import numpy as np
+    import torch
+
+    from zkie_b200.device import to_dev
+    m, k, n = 16, 1024, 1024
+    g = np.random.default_rng(5)
+
+    def fx(shape):
+        # signed fixed-point embedding x < 0 -> p - |x| (common/fixed_point.rs:53-59)
+        x = g.integers(-(1 << 15), 1 << 15, size=shape, dtype=np.int64)
+        return x.astype(np.uint64) + np.where(x < 0, np.uint64(P), np.uint64(0))
+
+    a = np.zeros((m, k), dtype=np.uint64)
+    wt = np.zeros((k, n), dtype=np.uint64)
+    a[:, :768] = fx((m, 768))
+    wt[:768, :768] = fx((768, 768))
+    d_a, d_w = to_dev(a), to_dev(wt)
+    times = []
+    for it in range(iters + 2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        d_c = zk.matmul_field(d_a, d_w, m, k, n)
+        cw = zk.Whir.with_params(20, 90, 17).commit(d_w)
+        ca = zk.Whir.with_params(14, 90, 17).commit(d_a)
+        cc = zk.Whir.with_params(14, 90, 17).commit(d_c)
+        proof = zk.op_matmul_prove(d_a, d_w, d_c, m, k, n, zk.shard_dag_child([[0, 1, 2]], 1, 0))
+        torch.cuda.synchronize()
+        if it >= 2:
+            times.append(time.perf_counter() - t0)
+    return {"config": "cfg1: MatMul 16x1024x1024 (768 real) shard: forward + WHIR commits W(n=20), A, C(n=14) "
+                      "+ 10-round GKR sumcheck", "ms": round(1e3 * statistics.median(times), 3),
+            "claimed": hex(proof.proof.claimed), "root_w": hex(int(cw.root[0]))}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,169 @@
+/*
+ * zkie2.h -- additive entry points of libzkie_b200.so (sm_100a).
+ *
+ * Conventions (same as zkie_goldilocks_cuda.h unless stated): plain pointers
+ * and sizes; d_* are device pointers owned by the caller, h_* host pointers;
+ * every int-returning call returns a cudaError_t (0 = success) and never
+ * falls back to a CPU path; work is enqueued on the explicit stream argument
+ * (NULL = legacy default stream) on the current device.  Scratch buffers are
+ * supplied by the caller, sized by the matching *_scratch_elems() query (in
+ * u64 elements).  Outputs are canonical Goldilocks elements.
+ *
+ * Reference functions replaced are cited as file:line of trustless-ai/zkIE.
+ */
+#ifndef ZKIE2_H
+#define ZKIE2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st *zkie_stream_t; /* ABI-identical to cudaStream_t */
+
+/* ---- Poseidon2 constants ---------------------------------------------------- */
+
+/* Round constants of Perm::new_from_rng_128(SmallRng::seed_from_u64(seed)) as
+ * derived by crates/zkie-core/src/pcs/merkle_cuda.rs:54-85 (host only). */
+int zkie2_p2_default_constants(uint64_t seed, uint64_t *rc_init, uint64_t *rc_final,
+                               uint64_t *rc_internal, uint64_t *diag15);
+/* Upload the seed-1 constants to the current device unless constants were
+ * already uploaded there (by this call or zkie_p2_upload_constants). */
+int zkie2_p2_init_default(void);
+/* reps full permutations of each of n 16-element states, in place. */
+int zkie2_p2_permute(uint64_t *d_states, uint64_t n, uint32_t reps, zkie_stream_t stream);
+
+/* ---- NTT / LDE -------------------------------------------------------------- */
+
+/* Zero-padded LDE of every column: d_in is L x w row-major (L = 2^lg_l),
+ * d_out is (L << lg_blowup) x w, out[i] = sum_j in[j] W^(ij) with W the
+ * generator of order L << lg_blowup (TWO_ADIC_GENERATORS).  Same contract as
+ * the pad + dft_batch of vendor/p3-whir/src/pcs/committer/writer.rs:73-82 and
+ * crates/zkie-core/src/pcs/dft_cuda.rs:161-221. */
+uint64_t zkie2_lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
+int zkie2_lde(const uint64_t *d_in, uint64_t *d_out, uint64_t *d_scratch, uint32_t lg_l,
+              uint32_t lg_blowup, uint64_t w, zkie_stream_t stream);
+/* Host-side builder of the twiddle table zkie_ntt_forward_goldilocks consumes
+ * (the make_twiddles of crates/zkie-core/src/pcs/dft_cuda.rs:44-59): h_out
+ * receives 2^lg - 1 entries, stage s at offset 2^(s-1) - 1. */
+int zkie2_dft_twiddles(uint32_t lg, uint64_t *h_out);
+/* Out-of-place DFT of every column (h = 2^lg_h); scratch as zkie2_lde(lg_h, 0, w). */
+int zkie2_dft(const uint64_t *d_in, uint64_t *d_out, uint64_t *d_scratch, uint32_t lg_h, uint64_t w,
+              zkie_stream_t stream);
+
+/* ---- Merkle ----------------------------------------------------------------- */
+
+/* Layer geometry of one h-row matrix (pcs/merkle_cuda.rs:203-209): layer 0 has
+ * padded_len(h, 2) digests, each next layer padded_len(prev / 2, 2), down to
+ * one root.  Layers are stored back to back, 8 u64 per digest. */
+uint64_t zkie2_merkle_total_digests(uint64_t h);
+uint32_t zkie2_merkle_num_layers(uint64_t h);
+/* Leaf digests of all h rows (PaddingFreeSponge<Perm,16,8,8>). */
+int zkie2_merkle_leaves(const uint64_t *d_mat, uint64_t h, uint64_t w, uint64_t *d_digests,
+                        zkie_stream_t stream);
+/* All layers (CudaMerkleTreeMmcs::commit_gpu, pcs/merkle_cuda.rs:177-312);
+ * the root is the last digest. */
+int zkie2_merkle_tree(const uint64_t *d_mat, uint64_t h, uint64_t w, uint64_t *d_layers,
+                      zkie_stream_t stream);
+/* Layers 1.. of the tree whose h leaf digests are already in d_layers[0 .. 8h)
+ * (the compression loop of pcs/merkle_cuda.rs:250-280). */
+int zkie2_merkle_tree_from_leaves(uint64_t h, uint64_t *d_layers, zkie_stream_t stream);
+
+/* ---- commit (LDE + Merkle) ---------------------------------------------------- */
+
+uint64_t zkie2_commit_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
+/* LDE of d_coeffs into d_lde ((L << lg_blowup) x w), then every Merkle layer
+ * of its rows into d_layers (zkie2_merkle_total_digests(L << lg_blowup) x 8). */
+int zkie2_commit(const uint64_t *d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                 uint64_t *d_lde, uint64_t *d_layers, uint64_t *d_scratch, zkie_stream_t stream);
+/* WHIR base commit of 2^n evaluations (n >= 5): a 2^(n-5) x 32 row-major
+ * matrix at blowup 2 (pcs/whir.rs:296-359,438-469).  d_lde is 2^(n-4) x 32. */
+uint64_t zkie2_whir_scratch_elems(uint32_t n);
+int zkie2_whir_commit(const uint64_t *d_evals, uint32_t n, uint64_t *d_lde, uint64_t *d_layers,
+                      uint64_t *d_scratch, zkie_stream_t stream);
+/* Host-buffer commit (the drop-in path of CudaDft::dft_batch followed by
+ * CudaMerkleTreeMmcs::commit): h_coeffs L x w in, root (8 u64) out, plus the
+ * LDE ((L << lg_blowup) x w) and all digest layers when those pointers are
+ * non-null.  Synchronous.  Allocates its device buffers from the current
+ * device's stream-ordered memory pool. */
+int zkie2_commit_host(const uint64_t *h_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                      uint64_t *h_lde, uint64_t *h_layers, uint64_t *h_root);
+
+/* ---- Fiat-Shamir (host) ---------------------------------------------------------- */
+
+/* Transcript of crates/zkie-core/src/common/transcript.rs:21-80. */
+typedef struct {
+    uint8_t state[32];
+    uint64_t counter;
+} zkie2_transcript;
+
+#define ZKIE2_CHALLENGER_XORSHIFT 0
+#define ZKIE2_CHALLENGER_TRANSCRIPT 1
+/* A ChallengeSource (common/field.rs:58-76): XorShift64 (common/field.rs:17-36)
+ * or Transcript. */
+typedef struct {
+    int32_t kind;
+    uint64_t xorshift_state;
+    zkie2_transcript transcript;
+} zkie2_challenger;
+
+void zkie2_sha256(const uint8_t *data, size_t len, uint8_t *out32);
+void zkie2_transcript_new(zkie2_transcript *t, const uint8_t *domain, size_t len);
+void zkie2_transcript_absorb(zkie2_transcript *t, const uint8_t *data, size_t len);
+void zkie2_transcript_absorb_u64(zkie2_transcript *t, uint64_t x);
+uint64_t zkie2_transcript_field(zkie2_transcript *t);
+uint64_t zkie2_transcript_next_u64(zkie2_transcript *t);
+void zkie2_challenger_xorshift(zkie2_challenger *c, uint64_t seed);
+uint64_t zkie2_challenger_field(zkie2_challenger *c);
+/* Child transcript of shard `shard_index` in prove_shard_dag
+ * (zkie-ops/src/compose.rs:2276-2311) for a statement of MatMul ops given as
+ * (a, b, c) tensor-id triples. */
+void zkie2_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_per_shard,
+                           uint64_t shard_index, zkie2_challenger *child);
+
+/* ---- MLE / sumcheck / matmul GKR ------------------------------------------------- */
+
+/* eq(r, x) for every x < 2^d (common/mle.rs:44-55). */
+int zkie2_eq_evals(const uint64_t *h_r, uint32_t d, uint64_t *d_out, zkie_stream_t stream);
+uint64_t zkie2_mle_scratch_elems(uint32_t t);
+/* partial_eval (common/mle.rs:25-38): fix the first f of t variables. */
+int zkie2_mle_partial_eval(const uint64_t *d_values, uint32_t t, const uint64_t *h_fix, uint32_t f,
+                           uint64_t *d_out, uint64_t *d_scratch, zkie_stream_t stream);
+/* eval (common/mle.rs:8-23); synchronous, result to *h_out. */
+int zkie2_mle_eval(const uint64_t *d_values, uint32_t t, const uint64_t *h_point, uint64_t *h_out,
+                   uint64_t *d_scratch, zkie_stream_t stream);
+/* sumcheck::prove (common/sumcheck.rs:33-79) over f, h of length 2^t with the
+ * t challenges h_ch: h_rounds gets (c0, c1, c2) per round, h_finals (f, h)
+ * after the last fold.  Synchronous. */
+uint64_t zkie2_sumcheck_scratch_elems(uint32_t t);
+int zkie2_sumcheck_prove(const uint64_t *d_f, const uint64_t *d_h, uint32_t t, const uint64_t *h_ch,
+                         uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch,
+                         zkie_stream_t stream);
+/* matmul::prove (common/matmul.rs:17-46): d_at = A^T (k x m), d_b (k x n),
+ * d_c (m x n), powers of two.  Synchronous. */
+uint64_t zkie2_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
+int zkie2_matmul_prove(const uint64_t *d_at, const uint64_t *d_b, const uint64_t *d_c, uint64_t m,
+                       uint64_t k, uint64_t n, const uint64_t *h_u, const uint64_t *h_v,
+                       const uint64_t *h_ch, uint64_t *h_claimed, uint64_t *h_rounds,
+                       uint64_t *h_finals, uint64_t *d_scratch, zkie_stream_t stream);
+/* Op::MatMul arm (zkie-ops/src/compose.rs:1724-1747): draws u, v, ch from src,
+ * proves C = A @ B with d_a (m x k) as stored, returns the draws, the proof and
+ * the claims eval(A, ch||u), eval(B, v||ch), eval(C, v||u).  Synchronous. */
+uint64_t zkie2_op_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
+int zkie2_op_matmul_prove(const uint64_t *d_a, const uint64_t *d_b, const uint64_t *d_c, uint64_t m,
+                          uint64_t k, uint64_t n, zkie2_challenger *src, uint64_t *out_u,
+                          uint64_t *out_v, uint64_t *out_ch, uint64_t *out_claimed,
+                          uint64_t *out_rounds, uint64_t *out_finals, uint64_t *out_claims,
+                          uint64_t *d_scratch, zkie_stream_t stream);
+/* C = A @ B over the field (the forward witness of Op::MatMul,
+ * zkie-ops/src/compose.rs:1327-1331, zkie-ops/src/par.rs:41-89). */
+int zkie2_matmul_field(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
+                       uint64_t *d_c, zkie_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,32 @@
+"""Build recipe for the CPU oracle (test infrastructure, never part of the product).
+
+Compiles oracle/zkie_oracle.c into oracle/liboracle.so with gcc + OpenMP.
+
+The reference itself is not compiled here: its CUDA files include sppark
+headers (``ff/goldilocks.hpp``, ``util/exception.cuh``) that are not in this
+tree, and its host code is Rust with no toolchain present, so there is no
+``oracle/_ref`` build.
+"""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "zkie_oracle.c")
+OUT = os.path.join(HERE, "liboracle.so")
+
+
+def build(force: bool = False) -> str:
+    if (not force and os.path.exists(OUT)
+            and os.path.getmtime(OUT) >= max(os.path.getmtime(SRC),
+                                             os.path.getmtime(os.path.join(HERE, "zkie_oracle.h")))):
+        return OUT
+    cmd = ["gcc", "-O3", "-std=gnu11", "-fPIC", "-shared", "-fopenmp", "-Wall",
+           "-Wno-unknown-pragmas", "-o", OUT + ".tmp", SRC]
+    subprocess.check_call(cmd)
+    os.replace(OUT + ".tmp", OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv))

@@ -1,0 +1,426 @@
+"""ctypes view of the CPU oracle (TEST INFRASTRUCTURE).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import
+this module, and only to check or time against the CUDA product.  Nothing in
+``zkie_b200`` imports it.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import build_oracle
+
+P = 0xFFFFFFFF00000001
+
+_u64 = C.c_uint64
+_u32 = C.c_uint32
+_pu64 = C.POINTER(C.c_uint64)
+_pu32 = C.POINTER(C.c_uint32)
+
+
+class P2Consts(C.Structure):
+    _fields_ = [("ext_init", (_u64 * 16) * 4), ("ext_final", (_u64 * 16) * 4),
+                ("internal", _u64 * 22), ("diag15", _u64)]
+
+    def as_arrays(self):
+        ei = np.array([[self.ext_init[r][i] for i in range(16)] for r in range(4)], dtype=np.uint64)
+        ef = np.array([[self.ext_final[r][i] for i in range(16)] for r in range(4)], dtype=np.uint64)
+        it = np.array([self.internal[i] for i in range(22)], dtype=np.uint64)
+        return ei, ef, it, int(self.diag15)
+
+
+class Transcript(C.Structure):
+    _fields_ = [("state", C.c_uint8 * 32), ("counter", _u64)]
+
+
+class Challenger(C.Structure):
+    _fields_ = [("kind", C.c_int), ("xs_state", _u64), ("tr", Transcript)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = build_oracle.build()
+        L = C.CDLL(path)
+        sig = {
+            "orc_add": (_u64, [_u64, _u64]), "orc_sub": (_u64, [_u64, _u64]),
+            "orc_mul": (_u64, [_u64, _u64]), "orc_pow": (_u64, [_u64, _u64]),
+            "orc_inv": (_u64, [_u64]), "orc_from_i64": (_u64, [C.c_int64]),
+            "orc_two_adic_generator": (_u64, [_u32]),
+            "orc_xorshift_init": (_u64, [_u64]), "orc_xorshift_next": (_u64, [_pu64]),
+            "orc_xorshift_field": (_u64, [_pu64]),
+            "orc_sha256": (None, [C.c_char_p, C.c_size_t, C.c_char_p]),
+            "orc_transcript_new": (None, [C.POINTER(Transcript), C.c_char_p, C.c_size_t]),
+            "orc_transcript_absorb": (None, [C.POINTER(Transcript), C.c_char_p, C.c_size_t]),
+            "orc_transcript_absorb_u64": (None, [C.POINTER(Transcript), _u64]),
+            "orc_transcript_field": (_u64, [C.POINTER(Transcript)]),
+            "orc_transcript_next_u64": (_u64, [C.POINTER(Transcript)]),
+            "orc_dft_batch": (None, [_pu64, _u32, _u64]),
+            "orc_dft_naive": (None, [_pu64, _pu64, _u32, _u64]),
+            "orc_lde": (None, [_pu64, _pu64, _u32, _u32, _u64]),
+            "orc_poly_eval_col": (_u64, [_pu64, _u64, _u64, _u64, _u64]),
+            "orc_p2_derive_constants": (None, [_u64, C.POINTER(P2Consts)]),
+            "orc_p2_permute": (None, [C.POINTER(P2Consts), _pu64]),
+            "orc_p2_hash_row": (None, [C.POINTER(P2Consts), _pu64, _u64, _pu64]),
+            "orc_p2_compress": (None, [C.POINTER(P2Consts), _pu64, _pu64, _pu64]),
+            "orc_padded_len": (_u64, [_u64, _u64]),
+            "orc_merkle_num_layers": (_u32, [_u64]),
+            "orc_merkle_total_digests": (_u64, [_u64]),
+            "orc_merkle_leaves": (None, [C.POINTER(P2Consts), _pu64, _u64, _u64, _pu64, C.c_int]),
+            "orc_merkle_tree": (None, [C.POINTER(P2Consts), _pu64, _u64, _u64, _pu64, _pu64, C.c_int]),
+            "orc_merkle_root_from_leaves": (None, [C.POINTER(P2Consts), _pu64, _u64, _pu64]),
+            "orc_whir_commit": (None, [C.POINTER(P2Consts), _pu64, _u32, _pu64, _pu64, C.c_int]),
+            "orc_mle_eval": (_u64, [_pu64, _u32, _pu64]),
+            "orc_mle_partial_eval": (None, [_pu64, _u32, _pu64, _u32, _pu64]),
+            "orc_eq_evals": (None, [_pu64, _u32, _pu64]),
+            "orc_sumcheck_prove": (None, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64]),
+            "orc_sumcheck_verify": (C.c_int, [_pu64, _u32, _u64, _pu64, _u64, _u64]),
+            "orc_sumcheck3_prove": (None, [_pu64, _pu64, _pu64, _u32, _pu64, _pu64, _pu64]),
+            "orc_sumcheck3_verify": (C.c_int, [_pu64, _u32, _u64, _pu64, _u64, _u64, _u64]),
+            "orc_sum_of_products_prove": (None, [_pu64, _pu64, _u32, _u32, _pu64, _pu64, _pu64]),
+            "orc_virtual_prove": (None, [_pu64, _u32, _u32, _pu64, _pu32, _pu32, _u32, _pu64, _pu64, _pu64]),
+            "orc_virtual_verify": (C.c_int, [_pu64, _u32, _pu64, _pu32, _pu32, _u32, _u64, _pu64, _pu64]),
+            "orc_matmul_prove": (None, [_pu64, _pu64, _pu64, _u64, _u64, _u64, _pu64, _pu64, _pu64,
+                                        _pu64, _pu64, _pu64]),
+            "orc_matmul_field": (None, [_pu64, _pu64, _u64, _u64, _u64, _pu64, C.c_int]),
+            "orc_challenger_field": (_u64, [C.POINTER(Challenger)]),
+            "orc_op_matmul_prove": (None, [_pu64, _pu64, _pu64, _u64, _u64, _u64, C.POINTER(Challenger),
+                                           _pu64, _pu64, _pu64, _pu64, _pu64, _pu64, _pu64]),
+            "orc_shard_dag_child": (None, [_pu64, _u32, _u64, _u64, C.POINTER(Transcript)]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def ptr(a):
+    assert a.flags["C_CONTIGUOUS"]
+    if a.dtype == np.uint32:
+        return a.ctypes.data_as(_pu32)
+    assert a.dtype == np.uint64, a.dtype
+    return a.ctypes.data_as(_pu64)
+
+
+def u64(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint64))
+
+
+# ---- field --------------------------------------------------------------------------
+def add(a, b): return lib().orc_add(a, b)
+def sub(a, b): return lib().orc_sub(a, b)
+def mul(a, b): return lib().orc_mul(a, b)
+def inv(a): return lib().orc_inv(a)
+def from_i64(x): return lib().orc_from_i64(int(x))
+def two_adic_generator(bits): return lib().orc_two_adic_generator(bits)
+
+
+# ---- PRNG / transcript --------------------------------------------------------------
+class XorShift64:
+    """common/field.rs:17-36."""
+
+    def __init__(self, seed):
+        self.s = _u64(lib().orc_xorshift_init(seed))
+
+    def next_u64(self):
+        return lib().orc_xorshift_next(C.byref(self.s))
+
+    def field(self):
+        return lib().orc_xorshift_field(C.byref(self.s))
+
+    def fields(self, n):
+        return np.array([self.field() for _ in range(n)], dtype=np.uint64)
+
+
+def sha256(data: bytes) -> bytes:
+    out = C.create_string_buffer(32)
+    lib().orc_sha256(data, len(data), out)
+    return out.raw
+
+
+class OracleTranscript:
+    """common/transcript.rs:21-80."""
+
+    def __init__(self, domain: bytes = None, raw=None):
+        self.t = Transcript()
+        if raw is not None:
+            C.memmove(C.byref(self.t), C.byref(raw), C.sizeof(Transcript))
+        else:
+            lib().orc_transcript_new(C.byref(self.t), domain, len(domain))
+
+    def absorb(self, data: bytes):
+        lib().orc_transcript_absorb(C.byref(self.t), data, len(data))
+
+    def absorb_u64(self, x):
+        lib().orc_transcript_absorb_u64(C.byref(self.t), x)
+
+    def field(self):
+        return lib().orc_transcript_field(C.byref(self.t))
+
+    def next_u64(self):
+        return lib().orc_transcript_next_u64(C.byref(self.t))
+
+    def state(self):
+        return bytes(self.t.state), int(self.t.counter)
+
+
+# ---- DFT ----------------------------------------------------------------------------
+def dft_batch(mat):
+    m = u64(mat).copy()
+    h = m.shape[0]
+    lg = h.bit_length() - 1
+    assert h == 1 << lg
+    w = m.shape[1] if m.ndim == 2 else 1
+    lib().orc_dft_batch(ptr(m), lg, w)
+    return m
+
+
+def dft_naive(mat):
+    m = u64(mat)
+    h = m.shape[0]
+    lg = h.bit_length() - 1
+    w = m.shape[1] if m.ndim == 2 else 1
+    out = np.zeros_like(m)
+    lib().orc_dft_naive(ptr(m), ptr(out), lg, w)
+    return out
+
+
+def lde_rows(coeffs, rows, H):
+    """Rows i of the H-row LDE of the L x w coefficient matrix, by Horner."""
+    m = u64(coeffs)
+    L, w = m.shape
+    lg = H.bit_length() - 1
+    wH = two_adic_generator(lg)
+    out = np.zeros((len(rows), w), dtype=np.uint64)
+    for a, i in enumerate(rows):
+        x = lib().orc_pow(wH, int(i))
+        for c in range(w):
+            out[a, c] = lib().orc_poly_eval_col(ptr(m), L, w, c, x)
+    return out
+
+
+def lde(mat, lg_blowup):
+    m = u64(mat)
+    L = m.shape[0]
+    w = m.shape[1]
+    out = np.zeros((L << lg_blowup, w), dtype=np.uint64)
+    lib().orc_lde(ptr(m), ptr(out), L.bit_length() - 1, lg_blowup, w)
+    return out
+
+
+# ---- Poseidon2 / Merkle -------------------------------------------------------------
+def p2_constants(seed=1):
+    c = P2Consts()
+    lib().orc_p2_derive_constants(seed, C.byref(c))
+    return c
+
+
+def p2_permute(consts, state):
+    st = u64(state).copy()
+    lib().orc_p2_permute(C.byref(consts), ptr(st))
+    return st
+
+
+def p2_hash_row(consts, row):
+    r = u64(row)
+    out = np.zeros(8, dtype=np.uint64)
+    lib().orc_p2_hash_row(C.byref(consts), ptr(r), r.size, ptr(out))
+    return out
+
+
+def p2_compress(consts, left, right):
+    out = np.zeros(8, dtype=np.uint64)
+    lib().orc_p2_compress(C.byref(consts), ptr(u64(left)), ptr(u64(right)), ptr(out))
+    return out
+
+
+def padded_len(raw, n=2): return lib().orc_padded_len(raw, n)
+
+
+def merkle_leaves(consts, mat, threads=0):
+    m = u64(mat)
+    h, w = m.shape
+    d = np.zeros((h, 8), dtype=np.uint64)
+    lib().orc_merkle_leaves(C.byref(consts), ptr(m), h, w, ptr(d), threads)
+    return d
+
+
+def merkle_tree(consts, mat, threads=0):
+    """Returns (list of layers as (len, 8) arrays, root)."""
+    m = u64(mat)
+    h, w = m.shape
+    tot = lib().orc_merkle_total_digests(h)
+    layers = np.zeros((tot, 8), dtype=np.uint64)
+    root = np.zeros(8, dtype=np.uint64)
+    lib().orc_merkle_tree(C.byref(consts), ptr(m), h, w, ptr(layers), ptr(root), threads)
+    out, off, ln = [], 0, padded_len(h)
+    while True:
+        out.append(layers[off:off + ln])
+        off += ln
+        if ln <= 1:
+            break
+        ln = padded_len(ln // 2)
+    return out, root
+
+
+def merkle_root_from_leaves(consts, leaves):
+    lv = u64(leaves)
+    root = np.zeros(8, dtype=np.uint64)
+    lib().orc_merkle_root_from_leaves(C.byref(consts), ptr(lv), lv.shape[0], ptr(root))
+    return root
+
+
+def whir_commit(consts, evals, threads=0):
+    e = u64(evals)
+    n = e.size.bit_length() - 1
+    lde_out = np.zeros((1 << (n - 4), 32), dtype=np.uint64)
+    root = np.zeros(8, dtype=np.uint64)
+    lib().orc_whir_commit(C.byref(consts), ptr(e), n, ptr(lde_out), ptr(root), threads)
+    return lde_out, root
+
+
+# ---- MLE / sumcheck -----------------------------------------------------------------
+def mle_eval(values, point):
+    v, pt = u64(values), u64(point)
+    return lib().orc_mle_eval(ptr(v), pt.size, ptr(pt) if pt.size else None)
+
+
+def mle_partial_eval(values, fix):
+    v, fx = u64(values), u64(fix)
+    t = v.size.bit_length() - 1
+    out = np.zeros(v.size >> fx.size, dtype=np.uint64)
+    lib().orc_mle_partial_eval(ptr(v), t, ptr(fx) if fx.size else None, fx.size, ptr(out))
+    return out
+
+
+def eq_evals(r):
+    rr = u64(r)
+    out = np.zeros(1 << rr.size, dtype=np.uint64)
+    lib().orc_eq_evals(ptr(rr) if rr.size else None, rr.size, ptr(out))
+    return out
+
+
+def sumcheck_prove(f, h, ch):
+    f, h, ch = u64(f), u64(h), u64(ch)
+    t = ch.size
+    rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+    finals = np.zeros(2, dtype=np.uint64)
+    lib().orc_sumcheck_prove(ptr(f), ptr(h), t, ptr(ch) if t else None, ptr(rounds), ptr(finals))
+    return rounds[:t], finals
+
+
+def sumcheck_verify(rounds, claimed, ch, f_eval, h_eval):
+    r, ch = u64(rounds).reshape(-1, 3), u64(ch)
+    return bool(lib().orc_sumcheck_verify(ptr(r), ch.size, claimed, ptr(ch) if ch.size else None, f_eval, h_eval))
+
+
+def sumcheck3_prove(f, g, h, ch):
+    f, g, h, ch = u64(f), u64(g), u64(h), u64(ch)
+    rounds = np.zeros((max(ch.size, 1), 4), dtype=np.uint64)
+    finals = np.zeros(3, dtype=np.uint64)
+    lib().orc_sumcheck3_prove(ptr(f), ptr(g), ptr(h), ch.size, ptr(ch), ptr(rounds), ptr(finals))
+    return rounds[:ch.size], finals
+
+
+def sumcheck3_verify(rounds, claimed, ch, fe, ge, he):
+    r, ch = u64(rounds).reshape(-1, 4), u64(ch)
+    return bool(lib().orc_sumcheck3_verify(ptr(r), ch.size, claimed, ptr(ch), fe, ge, he))
+
+
+def sum_of_products_prove(weights, values, ch):
+    w, v, ch = u64(weights), u64(values), u64(ch)
+    nt = w.shape[0]
+    rounds = np.zeros((max(ch.size, 1), 3), dtype=np.uint64)
+    be = _u64(0)
+    lib().orc_sum_of_products_prove(ptr(w), ptr(v), nt, ch.size, ptr(ch), ptr(rounds), C.byref(be))
+    return rounds[:ch.size], be.value
+
+
+def _terms(terms):
+    coeffs = u64([c for c, _ in terms])
+    off = [0]
+    idx = []
+    for _, ids in terms:
+        idx.extend(ids)
+        off.append(len(idx))
+    return coeffs, np.array(off, dtype=np.uint32), np.array(idx if idx else [0], dtype=np.uint32)
+
+
+def virtual_prove(mles, terms, ch):
+    m = u64(mles)
+    ch = u64(ch)
+    coeffs, off, idx = _terms(terms)
+    max_deg = max((len(ids) for _, ids in terms), default=0)
+    rounds = np.zeros((max(ch.size, 1), max_deg + 1), dtype=np.uint64)
+    finals = np.zeros(m.shape[0], dtype=np.uint64)
+    lib().orc_virtual_prove(ptr(m), m.shape[0], ch.size, ptr(coeffs), ptr(off), ptr(idx), len(terms),
+                            ptr(ch), ptr(rounds), ptr(finals))
+    return rounds[:ch.size], finals
+
+
+def virtual_verify(rounds, terms, claimed, ch, finals):
+    r, ch, fin = u64(rounds), u64(ch), u64(finals)
+    coeffs, off, idx = _terms(terms)
+    return bool(lib().orc_virtual_verify(ptr(np.ascontiguousarray(r)), ch.size, ptr(coeffs), ptr(off), ptr(idx),
+                                         len(terms), claimed, ptr(ch), ptr(fin)))
+
+
+def matmul_field(a, b):
+    a, b = u64(a), u64(b)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.zeros((m, n), dtype=np.uint64)
+    lib().orc_matmul_field(ptr(a), ptr(b), m, k, n, ptr(c), 0)
+    return c
+
+
+def matmul_prove(at, b, c, m, k, n, u, v, ch):
+    at, b, c, u, v, ch = map(u64, (at, b, c, u, v, ch))
+    claimed = _u64(0)
+    rounds = np.zeros((max(ch.size, 1), 3), dtype=np.uint64)
+    finals = np.zeros(2, dtype=np.uint64)
+    lib().orc_matmul_prove(ptr(at), ptr(b), ptr(c), m, k, n, ptr(u) if u.size else None,
+                           ptr(v) if v.size else None, ptr(ch) if ch.size else None,
+                           C.byref(claimed), ptr(rounds), ptr(finals))
+    return claimed.value, rounds[:ch.size], finals
+
+
+def op_matmul_prove(a, b, c, m, k, n, challenger):
+    """Op::MatMul arm.  challenger: XorShift64 or OracleTranscript (advanced in place)."""
+    a, b, c = u64(a), u64(b), u64(c)
+    ch_obj = Challenger()
+    if isinstance(challenger, XorShift64):
+        ch_obj.kind = 0
+        ch_obj.xs_state = challenger.s.value
+    else:
+        ch_obj.kind = 1
+        C.memmove(C.byref(ch_obj.tr), C.byref(challenger.t), C.sizeof(Transcript))
+    lm, lk, ln = (m.bit_length() - 1, k.bit_length() - 1, n.bit_length() - 1)
+    u = np.zeros(max(lm, 1), dtype=np.uint64)
+    v = np.zeros(max(ln, 1), dtype=np.uint64)
+    chv = np.zeros(max(lk, 1), dtype=np.uint64)
+    claimed = _u64(0)
+    rounds = np.zeros((max(lk, 1), 3), dtype=np.uint64)
+    finals = np.zeros(2, dtype=np.uint64)
+    claims = np.zeros(3, dtype=np.uint64)
+    lib().orc_op_matmul_prove(ptr(a), ptr(b), ptr(c), m, k, n, C.byref(ch_obj), ptr(u), ptr(v), ptr(chv),
+                              C.byref(claimed), ptr(rounds), ptr(finals), ptr(claims))
+    if isinstance(challenger, XorShift64):
+        challenger.s.value = ch_obj.xs_state
+    else:
+        C.memmove(C.byref(challenger.t), C.byref(ch_obj.tr), C.sizeof(Transcript))
+    return dict(u=u[:lm], v=v[:ln], ch=chv[:lk], claimed=claimed.value, rounds=rounds[:lk],
+                finals=finals, claims=claims)
+
+
+def shard_dag_child(op_ids, ops_per_shard, shard_index):
+    ids = u64(op_ids).reshape(-1)
+    t = OracleTranscript(b"x")
+    lib().orc_shard_dag_child(ptr(ids), ids.size // 3, ops_per_shard, shard_index, C.byref(t.t))
+    return t

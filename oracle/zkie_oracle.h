@@ -1,0 +1,172 @@
+/*
+ * zkie_oracle.h -- CPU restatement of the zkIE prover hot path (TEST INFRASTRUCTURE).
+ *
+ * This library is the parity checker for the CUDA product in zkie_b200/.  Only
+ * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm
+ * may load it.  It is never linked into, called by, or used as a fallback for
+ * the product path.
+ *
+ * Every function states the reference file:line it restates (paths relative to
+ * the trustless-ai/zkIE project root).  All arithmetic is exact over the
+ * Goldilocks field p = 2^64 - 2^32 + 1; values are kept canonical (< p).
+ *
+ * Parity status: the reference cannot be compiled in this environment (Rust
+ * toolchain absent; its CUDA files need sppark headers that are absent), and
+ * its tests hold no golden roots, digests or proof bytes.  The H2 restatement
+ * (MLE / sumcheck / matmul / transcript) follows the reference source line by
+ * line and is checked against the reference's own property tests, replayed
+ * with the same seeds.  The H1 restatement (NTT + Poseidon2 Merkle) follows the
+ * reference kernels; its constants (Poseidon2 round constants, internal
+ * diagonal entry 15) come from third-party crates that are absent here, so
+ * Merkle-root parity with the reference CPU path is UNPINNED.
+ */
+#ifndef ZKIE_ORACLE_H
+#define ZKIE_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_P 0xFFFFFFFF00000001ULL
+
+/* ---- field ---------------------------------------------------------------- */
+uint64_t orc_add(uint64_t a, uint64_t b);
+uint64_t orc_sub(uint64_t a, uint64_t b);
+uint64_t orc_mul(uint64_t a, uint64_t b);
+uint64_t orc_pow(uint64_t a, uint64_t e);
+uint64_t orc_inv(uint64_t a);
+uint64_t orc_from_i64(int64_t x);
+/* p3-goldilocks TWO_ADIC_GENERATORS[bits] = g^(2^(32-bits)), g = 7^((p-1)/2^32). */
+uint64_t orc_two_adic_generator(uint32_t bits);
+
+/* ---- PRNGs ---------------------------------------------------------------- */
+/* XorShift64 (crates/zkie-core/src/common/field.rs:17-36). state is in/out. */
+uint64_t orc_xorshift_init(uint64_t seed);
+uint64_t orc_xorshift_next(uint64_t *state);
+uint64_t orc_xorshift_field(uint64_t *state);
+
+/* ---- SHA-256 + Fiat-Shamir transcript (common/transcript.rs:21-80) -------- */
+void orc_sha256(const uint8_t *data, size_t len, uint8_t out[32]);
+typedef struct {
+    uint8_t state[32];
+    uint64_t counter;
+} orc_transcript;
+void orc_transcript_new(orc_transcript *t, const uint8_t *domain, size_t len);
+void orc_transcript_absorb(orc_transcript *t, const uint8_t *data, size_t len);
+void orc_transcript_absorb_u64(orc_transcript *t, uint64_t x);
+uint64_t orc_transcript_field(orc_transcript *t);
+uint64_t orc_transcript_next_u64(orc_transcript *t);
+
+/* ---- DFT (p3 TwoAdicSubgroupDft::dft_batch contract) ---------------------- */
+/* In-place radix-2 DFT of every column of a row-major h x w matrix (h = 2^lg). */
+void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w);
+/* O(h^2) definition, for cross-checking orc_dft_batch. */
+void orc_dft_naive(const uint64_t *in, uint64_t *out, uint32_t lg_h, uint64_t w);
+/* Horner evaluation of column `col` of the L x w row-major coefficient matrix
+ * at x: sum_j mat[j][col] x^j (size-independent LDE spot checks). */
+uint64_t orc_poly_eval_col(const uint64_t *mat, uint64_t L, uint64_t w, uint64_t col, uint64_t x);
+/* Zero-padded LDE: in is L x w (L = 2^lg_l), out is (L << lg_blowup) x w. */
+void orc_lde(const uint64_t *in, uint64_t *out, uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
+
+/* ---- Poseidon2-16 Goldilocks (cuda/poseidon2_merkle.cu:37-155) ----------- */
+typedef struct {
+    uint64_t ext_init[4][16];
+    uint64_t ext_final[4][16];
+    uint64_t internal[22];
+    uint64_t diag15;
+} orc_p2_consts;
+/* Round constants as Perm::new_from_rng_128(SmallRng::seed_from_u64(seed)),
+ * with SmallRng taken as xoshiro256++ seeded through SplitMix64 (UNPINNED). */
+void orc_p2_derive_constants(uint64_t seed, orc_p2_consts *c);
+void orc_p2_permute(const orc_p2_consts *c, uint64_t st[16]);
+/* PaddingFreeSponge<Perm,16,8,8> over one row (poseidon2_merkle.cu:161-184). */
+void orc_p2_hash_row(const orc_p2_consts *c, const uint64_t *row, uint64_t w, uint64_t out[8]);
+/* TruncatedPermutation<Perm,2,8,16> (poseidon2_merkle.cu:212-225). */
+void orc_p2_compress(const orc_p2_consts *c, const uint64_t l[8], const uint64_t r[8], uint64_t out[8]);
+
+/* ---- Merkle tree geometry (vendor/p3-merkle-tree/src/merkle_tree.rs) ----- */
+uint64_t orc_padded_len(uint64_t raw_len, uint64_t n);
+/* Number of digest layers and total digests for a single h-row matrix. */
+uint32_t orc_merkle_num_layers(uint64_t h);
+uint64_t orc_merkle_total_digests(uint64_t h);
+/* Leaf digests of all rows (OpenMP over rows). digests: h x 8. */
+void orc_merkle_leaves(const orc_p2_consts *c, const uint64_t *mat, uint64_t h, uint64_t w,
+                       uint64_t *digests, int threads);
+/* Full tree: layers concatenated (layer 0 first, padded lengths), root out. */
+void orc_merkle_tree(const orc_p2_consts *c, const uint64_t *mat, uint64_t h, uint64_t w,
+                     uint64_t *layers, uint64_t root[8], int threads);
+/* Root only, from precomputed leaf digests (h x 8). */
+void orc_merkle_root_from_leaves(const orc_p2_consts *c, const uint64_t *leaves, uint64_t h,
+                                 uint64_t root[8]);
+
+/* ---- WHIR base commit geometry (pcs/whir.rs:438-519) ---------------------- */
+/* evals: 2^n values (n >= 5).  lde_out: 2^(n-4) x 32.  root out. */
+void orc_whir_commit(const orc_p2_consts *c, const uint64_t *evals, uint32_t n, uint64_t *lde_out,
+                     uint64_t root[8], int threads);
+
+/* ---- MLE (common/mle.rs:8-64) --------------------------------------------- */
+uint64_t orc_mle_eval(const uint64_t *values, uint32_t t, const uint64_t *point);
+void orc_mle_partial_eval(const uint64_t *values, uint32_t t, const uint64_t *fix, uint32_t f,
+                          uint64_t *out);
+void orc_eq_evals(const uint64_t *r, uint32_t d, uint64_t *out);
+
+/* ---- sumchecks (common/sumcheck.rs) --------------------------------------- */
+/* prove (:33-79): rounds out = 3*t values (c0,c1,c2 per round); finals out = (f,h). */
+void orc_sumcheck_prove(const uint64_t *f, const uint64_t *h, uint32_t t, const uint64_t *ch,
+                        uint64_t *rounds, uint64_t finals[2]);
+int orc_sumcheck_verify(const uint64_t *rounds, uint32_t t, uint64_t claimed, const uint64_t *ch,
+                        uint64_t f_eval, uint64_t h_eval);
+/* prove3 (:162-209): rounds out = 4*t values; finals (f,g,h). */
+void orc_sumcheck3_prove(const uint64_t *f, const uint64_t *g, const uint64_t *h, uint32_t t,
+                         const uint64_t *ch, uint64_t *rounds, uint64_t finals[3]);
+int orc_sumcheck3_verify(const uint64_t *rounds, uint32_t t, uint64_t claimed, const uint64_t *ch,
+                         uint64_t f_eval, uint64_t g_eval, uint64_t h_eval);
+/* prove_sum_of_products (:243-286): weights/values are n_tables x 2^t, row-major. */
+void orc_sum_of_products_prove(const uint64_t *weights, const uint64_t *values, uint32_t n_tables,
+                               uint32_t t, const uint64_t *ch, uint64_t *rounds, uint64_t *b_eval);
+/* prove_virtual (:378-438).  mles: n_mles x 2^t row-major.  terms: n_terms entries;
+ * term i has coefficient coeffs[i] and factor list idx[idx_off[i] .. idx_off[i+1]).
+ * rounds out: t x (max_deg+1); finals out: n_mles. */
+void orc_virtual_prove(const uint64_t *mles, uint32_t n_mles, uint32_t t, const uint64_t *coeffs,
+                       const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms,
+                       const uint64_t *ch, uint64_t *rounds, uint64_t *finals);
+int orc_virtual_verify(const uint64_t *rounds, uint32_t t, const uint64_t *coeffs,
+                       const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms,
+                       uint64_t claimed, const uint64_t *ch, const uint64_t *finals);
+
+/* ---- matmul GKR (common/matmul.rs:17-56) ---------------------------------- */
+/* out: claimed, then rounds (3*log k), then f_eval, h_eval.  at is k x m (A^T). */
+void orc_matmul_prove(const uint64_t *at, const uint64_t *b, const uint64_t *c, uint64_t m,
+                      uint64_t k, uint64_t n, const uint64_t *u, const uint64_t *v,
+                      const uint64_t *ch, uint64_t *claimed, uint64_t *rounds, uint64_t finals[2]);
+/* Exact field matmul C = A (m x k) @ B (k x n). */
+void orc_matmul_field(const uint64_t *a, const uint64_t *b, uint64_t m, uint64_t k, uint64_t n,
+                      uint64_t *c, int threads);
+
+/* Op::MatMul arm of prove_shard_precomputed (zkie-ops/src/compose.rs:1724-1747).
+ * Challenge source: src_kind 0 = XorShift64 (state in/out), 1 = Transcript.
+ * Draw order: u (log m), v (log n), ch (log k).
+ * out_u/out_v/out_ch receive the draws; out_claims receives
+ * eval(A, ch||u), eval(B, v||ch), eval(C, v||u). */
+typedef struct {
+    int kind;
+    uint64_t xs_state;
+    orc_transcript tr;
+} orc_challenger;
+uint64_t orc_challenger_field(orc_challenger *s);
+void orc_op_matmul_prove(const uint64_t *a, const uint64_t *b, const uint64_t *c, uint64_t m,
+                         uint64_t k, uint64_t n, orc_challenger *src, uint64_t *out_u,
+                         uint64_t *out_v, uint64_t *out_ch, uint64_t *claimed, uint64_t *rounds,
+                         uint64_t finals[2], uint64_t claims[3]);
+/* Shard child transcript of prove_shard_dag (compose.rs:2276-2311) for a list
+ * of MatMul ops given as (a,b,c) tensor ids. */
+void orc_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_per_shard,
+                         uint64_t shard_index, orc_transcript *child);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

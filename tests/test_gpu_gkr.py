@@ -1,0 +1,115 @@
+"""GPU parity of the matmul GKR path (MLE contractions, the degree-2
+sumcheck, matmul::prove, the Op::MatMul arm) against the CPU oracle,
+bit-exact, through the C ABI."""
+import numpy as np
+import pytest
+
+P = 0xFFFFFFFF00000001
+pytestmark = pytest.mark.gpu
+
+
+def fields(seed, n):
+    g = np.random.default_rng(seed)
+    v = g.integers(0, 2 ** 64, size=n, dtype=np.uint64)
+    bad = v >= np.uint64(P)
+    while bad.any():
+        v[bad] = g.integers(0, 2 ** 64, size=int(bad.sum()), dtype=np.uint64)
+        bad = v >= np.uint64(P)
+    return v
+
+
+def signed16(seed, n):
+    g = np.random.default_rng(seed)
+    x = g.integers(-(2 ** 15), 2 ** 15, size=n, dtype=np.int64)
+    return np.where(x >= 0, x, np.int64(0)).astype(np.uint64) + np.where(x < 0, (np.uint64(P) - (-x).astype(np.uint64)), np.uint64(0))
+
+
+@pytest.mark.parametrize("t", [0, 1, 4, 10, 15, 20])
+def test_eq_and_eval(zk, orc, t):
+    vals = fields(t, 1 << t)
+    pt = fields(100 + t, t)
+    assert zk.mle_eval(vals, pt) == orc.mle_eval(vals, pt)
+    if t <= 12:
+        assert np.array_equal(zk.eq_evals(pt).cpu().numpy(), orc.eq_evals(pt))
+
+
+@pytest.mark.parametrize("t,f", [(4, 0), (4, 2), (10, 4), (10, 10), (20, 10), (20, 4), (22, 21)])
+def test_partial_eval(zk, orc, t, f):
+    vals = fields(t * 3 + f, 1 << t)
+    fix = fields(7 + f, f)
+    assert np.array_equal(zk.mle_partial_eval(vals, fix).cpu().numpy(), orc.mle_partial_eval(vals, fix))
+
+
+@pytest.mark.parametrize("t", [0, 1, 2, 8, 10, 11, 12, 16, 22, 23])
+def test_sumcheck_matches_oracle(zk, orc, t):
+    f, h, ch = fields(t, 1 << t), fields(t + 50, 1 << t), fields(t + 99, t)
+    got = zk.sumcheck_prove(f, h, 0, ch)
+    rounds, finals = orc.sumcheck_prove(f, h, ch)
+    assert np.array_equal(got.rounds, rounds)
+    assert (got.f_eval, got.h_eval) == (int(finals[0]), int(finals[1]))
+    if t <= 16:
+        claimed = int(sum(int(a) * int(b) for a, b in zip(f, h)) % P)
+        assert orc.sumcheck_verify(got.rounds, claimed, ch, got.f_eval, got.h_eval)
+
+
+def test_sumcheck_reference_seed(zk, orc):
+    # sumcheck.rs:316-335 with the reference's seed
+    rng = orc.XorShift64(3)
+    f, h = rng.fields(256), rng.fields(256)
+    true_sum = sum(int(a) * int(b) for a, b in zip(f, h)) % P
+    ch = rng.fields(8)
+    p = zk.sumcheck_prove(f, h, true_sum, ch)
+    assert orc.sumcheck_verify(p.rounds, true_sum, ch, p.f_eval, p.h_eval)
+    assert not orc.sumcheck_verify(p.rounds, (true_sum + 1) % P, ch, p.f_eval, p.h_eval)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (2, 4, 8), (4, 4, 4), (16, 64, 32), (16, 1024, 1024)])
+def test_matmul_prove_matches_oracle(zk, orc, m, k, n):
+    a = signed16(m + k, m * k).reshape(m, k)
+    b = signed16(n + 3, k * n).reshape(k, n)
+    c = orc.matmul_field(a, b)
+    assert np.array_equal(zk.matmul_field(a, b, m, k, n).cpu().numpy().reshape(m, n), c)
+    lm, lk, ln = (m.bit_length() - 1, k.bit_length() - 1, n.bit_length() - 1)
+    u, v, ch = fields(1, lm), fields(2, ln), fields(3, lk)
+    at = a.T.copy()
+    got = zk.matmul_prove(at, b, c, m, k, n, u, v, ch)
+    claimed, rounds, finals = orc.matmul_prove(at, b, c, m, k, n, u, v, ch)
+    assert got.claimed == claimed
+    assert np.array_equal(got.sumcheck.rounds, rounds)
+    assert (got.sumcheck.f_eval, got.sumcheck.h_eval) == tuple(int(x) for x in finals)
+
+
+def test_op_matmul_xorshift_reference_test(zk, orc):
+    # compose.rs:5199-5224: XorShift64(0x1818), m,k,n = 4,8,8, entries next_u64() % 50
+    zr, orr = zk.XorShift64(0x1818), orc.XorShift64(0x1818)
+    m, k, n = 4, 8, 8
+    a = np.array([orr.next_u64() % 50 for _ in range(m * k)], dtype=np.uint64).reshape(m, k)
+    b = np.array([orr.next_u64() % 50 for _ in range(k * n)], dtype=np.uint64).reshape(k, n)
+    for _ in range(m * k + k * n):
+        zr.next_u64()
+    c = orc.matmul_field(a, b)
+    got = zk.op_matmul_prove(a, b, c, m, k, n, zr)
+    exp = orc.op_matmul_prove(a, b, c, m, k, n, orr)
+    assert np.array_equal(got.u, exp["u"]) and np.array_equal(got.v, exp["v"]) and np.array_equal(got.ch, exp["ch"])
+    assert got.proof.claimed == exp["claimed"]
+    assert np.array_equal(got.proof.sumcheck.rounds, exp["rounds"])
+    assert np.array_equal(got.claims, exp["claims"])
+    assert zr.field() == orr.field()  # both sources advanced identically
+
+
+def test_op_matmul_cfg1_transcript(zk, orc):
+    """BASELINE config 1 shape (16x768 @ 768x768 padded to 16x1024 @ 1024x1024),
+    challenges from the shard-DAG child transcript."""
+    m, k, n = 16, 1024, 1024
+    a = np.zeros((m, k), dtype=np.uint64)
+    b = np.zeros((k, n), dtype=np.uint64)
+    a[:, :768] = signed16(11, m * 768).reshape(m, 768)
+    b[:768, :768] = signed16(12, 768 * 768).reshape(768, 768)
+    c = orc.matmul_field(a, b)
+    ids = [[0, 1, 2]]
+    got = zk.op_matmul_prove(a, b, c, m, k, n, zk.shard_dag_child(ids, 1, 0))
+    exp = orc.op_matmul_prove(a, b, c, m, k, n, orc.shard_dag_child(ids, 1, 0))
+    assert got.proof.claimed == exp["claimed"]
+    assert np.array_equal(got.proof.sumcheck.rounds, exp["rounds"])
+    assert np.array_equal(got.claims, exp["claims"])
+    assert np.array_equal(got.u, exp["u"]) and np.array_equal(got.ch, exp["ch"])

@@ -1,0 +1,15 @@
+"""zkie_b200: the zkIE prover hot path (shard commit + matmul GKR sumcheck)
+as hand-written sm_100a CUDA kernels behind a C ABI (libzkie_b200.so).
+
+The package is a thin host-side mirror of the reference's Rust interface; all
+compute runs in the shared object.  Importing fails if the shared object is
+missing -- there is no CPU fallback.
+"""
+from ._lib import LIB_PATH, ZkieError, check, lib  # noqa: F401
+from .commit import (  # noqa: F401
+    Committed, CudaDft, CudaMerkleTreeMmcs, MerkleTree, Whir, commit, commit_host, init_default_constants,
+    make_twiddles, merkle_layer_lengths, p2_default_constants, padded_len, split_layers, upload_constants)
+from .device import P  # noqa: F401
+from .gkr import (  # noqa: F401
+    MatmulProof, OpMatMulProof, SumcheckProof, Transcript, XorShift64, eq_evals, matmul_field, matmul_prove,
+    mle_eval, mle_partial_eval, op_matmul_prove, sha256, shard_dag_child, sumcheck_prove)

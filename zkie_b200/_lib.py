@@ -1,0 +1,97 @@
+"""ctypes binding of libzkie_b200.so: every symbol declared in include/*.h.
+
+The shared object is built in-tree by zkie_b200/build.py.  There is no
+fallback: if it is missing or fails to load, importing this module raises.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzkie_b200.so")
+
+u64, u32, i32, i64 = C.c_uint64, C.c_uint32, C.c_int32, C.c_int
+pu64 = C.POINTER(C.c_uint64)
+vp = C.c_void_p  # device pointers and streams travel as integers
+sz = C.c_size_t
+
+
+class Transcript(C.Structure):
+    _fields_ = [("state", C.c_uint8 * 32), ("counter", C.c_uint64)]
+
+
+class Challenger(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("xorshift_state", C.c_uint64), ("transcript", Transcript)]
+
+
+PTr = C.POINTER(Transcript)
+PCh = C.POINTER(Challenger)
+
+# name -> (restype, argtypes); one entry per declaration in include/*.h
+SIGNATURES = {
+    # include/zkie_goldilocks_cuda.h (reference symbols)
+    "zkie_cuda_device_count": (i64, []),
+    "zkie_ntt_forward_goldilocks": (i64, [vp, vp, u32, u64, vp]),
+    "zkie_p2_upload_constants": (i64, [pu64, pu64, pu64, u64]),
+    "zkie_p2_leaf_batch": (i64, [vp, vp, u32, u32]),
+    "zkie_p2_leaf_scalar": (i64, [vp, vp, u32, u32, u32]),
+    "zkie_p2_compress_batch": (i64, [vp, vp, u32, u32]),
+    "zkie_p2_compress_scalar": (i64, [vp, vp, u32, u32, u32]),
+    # include/zkie2.h
+    "zkie2_p2_default_constants": (i64, [u64, pu64, pu64, pu64, pu64]),
+    "zkie2_p2_init_default": (i64, []),
+    "zkie2_p2_permute": (i64, [vp, u64, u32, vp]),
+    "zkie2_lde_scratch_elems": (u64, [u32, u32, u64]),
+    "zkie2_lde": (i64, [vp, vp, vp, u32, u32, u64, vp]),
+    "zkie2_dft_twiddles": (i64, [u32, pu64]),
+    "zkie2_dft": (i64, [vp, vp, vp, u32, u64, vp]),
+    "zkie2_merkle_total_digests": (u64, [u64]),
+    "zkie2_merkle_num_layers": (u32, [u64]),
+    "zkie2_merkle_leaves": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_merkle_tree": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_merkle_tree_from_leaves": (i64, [u64, vp, vp]),
+    "zkie2_commit_scratch_elems": (u64, [u32, u32, u64]),
+    "zkie2_commit": (i64, [vp, u32, u32, u64, vp, vp, vp, vp]),
+    "zkie2_whir_scratch_elems": (u64, [u32]),
+    "zkie2_whir_commit": (i64, [vp, u32, vp, vp, vp, vp]),
+    "zkie2_commit_host": (i64, [vp, u32, u32, u64, vp, vp, vp]),
+    "zkie2_sha256": (None, [C.c_char_p, sz, C.c_char_p]),
+    "zkie2_transcript_new": (None, [PTr, C.c_char_p, sz]),
+    "zkie2_transcript_absorb": (None, [PTr, C.c_char_p, sz]),
+    "zkie2_transcript_absorb_u64": (None, [PTr, u64]),
+    "zkie2_transcript_field": (u64, [PTr]),
+    "zkie2_transcript_next_u64": (u64, [PTr]),
+    "zkie2_challenger_xorshift": (None, [PCh, u64]),
+    "zkie2_challenger_field": (u64, [PCh]),
+    "zkie2_shard_dag_child": (None, [pu64, u32, u64, u64, PCh]),
+    "zkie2_eq_evals": (i64, [pu64, u32, vp, vp]),
+    "zkie2_mle_scratch_elems": (u64, [u32]),
+    "zkie2_mle_partial_eval": (i64, [vp, u32, pu64, u32, vp, vp, vp]),
+    "zkie2_mle_eval": (i64, [vp, u32, pu64, pu64, vp, vp]),
+    "zkie2_sumcheck_scratch_elems": (u64, [u32]),
+    "zkie2_sumcheck_prove": (i64, [vp, vp, u32, pu64, pu64, pu64, vp, vp]),
+    "zkie2_matmul_scratch_elems": (u64, [u64, u64, u64]),
+    "zkie2_matmul_prove": (i64, [vp, vp, vp, u64, u64, u64, pu64, pu64, pu64, pu64, pu64, pu64, vp, vp]),
+    "zkie2_op_matmul_scratch_elems": (u64, [u64, u64, u64]),
+    "zkie2_op_matmul_prove": (i64, [vp, vp, vp, u64, u64, u64, PCh, pu64, pu64, pu64, pu64, pu64, pu64,
+                                    pu64, vp, vp]),
+    "zkie2_matmul_field": (i64, [vp, vp, u64, u64, u64, vp, vp]),
+}
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `python -m zkie_b200.build` "
+                      "(there is no CPU fallback)")
+
+lib = C.CDLL(LIB_PATH)
+for _name, (_res, _args) in SIGNATURES.items():
+    _f = getattr(lib, _name)
+    _f.restype = _res
+    _f.argtypes = _args
+
+
+class ZkieError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str):
+    if rc != 0:
+        raise ZkieError(f"{what} failed with CUDA error {rc}")

@@ -1,0 +1,140 @@
+// commit.cu -- the shard commit stage: zero-padded LDE + Poseidon2 Merkle tree
+// over the rows, in one device pipeline.
+//
+// The reference runs this as two host round trips (pcs/dft_cuda.rs:184-221
+// uploads the coefficients, downloads the LDE; pcs/merkle_cuda.rs:177-312
+// uploads the LDE again and downloads the digest layers).  Here the LDE stays
+// in HBM between the transform and the hashing; only the final results cross
+// PCIe, and the download of the LDE overlaps the hashing.
+#include <mutex>
+
+#include "../../include/zkie2.h"
+#include "common.cuh"
+#include "internal.h"
+
+namespace zk {
+
+namespace {
+
+struct DevStreams {
+    cudaStream_t compute = nullptr, copy = nullptr;
+    cudaEvent_t lde_ready = nullptr, done = nullptr;
+    bool ready = false;
+};
+std::mutex g_streams_mu;
+DevStreams g_streams[kMaxDevices];
+
+int get_streams(DevStreams** out) {
+    int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_streams_mu);
+    DevStreams& s = g_streams[d];
+    if (!s.ready) {
+        ZK_TRY(cudaStreamCreateWithFlags(&s.compute, cudaStreamNonBlocking));
+        ZK_TRY(cudaStreamCreateWithFlags(&s.copy, cudaStreamNonBlocking));
+        ZK_TRY(cudaEventCreateWithFlags(&s.lde_ready, cudaEventDisableTiming));
+        ZK_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        cudaMemPool_t pool;
+        if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
+            uint64_t thr = ~0ull;  // keep freed blocks cached across calls
+            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+        }
+        s.ready = true;
+    }
+    *out = &s;
+    return 0;
+}
+
+}  // namespace
+
+// LDE (rows >= rows_valid of the L-row input are zero) followed by the tree.
+int commit_device(const uint64_t* d_in, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                  uint64_t* d_lde, uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t s) {
+    int rc = p2_ensure_default();
+    if (rc) return rc;
+    rc = lde_launch(d_in, d_lde, d_scratch, lg_l, lg_blowup, w, s);
+    if (rc) return rc;
+    const uint64_t H = 1ull << (lg_l + lg_blowup);
+    return merkle_build(d_lde, H, w, d_layers, s);
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+uint64_t zkie2_commit_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w) {
+    return lde_scratch_elems(lg_l, lg_blowup, w);
+}
+
+int zkie2_commit(const uint64_t* d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                 uint64_t* d_lde, uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t stream) {
+    if (w == 0) return (int)cudaErrorInvalidValue;
+    return commit_device(d_coeffs, lg_l, lg_blowup, w, d_lde, d_layers, d_scratch, stream);
+}
+
+// WHIR base commit (pcs/whir.rs:438-469): 2^n evaluations as a row-major
+// 2^(n-5) x 32 matrix (width 2^folding, folding factor 5), zero-padded to
+// twice the height (starting_log_inv_rate 1), DFT per column, Merkle over rows.
+int zkie2_whir_commit(const uint64_t* d_evals, uint32_t n, uint64_t* d_lde, uint64_t* d_layers,
+                      uint64_t* d_scratch, cudaStream_t stream) {
+    if (n < 5) return (int)cudaErrorInvalidValue;
+    return commit_device(d_evals, n - 5, 1, 32, d_lde, d_layers, d_scratch, stream);
+}
+
+uint64_t zkie2_whir_scratch_elems(uint32_t n) { return n < 5 ? 0 : lde_scratch_elems(n - 5, 1, 32); }
+
+// Host-buffer commit: the end-to-end path a drop-in caller of
+// CudaDft::dft_batch + CudaMerkleTreeMmcs::commit takes.  Copies the L x w
+// coefficient matrix in, runs LDE + tree, and copies back the root and --
+// when the pointers are non-null -- the LDE (the tree's leaves) and every
+// digest layer.  Synchronous; device buffers come from the stream-ordered
+// pool of the current device.
+int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                      uint64_t* h_lde, uint64_t* h_layers, uint64_t* h_root) {
+    if (!h_coeffs || !h_root || w == 0) return (int)cudaErrorInvalidValue;
+    DevStreams* st = nullptr;
+    int rc = get_streams(&st);
+    if (rc) return rc;
+    const uint64_t L = 1ull << lg_l, H = L << lg_blowup;
+    const MerkleGeom g = merkle_geometry(H);
+    const uint64_t scratch = lde_scratch_elems(lg_l, lg_blowup, w);
+    uint64_t *d_in = nullptr, *d_lde = nullptr, *d_layers = nullptr, *d_scr = nullptr;
+    cudaStream_t cs = st->compute;
+    ZK_TRY(cudaMallocAsync((void**)&d_in, 8 * L * w, cs));
+    ZK_TRY(cudaMallocAsync((void**)&d_lde, 8 * H * w, cs));
+    ZK_TRY(cudaMallocAsync((void**)&d_layers, 64 * g.total, cs));
+    if (scratch) ZK_TRY(cudaMallocAsync((void**)&d_scr, 8 * scratch, cs));
+    ZK_TRY(cudaMemcpyAsync(d_in, h_coeffs, 8 * L * w, cudaMemcpyHostToDevice, cs));
+    rc = p2_ensure_default();
+    if (!rc) rc = lde_launch(d_in, d_lde, d_scr, lg_l, lg_blowup, w, cs);
+    if (!rc && h_lde) {
+        // Download the LDE on the copy stream while the compute stream hashes.
+        rc = (int)cudaEventRecord(st->lde_ready, cs);
+        if (!rc) rc = (int)cudaStreamWaitEvent(st->copy, st->lde_ready, 0);
+        if (!rc) rc = (int)cudaMemcpyAsync(h_lde, d_lde, 8 * H * w, cudaMemcpyDeviceToHost, st->copy);
+    }
+    if (!rc) rc = merkle_build(d_lde, H, w, d_layers, cs);
+    if (!rc) {
+        if (h_layers)
+            rc = (int)cudaMemcpyAsync(h_layers, d_layers, 64 * g.total, cudaMemcpyDeviceToHost, cs);
+        else
+            rc = (int)cudaMemcpyAsync(h_root, d_layers + 8 * g.offset.back(), 64, cudaMemcpyDeviceToHost, cs);
+    }
+    if (!rc && h_lde) {
+        rc = (int)cudaEventRecord(st->done, st->copy);
+        if (!rc) rc = (int)cudaStreamWaitEvent(cs, st->done, 0);
+    }
+    cudaFreeAsync(d_in, cs);
+    cudaFreeAsync(d_lde, cs);
+    cudaFreeAsync(d_layers, cs);
+    if (d_scr) cudaFreeAsync(d_scr, cs);
+    cudaError_t e = cudaStreamSynchronize(cs);
+    if (!rc && e != cudaSuccess) rc = (int)e;
+    if (!rc && h_layers)
+        for (int i = 0; i < 8; i++) h_root[i] = h_layers[8 * g.offset.back() + i];
+    return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+// internal.h -- host-side launch API shared between the translation units of
+// libzkie_b200 (not exported).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <vector>
+
+namespace zk {
+
+// ---- Poseidon2 / Merkle (poseidon2.cu) --------------------------------------
+// Constants must be present on the current device before any hashing launch.
+bool p2_constants_ready();
+int p2_upload(const uint64_t* rc_init, const uint64_t* rc_final, const uint64_t* rc_internal,
+              uint64_t diag15);
+// Derive the reference's default constants (SmallRng seed 1) and upload them
+// to the current device if nothing was uploaded there yet.
+int p2_ensure_default();
+
+int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint64_t row_end,
+                     uint64_t w, cudaStream_t s);
+int launch_compress(const uint64_t* prev, uint64_t* next, uint64_t from, uint64_t to,
+                    uint32_t step, cudaStream_t s);
+
+// Merkle layer geometry of one matrix of h rows (pcs/merkle_cuda.rs:203-209).
+struct MerkleGeom {
+    std::vector<uint64_t> len;     // padded length of each layer
+    std::vector<uint64_t> offset;  // digest offset of each layer in the flat buffer
+    uint64_t total = 0;            // total digests
+};
+MerkleGeom merkle_geometry(uint64_t h);
+// Hash every row and build every layer into `layers` (flat, geometry above).
+int merkle_build(const uint64_t* mat, uint64_t h, uint64_t w, uint64_t* layers, cudaStream_t s);
+// Build layers 1.. from a leaf layer already in layers[0 .. h).
+int merkle_build_from_leaves(uint64_t h, uint64_t* layers, cudaStream_t s);
+
+// ---- NTT (ntt.cu) ------------------------------------------------------------
+// Zero-padded LDE of every column: in is L x w (L = 2^lg_l), out is
+// (L << lg_blowup) x w, scratch holds (L << lg_blowup) * w u64.
+int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l,
+               uint32_t lg_blowup, uint64_t w, cudaStream_t s);
+uint64_t lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
+
+// ---- host-side primitives (host.cpp) -------------------------------------------
+void p2_derive_constants_host(uint64_t seed, uint64_t rc_init[64], uint64_t rc_final[64],
+                              uint64_t rc_internal[22], uint64_t* diag15);
+uint64_t gl_mul_host(uint64_t a, uint64_t b);
+uint64_t gl_add_host(uint64_t a, uint64_t b);
+uint64_t gl_sub_host(uint64_t a, uint64_t b);
+uint64_t gl_pow_host(uint64_t a, uint64_t e);
+uint64_t two_adic_generator_host(uint32_t bits);
+
+}  // namespace zk

@@ -1,0 +1,309 @@
+// poseidon2.cu -- Poseidon2 Merkle hashing kernels and the reference-facing
+// zkie_p2_* entry points (crates/zkie-core/cuda/poseidon2_merkle.cu:252-318).
+//
+// Hash configuration (pcs/merkle_cuda.rs:39-45): Poseidon2Goldilocks<16>,
+// leaves PaddingFreeSponge<Perm,16,8,8>, nodes TruncatedPermutation<Perm,2,8,16>,
+// binary tree, 8-element digests.
+//
+// Design: one thread per row (leaf) or per node; the 16-element state stays
+// in registers, the round constants in __constant__ memory.  Unlike the
+// reference (one thread serially hashing 8 rows), every thread hashes one
+// row, so a launch exposes 8x more parallelism and the integer pipes stay fed.
+#include <mutex>
+
+#include "../../include/zkie_goldilocks_cuda.h"
+#include "../../include/zkie2.h"
+#include "common.cuh"
+#include "internal.h"
+#include "poseidon2.cuh"
+
+namespace zk {
+
+__constant__ P2Const c_p2;
+
+namespace {
+std::mutex g_p2_mu;
+bool g_p2_ready[kMaxDevices];
+
+constexpr int kHashThreads = 128;
+
+// Leaf digests of rows [row0, row_end): sponge with rate 8, overwrite mode,
+// one permutation per full 8-block and one after a partial tail
+// (poseidon2_merkle.cu:161-184).  Row r starts at mat + r*w.
+__global__ void __launch_bounds__(kHashThreads)
+    k_leaf_rows(const uint64_t* __restrict__ mat, uint64_t* __restrict__ digests, uint64_t row0,
+                uint64_t row_end, uint64_t w) {
+    const uint64_t row = row0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= row_end) return;
+    const uint64_t* src = mat + row * w;
+    uint64_t s[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) s[i] = 0;
+    const uint64_t nblk = (w + 7) >> 3;
+    const bool vec = ((w & 1) == 0) && ((reinterpret_cast<uintptr_t>(mat) & 15) == 0);
+    for (uint64_t b = 0; b < nblk; b++) {
+        const uint64_t base = b << 3;
+        const uint64_t n = (w - base) < 8 ? (w - base) : 8;
+        if (n == 8 && vec) {
+            const ulonglong2* p = reinterpret_cast<const ulonglong2*>(src + base);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                ulonglong2 v = __ldg(p + q);
+                s[2 * q] = v.x;
+                s[2 * q + 1] = v.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if ((uint64_t)i < n) s[i] = __ldg(src + base + i);
+        }
+        p2_permute(s, c_p2);
+    }
+    ulonglong2* dst = reinterpret_cast<ulonglong2*>(digests + row * 8);
+#pragma unroll
+    for (int q = 0; q < 4; q++) dst[q] = make_ulonglong2(gl_canon(s[2 * q]), gl_canon(s[2 * q + 1]));
+}
+
+// Node i of the next layer: state = [prev[step*i], prev[step*i+1] (if step
+// is 2), zeros], permute, keep state[0..8] (poseidon2_merkle.cu:212-225).
+__global__ void __launch_bounds__(kHashThreads)
+    k_compress(const uint64_t* __restrict__ prev, uint64_t* __restrict__ next, uint64_t from,
+               uint64_t to, uint32_t step) {
+    const uint64_t i = from + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= to) return;
+    const ulonglong2* src = reinterpret_cast<const ulonglong2*>(prev + (uint64_t)step * i * 8);
+    uint64_t s[16];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        ulonglong2 v = __ldg(src + q);
+        s[2 * q] = v.x;
+        s[2 * q + 1] = v.y;
+    }
+    if (step >= 2) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            ulonglong2 v = __ldg(src + 4 + q);
+            s[8 + 2 * q] = v.x;
+            s[8 + 2 * q + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int i2 = 8; i2 < 16; i2++) s[i2] = 0;
+    }
+    p2_permute(s, c_p2);
+    ulonglong2* dst = reinterpret_cast<ulonglong2*>(next + i * 8);
+#pragma unroll
+    for (int q = 0; q < 4; q++) dst[q] = make_ulonglong2(gl_canon(s[2 * q]), gl_canon(s[2 * q + 1]));
+}
+
+// Full permutations of a batch of 16-element states (tests and the
+// permutation throughput probe used for the integer-pipe roofline).
+__global__ void __launch_bounds__(kHashThreads)
+    k_permute(uint64_t* __restrict__ states, uint64_t n, uint32_t reps) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t s[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) s[q] = states[i * 16 + q];
+    for (uint32_t r = 0; r < reps; r++) p2_permute(s, c_p2);
+#pragma unroll
+    for (int q = 0; q < 16; q++) states[i * 16 + q] = gl_canon(s[q]);
+}
+
+uint64_t canon_host(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
+
+}  // namespace
+
+bool p2_constants_ready() {
+    int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> g(g_p2_mu);
+    return g_p2_ready[d];
+}
+
+int p2_upload(const uint64_t* rc_init, const uint64_t* rc_final, const uint64_t* rc_internal,
+              uint64_t diag15) {
+    if (!rc_init || !rc_final || !rc_internal) return (int)cudaErrorInvalidValue;
+    P2Const h;
+    for (int r = 0; r < 4; r++)
+        for (int i = 0; i < 16; i++) {
+            h.ext_init[r][i] = canon_host(rc_init[r * 16 + i]);
+            h.ext_final[r][i] = canon_host(rc_final[r * 16 + i]);
+        }
+    for (int r = 0; r < 22; r++) h.internal[r] = canon_host(rc_internal[r]);
+    h.diag15 = canon_host(diag15);
+    int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    ZK_TRY(cudaMemcpyToSymbol(c_p2, &h, sizeof(P2Const)));
+    std::lock_guard<std::mutex> g(g_p2_mu);
+    g_p2_ready[d] = true;
+    return 0;
+}
+
+int p2_ensure_default() {
+    if (p2_constants_ready()) return 0;
+    uint64_t ri[64], rf[64], rp[22], d15;
+    p2_derive_constants_host(1, ri, rf, rp, &d15);
+    return p2_upload(ri, rf, rp, d15);
+}
+
+int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint64_t row_end,
+                     uint64_t w, cudaStream_t s) {
+    if (row_end <= row0) return 0;
+    if (!digests || (!mat && w != 0)) return (int)cudaErrorInvalidValue;
+    const uint64_t n = row_end - row0;
+    k_leaf_rows<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0,
+                                                                              row_end, w);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int launch_compress(const uint64_t* prev, uint64_t* next, uint64_t from, uint64_t to, uint32_t step,
+                    cudaStream_t s) {
+    if (to <= from) return 0;
+    if (!prev || !next || step < 1 || step > 2) return (int)cudaErrorInvalidValue;
+    const uint64_t n = to - from;
+    k_compress<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+static uint64_t padded_len(uint64_t raw, uint64_t n) {
+    if (raw <= 1) return raw;
+    if (raw >= n) return (raw + n - 1) / n * n;
+    return n;
+}
+
+MerkleGeom merkle_geometry(uint64_t h) {
+    MerkleGeom g;
+    uint64_t len = padded_len(h, 2), off = 0;
+    g.len.push_back(len);
+    g.offset.push_back(off);
+    off += len;
+    while (len > 1) {
+        len = padded_len(len / 2, 2);
+        g.len.push_back(len);
+        g.offset.push_back(off);
+        off += len;
+    }
+    g.total = off;
+    return g;
+}
+
+int merkle_build_from_leaves(uint64_t h, uint64_t* layers, cudaStream_t s) {
+    MerkleGeom g = merkle_geometry(h);
+    // Padding slots hold the default (zero) digest.
+    if (g.len[0] > h) ZK_TRY(cudaMemsetAsync(layers + 8 * h, 0, 64 * (g.len[0] - h), s));
+    for (size_t i = 0; i + 1 < g.len.size(); i++) {
+        uint64_t raw = g.len[i] / 2;
+        uint64_t* prev = layers + 8 * g.offset[i];
+        uint64_t* next = layers + 8 * g.offset[i + 1];
+        if (g.len[i + 1] > raw) ZK_TRY(cudaMemsetAsync(next + 8 * raw, 0, 64 * (g.len[i + 1] - raw), s));
+        int rc = launch_compress(prev, next, 0, raw, 2, s);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int merkle_build(const uint64_t* mat, uint64_t h, uint64_t w, uint64_t* layers, cudaStream_t s) {
+    if (h == 0) return (int)cudaErrorInvalidValue;
+    int rc = launch_leaf_rows(mat, layers, 0, h, w, s);
+    if (rc) return rc;
+    return merkle_build_from_leaves(h, layers, s);
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+// ============================================================================
+// Reference-facing entry points (same names, signatures and semantics as
+// crates/zkie-core/cuda/poseidon2_merkle.cu:252-318, bound in
+// crates/zkie-core/src/pcs/cuda_ffi.rs:19-45).  Default stream, asynchronous;
+// return the CUDA error code.  Where the reference would dereference a null
+// pointer on the device, these return cudaErrorInvalidValue instead.
+// ============================================================================
+extern "C" {
+
+int zkie_p2_upload_constants(const uint64_t* rc_init, const uint64_t* rc_final,
+                             const uint64_t* rc_internal, uint64_t diag15) {
+    return p2_upload(rc_init, rc_final, rc_internal, diag15);
+}
+
+int zkie_p2_leaf_batch(const uint64_t* mat, uint64_t* digests, uint32_t h, uint32_t w) {
+    uint64_t rows = (uint64_t)(h / 8) * 8;
+    if (rows == 0) return 0;
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    return launch_leaf_rows(mat, digests, 0, rows, w, 0);
+}
+
+int zkie_p2_leaf_scalar(const uint64_t* mat, uint64_t* digests, uint32_t start_row, uint32_t h,
+                        uint32_t w) {
+    if (start_row >= h) return 0;
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    return launch_leaf_rows(mat, digests, start_row, h, w, 0);
+}
+
+int zkie_p2_compress_batch(const uint64_t* prev, uint64_t* next, uint32_t next_len, uint32_t step) {
+    uint64_t n = (uint64_t)(next_len / 8) * 8;
+    if (n == 0) return 0;
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    return launch_compress(prev, next, 0, n, step, 0);
+}
+
+int zkie_p2_compress_scalar(const uint64_t* prev, uint64_t* next, uint32_t from, uint32_t to,
+                            uint32_t step) {
+    if (from >= to) return 0;
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    return launch_compress(prev, next, from, to, step, 0);
+}
+
+int zkie_cuda_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+// ---- new entry points --------------------------------------------------------
+int zkie2_p2_default_constants(uint64_t seed, uint64_t* rc_init, uint64_t* rc_final,
+                               uint64_t* rc_internal, uint64_t* diag15) {
+    if (!rc_init || !rc_final || !rc_internal || !diag15) return (int)cudaErrorInvalidValue;
+    p2_derive_constants_host(seed, rc_init, rc_final, rc_internal, diag15);
+    return 0;
+}
+
+int zkie2_p2_init_default(void) { return p2_ensure_default(); }
+
+int zkie2_p2_permute(uint64_t* d_states, uint64_t n, uint32_t reps, cudaStream_t stream) {
+    if (n == 0) return 0;
+    if (!d_states) return (int)cudaErrorInvalidValue;
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    k_permute<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, stream>>>(d_states, n, reps);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+uint64_t zkie2_merkle_total_digests(uint64_t h) { return h ? merkle_geometry(h).total : 0; }
+
+uint32_t zkie2_merkle_num_layers(uint64_t h) { return h ? (uint32_t)merkle_geometry(h).len.size() : 0; }
+
+int zkie2_merkle_leaves(const uint64_t* d_mat, uint64_t h, uint64_t w, uint64_t* d_digests,
+                        cudaStream_t stream) {
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    return launch_leaf_rows(d_mat, d_digests, 0, h, w, stream);
+}
+
+int zkie2_merkle_tree(const uint64_t* d_mat, uint64_t h, uint64_t w, uint64_t* d_layers,
+                      cudaStream_t stream) {
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    if (!d_layers) return (int)cudaErrorInvalidValue;
+    return merkle_build(d_mat, h, w, d_layers, stream);
+}
+
+int zkie2_merkle_tree_from_leaves(uint64_t h, uint64_t* d_layers, cudaStream_t stream) {
+    if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
+    if (!d_layers || h == 0) return (int)cudaErrorInvalidValue;
+    return merkle_build_from_leaves(h, d_layers, stream);
+}
+
+}  // extern "C"
