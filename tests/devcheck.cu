@@ -1,0 +1,120 @@
+// devcheck.cu -- test-side self-check of the device arithmetic (TEST INFRASTRUCTURE).
+//
+// Runs the product's Goldilocks primitives and Poseidon2 stages (from
+// zkie_b200/csrc/*.cuh) element-wise on the device and, from the same source,
+// on the host, so a test can compare the two on identical inputs.  The host
+// path is itself checked against the CPU oracle.  Constants are passed by
+// value (kernel parameter), independent of the product's __constant__ upload.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../zkie_b200/csrc/poseidon2.cuh"
+
+using namespace zk;
+
+namespace {
+
+ZK_HD uint64_t scalar_op(int op, uint64_t a, uint64_t b) {
+    switch (op) {
+        case 0: return gl_add(a, b);
+        case 1: return gl_add_c(a, gl_canon(b));
+        case 2: return gl_sub(a, b);
+        case 3: return gl_mul(a, b);
+        case 4: return gl_sqr(a);
+        case 5: return gl_div_pow2<1>(a);
+        case 6: return gl_div_pow2<3>(a);
+        case 7: return gl_div_pow2<4>(a);
+        case 8: return gl_div_pow2<5>(a);
+        case 9: return gl_div_pow2<32>(a);
+        case 10: return gl_canon(a);
+        case 11: return p2_sbox(a);
+        case 12: return mul_hi(a, b);
+        case 13: return gl_reduce128(a, b);
+        default: return 0;
+    }
+}
+
+// Stage ops on 16-element states.
+ZK_HD void state_op(int op, uint64_t s[16], const P2Const& c) {
+    switch (op) {
+        case 100: p2_mds_light(s); break;
+        case 101:
+            for (int i = 0; i < 16; i++) s[i] = p2_sbox(gl_add_c(s[i], c.ext_init[0][i]));
+            p2_mds_light(s);
+            break;
+        case 102: p2_internal_linear(s, c.diag15); break;
+        case 103:
+            s[0] = p2_sbox(gl_add_c(s[0], c.internal[0]));
+            p2_internal_linear(s, c.diag15);
+            break;
+        case 104: p2_permute(s, c); break;
+        case 105: {
+            uint64_t a = s[0], b = s[1], x = s[2], d = s[3];
+            p2_mat4(a, b, x, d);
+            s[0] = a; s[1] = b; s[2] = x; s[3] = d;
+            break;
+        }
+        default: break;
+    }
+}
+
+__global__ void k_scalar(int op, const uint64_t* a, const uint64_t* b, uint64_t* out, uint64_t n) {
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = scalar_op(op, a[i], b[i]);
+}
+
+__global__ void k_state(int op, uint64_t* st, uint64_t n, P2Const c) {
+    uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t s[16];
+    for (int q = 0; q < 16; q++) s[q] = st[i * 16 + q];
+    state_op(op, s, c);
+    for (int q = 0; q < 16; q++) st[i * 16 + q] = s[q];
+}
+
+}  // namespace
+
+extern "C" {
+
+// Device: out[i] = op(a[i], b[i]) for device arrays of n u64.
+int devcheck_scalar(int op, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, uint64_t n) {
+    k_scalar<<<(unsigned)((n + 127) / 128), 128>>>(op, d_a, d_b, d_out, n);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return (int)e;
+}
+
+int devcheck_state(int op, uint64_t* d_states, uint64_t n, const uint64_t* h_consts151) {
+    P2Const c;
+    for (int r = 0; r < 4; r++)
+        for (int i = 0; i < 16; i++) {
+            c.ext_init[r][i] = h_consts151[r * 16 + i];
+            c.ext_final[r][i] = h_consts151[64 + r * 16 + i];
+        }
+    for (int i = 0; i < 22; i++) c.internal[i] = h_consts151[128 + i];
+    c.diag15 = h_consts151[150];
+    k_state<<<(unsigned)((n + 127) / 128), 128>>>(op, d_states, n, c);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return (int)e;
+}
+
+// Host: the same functions compiled for the CPU.
+void hostcheck_scalar(int op, const uint64_t* a, const uint64_t* b, uint64_t* out, uint64_t n) {
+    for (uint64_t i = 0; i < n; i++) out[i] = scalar_op(op, a[i], b[i]);
+}
+
+void hostcheck_state(int op, uint64_t* states, uint64_t n, const uint64_t* h_consts151) {
+    P2Const c;
+    for (int r = 0; r < 4; r++)
+        for (int i = 0; i < 16; i++) {
+            c.ext_init[r][i] = h_consts151[r * 16 + i];
+            c.ext_final[r][i] = h_consts151[64 + r * 16 + i];
+        }
+    for (int i = 0; i < 22; i++) c.internal[i] = h_consts151[128 + i];
+    c.diag15 = h_consts151[150];
+    for (uint64_t i = 0; i < n; i++) state_op(op, states + 16 * i, c);
+}
+
+}  // extern "C"

@@ -173,7 +173,7 @@ def test_commit_sweep_sampled(zk, orc, consts, lg_l, lb, w):
     com = zk.commit(m, lb)
     H = 1 << (lg_l + lb)
     rows = [0, 1, 2, H // 2 + 1, H - 1] + [int(x) for x in np.random.default_rng(1).integers(0, H, 3)]
-    lde_rows = com.lde[torch.tensor(rows, device="cuda")].cpu().numpy()
+    lde_rows = com.lde.view(torch.int64)[torch.tensor(rows, device="cuda")].cpu().numpy().view(np.uint64)
     cols = list(range(w)) if w <= 16 else [0, 1, w // 2, w - 1]
     exp = orc.lde_rows(m[:, cols].copy(), rows, H)
     assert np.array_equal(lde_rows[:, cols], exp)

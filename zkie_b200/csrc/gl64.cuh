@@ -8,110 +8,127 @@
 // 13-15: "values stay partially reduced between stages; the final scatter
 // canonicalizes").
 //
-// Carry handling is written with PTX add/sub-with-carry so the 64-bit
-// operations map onto 32-bit carry chains without 128-bit emulation.
+// On the device the carry handling is PTX add/sub-with-carry, so the 64-bit
+// operations map onto 32-bit carry chains without 128-bit emulation.  The
+// same functions compile for the host (portable C), which lets the kernel-side
+// permutation and NTT logic be unit-tested on a CPU.
 #pragma once
 #include <cstdint>
+
+#if defined(__CUDACC__)
+#define ZK_HD __host__ __device__ __forceinline__
+#else
+#define ZK_HD inline
+#endif
 
 namespace zk {
 
 constexpr uint64_t GL_P = 0xFFFFFFFF00000001ull;
 constexpr uint64_t GL_EPS = 0xFFFFFFFFull;  // 2^64 mod p
 
-__device__ __forceinline__ uint64_t gl_canon(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
+ZK_HD uint64_t gl_canon(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
 
-// a + b mod p.  2^64 == EPS, so a carry out of bit 63 is folded back as +EPS;
-// a second carry is only possible when both inputs are >= 2^64 - 2^32.
-__device__ __forceinline__ uint64_t gl_add(uint64_t a, uint64_t b) {
+// s = a + b (mod 2^64) and the carry out of bit 63.
+ZK_HD uint64_t add_carry(uint64_t a, uint64_t b, uint32_t& c) {
+#if defined(__CUDA_ARCH__)
     uint64_t s;
-    uint32_t c;
     asm("add.cc.u64 %0, %2, %3;\n\t"
         "addc.u32 %1, 0, 0;"
         : "=l"(s), "=r"(c)
         : "l"(a), "l"(b));
-    uint64_t fix = (uint64_t)(0u - c) & GL_EPS;  // EPS if carry
-    uint64_t t;
-    asm("add.cc.u64 %0, %2, %3;\n\t"
-        "addc.u32 %1, 0, 0;"
-        : "=l"(t), "=r"(c)
-        : "l"(s), "l"(fix));
-    return t + ((uint64_t)(0u - c) & GL_EPS);
+    return s;
+#else
+    uint64_t s = a + b;
+    c = s < a ? 1u : 0u;
+    return s;
+#endif
+}
+
+// d = a - b (mod 2^64) and the borrow as a mask (0 or 0xFFFFFFFF).
+ZK_HD uint64_t sub_borrow(uint64_t a, uint64_t b, uint32_t& mask) {
+#if defined(__CUDA_ARCH__)
+    uint64_t d;
+    asm("sub.cc.u64 %0, %2, %3;\n\t"
+        "subc.u32 %1, 0, 0;"
+        : "=l"(d), "=r"(mask)
+        : "l"(a), "l"(b));
+    return d;
+#else
+    mask = a < b ? 0xFFFFFFFFu : 0u;
+    return a - b;
+#endif
+}
+
+// a + b mod p.  2^64 == EPS, so a carry out of bit 63 is folded back as +EPS;
+// a second carry is only possible when both inputs are >= 2^64 - 2^32.
+ZK_HD uint64_t gl_add(uint64_t a, uint64_t b) {
+    uint32_t c;
+    uint64_t s = add_carry(a, b, c);
+    s = add_carry(s, (uint64_t)(0u - c) & GL_EPS, c);
+    return s + ((uint64_t)(0u - c) & GL_EPS);
 }
 
 // a + b where b < p (canonical): at most one fold is needed.
-__device__ __forceinline__ uint64_t gl_add_c(uint64_t a, uint64_t b_canon) {
-    uint64_t s;
+ZK_HD uint64_t gl_add_c(uint64_t a, uint64_t b_canon) {
     uint32_t c;
-    asm("add.cc.u64 %0, %2, %3;\n\t"
-        "addc.u32 %1, 0, 0;"
-        : "=l"(s), "=r"(c)
-        : "l"(a), "l"(b_canon));
+    uint64_t s = add_carry(a, b_canon, c);
     return s + ((uint64_t)(0u - c) & GL_EPS);
 }
 
 // a - b mod p.  A borrow means the wrapped result is 2^64 too large, i.e.
 // EPS too large modulo p; a second borrow can only occur for b >= 2^64 - 2^32.
-__device__ __forceinline__ uint64_t gl_sub(uint64_t a, uint64_t b) {
-    uint64_t d;
+ZK_HD uint64_t gl_sub(uint64_t a, uint64_t b) {
     uint32_t br;
-    asm("sub.cc.u64 %0, %2, %3;\n\t"
-        "subc.u32 %1, 0, 0;"
-        : "=l"(d), "=r"(br)
-        : "l"(a), "l"(b));
-    uint64_t fix = (uint64_t)br & GL_EPS;  // br is 0 or 0xFFFFFFFF
-    uint64_t t;
-    asm("sub.cc.u64 %0, %2, %3;\n\t"
-        "subc.u32 %1, 0, 0;"
-        : "=l"(t), "=r"(br)
-        : "l"(d), "l"(fix));
-    return t - ((uint64_t)br & GL_EPS);
+    uint64_t d = sub_borrow(a, b, br);
+    d = sub_borrow(d, (uint64_t)br & GL_EPS, br);
+    return d - ((uint64_t)br & GL_EPS);
 }
 
 // Reduce hi*2^64 + lo.  With hi = hh*2^32 + hl: 2^64 == 2^32 - 1 and
 // 2^96 == -1, so the value is lo - hh + hl*(2^32 - 1).
-__device__ __forceinline__ uint64_t gl_reduce128(uint64_t lo, uint64_t hi) {
-    uint32_t hh = (uint32_t)(hi >> 32);
-    uint32_t hl = (uint32_t)hi;
-    uint64_t t0;
+ZK_HD uint64_t gl_reduce128(uint64_t lo, uint64_t hi) {
+    const uint32_t hh = (uint32_t)(hi >> 32);
+    const uint32_t hl = (uint32_t)hi;
     uint32_t br;
-    asm("sub.cc.u64 %0, %2, %3;\n\t"
-        "subc.u32 %1, 0, 0;"
-        : "=l"(t0), "=r"(br)
-        : "l"(lo), "l"((uint64_t)hh));
-    t0 -= (uint64_t)br & GL_EPS;             // borrow: +p == -EPS (mod 2^64), no underflow
-    uint64_t t1 = ((uint64_t)hl << 32) - hl;  // hl * (2^32 - 1) < 2^64
-    uint64_t t2;
+    uint64_t t0 = sub_borrow(lo, (uint64_t)hh, br);
+    t0 -= (uint64_t)br & GL_EPS;              // borrow: +p == -EPS (mod 2^64), no underflow
+    const uint64_t t1 = ((uint64_t)hl << 32) - hl;  // hl * (2^32 - 1) < 2^64
     uint32_t c;
-    asm("add.cc.u64 %0, %2, %3;\n\t"
-        "addc.u32 %1, 0, 0;"
-        : "=l"(t2), "=r"(c)
-        : "l"(t0), "l"(t1));
+    const uint64_t t2 = add_carry(t0, t1, c);
     return t2 + ((uint64_t)(0u - c) & GL_EPS);  // cannot carry again
 }
 
-__device__ __forceinline__ uint64_t gl_mul(uint64_t a, uint64_t b) {
-    return gl_reduce128(a * b, __umul64hi(a, b));
+ZK_HD uint64_t mul_hi(uint64_t a, uint64_t b) {
+#if defined(__CUDA_ARCH__)
+    return __umul64hi(a, b);
+#else
+    return (uint64_t)(((unsigned __int128)a * b) >> 64);
+#endif
 }
 
-__device__ __forceinline__ uint64_t gl_sqr(uint64_t a) { return gl_mul(a, a); }
+ZK_HD uint64_t gl_mul(uint64_t a, uint64_t b) { return gl_reduce128(a * b, mul_hi(a, b)); }
+
+ZK_HD uint64_t gl_sqr(uint64_t a) { return gl_mul(a, a); }
 
 // x / 2^k mod p for 1 <= k <= 32.  p == 1 (mod 2^k), so with
 // m = (-x) mod 2^k the sum x + m*p is divisible by 2^k and
-// (x + m*p) / 2^k = (x >> k) + [x mod 2^k != 0] + m*2^(64-k) - m*2^(32-k),
-// which is below 2^64 for every x < 2^64.
+// (x + m*p) / 2^k = (x >> k) + [x mod 2^k != 0] + t*(2^32 - 1), t = m*2^(32-k),
+// which is below 2^64 for every x < 2^64.  t < 2^32 is formed as a 32-bit
+// value and widened with one 32x32->64 multiply: the equivalent 64-bit shift
+// form (m << (64-k)) - (m << (32-k)) produced wrong high bits on sm_100a
+// with nvcc 12.9 (caught by tests/test_devcheck.py).
 template <int K>
-__device__ __forceinline__ uint64_t gl_div_pow2(uint64_t x) {
+ZK_HD uint64_t gl_div_pow2(uint64_t x) {
     static_assert(K >= 1 && K <= 32, "k in [1, 32]");
-    const uint64_t mask = (K == 32) ? 0xFFFFFFFFull : ((1ull << K) - 1);
-    uint64_t m = (0ull - x) & mask;
-    uint64_t r = (x >> K) + (m != 0 ? 1ull : 0ull);
-    r += (m << (64 - K)) - (m << (32 - K));
-    return r;
+    const uint32_t mask = (K == 32) ? 0xFFFFFFFFu : ((1u << (K & 31)) - 1u);
+    const uint32_t m = (0u - (uint32_t)x) & mask;
+    const uint32_t t = m << (32 - K);  // K == 32: t = m
+    return (x >> K) + (m != 0u ? 1ull : 0ull) + (uint64_t)t * GL_EPS;
 }
 
-__device__ __forceinline__ uint64_t gl_neg(uint64_t a) { return gl_sub(0, a); }
+ZK_HD uint64_t gl_neg(uint64_t a) { return gl_sub(0, a); }
 
-__device__ __forceinline__ uint64_t gl_pow(uint64_t a, uint64_t e) {
+ZK_HD uint64_t gl_pow(uint64_t a, uint64_t e) {
     uint64_t r = 1;
     while (e) {
         if (e & 1) r = gl_mul(r, a);

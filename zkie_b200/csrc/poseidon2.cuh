@@ -20,7 +20,7 @@ struct P2Const {
     uint64_t diag15;
 };
 
-__device__ __forceinline__ uint64_t p2_sbox(uint64_t x) {
+ZK_HD uint64_t p2_sbox(uint64_t x) {
     uint64_t x2 = gl_sqr(x);
     uint64_t x3 = gl_mul(x2, x);
     uint64_t x4 = gl_sqr(x2);
@@ -28,7 +28,7 @@ __device__ __forceinline__ uint64_t p2_sbox(uint64_t x) {
 }
 
 // [2 3 1 1; 1 2 3 1; 1 1 2 3; 3 1 1 2] on one 4-lane block.
-__device__ __forceinline__ void p2_mat4(uint64_t& x0, uint64_t& x1, uint64_t& x2, uint64_t& x3) {
+ZK_HD void p2_mat4(uint64_t& x0, uint64_t& x1, uint64_t& x2, uint64_t& x3) {
     uint64_t t01 = gl_add(x0, x1);
     uint64_t t23 = gl_add(x2, x3);
     uint64_t t0123 = gl_add(t01, t23);
@@ -43,7 +43,7 @@ __device__ __forceinline__ void p2_mat4(uint64_t& x0, uint64_t& x1, uint64_t& x2
 }
 
 // Light external MDS: 4x4 block on each chunk, then add per-residue column sums.
-__device__ __forceinline__ void p2_mds_light(uint64_t s[16]) {
+ZK_HD void p2_mds_light(uint64_t s[16]) {
 #pragma unroll
     for (int j = 0; j < 16; j += 4) p2_mat4(s[j], s[j + 1], s[j + 2], s[j + 3]);
     uint64_t sum[4];
@@ -56,7 +56,7 @@ __device__ __forceinline__ void p2_mds_light(uint64_t s[16]) {
 // Internal linear layer: s_i <- sum + V_i * s_i with
 // V = [-2, 1, 2, 1/2, 3, 4, -1/2, -3, -4, 1/2^3, 1/2^4, 1/2^5, -1/2^3,
 //      -1/2^4, -1/2^5, diag15] (poseidon2_merkle.cu:111-142).
-__device__ __forceinline__ void p2_internal_linear(uint64_t s[16], uint64_t diag15) {
+ZK_HD void p2_internal_linear(uint64_t s[16], uint64_t diag15) {
     uint64_t sum = s[0];
 #pragma unroll
     for (int i = 1; i < 16; i++) sum = gl_add(sum, s[i]);
@@ -83,7 +83,7 @@ __device__ __forceinline__ void p2_internal_linear(uint64_t s[16], uint64_t diag
     s[15] = gl_add(sum, gl_mul(s[15], diag15));
 }
 
-__device__ __forceinline__ void p2_permute(uint64_t s[16], const P2Const& c) {
+ZK_HD void p2_permute(uint64_t s[16], const P2Const& c) {
     p2_mds_light(s);
 #pragma unroll 1
     for (int r = 0; r < 4; r++) {
