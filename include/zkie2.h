@@ -142,6 +142,25 @@ uint64_t zkie2_sumcheck_scratch_elems(uint32_t t);
 int zkie2_sumcheck_prove(const uint64_t *d_f, const uint64_t *d_h, uint32_t t, const uint64_t *h_ch,
                          uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch,
                          zkie_stream_t stream);
+/* Allocation-free variant of zkie2_sumcheck_prove; it has no counterpart in
+ * the reference.  It is for callers that cannot allocate device memory: a
+ * prover embedded in a process whose framework allocator (PyTorch's caching
+ * allocator, an inference server's pool) has already reserved the GPU's
+ * memory, so a cudaMalloc fails or fragments that pool, and latency-critical
+ * callers that cannot afford the device-wide synchronization cudaFree
+ * implies.  The caller still passes f, h (device), the challenges and the
+ * host outputs; the scratch is a fixed array inside the library (about
+ * 2.4 MB, held on every GPU that loads the library until exit), so this call
+ * allocates nothing.  Limit: t <= zkie2_sumcheck_noalloc_max_vars() (24);
+ * larger t returns cudaErrorInvalidValue.  The first call on a device looks
+ * up the array's device address (once per device), so make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (other threads or streams) race and must be serialized
+ * by the caller.  Synchronous, same outputs as zkie2_sumcheck_prove. */
+uint32_t zkie2_sumcheck_noalloc_max_vars(void);
+int zkie2_sumcheck_prove_noalloc(const uint64_t *d_f, const uint64_t *d_h, uint32_t t,
+                                 const uint64_t *h_ch, uint64_t *h_rounds, uint64_t *h_finals,
+                                 zkie_stream_t stream);
 /* matmul::prove (common/matmul.rs:17-46): d_at = A^T (k x m), d_b (k x n),
  * d_c (m x n), powers of two.  Synchronous. */
 uint64_t zkie2_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n);

@@ -69,6 +69,8 @@ SIGNATURES = {
     "zkie2_mle_eval": (i64, [vp, u32, pu64, pu64, vp, vp]),
     "zkie2_sumcheck_scratch_elems": (u64, [u32]),
     "zkie2_sumcheck_prove": (i64, [vp, vp, u32, pu64, pu64, pu64, vp, vp]),
+    "zkie2_sumcheck_noalloc_max_vars": (u32, []),
+    "zkie2_sumcheck_prove_noalloc": (i64, [vp, vp, u32, pu64, pu64, pu64, vp]),
     "zkie2_matmul_scratch_elems": (u64, [u64, u64, u64]),
     "zkie2_matmul_prove": (i64, [vp, vp, vp, u64, u64, u64, pu64, pu64, pu64, pu64, pu64, pu64, vp, vp]),
     "zkie2_op_matmul_scratch_elems": (u64, [u64, u64, u64]),

@@ -11,6 +11,7 @@
 // MLE evaluation by folding (a + r(b - a) per variable) and by contraction
 // with the equality table (sum_x v[x] eq(r, x)) give the same field element;
 // the contraction form reads each input once and needs no scratch writes.
+#include <mutex>
 #include <vector>
 
 #include "../../include/zkie2.h"
@@ -295,11 +296,12 @@ int eval_dev(const uint64_t* d_values, uint32_t t, const uint64_t* h_point, uint
     return 0;
 }
 
-uint64_t sumcheck_scratch_elems(uint32_t t) {
+constexpr uint64_t sumcheck_scratch_elems_c(uint32_t t) {
     // two folded vectors per launch level (<= 2^(t-11) each) + partials
-    const uint64_t chunks = t > kMaxQ ? (1ull << (t - kMaxQ)) : 1;
-    return 4 * chunks + chunks * kMaxQ * 3 + 64;
+    return 4 * (t > kMaxQ ? (1ull << (t - kMaxQ)) : 1) + (t > kMaxQ ? (1ull << (t - kMaxQ)) : 1) * kMaxQ * 3 + 64;
 }
+
+uint64_t sumcheck_scratch_elems(uint32_t t) { return sumcheck_scratch_elems_c(t); }
 
 // All t rounds of sumcheck::prove on device.  rounds (3t) and finals (2) are
 // written to device memory d_rounds.
@@ -372,4 +374,62 @@ int contract_dev(const uint64_t* v, const uint64_t* eq, uint64_t X, uint64_t Y, 
     return contract(v, eq, X, Y, out, s);
 }
 
+// ---- allocation-free sumcheck ------------------------------------------------------
+// The scratch of zkie2_sumcheck_prove_noalloc lives in this file-scope device
+// array, sized for the largest accepted sumcheck: partial sums and folded
+// vectors of a 2^kNoAllocMaxVars-element f and h, then the round polynomials
+// and the two final values.  Every GPU that loads the library holds it
+// (about 2.4 MB) until the process exits.
+constexpr uint32_t kNoAllocMaxVars = 24;
+constexpr uint64_t kNoAllocScratchElems = sumcheck_scratch_elems_c(kNoAllocMaxVars) + 3ull * kNoAllocMaxVars + 4;
+static __device__ __align__(256) uint64_t g_noalloc_scratch[kNoAllocScratchElems];
+
+namespace {
+std::mutex g_noalloc_mu;
+uint64_t* g_noalloc_ptr[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  In host code the array's name is only a host-side stand-in, so
+// its device address must come from cudaGetSymbolAddress.
+int noalloc_scratch(uint64_t** out) {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[d]) {
+        void* p = nullptr;
+        ZK_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_ptr[d] = static_cast<uint64_t*>(p);
+    }
+    *out = g_noalloc_ptr[d];
+    return 0;
+}
+}  // namespace
+
 }  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+uint32_t zkie2_sumcheck_noalloc_max_vars(void) { return kNoAllocMaxVars; }
+
+int zkie2_sumcheck_prove_noalloc(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uint64_t* h_ch,
+                                 uint64_t* h_rounds, uint64_t* h_finals, cudaStream_t stream) {
+    if (t > kNoAllocMaxVars) return (int)cudaErrorInvalidValue;  // larger than the static scratch
+    if (!d_f || !d_h || !h_finals || (t && (!h_ch || !h_rounds))) return (int)cudaErrorInvalidValue;
+    uint64_t* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // No part of the scratch needs to start at zero: every partial sum and
+    // folded value is written by the launch that precedes its first read.
+    uint64_t* d_rounds = scratch + sumcheck_scratch_elems_c(t);
+    uint64_t* d_finals = d_rounds + 3ull * t;
+    rc = sumcheck_dev(d_f, d_h, t, h_ch, d_rounds, d_finals, scratch, stream);
+    if (rc) return rc;
+    if (t) ZK_TRY(cudaMemcpyAsync(h_rounds, d_rounds, 24ull * t, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaMemcpyAsync(h_finals, d_finals, 16, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaStreamSynchronize(stream));
+    return 0;
+}
+
+}  // extern "C"
