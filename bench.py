@@ -38,6 +38,7 @@ UNIT = "Melem/s"
 P = 0xFFFFFFFF00000001
 LG_L, W, LG_B = 20, 256, 1
 HBM_FALLBACK_GBS = 6650.0
+MULS_PER_PERM = 8 * 16 * 4 + 22 * 4 + 22
 
 
 def workload_config(lg_l, w, lg_b, n_gpus):
@@ -123,7 +124,7 @@ def run_reference(args):
 
 # ---- clocks ------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("timestamp,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
@@ -143,26 +144,38 @@ class ClockSampler:
         self.th.start()
 
     def _read(self):
+        import datetime
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 8:
-                self.rows.append(parts)
+            if len(parts) >= 9:
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    ts = time.time()
+                self.rows.append([ts] + parts[1:])
+
+    def window(self, t0, t1):
+        self.t0, self.t1 = t0, t1
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        mine = [r for r in self.rows if not self.bus or r[0].lower().endswith(self.bus)] or self.rows
-        sm = [float(r[1]) for r in mine if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        mine = [r for r in self.rows if not self.bus or r[1].lower().endswith(self.bus)] or self.rows
+        t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", 1e30)
+        inside = [r for r in mine if t0 - 0.25 <= r[0] <= t1 + 0.25]
+        use = inside or mine
+        sm = [float(r[2]) for r in use if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in use if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in mine for i in range(4) if r[4 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in use for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(mine)}
+                "reasons": reasons, "samples_in_timed_region": len(inside), "samples": len(use)}
 
 
 # ---- GPU side -------------------------------------------------------------------------------------
@@ -180,7 +193,8 @@ def synth_device(n, seed, device):
 
 
 def ntt_passes(lg):
-    return 1 if lg <= 10 else (2 if lg <= 20 else 3)
+    """Launches of k_ntt_pass per LDE (the plan in zkie_b200/csrc/ntt.cu)."""
+    return 1 if lg <= 10 else (2 if lg <= 22 else 3)
 
 
 def main():
@@ -254,11 +268,14 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     sampler.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
+    host_t0 = time.time()
     t_start.record(stream)
     for s in range(args.steps):
         step(evs[s])
     t_end.record(stream)
     torch.cuda.synchronize()
+    sampler.window(host_t0, time.time())
     clocks = sampler.stop()
     if world > 1:
         dist.barrier()
@@ -274,16 +291,24 @@ def main():
     value = world * n_in / (ms_per_step / 1e3) / 1e6
     root = d_layers[-8:].cpu().numpy()
 
-    # permutation ceiling of the same Poseidon2 code: register-resident states, no HBM traffic
-    n_states, reps = 148 * 16 * 128, 16
-    st = synth_device(n_states * 16, 99, dev)
-    check(lib.zkie2_p2_permute(st.data_ptr(), n_states, 1, sh), "permute warmup")
+    # integer-pipe peak: Goldilocks multiplications per second of independent
+    # register-resident chains (no memory traffic), measured on this GPU now
+    n_thr, iters = 148 * 16 * 128, 2048
+    st = synth_device(n_thr * 16, 99, dev)
+    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, 16, sh), "mul probe warmup")
     pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pe0.record(stream)
-    check(lib.zkie2_p2_permute(st.data_ptr(), n_states, reps, sh), "permute")
+    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, iters, sh), "mul probe")
     pe1.record(stream)
     torch.cuda.synchronize()
-    perm_ceiling = n_states * reps / (pe0.elapsed_time(pe1) / 1e3)
+    mul_peak = n_thr * 8 * iters / (pe0.elapsed_time(pe1) / 1e3)
+    # the permutation itself without memory traffic (ceiling of the hash code)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 1, sh), "permute warmup")
+    pe0.record(stream)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 4, sh), "permute")
+    pe1.record(stream)
+    torch.cuda.synchronize()
+    perm_ceiling = n_thr * 4 / (pe0.elapsed_time(pe1) / 1e3)
 
     perms_leaf = H * ((w + 7) // 8)
     leaf_rate = perms_leaf / (leaf_ms / 1e3)
@@ -339,11 +364,14 @@ def main():
         "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Goldilocks mod-p integer)", "data": "synthetic",
         "config": workload_config(lg_l, w, lg_b, world),
         "roofline": {
-            "bound": "int", "kernel": "k_leaf_rows (Poseidon2 leaf sponge, 32 permutations per row)",
-            "achieved": round(leaf_rate / 1e9, 4), "peak": round(perm_ceiling / 1e9, 4), "unit": "Gperm/s",
-            "frac": round(leaf_rate / perm_ceiling, 4), "traffic": None,
-            "peak_source": "measured live: the same permutation code with register-resident states and no memory "
-                           "traffic (zkie2_p2_permute), i.e. the integer-pipe ceiling of this implementation",
+            "bound": "int", "kernel": f"k_leaf_rows (Poseidon2 leaf sponge, {(w + 7) // 8} permutations per row)",
+            "achieved": round(leaf_rate * MULS_PER_PERM / 1e9, 2), "peak": round(mul_peak / 1e9, 2),
+            "unit": "G Goldilocks mul/s", "frac": round(leaf_rate * MULS_PER_PERM / mul_peak, 4), "traffic": None,
+            "work_per_unit": f"{MULS_PER_PERM} field multiplications per Poseidon2-16 permutation "
+                             "(8x16 + 22 S-boxes x^7 at 4 each, 22 diagonal products)",
+            "peak_source": "measured live: zkie2_gl_mul_probe, independent register-resident multiply chains",
+            "perm_rate_gperm_s": round(leaf_rate / 1e9, 4),
+            "perm_ceiling_gperm_s": round(perm_ceiling / 1e9, 4),
             "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
         },
         "roofline_ntt": {

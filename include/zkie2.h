@@ -35,6 +35,10 @@ int zkie2_p2_default_constants(uint64_t seed, uint64_t *rc_init, uint64_t *rc_fi
 int zkie2_p2_init_default(void);
 /* reps full permutations of each of n 16-element states, in place. */
 int zkie2_p2_permute(uint64_t *d_states, uint64_t n, uint32_t reps, zkie_stream_t stream);
+/* Measurement helper: n threads each run 8 independent chains of iters
+ * Goldilocks multiplications on d_buf[16 * i .. 16 * i + 16) (x *= y), in
+ * registers; the peak field-multiplication rate of the integer pipes. */
+int zkie2_gl_mul_probe(uint64_t *d_buf, uint64_t n, uint32_t iters, zkie_stream_t stream);
 
 /* ---- NTT / LDE -------------------------------------------------------------- */
 

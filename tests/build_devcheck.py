@@ -15,6 +15,6 @@ def build() -> str:
         return OUT
     nvcc = "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc"
     subprocess.check_call([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
-                           "-Xcompiler", "-fPIC", "-shared", "--cudart", "static", "-o", OUT + ".tmp", SRC])
+                           "-Xcompiler", "-fPIC", "-shared", "--cudart", "static", "-diag-suppress", "550", "-o", OUT + ".tmp", SRC])
     os.replace(OUT + ".tmp", OUT)
     return OUT

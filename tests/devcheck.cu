@@ -40,13 +40,11 @@ ZK_HD void state_op(int op, uint64_t s[16], const P2Const& c) {
     switch (op) {
         case 100: p2_mds_light(s); break;
         case 101:
-            for (int i = 0; i < 16; i++) s[i] = p2_sbox(gl_add_c(s[i], c.ext_init[0][i]));
-            p2_mds_light(s);
+            p2_external_round(s, c.ext[0]);
             break;
         case 102: p2_internal_linear(s, c.diag15); break;
         case 103:
-            s[0] = p2_sbox(gl_add_c(s[0], c.internal[0]));
-            p2_internal_linear(s, c.diag15);
+            p2_internal_round(s, c.internal[0], c.diag15);
             break;
         case 104: p2_permute(s, c); break;
         case 105: {
@@ -89,8 +87,8 @@ int devcheck_state(int op, uint64_t* d_states, uint64_t n, const uint64_t* h_con
     P2Const c;
     for (int r = 0; r < 4; r++)
         for (int i = 0; i < 16; i++) {
-            c.ext_init[r][i] = h_consts151[r * 16 + i];
-            c.ext_final[r][i] = h_consts151[64 + r * 16 + i];
+            c.ext[r][i] = h_consts151[r * 16 + i];
+            c.ext[4 + r][i] = h_consts151[64 + r * 16 + i];
         }
     for (int i = 0; i < 22; i++) c.internal[i] = h_consts151[128 + i];
     c.diag15 = h_consts151[150];
@@ -109,8 +107,8 @@ void hostcheck_state(int op, uint64_t* states, uint64_t n, const uint64_t* h_con
     P2Const c;
     for (int r = 0; r < 4; r++)
         for (int i = 0; i < 16; i++) {
-            c.ext_init[r][i] = h_consts151[r * 16 + i];
-            c.ext_final[r][i] = h_consts151[64 + r * 16 + i];
+            c.ext[r][i] = h_consts151[r * 16 + i];
+            c.ext[4 + r][i] = h_consts151[64 + r * 16 + i];
         }
     for (int i = 0; i < 22; i++) c.internal[i] = h_consts151[128 + i];
     c.diag15 = h_consts151[150];

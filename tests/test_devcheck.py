@@ -29,6 +29,10 @@ def dc():
     return lib
 
 
+def _canon(a):
+    return np.where(a >= np.uint64(P), a - np.uint64(P), a)
+
+
 def _p(a):
     return a.ctypes.data_as(C.POINTER(C.c_uint64))
 
@@ -99,6 +103,10 @@ def test_device_scalar_ops_match_host(dc):
         hout = np.zeros_like(a)
         dc.hostcheck_scalar(op, _p(a), _p(b), _p(hout), a.size)
         got = dout.cpu().numpy()
+        if op not in (10, 12):
+            # partially reduced results: the device and host builds may pick
+            # different representatives of the same residue
+            got, hout = _canon(got), _canon(hout)
         if not np.array_equal(got, hout):
             i = int(np.nonzero(got != hout)[0][0])
             bad.append(f"{name}: a={hex(int(a[i]))} b={hex(int(b[i]))} dev={hex(int(got[i]))} host={hex(int(hout[i]))}")
@@ -117,7 +125,8 @@ def test_device_state_ops_match_host(dc, orc):
         assert dc.devcheck_state(op, d.data_ptr(), 512, _p(c)) == 0
         h = st.copy()
         dc.hostcheck_state(op, _p(h), 512, _p(c))
-        got = d.cpu().numpy()
+        got = _canon(d.cpu().numpy())
+        h = _canon(h)
         if not np.array_equal(got, h):
             rows = np.nonzero((got != h).any(axis=1))[0]
             bad.append(f"{name}: {rows.size} states differ, first {int(rows[0])}")

@@ -40,6 +40,7 @@ SIGNATURES = {
     "zkie2_p2_default_constants": (i64, [u64, pu64, pu64, pu64, pu64]),
     "zkie2_p2_init_default": (i64, []),
     "zkie2_p2_permute": (i64, [vp, u64, u32, vp]),
+    "zkie2_gl_mul_probe": (i64, [vp, u64, u32, vp]),
     "zkie2_lde_scratch_elems": (u64, [u32, u32, u64]),
     "zkie2_lde": (i64, [vp, vp, vp, u32, u32, u64, vp]),
     "zkie2_dft_twiddles": (i64, [u32, pu64]),

@@ -18,7 +18,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libzkie_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
+NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-diag-suppress", "550",
                      "--expt-relaxed-constexpr", "-I" + INCLUDE]
 
 

@@ -59,8 +59,13 @@ ZK_HD uint64_t sub_borrow(uint64_t a, uint64_t b, uint32_t& mask) {
 #endif
 }
 
+ZK_HD uint64_t pack64(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+
 // a + b mod p.  2^64 == EPS, so a carry out of bit 63 is folded back as +EPS;
 // a second carry is only possible when both inputs are >= 2^64 - 2^32.
+// (Measured on sm_100a: this carry-mask form issues fewer instructions than
+// folding the carry with multiply-adds or leaving the carries to the
+// compiler.)
 ZK_HD uint64_t gl_add(uint64_t a, uint64_t b) {
     uint32_t c;
     uint64_t s = add_carry(a, b, c);
@@ -71,7 +76,7 @@ ZK_HD uint64_t gl_add(uint64_t a, uint64_t b) {
 // a + b where b < p (canonical): at most one fold is needed.
 ZK_HD uint64_t gl_add_c(uint64_t a, uint64_t b_canon) {
     uint32_t c;
-    uint64_t s = add_carry(a, b_canon, c);
+    const uint64_t s = add_carry(a, b_canon, c);
     return s + ((uint64_t)(0u - c) & GL_EPS);
 }
 
@@ -84,6 +89,17 @@ ZK_HD uint64_t gl_sub(uint64_t a, uint64_t b) {
     return d - ((uint64_t)br & GL_EPS);
 }
 
+// 32 x 32 -> 64 product (one wide IMAD on the device).
+ZK_HD uint64_t mul_wide32(uint32_t a, uint32_t b) {
+#if defined(__CUDA_ARCH__)
+    uint64_t r;
+    asm("mul.wide.u32 %0, %1, %2;" : "=l"(r) : "r"(a), "r"(b));
+    return r;
+#else
+    return (uint64_t)a * b;
+#endif
+}
+
 // Reduce hi*2^64 + lo.  With hi = hh*2^32 + hl: 2^64 == 2^32 - 1 and
 // 2^96 == -1, so the value is lo - hh + hl*(2^32 - 1).
 ZK_HD uint64_t gl_reduce128(uint64_t lo, uint64_t hi) {
@@ -91,22 +107,102 @@ ZK_HD uint64_t gl_reduce128(uint64_t lo, uint64_t hi) {
     const uint32_t hl = (uint32_t)hi;
     uint32_t br;
     uint64_t t0 = sub_borrow(lo, (uint64_t)hh, br);
-    t0 -= (uint64_t)br & GL_EPS;              // borrow: +p == -EPS (mod 2^64), no underflow
-    const uint64_t t1 = ((uint64_t)hl << 32) - hl;  // hl * (2^32 - 1) < 2^64
+    t0 -= (uint64_t)br & GL_EPS;                      // borrow: +p == -EPS (mod 2^64), no underflow
+    const uint64_t t1 = mul_wide32(hl, 0xFFFFFFFFu);  // hl * (2^32 - 1) < 2^64
     uint32_t c;
     const uint64_t t2 = add_carry(t0, t1, c);
     return t2 + ((uint64_t)(0u - c) & GL_EPS);  // cannot carry again
 }
 
-ZK_HD uint64_t mul_hi(uint64_t a, uint64_t b) {
+// Full 64 x 64 -> 128 product.  On the device: schoolbook over 32-bit limbs
+// as one multiply-add carry chain (the integer-multiply pipe does nearly all
+// of it, leaving the ALU pipe to the additions).
+ZK_HD void mul_wide64(uint64_t a, uint64_t b, uint64_t& lo, uint64_t& hi) {
 #if defined(__CUDA_ARCH__)
-    return __umul64hi(a, b);
+    const uint32_t a0 = (uint32_t)a, a1 = (uint32_t)(a >> 32);
+    const uint32_t b0 = (uint32_t)b, b1 = (uint32_t)(b >> 32);
+    uint32_t r0, r1, r2, r3;
+    asm("mul.lo.u32     %0, %4, %6;\n\t"
+        "mul.hi.u32     %1, %4, %6;\n\t"
+        "mad.lo.cc.u32  %1, %4, %7, %1;\n\t"
+        "madc.hi.u32    %2, %4, %7, 0;\n\t"
+        "mad.lo.cc.u32  %1, %5, %6, %1;\n\t"
+        "madc.hi.cc.u32 %2, %5, %6, %2;\n\t"
+        "madc.hi.u32    %3, %5, %7, 0;\n\t"
+        "mad.lo.cc.u32  %2, %5, %7, %2;\n\t"
+        "addc.u32       %3, %3, 0;"
+        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+        : "r"(a0), "r"(a1), "r"(b0), "r"(b1));
+    lo = ((uint64_t)r1 << 32) | r0;
+    hi = ((uint64_t)r3 << 32) | r2;
 #else
-    return (uint64_t)(((unsigned __int128)a * b) >> 64);
+    const unsigned __int128 p = (unsigned __int128)a * b;
+    lo = (uint64_t)p;
+    hi = (uint64_t)(p >> 64);
 #endif
 }
 
-ZK_HD uint64_t gl_mul(uint64_t a, uint64_t b) { return gl_reduce128(a * b, mul_hi(a, b)); }
+ZK_HD uint64_t mul_hi(uint64_t a, uint64_t b) {
+    uint64_t lo, hi;
+    mul_wide64(a, b, lo, hi);
+    return hi;
+}
+
+ZK_HD uint64_t gl_mul(uint64_t a, uint64_t b) {
+    uint64_t lo, hi;
+    mul_wide64(a, b, lo, hi);
+    return gl_reduce128(lo, hi);
+}
+
+// ---- lazy accumulation ---------------------------------------------------------------
+// A non-negative integer below 2^96 held as lo + hi * 2^64.  Sums of a few
+// dozen partially reduced elements fit; each addition is a 3-instruction
+// carry chain instead of a modular add, and the sum is reduced once.
+struct Acc {
+    uint64_t lo;
+    uint32_t hi;
+};
+
+ZK_HD Acc acc_of(uint64_t x) { return Acc{x, 0u}; }
+
+// a + x
+ZK_HD Acc acc_add(Acc a, uint64_t x) {
+#if defined(__CUDA_ARCH__)
+    asm("add.cc.u64 %0, %0, %2;\n\t"
+        "addc.u32 %1, %1, 0;"
+        : "+l"(a.lo), "+r"(a.hi)
+        : "l"(x));
+    return a;
+#else
+    const uint64_t s = a.lo + x;
+    return Acc{s, a.hi + (s < x ? 1u : 0u)};
+#endif
+}
+
+// a + b
+ZK_HD Acc acc_add(Acc a, Acc b) {
+#if defined(__CUDA_ARCH__)
+    asm("add.cc.u64 %0, %0, %2;\n\t"
+        "addc.u32 %1, %1, %3;"
+        : "+l"(a.lo), "+r"(a.hi)
+        : "l"(b.lo), "r"(b.hi));
+    return a;
+#else
+    const uint64_t s = a.lo + b.lo;
+    return Acc{s, a.hi + b.hi + (s < b.lo ? 1u : 0u)};
+#endif
+}
+
+// x + y of two partially reduced elements, as an accumulator
+ZK_HD Acc acc_sum(uint64_t x, uint64_t y) { return acc_add(acc_of(x), y); }
+
+// lo + hi * 2^64 == lo + hi * (2^32 - 1) (mod p); hi * (2^32 - 1) < 2^64 and
+// after a carry the sum is below hi * (2^32 - 1), so one fold suffices.
+ZK_HD uint64_t acc_reduce(Acc a) {
+    uint32_t c;
+    const uint64_t s = add_carry(a.lo, mul_wide32(a.hi, 0xFFFFFFFFu), c);
+    return s + ((uint64_t)(0u - c) & GL_EPS);
+}
 
 ZK_HD uint64_t gl_sqr(uint64_t a) { return gl_mul(a, a); }
 

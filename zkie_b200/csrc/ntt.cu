@@ -92,94 +92,125 @@ __device__ __forceinline__ uint32_t brev_m(uint32_t j, uint32_t m) { return m ? 
 
 constexpr int kNttThreads = 256;
 
-template <bool kCallerTab>
+// IdxT: uint32_t when every element offset of the matrices fits in 32 bits
+// (fewer integer instructions for the address arithmetic), else uint64_t.
+template <bool kCallerTab, typename IdxT>
 __global__ void __launch_bounds__(kNttThreads) k_ntt_pass(PassDesc d) {
     extern __shared__ uint64_t sm[];
-    const uint32_t M = 1u << d.m;
-    const uint32_t C = 1u << d.logC, R = 1u << d.logR;
-    const uint32_t LW = C * R;
-    const uint32_t logLW = d.logC + d.logR;
-    uint64_t* data = sm;                       // [M][LW]
-    uint64_t* tws = sm + (uint64_t)M * LW;     // [M/2] powers of W_M
+    const uint32_t m = d.m, M = 1u << m;
+    const uint32_t logC = d.logC, logR = d.logR, logLW = logC + logR;
+    const uint32_t C = 1u << logC, LW = 1u << logLW;
+    uint64_t* data = sm;                         // [M][LW], row-major
+    uint64_t* tws = sm + ((size_t)M << logLW);   // [M/2] powers of W_M
 
-    const uint64_t tiles_f = d.F >> d.logR;
-    const uint64_t tile = blockIdx.x;
-    const uint64_t s_idx = tile / tiles_f;
-    const uint64_t f0 = (tile % tiles_f) << d.logR;
-    const uint64_t c0 = (uint64_t)blockIdx.y << d.logC;
-    const uint64_t ccur = (d.w - c0) < C ? (d.w - c0) : C;
+    const uint64_t tiles_f = d.F >> logR;
+    const uint64_t s_idx = blockIdx.x / tiles_f;
+    const uint64_t f0 = (blockIdx.x % tiles_f) << logR;
+    const uint64_t c0 = (uint64_t)blockIdx.y << logC;
+    const uint32_t ccur = (d.w - c0) < C ? (uint32_t)(d.w - c0) : C;
     const uint32_t tid = threadIdx.x;
 
-    for (uint32_t i = tid; i < M / 2; i += kNttThreads) tws[i] = root_pow<kCallerTab>(d, d.m, i);
+    for (uint32_t i = tid; i < M / 2; i += kNttThreads) tws[i] = root_pow<kCallerTab>(d, m, i);
 
-    const uint64_t sbase_in = s_idx * d.sin;
+    // ---- load: element (j, lane fl, column c) of the tile is input row
+    // (f0 + fl)*fin + s*sin + j*jin; stored at the bit-reversed position of j.
     const uint32_t total = M << logLW;
-    if (d.jin == 1) {
-        // j is the contiguous direction: c fastest, then j, then lane.
-        for (uint32_t idx = tid; idx < total; idx += kNttThreads) {
-            const uint32_t c = idx & (C - 1);
-            const uint32_t j = (idx >> d.logC) & (M - 1);
-            const uint32_t fl = idx >> (d.logC + d.m);
-            const uint64_t row = (f0 + fl) * d.fin + sbase_in + j;
+    // Each thread keeps one column c of the tile and walks the (lane, j) pairs.
+    const uint32_t c = tid & (C - 1);
+    const bool cok = c < ccur;
+    const uint32_t nq = total >> logC, qstep = kNttThreads >> logC;
+    const IdxT w = (IdxT)d.w;
+    {
+        const IdxT row0 = (IdxT)(f0 * d.fin + s_idx * d.sin);
+        const IdxT fin = (IdxT)d.fin, jin = (IdxT)d.jin;
+        const IdxT rows_valid = (IdxT)(d.rows_valid < (uint64_t)(IdxT)~(IdxT)0 ? d.rows_valid : (uint64_t)(IdxT)~(IdxT)0);
+        const uint64_t* gin = d.in + c0 + c;
+        const bool lane_major = d.jin != 1;  // consecutive lanes are consecutive rows
+        for (uint32_t q = tid >> logC; q < nq; q += qstep) {
+            uint32_t fl, j;
+            if (lane_major) {
+                fl = q & ((1u << logR) - 1);
+                j = q >> logR;
+            } else {
+                j = q & (M - 1);
+                fl = q >> m;
+            }
+            const IdxT row = row0 + (IdxT)fl * fin + (IdxT)j * jin;
             uint64_t v = 0;
-            if (row < d.rows_valid && c < ccur) v = __ldg(d.in + row * d.w + c0 + c);
-            data[((uint64_t)brev_m(j, d.m) << logLW) + (fl << d.logC) + c] = v;
-        }
-    } else {
-        // lanes are the contiguous direction: c fastest, then lane, then j.
-        for (uint32_t idx = tid; idx < total; idx += kNttThreads) {
-            const uint32_t c = idx & (C - 1);
-            const uint32_t fl = (idx >> d.logC) & (R - 1);
-            const uint32_t j = idx >> logLW;
-            const uint64_t row = (f0 + fl) * d.fin + sbase_in + (uint64_t)j * d.jin;
-            uint64_t v = 0;
-            if (row < d.rows_valid && c < ccur) v = __ldg(d.in + row * d.w + c0 + c);
-            data[((uint64_t)brev_m(j, d.m) << logLW) + (fl << d.logC) + c] = v;
+            if (cok && row < rows_valid) v = __ldg(gin + row * w);
+            data[(brev_m(j, m) << logLW) | (fl << logC) | c] = v;
         }
     }
     __syncthreads();
 
-    // Radix-2 DIT stages on bit-reversed input -> natural-order output.
-    const uint32_t nbf = (M / 2) << logLW;
-    for (uint32_t s = 1; s <= d.m; s++) {
+    // ---- DIT stages on bit-reversed input -> natural order.  Stage s pairs
+    // rows at distance 2^(s-1) with twiddle W_{2^s}^(i mod 2^(s-1)).  Stages
+    // run two at a time as radix-4 groups in registers (one shared-memory
+    // round trip and one barrier per two stages); an odd first stage, whose
+    // twiddle is 1, runs alone.
+    uint32_t s = 1;
+    if (m & 1) {
+        const uint32_t nb = (M / 2) << logLW;
+        for (uint32_t b = tid; b < nb; b += kNttThreads) {
+            uint64_t* p = data + (((b >> logLW) << 1) << logLW) + (b & (LW - 1));
+            const uint64_t u = p[0], v = p[LW];
+            p[0] = gl_add(u, v);
+            p[LW] = gl_sub(u, v);
+        }
+        s = 2;
+        __syncthreads();
+    }
+    for (; s < m; s += 2) {
         const uint32_t hb = s - 1;
-        for (uint32_t b = tid; b < nbf; b += kNttThreads) {
-            const uint32_t lane = b & (LW - 1);
-            const uint32_t bb = b >> logLW;
-            const uint32_t jj = bb & ((1u << hb) - 1);
-            const uint32_t i = ((bb >> hb) << s) | jj;
-            const uint64_t tw = tws[jj << (d.m - s)];
-            uint64_t* p = data + ((uint64_t)i << logLW) + lane;
-            uint64_t* q = p + ((uint64_t)1 << (hb + logLW));
-            const uint64_t u = *p;
-            const uint64_t v = gl_mul(*q, tw);
-            *p = gl_add(u, v);
-            *q = gl_sub(u, v);
+        const uint32_t h = 1u << hb;
+        const uint32_t hs = h << logLW;  // distance between the group's rows, in elements
+        const uint32_t nq = (M / 4) << logLW;
+        for (uint32_t g = tid; g < nq; g += kNttThreads) {
+            const uint32_t gg = g >> logLW;
+            const uint32_t j0 = gg & (h - 1);
+            const uint32_t i0 = ((gg >> hb) << (s + 1)) | j0;
+            uint64_t* p = data + (i0 << logLW) + (g & (LW - 1));
+            const uint64_t e0 = p[0], e1 = p[hs], e2 = p[2 * hs], e3 = p[3 * hs];
+            const uint64_t w1 = tws[j0 << (m - s)];             // W_{2^s}^j0
+            const uint64_t w2 = tws[j0 << (m - s - 1)];         // W_{2^(s+1)}^j0
+            const uint64_t w3 = tws[(j0 + h) << (m - s - 1)];   // W_{2^(s+1)}^(j0 + h)
+            uint64_t t = gl_mul(e1, w1);
+            const uint64_t a0 = gl_add(e0, t), a1 = gl_sub(e0, t);
+            t = gl_mul(e3, w1);
+            const uint64_t a2 = gl_add(e2, t), a3 = gl_sub(e2, t);
+            t = gl_mul(a2, w2);
+            p[0] = gl_add(a0, t);
+            p[2 * hs] = gl_sub(a0, t);
+            t = gl_mul(a3, w3);
+            p[hs] = gl_add(a1, t);
+            p[3 * hs] = gl_sub(a1, t);
         }
         __syncthreads();
     }
 
-    const uint64_t sbase_out = s_idx * d.sout;
-    // Outputs: lanes contiguous (fout == 1) -> c fastest, then lane, then k.
-    for (uint32_t idx = tid; idx < total; idx += kNttThreads) {
-        uint32_t c, fl, k;
-        if (d.fout == 1) {
-            c = idx & (C - 1);
-            fl = (idx >> d.logC) & (R - 1);
-            k = idx >> logLW;
-        } else {
-            c = idx & (C - 1);
-            k = (idx >> d.logC) & (M - 1);
-            fl = idx >> (d.logC + d.m);
+    // ---- store: output k of lane fl goes to row (f0 + fl)*fout + s*sout + k*kout,
+    // after the inter-pass twiddle W_{2^tw_log}^((f0 + fl) * k).
+    {
+        const IdxT row0 = (IdxT)(f0 * d.fout + s_idx * d.sout);
+        const IdxT fout = (IdxT)d.fout, kout = (IdxT)d.kout;
+        uint64_t* gout = d.out + c0 + c;
+        const uint64_t emask = (1ull << d.tw_log) - 1;
+        const bool lane_major = d.fout == 1;
+        for (uint32_t q = tid >> logC; q < nq; q += qstep) {
+            uint32_t fl, k;
+            if (lane_major) {
+                fl = q & ((1u << logR) - 1);
+                k = q >> logR;
+            } else {
+                k = q & (M - 1);
+                fl = q >> m;
+            }
+            uint64_t v = data[(k << logLW) | (fl << logC) | c];
+            if (d.tw_log) v = gl_mul(v, root_pow<kCallerTab>(d, d.tw_log, ((f0 + fl) * k) & emask));
+            if (d.canon) v = gl_canon(v);
+            const IdxT row = row0 + (IdxT)fl * fout + (IdxT)k * kout;
+            if (cok) gout[row * w] = v;
         }
-        uint64_t v = data[((uint64_t)k << logLW) + (fl << d.logC) + c];
-        if (d.tw_log) {
-            const uint64_t e = ((f0 + fl) * (uint64_t)k) & ((1ull << d.tw_log) - 1);
-            v = gl_mul(v, root_pow<kCallerTab>(d, d.tw_log, e));
-        }
-        if (d.canon) v = gl_canon(v);
-        const uint64_t row = (f0 + fl) * d.fout + sbase_out + (uint64_t)k * d.kout;
-        if (c < ccur) d.out[row * d.w + c0 + c] = v;
     }
 }
 
@@ -190,15 +221,15 @@ uint32_t floor_log2(uint64_t x) {
 }
 
 // Tile width (C * R) for a sub-DFT of 2^m rows: keep M * C * R * 8 bytes
-// around 64 KB of shared memory, between 8 and 32 u64 per row chunk.
+// around 64 KB of shared memory, between 4 and 32 u64 per row chunk.
 uint32_t tile_log_width(uint32_t m) {
     int lw = 13 - (int)m;
-    if (lw < 3) lw = 3;
+    if (lw < 2) lw = 2;
     if (lw > 5) lw = 5;
     return (uint32_t)lw;
 }
 
-template <bool kCallerTab>
+template <bool kCallerTab, typename IdxT>
 int run_pass(PassDesc d, uint64_t S, cudaStream_t s) {
     const uint32_t logLW = tile_log_width(d.m);
     uint32_t logC = floor_log2(d.w);
@@ -213,18 +244,18 @@ int run_pass(PassDesc d, uint64_t S, cudaStream_t s) {
     if (tiles > 0x7FFFFFFFull || cblocks > 65535) return (int)cudaErrorInvalidConfiguration;
     const size_t smem = 8ull * (((uint64_t)1 << d.m) << (logC + logR)) + 8ull * ((1ull << d.m) / 2);
     if (smem > 48 * 1024)
-        ZK_TRY(cudaFuncSetAttribute(k_ntt_pass<kCallerTab>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        ZK_TRY(cudaFuncSetAttribute(k_ntt_pass<kCallerTab, IdxT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem));
     dim3 grid((unsigned)tiles, (unsigned)cblocks);
-    k_ntt_pass<kCallerTab><<<grid, kNttThreads, smem, s>>>(d);
+    k_ntt_pass<kCallerTab, IdxT><<<grid, kNttThreads, smem, s>>>(d);
     ZK_LAUNCH_CHECK();
     return 0;
 }
 
 // Full transform of size 2^lg over the columns of `in` (rows >= rows_valid
 // are zero) into `out`, using `scratch` (2^lg * w u64) between passes.
-template <bool kCallerTab>
-int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w,
+template <bool kCallerTab, typename IdxT>
+int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w,
              uint64_t rows_valid, const uint64_t* tab, uint32_t tab_log, cudaStream_t s) {
     PassDesc base{};
     base.w = w;
@@ -241,24 +272,24 @@ int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, 
         d.m = lg;
         d.tw_log = 0;
         d.canon = 1;
-        return run_pass<kCallerTab>(d, 1, s);
+        return run_pass<kCallerTab, IdxT>(d, 1, s);
     }
-    if (lg <= 20) {
-        const uint32_t a = (lg + 1) / 2, b = lg - a;  // N1 = 2^a, N2 = 2^b
+    if (lg <= 22) {
+        const uint32_t a = (lg + 1) / 2, b = lg - a;  // N1 = 2^a, N2 = 2^b (<= 2^11 each)
         const uint64_t N1 = 1ull << a, N2 = 1ull << b;
         PassDesc A = base;
         A.in = in; A.out = scratch; A.rows_valid = rows_valid;
         A.F = N2; A.fin = 1; A.sin = 0; A.jin = N2;
         A.fout = 1; A.sout = 0; A.kout = N2;
         A.m = a; A.tw_log = lg; A.canon = 0;
-        int rc = run_pass<kCallerTab>(A, 1, s);
+        int rc = run_pass<kCallerTab, IdxT>(A, 1, s);
         if (rc) return rc;
         PassDesc B = base;
         B.in = scratch; B.out = out; B.rows_valid = ~0ull;
         B.F = N1; B.fin = N2; B.sin = 0; B.jin = 1;
         B.fout = 1; B.sout = 0; B.kout = N1;
         B.m = b; B.tw_log = 0; B.canon = 1;
-        return run_pass<kCallerTab>(B, 1, s);
+        return run_pass<kCallerTab, IdxT>(B, 1, s);
     }
     if (lg <= 30) {
         const uint32_t a = (lg + 2) / 3, rest = lg - a, b = (rest + 1) / 2, c = rest - b;
@@ -268,23 +299,32 @@ int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, 
         A.F = N23; A.fin = 1; A.sin = 0; A.jin = N23;
         A.fout = 1; A.sout = 0; A.kout = N23;
         A.m = a; A.tw_log = lg; A.canon = 0;
-        int rc = run_pass<kCallerTab>(A, 1, s);
+        int rc = run_pass<kCallerTab, IdxT>(A, 1, s);
         if (rc) return rc;
         PassDesc B1 = base;
         B1.in = scratch; B1.out = scratch; B1.rows_valid = ~0ull;
         B1.F = N3; B1.fin = 1; B1.sin = N23; B1.jin = N3;
         B1.fout = 1; B1.sout = N23; B1.kout = N3;
         B1.m = b; B1.tw_log = b + c; B1.canon = 0;
-        rc = run_pass<kCallerTab>(B1, N1, s);
+        rc = run_pass<kCallerTab, IdxT>(B1, N1, s);
         if (rc) return rc;
         PassDesc B2 = base;
         B2.in = scratch; B2.out = out; B2.rows_valid = ~0ull;
         B2.F = N1; B2.fin = N23; B2.sin = N3; B2.jin = 1;
         B2.fout = 1; B2.sout = N1; B2.kout = N1 * N2;
         B2.m = c; B2.tw_log = 0; B2.canon = 1;
-        return run_pass<kCallerTab>(B2, N2, s);
+        return run_pass<kCallerTab, IdxT>(B2, N2, s);
     }
     return (int)cudaErrorInvalidValue;
+}
+
+template <bool kCallerTab>
+int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w,
+             uint64_t rows_valid, const uint64_t* tab, uint32_t tab_log, cudaStream_t s) {
+    // 32-bit offsets when the whole 2^lg x w matrix is addressable with them
+    if (lg < 32 && (w << lg) < (1ull << 32))
+        return dft_plan_t<kCallerTab, uint32_t>(in, out, scratch, lg, w, rows_valid, tab, tab_log, s);
+    return dft_plan_t<kCallerTab, uint64_t>(in, out, scratch, lg, w, rows_valid, tab, tab_log, s);
 }
 
 }  // namespace

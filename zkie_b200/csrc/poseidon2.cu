@@ -110,6 +110,27 @@ __global__ void __launch_bounds__(kHashThreads)
     for (int q = 0; q < 16; q++) states[i * 16 + q] = gl_canon(s[q]);
 }
 
+// Peak Goldilocks multiplication throughput: 8 independent multiply chains
+// per thread in registers, no memory traffic in the loop.  The measured rate
+// is the denominator of the hashing kernels' integer roofline.
+__global__ void __launch_bounds__(kHashThreads) k_gl_mul_probe(uint64_t* __restrict__ buf, uint64_t n,
+                                                              uint32_t iters) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t x[8], y[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        x[q] = buf[i * 16 + q];
+        y[q] = buf[i * 16 + 8 + q];
+    }
+    for (uint32_t it = 0; it < iters; it++) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) x[q] = gl_mul(x[q], y[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) buf[i * 16 + q] = gl_canon(x[q]);
+}
+
 uint64_t canon_host(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
 
 }  // namespace
@@ -127,8 +148,8 @@ int p2_upload(const uint64_t* rc_init, const uint64_t* rc_final, const uint64_t*
     P2Const h;
     for (int r = 0; r < 4; r++)
         for (int i = 0; i < 16; i++) {
-            h.ext_init[r][i] = canon_host(rc_init[r * 16 + i]);
-            h.ext_final[r][i] = canon_host(rc_final[r * 16 + i]);
+            h.ext[r][i] = canon_host(rc_init[r * 16 + i]);
+            h.ext[4 + r][i] = canon_host(rc_final[r * 16 + i]);
         }
     for (int r = 0; r < 22; r++) h.internal[r] = canon_host(rc_internal[r]);
     h.diag15 = canon_host(diag15);
@@ -279,6 +300,14 @@ int zkie2_p2_permute(uint64_t* d_states, uint64_t n, uint32_t reps, cudaStream_t
     if (!d_states) return (int)cudaErrorInvalidValue;
     if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
     k_permute<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, stream>>>(d_states, n, reps);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_gl_mul_probe(uint64_t* d_buf, uint64_t n, uint32_t iters, cudaStream_t stream) {
+    if (n == 0) return 0;
+    if (!d_buf) return (int)cudaErrorInvalidValue;
+    k_gl_mul_probe<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, stream>>>(d_buf, n, iters);
     ZK_LAUNCH_CHECK();
     return 0;
 }
