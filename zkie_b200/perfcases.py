@@ -1,0 +1,146 @@
+"""Timed cases for the kernel families of libzkie_b200 (used for profiling).
+
+    python -m zkie_b200.perfcases sumcheck --log-size 24
+    python -m zkie_b200.perfcases mle --log-size 24
+    python -m zkie_b200.perfcases matmul --m 512 --k 1024 --n 4096
+    python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
+
+Each case prints one JSON line: device time per call (CUDA events on the
+launching stream, after warm-up) and the algorithmic HBM bytes per call.
+Inputs are synthetic, uniform canonical field elements.
+"""
+import argparse
+import json
+import sys
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+P = 0xFFFFFFFF00000001
+
+
+def _rand(n, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    hi = torch.randint(0, 1 << 32, (n,), generator=g, device="cuda", dtype=torch.int64)
+    lo = torch.randint(0, 1 << 32, (n,), generator=g, device="cuda", dtype=torch.int64)
+    x = (hi << 32) | lo
+    x = torch.where((x < 0) & (x >= -(1 << 32) + 1), x + ((1 << 32) - 1), x)
+    return x.view(torch.uint64)
+
+
+def _time(fn, iters, warmup=2):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def _p(a):
+    return a.ctypes.data_as(_lib.pu64)
+
+
+def case_sumcheck(a):
+    t = a.log_size
+    f, h = _rand(1 << t, 1), _rand(1 << t, 2)
+    ch = np.arange(1, t + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15 % P)
+    rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+    finals = np.zeros(2, dtype=np.uint64)
+    scr = torch.empty(lib.zkie2_sumcheck_scratch_elems(t), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        check(lib.zkie2_sumcheck_prove(f.data_ptr(), h.data_ptr(), t, _p(ch), _p(rounds), _p(finals),
+                                       scr.data_ptr(), st), "sumcheck")
+    ms = _time(run, a.iters)
+    return {"case": "sumcheck", "log_size": t, "ms": ms, "bytes": 16 << t,
+            "gbs": (16 << t) / (ms / 1e3) / 1e9}
+
+
+def case_mle(a):
+    t = a.log_size
+    v = _rand(1 << t, 3)
+    pt = (np.arange(1, t + 1, dtype=np.uint64) * np.uint64(12345)).astype(np.uint64)
+    out = _lib.u64(0)
+    scr = torch.empty(lib.zkie2_mle_scratch_elems(t), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    import ctypes as C
+
+    def run():
+        check(lib.zkie2_mle_eval(v.data_ptr(), t, _p(pt), C.byref(out), scr.data_ptr(), st), "mle_eval")
+    ms = _time(run, a.iters)
+    return {"case": "mle_eval", "log_size": t, "ms": ms, "bytes": 8 << t, "gbs": (8 << t) / (ms / 1e3) / 1e9}
+
+
+def case_matmul(a):
+    m, k, n = a.m, a.k, a.n
+    A, B, Cm = _rand(m * k, 4), _rand(k * n, 5), _rand(m * n, 6)
+    scr = torch.empty(lib.zkie2_op_matmul_scratch_elems(m, k, n), dtype=torch.uint64, device="cuda")
+    lm, lk, ln = m.bit_length() - 1, k.bit_length() - 1, n.bit_length() - 1
+    outs = [np.zeros(max(x, 1), dtype=np.uint64) for x in (lm, ln, lk)]
+    rounds = np.zeros((max(lk, 1), 3), dtype=np.uint64)
+    fin, cl = np.zeros(2, dtype=np.uint64), np.zeros(3, dtype=np.uint64)
+    claimed = _lib.u64(0)
+    st = torch.cuda.current_stream().cuda_stream
+    import ctypes as C
+
+    def run():
+        chal = _lib.Challenger()
+        lib.zkie2_challenger_xorshift(C.byref(chal), 7)
+        check(lib.zkie2_op_matmul_prove(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), m, k, n, C.byref(chal),
+                                        _p(outs[0]), _p(outs[1]), _p(outs[2]), C.byref(claimed), _p(rounds),
+                                        _p(fin), _p(cl), scr.data_ptr(), st), "op_matmul_prove")
+    ms = _time(run, a.iters)
+    byts = 8 * (m * k + k * n + m * n)
+    return {"case": "op_matmul_prove", "m": m, "k": k, "n": n, "ms": ms, "bytes": byts,
+            "gbs": byts / (ms / 1e3) / 1e9}
+
+
+def case_commit(a):
+    lg_l, w, lb = a.log_size, a.polys, a.lg_blowup
+    L, H = 1 << lg_l, 1 << (lg_l + lb)
+    d_in = _rand(L * w, 7)
+    d_lde = torch.empty(H * w, dtype=torch.uint64, device="cuda")
+    d_layers = torch.empty(lib.zkie2_merkle_total_digests(H) * 8, dtype=torch.uint64, device="cuda")
+    d_scr = torch.empty(max(lib.zkie2_commit_scratch_elems(lg_l, lb, w), 1), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        check(lib.zkie2_commit(d_in.data_ptr(), lg_l, lb, w, d_lde.data_ptr(), d_layers.data_ptr(),
+                               d_scr.data_ptr(), st), "commit")
+    ms = _time(run, a.iters)
+    return {"case": "commit", "log_size": lg_l, "polys": w, "blowup": 1 << lb, "ms": ms,
+            "melem_s": L * w / (ms / 1e3) / 1e6}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit"])
+    ap.add_argument("--log-size", type=int, default=20)
+    ap.add_argument("--polys", type=int, default=16)
+    ap.add_argument("--lg-blowup", type=int, default=1)
+    ap.add_argument("--m", type=int, default=16)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--n", type=int, default=1024)
+    ap.add_argument("--iters", type=int, default=5)
+    a = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("perfcases needs a CUDA device")
+    check(lib.zkie2_p2_init_default(), "constants")
+    res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit}[a.case](a)
+    print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
