@@ -154,7 +154,7 @@ int zkie2_sumcheck_prove(const uint64_t *d_f, const uint64_t *d_h, uint32_t t, c
  * callers that cannot afford the device-wide synchronization cudaFree
  * implies.  The caller still passes f, h (device), the challenges and the
  * host outputs; the scratch is a fixed array inside the library (about
- * 2.4 MB, held on every GPU that loads the library until exit), so this call
+ * 1.9 MB, held on every GPU that loads the library until exit), so this call
  * allocates nothing.  Limit: t <= zkie2_sumcheck_noalloc_max_vars() (24);
  * larger t returns cudaErrorInvalidValue.  The first call on a device looks
  * up the array's device address (once per device), so make that first call
@@ -185,6 +185,26 @@ int zkie2_op_matmul_prove(const uint64_t *d_a, const uint64_t *d_b, const uint64
  * zkie-ops/src/compose.rs:1327-1331, zkie-ops/src/par.rs:41-89). */
 int zkie2_matmul_field(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
                        uint64_t *d_c, zkie_stream_t stream);
+/* prove_sum_of_products (common/sumcheck.rs:243-286): the batch-opening
+ * sumcheck of sum_x sum_i w_i(x) v_i(x) over n_tables pairs of 2^t tables,
+ * stored row-major: table i of d_weights / d_values starts at element i * 2^t.
+ * h_rounds gets (c0, c1, c2) per round, h_b_eval = sum_i w_i(r) v_i(r).
+ * Synchronous. */
+uint64_t zkie2_sum_of_products_scratch_elems(uint32_t n_tables, uint32_t t);
+int zkie2_sum_of_products_prove(const uint64_t *d_weights, const uint64_t *d_values, uint32_t n_tables,
+                                uint32_t t, const uint64_t *h_ch, uint64_t *h_rounds, uint64_t *h_b_eval,
+                                uint64_t *d_scratch, zkie_stream_t stream);
+/* prove_virtual (common/sumcheck.rs:378-438): sum over {0,1}^t of
+ * sum_i coeffs[i] * prod_{j in term i} f_j, over n_mles (<= 16) device tables
+ * of 2^t values (d_mles is a host array of device pointers).  Term i has the
+ * factors idx[idx_off[i] .. idx_off[i+1]) (at most 8 per term, 64 in all,
+ * n_terms <= 32, idx_off[0] = 0).  h_rounds gets t x (d + 1) evaluations,
+ * d = the largest term size; h_finals the n_mles folded values.
+ * Synchronous. */
+uint64_t zkie2_virtual_scratch_elems(uint32_t n_mles, uint32_t t);
+int zkie2_virtual_prove(const uint64_t *const *d_mles, uint32_t n_mles, uint32_t t, const uint64_t *coeffs,
+                        const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms, const uint64_t *h_ch,
+                        uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch, zkie_stream_t stream);
 
 #ifdef __cplusplus
 }

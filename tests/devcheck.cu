@@ -31,6 +31,19 @@ ZK_HD uint64_t scalar_op(int op, uint64_t a, uint64_t b) {
         case 11: return p2_sbox(a);
         case 12: return mul_hi(a, b);
         case 13: return gl_reduce128(a, b);
+        case 14: {
+            Acc160 s = acc160_zero();
+            acc160_mac(s, a, b);
+            acc160_mac(s, a, a);
+            acc160_mac(s, b, b);
+            acc160_mac(s, a ^ b, ~a);
+            return acc160_reduce(s);
+        }
+        case 15: {
+            Acc160 s = acc160_zero();
+            for (uint64_t k = 0; k <= (b & 1023); k++) acc160_mac(s, a, a);
+            return acc160_reduce(s);
+        }
         default: return 0;
     }
 }

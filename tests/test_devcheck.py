@@ -13,7 +13,8 @@ from tests import build_devcheck
 P = 0xFFFFFFFF00000001
 M64 = 2 ** 64
 SCALAR_OPS = {0: "add", 1: "add_c", 2: "sub", 3: "mul", 4: "sqr", 5: "div2", 6: "div8", 7: "div16",
-              8: "div32", 9: "div2^32", 10: "canon", 11: "sbox", 12: "mul_hi", 13: "reduce128"}
+              8: "div32", 9: "div2^32", 10: "canon", 11: "sbox", 12: "mul_hi", 13: "reduce128",
+              14: "acc160_dot4", 15: "acc160_repeat"}
 STATE_OPS = {105: "mat4", 100: "mds_light", 101: "ext_round0", 102: "internal_linear", 103: "int_round0",
              104: "permute"}
 
@@ -63,6 +64,8 @@ def expected_scalar(op, a, b):
     if op == 11: return pow(a, 7, P)
     if op == 12: return (a * b) >> 64
     if op == 13: return (b * M64 + a) % P
+    if op == 14: return (a * b + a * a + b * b + (a ^ b) * (M64 - 1 - a)) % P
+    if op == 15: return ((b & 1023) + 1) * a * a % P
 
 
 def test_host_scalar_ops_match_bigint(dc):

@@ -52,6 +52,65 @@ def test_sumcheck_matches_oracle(zk, orc, t):
         assert orc.sumcheck_verify(got.rounds, claimed, ch, got.f_eval, got.h_eval)
 
 
+def noncanonical(v):
+    """The same field elements, with every value below 2^32 - 1 replaced by v + p."""
+    return np.where(v < np.uint64(0xFFFFFFFF), v + np.uint64(P), v)
+
+
+def offset_tensor(v):
+    """A device tensor holding v whose data pointer is 8 bytes past a 16-byte boundary."""
+    import torch
+    t = torch.zeros(v.size + 1, dtype=torch.uint64, device="cuda")
+    t[1:] = torch.from_numpy(v).cuda()
+    out = t[1:]
+    assert out.data_ptr() % 16 == 8
+    return out
+
+
+@pytest.mark.parametrize("t", [3, 5, 9, 13, 17, 18, 19, 24])
+def test_sumcheck_level_boundaries(zk, orc, t):
+    """Sizes around the nine-round chunk levels (9 | 9+4 | 9+9 | 9+9+1 | 9+9+6),
+    inputs given as non-canonical representatives."""
+    f, h, ch = fields(3 * t, 1 << t), fields(3 * t + 1, 1 << t), fields(3 * t + 2, t)
+    got = zk.sumcheck_prove(noncanonical(f), noncanonical(h), 0, ch)
+    rounds, finals = orc.sumcheck_prove(f, h, ch)
+    assert np.array_equal(got.rounds, rounds)
+    assert (got.f_eval, got.h_eval) == (int(finals[0]), int(finals[1]))
+
+
+@pytest.mark.parametrize("t", [4, 12, 19])
+def test_sumcheck_unaligned_inputs(zk, orc, t):
+    """Inputs 8 bytes off a 16-byte boundary take the scalar-load path."""
+    f, h, ch = fields(5 * t, 1 << t), fields(5 * t + 1, 1 << t), fields(5 * t + 2, t)
+    got = zk.sumcheck_prove(offset_tensor(f), offset_tensor(h), 0, ch)
+    rounds, finals = orc.sumcheck_prove(f, h, ch)
+    assert np.array_equal(got.rounds, rounds)
+    assert (got.f_eval, got.h_eval) == (int(finals[0]), int(finals[1]))
+
+
+@pytest.mark.parametrize("t,f", [(6, 1), (6, 3), (6, 5), (12, 6), (16, 12)])
+def test_partial_eval_unaligned_noncanonical(zk, orc, t, f):
+    vals = fields(t * 5 + f, 1 << t)
+    fix = fields(11 + f, f)
+    want = orc.mle_partial_eval(vals, fix)
+    assert np.array_equal(zk.mle_partial_eval(offset_tensor(vals), fix).cpu().numpy(), want)
+    assert np.array_equal(zk.mle_partial_eval(noncanonical(vals), fix).cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 256, 128), (256, 512, 256), (1024, 32, 64)])
+def test_op_matmul_row_blocks(zk, orc, m, k, n):
+    """Row contraction of A split over several row blocks; A, B, C arbitrary
+    field matrices (the proof is computed whether or not C = A B)."""
+    a = fields(m, m * k).reshape(m, k)
+    b = fields(k, k * n).reshape(k, n)
+    c = fields(n, m * n).reshape(m, n)
+    got = zk.op_matmul_prove(a, b, c, m, k, n, zk.XorShift64(m + k + n))
+    exp = orc.op_matmul_prove(a, b, c, m, k, n, orc.XorShift64(m + k + n))
+    assert got.proof.claimed == exp["claimed"]
+    assert np.array_equal(got.proof.sumcheck.rounds, exp["rounds"])
+    assert np.array_equal(got.claims, exp["claims"])
+
+
 def test_sumcheck_reference_seed(zk, orc):
     # sumcheck.rs:316-335 with the reference's seed
     rng = orc.XorShift64(3)

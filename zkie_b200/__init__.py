@@ -11,5 +11,6 @@ from .commit import (  # noqa: F401
     make_twiddles, merkle_layer_lengths, p2_default_constants, padded_len, split_layers, upload_constants)
 from .device import P  # noqa: F401
 from .gkr import (  # noqa: F401
-    MatmulProof, OpMatMulProof, SumcheckProof, Transcript, XorShift64, eq_evals, matmul_field, matmul_prove,
-    mle_eval, mle_partial_eval, op_matmul_prove, sha256, shard_dag_child, sumcheck_prove)
+    MatmulProof, OpMatMulProof, SumcheckProof, SumcheckProofBatch, Transcript, VirtualProof, XorShift64, eq_evals,
+    matmul_field, matmul_prove, mle_eval, mle_partial_eval, op_matmul_prove, prove_sum_of_products, prove_virtual,
+    sha256, shard_dag_child, sumcheck_prove)

@@ -11,6 +11,7 @@ LIB_PATH = os.path.join(HERE, "libzkie_b200.so")
 
 u64, u32, i32, i64 = C.c_uint64, C.c_uint32, C.c_int32, C.c_int
 pu64 = C.POINTER(C.c_uint64)
+pu32 = C.POINTER(C.c_uint32)
 vp = C.c_void_p  # device pointers and streams travel as integers
 sz = C.c_size_t
 
@@ -78,6 +79,10 @@ SIGNATURES = {
     "zkie2_op_matmul_prove": (i64, [vp, vp, vp, u64, u64, u64, PCh, pu64, pu64, pu64, pu64, pu64, pu64,
                                     pu64, vp, vp]),
     "zkie2_matmul_field": (i64, [vp, vp, u64, u64, u64, vp, vp]),
+    "zkie2_sum_of_products_scratch_elems": (u64, [u32, u32]),
+    "zkie2_sum_of_products_prove": (i64, [vp, vp, u32, u32, pu64, pu64, pu64, vp, vp]),
+    "zkie2_virtual_scratch_elems": (u64, [u32, u32]),
+    "zkie2_virtual_prove": (i64, [C.POINTER(vp), u32, u32, pu64, pu32, pu32, u32, pu64, pu64, pu64, vp, vp]),
 }
 
 if not os.path.exists(LIB_PATH):

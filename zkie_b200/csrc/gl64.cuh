@@ -204,6 +204,57 @@ ZK_HD uint64_t acc_reduce(Acc a) {
     return s + ((uint64_t)(0u - c) & GL_EPS);
 }
 
+// ---- lazy sums of products -------------------------------------------------------------
+// A non-negative integer below 2^160 in five 32-bit limbs (little-endian).
+// Sums of up to 2^32 full 64 x 64 -> 128 products fit, so a dot product
+// accumulates every product exactly and reduces once at the end instead of
+// reducing each product and adding modulo p.
+struct Acc160 {
+    uint32_t w[5];
+};
+
+ZK_HD Acc160 acc160_zero() { return Acc160{{0u, 0u, 0u, 0u, 0u}}; }
+
+// a += x * y: the four 32 x 32 partial products as three multiply-add carry
+// chains (x0*y0 and x1*y1 on the even diagonals, then x0*y1 and x1*y0).
+ZK_HD void acc160_mac(Acc160& a, uint64_t x, uint64_t y) {
+#if defined(__CUDA_ARCH__)
+    const uint32_t x0 = (uint32_t)x, x1 = (uint32_t)(x >> 32);
+    const uint32_t y0 = (uint32_t)y, y1 = (uint32_t)(y >> 32);
+    asm("mad.lo.cc.u32  %0, %5, %7, %0;\n\t"
+        "madc.hi.cc.u32 %1, %5, %7, %1;\n\t"
+        "madc.lo.cc.u32 %2, %6, %8, %2;\n\t"
+        "madc.hi.cc.u32 %3, %6, %8, %3;\n\t"
+        "addc.u32       %4, %4, 0;\n\t"
+        "mad.lo.cc.u32  %1, %5, %8, %1;\n\t"
+        "madc.hi.cc.u32 %2, %5, %8, %2;\n\t"
+        "addc.cc.u32    %3, %3, 0;\n\t"
+        "addc.u32       %4, %4, 0;\n\t"
+        "mad.lo.cc.u32  %1, %6, %7, %1;\n\t"
+        "madc.hi.cc.u32 %2, %6, %7, %2;\n\t"
+        "addc.cc.u32    %3, %3, 0;\n\t"
+        "addc.u32       %4, %4, 0;"
+        : "+r"(a.w[0]), "+r"(a.w[1]), "+r"(a.w[2]), "+r"(a.w[3]), "+r"(a.w[4])
+        : "r"(x0), "r"(x1), "r"(y0), "r"(y1));
+#else
+    const unsigned __int128 p = (unsigned __int128)x * y;
+    const unsigned __int128 lo = ((unsigned __int128)a.w[1] << 32 | a.w[0]) |
+                                 ((unsigned __int128)((uint64_t)a.w[3] << 32 | a.w[2]) << 64);
+    const unsigned __int128 s = lo + p;
+    a.w[4] += s < p ? 1u : 0u;
+    a.w[0] = (uint32_t)s;
+    a.w[1] = (uint32_t)(s >> 32);
+    a.w[2] = (uint32_t)(s >> 64);
+    a.w[3] = (uint32_t)(s >> 96);
+#endif
+}
+
+// lo + mid * 2^64 + hi * 2^128 with 2^128 == -2^32 (mod p); hi * 2^32 < p.
+ZK_HD uint64_t acc160_reduce(const Acc160& a) {
+    const uint64_t r = gl_reduce128(pack64(a.w[0], a.w[1]), pack64(a.w[2], a.w[3]));
+    return gl_sub(r, (uint64_t)a.w[4] << 32);
+}
+
 ZK_HD uint64_t gl_sqr(uint64_t a) { return gl_mul(a, a); }
 
 // x / 2^k mod p for 1 <= k <= 32.  p == 1 (mod 2^k), so with

@@ -20,12 +20,16 @@ int sumcheck_dev(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uin
 int matmul_field_dev(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n,
                      uint64_t* d_c, cudaStream_t s);
 int contract_rows_dev(const uint64_t* d_v, const uint64_t* d_eq, uint64_t R, uint64_t K, uint64_t* d_out,
-                      cudaStream_t s);
+                      uint64_t* d_part, cudaStream_t s);
+uint64_t contract_rows_scratch_elems(uint64_t R, uint64_t K);
 int eq_table_dev(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s);
 int contract_dev(const uint64_t* v, const uint64_t* eq, uint64_t X, uint64_t Y, uint64_t* out,
                  cudaStream_t s);
 int commit_device(const uint64_t* d_in, uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint64_t* d_lde,
                   uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t s);
+uint64_t sum_of_products_scratch_elems(uint32_t n, uint32_t t);
+int sum_of_products_dev(const uint64_t* d_w, const uint64_t* d_v, uint32_t n, uint32_t t, const uint64_t* h_ch,
+                        uint64_t* d_out, uint64_t* d_scratch, cudaStream_t s);
 
 namespace {
 
@@ -33,7 +37,7 @@ bool pow2(uint64_t x) { return x && !(x & (x - 1)); }
 
 // Device layout of a matmul proof: claimed | rounds (3 lk) | finals (2).
 struct MatmulScratch {
-    uint64_t *eq_u, *eq_v, *ar, *br, *eval_scr, *sc_scr, *out;
+    uint64_t *eq_u, *eq_v, *ar, *br, *eval_scr, *sc_scr, *rows_part, *out;
 };
 
 uint64_t matmul_scratch(uint64_t m, uint64_t k, uint64_t n, MatmulScratch* ms, uint64_t* base) {
@@ -51,6 +55,7 @@ uint64_t matmul_scratch(uint64_t m, uint64_t k, uint64_t n, MatmulScratch* ms, u
     take(&s.br, k);
     take(&s.eval_scr, eval_scratch_elems(ln + lm) + m);
     take(&s.sc_scr, sumcheck_scratch_elems(lk));
+    take(&s.rows_part, contract_rows_scratch_elems(m, k));
     take(&s.out, 1 + 3 * lk + 2 + 8);
     if (ms) *ms = s;
     return off;
@@ -190,7 +195,7 @@ int zkie2_op_matmul_prove(const uint64_t* d_a, const uint64_t* d_b, const uint64
     matmul_scratch(m, k, n, &ms, d_scratch);
     int rc = eq_table_dev(u.data(), lm, ms.eq_u, stream);
     if (rc) return rc;
-    rc = contract_rows_dev(d_a, ms.eq_u, m, k, ms.ar, stream);
+    rc = contract_rows_dev(d_a, ms.eq_u, m, k, ms.ar, ms.rows_part, stream);
     if (rc) return rc;
     rc = matmul_core(d_b, d_c, m, k, n, u.data(), v.data(), ch.data(), ms, stream);
     if (rc) return rc;
@@ -209,6 +214,28 @@ int zkie2_matmul_field(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uin
                        uint64_t* d_c, cudaStream_t stream) {
     if (!d_a || !d_b || !d_c) return (int)cudaErrorInvalidValue;
     return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
+}
+
+// scratch of the batch sumcheck, then rounds (3t) and b_eval
+uint64_t zkie2_sum_of_products_scratch_elems(uint32_t n_tables, uint32_t t) {
+    if (n_tables == 0 || n_tables > 65535 || t > 40) return 0;
+    return sum_of_products_scratch_elems(n_tables, t) + 3ull * t + 2;
+}
+
+// prove_sum_of_products (crates/zkie-core/src/common/sumcheck.rs:243-286).
+int zkie2_sum_of_products_prove(const uint64_t* d_weights, const uint64_t* d_values, uint32_t n_tables, uint32_t t,
+                                const uint64_t* h_ch, uint64_t* h_rounds, uint64_t* h_b_eval, uint64_t* d_scratch,
+                                cudaStream_t stream) {
+    if (!d_weights || !d_values || !h_b_eval || !d_scratch || n_tables == 0 || n_tables > 65535 || t > 40 ||
+        (t && (!h_ch || !h_rounds)))
+        return (int)cudaErrorInvalidValue;
+    uint64_t* d_out = d_scratch + sum_of_products_scratch_elems(n_tables, t);
+    int rc = sum_of_products_dev(d_weights, d_values, n_tables, t, h_ch, d_out, d_scratch, stream);
+    if (rc) return rc;
+    if (t) ZK_TRY(cudaMemcpyAsync(h_rounds, d_out, 24ull * t, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaMemcpyAsync(h_b_eval, d_out + 3ull * t, 8, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaStreamSynchronize(stream));
+    return 0;
 }
 
 }  // extern "C"

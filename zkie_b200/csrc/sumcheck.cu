@@ -5,8 +5,9 @@
 // Reference: crates/zkie-core/src/common/{mle.rs:8-64, sumcheck.rs:33-89,
 // matmul.rs:17-46}.  Because the reference draws every challenge before it
 // proves (sumcheck.rs:33-38, zkie-ops/src/compose.rs:1727-1735), no round needs
-// a host round trip: one launch folds up to 11 rounds of a chunk in shared
-// memory, so a 2^t-element sumcheck reads f and h from HBM once per 11 rounds.
+// a host round trip: one launch runs nine rounds, each warp folding its own
+// 512-element chunk in registers, so a 2^t-element sumcheck reads f and h from
+// HBM once per nine rounds (in practice once: the second level reads 1/512).
 //
 // MLE evaluation by folding (a + r(b - a) per variable) and by contraction
 // with the equality table (sum_x v[x] eq(r, x)) give the same field element;
@@ -48,149 +49,290 @@ __device__ __forceinline__ uint64_t warp_sum(uint64_t v) {
     return v;
 }
 
-// out[y] = sum_{x < X} v[y*X + x] * eq[x], X >= 32: one warp per output.
-__global__ void k_contract_warp(const uint64_t* __restrict__ v, const uint64_t* __restrict__ eq,
-                                uint64_t X, uint64_t Y, uint64_t* __restrict__ out) {
-    const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint32_t lane = threadIdx.x & 31;
-    if (warp >= Y) return;
-    const uint64_t* src = v + warp * X;
-    uint64_t acc = 0;
-    for (uint64_t x = lane; x < X; x += 32) acc = gl_add(acc, gl_mul(__ldg(src + x), __ldg(eq + x)));
-    acc = warp_sum(acc);
-    if (lane == 0) out[warp] = gl_canon(acc);
+// Two consecutive elements p[2i], p[2i+1]: one 16-byte load when the caller
+// guarantees 16-byte alignment of p, else two 8-byte loads.
+template <bool kVec>
+__device__ __forceinline__ ulonglong2 load_pair(const uint64_t* __restrict__ p, uint64_t i) {
+    if (kVec) return __ldg(reinterpret_cast<const ulonglong2*>(p) + i);
+    return make_ulonglong2(__ldg(p + 2 * i), __ldg(p + 2 * i + 1));
 }
 
-// Same contraction for X < 32: one thread per output.
-__global__ void k_contract_thread(const uint64_t* __restrict__ v, const uint64_t* __restrict__ eq,
-                                  uint64_t X, uint64_t Y, uint64_t* __restrict__ out) {
-    const uint64_t y = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (y >= Y) return;
-    const uint64_t* src = v + y * X;
-    uint64_t acc = 0;
-    for (uint64_t x = 0; x < X; x++) acc = gl_add(acc, gl_mul(__ldg(src + x), __ldg(eq + x)));
-    out[y] = gl_canon(acc);
+// out[y] = sum_{x < X} v[y*X + x] * eq[x] for X = 2^lg_x >= 2 (mle.rs:25-38
+// as a contraction with the equality table).  A group of L = 2^lg_l lanes
+// (L <= min(32, X/2)) owns one row; lane j streams the element pairs
+// j, j + L, j + 2L, ... of the row and of eq, four pairs per iteration so
+// eight 16-byte loads are in flight, and accumulates the exact products in
+// an Acc160.  Each lane reduces once; a shuffle tree sums the group.
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads)
+    k_contract(const uint64_t* __restrict__ v, const uint64_t* __restrict__ eq, uint32_t lg_x, uint32_t lg_l,
+               uint64_t Y, uint64_t* __restrict__ out) {
+    const uint64_t gt = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t y = gt >> lg_l;
+    const uint32_t L = 1u << lg_l;
+    const uint32_t j = (uint32_t)gt & (L - 1);
+    Acc160 acc = acc160_zero();
+    if (y < Y) {
+        const uint64_t* row = v + (y << lg_x);
+        const uint32_t npairs = 1u << (lg_x - 1);
+        uint32_t i = j;
+        for (; i + 3 * L < npairs; i += 4 * L) {
+            const ulonglong2 a0 = load_pair<kVec>(row, i), a1 = load_pair<kVec>(row, i + L);
+            const ulonglong2 a2 = load_pair<kVec>(row, i + 2 * L), a3 = load_pair<kVec>(row, i + 3 * L);
+            const ulonglong2 e0 = load_pair<kVec>(eq, i), e1 = load_pair<kVec>(eq, i + L);
+            const ulonglong2 e2 = load_pair<kVec>(eq, i + 2 * L), e3 = load_pair<kVec>(eq, i + 3 * L);
+            acc160_mac(acc, a0.x, e0.x);
+            acc160_mac(acc, a0.y, e0.y);
+            acc160_mac(acc, a1.x, e1.x);
+            acc160_mac(acc, a1.y, e1.y);
+            acc160_mac(acc, a2.x, e2.x);
+            acc160_mac(acc, a2.y, e2.y);
+            acc160_mac(acc, a3.x, e3.x);
+            acc160_mac(acc, a3.y, e3.y);
+        }
+        for (; i < npairs; i += L) {
+            const ulonglong2 a = load_pair<kVec>(row, i), e = load_pair<kVec>(eq, i);
+            acc160_mac(acc, a.x, e.x);
+            acc160_mac(acc, a.y, e.y);
+        }
+    }
+    uint64_t s = acc160_reduce(acc);
+    for (uint32_t o = L >> 1; o > 0; o >>= 1) s = gl_add(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (y < Y && j == 0) out[y] = gl_canon(s);
 }
 
-// out[c] = sum_{r < R} v[r*K + c] * eq[r]: contraction over the rows of an
-// R x K row-major matrix, i.e. partial_eval of its transpose without
-// materialising the transpose (zkie-ops/src/compose.rs:52-60 + mle.rs:25-38).
-__global__ void k_contract_rows(const uint64_t* __restrict__ v, const uint64_t* __restrict__ eq,
-                                uint64_t R, uint64_t K, uint64_t* __restrict__ out) {
+// part[b][c] = sum over rows r of row block b of v[r*K + c] * eq[r]: the
+// contraction over the rows of an R x K row-major matrix, i.e. partial_eval
+// of its transpose without materialising the transpose (zkie-ops/src/
+// compose.rs:52-60 + mle.rs:25-38).  Grid (column-pair groups, row blocks);
+// each thread owns two adjacent columns and streams its block's rows four at
+// a time.  With a single row block the result is final and canonical.
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads)
+    k_contract_rows(const uint64_t* __restrict__ v, const uint64_t* __restrict__ eq, uint64_t R, uint64_t K,
+                    uint64_t rows_per_block, uint64_t* __restrict__ part) {
+    const uint64_t c = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (c >= K) return;
+    const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_block;
+    const uint64_t r1 = r0 + rows_per_block < R ? r0 + rows_per_block : R;
+    const bool two = c + 1 < K;  // always true on the vector path (K even)
+    Acc160 a0 = acc160_zero(), a1 = acc160_zero();
+    auto pair_at = [&](uint64_t r) -> ulonglong2 {
+        const uint64_t* p = v + r * K + c;
+        if (kVec) return __ldg(reinterpret_cast<const ulonglong2*>(p));
+        return make_ulonglong2(__ldg(p), two ? __ldg(p + 1) : 0ull);
+    };
+    uint64_t r = r0;
+    for (; r + 4 <= r1; r += 4) {
+        const ulonglong2 x0 = pair_at(r), x1 = pair_at(r + 1), x2 = pair_at(r + 2), x3 = pair_at(r + 3);
+        const uint64_t e0 = __ldg(eq + r), e1 = __ldg(eq + r + 1), e2 = __ldg(eq + r + 2), e3 = __ldg(eq + r + 3);
+        acc160_mac(a0, x0.x, e0);
+        acc160_mac(a1, x0.y, e0);
+        acc160_mac(a0, x1.x, e1);
+        acc160_mac(a1, x1.y, e1);
+        acc160_mac(a0, x2.x, e2);
+        acc160_mac(a1, x2.y, e2);
+        acc160_mac(a0, x3.x, e3);
+        acc160_mac(a1, x3.y, e3);
+    }
+    for (; r < r1; r++) {
+        const ulonglong2 x = pair_at(r);
+        const uint64_t e = __ldg(eq + r);
+        acc160_mac(a0, x.x, e);
+        acc160_mac(a1, x.y, e);
+    }
+    uint64_t* o = part + (uint64_t)blockIdx.y * K + c;
+    const bool fin = gridDim.y == 1;
+    const uint64_t s0 = acc160_reduce(a0), s1 = acc160_reduce(a1);
+    o[0] = fin ? gl_canon(s0) : s0;
+    if (two) o[1] = fin ? gl_canon(s1) : s1;
+}
+
+// out[c] = sum_{b < nb} part[b*K + c], canonical.
+__global__ void k_sum_rows(const uint64_t* __restrict__ part, uint64_t nb, uint64_t K, uint64_t* __restrict__ out) {
     const uint64_t c = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= K) return;
-    uint64_t acc = 0;
-    for (uint64_t r = 0; r < R; r++) acc = gl_add(acc, gl_mul(__ldg(v + r * K + c), __ldg(eq + r)));
-    out[c] = gl_canon(acc);
+    uint64_t s = 0;
+    for (uint64_t b = 0; b < nb; b++) s = gl_add(s, __ldg(part + b * K + c));
+    out[c] = gl_canon(s);
 }
 
-// Up to kMaxQ sumcheck rounds on one chunk of 2^q consecutive elements of f
-// and h (sumcheck.rs:48-72): for each round the chunk's contributions to
-// y0 = sum f0 h0, y1 = sum f1 h1, y2 = sum (2f1 - f0)(2h1 - h0) go to
-// partials[chunk][round][3]; then both vectors fold with the round's challenge
-// (a + r(b - a)).  The folded single values go to f_out/h_out[chunk].
-constexpr int kMaxQ = 11;
+// ---- sumcheck rounds -------------------------------------------------------------------
+// sumcheck.rs:48-72: round i sums, over the pairs (f0, f1), (h0, h1) of
+// adjacent elements, y0 = f0 h0, y1 = f1 h1 and y2 = (2f1 - f0)(2h1 - h0),
+// emits c0 = y0, c1 = (4y1 - y2 - 3y0)/2, c2 = (y2 - 2y1 + y0)/2, then folds
+// both vectors to a + r_i (b - a).  Here the third sum is s = (f0 + f1)(h0 + h1)
+// instead: y2 = 6y1 + 3y0 - 2s, which turns the coefficients into
+// c1 = s - y1 - 3y0 and c2 = 2(y0 + y1) - s -- the same field elements with
+// two field additions per pair fewer and no halving.
+//
+// One warp owns a chunk of 2^9 consecutive elements of f and of h and runs all
+// nine rounds of it without shared memory: each lane holds 16 consecutive
+// elements and does rounds 0-3 in registers (the sums accumulate exactly in
+// Acc160 and reduce once per round), then rounds 4-8 pair lanes by shuffles.
+// The 27 per-round sums are reduced across the warp by a butterfly
+// reduce-scatter and across the block's 8 warps through shared memory, so each
+// block writes one row of 27 partial sums.
+constexpr int kWarpRounds = 9;
+constexpr int kLaneElems = 16;
+constexpr int kChunkWarps = kThreads / 32;
+constexpr int kRoundVals = 3 * kWarpRounds;
 struct Chal {
-    uint64_t r[kMaxQ];
+    uint64_t r[kWarpRounds];
 };
 
-__device__ __forceinline__ void block_sum3(uint64_t& a, uint64_t& b, uint64_t& c, uint64_t* red) {
-    a = warp_sum(a);
-    b = warp_sum(b);
-    c = warp_sum(c);
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) {
-        red[3 * w] = a;
-        red[3 * w + 1] = b;
-        red[3 * w + 2] = c;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int nw = blockDim.x >> 5;
-        for (int i = 1; i < nw; i++) {
-            a = gl_add(a, red[3 * i]);
-            b = gl_add(b, red[3 * i + 1]);
-            c = gl_add(c, red[3 * i + 2]);
+// Butterfly reduce-scatter over a warp: afterwards lane l holds the sum over
+// all 32 lanes of v[l].
+__device__ __forceinline__ uint64_t warp_transpose_sum(uint64_t (&v)[32]) {
+    const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+    for (int n = 16; n >= 1; n >>= 1) {
+        const bool upper = (lane & n) != 0;
+#pragma unroll
+        for (int i = 0; i < n; i++) {
+            const uint64_t send = upper ? v[i] : v[i + n];
+            const uint64_t keep = upper ? v[i + n] : v[i];
+            v[i] = gl_add(keep, __shfl_xor_sync(0xffffffffu, send, n));
         }
     }
+    return v[0];
 }
 
+// Chunk c of the current vectors covers elements [c*512, c*512 + 512); only
+// the first n_valid elements of f and h exist, the rest read as zero.  A batch
+// of tables runs as gridDim.y tables at element stride in_stride; table y
+// writes its folded values at y * out_stride and its block partials after
+// those of tables < y, so one reduce over all rows sums the batch.  A tail
+// chunk (q < 9 rounds, one chunk) is padded that way: zero pairs add nothing
+// to the sums of rounds < q, and the folded value of the real data is taken
+// from lane 0 after round q - 1.  Sums of rounds >= q are never read.
+template <bool kVec>
 __global__ void __launch_bounds__(kThreads)
-    k_sumcheck_chunk(const uint64_t* __restrict__ f, const uint64_t* __restrict__ h, uint32_t q,
-                     Chal ch, uint64_t* __restrict__ partials, uint64_t* __restrict__ f_out,
-                     uint64_t* __restrict__ h_out) {
-    __shared__ uint64_t sf[1 << kMaxQ], sh[1 << kMaxQ];
-    __shared__ uint64_t red[3 * (kThreads / 32)];
-    const uint32_t Q = 1u << q;
-    const uint64_t base = (uint64_t)blockIdx.x << q;
-    for (uint32_t i = threadIdx.x; i < Q; i += kThreads) {
-        sf[i] = __ldg(f + base + i);
-        sh[i] = __ldg(h + base + i);
+    k_sumcheck_warp(const uint64_t* __restrict__ f, const uint64_t* __restrict__ h, uint64_t n_valid, uint64_t G,
+                    uint32_t q, Chal ch, uint64_t* __restrict__ partials, uint64_t* __restrict__ f_out,
+                    uint64_t* __restrict__ h_out, uint64_t in_stride, uint64_t out_stride) {
+    __shared__ uint64_t red[kChunkWarps][32];
+    // blockIdx.y selects the table of a batch (prove_sum_of_products)
+    f += blockIdx.y * in_stride;
+    h += blockIdx.y * in_stride;
+    f_out += blockIdx.y * out_stride;
+    h_out += blockIdx.y * out_stride;
+    partials += (uint64_t)blockIdx.y * gridDim.x * kRoundVals;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t chunk = (uint64_t)blockIdx.x * kChunkWarps + warp;
+    uint64_t fv[kLaneElems], hv[kLaneElems], vals[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) vals[i] = 0;
+    const uint64_t base = (chunk << kWarpRounds) + (uint64_t)lane * kLaneElems;
+    if (chunk < G && kVec && base + kLaneElems <= n_valid) {
+        const ulonglong2* f2 = reinterpret_cast<const ulonglong2*>(f + base);
+        const ulonglong2* h2 = reinterpret_cast<const ulonglong2*>(h + base);
+#pragma unroll
+        for (int i = 0; i < kLaneElems / 2; i++) {
+            const ulonglong2 a = __ldg(f2 + i), b = __ldg(h2 + i);
+            fv[2 * i] = a.x;
+            fv[2 * i + 1] = a.y;
+            hv[2 * i] = b.x;
+            hv[2 * i + 1] = b.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kLaneElems; i++) {
+            const bool ok = chunk < G && base + i < n_valid;
+            fv[i] = ok ? __ldg(f + base + i) : 0ull;
+            hv[i] = ok ? __ldg(h + base + i) : 0ull;
+        }
     }
-    __syncthreads();
-    constexpr int kPer = (1 << kMaxQ) / 2 / kThreads;  // pairs per thread at most
-    for (uint32_t rd = 0; rd < q; rd++) {
-        const uint32_t pairs = (Q >> rd) >> 1;
-        uint64_t y0 = 0, y1 = 0, y2 = 0;
-        uint64_t nf[kPer > 0 ? kPer : 1], nh[kPer > 0 ? kPer : 1];
+    uint64_t fin_f = 0, fin_h = 0;
+    // rounds 0-3: pairs inside the lane's registers
+#pragma unroll
+    for (int rd = 0; rd < 4; rd++) {
+        const int pairs = (kLaneElems / 2) >> rd;
         const uint64_t r = ch.r[rd];
+        Acc160 a0 = acc160_zero(), a1 = acc160_zero(), as = acc160_zero();
 #pragma unroll
-        for (int t = 0; t < (kPer > 0 ? kPer : 1); t++) {
-            const uint32_t s = threadIdx.x + t * kThreads;
-            if (s < pairs) {
-                const uint64_t f0 = sf[2 * s], f1 = sf[2 * s + 1];
-                const uint64_t h0 = sh[2 * s], h1 = sh[2 * s + 1];
-                y0 = gl_add(y0, gl_mul(f0, h0));
-                y1 = gl_add(y1, gl_mul(f1, h1));
-                y2 = gl_add(y2, gl_mul(gl_sub(gl_add(f1, f1), f0), gl_sub(gl_add(h1, h1), h0)));
-                nf[t] = gl_add(f0, gl_mul(r, gl_sub(f1, f0)));
-                nh[t] = gl_add(h0, gl_mul(r, gl_sub(h1, h0)));
-            }
+        for (int s = 0; s < pairs; s++) {
+            const uint64_t f0 = fv[2 * s], f1 = fv[2 * s + 1], h0 = hv[2 * s], h1 = hv[2 * s + 1];
+            acc160_mac(a0, f0, h0);
+            acc160_mac(a1, f1, h1);
+            acc160_mac(as, gl_add(f0, f1), gl_add(h0, h1));
+            fv[s] = gl_add(f0, gl_mul(r, gl_sub(f1, f0)));
+            hv[s] = gl_add(h0, gl_mul(r, gl_sub(h1, h0)));
         }
-        block_sum3(y0, y1, y2, red);
-        if (threadIdx.x == 0) {
-            uint64_t* p = partials + ((uint64_t)blockIdx.x * kMaxQ + rd) * 3;
-            p[0] = y0;
-            p[1] = y1;
-            p[2] = y2;
+        vals[3 * rd] = acc160_reduce(a0);
+        vals[3 * rd + 1] = acc160_reduce(a1);
+        vals[3 * rd + 2] = acc160_reduce(as);
+        if ((uint32_t)rd + 1 == q) {
+            fin_f = fv[0];
+            fin_h = hv[0];
         }
-        __syncthreads();
-#pragma unroll
-        for (int t = 0; t < (kPer > 0 ? kPer : 1); t++) {
-            const uint32_t s = threadIdx.x + t * kThreads;
-            if (s < pairs) {
-                sf[s] = nf[t];
-                sh[s] = nh[t];
-            }
-        }
-        __syncthreads();
     }
-    if (threadIdx.x == 0) {
-        f_out[blockIdx.x] = sf[0];
-        h_out[blockIdx.x] = sh[0];
+    // rounds 4-8: lane l pairs with lane l + 2^k, active when l % 2^(k+1) == 0
+    uint64_t x = fv[0], z = hv[0];
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        const int rd = 4 + k;
+        const uint32_t o = 1u << k;
+        const uint64_t x1 = __shfl_down_sync(0xffffffffu, x, o);
+        const uint64_t z1 = __shfl_down_sync(0xffffffffu, z, o);
+        if ((lane & (2 * o - 1)) == 0) {
+            vals[3 * rd] = gl_mul(x, z);
+            vals[3 * rd + 1] = gl_mul(x1, z1);
+            vals[3 * rd + 2] = gl_mul(gl_add(x, x1), gl_add(z, z1));
+        }
+        const uint64_t r = ch.r[rd];
+        x = gl_add(x, gl_mul(r, gl_sub(x1, x)));
+        z = gl_add(z, gl_mul(r, gl_sub(z1, z)));
+        if ((uint32_t)rd + 1 == q) {
+            fin_f = x;
+            fin_h = z;
+        }
+    }
+    red[warp][lane] = warp_transpose_sum(vals);
+    __syncthreads();
+    if (warp == 0 && lane < kRoundVals) {
+        uint64_t s = red[0][lane];
+#pragma unroll
+        for (int w = 1; w < kChunkWarps; w++) s = gl_add(s, red[w][lane]);
+        partials[(uint64_t)blockIdx.x * kRoundVals + lane] = s;
+    }
+    if (lane == 0 && chunk < G) {
+        f_out[chunk] = gl_canon(fin_f);
+        h_out[chunk] = gl_canon(fin_h);
     }
 }
 
-// Sum the per-chunk partials of each round and turn (y0, y1, y2) into the
-// round polynomial c0 = y0, c1 = (4y1 - y2 - 3y0)/2, c2 = (y2 - 2y1 + y0)/2
-// (sumcheck.rs:65-68).  One block per round.
-__global__ void k_sumcheck_reduce(const uint64_t* __restrict__ partials, uint64_t G, uint32_t q,
+// One block per round: sum (y0, y1, s) over the nb block rows of partials and
+// write the round polynomial c0 = y0, c1 = s - y1 - 3y0, c2 = 2(y0 + y1) - s.
+__global__ void k_sumcheck_reduce(const uint64_t* __restrict__ partials, uint64_t nb,
                                   uint64_t* __restrict__ rounds) {
-    __shared__ uint64_t red[3 * (kThreads / 32)];
+    __shared__ uint64_t red[3][kThreads / 32];
     const uint32_t rd = blockIdx.x;
-    uint64_t y0 = 0, y1 = 0, y2 = 0;
-    for (uint64_t g = threadIdx.x; g < G; g += kThreads) {
-        const uint64_t* p = partials + (g * kMaxQ + rd) * 3;
-        y0 = gl_add(y0, p[0]);
-        y1 = gl_add(y1, p[1]);
-        y2 = gl_add(y2, p[2]);
+    uint64_t y0 = 0, y1 = 0, s = 0;
+    for (uint64_t b = threadIdx.x; b < nb; b += kThreads) {
+        const uint64_t* p = partials + b * kRoundVals + 3 * rd;
+        y0 = gl_add(y0, __ldg(p));
+        y1 = gl_add(y1, __ldg(p + 1));
+        s = gl_add(s, __ldg(p + 2));
     }
-    block_sum3(y0, y1, y2, red);
+    y0 = warp_sum(y0);
+    y1 = warp_sum(y1);
+    s = warp_sum(s);
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        red[0][w] = y0;
+        red[1][w] = y1;
+        red[2][w] = s;
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
-        const uint64_t inv2 = 0x7FFFFFFF80000001ull;  // (p + 1) / 2
-        const uint64_t c1 = gl_mul(gl_sub(gl_sub(gl_mul(4, y1), y2), gl_mul(3, y0)), inv2);
-        const uint64_t c2 = gl_mul(gl_add(gl_sub(y2, gl_add(y1, y1)), y0), inv2);
+        for (int i = 1; i < kThreads / 32; i++) {
+            y0 = gl_add(y0, red[0][i]);
+            y1 = gl_add(y1, red[1][i]);
+            s = gl_add(s, red[2][i]);
+        }
+        const uint64_t c1 = gl_sub(gl_sub(s, y1), gl_mul(3, y0));
+        const uint64_t c2 = gl_sub(gl_add(gl_add(y0, y0), gl_add(y1, y1)), s);
         uint64_t* o = rounds + 3ull * rd;
         o[0] = gl_canon(y0);
         o[1] = gl_canon(c1);
@@ -226,16 +368,34 @@ int eq_table(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s) {
     return 0;
 }
 
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// X must be a power of two (the eq table of log2(X) variables).
 int contract(const uint64_t* v, const uint64_t* eq, uint64_t X, uint64_t Y, uint64_t* out, cudaStream_t s) {
     if (Y == 0) return 0;
-    if (X >= 32) {
-        const uint64_t threads = Y * 32;
-        k_contract_warp<<<(unsigned)ceil_div(threads, kThreads), kThreads, 0, s>>>(v, eq, X, Y, out);
-    } else {
-        k_contract_thread<<<(unsigned)ceil_div(Y, kThreads), kThreads, 0, s>>>(v, eq, X, Y, out);
+    if (X == 0 || (X & (X - 1)) || X > (1ull << 31)) return (int)cudaErrorInvalidValue;
+    if (X == 1) {
+        // eq of zero variables is the single value 1
+        k_canon_copy<<<(unsigned)ceil_div(Y, kThreads), kThreads, 0, s>>>(v, out, Y);
+        ZK_LAUNCH_CHECK();
+        return 0;
     }
+    const uint32_t lg_x = log2_exact(X);
+    const uint32_t lg_l = lg_x - 1 < 5 ? lg_x - 1 : 5;
+    const uint64_t blocks = ceil_div(Y << lg_l, kThreads);
+    if (blocks > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
+    if (aligned16(v) && aligned16(eq))
+        k_contract<true><<<(unsigned)blocks, kThreads, 0, s>>>(v, eq, lg_x, lg_l, Y, out);
+    else
+        k_contract<false><<<(unsigned)blocks, kThreads, 0, s>>>(v, eq, lg_x, lg_l, Y, out);
     ZK_LAUNCH_CHECK();
     return 0;
+}
+
+// Row blocks of the row contraction: at most 64, of at least 8 rows.
+uint64_t rows_blocks(uint64_t R) {
+    const uint64_t nb = ceil_div(R, 8);
+    return nb < 64 ? (nb ? nb : 1) : 64;
 }
 
 }  // namespace
@@ -296,55 +456,106 @@ int eval_dev(const uint64_t* d_values, uint32_t t, const uint64_t* h_point, uint
     return 0;
 }
 
-constexpr uint64_t sumcheck_scratch_elems_c(uint32_t t) {
-    // two folded vectors per launch level (<= 2^(t-11) each) + partials
-    return 4 * (t > kMaxQ ? (1ull << (t - kMaxQ)) : 1) + (t > kMaxQ ? (1ull << (t - kMaxQ)) : 1) * kMaxQ * 3 + 64;
+constexpr uint64_t sumcheck_chunks0(uint32_t t) {
+    return t > (uint32_t)kWarpRounds ? (1ull << (t - kWarpRounds)) : 2;
 }
+
+constexpr uint64_t sumcheck_batch_scratch_elems_c(uint64_t n_tables, uint32_t t) {
+    // per table: two ping-pong pairs of folded vectors (<= 2^(t-9) each) and
+    // one row of partial sums per block of the first level
+    return n_tables * (4 * sumcheck_chunks0(t) +
+                       kRoundVals * ((sumcheck_chunks0(t) + kChunkWarps - 1) / kChunkWarps)) + 64;
+}
+
+constexpr uint64_t sumcheck_scratch_elems_c(uint32_t t) { return sumcheck_batch_scratch_elems_c(1, t); }
 
 uint64_t sumcheck_scratch_elems(uint32_t t) { return sumcheck_scratch_elems_c(t); }
 
-// All t rounds of sumcheck::prove on device.  rounds (3t) and finals (2) are
-// written to device memory d_rounds.
-int sumcheck_dev(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uint64_t* h_ch,
-                 uint64_t* d_rounds, uint64_t* d_finals, uint64_t* d_scratch, cudaStream_t s) {
-    const uint64_t chunks0 = t > kMaxQ ? (1ull << (t - kMaxQ)) : 1;
+// All t rounds of the degree-2 sumcheck over a batch of n tables (table i of
+// f and h at element i * 2^t), nine rounds per level: each level is one
+// chunk launch over every table and one reduce launch over all their block
+// partials, so the round messages are those of sum_i f_i h_i.  rounds (3t)
+// go to d_rounds, the folded f_i and h_i (canonical) to d_ffin[i], d_hfin[i].
+int sumcheck_batch_dev(const uint64_t* d_f, const uint64_t* d_h, uint32_t n, uint32_t t, const uint64_t* h_ch,
+                       uint64_t* d_rounds, uint64_t* d_ffin, uint64_t* d_hfin, uint64_t* d_scratch, cudaStream_t s) {
+    if (n == 0 || n > 65535) return (int)cudaErrorInvalidValue;
+    if (t == 0) {
+        k_canon_copy<<<(unsigned)ceil_div(n, kThreads), kThreads, 0, s>>>(d_f, d_ffin, n);
+        k_canon_copy<<<(unsigned)ceil_div(n, kThreads), kThreads, 0, s>>>(d_h, d_hfin, n);
+        ZK_LAUNCH_CHECK();
+        return 0;
+    }
+    const uint64_t chunks0 = sumcheck_chunks0(t) * n;
     uint64_t* fa = d_scratch;
     uint64_t* ha = fa + chunks0;
     uint64_t* fb = ha + chunks0;
     uint64_t* hb = fb + chunks0;
     uint64_t* partials = hb + chunks0;
-    if (t == 0) {
-        k_canon_copy<<<1, 1, 0, s>>>(d_f, d_finals, 1);
-        k_canon_copy<<<1, 1, 0, s>>>(d_h, d_finals + 1, 1);
-        ZK_LAUNCH_CHECK();
-        return 0;
-    }
     const uint64_t* cf = d_f;
     const uint64_t* chh = d_h;
     uint32_t done = 0;
     bool first = true;
     while (done < t) {
         const uint32_t rem = t - done;
-        const uint32_t q = rem < (uint32_t)kMaxQ ? rem : (uint32_t)kMaxQ;
+        const uint32_t q = rem < (uint32_t)kWarpRounds ? rem : (uint32_t)kWarpRounds;
         const uint64_t G = 1ull << (rem - q);
+        const uint64_t nb = ceil_div(G, kChunkWarps);
+        if (nb > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
         Chal ch{};
         for (uint32_t i = 0; i < q; i++) ch.r[i] = h_ch[done + i];
-        uint64_t* of = (rem - q == 0) ? d_finals : (first ? fa : (cf == fa ? fb : fa));
-        uint64_t* oh = (rem - q == 0) ? d_finals + 1 : (first ? ha : (chh == ha ? hb : ha));
-        k_sumcheck_chunk<<<(unsigned)G, kThreads, 0, s>>>(cf, chh, q, ch, partials, of, oh);
+        const bool last = rem == q;
+        uint64_t* of = last ? d_ffin : (first ? fa : (cf == fa ? fb : fa));
+        uint64_t* oh = last ? d_hfin : (first ? ha : (chh == ha ? hb : ha));
+        const uint64_t n_valid = 1ull << rem;
+        const dim3 grid((unsigned)nb, n);
+        if (aligned16(cf) && aligned16(chh))
+            k_sumcheck_warp<true><<<grid, kThreads, 0, s>>>(cf, chh, n_valid, G, q, ch, partials, of, oh, n_valid, G);
+        else
+            k_sumcheck_warp<false><<<grid, kThreads, 0, s>>>(cf, chh, n_valid, G, q, ch, partials, of, oh, n_valid, G);
         ZK_LAUNCH_CHECK();
-        k_sumcheck_reduce<<<q, kThreads, 0, s>>>(partials, G, q, d_rounds + 3ull * done);
+        k_sumcheck_reduce<<<q, kThreads, 0, s>>>(partials, nb * n, d_rounds + 3ull * done);
         ZK_LAUNCH_CHECK();
         cf = of;
         chh = oh;
         done += q;
         first = false;
     }
-    if (t > 0) {
-        // finals were written by the last chunk launch without canonicalization
-        k_canon_copy<<<1, 2, 0, s>>>(d_finals, d_finals, 2);
-        ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+// sumcheck::prove on one pair: rounds (3t) and finals (f, h) in device memory.
+int sumcheck_dev(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uint64_t* h_ch,
+                 uint64_t* d_rounds, uint64_t* d_finals, uint64_t* d_scratch, cudaStream_t s) {
+    return sumcheck_batch_dev(d_f, d_h, 1, t, h_ch, d_rounds, d_finals, d_finals + 1, d_scratch, s);
+}
+
+// out[0] = sum_i f[i] h[i], canonical (one block).
+__global__ void k_dot_small(const uint64_t* __restrict__ f, const uint64_t* __restrict__ h, uint32_t n,
+                            uint64_t* __restrict__ out) {
+    __shared__ uint64_t red[kThreads / 32];
+    Acc160 a = acc160_zero();
+    for (uint32_t i = threadIdx.x; i < n; i += kThreads) acc160_mac(a, f[i], h[i]);
+    uint64_t v = warp_sum(acc160_reduce(a));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < kThreads / 32; w++) v = gl_add(v, red[w]);
+        out[0] = gl_canon(v);
     }
+}
+
+uint64_t sum_of_products_scratch_elems(uint32_t n, uint32_t t) {
+    return sumcheck_batch_scratch_elems_c(n, t) + 3ull * t + 2ull * n + 8;
+}
+
+// prove_sum_of_products: rounds (3t) then b_eval (1) at d_out.
+int sum_of_products_dev(const uint64_t* d_w, const uint64_t* d_v, uint32_t n, uint32_t t, const uint64_t* h_ch,
+                        uint64_t* d_out, uint64_t* d_scratch, cudaStream_t s) {
+    uint64_t* fin = d_scratch + sumcheck_batch_scratch_elems_c(n, t);
+    int rc = sumcheck_batch_dev(d_w, d_v, n, t, h_ch, d_out, fin, fin + n, d_scratch, s);
+    if (rc) return rc;
+    k_dot_small<<<1, kThreads, 0, s>>>(fin, fin + n, n, d_out + 3ull * t);
+    ZK_LAUNCH_CHECK();
     return 0;
 }
 
@@ -358,10 +569,30 @@ int matmul_field_dev(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint6
     return 0;
 }
 
+uint64_t contract_rows_scratch_elems(uint64_t R, uint64_t K) {
+    const uint64_t nb = rows_blocks(R);
+    return nb > 1 ? nb * K : 0;
+}
+
+// out[c] = sum_r v[r*K + c] eq[r] for an R x K row-major v; d_part holds
+// contract_rows_scratch_elems(R, K) u64.
 int contract_rows_dev(const uint64_t* d_v, const uint64_t* d_eq, uint64_t R, uint64_t K, uint64_t* d_out,
-                      cudaStream_t s) {
-    k_contract_rows<<<(unsigned)ceil_div(K, kThreads), kThreads, 0, s>>>(d_v, d_eq, R, K, d_out);
+                      uint64_t* d_part, cudaStream_t s) {
+    if (K == 0) return 0;
+    const uint64_t nb = rows_blocks(R);
+    const uint64_t rpb = ceil_div(R ? R : 1, nb);
+    const dim3 grid((unsigned)ceil_div(ceil_div(K, 2), kThreads), (unsigned)nb);
+    uint64_t* part = nb > 1 ? d_part : d_out;
+    if (nb > 1 && !d_part) return (int)cudaErrorInvalidValue;
+    if (aligned16(d_v) && (K % 2) == 0)
+        k_contract_rows<true><<<grid, kThreads, 0, s>>>(d_v, d_eq, R, K, rpb, part);
+    else
+        k_contract_rows<false><<<grid, kThreads, 0, s>>>(d_v, d_eq, R, K, rpb, part);
     ZK_LAUNCH_CHECK();
+    if (nb > 1) {
+        k_sum_rows<<<(unsigned)ceil_div(K, kThreads), kThreads, 0, s>>>(part, nb, K, d_out);
+        ZK_LAUNCH_CHECK();
+    }
     return 0;
 }
 
@@ -379,7 +610,7 @@ int contract_dev(const uint64_t* v, const uint64_t* eq, uint64_t X, uint64_t Y, 
 // array, sized for the largest accepted sumcheck: partial sums and folded
 // vectors of a 2^kNoAllocMaxVars-element f and h, then the round polynomials
 // and the two final values.  Every GPU that loads the library holds it
-// (about 2.4 MB) until the process exits.
+// (about 1.9 MB) until the process exits.
 constexpr uint32_t kNoAllocMaxVars = 24;
 constexpr uint64_t kNoAllocScratchElems = sumcheck_scratch_elems_c(kNoAllocMaxVars) + 3ull * kNoAllocMaxVars + 4;
 static __device__ __align__(256) uint64_t g_noalloc_scratch[kNoAllocScratchElems];

@@ -5,6 +5,8 @@
 - ``sumcheck_prove`` -> ``SumcheckProof``    <- common/sumcheck.rs:10-89
 - ``matmul_prove``   -> ``MatmulProof``      <- common/matmul.rs:17-46
 - ``op_matmul_prove``                        <- zkie-ops/src/compose.rs:1724-1747
+- ``prove_sum_of_products``                  <- common/sumcheck.rs:243-286
+- ``prove_virtual`` -> ``VirtualProof``      <- common/sumcheck.rs:378-438
 - ``shard_dag_child``                        <- zkie-ops/src/compose.rs:2276-2311
 """
 import ctypes as C
@@ -236,3 +238,71 @@ def matmul_field(a, b, m, k, n) -> torch.Tensor:
     dc = empty(m * n)
     check(lib.zkie2_matmul_field(ptr(da), ptr(db), m, k, n, ptr(dc), stream_handle()), "zkie2_matmul_field")
     return dc
+
+
+# ---- batch-opening and virtual-polynomial sumchecks -------------------------------------
+def _stack(tables) -> torch.Tensor:
+    if isinstance(tables, torch.Tensor):
+        d = to_dev(tables)
+        return d.reshape(1, -1) if d.dim() == 1 else d.reshape(d.shape[0], -1)
+    return to_dev(np.stack([np.asarray(x, dtype=np.uint64) for x in tables]))
+
+
+@dataclass
+class SumcheckProofBatch:
+    rounds: np.ndarray  # (t, 3): c0, c1, c2 per round
+    b_eval: int
+
+
+def prove_sum_of_products(weights, values, claimed_sum, challenges) -> SumcheckProofBatch:
+    """sumcheck::prove_sum_of_products over n tables of 2^t (the claimed sum is
+    not used by the prover, as in the reference)."""
+    dw, dv = _stack(weights), _stack(values)
+    if dw.shape != dv.shape:
+        raise ValueError("sum of products: shape mismatch")
+    n, t = dw.shape[0], _lg(dw.shape[1])
+    ch = _arr(challenges)
+    if ch.size != t:
+        raise ValueError("challenge count mismatch")
+    rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+    b_eval = _lib.u64(0)
+    scr = empty(lib.zkie2_sum_of_products_scratch_elems(n, t))
+    check(lib.zkie2_sum_of_products_prove(ptr(dw), ptr(dv), n, t, _p(ch), _p(rounds), C.byref(b_eval), ptr(scr),
+                                          stream_handle()), "zkie2_sum_of_products_prove")
+    return SumcheckProofBatch(rounds[:t], int(b_eval.value))
+
+
+@dataclass
+class VirtualProof:
+    rounds: np.ndarray       # (t, d + 1): the round polynomial's values at 0..d
+    final_evals: np.ndarray  # one per MLE
+
+
+def prove_virtual(mles, terms, claimed, challenges) -> VirtualProof:
+    """sumcheck::prove_virtual: mles is a list of 2^t tables, terms a list of
+    (coeff, [mle indices]); the claimed sum is not used by the prover."""
+    ds = [to_dev(m).reshape(-1) for m in mles]
+    if not ds:
+        raise ValueError("prove_virtual: no MLEs")
+    t = _lg(ds[0].numel())
+    if any(d.numel() != ds[0].numel() for d in ds):
+        raise ValueError("prove_virtual: MLE length mismatch")
+    ch = _arr(challenges)
+    if ch.size != t:
+        raise ValueError("challenge count mismatch")
+    coeffs = np.array([int(c) % 0xFFFFFFFF00000001 for c, _ in terms] or [0], dtype=np.uint64)
+    off, idx = [0], []
+    for _, ids in terms:
+        idx.extend(int(i) for i in ids)
+        off.append(len(idx))
+    off = np.array(off, dtype=np.uint32)
+    idx = np.array(idx or [0], dtype=np.uint32)
+    deg = max((len(ids) for _, ids in terms), default=0)
+    ptrs = (C.c_void_p * len(ds))(*[ptr(d) for d in ds])
+    rounds = np.zeros((max(t, 1), deg + 1), dtype=np.uint64)
+    finals = np.zeros(len(ds), dtype=np.uint64)
+    scr = empty(max(lib.zkie2_virtual_scratch_elems(len(ds), t), 1))
+    check(lib.zkie2_virtual_prove(ptrs, len(ds), t, _p(coeffs), off.ctypes.data_as(_lib.pu32),
+                                  idx.ctypes.data_as(_lib.pu32), len(terms), _p(ch), _p(rounds), _p(finals),
+                                  ptr(scr), stream_handle()), "zkie2_virtual_prove")
+    return VirtualProof(rounds[:t], finals)

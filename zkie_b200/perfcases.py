@@ -4,6 +4,8 @@
     python -m zkie_b200.perfcases mle --log-size 24
     python -m zkie_b200.perfcases matmul --m 512 --k 1024 --n 4096
     python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
+    python -m zkie_b200.perfcases virtual --log-size 21
+    python -m zkie_b200.perfcases sop --log-size 20 --polys 4
 
 Each case prints one JSON line: device time per call (CUDA events on the
 launching stream, after warm-up) and the algorithmic HBM bytes per call.
@@ -106,6 +108,52 @@ def case_matmul(a):
             "gbs": byts / (ms / 1e3) / 1e9}
 
 
+def case_virtual(a):
+    """prove_virtual with the Projection-affine term shape (6 MLEs, 5 degree-2 terms)."""
+    import ctypes as C
+    t = a.log_size
+    mles = [_rand(1 << t, 20 + j) for j in range(6)]
+    neg = lambda x: (P - x) % P  # noqa: E731
+    terms = [(1, [0, 1]), (neg(1), [0, 2]), (1 << 16, [0, 3]), (neg(1 << 16), [0, 4]), (neg(1 << 15), [0, 5])]
+    coeffs = np.array([c for c, _ in terms], dtype=np.uint64)
+    off = np.array([0, 2, 4, 6, 8, 10], dtype=np.uint32)
+    idx = np.array([j for _, ids in terms for j in ids], dtype=np.uint32)
+    ch = np.arange(1, t + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15 % P)
+    ptrs = (C.c_void_p * 6)(*[m.data_ptr() for m in mles])
+    rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+    finals = np.zeros(6, dtype=np.uint64)
+    scr = torch.empty(lib.zkie2_virtual_scratch_elems(6, t), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    pu32 = _lib.pu32
+
+    def run():
+        check(lib.zkie2_virtual_prove(ptrs, 6, t, _p(coeffs), off.ctypes.data_as(pu32), idx.ctypes.data_as(pu32),
+                                      5, _p(ch), _p(rounds), _p(finals), scr.data_ptr(), st), "virtual")
+    ms = _time(run, a.iters)
+    return {"case": "virtual_affine6", "log_size": t, "ms": ms, "bytes": 48 << t,
+            "gbs": (48 << t) / (ms / 1e3) / 1e9}
+
+
+def case_sop(a):
+    """prove_sum_of_products over `polys` table pairs of 2^log_size."""
+    t, n = a.log_size, a.polys
+    w, v = _rand(n << t, 30), _rand(n << t, 31)
+    ch = np.arange(1, t + 1, dtype=np.uint64) * np.uint64(12345)
+    rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+    be = _lib.u64(0)
+    scr = torch.empty(lib.zkie2_sum_of_products_scratch_elems(n, t), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    import ctypes as C
+
+    def run():
+        check(lib.zkie2_sum_of_products_prove(w.data_ptr(), v.data_ptr(), n, t, _p(ch), _p(rounds), C.byref(be),
+                                              scr.data_ptr(), st), "sum_of_products")
+    ms = _time(run, a.iters)
+    byts = 16 * (n << t)
+    return {"case": "sum_of_products", "tables": n, "log_size": t, "ms": ms, "bytes": byts,
+            "gbs": byts / (ms / 1e3) / 1e9}
+
+
 def case_commit(a):
     lg_l, w, lb = a.log_size, a.polys, a.lg_blowup
     L, H = 1 << lg_l, 1 << (lg_l + lb)
@@ -125,7 +173,7 @@ def case_commit(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit"])
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop"])
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
     ap.add_argument("--lg-blowup", type=int, default=1)
@@ -137,7 +185,8 @@ def main(argv=None):
     if not torch.cuda.is_available():
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
-    res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit}[a.case](a)
+    res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
+           "virtual": case_virtual, "sop": case_sop}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 
