@@ -9,10 +9,12 @@
 //
 // As in the degree-2 sumcheck all challenges are known before proving
 // (callers draw them up front: compose.rs:392, projection.rs:83), so a launch
-// runs q rounds on independent chunks of 2^q consecutive positions: one block
-// stages its chunk of every table in shared memory, runs the q rounds there
-// (ping-pong buffers, one barrier per round) and writes per-round partial
-// sums plus one folded value per table.  A second launch sums the partials of
+// runs q <= 8 rounds on independent chunks of 2^q consecutive positions: one
+// 128-thread block stages its chunk of every table in shared memory, runs the
+// q rounds there (ping-pong buffers, one barrier per round) and writes
+// per-round partial sums plus one folded value per table.  A round is split
+// into (term, pair) work items rather than pairs, so the late rounds with few
+// pairs still spread over the block.  A second launch sums the partials of
 // all chunks.  The folded vectors (1/2^q of the input) feed the next level.
 // The input tables are read from HBM exactly once.
 //
@@ -28,12 +30,13 @@ namespace zk {
 
 namespace {
 
-constexpr int kVThreads = 256;
+constexpr int kVThreads = 128;
 constexpr int kVMaxMles = 16;
 constexpr int kVMaxTerms = 32;
 constexpr int kVMaxFactors = 64;
 constexpr int kVMaxDeg = 8;
 constexpr int kVMaxQ = 10;
+constexpr int kVQCap = 8;  // rounds per launch: 2^8 positions per 128-thread block
 constexpr uint32_t kVSmemBytes = 46 * 1024;  // dynamic part; the static reduction buffer rides on top
 
 struct VTerms {
@@ -59,70 +62,92 @@ __device__ __forceinline__ uint64_t v_warp_sum(uint64_t v) {
 // (n_mles x 2^q) followed by a half-size buffer (n_mles x 2^(q-1)).
 // partials[(chunk * q + round) * (d + 1) + k]; out[j * out_stride + chunk] is
 // the chunk's folded value of table j (canonical).
+// kF bounds the factors per term (and so the degree): the kernel is
+// instantiated for 2, 4 and 8 so the per-factor loops unroll to what the
+// terms need.  The term tables are copied to shared memory once per block,
+// where the per-pair lookups by term and factor index are cheap.
+template <int kF>
 __global__ void __launch_bounds__(kVThreads)
     k_virtual_chunk(VIn in, uint32_t q, VTerms T, VChal ch, uint64_t* __restrict__ partials,
                     uint64_t* __restrict__ out, uint64_t out_stride) {
-    extern __shared__ uint64_t sm[];
-    __shared__ uint64_t red[2][kVThreads / 32][kVMaxDeg + 1];
-    const uint32_t nm = T.n_mles, deg = T.deg, Q = 1u << q;
+    extern __shared__ __align__(16) uint64_t sm[];
+    __shared__ uint64_t red[2][kVThreads / 32][kF + 1];
+    __shared__ uint64_t s_coeff[kVMaxTerms];
+    __shared__ uint32_t s_off[kVMaxTerms + 1], s_idx[kVMaxFactors];
+    __shared__ uint64_t s_ch[kVMaxQ];
+    const uint32_t nm = T.n_mles, deg = T.deg, nt = T.n_terms, Q = 1u << q;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid < kVMaxTerms) s_coeff[tid] = T.coeff[tid];
+    if (tid <= kVMaxTerms) s_off[tid] = T.off[tid];
+    if (tid < kVMaxFactors) s_idx[tid] = T.idx[tid];
+    if (tid < kVMaxQ) s_ch[tid] = ch.r[tid];
     const uint64_t base = (uint64_t)blockIdx.x << q;
-    for (uint32_t j = 0; j < nm; j++) {
-        const uint64_t* src = in.p[j] + base;
-        for (uint32_t i = tid; i < Q; i += kVThreads) sm[j * Q + i] = __ldg(src + i);
+#pragma unroll
+    for (int j = 0; j < kVMaxMles; j++) {
+        if ((uint32_t)j < nm) {
+            const uint64_t* src = in.p[j] + base;
+            for (uint32_t i = tid; i < Q; i += kVThreads) sm[j * Q + i] = __ldg(src + i);
+        }
     }
     __syncthreads();
     uint64_t* cur = sm;
     uint64_t* nxt = sm + (size_t)nm * Q;
     uint32_t sc = Q, sn = Q >> 1;
     for (uint32_t rd = 0; rd < q; rd++) {
-        const uint32_t pairs = Q >> (rd + 1);
-        const uint64_t r = ch.r[rd];
-        Acc160 acc[kVMaxDeg + 1];
+        const uint32_t lg_pairs = q - 1 - rd, pairs = 1u << lg_pairs;
+        const uint64_t r = s_ch[rd];
+        Acc160 acc[kF + 1];
 #pragma unroll
-        for (int k = 0; k <= kVMaxDeg; k++) acc[k] = acc160_zero();
-        for (uint32_t s = tid; s < pairs; s += kVThreads) {
-            for (uint32_t ti = 0; ti < T.n_terms; ti++) {
-                const uint32_t o0 = T.off[ti], nf = T.off[ti + 1] - o0;
-                const uint64_t c = T.coeff[ti];
-                uint64_t fv[kVMaxDeg], dv[kVMaxDeg];
+        for (int k = 0; k <= kF; k++) acc[k] = acc160_zero();
+        // work items (term ti, pair s), term-major: neighbouring threads take
+        // neighbouring pairs of one term, so their shared-memory reads are
+        // consecutive 16-byte pairs
+        const uint32_t items = nt << lg_pairs;
+        for (uint32_t it = tid; it < items; it += kVThreads) {
+            const uint32_t ti = it >> lg_pairs, s = it & (pairs - 1);
+            const uint32_t o0 = s_off[ti], nf = s_off[ti + 1] - o0;
+            const uint64_t c = s_coeff[ti];
+            uint64_t fv[kF], dv[kF];
 #pragma unroll
-                for (int f = 0; f < kVMaxDeg; f++) {
-                    if ((uint32_t)f < nf) {
-                        const uint32_t j = T.idx[o0 + f];
-                        const uint64_t f0 = cur[j * sc + 2 * s], f1 = cur[j * sc + 2 * s + 1];
-                        fv[f] = f0;
-                        dv[f] = gl_sub(f1, f0);
-                    } else {
-                        fv[f] = 1;
-                        dv[f] = 0;
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k <= kVMaxDeg; k++) {
-                    if ((uint32_t)k <= deg) {
-                        // c * prod_{f < nf} f_f(k): all but the last factor reduced,
-                        // the last one multiplied into the exact sum
-                        uint64_t p = c, last = 1;
-#pragma unroll
-                        for (int f = 0; f < kVMaxDeg; f++) {
-                            if ((uint32_t)f + 1 < nf) p = gl_mul(p, fv[f]);
-                            else if ((uint32_t)f + 1 == nf) last = fv[f];
-                        }
-                        acc160_mac(acc[k], p, last);
-#pragma unroll
-                        for (int f = 0; f < kVMaxDeg; f++) fv[f] = gl_add(fv[f], dv[f]);
-                    }
+            for (int f = 0; f < kF; f++) {
+                fv[f] = 1;
+                dv[f] = 0;
+                if ((uint32_t)f < nf) {
+                    const ulonglong2 pr = reinterpret_cast<const ulonglong2*>(cur + s_idx[o0 + f] * sc)[s];
+                    fv[f] = pr.x;
+                    dv[f] = gl_sub(pr.y, pr.x);
                 }
             }
-            for (uint32_t j = 0; j < nm; j++) {
-                const uint64_t f0 = cur[j * sc + 2 * s], f1 = cur[j * sc + 2 * s + 1];
-                nxt[j * sn + s] = gl_add(f0, gl_mul(r, gl_sub(f1, f0)));
+#pragma unroll
+            for (int k = 0; k <= kF; k++) {
+                if ((uint32_t)k <= deg) {
+                    // c * prod_{f < nf} f_f(k): all but the last factor reduced,
+                    // the last one multiplied into the exact sum
+                    uint64_t p = c, last = 1;
+#pragma unroll
+                    for (int f = 0; f < kF; f++) {
+                        if ((uint32_t)f + 1 < nf) p = gl_mul(p, fv[f]);
+                        else if ((uint32_t)f + 1 == nf) last = fv[f];
+                    }
+                    acc160_mac(acc[k], p, last);
+                    if ((uint32_t)k < deg) {
+#pragma unroll
+                        for (int f = 0; f < kF; f++)
+                            if ((uint32_t)f < nf) fv[f] = gl_add(fv[f], dv[f]);
+                    }
+                }
             }
         }
-        if (warp * 32 < pairs) {  // warp-uniform: warps past the last pair hold zeros
+        // fold items (table j, pair s)
+        const uint32_t fitems = nm << lg_pairs;
+        for (uint32_t it = tid; it < fitems; it += kVThreads) {
+            const uint32_t j = it >> lg_pairs, s = it & (pairs - 1);
+            const ulonglong2 pr = reinterpret_cast<const ulonglong2*>(cur + j * sc)[s];
+            nxt[j * sn + s] = gl_add(pr.x, gl_mul(r, gl_sub(pr.y, pr.x)));
+        }
+        if (warp * 32 < items) {  // warp-uniform: warps past the last item hold zeros
 #pragma unroll
-            for (int k = 0; k <= kVMaxDeg; k++) {
+            for (int k = 0; k <= kF; k++) {
                 if ((uint32_t)k <= deg) {
                     const uint64_t v = v_warp_sum(acc160_reduce(acc[k]));
                     if (lane == 0) red[rd & 1][warp][k] = v;
@@ -131,9 +156,9 @@ __global__ void __launch_bounds__(kVThreads)
         }
         __syncthreads();
         if (tid <= deg) {
-            const uint32_t nw = pairs >= (uint32_t)kVThreads ? kVThreads / 32 : (pairs + 31) / 32;
-            uint64_t v = red[rd & 1][0][tid];
-            for (uint32_t w = 1; w < nw; w++) v = gl_add(v, red[rd & 1][w][tid]);
+            const uint32_t nw = items >= (uint32_t)kVThreads ? kVThreads / 32 : (items + 31) / 32;
+            uint64_t v = 0;  // no terms: every round sends zeros
+            for (uint32_t w = 0; w < nw; w++) v = gl_add(v, red[rd & 1][w][tid]);
             partials[((uint64_t)blockIdx.x * q + rd) * (deg + 1) + tid] = v;
         }
         uint64_t* t = cur;
@@ -173,7 +198,7 @@ __global__ void k_virtual_t0(VIn in, uint32_t nm, uint64_t* __restrict__ out) {
 // memory (under the 48 KB default limit together with the static part).
 uint32_t v_qmax(uint32_t nm) {
     uint32_t q = 1;
-    while (q < (uint32_t)kVMaxQ && 12ull * nm * (2ull << q) <= kVSmemBytes) q++;
+    while (q < (uint32_t)kVQCap && 12ull * nm * (2ull << q) <= kVSmemBytes) q++;
     return q;
 }
 
@@ -223,7 +248,12 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
         uint64_t* out = last ? d_finals : buf[which];
         const uint64_t out_stride = last ? 1 : G;
         const size_t smem = ((size_t)12 * nm) << q;  // nm x (2^q + 2^(q-1)) u64
-        k_virtual_chunk<<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+        if (T.deg <= 2)
+            k_virtual_chunk<2><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+        else if (T.deg <= 4)
+            k_virtual_chunk<4><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+        else
+            k_virtual_chunk<8><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
         ZK_LAUNCH_CHECK();
         k_virtual_reduce<<<q * (T.deg + 1), kVThreads, 0, s>>>(partials, G, q, T.deg, d_rounds + (uint64_t)done * (T.deg + 1));
         ZK_LAUNCH_CHECK();
