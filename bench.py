@@ -13,8 +13,11 @@ case: 256 polynomials of 2^20 coefficients each, blowup 2 -- an LDE of
   e2e:   the same commit through the host-buffer C-ABI call zkie2_commit_host
          (pinned coefficients in, LDE + all digest layers + root out).
 
-N > 1: one process per GPU, each commits its own independent batch (weak
-scaling); no collective touches the data path, only the timing barrier/max.
+N > 1: one process per GPU, and ONE commit of the same workload split over
+the N GPUs (strong scaling): each GPU computes a coset of the LDE rows and
+hashes them, one NCCL all-to-all of 64-byte leaf digests gives each GPU a
+contiguous leaf block, and an all-gather of the N subtree roots finishes the
+tree.  The root is checked against the single-GPU commit of the same input.
 
 --impl reference times the reference algorithm on the host cores (the C
 restatement under oracle/, OpenMP over all cores -- the reference itself is
@@ -48,7 +51,9 @@ def workload_config(lg_l, w, lg_b, n_gpus):
         "lde_rows": 1 << (lg_l + lg_b),
         "bytes_in_per_rank": 8 * w << lg_l,
         "l2_policy": "inputs (2 GiB) and LDE (4 GiB) per step exceed the 126 MB L2; no flush",
-        "parallelism": f"independent commit per GPU x{n_gpus}",
+        "parallelism": "single GPU" if n_gpus == 1 else
+                       f"one commit split over {n_gpus} GPUs: coset rows per GPU, NCCL all-to-all of leaf digests, "
+                       "all-gather of subtree roots",
     }
 
 
@@ -197,6 +202,192 @@ def ntt_passes(lg):
     return 1 if lg <= 10 else (2 if lg <= 22 else 3)
 
 
+def int_peaks(zk, dev):
+    """Integer-pipe peak of this GPU, measured now: Goldilocks multiplications
+    per second of independent register-resident chains (no memory traffic),
+    and the Poseidon2 permutation rate without memory traffic (the ceiling of
+    the hash code)."""
+    import torch
+    lib, check = zk.lib, zk.check
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    n_thr, iters = 148 * 16 * 128, 2048
+    st = synth_device(n_thr * 16, 99, dev)
+    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, 16, sh), "mul probe warmup")
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pe0.record(stream)
+    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, iters, sh), "mul probe")
+    pe1.record(stream)
+    torch.cuda.synchronize()
+    mul_peak = n_thr * 8 * iters / (pe0.elapsed_time(pe1) / 1e3)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 1, sh), "permute warmup")
+    pe0.record(stream)
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 4, sh), "permute")
+    pe1.record(stream)
+    torch.cuda.synchronize()
+    return mul_peak, n_thr * 4 / (pe0.elapsed_time(pe1) / 1e3)
+
+
+def hbm_peak_gbs():
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(peaks_path):
+        try:
+            return float(json.load(open(peaks_path))["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (measured)"
+        except Exception:
+            pass
+    return HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
+
+
+def bus_id(dev):
+    import torch
+    props = torch.cuda.get_device_properties(dev)
+    bus = getattr(props, "pci_bus_id", None)
+    if bus is None:
+        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
+                                     getattr(props, "pci_device_id", 0))
+    return str(bus)
+
+
+def max_over_ranks(x, dev):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main_split(args, zk, dev, world, rank):
+    """N > 1: ONE commit of the workload split over the N ranks (strong
+    scaling): rank g computes the LDE rows g, g + N, ... (coset LDE, no data
+    exchange), hashes them, one all-to-all of 64-byte leaf digests gives each
+    rank a contiguous leaf block, each rank builds its subtree, and an
+    all-gather of the N subtree roots plus log2(N) compressions give the root
+    (zkie_b200/multigpu.py)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from zkie_b200.multigpu import SplitCommitter
+    lib, check = zk.lib, zk.check
+    lg_l, w, lg_b = args.lg_size, args.polys, args.lg_blowup
+    L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+    n_in = L * w
+    check(lib.zkie2_p2_init_default(), "init constants")
+    d_in = synth_device(n_in, 1234, dev)  # the same coefficients on every rank (replicated input)
+    sc = SplitCommitter(lg_l, lg_b, w)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        sc.run(d_in)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(bus_id(dev))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.5)
+    host_t0 = time.time()
+    t_start.record(stream)
+    for s in range(args.steps):
+        evs[s][0].record(stream)
+        sc.run(d_in, evs[s][1:])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    sampler.window(host_t0, time.time())
+    clocks = sampler.stop()
+    dist.barrier()
+    ms_per_step = max_over_ranks(t_start.elapsed_time(t_end), dev) / args.steps
+    phase = [sum(e[i].elapsed_time(e[i + 1]) for e in evs) / args.steps for i in range(4)]
+    ntt_ms, leaf_ms, exch_ms, tree_ms = phase
+    value = n_in / (ms_per_step / 1e3) / 1e6
+    root = sc.root()
+    # the split root must equal the single-device commit root of the same input
+    if rank == 0:
+        full = zk.commit(d_in.reshape(L, w), lg_b)
+        root_ok = bool((np.asarray(full.root, dtype=np.uint64) == root).all())
+        del full
+    else:
+        root_ok = None
+    torch.cuda.empty_cache()
+
+    mul_peak, perm_ceiling = int_peaks(zk, dev)
+    perms_leaf = sc.n_local * ((w + 7) // 8)
+    leaf_rate = perms_leaf / (leaf_ms / 1e3)
+    hbm_peak, hbm_src = hbm_peak_gbs()
+    ntt_bytes = 8 * w * (L + sc.n_local)
+    ntt_gbs = ntt_bytes / (ntt_ms / 1e3) / 1e9
+
+    # e2e: each rank copies its 1/N row slice of the pinned host input in,
+    # the full input is all-gathered over NVLink, and each rank copies its LDE
+    # rows and subtree layers back to pinned host memory
+    e2e = None
+    if not args.no_e2e:
+        rows = L // world
+        h_part = torch.empty(rows * w, dtype=torch.uint64, pin_memory=True)
+        h_part.view(torch.int64).copy_(d_in.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w])
+        h_lde = torch.empty(sc.n_local * w, dtype=torch.uint64, pin_memory=True)
+        h_layers = torch.empty(sc.layers.numel(), dtype=torch.uint64, pin_memory=True)
+        for _ in range(max(1, args.warmup)):
+            sc.run_host(h_part, h_lde, h_layers)
+        k_e2e = max(1, min(args.steps, 5))
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(k_e2e):
+            r = sc.run_host(h_part, h_lde, h_layers)
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / k_e2e, dev)
+        assert (r == root).all(), "host-path root differs from the device-path root"
+        e2e = {"value": round(n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
+               "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 8 * world * sc.layers.numel(),
+               "call": "SplitCommitter.run_host (per rank: pinned 1/N input slice in, NVLink all-gather, "
+                       "split commit, LDE rows + subtree layers back to pinned host)"}
+        del h_part, h_lde, h_layers
+
+    lg_local = lg_l + lg_b - sc.lg_g
+    launches = (1 + ntt_passes(lg_local)) + 1 + 1 + (lib.zkie2_merkle_num_layers(sc.n_local) - 1) + \
+        (lib.zkie2_merkle_num_layers(world) - 1)
+    cfg = workload_config(lg_l, w, lg_b, world)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "u64 (Goldilocks mod-p integer)", "data": "synthetic",
+        "config": cfg,
+        "roofline": {
+            "bound": "int", "kernel": f"k_leaf_rows (Poseidon2 leaf sponge, {(w + 7) // 8} permutations per row, "
+                                      f"{sc.n_local} rows per rank)",
+            "achieved": round(leaf_rate * MULS_PER_PERM / 1e9, 2), "peak": round(mul_peak / 1e9, 2),
+            "unit": "G Goldilocks mul/s (per GPU)", "frac": round(leaf_rate * MULS_PER_PERM / mul_peak, 4),
+            "traffic": None,
+            "work_per_unit": f"{MULS_PER_PERM} field multiplications per Poseidon2-16 permutation",
+            "peak_source": "measured live: zkie2_gl_mul_probe, independent register-resident multiply chains",
+            "perm_rate_gperm_s": round(leaf_rate / 1e9, 4), "perm_ceiling_gperm_s": round(perm_ceiling / 1e9, 4),
+            "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
+        },
+        "roofline_ntt": {
+            "bound": "hbm", "kernel": f"k_coset_twist + k_ntt_pass x{ntt_passes(lg_local)} (coset LDE, "
+                                      f"2^{lg_local} rows per rank)",
+            "achieved": round(ntt_gbs, 1), "peak": hbm_peak, "unit": "GB/s (per GPU)",
+            "frac": round(ntt_gbs / hbm_peak, 4), "traffic": None,
+            "algorithmic_bytes": ntt_bytes, "peak_source": hbm_src,
+            "ms_per_step": round(ntt_ms, 4), "share_of_step": round(ntt_ms / ms_per_step, 4),
+        },
+        "exchange_ms_per_step": round(exch_ms, 4),
+        "exchange_bytes_per_rank": 64 * sc.n_local * (world - 1) // world,
+        "nodes_ms_per_step": round(tree_ms, 4),
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+        "root_rank0": [hex(int(x)) for x in root[:2]],
+        "root_matches_single_gpu_commit": root_ok,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -225,13 +416,15 @@ def main():
         b.build()
         import zkie_b200 as zk
     lib, check = zk.lib, zk.check
+    if world > 1:
+        return main_split(args, zk, dev, world, rank)
 
     lg_l, w, lg_b = args.lg_size, args.polys, args.lg_blowup
     L, H = 1 << lg_l, 1 << (lg_l + lg_b)
     lg = lg_l + lg_b
     n_in = L * w
     check(lib.zkie2_p2_init_default(), "init constants")
-    d_in = synth_device(n_in, 1234 + rank, dev)
+    d_in = synth_device(n_in, 1234, dev)
     d_lde = torch.empty(H * w, dtype=torch.uint64, device=dev)
     total_dig = lib.zkie2_merkle_total_digests(H)
     d_layers = torch.empty(total_dig * 8, dtype=torch.uint64, device=dev)
@@ -255,12 +448,7 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    bus = getattr(torch.cuda.get_device_properties(dev), "pci_bus_id", None)
-    if bus is None:
-        props = torch.cuda.get_device_properties(dev)
-        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
-                                     getattr(props, "pci_device_id", 0))
-    sampler = ClockSampler(str(bus))
+    sampler = ClockSampler(bus_id(dev))
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -291,38 +479,12 @@ def main():
     value = world * n_in / (ms_per_step / 1e3) / 1e6
     root = d_layers[-8:].cpu().numpy()
 
-    # integer-pipe peak: Goldilocks multiplications per second of independent
-    # register-resident chains (no memory traffic), measured on this GPU now
-    n_thr, iters = 148 * 16 * 128, 2048
-    st = synth_device(n_thr * 16, 99, dev)
-    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, 16, sh), "mul probe warmup")
-    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    pe0.record(stream)
-    check(lib.zkie2_gl_mul_probe(st.data_ptr(), n_thr, iters, sh), "mul probe")
-    pe1.record(stream)
-    torch.cuda.synchronize()
-    mul_peak = n_thr * 8 * iters / (pe0.elapsed_time(pe1) / 1e3)
-    # the permutation itself without memory traffic (ceiling of the hash code)
-    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 1, sh), "permute warmup")
-    pe0.record(stream)
-    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 4, sh), "permute")
-    pe1.record(stream)
-    torch.cuda.synchronize()
-    perm_ceiling = n_thr * 4 / (pe0.elapsed_time(pe1) / 1e3)
-
+    mul_peak, perm_ceiling = int_peaks(zk, dev)
     perms_leaf = H * ((w + 7) // 8)
     leaf_rate = perms_leaf / (leaf_ms / 1e3)
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    hbm_peak, hbm_src = HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
-    if os.path.exists(peaks_path):
-        try:
-            hbm_peak = float(json.load(open(peaks_path))["hbm_gbs"])
-            hbm_src = "MEASURED_PEAKS.json hbm_gbs (measured)"
-        except Exception:
-            pass
+    hbm_peak, hbm_src = hbm_peak_gbs()
     ntt_bytes = 8 * w * (L + H)
     ntt_gbs = ntt_bytes / (ntt_ms / 1e3) / 1e9
-    del st
 
     # ---- e2e through the host-buffer C-ABI call ----
     e2e = None

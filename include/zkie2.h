@@ -57,6 +57,14 @@ int zkie2_dft_twiddles(uint32_t lg, uint64_t *h_out);
 /* Out-of-place DFT of every column (h = 2^lg_h); scratch as zkie2_lde(lg_h, 0, w). */
 int zkie2_dft(const uint64_t *d_in, uint64_t *d_out, uint64_t *d_scratch, uint32_t lg_h, uint64_t w,
               zkie_stream_t stream);
+/* One coset of the zero-padded LDE, for commits split over G = 2^lg_g GPUs:
+ * d_out ((H/G) x w, H = L << lg_blowup) receives rows g, g + G, g + 2G, ...
+ * of the zkie2_lde output, computed by one H/G-point DFT of the twisted (and,
+ * when G > 2^lg_blowup, folded) input.  No reference counterpart: the
+ * reference commits on one device. */
+uint64_t zkie2_lde_coset_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_g);
+int zkie2_lde_coset(const uint64_t *d_in, uint64_t *d_out, uint64_t *d_scratch, uint32_t lg_l,
+                    uint32_t lg_blowup, uint64_t w, uint32_t lg_g, uint64_t g, zkie_stream_t stream);
 
 /* ---- Merkle ----------------------------------------------------------------- */
 
@@ -75,6 +83,12 @@ int zkie2_merkle_tree(const uint64_t *d_mat, uint64_t h, uint64_t w, uint64_t *d
 /* Layers 1.. of the tree whose h leaf digests are already in d_layers[0 .. 8h)
  * (the compression loop of pcs/merkle_cuda.rs:250-280). */
 int zkie2_merkle_tree_from_leaves(uint64_t h, uint64_t *d_layers, zkie_stream_t stream);
+/* Split commit over g GPUs: after the all-to-all of leaf digests a rank holds,
+ * per source rank r, the n digests of rows r, r + g, r + 2g, ... of its leaf
+ * block (source-major); d_out receives them in row order:
+ * d_out[c*g + r] = d_in[r*n + c] (64-byte digests; d_in != d_out). */
+int zkie2_digests_interleave(const uint64_t *d_in, uint64_t g, uint64_t n, uint64_t *d_out,
+                             zkie_stream_t stream);
 
 /* ---- commit (LDE + Merkle) ---------------------------------------------------- */
 

@@ -1,0 +1,98 @@
+"""Split commit on the GPU: zkie2_lde_coset against the full zkie2_lde, the
+whole split path emulated on one device (all G ranks in turn) against the
+single-device commit root, and, when the box has two or more GPUs, the real
+NCCL split over two ranks."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+P = 0xFFFFFFFF00000001
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _constants(zk):
+    zk.check(zk.lib.zkie2_p2_init_default(), "constants")
+
+
+def coeffs(seed, L, w):
+    g = np.random.default_rng(seed)
+    v = g.integers(0, 2 ** 64, size=(L, w), dtype=np.uint64)
+    return np.where(v >= np.uint64(P), v - np.uint64(P), v)
+
+
+@pytest.mark.parametrize("lg_l,lg_b,w,G", [(4, 1, 3, 2), (10, 1, 8, 2), (10, 1, 8, 8), (12, 2, 5, 4),
+                                          (12, 1, 16, 16), (16, 1, 32, 8), (18, 1, 4, 2)])
+def test_lde_coset_rows(zk, lg_l, lg_b, w, G):
+    from zkie_b200.multigpu import DeviceOps
+    x = torch.from_numpy(coeffs(lg_l + G, 1 << lg_l, w).reshape(-1)).cuda()
+    full = zk.commit(x.reshape(1 << lg_l, w), lg_b).lde.reshape(-1, w)
+    ops = DeviceOps()
+    lg_g = G.bit_length() - 1
+    for g in range(G):
+        rows = ops.lde_coset(x, lg_l, lg_b, w, lg_g, g).reshape(-1, w)
+        assert torch.equal(rows.view(torch.int64), full.view(torch.int64)[g::G]), (g, G)
+
+
+def test_lde_coset_matches_oracle(zk, orc):
+    from zkie_b200.multigpu import DeviceOps
+    lg_l, lg_b, w, G = 8, 1, 4, 4
+    x = coeffs(3, 1 << lg_l, w)
+    full = orc.lde(x, lg_b)
+    for g in range(G):
+        rows = DeviceOps().lde_coset(torch.from_numpy(x.reshape(-1)).cuda(), lg_l, lg_b, w, 2, g)
+        assert np.array_equal(rows.cpu().numpy().reshape(-1, w), full[g::G])
+
+
+@pytest.mark.parametrize("lg_l,lg_b,w,G", [(10, 1, 16, 2), (12, 1, 32, 4), (14, 1, 32, 8), (16, 2, 8, 8)])
+def test_split_commit_emulated_root(zk, lg_l, lg_b, w, G):
+    from zkie_b200.multigpu import split_commit_emulated
+    x = torch.from_numpy(coeffs(lg_l * G, 1 << lg_l, w).reshape(-1)).cuda()
+    want = zk.commit(x.reshape(1 << lg_l, w), lg_b).root
+    root, _ = split_commit_emulated(x, lg_l, lg_b, w, G)
+    assert np.array_equal(root, np.asarray(want, dtype=np.uint64))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _nccl_rank(rank, world, port, lg_l, lg_b, w, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import zkie_b200 as zk
+        from zkie_b200.multigpu import split_commit
+        zk.check(zk.lib.zkie2_p2_init_default(), "constants")
+        x = torch.from_numpy(coeffs(91, 1 << lg_l, w).reshape(-1)).cuda()
+        res = split_commit(x, lg_l, lg_b, w)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"root{rank}.npy"), res.root)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_split_commit_nccl_two_ranks(zk, tmp_path):
+    lg_l, lg_b, w = 14, 1, 32
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), lg_l, lg_b, w, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    x = torch.from_numpy(coeffs(91, 1 << lg_l, w).reshape(-1)).cuda()
+    want = np.asarray(zk.commit(x.reshape(1 << lg_l, w), lg_b).root, dtype=np.uint64)
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"root{r}.npy"), want), r

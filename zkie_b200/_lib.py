@@ -46,11 +46,14 @@ SIGNATURES = {
     "zkie2_lde": (i64, [vp, vp, vp, u32, u32, u64, vp]),
     "zkie2_dft_twiddles": (i64, [u32, pu64]),
     "zkie2_dft": (i64, [vp, vp, vp, u32, u64, vp]),
+    "zkie2_lde_coset_scratch_elems": (u64, [u32, u32, u64, u32]),
+    "zkie2_lde_coset": (i64, [vp, vp, vp, u32, u32, u64, u32, u64, vp]),
     "zkie2_merkle_total_digests": (u64, [u64]),
     "zkie2_merkle_num_layers": (u32, [u64]),
     "zkie2_merkle_leaves": (i64, [vp, u64, u64, vp, vp]),
     "zkie2_merkle_tree": (i64, [vp, u64, u64, vp, vp]),
     "zkie2_merkle_tree_from_leaves": (i64, [u64, vp, vp]),
+    "zkie2_digests_interleave": (i64, [vp, u64, u64, vp, vp]),
     "zkie2_commit_scratch_elems": (u64, [u32, u32, u64]),
     "zkie2_commit": (i64, [vp, u32, u32, u64, vp, vp, vp, vp]),
     "zkie2_whir_scratch_elems": (u64, [u32]),

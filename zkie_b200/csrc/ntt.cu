@@ -327,6 +327,28 @@ int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, 
     return dft_plan_t<kCallerTab, uint64_t>(in, out, scratch, lg, w, rows_valid, tab, tab_log, s);
 }
 
+// Input of one coset of the LDE (the rows i = g + G*i' of the H-row output):
+// y[j'][c] = sum_{m < nfold} x[j' + m*stride][c] * W_H^((j' + m*stride) * g)
+// for j' < R.  Rows of x at or past L are zero.  Then the coset is the
+// R-point DFT of y (zero-padded to H/G rows when R = L < H/G).
+__global__ void __launch_bounds__(256)
+    k_coset_twist(const uint64_t* __restrict__ x, uint64_t L, uint64_t w, uint32_t lg_h, uint64_t g, uint64_t R,
+                  uint64_t stride, uint32_t nfold, uint64_t* __restrict__ y) {
+    const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= R * w) return;
+    const uint64_t jp = idx / w, c = idx - jp * w;
+    Acc160 acc = acc160_zero();
+    for (uint32_t m = 0; m < nfold; m++) {
+        const uint64_t j = jp + m * stride;
+        if (j >= L) break;
+        // W_H^(j g) with W_H = w32^(2^(32 - lg_h)): exponent of w32 mod 2^32
+        const uint32_t E = (uint32_t)(((j * g) << (32 - lg_h)) & 0xFFFFFFFFull);
+        const uint64_t tw = gl_mul(__ldg(g_tw_lo + (E & 0xFFFF)), __ldg(g_tw_hi + (E >> 16)));
+        acc160_mac(acc, __ldg(x + j * w + c), tw);
+    }
+    y[idx] = gl_canon(acc160_reduce(acc));
+}
+
 }  // namespace
 
 uint64_t lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w) {
@@ -343,6 +365,40 @@ int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
     int rc = ensure_twiddles();
     if (rc) return rc;
     return dft_plan<false>(in, out, scratch, lg, w, 1ull << lg_l, nullptr, 0, s);
+}
+
+// Coset g of G = 2^lg_g of the LDE (H = 2^(lg_l + lg_blowup) rows): rows
+// i = g + G*i', i' < H/G, in order.  Row i of the LDE is X(W_H^i), so the
+// coset is the H/G-point DFT of x[j] W_H^(j g) with the input folded modulo
+// H/G: when G <= blowup the L nonzero rows fit (twist, then an LDE of blowup
+// 2^(lg_blowup - lg_g)); when G > blowup, G/blowup input rows land on each
+// of the H/G DFT inputs.  Scratch: rows(y) * w for y, then the sub-LDE's.
+uint64_t lde_coset_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_g) {
+    const uint32_t lg_h = lg_l + lg_blowup;
+    if (lg_g > lg_h) return 0;
+    const uint32_t lg_y = lg_g <= lg_blowup ? lg_l : lg_h - lg_g;
+    const uint32_t lg_sub = lg_h - lg_g;
+    return (w << lg_y) + lde_scratch_elems(lg_sub, 0, w) + 2;
+}
+
+int lde_coset_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l, uint32_t lg_blowup,
+                     uint64_t w, uint32_t lg_g, uint64_t g, cudaStream_t s) {
+    const uint32_t lg_h = lg_l + lg_blowup;
+    if (w == 0) return 0;
+    if (!in || !out || !scratch || lg_g > lg_h || lg_h > 30 || g >= (1ull << lg_g)) return (int)cudaErrorInvalidValue;
+    int rc = ensure_twiddles();
+    if (rc) return rc;
+    const bool fold = lg_g > lg_blowup;
+    const uint32_t lg_y = fold ? lg_h - lg_g : lg_l;
+    const uint64_t R = 1ull << lg_y;
+    uint64_t* y = scratch;
+    uint64_t* sub = scratch + ((w << lg_y) + 1 & ~1ull);  // keep 16-byte alignment
+    const uint64_t n = R * w;
+    k_coset_twist<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(in, 1ull << lg_l, w, lg_h, g, R, 1ull << (lg_h - lg_g),
+                                                              fold ? 1u << (lg_g - lg_blowup) : 1u, y);
+    ZK_LAUNCH_CHECK();
+    if (fold) return dft_plan<false>(y, out, sub, lg_h - lg_g, w, ~0ull, nullptr, 0, s);
+    return dft_plan<false>(y, out, sub, lg_h - lg_g, w, 1ull << lg_l, nullptr, 0, s);
 }
 
 }  // namespace zk
@@ -397,6 +453,15 @@ int zkie2_dft_twiddles(uint32_t lg, uint64_t* h_out) {
 int zkie2_dft(const uint64_t* d_in, uint64_t* d_out, uint64_t* d_scratch, uint32_t lg_h, uint64_t w,
               cudaStream_t stream) {
     return lde_launch(d_in, d_out, d_scratch, lg_h, 0, w, stream);
+}
+
+uint64_t zkie2_lde_coset_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_g) {
+    return lde_coset_scratch_elems(lg_l, lg_blowup, w, lg_g);
+}
+
+int zkie2_lde_coset(const uint64_t* d_in, uint64_t* d_out, uint64_t* d_scratch, uint32_t lg_l, uint32_t lg_blowup,
+                    uint64_t w, uint32_t lg_g, uint64_t g, cudaStream_t stream) {
+    return lde_coset_launch(d_in, d_out, d_scratch, lg_l, lg_blowup, w, lg_g, g, stream);
 }
 
 }  // extern "C"

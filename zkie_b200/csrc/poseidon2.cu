@@ -131,6 +131,16 @@ __global__ void __launch_bounds__(kHashThreads) k_gl_mul_probe(uint64_t* __restr
     for (int q = 0; q < 8; q++) buf[i * 16 + q] = gl_canon(x[q]);
 }
 
+// out digest c*G + r = in digest r*n + c (a G x n -> n x G transpose of
+// 64-byte digests), one thread per u64 word.
+__global__ void k_digest_interleave(const uint64_t* __restrict__ in, uint64_t G, uint64_t n,
+                                    uint64_t* __restrict__ out) {
+    const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= G * n * 8) return;
+    const uint64_t d = idx >> 3, c = d / G, r = d - c * G;
+    out[idx] = __ldg(in + ((r * n + c) << 3) + (idx & 7));
+}
+
 uint64_t canon_host(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
 
 }  // namespace
@@ -333,6 +343,18 @@ int zkie2_merkle_tree_from_leaves(uint64_t h, uint64_t* d_layers, cudaStream_t s
     if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
     if (!d_layers || h == 0) return (int)cudaErrorInvalidValue;
     return merkle_build_from_leaves(h, d_layers, stream);
+}
+
+// Split commit: after the all-to-all of leaf digests a rank holds, for each of
+// the G source ranks r, the n digests of rows r, r + G, r + 2G, ... of its
+// leaf block; this puts them in row order (d_out[c*G + r] = d_in[r*n + c]).
+int zkie2_digests_interleave(const uint64_t* d_in, uint64_t g, uint64_t n, uint64_t* d_out, cudaStream_t stream) {
+    if (!d_in || !d_out || d_in == d_out) return (int)cudaErrorInvalidValue;
+    const uint64_t words = g * n * 8;
+    if (words == 0) return 0;
+    k_digest_interleave<<<(unsigned)ceil_div(words, 256), 256, 0, stream>>>(d_in, g, n, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
 }
 
 }  // extern "C"

@@ -1,0 +1,220 @@
+"""Multi-GPU shard commit: one LDE + Merkle commitment split over the ranks of
+a process group (one process per GPU, torch.distributed over NCCL).
+
+The reference commits each matrix on one device (pcs/merkle_cuda.rs:177-312,
+pcs/dft_cuda.rs:161-221); the split gives the same root.  With G ranks
+(G a power of two, G^2 <= H):
+
+1. Rank g computes the LDE rows i = g + G*i' (i' < H/G): the coset
+   W_H^g <W_H^G> of the evaluation domain, one H/G-point DFT of the twisted
+   input (``zkie2_lde_coset``).  The coefficients are replicated; no data
+   moves for the NTT.  The LDE stays sharded that way.
+2. Rank g hashes its rows (each rank holds every column of its rows).
+3. One all-to-all of leaf digests (64 B per row): rank g's digests are
+   already grouped by destination (rows of rank d's leaf block
+   [d*H/G, (d+1)*H/G) are its local rows [d*H/G^2, (d+1)*H/G^2)), so the
+   exchange is an equal-split ``all_to_all_single``.  The receiver puts the G
+   source-major runs in row order (``zkie2_digests_interleave``).
+4. Each rank builds the subtree of its contiguous leaf block; an all-gather of
+   the G subtree roots and the top log2(G) compressions (computed on every
+   rank) give the root.
+
+Collectives carry u64 payloads as int64 views (bit-identical).  The compute
+steps go through an ops object: ``DeviceOps`` (the C ABI, CUDA tensors) in
+production; the CPU tests pass an oracle-backed implementation with the same
+methods and run the same orchestration under gloo.
+"""
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ._lib import check, lib
+from .device import empty, ptr, stream_handle, to_dev
+
+
+def _lg(n: int) -> int:
+    lg = n.bit_length() - 1
+    if n != 1 << lg:
+        raise ValueError("not a power of two")
+    return lg
+
+
+class DeviceOps:
+    """Compute steps of the split commit on the current CUDA device."""
+
+    def lde_coset(self, coeffs, lg_l, lg_b, w, lg_g, g):
+        rows = 1 << (lg_l + lg_b - lg_g)
+        out = empty(rows * w)
+        scr = empty(max(lib.zkie2_lde_coset_scratch_elems(lg_l, lg_b, w, lg_g), 2))
+        check(lib.zkie2_lde_coset(ptr(coeffs), ptr(out), ptr(scr), lg_l, lg_b, w, lg_g, g, stream_handle()),
+              "zkie2_lde_coset")
+        return out
+
+    def leaves(self, lde, rows, w):
+        out = empty(rows * 8)
+        check(lib.zkie2_merkle_leaves(ptr(lde), rows, w, ptr(out), stream_handle()), "zkie2_merkle_leaves")
+        return out
+
+    def interleave(self, buf, G, n):
+        out = empty(G * n * 8)
+        check(lib.zkie2_digests_interleave(ptr(buf), G, n, ptr(out), stream_handle()), "zkie2_digests_interleave")
+        return out
+
+    def tree(self, leaves, n):
+        """All layers of the tree over n leaf digests; returns (layers, root)."""
+        layers = empty(lib.zkie2_merkle_total_digests(n) * 8)
+        layers[: n * 8].copy_(leaves[: n * 8])
+        check(lib.zkie2_merkle_tree_from_leaves(n, ptr(layers), stream_handle()), "zkie2_merkle_tree_from_leaves")
+        return layers, layers[-8:]
+
+
+@dataclass
+class SplitCommit:
+    root: np.ndarray          # 8 u64, identical on every rank
+    lde: object               # this rank's LDE rows g, g + G, ... ((H/G) x w)
+    layers: object            # layers of this rank's subtree (leaf block [g*H/G, (g+1)*H/G))
+    top_layers: object        # layers of the tree over the G subtree roots
+    rank: int
+    world: int
+
+
+def _as_i64(t):
+    return t.view(torch.int64) if t.dtype == torch.uint64 else t
+
+
+def split_commit(coeffs, lg_l: int, lg_blowup: int, w: int, group=None, ops=None) -> SplitCommit:
+    """Commit the L x w coefficient matrix (replicated on every rank) at
+    blowup 2^lg_blowup, split over the ranks of ``group``."""
+    ops = ops or DeviceOps()
+    G = dist.get_world_size(group) if dist.is_initialized() else 1
+    g = dist.get_rank(group) if dist.is_initialized() else 0
+    lg_g = _lg(G)
+    H = 1 << (lg_l + lg_blowup)
+    if G * G > H:
+        raise ValueError("split commit needs G^2 <= rows")
+    n_local = H // G
+    lde = ops.lde_coset(coeffs, lg_l, lg_blowup, w, lg_g, g)
+    dig = ops.leaves(lde, n_local, w)
+    if G > 1:
+        recv = torch.empty_like(_as_i64(dig))
+        dist.all_to_all_single(recv, _as_i64(dig), group=group)
+        leaves = ops.interleave(recv.view(dig.dtype), G, n_local // G)
+    else:
+        leaves = dig
+    layers, sub_root = ops.tree(leaves, n_local)
+    if G > 1:
+        parts = [torch.empty(8, dtype=torch.int64, device=sub_root.device) for _ in range(G)]
+        dist.all_gather(parts, _as_i64(sub_root).contiguous(), group=group)
+        top_layers, root = ops.tree(torch.cat(parts).view(sub_root.dtype), G)
+    else:
+        top_layers, root = None, sub_root
+    return SplitCommit(np.asarray(root.cpu().numpy() if hasattr(root, "cpu") else root, dtype=np.uint64),
+                       lde, layers, top_layers, g, G)
+
+
+def split_commit_emulated(coeffs, lg_l: int, lg_blowup: int, w: int, G: int, ops=None):
+    """All G ranks of ``split_commit`` run one after another in this process,
+    with the all-to-all and the all-gather done by slicing.  Returns the root
+    and the per-rank LDE cosets; used to check the split path on one device."""
+    ops = ops or DeviceOps()
+    lg_g = _lg(G)
+    H = 1 << (lg_l + lg_blowup)
+    n_local = H // G
+    ldes = [ops.lde_coset(coeffs, lg_l, lg_blowup, w, lg_g, g) for g in range(G)]
+    digs = [ops.leaves(lde, n_local, w) for lde in ldes]
+    per = n_local // G  # digests rank g sends to each destination
+    sub_roots = []
+    for d in range(G):
+        recv = torch.cat([digs[g][d * per * 8:(d + 1) * per * 8] for g in range(G)])
+        leaves = ops.interleave(recv, G, per) if G > 1 else recv
+        sub_roots.append(ops.tree(leaves, n_local)[1])
+    if G > 1:
+        _, root = ops.tree(torch.cat(sub_roots), G)
+    else:
+        root = sub_roots[0]
+    return np.asarray(root.cpu().numpy() if hasattr(root, "cpu") else root, dtype=np.uint64), ldes
+
+
+def commit_inputs(coeffs):
+    """The coefficient matrix as a contiguous device tensor."""
+    return to_dev(coeffs).reshape(-1)
+
+
+class SplitCommitter:
+    """``split_commit`` with every buffer allocated once, for repeated commits
+    of the same geometry on this rank (the timed loop of bench.py).  ``run``
+    takes the replicated coefficients already on the device; ``run_host``
+    takes this rank's 1/G row slice of a pinned host matrix, copies it in,
+    all-gathers the full matrix over NVLink and copies this rank's LDE rows
+    and subtree layers back to pinned host buffers."""
+
+    def __init__(self, lg_l: int, lg_blowup: int, w: int, group=None):
+        self.group = group
+        self.G = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.g = dist.get_rank(group) if dist.is_initialized() else 0
+        self.lg_g = _lg(self.G)
+        self.lg_l, self.lg_b, self.w = lg_l, lg_blowup, w
+        H = 1 << (lg_l + lg_blowup)
+        if self.G * self.G > H:
+            raise ValueError("split commit needs G^2 <= rows")
+        self.n_local = H // self.G
+        self.lde = empty(self.n_local * w)
+        self.scr = empty(max(lib.zkie2_lde_coset_scratch_elems(lg_l, lg_blowup, w, self.lg_g), 2))
+        self.dig = empty(self.n_local * 8)
+        self.recv = empty(self.n_local * 8)
+        self.layers = empty(lib.zkie2_merkle_total_digests(self.n_local) * 8)
+        self.roots = torch.empty(self.G * 8, dtype=torch.int64, device=self.lde.device)
+        self.top = empty(lib.zkie2_merkle_total_digests(self.G) * 8)
+        self.full_in = None
+
+    def run(self, coeffs, events=None):
+        """One split commit; events (if given) are recorded after the LDE, the
+        leaf hashes, the digest exchange and the tree, on the current stream."""
+        s = stream_handle()
+        cur = torch.cuda.current_stream()
+        check(lib.zkie2_lde_coset(ptr(coeffs), ptr(self.lde), ptr(self.scr), self.lg_l, self.lg_b, self.w,
+                                  self.lg_g, self.g, s), "zkie2_lde_coset")
+        if events:
+            events[0].record(cur)
+        check(lib.zkie2_merkle_leaves(ptr(self.lde), self.n_local, self.w, ptr(self.dig), s), "zkie2_merkle_leaves")
+        if events:
+            events[1].record(cur)
+        if self.G > 1:
+            dist.all_to_all_single(self.recv.view(torch.int64), self.dig.view(torch.int64), group=self.group)
+            check(lib.zkie2_digests_interleave(ptr(self.recv), self.G, self.n_local // self.G, ptr(self.layers), s),
+                  "zkie2_digests_interleave")
+        else:
+            self.layers[: self.n_local * 8].copy_(self.dig)
+        if events:
+            events[2].record(cur)
+        check(lib.zkie2_merkle_tree_from_leaves(self.n_local, ptr(self.layers), s), "zkie2_merkle_tree_from_leaves")
+        if self.G > 1:
+            dist.all_gather_into_tensor(self.roots, self.layers[-8:].view(torch.int64), group=self.group)
+            self.top[: self.G * 8].view(torch.int64).copy_(self.roots)
+            check(lib.zkie2_merkle_tree_from_leaves(self.G, ptr(self.top), s), "zkie2_merkle_tree_from_leaves")
+        if events:
+            events[3].record(cur)
+
+    def root(self):
+        src = self.top if self.G > 1 else self.layers
+        return src[-8:].cpu().numpy()
+
+    def run_host(self, h_part, h_lde, h_layers):
+        """h_part: this rank's rows [g*L/G, (g+1)*L/G) of the L x w input (pinned
+        host, int64 or uint64 view); h_lde / h_layers: pinned outputs."""
+        L = 1 << self.lg_l
+        if self.full_in is None:
+            self.full_in = empty(L * self.w)
+            self.part = empty(L * self.w // self.G)
+        self.part.view(torch.int64).copy_(h_part.view(torch.int64), non_blocking=True)
+        if self.G > 1:
+            dist.all_gather_into_tensor(self.full_in.view(torch.int64), self.part.view(torch.int64), group=self.group)
+        else:
+            self.full_in.copy_(self.part)
+        self.run(self.full_in)
+        h_lde.view(torch.int64).copy_(self.lde.view(torch.int64), non_blocking=True)
+        h_layers.view(torch.int64).copy_(self.layers.view(torch.int64), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return self.root()
