@@ -45,3 +45,16 @@ class OracleOps:
     def tree(self, leaves, n):
         root = self.orc.merkle_root_from_leaves(self.consts, self._np(leaves).reshape(n, 8))
         return None, torch.from_numpy(root.copy())
+
+
+class OracleSumcheckOps:
+    """Local degree-2 sumcheck by the oracle (sumcheck.rs:33-79 restated)."""
+
+    def __init__(self, orc):
+        self.orc = orc
+
+    def sumcheck(self, f, h, challenges):
+        f = f.numpy() if isinstance(f, torch.Tensor) else np.asarray(f, dtype=np.uint64)
+        h = h.numpy() if isinstance(h, torch.Tensor) else np.asarray(h, dtype=np.uint64)
+        rounds, finals = self.orc.sumcheck_prove(f, h, np.asarray(challenges, dtype=np.uint64))
+        return np.asarray(rounds, dtype=np.uint64).reshape(-1, 3), int(finals[0]), int(finals[1])

@@ -96,3 +96,60 @@ def test_split_commit_nccl_two_ranks(zk, tmp_path):
     want = np.asarray(zk.commit(x.reshape(1 << lg_l, w), lg_b).root, dtype=np.uint64)
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"root{r}.npy"), want), r
+
+
+@pytest.mark.parametrize("G,t", [(2, 12), (4, 20), (8, 16)])
+def test_split_sumcheck_math_on_one_gpu(zk, orc, G, t):
+    """The split-sumcheck combination on one device: local proofs of the G
+    high-variable chunks, round messages summed mod p, the last log2(G) rounds
+    over the gathered folded values -- equal to the single-device proof."""
+    from zkie_b200.multigpu import DeviceSumcheckOps
+    f, h = coeffs(t, 1 << t, 1).reshape(-1), coeffs(t + 1, 1 << t, 1).reshape(-1)
+    ch = coeffs(t + 2, t, 1).reshape(-1)
+    lg_g = G.bit_length() - 1
+    n = (1 << t) // G
+    ops = DeviceSumcheckOps()
+    loc = [ops.sumcheck(f[g * n:(g + 1) * n], h[g * n:(g + 1) * n], ch[:t - lg_g]) for g in range(G)]
+    summed = np.array([[sum(int(p[0][r][c]) for p in loc) % P for c in range(3)] for r in range(t - lg_g)],
+                      dtype=np.uint64)
+    tail, fe, he = ops.sumcheck(np.array([p[1] for p in loc], dtype=np.uint64),
+                                np.array([p[2] for p in loc], dtype=np.uint64), ch[t - lg_g:])
+    rounds, finals = orc.sumcheck_prove(f, h, ch)
+    assert np.array_equal(np.concatenate([summed, tail]), rounds)
+    assert (fe, he) == (int(finals[0]), int(finals[1]))
+
+
+def _nccl_sumcheck_rank(rank, world, port, t, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from zkie_b200.multigpu import split_sumcheck
+        f, h = coeffs(31, 1 << t, 1).reshape(-1), coeffs(32, 1 << t, 1).reshape(-1)
+        ch = coeffs(33, t, 1).reshape(-1)
+        n = (1 << t) // world
+        df = torch.from_numpy(f[rank * n:(rank + 1) * n].copy()).cuda()
+        dh = torch.from_numpy(h[rank * n:(rank + 1) * n].copy()).cuda()
+        rounds, fe, he = split_sumcheck(df, dh, t, ch)
+        np.save(os.path.join(out_dir, f"sc{rank}.npy"),
+                np.concatenate([rounds.reshape(-1), np.array([fe, he], dtype=np.uint64)]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_split_sumcheck_nccl_two_ranks(orc, tmp_path):
+    t = 20
+    mp.start_processes(_nccl_sumcheck_rank, args=(2, _free_port(), t, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    f, h = coeffs(31, 1 << t, 1).reshape(-1), coeffs(32, 1 << t, 1).reshape(-1)
+    rounds, finals = orc.sumcheck_prove(f, h, coeffs(33, t, 1).reshape(-1))
+    want = np.concatenate([np.asarray(rounds, dtype=np.uint64).reshape(-1), np.asarray(finals, dtype=np.uint64)])
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"sc{r}.npy"), want), r

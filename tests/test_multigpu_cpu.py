@@ -79,3 +79,36 @@ def test_gloo_split_commit(orc, consts, tmp_path, world):
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"root{r}.npy"), want), r
         assert np.array_equal(np.load(tmp_path / f"lde{r}.npy").reshape(-1, w), full[r::world]), r
+
+
+def _sc_rank_main(rank, world, port, t, out_dir):
+    import torch.distributed as dist
+
+    from oracle import oracle as orc
+    from tests.mgpu_ops import OracleSumcheckOps
+    from zkie_b200.multigpu import split_sumcheck
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        f, h, ch = coeffs(5, 1 << t, 1).reshape(-1), coeffs(6, 1 << t, 1).reshape(-1), coeffs(7, t, 1).reshape(-1)
+        n = (1 << t) // world
+        rounds, fe, he = split_sumcheck(f[rank * n:(rank + 1) * n], h[rank * n:(rank + 1) * n], t, ch,
+                                        ops=OracleSumcheckOps(orc), device=torch.device("cpu"))
+        np.save(os.path.join(out_dir, f"sc{rank}.npy"),
+                np.concatenate([rounds.reshape(-1), np.array([fe, he], dtype=np.uint64)]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,t", [(2, 9), (4, 10), (4, 2)])
+def test_gloo_split_sumcheck(orc, tmp_path, world, t):
+    """Hypercube split by the high variables: local rounds, one all-reduce of
+    the round messages (32-bit limbs), last log2(world) rounds on every rank."""
+    mp.start_processes(_sc_rank_main, args=(world, _free_port(), t, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    f, h, ch = coeffs(5, 1 << t, 1).reshape(-1), coeffs(6, 1 << t, 1).reshape(-1), coeffs(7, t, 1).reshape(-1)
+    rounds, finals = orc.sumcheck_prove(f, h, ch)
+    want = np.concatenate([np.asarray(rounds, dtype=np.uint64).reshape(-1), np.asarray(finals, dtype=np.uint64)])
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"sc{r}.npy"), want), r

@@ -142,6 +142,61 @@ def commit_inputs(coeffs):
     return to_dev(coeffs).reshape(-1)
 
 
+# ---- split sumcheck ------------------------------------------------------------------------
+P = 0xFFFFFFFF00000001
+
+
+class DeviceSumcheckOps:
+    """Local degree-2 sumcheck on the current CUDA device (zkie2_sumcheck_prove)."""
+
+    def sumcheck(self, f, h, challenges):
+        from .gkr import sumcheck_prove
+        p = sumcheck_prove(f, h, 0, challenges)
+        return np.asarray(p.rounds, dtype=np.uint64).reshape(-1, 3), p.f_eval, p.h_eval
+
+
+def field_allreduce_sum(vals: np.ndarray, device, group=None) -> np.ndarray:
+    """Sum of canonical field elements over the ranks: one all-reduce of their
+    32-bit limbs as int64 (exact for up to 2^31 ranks), then mod p."""
+    v = np.asarray(vals, dtype=np.uint64).reshape(-1)
+    limbs = np.stack([v & np.uint64(0xFFFFFFFF), v >> np.uint64(32)]).astype(np.int64)
+    t = torch.from_numpy(limbs).to(device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    lo, hi = t.cpu().numpy().astype(object)
+    return np.array([(int(a) + (int(b) << 32)) % P for a, b in zip(lo, hi)], dtype=np.uint64)
+
+
+def split_sumcheck(f_local, h_local, t: int, challenges, group=None, ops=None, device=None):
+    """sumcheck::prove (common/sumcheck.rs:33-79) of f, h of length 2^t split
+    over G ranks by the high variables: rank g holds elements
+    [g*2^t/G, (g+1)*2^t/G).  Rounds fold the low variable first, so each rank
+    runs the first t - log2(G) rounds on its chunk alone (challenges are known
+    up front); the round messages are linear in the pair sums, so their sum
+    over ranks is the global message: one all-reduce for all local rounds.
+    The G folded values of f and h are all-gathered and the last log2(G)
+    rounds run on every rank.  Returns (rounds (t x 3), f_eval, h_eval),
+    identical to the single-device proof."""
+    ops = ops or DeviceSumcheckOps()
+    G = dist.get_world_size(group) if dist.is_initialized() else 1
+    lg_g = _lg(G)
+    if t < lg_g:
+        raise ValueError("fewer variables than log2(ranks)")
+    ch = np.asarray(challenges, dtype=np.uint64)
+    t_loc = t - lg_g
+    rounds, fe, he = ops.sumcheck(f_local, h_local, ch[:t_loc])
+    if G == 1:
+        return rounds, fe, he
+    if device is None:
+        device = f_local.device if isinstance(f_local, torch.Tensor) else torch.device("cpu")
+    summed = field_allreduce_sum(rounds, device, group).reshape(-1, 3) if t_loc else rounds
+    mine = torch.from_numpy(np.array([fe, he], dtype=np.uint64)).view(torch.int64).to(device)
+    parts = [torch.empty(2, dtype=torch.int64, device=device) for _ in range(G)]
+    dist.all_gather(parts, mine, group=group)
+    fin = torch.stack(parts).cpu().view(torch.uint64).numpy()
+    tail, fe, he = ops.sumcheck(np.ascontiguousarray(fin[:, 0]), np.ascontiguousarray(fin[:, 1]), ch[t_loc:])
+    return np.concatenate([summed.reshape(-1, 3), tail.reshape(-1, 3)]), fe, he
+
+
 class SplitCommitter:
     """``split_commit`` with every buffer allocated once, for repeated commits
     of the same geometry on this rank (the timed loop of bench.py).  ``run``
