@@ -102,6 +102,16 @@ int zkie2_commit(const uint64_t *d_coeffs, uint32_t lg_l, uint32_t lg_blowup, ui
 uint64_t zkie2_whir_scratch_elems(uint32_t n);
 int zkie2_whir_commit(const uint64_t *d_evals, uint32_t n, uint64_t *d_lde, uint64_t *d_layers,
                       uint64_t *d_scratch, zkie_stream_t stream);
+/* WHIR round commit of a folded extension-field polynomial (commit_extension,
+ * vendor/p3-whir/src/pcs/committer/writer.rs:21-86, Suffix order): d_evals
+ * holds 2^n EF elements (degree-2 binomial extension, c0 then c1 per
+ * element), n >= 5; the encoding is (2^(n-5) << log_inv_rate) rows x 32 EF,
+ * stored in d_lde as 64 base columns per row, and the tree hashes those
+ * 64-element rows (ExtensionMmcs).  d_layers as zkie2_merkle_total_digests of
+ * the row count. */
+uint64_t zkie2_commit_extension_scratch_elems(uint32_t n, uint32_t log_inv_rate);
+int zkie2_commit_extension(const uint64_t *d_evals, uint32_t n, uint32_t log_inv_rate, uint64_t *d_lde,
+                           uint64_t *d_layers, uint64_t *d_scratch, zkie_stream_t stream);
 /* Host-buffer commit (the drop-in path of CudaDft::dft_batch followed by
  * CudaMerkleTreeMmcs::commit): h_coeffs L x w in, root (8 u64) out, plus the
  * LDE ((L << lg_blowup) x w) and all digest layers when those pointers are

@@ -285,6 +285,41 @@ def whir_commit(consts, evals, threads=0):
     return lde_out, root
 
 
+def ef_dft_naive(evals_ef, H):
+    """The H-point DFT of an extension-field column zero-padded from len(evals)
+    to H entries, in extension arithmetic: out[k] = sum_j e_j * W_H^(jk),
+    with e_j = (c0, c1) in F[X]/(X^2 - 7) and W_H in F (scalar
+    multiplication of both coefficients).  O(H * len), small cases only."""
+    e = u64(evals_ef).reshape(-1, 2)
+    lg = H.bit_length() - 1
+    wh = two_adic_generator(lg)
+    out = np.zeros((H, 2), dtype=np.uint64)
+    for k in range(H):
+        wk = lib().orc_pow(wh, k)
+        x, acc0, acc1 = 1, 0, 0
+        for j in range(e.shape[0]):
+            acc0 = add(acc0, mul(int(e[j, 0]), x))
+            acc1 = add(acc1, mul(int(e[j, 1]), x))
+            x = mul(x, wk)
+        out[k] = (acc0, acc1)
+    return out
+
+
+def commit_extension(consts, evals_ef, log_inv_rate, threads=0):
+    """commit_extension (vendor/p3-whir/src/pcs/committer/writer.rs:21-86,
+    Suffix order): 2^n EF evaluations (rows of (c0, c1)) fill the first
+    2^(n-5) rows of the (2^(n-5) << log_inv_rate) x 32 EF matrix, each EF
+    column is DFT'd (dft_algebra_batch: coefficient-wise, the twiddles being
+    base-field elements), and the tree hashes each row's 64 base coefficients
+    (ExtensionMmcs over FlatMatrixView).  Returns (encoding as H x 64, root)."""
+    e = u64(evals_ef).reshape(-1)
+    n = (e.size // 2).bit_length() - 1
+    mat = e.reshape(1 << (n - 5), 64)
+    enc = lde(mat, log_inv_rate)
+    _, root = merkle_tree(consts, enc, threads)
+    return enc, root
+
+
 # ---- MLE / sumcheck -----------------------------------------------------------------
 def mle_eval(values, point):
     v, pt = u64(values), u64(point)

@@ -273,3 +273,55 @@ class Whir:
         stacked[:total] = torch.cat(tabs)
         batch_whir = Whir(total_vars, self.security_level, self.pow_bits)
         return batch_whir.commit(stacked, stream), batch_whir
+
+    # ---- per-round commits of the WHIR prover -----------------------------------------
+    MAX_NUM_VARIABLES_TO_SEND_COEFFS = 6
+
+    @staticmethod
+    def folding_schedule(num_variables: int, factor: int = FOLDING_FACTOR):
+        """FoldingFactor::Constant(factor).compute_folding_schedule
+        (vendor/p3-whir/src/parameters/folding.rs:88-104): fold `factor`
+        variables per round until at most 6 remain."""
+        if factor == 0:
+            raise ValueError("zero folding factor")
+        if factor > num_variables:
+            raise ValueError("folding factor larger than the number of variables")
+        remaining, schedule = num_variables, []
+        while True:
+            f = min(factor, remaining)
+            schedule.append(f)
+            remaining -= f
+            if remaining <= Whir.MAX_NUM_VARIABLES_TO_SEND_COEFFS:
+                return schedule
+
+    def round_commits(self):
+        """(num_variables, log_inv_rate) of each round's commit_extension:
+        num_rounds = len(schedule) - 1 (folding.rs:177-184); round i commits
+        the polynomial folded i + 1 times, at log_inv_rate 1 + (i + 1)(5 - 1)
+        (round_log_inv_rates of pcs/whir.rs:298-304)."""
+        sched = self.folding_schedule(self.num_variables)
+        out, n, rate = [], self.num_variables, self.STARTING_LOG_INV_RATE
+        for r in range(len(sched) - 1):
+            n -= sched[r]
+            rate += sched[r] - 1
+            out.append((n, rate))
+        return out
+
+    @staticmethod
+    def commit_extension(evals_ef, log_inv_rate: int, stream=None) -> Committed:
+        """commit_extension (vendor/p3-whir/src/pcs/committer/writer.rs:21-86,
+        Suffix order) of 2^n extension-field evaluations given as a (2^n, 2)
+        array of base coefficients (c0, c1): the (2^(n-5) << log_inv_rate) x 32
+        EF encoding, stored and hashed as 64 base columns per row."""
+        d = to_dev(evals_ef).reshape(-1)
+        n = _lg(d.numel() // 2)
+        if d.numel() != 2 << n or n < 5:
+            raise ValueError("commit_extension needs 2^n >= 32 EF elements (2 u64 each)")
+        H = 1 << (n - 5 + log_inv_rate)
+        d_lde = empty(H * 64)
+        d_layers = empty(lib.zkie2_merkle_total_digests(H) * DIGEST_ELEMS)
+        d_scr = empty(max(lib.zkie2_commit_extension_scratch_elems(n, log_inv_rate), 1))
+        check(lib.zkie2_commit_extension(ptr(d), n, log_inv_rate, ptr(d_lde), ptr(d_layers), ptr(d_scr),
+                                         stream_handle(stream)), "zkie2_commit_extension")
+        root = to_host(d_layers[-DIGEST_ELEMS:]).copy()
+        return Committed(root, d_lde.view(H, 64), d_layers, H, 64)

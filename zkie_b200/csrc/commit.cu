@@ -85,6 +85,25 @@ int zkie2_whir_commit(const uint64_t* d_evals, uint32_t n, uint64_t* d_lde, uint
 
 uint64_t zkie2_whir_scratch_elems(uint32_t n) { return n < 5 ? 0 : lde_scratch_elems(n - 5, 1, 32); }
 
+// commit_extension (vendor/p3-whir/src/pcs/committer/writer.rs:21-86, Suffix
+// order): the 2^n extension-field evaluations (degree-2 binomial extension,
+// each element stored as its two base coefficients c0, c1) fill the first
+// 2^(n-5) rows of a (2^(n-5) << log_inv_rate) x 32 EF matrix, zero rows
+// below, and every EF column is DFT'd.  The twiddles are base-field elements,
+// so the EF DFT acts on each coefficient column separately
+// (dft_algebra_batch); and ExtensionMmcs hashes each row as its 64 base
+// coefficients.  Together: an LDE of the 2^(n-5) x 64 base matrix at
+// blowup 2^log_inv_rate and the Merkle tree over its 64-wide rows.
+int zkie2_commit_extension(const uint64_t* d_evals, uint32_t n, uint32_t log_inv_rate, uint64_t* d_lde,
+                           uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t stream) {
+    if (n < 5) return (int)cudaErrorInvalidValue;
+    return commit_device(d_evals, n - 5, log_inv_rate, 64, d_lde, d_layers, d_scratch, stream);
+}
+
+uint64_t zkie2_commit_extension_scratch_elems(uint32_t n, uint32_t log_inv_rate) {
+    return n < 5 ? 0 : lde_scratch_elems(n - 5, log_inv_rate, 64);
+}
+
 // Host-buffer commit: the end-to-end path a drop-in caller of
 // CudaDft::dft_batch + CudaMerkleTreeMmcs::commit takes.  Copies the L x w
 // coefficient matrix in, runs LDE + tree, and copies back the root and --
