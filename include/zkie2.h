@@ -209,6 +209,20 @@ int zkie2_op_matmul_prove(const uint64_t *d_a, const uint64_t *d_b, const uint64
  * zkie-ops/src/compose.rs:1327-1331, zkie-ops/src/par.rs:41-89). */
 int zkie2_matmul_field(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
                        uint64_t *d_c, zkie_stream_t stream);
+/* One MatMul shard in one call: C = A W into d_c
+ * (m x n), WHIR base commits of W (k*n evaluations), A (m*k) and C (m*n)
+ * (pcs/whir.rs:438-469, each >= 32 evaluations), and the Op::MatMul proof
+ * with challenges from the shard's child transcript (zkie2_shard_dag_child
+ * of op_ids = {a, b, c}, one op).  The stages run concurrently on four
+ * streams; one synchronization at the end.  h_roots gets 3 x 8 u64 (W, A, C),
+ * the rest as zkie2_op_matmul_prove.  The LDEs and digest layers stay in
+ * d_scratch (zkie2_shard_prove_matmul_scratch_elems u64).  Synchronous. */
+uint64_t zkie2_shard_prove_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
+int zkie2_shard_prove_matmul(const uint64_t *d_a, const uint64_t *d_w, uint64_t m, uint64_t k, uint64_t n,
+                             const uint64_t *op_ids, uint64_t ops_per_shard, uint64_t shard_index,
+                             uint64_t *d_c, uint64_t *h_roots, uint64_t *h_claimed, uint64_t *h_rounds,
+                             uint64_t *h_finals, uint64_t *h_claims, uint64_t *d_scratch,
+                             zkie_stream_t stream);
 /* prove_sum_of_products (common/sumcheck.rs:243-286): the batch-opening
  * sumcheck of sum_x sum_i w_i(x) v_i(x) over n_tables pairs of 2^t tables,
  * stored row-major: table i of d_weights / d_values starts at element i * 2^t.

@@ -172,3 +172,24 @@ def test_op_matmul_cfg1_transcript(zk, orc):
     assert np.array_equal(got.proof.sumcheck.rounds, exp["rounds"])
     assert np.array_equal(got.claims, exp["claims"])
     assert np.array_equal(got.u, exp["u"]) and np.array_equal(got.ch, exp["ch"])
+
+
+@pytest.mark.parametrize("m,k,n", [(16, 1024, 1024), (4, 64, 32), (32, 256, 512)])
+def test_shard_prove_matmul_matches_composition(zk, orc, m, k, n):
+    """The fused four-stream shard call equals its parts run one by one:
+    forward C, the three WHIR commits and the Op::MatMul proof with the
+    shard's child transcript (and the oracle for C and the proof)."""
+    zk.check(zk.lib.zkie2_p2_init_default(), "constants")
+    a = signed16(m * 3 + k, m * k).reshape(m, k)
+    w = signed16(n * 5 + k, k * n).reshape(k, n)
+    res = zk.ShardProver(m, k, n).prove(a, w, op_ids=(4, 5, 6), ops_per_shard=1, shard_index=2)
+    c = orc.matmul_field(a, w)
+    assert np.array_equal(res.c.cpu().numpy(), c)
+    for i, t in enumerate((w, a, c)):
+        assert np.array_equal(res.roots[i], np.asarray(zk.Whir.with_params(int(t.size).bit_length() - 1, 90, 17)
+                                                          .commit(t.reshape(-1)).root, dtype=np.uint64)), i
+    exp = orc.op_matmul_prove(a, w, c, m, k, n, orc.shard_dag_child([[4, 5, 6]], 1, 2))
+    assert res.proof.proof.claimed == exp["claimed"]
+    assert np.array_equal(res.proof.proof.sumcheck.rounds, exp["rounds"])
+    assert np.array_equal(res.proof.claims, exp["claims"])
+    assert np.array_equal(res.proof.u, exp["u"]) and np.array_equal(res.proof.ch, exp["ch"])

@@ -41,6 +41,16 @@ int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
                uint32_t lg_blowup, uint64_t w, cudaStream_t s);
 uint64_t lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
 
+// ---- commit / GKR pieces used by the fused shard prove (shard.cu) ------------------
+int commit_device(const uint64_t* d_in, uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint64_t* d_lde,
+                  uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t s);
+int matmul_field_dev(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n,
+                     uint64_t* d_c, cudaStream_t s);
+uint64_t op_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
+int op_matmul_enqueue(const uint64_t* d_a, const uint64_t* d_b, const uint64_t* d_c, uint64_t m, uint64_t k,
+                      uint64_t n, const uint64_t* u, const uint64_t* v, const uint64_t* ch, uint64_t* d_scratch,
+                      uint64_t** d_out, cudaStream_t s);
+
 // ---- host-side primitives (host.cpp) -------------------------------------------
 void p2_derive_constants_host(uint64_t seed, uint64_t rc_init[64], uint64_t rc_final[64],
                               uint64_t rc_internal[22], uint64_t* diag15);

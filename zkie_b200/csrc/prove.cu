@@ -91,6 +91,31 @@ int download_proof(const MatmulScratch& ms, uint32_t lk, uint64_t* claimed, uint
 }
 
 }  // namespace
+
+uint64_t op_matmul_scratch_elems(uint64_t m, uint64_t k, uint64_t n) {
+    return matmul_scratch(m, k, n, nullptr, nullptr);
+}
+
+// The Op::MatMul proof with host-drawn challenges u, v, ch, enqueued on s with
+// no synchronization: claimed | rounds (3 lk) | finals (2) land at *d_out
+// (a pointer into d_scratch).  Dimensions must be powers of two.
+int op_matmul_enqueue(const uint64_t* d_a, const uint64_t* d_b, const uint64_t* d_c, uint64_t m, uint64_t k,
+                      uint64_t n, const uint64_t* u, const uint64_t* v, const uint64_t* ch, uint64_t* d_scratch,
+                      uint64_t** d_out, cudaStream_t s) {
+    if (!pow2(m) || !pow2(k) || !pow2(n)) return (int)cudaErrorInvalidValue;
+    const uint32_t lm = log2_exact(m);
+    MatmulScratch ms;
+    matmul_scratch(m, k, n, &ms, d_scratch);
+    int rc = eq_table_dev(u, lm, ms.eq_u, s);
+    if (rc) return rc;
+    rc = contract_rows_dev(d_a, ms.eq_u, m, k, ms.ar, ms.rows_part, s);
+    if (rc) return rc;
+    rc = matmul_core(d_b, d_c, m, k, n, u, v, ch, ms, s);
+    if (rc) return rc;
+    *d_out = ms.out;
+    return 0;
+}
+
 }  // namespace zk
 
 using namespace zk;

@@ -306,3 +306,46 @@ def prove_virtual(mles, terms, claimed, challenges) -> VirtualProof:
                                   idx.ctypes.data_as(_lib.pu32), len(terms), _p(ch), _p(rounds), _p(finals),
                                   ptr(scr), stream_handle()), "zkie2_virtual_prove")
     return VirtualProof(rounds[:t], finals)
+
+
+# ---- one MatMul shard in one call -------------------------------------------------------
+@dataclass
+class ShardMatMulProof:
+    c: torch.Tensor           # C = A W (device, m x n)
+    roots: np.ndarray         # (3, 8): WHIR roots of W, A, C
+    proof: OpMatMulProof
+
+
+class ShardProver:
+    """zkie2_shard_prove_matmul with its device scratch kept across calls."""
+
+    def __init__(self, m, k, n):
+        self.m, self.k, self.n = m, k, n
+        ne = lib.zkie2_shard_prove_matmul_scratch_elems(m, k, n)
+        if ne == 0:
+            raise ValueError("shard shape: powers of two with >= 32 elements per tensor")
+        self.scr = empty(ne)
+        self.c = empty(m * n)
+
+    def prove(self, a, w, op_ids=(0, 1, 2), ops_per_shard=1, shard_index=0) -> ShardMatMulProof:
+        m, k, n = self.m, self.k, self.n
+        da, dw = to_dev(a).reshape(-1), to_dev(w).reshape(-1)
+        if da.numel() != m * k or dw.numel() != k * n:
+            raise ValueError("shard: shape mismatch")
+        lm, lk, ln = _lg(m), _lg(k), _lg(n)
+        ids = np.ascontiguousarray(np.asarray(op_ids, dtype=np.uint64))
+        roots = np.zeros((3, 8), dtype=np.uint64)
+        claimed = _lib.u64(0)
+        rounds = np.zeros((max(lk, 1), 3), dtype=np.uint64)
+        finals = np.zeros(2, dtype=np.uint64)
+        claims = np.zeros(3, dtype=np.uint64)
+        check(lib.zkie2_shard_prove_matmul(ptr(da), ptr(dw), m, k, n, _p(ids), ops_per_shard, shard_index,
+                                           ptr(self.c), _p(roots), C.byref(claimed), _p(rounds), _p(finals),
+                                           _p(claims), ptr(self.scr), stream_handle()), "zkie2_shard_prove_matmul")
+        # the challenge draws, replayed on the host for the proof object
+        child = shard_dag_child([list(op_ids)], ops_per_shard, shard_index)
+        u = np.array([child.field() for _ in range(lm)], dtype=np.uint64)
+        v = np.array([child.field() for _ in range(ln)], dtype=np.uint64)
+        ch = np.array([child.field() for _ in range(lk)], dtype=np.uint64)
+        proof = MatmulProof(int(claimed.value), SumcheckProof(rounds[:lk], int(finals[0]), int(finals[1])))
+        return ShardMatMulProof(self.c.view(m, n), roots, OpMatMulProof(proof, u, v, ch, claims))
