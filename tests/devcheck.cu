@@ -84,9 +84,41 @@ __global__ void k_state(int op, uint64_t* st, uint64_t n, P2Const c) {
     for (int q = 0; q < 16; q++) st[i * 16 + q] = s[q];
 }
 
+// The four-threads-per-state permutation: group i of four lanes permutes
+// state i (every lane of the grid runs it; groups past n use zeros).
+__global__ void k_permute_x4(uint64_t* st, uint64_t n, P2Const c) {
+    const uint64_t i = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+    const uint32_t g = threadIdx.x & 3;
+    uint64_t v[4] = {0, 0, 0, 0};
+    if (i < n)
+        for (int j = 0; j < 4; j++) v[j] = st[i * 16 + 4 * g + j];
+    p2_permute_x4(v, g, c);
+    if (i < n)
+        for (int j = 0; j < 4; j++) st[i * 16 + 4 * g + j] = v[j];
+}
+
+P2Const consts_from151(const uint64_t* h) {
+    P2Const c;
+    for (int r = 0; r < 4; r++)
+        for (int i = 0; i < 16; i++) {
+            c.ext[r][i] = h[r * 16 + i];
+            c.ext[4 + r][i] = h[64 + r * 16 + i];
+        }
+    for (int i = 0; i < 22; i++) c.internal[i] = h[128 + i];
+    c.diag15 = h[150];
+    return c;
+}
+
 }  // namespace
 
 extern "C" {
+
+int devcheck_permute_x4(uint64_t* d_states, uint64_t n, const uint64_t* h_consts151) {
+    k_permute_x4<<<(unsigned)((4 * n + 127) / 128), 128>>>(d_states, n, consts_from151(h_consts151));
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return (int)e;
+}
 
 // Device: out[i] = op(a[i], b[i]) for device arrays of n u64.
 int devcheck_scalar(int op, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, uint64_t n) {

@@ -27,6 +27,7 @@ def dc():
     lib.hostcheck_state.argtypes = [C.c_int, p, C.c_uint64, p]
     lib.devcheck_scalar.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64]
     lib.devcheck_state.argtypes = [C.c_int, C.c_void_p, C.c_uint64, p]
+    lib.devcheck_permute_x4.argtypes = [C.c_void_p, C.c_uint64, p]
     return lib
 
 
@@ -134,3 +135,19 @@ def test_device_state_ops_match_host(dc, orc):
             rows = np.nonzero((got != h).any(axis=1))[0]
             bad.append(f"{name}: {rows.size} states differ, first {int(rows[0])}")
     assert not bad, "\n".join(bad)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [1, 7, 513])
+def test_device_permute_x4_matches_host(dc, orc, n):
+    """The four-threads-per-state permutation (latency-bound Merkle kernels)
+    against the one-thread host permutation, partially reduced inputs."""
+    import torch
+    c = consts151(orc)
+    st = np.random.default_rng(11 + n).integers(0, 2 ** 64, size=(n, 16), dtype=np.uint64)
+    st[0] = np.arange(16, dtype=np.uint64)
+    d = torch.from_numpy(st.copy()).cuda()
+    assert dc.devcheck_permute_x4(d.data_ptr(), n, _p(c)) == 0
+    h = st.copy()
+    dc.hostcheck_state(104, _p(h), n, _p(c))
+    assert np.array_equal(_canon(d.cpu().numpy()), _canon(h))

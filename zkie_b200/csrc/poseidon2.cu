@@ -26,6 +26,12 @@ std::mutex g_p2_mu;
 bool g_p2_ready[kMaxDevices];
 
 constexpr int kHashThreads = 128;
+// Up to this many states per launch the four-threads-per-state kernels run:
+// 4 x 2^16 threads fit the GPU in under one wave, so the launch is bound by
+// one permutation's latency, which the cooperative form cuts by about 3x.
+// Larger launches are throughput-bound and take one thread per state
+// (fewer instructions per permutation).
+constexpr uint64_t kX4MaxStates = 1ull << 16;
 
 // Leaf digests of rows [row0, row_end): sponge with rate 8, overwrite mode,
 // one permutation per full 8-block and one after a partial tail
@@ -94,6 +100,60 @@ __global__ void __launch_bounds__(kHashThreads)
     ulonglong2* dst = reinterpret_cast<ulonglong2*>(next + i * 8);
 #pragma unroll
     for (int q = 0; q < 4; q++) dst[q] = make_ulonglong2(gl_canon(s[2 * q]), gl_canon(s[2 * q + 1]));
+}
+
+// Latency-bound shapes (few rows or nodes): the same leaf sponge and
+// compression with four threads per state (p2_permute_x4).  Lane g of each
+// aligned 4-lane group holds state lanes 4g..4g+3; g = 0, 1 hold the rate and
+// the digest.  Groups past the end still run the permutation (the shuffles
+// need every lane) but load zeros and store nothing.
+__global__ void __launch_bounds__(kHashThreads)
+    k_leaf_rows_x4(const uint64_t* __restrict__ mat, uint64_t* __restrict__ digests, uint64_t row0,
+                   uint64_t row_end, uint64_t w) {
+    const uint64_t row = row0 + (((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2);
+    const uint32_t g = threadIdx.x & 3;
+    const bool ok = row < row_end;
+    const uint64_t* src = mat + (ok ? row : row0) * w;
+    uint64_t v[4] = {0, 0, 0, 0};
+    const uint64_t nblk = (w + 7) >> 3;
+    for (uint64_t b = 0; b < nblk; b++) {
+        const uint64_t base = b << 3;
+        const uint64_t n = (w - base) < 8 ? (w - base) : 8;
+        if (ok && g < 2) {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (4 * g + j < n) v[j] = __ldg(src + base + 4 * g + j);
+        }
+        p2_permute_x4(v, g, c_p2);
+    }
+    if (ok && g < 2) {
+        ulonglong2* dst = reinterpret_cast<ulonglong2*>(digests + row * 8 + 4 * g);
+        dst[0] = make_ulonglong2(gl_canon(v[0]), gl_canon(v[1]));
+        dst[1] = make_ulonglong2(gl_canon(v[2]), gl_canon(v[3]));
+    }
+}
+
+__global__ void __launch_bounds__(kHashThreads)
+    k_compress_x4(const uint64_t* __restrict__ prev, uint64_t* __restrict__ next, uint64_t from, uint64_t to,
+                  uint32_t step) {
+    const uint64_t i = from + (((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2);
+    const uint32_t g = threadIdx.x & 3;
+    const bool ok = i < to;
+    uint64_t v[4] = {0, 0, 0, 0};
+    if (ok && (g < 2 || step >= 2)) {
+        const ulonglong2* src = reinterpret_cast<const ulonglong2*>(prev + ((uint64_t)step * i * 8 + 4 * g));
+        const ulonglong2 a = __ldg(src), b = __ldg(src + 1);
+        v[0] = a.x;
+        v[1] = a.y;
+        v[2] = b.x;
+        v[3] = b.y;
+    }
+    p2_permute_x4(v, g, c_p2);
+    if (ok && g < 2) {
+        ulonglong2* dst = reinterpret_cast<ulonglong2*>(next + i * 8 + 4 * g);
+        dst[0] = make_ulonglong2(gl_canon(v[0]), gl_canon(v[1]));
+        dst[1] = make_ulonglong2(gl_canon(v[2]), gl_canon(v[3]));
+    }
 }
 
 // Full permutations of a batch of 16-element states (tests and the
@@ -183,8 +243,11 @@ int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint
     if (row_end <= row0) return 0;
     if (!digests || (!mat && w != 0)) return (int)cudaErrorInvalidValue;
     const uint64_t n = row_end - row0;
-    k_leaf_rows<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0,
-                                                                              row_end, w);
+    if (n <= kX4MaxStates)
+        k_leaf_rows_x4<<<(unsigned)ceil_div(4 * n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0, row_end,
+                                                                                     w);
+    else
+        k_leaf_rows<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0, row_end, w);
     ZK_LAUNCH_CHECK();
     return 0;
 }
@@ -194,7 +257,10 @@ int launch_compress(const uint64_t* prev, uint64_t* next, uint64_t from, uint64_
     if (to <= from) return 0;
     if (!prev || !next || step < 1 || step > 2) return (int)cudaErrorInvalidValue;
     const uint64_t n = to - from;
-    k_compress<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);
+    if (n <= kX4MaxStates)
+        k_compress_x4<<<(unsigned)ceil_div(4 * n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);
+    else
+        k_compress<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);
     ZK_LAUNCH_CHECK();
     return 0;
 }

@@ -121,4 +121,75 @@ ZK_HD void p2_permute(uint64_t s[16], const P2Const& c) {
     }
 }
 
+#if defined(__CUDACC__)
+// ---- four threads per permutation ---------------------------------------------------
+// For latency-bound hashing (few rows or tree nodes), an aligned group of four
+// lanes shares one state: lane g (= lane & 3) holds state lanes 4g .. 4g+3,
+// which is exactly one 4x4 block of the external MDS.  Per external round a
+// thread does its four S-boxes and its block locally; the per-residue column
+// sums are two xor-shuffle steps.  Per internal round lane 0's S-box runs on
+// g = 0, the full-state sum is a local sum plus two shuffle steps, and each
+// thread applies its four diagonal entries as multiplications by the
+// constants V_i.  The values equal the one-thread permutation's modulo p; the
+// critical path is about a third as long.  Every lane of the warp must call
+// this (the shuffles use the full mask).
+
+// V_i of the internal layer as field elements (1/2^k = p - (p-1)/2^k).
+__device__ __forceinline__ uint64_t p2_vdiag(uint32_t i, uint64_t diag15) {
+    switch (i) {
+        case 0: return GL_P - 2;
+        case 1: return 1;
+        case 2: return 2;
+        case 3: return GL_P - (GL_P - 1) / 2;
+        case 4: return 3;
+        case 5: return 4;
+        case 6: return (GL_P - 1) / 2;
+        case 7: return GL_P - 3;
+        case 8: return GL_P - 4;
+        case 9: return GL_P - (GL_P - 1) / 8;
+        case 10: return GL_P - (GL_P - 1) / 16;
+        case 11: return GL_P - (GL_P - 1) / 32;
+        case 12: return (GL_P - 1) / 8;
+        case 13: return (GL_P - 1) / 16;
+        case 14: return (GL_P - 1) / 32;
+        default: return diag15;
+    }
+}
+
+__device__ __forceinline__ uint64_t p2x4_group_sum(uint64_t x) {
+    x = gl_add(x, __shfl_xor_sync(0xffffffffu, x, 1));
+    return gl_add(x, __shfl_xor_sync(0xffffffffu, x, 2));
+}
+
+__device__ __forceinline__ void p2x4_mds_light(uint64_t v[4]) {
+    Acc y[4];
+    p2_mat4_acc(v[0], v[1], v[2], v[3], y);
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = acc_reduce(acc_add(y[k], p2x4_group_sum(acc_reduce(y[k]))));
+}
+
+__device__ __forceinline__ void p2_permute_x4(uint64_t v[4], uint32_t g, const P2Const& c) {
+    uint64_t vd[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) vd[j] = p2_vdiag(4 * g + j, c.diag15);
+    p2x4_mds_light(v);
+#pragma unroll 1
+    for (int r = 0; r < 8; r++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = p2_sbox(gl_add_c(v[j], c.ext[r][4 * g + j]));
+        p2x4_mds_light(v);
+        if (r == 3) {
+#pragma unroll 1
+            for (int q = 0; q < 22; q++) {
+                if (g == 0) v[0] = p2_sbox(gl_add_c(v[0], c.internal[q]));
+                const Acc a = acc_add(acc_add(acc_sum(v[0], v[1]), v[2]), v[3]);
+                const uint64_t sum = gl_canon(p2x4_group_sum(acc_reduce(a)));
+#pragma unroll
+                for (int j = 0; j < 4; j++) v[j] = gl_add_c(gl_mul(v[j], vd[j]), sum);
+            }
+        }
+    }
+}
+#endif
+
 }  // namespace zk

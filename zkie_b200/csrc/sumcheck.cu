@@ -343,14 +343,43 @@ __global__ void k_sumcheck_reduce(const uint64_t* __restrict__ partials, uint64_
 // Field matmul C = A (m x k) @ B (k x n), the forward witness of Op::MatMul
 // (zkie-ops/src/compose.rs:1327-1331; par.rs:41-89 computes the same field
 // value through i64 when it cannot overflow).
-__global__ void k_matmul_field(const uint64_t* __restrict__ a, const uint64_t* __restrict__ b,
-                               uint64_t m, uint64_t k, uint64_t n, uint64_t* __restrict__ c) {
-    const uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Block (32 columns x 8 k-slices): lane x owns column j of row i, warp y the
+// k-slice q = y, y + 8, ...; each thread sums its products exactly (Acc160)
+// and the eight slices are added through shared memory.  A warp reads 32
+// consecutive entries of a row of B per q (coalesced) and one broadcast
+// entry of A.
+constexpr int kMmSlices = 8;
+__global__ void __launch_bounds__(32 * kMmSlices)
+    k_matmul_field(const uint64_t* __restrict__ a, const uint64_t* __restrict__ b, uint64_t m, uint64_t k,
+                   uint64_t n, uint64_t* __restrict__ c) {
+    __shared__ uint64_t red[kMmSlices][32];
+    const uint64_t j = (uint64_t)blockIdx.x * 32 + threadIdx.x;
     const uint64_t i = blockIdx.y;
-    if (j >= n || i >= m) return;
-    uint64_t acc = 0;
-    for (uint64_t q = 0; q < k; q++) acc = gl_add(acc, gl_mul(__ldg(a + i * k + q), __ldg(b + q * n + j)));
-    c[i * n + j] = gl_canon(acc);
+    const uint32_t y = threadIdx.y;
+    Acc160 acc = acc160_zero();
+    if (j < n) {
+        const uint64_t* ar = a + i * k;
+        uint64_t q = y;
+        for (; q + 3 * kMmSlices < k; q += 4 * kMmSlices) {
+            const uint64_t a0 = __ldg(ar + q), a1 = __ldg(ar + q + kMmSlices);
+            const uint64_t a2 = __ldg(ar + q + 2 * kMmSlices), a3 = __ldg(ar + q + 3 * kMmSlices);
+            const uint64_t b0 = __ldg(b + q * n + j), b1 = __ldg(b + (q + kMmSlices) * n + j);
+            const uint64_t b2 = __ldg(b + (q + 2 * kMmSlices) * n + j), b3 = __ldg(b + (q + 3 * kMmSlices) * n + j);
+            acc160_mac(acc, a0, b0);
+            acc160_mac(acc, a1, b1);
+            acc160_mac(acc, a2, b2);
+            acc160_mac(acc, a3, b3);
+        }
+        for (; q < k; q += kMmSlices) acc160_mac(acc, __ldg(ar + q), __ldg(b + q * n + j));
+    }
+    red[y][threadIdx.x] = acc160_reduce(acc);
+    __syncthreads();
+    if (y == 0 && j < n) {
+        uint64_t s = red[0][threadIdx.x];
+#pragma unroll
+        for (int t = 1; t < kMmSlices; t++) s = gl_add(s, red[t][threadIdx.x]);
+        c[i * n + j] = gl_canon(s);
+    }
 }
 
 __global__ void k_canon_copy(const uint64_t* __restrict__ in, uint64_t* __restrict__ out, uint64_t n) {
@@ -563,8 +592,9 @@ int matmul_field_dev(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint6
                      uint64_t* d_c, cudaStream_t s) {
     if (m == 0 || n == 0) return 0;
     if (m > 65535) return (int)cudaErrorInvalidValue;
-    dim3 grid((unsigned)ceil_div(n, kThreads), (unsigned)m);
-    k_matmul_field<<<grid, kThreads, 0, s>>>(d_a, d_b, m, k, n, d_c);
+    if (ceil_div(n, 32) > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
+    const dim3 grid((unsigned)ceil_div(n, 32), (unsigned)m), block(32, kMmSlices);
+    k_matmul_field<<<grid, block, 0, s>>>(d_a, d_b, m, k, n, d_c);
     ZK_LAUNCH_CHECK();
     return 0;
 }
