@@ -44,6 +44,16 @@ ZK_HD uint64_t scalar_op(int op, uint64_t a, uint64_t b) {
             for (uint64_t k = 0; k <= (b & 1023); k++) acc160_mac(s, a, a);
             return acc160_reduce(s);
         }
+        case 16: return gl_mul_pow2<1>(a);
+        case 17: return gl_mul_pow2<33>(a);
+        case 18: return gl_mul_pow2<63>(a);
+        case 19: return gl_mul_pow2<64>(a);
+        case 20: return gl_mul_pow2<95>(a);
+        case 21: return gl_mul_pow2<96>(a);
+        case 22: return gl_mul_pow2<120>(a);
+        case 23: return gl_mul_pow2<156>(a);
+        case 24: return gl_mul_pow2<191>(a);
+        case 25: return gl_mul_pow2<39>(a);
         default: return 0;
     }
 }

@@ -14,7 +14,9 @@ P = 0xFFFFFFFF00000001
 M64 = 2 ** 64
 SCALAR_OPS = {0: "add", 1: "add_c", 2: "sub", 3: "mul", 4: "sqr", 5: "div2", 6: "div8", 7: "div16",
               8: "div32", 9: "div2^32", 10: "canon", 11: "sbox", 12: "mul_hi", 13: "reduce128",
-              14: "acc160_dot4", 15: "acc160_repeat"}
+              14: "acc160_dot4", 15: "acc160_repeat", 16: "pow2_1", 17: "pow2_33", 18: "pow2_63", 19: "pow2_64",
+              20: "pow2_95", 21: "pow2_96", 22: "pow2_120", 23: "pow2_156", 24: "pow2_191", 25: "pow2_39"}
+POW2_K = {16: 1, 17: 33, 18: 63, 19: 64, 20: 95, 21: 96, 22: 120, 23: 156, 24: 191, 25: 39}
 STATE_OPS = {105: "mat4", 100: "mds_light", 101: "ext_round0", 102: "internal_linear", 103: "int_round0",
              104: "permute"}
 
@@ -67,6 +69,7 @@ def expected_scalar(op, a, b):
     if op == 13: return (b * M64 + a) % P
     if op == 14: return (a * b + a * a + b * b + (a ^ b) * (M64 - 1 - a)) % P
     if op == 15: return ((b & 1023) + 1) * a * a % P
+    if op in POW2_K: return a * pow(2, POW2_K[op], P) % P
 
 
 def test_host_scalar_ops_match_bigint(dc):

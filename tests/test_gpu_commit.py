@@ -191,3 +191,22 @@ def test_commit_sweep_sampled(zk, orc, consts, lg_l, lb, w):
     # determinism: a second run is bit-identical (integer math, any race would show)
     com2 = zk.commit(m, lb)
     assert np.array_equal(com2.root, com.root)
+
+
+@pytest.mark.parametrize("lg", [4, 5, 6, 7, 8, 9, 10, 13])
+@pytest.mark.parametrize("w", [1, 5, 64, 600])
+def test_dft_every_radix_schedule(zk, orc, lg, w):
+    """zkie2_dft at every single-pass size (radix-16 register steps with a
+    2..16 remainder step) and a two-pass size, partially reduced inputs,
+    widths below, at and above a tile's column count."""
+    if (w << lg) > (1 << 21):
+        pytest.skip("covered by smaller widths")
+    m = rand_mat_fast(lg * 100 + w, 1 << lg, w)
+    raw = m.copy()
+    raw[::3] = np.where(raw[::3] < np.uint64(0xFFFFFFFF), raw[::3] + np.uint64(P), raw[::3])
+    d_in = torch.from_numpy(raw.reshape(-1)).cuda()
+    d_out = torch.empty_like(d_in)
+    scr = torch.empty(max(zk.lib.zkie2_lde_scratch_elems(lg, 0, w), 1), dtype=torch.uint64, device="cuda")
+    zk.check(zk.lib.zkie2_dft(d_in.data_ptr(), d_out.data_ptr(), scr.data_ptr(), lg, w,
+                              torch.cuda.current_stream().cuda_stream), "dft")
+    assert np.array_equal(d_out.cpu().numpy().reshape(1 << lg, w), orc.dft_batch(m))

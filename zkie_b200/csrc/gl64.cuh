@@ -275,6 +275,28 @@ ZK_HD uint64_t gl_div_pow2(uint64_t x) {
 
 ZK_HD uint64_t gl_neg(uint64_t a) { return gl_sub(0, a); }
 
+// x * 2^K for 0 <= K < 192 without a multiplication, as t with the sign
+// separate (x * 2^K = neg ? -t : t): 2^96 = -1, so K = 96 + K' flips the
+// sign; for 0 < K' < 64 the 128-bit shift x * 2^K' is reduced once; for
+// 64 <= K' < 96, 2^K' = -2^-(96-K') is a division by a power of two.
+template <int K>
+struct GlPow2 {
+    static_assert(K >= 0 && K < 192, "exponent in [0, 192)");
+    static constexpr int Kp = K % 96;
+    static constexpr bool neg = (K >= 96) != (Kp >= 64);
+    ZK_HD static uint64_t mag(uint64_t x) {
+        if constexpr (Kp == 0) return x;
+        else if constexpr (Kp < 64) return gl_reduce128(x << Kp, x >> (64 - Kp));
+        else return gl_div_pow2<96 - Kp>(x);
+    }
+};
+
+template <int K>
+ZK_HD uint64_t gl_mul_pow2(uint64_t x) {
+    const uint64_t t = GlPow2<K>::mag(x);
+    return GlPow2<K>::neg ? gl_neg(t) : t;
+}
+
 ZK_HD uint64_t gl_pow(uint64_t a, uint64_t e) {
     uint64_t r = 1;
     while (e) {

@@ -17,6 +17,7 @@
 // one write of the H output rows -- instead of the reference's lg h + 2 full
 // passes with one launch per radix-2 stage.
 #include <mutex>
+#include <utility>
 
 #include "../../include/zkie_goldilocks_cuda.h"
 #include "../../include/zkie2.h"
@@ -214,10 +215,217 @@ __global__ void __launch_bounds__(kNttThreads) k_ntt_pass(PassDesc d) {
     }
 }
 
+// ---- register-radix pass ------------------------------------------------------------
+// The same pass contract (PassDesc) as k_ntt_pass, computed as a mixed-radix
+// decimation in frequency over radix-2^L steps (L <= 4) held in registers.
+// Step i takes each group of R_i elements at stride M_i/R_i inside its
+// current sub-problem of M_i elements, does the R_i-point DFT in registers,
+// multiplies output e by W_{M_i}^(j' e) (j' = the group's offset) and writes
+// it back in place; the sub-problems of the next step are the contiguous
+// blocks of M_i/R_i elements.  After the last step, position
+// e_1 (M/R_1) + e_2 (M/(R_1 R_2)) + ... holds output k = e_1 + R_1 e_2 + ....
+// Inside an R-point DFT every twiddle is a power of W_16 or smaller, i.e. a
+// power of two in Goldilocks (W_{2^s} = 2^(39 * 2^(6-s) mod 192)), so those
+// multiplications are shifts (GlPow2); only the inter-step twiddles are
+// general multiplications, read from a shared-memory table of W_M powers.
+// The first step loads from global memory and the last stores to it, so a
+// pass makes (steps - 1) shared-memory round trips instead of one per stage
+// pair.
+
+constexpr int kN2Threads = 512;
+constexpr int kN2Elems = 16;  // elements per thread per step
+
+struct Sched {
+    uint32_t n;       // steps
+    uint32_t lg[4];   // log2 radix of each step
+    uint32_t lgm[4];  // log2 of the sub-problem size M_i at step i
+};
+
+template <int L>
+__device__ __forceinline__ constexpr int brev_c(int i) {
+    int r = 0;
+    for (int b = 0; b < L; b++)
+        if ((i >> b) & 1) r |= 1 << (L - 1 - b);
+    return r;
+}
+
+// Butterfly (a, b) <- (a + W b, a - W b) with W = 2^K.
+template <int K>
+__device__ __forceinline__ void bfly_pow2(uint64_t& a, uint64_t& b) {
+    const uint64_t t = GlPow2<K>::mag(b), u = a;
+    if (GlPow2<K>::neg) {
+        a = gl_sub(u, t);
+        b = gl_add(u, t);
+    } else {
+        a = gl_add(u, t);
+        b = gl_sub(u, t);
+    }
+}
+
+// Butterfly I of DIT stage S (1-based) of a 2^L-point transform on
+// bit-reversed input: rows a, a + 2^(S-1), twiddle W_{2^S}^j.
+template <int S, int I>
+__device__ __forceinline__ void dit_bfly(uint64_t* y) {
+    constexpr int h = 1 << (S - 1), j = I % h, a = (I / h) * 2 * h + j;
+    constexpr int K = ((39 << (6 - S)) * j) % 192;
+    bfly_pow2<K>(y[a], y[a + h]);
+}
+template <int S, int... I>
+__device__ __forceinline__ void dit_stage(uint64_t* y, std::integer_sequence<int, I...>) {
+    (dit_bfly<S, I>(y), ...);
+}
+template <int L, int... S>
+__device__ __forceinline__ void dit_stages(uint64_t* y, std::integer_sequence<int, S...>) {
+    (dit_stage<S + 1>(y, std::make_integer_sequence<int, (1 << (L - 1))>{}), ...);
+}
+// x[e] <- sum_d x[d] W_{2^L}^(d e), natural order in and out.
+template <int L>
+__device__ __forceinline__ void dft_reg(uint64_t* x) {
+    constexpr int R = 1 << L;
+    uint64_t y[R];
+#pragma unroll
+    for (int i = 0; i < R; i++) y[i] = x[brev_c<L>(i)];
+    dit_stages<L>(y, std::make_integer_sequence<int, L>{});
+#pragma unroll
+    for (int i = 0; i < R; i++) x[i] = y[i];
+}
+
+// Output index of the last step's group gam: the digit of step i sits at bits
+// [lgm_i - lg_i, lgm_i) of the position and goes to bits
+// [lg_0 + ... + lg_{i-1}, ...) of k; the last step's own digit is added by
+// the caller.
+__device__ __forceinline__ uint32_t n2_out_base(const Sched& sc, uint32_t gam, uint32_t lg_last) {
+    const uint32_t pos = gam << lg_last;
+    uint32_t k = 0, sh = 0;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        if ((uint32_t)i + 1 < sc.n) {
+            k |= ((pos >> (sc.lgm[i] - sc.lg[i])) & ((1u << sc.lg[i]) - 1)) << sh;
+            sh += sc.lg[i];
+        }
+    }
+    return k;
+}
+
+// One step with radix 2^L: the thread's 16 elements are G = 16 / 2^L groups.
+template <int L, typename IdxT>
+__device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint32_t lgm, bool first, bool last,
+                                        uint64_t* data, const uint64_t* tws, uint32_t q, uint32_t cc, uint32_t logC,
+                                        bool cok, IdxT row_in0, IdxT row_out0, uint64_t f) {
+    constexpr int R = 1 << L, G = kN2Elems / R;
+    const uint32_t m = d.m, lgs = lgm - L;  // stride M_i / R
+    const IdxT w = (IdxT)d.w;
+    uint64_t* gcol = d.out + (uint64_t)(blockIdx.y << logC) + cc;
+    const uint64_t* gin = d.in + (uint64_t)(blockIdx.y << logC) + cc;
+#pragma unroll
+    for (int gi = 0; gi < G; gi++) {
+        const uint32_t gam = q * G + gi;
+        const uint32_t jp = gam & ((1u << lgs) - 1);
+        const uint32_t base = ((gam >> lgs) << lgm) + jp;
+        uint64_t x[R];
+#pragma unroll
+        for (int e = 0; e < R; e++) {
+            const uint32_t pos = base + ((uint32_t)e << lgs);
+            if (first) {
+                const IdxT row = row_in0 + (IdxT)pos * (IdxT)d.jin;
+                x[e] = (cok && (uint64_t)row < d.rows_valid) ? __ldg(gin + row * w) : 0ull;
+            } else {
+                x[e] = data[(pos << logC) + cc];
+            }
+        }
+        dft_reg<L>(x);
+        if (!last) {
+            // W_{M_i}^(j' e) = W_M^(j' e 2^(m - lgm))
+#pragma unroll
+            for (int e = 1; e < R; e++) x[e] = gl_mul(x[e], tws[((jp * (uint32_t)e) << (m - lgm)) & ((1u << m) - 1)]);
+#pragma unroll
+            for (int e = 0; e < R; e++) data[((base + ((uint32_t)e << lgs)) << logC) + cc] = x[e];
+        } else {
+            // in the last step M_i = R: lgs = 0, jp = 0, base = gam << L
+            const uint32_t kb = n2_out_base(sc, gam, L);
+#pragma unroll
+            for (int e = 0; e < R; e++) {
+                const uint32_t k = kb | ((uint32_t)e << (m - L));
+                uint64_t v = x[e];
+                if (d.tw_log) v = gl_mul(v, root_pow<false>(d, d.tw_log, (f * k) & ((1ull << d.tw_log) - 1)));
+                if (d.canon) v = gl_canon(v);
+                const IdxT row = row_out0 + (IdxT)k * (IdxT)d.kout;
+                if (cok) gcol[row * w] = v;
+            }
+        }
+    }
+}
+
+template <typename IdxT>
+__global__ void __launch_bounds__(kN2Threads) k_ntt_pass2(PassDesc d, Sched sc) {
+    extern __shared__ uint64_t sm[];
+    const uint32_t m = d.m, M = 1u << m, logC = d.logC;
+    uint64_t* data = sm;                         // [M][C]
+    uint64_t* tws = sm + ((size_t)M << logC);    // [M] powers of W_M
+    const uint64_t f = blockIdx.x % d.F;         // one lane per block
+    const uint64_t s_idx = blockIdx.x / d.F;
+    const uint32_t tid = threadIdx.x, cc = tid & ((1u << logC) - 1), q = tid >> logC;
+    const bool cok = ((uint64_t)blockIdx.y << logC) + cc < d.w;
+    for (uint32_t i = tid; i < M; i += blockDim.x) tws[i] = root_pow<false>(d, m, i);
+    __syncthreads();
+    const IdxT row_in0 = (IdxT)(f * d.fin + s_idx * d.sin);
+    const IdxT row_out0 = (IdxT)(f * d.fout + s_idx * d.sout);
+#pragma unroll 1
+    for (int st = 0; st < 4; st++) {
+        if ((uint32_t)st >= sc.n) break;
+        const uint32_t lgm = sc.lgm[st];
+        const bool first = st == 0, last = (uint32_t)st + 1 == sc.n;
+        switch (sc.lg[st]) {
+            case 4: n2_step<4, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+            case 3: n2_step<3, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+            case 2: n2_step<2, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+            default: n2_step<1, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+        }
+        if (!last) __syncthreads();
+    }
+}
+
 uint32_t floor_log2(uint64_t x) {
     uint32_t r = 0;
     while ((2ull << r) <= x) r++;
     return r;
+}
+
+// Radix schedule of an M = 2^m point sub-transform (m >= 4): steps of 4 bits,
+// the remainder last.
+Sched make_sched(uint32_t m) {
+    Sched sc{};
+    uint32_t rem = m;
+    while (rem > 0) {
+        const uint32_t l = rem >= 4 ? 4 : rem;
+        sc.lg[sc.n] = l;
+        sc.lgm[sc.n] = rem;
+        sc.n++;
+        rem -= l;
+    }
+    return sc;
+}
+
+// Register-radix pass: one lane per block, C = 2^logC columns, M/16 threads
+// per column (at most 512 threads).
+template <typename IdxT>
+int run_pass2(PassDesc d, uint64_t S, cudaStream_t s) {
+    const uint32_t m = d.m;
+    uint32_t logC = floor_log2(d.w);
+    const uint32_t maxC = floor_log2(kN2Threads) - (m - 4);  // (M/16) << logC <= 512
+    if (logC > maxC) logC = maxC;
+    d.logC = logC;
+    d.logR = 0;
+    const uint64_t blocks = d.F * S, cblocks = ceil_div(d.w, 1ull << logC);
+    if (blocks > 0x7FFFFFFFull || cblocks > 65535) return (int)cudaErrorInvalidConfiguration;
+    const size_t smem = 8ull * ((1ull << m) << logC) + 8ull * (1ull << m);
+    if (smem > 48 * 1024)
+        ZK_TRY(cudaFuncSetAttribute(k_ntt_pass2<IdxT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const Sched sc = make_sched(m);
+    const uint32_t threads = (1u << (m - 4)) << logC;
+    k_ntt_pass2<IdxT><<<dim3((unsigned)blocks, (unsigned)cblocks), threads, smem, s>>>(d, sc);
+    ZK_LAUNCH_CHECK();
+    return 0;
 }
 
 // Tile width (C * R) for a sub-DFT of 2^m rows: keep M * C * R * 8 bytes
@@ -252,6 +460,17 @@ int run_pass(PassDesc d, uint64_t S, cudaStream_t s) {
     return 0;
 }
 
+// The register-radix kernel for sub-transforms of 2^4 .. 2^11 points on the
+// library's own twiddles; the shared-memory radix-2/4 kernel for the rest and
+// for the reference entry (which reads the caller's twiddle table).
+template <bool kCallerTab, typename IdxT>
+int run_pass_sel(PassDesc d, uint64_t S, cudaStream_t s) {
+    if constexpr (!kCallerTab) {
+        if (d.m >= 4 && d.m <= 11) return run_pass2<IdxT>(d, S, s);
+    }
+    return run_pass<kCallerTab, IdxT>(d, S, s);
+}
+
 // Full transform of size 2^lg over the columns of `in` (rows >= rows_valid
 // are zero) into `out`, using `scratch` (2^lg * w u64) between passes.
 template <bool kCallerTab, typename IdxT>
@@ -272,7 +491,7 @@ int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
         d.m = lg;
         d.tw_log = 0;
         d.canon = 1;
-        return run_pass<kCallerTab, IdxT>(d, 1, s);
+        return run_pass_sel<kCallerTab, IdxT>(d, 1, s);
     }
     if (lg <= 22) {
         const uint32_t a = (lg + 1) / 2, b = lg - a;  // N1 = 2^a, N2 = 2^b (<= 2^11 each)
@@ -282,14 +501,14 @@ int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
         A.F = N2; A.fin = 1; A.sin = 0; A.jin = N2;
         A.fout = 1; A.sout = 0; A.kout = N2;
         A.m = a; A.tw_log = lg; A.canon = 0;
-        int rc = run_pass<kCallerTab, IdxT>(A, 1, s);
+        int rc = run_pass_sel<kCallerTab, IdxT>(A, 1, s);
         if (rc) return rc;
         PassDesc B = base;
         B.in = scratch; B.out = out; B.rows_valid = ~0ull;
         B.F = N1; B.fin = N2; B.sin = 0; B.jin = 1;
         B.fout = 1; B.sout = 0; B.kout = N1;
         B.m = b; B.tw_log = 0; B.canon = 1;
-        return run_pass<kCallerTab, IdxT>(B, 1, s);
+        return run_pass_sel<kCallerTab, IdxT>(B, 1, s);
     }
     if (lg <= 30) {
         const uint32_t a = (lg + 2) / 3, rest = lg - a, b = (rest + 1) / 2, c = rest - b;
@@ -299,21 +518,21 @@ int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
         A.F = N23; A.fin = 1; A.sin = 0; A.jin = N23;
         A.fout = 1; A.sout = 0; A.kout = N23;
         A.m = a; A.tw_log = lg; A.canon = 0;
-        int rc = run_pass<kCallerTab, IdxT>(A, 1, s);
+        int rc = run_pass_sel<kCallerTab, IdxT>(A, 1, s);
         if (rc) return rc;
         PassDesc B1 = base;
         B1.in = scratch; B1.out = scratch; B1.rows_valid = ~0ull;
         B1.F = N3; B1.fin = 1; B1.sin = N23; B1.jin = N3;
         B1.fout = 1; B1.sout = N23; B1.kout = N3;
         B1.m = b; B1.tw_log = b + c; B1.canon = 0;
-        rc = run_pass<kCallerTab, IdxT>(B1, N1, s);
+        rc = run_pass_sel<kCallerTab, IdxT>(B1, N1, s);
         if (rc) return rc;
         PassDesc B2 = base;
         B2.in = scratch; B2.out = out; B2.rows_valid = ~0ull;
         B2.F = N1; B2.fin = N23; B2.sin = N3; B2.jin = 1;
         B2.fout = 1; B2.sout = N1; B2.kout = N1 * N2;
         B2.m = c; B2.tw_log = 0; B2.canon = 1;
-        return run_pass<kCallerTab, IdxT>(B2, N2, s);
+        return run_pass_sel<kCallerTab, IdxT>(B2, N2, s);
     }
     return (int)cudaErrorInvalidValue;
 }
