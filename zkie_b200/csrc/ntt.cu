@@ -308,56 +308,74 @@ __device__ __forceinline__ uint32_t n2_out_base(const Sched& sc, uint32_t gam, u
 }
 
 // One step with radix 2^L: the thread's 16 elements are G = 16 / 2^L groups.
-template <int L, typename IdxT>
-__device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint32_t lgm, bool first, bool last,
-                                        uint64_t* data, const uint64_t* tws, uint32_t q, uint32_t cc, uint32_t logC,
-                                        bool cok, IdxT row_in0, IdxT row_out0, uint64_t f) {
+// kIn / kOut: the step reads from global memory (first step) or shared
+// memory, and writes to global memory (last step) or shared memory.
+template <int L, bool kIn, bool kOut, typename IdxT>
+__device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint32_t lgm, uint64_t* data,
+                                        const uint64_t* tws, uint32_t q, uint32_t cc, uint32_t logC, bool cok,
+                                        IdxT row_in0, IdxT row_out0, uint64_t f) {
     constexpr int R = 1 << L, G = kN2Elems / R;
     const uint32_t m = d.m, lgs = lgm - L;  // stride M_i / R
     const IdxT w = (IdxT)d.w;
-    uint64_t* gcol = d.out + (uint64_t)(blockIdx.y << logC) + cc;
-    const uint64_t* gin = d.in + (uint64_t)(blockIdx.y << logC) + cc;
 #pragma unroll
     for (int gi = 0; gi < G; gi++) {
         const uint32_t gam = q * G + gi;
         const uint32_t jp = gam & ((1u << lgs) - 1);
         const uint32_t base = ((gam >> lgs) << lgm) + jp;
         uint64_t x[R];
-#pragma unroll
-        for (int e = 0; e < R; e++) {
-            const uint32_t pos = base + ((uint32_t)e << lgs);
-            if (first) {
-                const IdxT row = row_in0 + (IdxT)pos * (IdxT)d.jin;
-                x[e] = (cok && (uint64_t)row < d.rows_valid) ? __ldg(gin + row * w) : 0ull;
-            } else {
-                x[e] = data[(pos << logC) + cc];
-            }
-        }
-        dft_reg<L>(x);
-        if (!last) {
-            // W_{M_i}^(j' e) = W_M^(j' e 2^(m - lgm))
-#pragma unroll
-            for (int e = 1; e < R; e++) x[e] = gl_mul(x[e], tws[((jp * (uint32_t)e) << (m - lgm)) & ((1u << m) - 1)]);
-#pragma unroll
-            for (int e = 0; e < R; e++) data[((base + ((uint32_t)e << lgs)) << logC) + cc] = x[e];
-        } else {
-            // in the last step M_i = R: lgs = 0, jp = 0, base = gam << L
-            const uint32_t kb = n2_out_base(sc, gam, L);
+        if (kIn) {
+            // rows row_in0 + (base + e 2^lgs) jin of column c0 + cc
+            const IdxT rstep = (IdxT)d.jin << lgs;
+            const IdxT row_b = row_in0 + (IdxT)base * (IdxT)d.jin;
+            const uint64_t* g = d.in + ((uint64_t)blockIdx.y << logC) + cc + (uint64_t)row_b * w;
+            const IdxT gstep = rstep * w;
 #pragma unroll
             for (int e = 0; e < R; e++) {
-                const uint32_t k = kb | ((uint32_t)e << (m - L));
-                uint64_t v = x[e];
-                if (d.tw_log) v = gl_mul(v, root_pow<false>(d, d.tw_log, (f * k) & ((1ull << d.tw_log) - 1)));
-                if (d.canon) v = gl_canon(v);
-                const IdxT row = row_out0 + (IdxT)k * (IdxT)d.kout;
-                if (cok) gcol[row * w] = v;
+                x[e] = 0;
+                if (cok && (uint64_t)(row_b + (IdxT)e * rstep) < d.rows_valid) x[e] = __ldg(g + (IdxT)e * gstep);
+            }
+        } else {
+            const uint64_t* p = data + (base << logC) + cc;
+            const uint32_t st = 1u << (lgs + logC);
+#pragma unroll
+            for (int e = 0; e < R; e++) x[e] = p[e * st];
+        }
+        dft_reg<L>(x);
+        if (!kOut) {
+            // W_{M_i}^(j' e) = W_M^(j' e 2^(m - lgm))
+            const uint32_t tsh = m - lgm;
+#pragma unroll
+            for (int e = 1; e < R; e++) x[e] = gl_mul(x[e], tws[(jp * (uint32_t)e) << tsh]);
+            uint64_t* p = data + (base << logC) + cc;
+            const uint32_t st = 1u << (lgs + logC);
+#pragma unroll
+            for (int e = 0; e < R; e++) p[e * st] = x[e];
+        } else {
+            // the last step has M_i = R: lgs = 0, jp = 0, base = gam << L; output
+            // k = kb + e 2^(m-L), row row_out0 + k kout
+            const uint32_t kb = n2_out_base(sc, gam, L);
+            if (d.tw_log) {
+                const uint64_t emask = (1ull << d.tw_log) - 1;
+#pragma unroll
+                for (int e = 0; e < R; e++)
+                    x[e] = gl_mul(x[e], root_pow<false>(d, d.tw_log, (f * (kb | ((uint32_t)e << (m - L)))) & emask));
+            }
+            if (d.canon) {
+#pragma unroll
+                for (int e = 0; e < R; e++) x[e] = gl_canon(x[e]);
+            }
+            if (cok) {
+                uint64_t* g = d.out + ((uint64_t)blockIdx.y << logC) + cc + (uint64_t)(row_out0 + (IdxT)kb * (IdxT)d.kout) * w;
+                const IdxT gstep = ((IdxT)d.kout << (m - L)) * w;
+#pragma unroll
+                for (int e = 0; e < R; e++) g[(IdxT)e * gstep] = x[e];
             }
         }
     }
 }
 
 template <typename IdxT>
-__global__ void __launch_bounds__(kN2Threads) k_ntt_pass2(PassDesc d, Sched sc) {
+__global__ void __launch_bounds__(kN2Threads, 2) k_ntt_pass2(PassDesc d, Sched sc) {
     extern __shared__ uint64_t sm[];
     const uint32_t m = d.m, M = 1u << m, logC = d.logC;
     uint64_t* data = sm;                         // [M][C]
@@ -370,18 +388,24 @@ __global__ void __launch_bounds__(kN2Threads) k_ntt_pass2(PassDesc d, Sched sc) 
     __syncthreads();
     const IdxT row_in0 = (IdxT)(f * d.fin + s_idx * d.sin);
     const IdxT row_out0 = (IdxT)(f * d.fout + s_idx * d.sout);
-#pragma unroll 1
-    for (int st = 0; st < 4; st++) {
-        if ((uint32_t)st >= sc.n) break;
-        const uint32_t lgm = sc.lgm[st];
-        const bool first = st == 0, last = (uint32_t)st + 1 == sc.n;
-        switch (sc.lg[st]) {
-            case 4: n2_step<4, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-            case 3: n2_step<3, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-            case 2: n2_step<2, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-            default: n2_step<1, IdxT>(d, sc, lgm, first, last, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-        }
-        if (!last) __syncthreads();
+    // The schedule (make_sched) is 4-bit steps with the remainder last, so
+    // only the last step can have a radix below 16.
+    if (sc.n == 1) {
+        n2_step<4, true, true, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+        return;
+    }
+    n2_step<4, true, false, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+    __syncthreads();
+    if (sc.n == 3) {
+        n2_step<4, false, false, IdxT>(d, sc, sc.lgm[1], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+        __syncthreads();
+    }
+    const uint32_t lgm = sc.n == 3 ? sc.lgm[2] : sc.lgm[1];
+    switch (lgm) {
+        case 4: n2_step<4, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+        case 3: n2_step<3, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+        case 2: n2_step<2, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+        default: n2_step<1, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
     }
 }
 
