@@ -364,7 +364,7 @@ def main_split(args, zk, dev, world, rank):
             "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
         },
         "roofline_ntt": {
-            "bound": "hbm", "kernel": f"k_coset_twist + k_ntt_pass x{ntt_passes(lg_local)} (coset LDE, "
+            "bound": "hbm", "kernel": f"k_coset_twist + k_ntt_pass2 x{ntt_passes(lg_local)} (coset LDE, "
                                       f"2^{lg_local} rows per rank)",
             "achieved": round(ntt_gbs, 1), "peak": hbm_peak, "unit": "GB/s (per GPU)",
             "frac": round(ntt_gbs / hbm_peak, 4), "traffic": None,
@@ -537,7 +537,7 @@ def main():
             "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
         },
         "roofline_ntt": {
-            "bound": "hbm", "kernel": f"k_ntt_pass x{ntt_passes(lg)} (LDE 2^{lg_l} -> 2^{lg})",
+            "bound": "hbm", "kernel": f"k_ntt_pass2 x{ntt_passes(lg)} (register-radix passes, LDE 2^{lg_l} -> 2^{lg})",
             "achieved": round(ntt_gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(ntt_gbs / hbm_peak, 4),
             "traffic": None, "algorithmic_bytes": ntt_bytes, "peak_source": hbm_src,
             "ms_per_step": round(ntt_ms, 4), "share_of_step": round(ntt_ms / ms_per_step, 4),

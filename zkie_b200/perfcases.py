@@ -154,6 +154,26 @@ def case_sop(a):
             "gbs": byts / (ms / 1e3) / 1e9}
 
 
+def case_shard(a):
+    """zkie2_shard_prove_matmul at BASELINE configuration 1 (16 x 1024 x 1024,
+    entries uniform in [-2^15, 2^15) embedded in the field)."""
+    from .gkr import ShardProver
+    m, k, n = a.m, a.k, a.n
+    g = np.random.default_rng(5)
+
+    def fx(shape):
+        x = g.integers(-(1 << 15), 1 << 15, size=shape, dtype=np.int64)
+        return x.astype(np.uint64) + np.where(x < 0, np.uint64(P), np.uint64(0))
+    A = torch.from_numpy(fx(m * k)).cuda()
+    W = torch.from_numpy(fx(k * n)).cuda()
+    prover = ShardProver(m, k, n)
+
+    def run():
+        prover.prove(A, W)
+    ms = _time(run, a.iters)
+    return {"case": "shard_prove_matmul", "m": m, "k": k, "n": n, "ms": ms}
+
+
 def case_commit(a):
     lg_l, w, lb = a.log_size, a.polys, a.lg_blowup
     L, H = 1 << lg_l, 1 << (lg_l + lb)
@@ -173,7 +193,7 @@ def case_commit(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop"])
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard"])
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
     ap.add_argument("--lg-blowup", type=int, default=1)
@@ -186,7 +206,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "sop": case_sop}[a.case](a)
+           "virtual": case_virtual, "sop": case_sop, "shard": case_shard}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 
