@@ -116,8 +116,8 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u64 (Goldilocks)", "data": "synthetic",
-        "impl": "reference", "config": cfg,
+        "scaling": "weak" if args.gpus == 1 else "strong", "vs_baseline": None, "dtype": "u64 (Goldilocks)",
+        "data": "synthetic", "impl": "reference", "config": cfg,
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                          "sample": f"{args.polys} polys x 2^{lg_rows} coeffs per step (bounded sample of the "
                                    f"workload), oracle/zkie_oracle.c on all host threads"},

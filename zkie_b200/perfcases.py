@@ -174,6 +174,19 @@ def case_shard(a):
     return {"case": "shard_prove_matmul", "m": m, "k": k, "n": n, "ms": ms}
 
 
+def case_split(a):
+    """The split commit over `gpus` ranks emulated on this one GPU (every
+    rank's coset LDE, leaf hashes, digest interleave and subtree in turn)."""
+    from .multigpu import split_commit_emulated
+    lg_l, w, lb, G = a.log_size, a.polys, a.lg_blowup, a.gpus
+    d_in = _rand((1 << lg_l) * w, 8)
+
+    def run():
+        split_commit_emulated(d_in, lg_l, lb, w, G)
+    ms = _time(run, a.iters)
+    return {"case": "split_commit_emulated", "log_size": lg_l, "polys": w, "blowup": 1 << lb, "ranks": G, "ms": ms}
+
+
 def case_commit(a):
     lg_l, w, lb = a.log_size, a.polys, a.lg_blowup
     L, H = 1 << lg_l, 1 << (lg_l + lb)
@@ -193,7 +206,8 @@ def case_commit(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard"])
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split"])
+    ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
     ap.add_argument("--lg-blowup", type=int, default=1)
@@ -206,7 +220,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "sop": case_sop, "shard": case_shard}[a.case](a)
+           "virtual": case_virtual, "sop": case_sop, "shard": case_shard, "split": case_split}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 
