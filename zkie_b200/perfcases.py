@@ -187,6 +187,44 @@ def case_split(a):
     return {"case": "split_commit_emulated", "log_size": lg_l, "polys": w, "blowup": 1 << lb, "ranks": G, "ms": ms}
 
 
+def case_sweep(a):
+    """batches of 1, 16, 256 polynomials of 2^16,
+    2^20, 2^24 coefficients at blowup 2 and 4.  One JSON line per case that
+    fits this GPU's free memory (input + LDE + NTT scratch + digest layers),
+    commit time with inputs resident."""
+    free, _ = torch.cuda.mem_get_info()
+    out = []
+    for lg_l in (16, 20, 24):
+        for w in (1, 16, 256):
+            for lb in (1, 2):
+                L, H = 1 << lg_l, 1 << (lg_l + lb)
+                need = 8 * (L * w + 2 * H * w) + 64 * 2 * H
+                case = {"case": "cfg2_commit", "log_size": lg_l, "polys": w, "blowup": 1 << lb}
+                if need > 0.9 * free:
+                    case["skipped"] = f"needs {need / 2**30:.1f} GiB of {free / 2**30:.1f} GiB free (one GPU)"
+                    print(json.dumps(case), flush=True)
+                    continue
+                d_in = _rand(L * w, 7)
+                d_lde = torch.empty(H * w, dtype=torch.uint64, device="cuda")
+                d_layers = torch.empty(lib.zkie2_merkle_total_digests(H) * 8, dtype=torch.uint64, device="cuda")
+                d_scr = torch.empty(max(lib.zkie2_commit_scratch_elems(lg_l, lb, w), 1), dtype=torch.uint64,
+                                    device="cuda")
+                st = torch.cuda.current_stream().cuda_stream
+
+                def run():
+                    check(lib.zkie2_commit(d_in.data_ptr(), lg_l, lb, w, d_lde.data_ptr(), d_layers.data_ptr(),
+                                           d_scr.data_ptr(), st), "commit")
+                iters = max(1, min(a.iters, int(2e9 // (H * max(w, 8)))))
+                ms = _time(run, iters, warmup=1)
+                case.update({"ms": round(ms, 4), "melem_s": round(L * w / (ms / 1e3) / 1e6, 1),
+                             "lde_melem_s": round(H * w / (ms / 1e3) / 1e6, 1),
+                             "root0": hex(int(d_layers[-8:].cpu().view(torch.int64)[0].item()) & (2**64 - 1))})
+                print(json.dumps(case), flush=True)
+                del d_in, d_lde, d_layers, d_scr
+                torch.cuda.empty_cache()
+    return {"case": "cfg2_sweep", "done": True}
+
+
 def case_commit(a):
     lg_l, w, lb = a.log_size, a.polys, a.lg_blowup
     L, H = 1 << lg_l, 1 << (lg_l + lb)
@@ -206,7 +244,7 @@ def case_commit(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split"])
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -220,7 +258,8 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "sop": case_sop, "shard": case_shard, "split": case_split}[a.case](a)
+           "virtual": case_virtual, "sop": case_sop, "shard": case_shard, "split": case_split,
+           "sweep": case_sweep}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 
