@@ -210,3 +210,16 @@ def test_dft_every_radix_schedule(zk, orc, lg, w):
     zk.check(zk.lib.zkie2_dft(d_in.data_ptr(), d_out.data_ptr(), scr.data_ptr(), lg, w,
                               torch.cuda.current_stream().cuda_stream), "dft")
     assert np.array_equal(d_out.cpu().numpy().reshape(1 << lg, w), orc.dft_batch(m))
+
+
+@pytest.mark.parametrize("lg_l,lb,w", [(1, 1, 100), (3, 1, 72), (9, 1, 64), (12, 1, 100), (14, 2, 256), (11, 1, 65)])
+def test_commit_host_column_pipeline(zk, orc, consts, lg_l, lb, w):
+    """zkie2_commit_host uploads, transforms and downloads the matrix in
+    column blocks (pitched copies, the LDE on a column block of the full-width
+    matrix): every block boundary and a ragged last block against the oracle."""
+    m = rand_mat_fast(lg_l * 7 + w, 1 << lg_l, w)
+    root, lde, layers = zk.commit_host(m, lb)
+    exp_lde = orc.lde(m, lb)
+    assert np.array_equal(lde, exp_lde)
+    _, exp_root = orc.merkle_tree(consts, exp_lde)
+    assert np.array_equal(root, exp_root)

@@ -16,9 +16,12 @@ namespace zk {
 
 namespace {
 
+constexpr int kMaxChunks = 8;  // column blocks of the pipelined host commit
+
 struct DevStreams {
-    cudaStream_t compute = nullptr, copy = nullptr;
+    cudaStream_t compute = nullptr, copy = nullptr, copy_out = nullptr;
     cudaEvent_t lde_ready = nullptr, done = nullptr;
+    cudaEvent_t in_ready[kMaxChunks] = {}, chunk_lde[kMaxChunks] = {};
     bool ready = false;
 };
 std::mutex g_streams_mu;
@@ -32,8 +35,13 @@ int get_streams(DevStreams** out) {
     if (!s.ready) {
         ZK_TRY(cudaStreamCreateWithFlags(&s.compute, cudaStreamNonBlocking));
         ZK_TRY(cudaStreamCreateWithFlags(&s.copy, cudaStreamNonBlocking));
+        ZK_TRY(cudaStreamCreateWithFlags(&s.copy_out, cudaStreamNonBlocking));
         ZK_TRY(cudaEventCreateWithFlags(&s.lde_ready, cudaEventDisableTiming));
         ZK_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        for (int i = 0; i < kMaxChunks; i++) {
+            ZK_TRY(cudaEventCreateWithFlags(&s.in_ready[i], cudaEventDisableTiming));
+            ZK_TRY(cudaEventCreateWithFlags(&s.chunk_lde[i], cudaEventDisableTiming));
+        }
         cudaMemPool_t pool;
         if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
             uint64_t thr = ~0ull;  // keep freed blocks cached across calls
@@ -125,14 +133,29 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
     ZK_TRY(cudaMallocAsync((void**)&d_lde, 8 * H * w, cs));
     ZK_TRY(cudaMallocAsync((void**)&d_layers, 64 * g.total, cs));
     if (scratch) ZK_TRY(cudaMallocAsync((void**)&d_scr, 8 * scratch, cs));
-    ZK_TRY(cudaMemcpyAsync(d_in, h_coeffs, 8 * L * w, cudaMemcpyHostToDevice, cs));
     rc = p2_ensure_default();
-    if (!rc) rc = lde_launch(d_in, d_lde, d_scr, lg_l, lg_blowup, w, cs);
-    if (!rc && h_lde) {
-        // Download the LDE on the copy stream while the compute stream hashes.
-        rc = (int)cudaEventRecord(st->lde_ready, cs);
-        if (!rc) rc = (int)cudaStreamWaitEvent(st->copy, st->lde_ready, 0);
-        if (!rc) rc = (int)cudaMemcpyAsync(h_lde, d_lde, 8 * H * w, cudaMemcpyDeviceToHost, st->copy);
+    // Pipeline over column blocks: block j is uploaded (copy stream), its
+    // LDE computed (compute stream) and downloaded (copy_out stream) while
+    // block j + 1 is uploaded, so both PCIe directions and the NTT overlap.
+    // The tree needs whole rows and starts after the last block's LDE.
+    const uint64_t cw = w >= 64 ? ((w + 3) / 4 + 7) / 8 * 8 : w;  // about four blocks, multiples of 8
+    const uint64_t nchunks = (w + cw - 1) / cw;
+    ZK_TRY(cudaEventRecord(st->lde_ready, cs));  // the allocations above, in stream order
+    ZK_TRY(cudaStreamWaitEvent(st->copy, st->lde_ready, 0));
+    for (uint64_t j = 0; !rc && j < nchunks; j++) {
+        const uint64_t c0 = j * cw, cn = (w - c0) < cw ? (w - c0) : cw;
+        rc = (int)cudaMemcpy2DAsync(d_in + c0, 8 * w, h_coeffs + c0, 8 * w, 8 * cn, L, cudaMemcpyHostToDevice,
+                                    st->copy);
+        if (!rc) rc = (int)cudaEventRecord(st->in_ready[j], st->copy);
+        if (!rc) rc = (int)cudaStreamWaitEvent(cs, st->in_ready[j], 0);
+        if (!rc) rc = lde_launch_ld(d_in + c0, d_lde + c0, d_scr ? d_scr + c0 : nullptr, lg_l, lg_blowup, cn, w, cs);
+        if (!rc && h_lde) {
+            rc = (int)cudaEventRecord(st->chunk_lde[j], cs);
+            if (!rc) rc = (int)cudaStreamWaitEvent(st->copy_out, st->chunk_lde[j], 0);
+            if (!rc)
+                rc = (int)cudaMemcpy2DAsync(h_lde + c0, 8 * w, d_lde + c0, 8 * w, 8 * cn, H, cudaMemcpyDeviceToHost,
+                                            st->copy_out);
+        }
     }
     if (!rc) rc = merkle_build(d_lde, H, w, d_layers, cs);
     if (!rc) {
@@ -142,7 +165,7 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
             rc = (int)cudaMemcpyAsync(h_root, d_layers + 8 * g.offset.back(), 64, cudaMemcpyDeviceToHost, cs);
     }
     if (!rc && h_lde) {
-        rc = (int)cudaEventRecord(st->done, st->copy);
+        rc = (int)cudaEventRecord(st->done, st->copy_out);
         if (!rc) rc = (int)cudaStreamWaitEvent(cs, st->done, 0);
     }
     cudaFreeAsync(d_in, cs);

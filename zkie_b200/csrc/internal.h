@@ -39,6 +39,10 @@ int merkle_build_from_leaves(uint64_t h, uint64_t* layers, cudaStream_t s);
 // (L << lg_blowup) x w, scratch holds (L << lg_blowup) * w u64.
 int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l,
                uint32_t lg_blowup, uint64_t w, cudaStream_t s);
+// The same on w columns of wider matrices: in, out and scratch all have row
+// stride ld (e.g. a column block, pointers offset to its first column).
+int lde_launch_ld(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l, uint32_t lg_blowup,
+                  uint64_t w, uint64_t ld, cudaStream_t s);
 uint64_t lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w);
 
 // ---- commit / GKR pieces used by the fused shard prove (shard.cu) ------------------

@@ -59,7 +59,8 @@ int ensure_twiddles() {
 struct PassDesc {
     const uint64_t* in;
     uint64_t* out;
-    uint64_t w;           // row width of in and out
+    uint64_t w;           // columns transformed
+    uint64_t ld;          // row stride of in and out, in elements (>= w)
     uint64_t rows_valid;  // input rows >= rows_valid are zero (LDE padding)
     uint64_t F;           // lanes
     uint64_t fin, sin, jin;
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(kNttThreads) k_ntt_pass(PassDesc d) {
     const uint32_t c = tid & (C - 1);
     const bool cok = c < ccur;
     const uint32_t nq = total >> logC, qstep = kNttThreads >> logC;
-    const IdxT w = (IdxT)d.w;
+    const IdxT w = (IdxT)d.ld;  // row stride
     {
         const IdxT row0 = (IdxT)(f0 * d.fin + s_idx * d.sin);
         const IdxT fin = (IdxT)d.fin, jin = (IdxT)d.jin;
@@ -316,7 +317,7 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
                                         IdxT row_in0, IdxT row_out0, uint64_t f) {
     constexpr int R = 1 << L, G = kN2Elems / R;
     const uint32_t m = d.m, lgs = lgm - L;  // stride M_i / R
-    const IdxT w = (IdxT)d.w;
+    const IdxT w = (IdxT)d.ld;  // row stride
 #pragma unroll
     for (int gi = 0; gi < G; gi++) {
         const uint32_t gam = q * G + gi;
@@ -495,13 +496,15 @@ int run_pass_sel(PassDesc d, uint64_t S, cudaStream_t s) {
     return run_pass<kCallerTab, IdxT>(d, S, s);
 }
 
-// Full transform of size 2^lg over the columns of `in` (rows >= rows_valid
-// are zero) into `out`, using `scratch` (2^lg * w u64) between passes.
+// Full transform of size 2^lg over the w columns of `in` (row stride ld;
+// rows >= rows_valid are zero) into `out` (row stride ld), using `scratch`
+// (2^lg rows of stride ld) between passes.
 template <bool kCallerTab, typename IdxT>
-int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w,
-             uint64_t rows_valid, const uint64_t* tab, uint32_t tab_log, cudaStream_t s) {
+int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w, uint64_t ld,
+               uint64_t rows_valid, const uint64_t* tab, uint32_t tab_log, cudaStream_t s) {
     PassDesc base{};
     base.w = w;
+    base.ld = ld;
     base.tab = tab;
     base.tab_log = tab_log;
     if (lg <= 10) {
@@ -562,12 +565,12 @@ int dft_plan_t(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg
 }
 
 template <bool kCallerTab>
-int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w,
+int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, uint64_t w, uint64_t ld,
              uint64_t rows_valid, const uint64_t* tab, uint32_t tab_log, cudaStream_t s) {
-    // 32-bit offsets when the whole 2^lg x w matrix is addressable with them
-    if (lg < 32 && (w << lg) < (1ull << 32))
-        return dft_plan_t<kCallerTab, uint32_t>(in, out, scratch, lg, w, rows_valid, tab, tab_log, s);
-    return dft_plan_t<kCallerTab, uint64_t>(in, out, scratch, lg, w, rows_valid, tab, tab_log, s);
+    // 32-bit offsets when the whole 2^lg x ld matrix is addressable with them
+    if (lg < 32 && (ld << lg) < (1ull << 32))
+        return dft_plan_t<kCallerTab, uint32_t>(in, out, scratch, lg, w, ld, rows_valid, tab, tab_log, s);
+    return dft_plan_t<kCallerTab, uint64_t>(in, out, scratch, lg, w, ld, rows_valid, tab, tab_log, s);
 }
 
 // Input of one coset of the LDE (the rows i = g + G*i' of the H-row output):
@@ -599,15 +602,20 @@ uint64_t lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w) {
     return lg <= 10 ? 0 : (w << lg);
 }
 
-int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l,
-               uint32_t lg_blowup, uint64_t w, cudaStream_t s) {
+int lde_launch_ld(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l, uint32_t lg_blowup,
+                  uint64_t w, uint64_t ld, cudaStream_t s) {
     const uint32_t lg = lg_l + lg_blowup;
     if (w == 0) return 0;
-    if (!in || !out || (lg > 10 && !scratch)) return (int)cudaErrorInvalidValue;
+    if (!in || !out || (lg > 10 && !scratch) || ld < w) return (int)cudaErrorInvalidValue;
     if (lg > 30) return (int)cudaErrorInvalidValue;
     int rc = ensure_twiddles();
     if (rc) return rc;
-    return dft_plan<false>(in, out, scratch, lg, w, 1ull << lg_l, nullptr, 0, s);
+    return dft_plan<false>(in, out, scratch, lg, w, ld, 1ull << lg_l, nullptr, 0, s);
+}
+
+int lde_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg_l,
+               uint32_t lg_blowup, uint64_t w, cudaStream_t s) {
+    return lde_launch_ld(in, out, scratch, lg_l, lg_blowup, w, w, s);
 }
 
 // Coset g of G = 2^lg_g of the LDE (H = 2^(lg_l + lg_blowup) rows): rows
@@ -640,8 +648,8 @@ int lde_coset_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint3
     k_coset_twist<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(in, 1ull << lg_l, w, lg_h, g, R, 1ull << (lg_h - lg_g),
                                                               fold ? 1u << (lg_g - lg_blowup) : 1u, y);
     ZK_LAUNCH_CHECK();
-    if (fold) return dft_plan<false>(y, out, sub, lg_h - lg_g, w, ~0ull, nullptr, 0, s);
-    return dft_plan<false>(y, out, sub, lg_h - lg_g, w, 1ull << lg_l, nullptr, 0, s);
+    if (fold) return dft_plan<false>(y, out, sub, lg_h - lg_g, w, w, ~0ull, nullptr, 0, s);
+    return dft_plan<false>(y, out, sub, lg_h - lg_g, w, w, 1ull << lg_l, nullptr, 0, s);
 }
 
 }  // namespace zk
@@ -663,7 +671,7 @@ int zkie_ntt_forward_goldilocks(uint64_t* d_mat, uint64_t* d_temp, uint32_t lg_h
     if (!d_mat || !d_tw || (lg_h > 10 && !d_temp)) return (int)cudaErrorInvalidValue;
     if (lg_h > 30) return (int)cudaErrorInvalidValue;
     const uint64_t* top = d_tw + ((1ull << (lg_h - 1)) - 1);
-    return dft_plan<true>(d_mat, d_mat, d_temp, lg_h, w, ~0ull, top, lg_h, 0);
+    return dft_plan<true>(d_mat, d_mat, d_temp, lg_h, w, w, ~0ull, top, lg_h, 0);
 }
 
 uint64_t zkie2_lde_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w) {

@@ -6,10 +6,14 @@
     python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
     python -m zkie_b200.perfcases virtual --log-size 21
     python -m zkie_b200.perfcases sop --log-size 20 --polys 4
+    python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
+    python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
+    python -m zkie_b200.perfcases sweep
 
-Each case prints one JSON line: device time per call (CUDA events on the
-launching stream, after warm-up) and the algorithmic HBM bytes per call.
-Inputs are synthetic, uniform canonical field elements.
+Each case prints one JSON line (the sweep one per configuration-2 case):
+time per call (CUDA events on the launching stream, after warm-up) and,
+where meaningful, the algorithmic HBM bytes per call.  Inputs are synthetic,
+uniform canonical field elements.
 """
 import argparse
 import json
