@@ -19,8 +19,8 @@ namespace {
 constexpr int kMaxChunks = 8;  // column blocks of the pipelined host commit
 
 struct DevStreams {
-    cudaStream_t compute = nullptr, copy = nullptr, copy_out = nullptr;
-    cudaEvent_t lde_ready = nullptr, done = nullptr;
+    cudaStream_t compute = nullptr, copy = nullptr, copy_out = nullptr, hash = nullptr;
+    cudaEvent_t lde_ready = nullptr, done = nullptr, hashed = nullptr;
     cudaEvent_t in_ready[kMaxChunks] = {}, chunk_lde[kMaxChunks] = {};
     bool ready = false;
 };
@@ -36,8 +36,10 @@ int get_streams(DevStreams** out) {
         ZK_TRY(cudaStreamCreateWithFlags(&s.compute, cudaStreamNonBlocking));
         ZK_TRY(cudaStreamCreateWithFlags(&s.copy, cudaStreamNonBlocking));
         ZK_TRY(cudaStreamCreateWithFlags(&s.copy_out, cudaStreamNonBlocking));
+        ZK_TRY(cudaStreamCreateWithFlags(&s.hash, cudaStreamNonBlocking));
         ZK_TRY(cudaEventCreateWithFlags(&s.lde_ready, cudaEventDisableTiming));
         ZK_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        ZK_TRY(cudaEventCreateWithFlags(&s.hashed, cudaEventDisableTiming));
         for (int i = 0; i < kMaxChunks; i++) {
             ZK_TRY(cudaEventCreateWithFlags(&s.in_ready[i], cudaEventDisableTiming));
             ZK_TRY(cudaEventCreateWithFlags(&s.chunk_lde[i], cudaEventDisableTiming));
@@ -134,14 +136,21 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
     ZK_TRY(cudaMallocAsync((void**)&d_layers, 64 * g.total, cs));
     if (scratch) ZK_TRY(cudaMallocAsync((void**)&d_scr, 8 * scratch, cs));
     rc = p2_ensure_default();
-    // Pipeline over column blocks: block j is uploaded (copy stream), its
-    // LDE computed (compute stream) and downloaded (copy_out stream) while
-    // block j + 1 is uploaded, so both PCIe directions and the NTT overlap.
-    // The tree needs whole rows and starts after the last block's LDE.
+    // Pipeline over column blocks: block j is uploaded (copy stream), its LDE
+    // computed (compute stream), downloaded (copy_out stream) and absorbed
+    // into every row's sponge (hash stream) while block j + 1 is uploaded.
+    // Both PCIe directions, the NTT and the hashing overlap; the sponge state
+    // of each row waits in HBM between blocks (block boundaries are
+    // multiples of 8 columns, i.e. absorption boundaries).  The tree above
+    // the leaves follows the last block.
     const uint64_t cw = w >= 64 ? ((w + 3) / 4 + 7) / 8 * 8 : w;  // about four blocks, multiples of 8
     const uint64_t nchunks = (w + cw - 1) / cw;
+    uint64_t* d_states = nullptr;
+    if (nchunks > 1) ZK_TRY(cudaMallocAsync((void**)&d_states, 128 * H, cs));
+    cudaStream_t hs = st->hash;
     ZK_TRY(cudaEventRecord(st->lde_ready, cs));  // the allocations above, in stream order
     ZK_TRY(cudaStreamWaitEvent(st->copy, st->lde_ready, 0));
+    ZK_TRY(cudaStreamWaitEvent(hs, st->lde_ready, 0));
     for (uint64_t j = 0; !rc && j < nchunks; j++) {
         const uint64_t c0 = j * cw, cn = (w - c0) < cw ? (w - c0) : cw;
         rc = (int)cudaMemcpy2DAsync(d_in + c0, 8 * w, h_coeffs + c0, 8 * w, 8 * cn, L, cudaMemcpyHostToDevice,
@@ -149,29 +158,32 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
         if (!rc) rc = (int)cudaEventRecord(st->in_ready[j], st->copy);
         if (!rc) rc = (int)cudaStreamWaitEvent(cs, st->in_ready[j], 0);
         if (!rc) rc = lde_launch_ld(d_in + c0, d_lde + c0, d_scr ? d_scr + c0 : nullptr, lg_l, lg_blowup, cn, w, cs);
+        if (!rc) rc = (int)cudaEventRecord(st->chunk_lde[j], cs);
         if (!rc && h_lde) {
-            rc = (int)cudaEventRecord(st->chunk_lde[j], cs);
-            if (!rc) rc = (int)cudaStreamWaitEvent(st->copy_out, st->chunk_lde[j], 0);
+            rc = (int)cudaStreamWaitEvent(st->copy_out, st->chunk_lde[j], 0);
             if (!rc)
                 rc = (int)cudaMemcpy2DAsync(h_lde + c0, 8 * w, d_lde + c0, 8 * w, 8 * cn, H, cudaMemcpyDeviceToHost,
                                             st->copy_out);
         }
+        if (!rc) rc = (int)cudaStreamWaitEvent(hs, st->chunk_lde[j], 0);
+        if (!rc && nchunks > 1)
+            rc = launch_leaf_absorb(d_lde, w, c0, cn, H, d_states, d_layers, j == 0, j + 1 == nchunks, hs);
     }
-    if (!rc) rc = merkle_build(d_lde, H, w, d_layers, cs);
+    if (!rc) rc = nchunks > 1 ? merkle_build_from_leaves(H, d_layers, hs) : merkle_build(d_lde, H, w, d_layers, hs);
     if (!rc) {
         if (h_layers)
-            rc = (int)cudaMemcpyAsync(h_layers, d_layers, 64 * g.total, cudaMemcpyDeviceToHost, cs);
+            rc = (int)cudaMemcpyAsync(h_layers, d_layers, 64 * g.total, cudaMemcpyDeviceToHost, hs);
         else
-            rc = (int)cudaMemcpyAsync(h_root, d_layers + 8 * g.offset.back(), 64, cudaMemcpyDeviceToHost, cs);
+            rc = (int)cudaMemcpyAsync(h_root, d_layers + 8 * g.offset.back(), 64, cudaMemcpyDeviceToHost, hs);
     }
-    if (!rc && h_lde) {
-        rc = (int)cudaEventRecord(st->done, st->copy_out);
-        if (!rc) rc = (int)cudaStreamWaitEvent(cs, st->done, 0);
-    }
+    // join everything on the compute stream before the frees
+    if (cudaEventRecord(st->hashed, hs) == cudaSuccess) cudaStreamWaitEvent(cs, st->hashed, 0);
+    if (h_lde && cudaEventRecord(st->done, st->copy_out) == cudaSuccess) cudaStreamWaitEvent(cs, st->done, 0);
     cudaFreeAsync(d_in, cs);
     cudaFreeAsync(d_lde, cs);
     cudaFreeAsync(d_layers, cs);
     if (d_scr) cudaFreeAsync(d_scr, cs);
+    if (d_states) cudaFreeAsync(d_states, cs);
     cudaError_t e = cudaStreamSynchronize(cs);
     if (!rc && e != cudaSuccess) rc = (int)e;
     if (!rc && h_layers)

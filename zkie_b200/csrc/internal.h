@@ -21,6 +21,11 @@ int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint
                      uint64_t w, cudaStream_t s);
 int launch_compress(const uint64_t* prev, uint64_t* next, uint64_t from, uint64_t to,
                     uint32_t step, cudaStream_t s);
+// Leaf sponge over columns [c0, c0 + cn) of each of h rows (row stride ld,
+// c0 a multiple of 8); per-row states (16 u64) carried in `states` between
+// column blocks; the last block writes the digests.
+int launch_leaf_absorb(const uint64_t* mat, uint64_t ld, uint64_t c0, uint64_t cn, uint64_t h, uint64_t* states,
+                       uint64_t* digests, bool first, bool last, cudaStream_t s);
 
 // Merkle layer geometry of one matrix of h rows (pcs/merkle_cuda.rs:203-209).
 struct MerkleGeom {

@@ -102,6 +102,50 @@ __global__ void __launch_bounds__(kHashThreads)
     for (int q = 0; q < 4; q++) dst[q] = make_ulonglong2(gl_canon(s[2 * q]), gl_canon(s[2 * q + 1]));
 }
 
+// The leaf sponge over one block of columns [c0, c0 + cn) of every row (rows
+// of stride ld), so hashing can run while later column blocks are still
+// being uploaded and transformed.  c0 is a multiple of 8, so block
+// boundaries are absorption boundaries and the result equals k_leaf_rows.
+// The 16-element state of each row waits in `states` between blocks; the
+// first block starts from zeros, the last writes the digest.
+__global__ void __launch_bounds__(kHashThreads)
+    k_leaf_absorb(const uint64_t* __restrict__ mat, uint64_t ld, uint64_t c0, uint64_t cn, uint64_t h,
+                  uint64_t* __restrict__ states, uint64_t* __restrict__ digests, int first, int last) {
+    const uint64_t row = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= h) return;
+    uint64_t s[16];
+    ulonglong2* sp = reinterpret_cast<ulonglong2*>(states + row * 16);
+    if (first) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) s[i] = 0;
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const ulonglong2 v = sp[q];
+            s[2 * q] = v.x;
+            s[2 * q + 1] = v.y;
+        }
+    }
+    const uint64_t* src = mat + row * ld + c0;
+    const uint64_t nblk = (cn + 7) >> 3;
+    for (uint64_t b = 0; b < nblk; b++) {
+        const uint64_t base = b << 3;
+        const uint64_t n = (cn - base) < 8 ? (cn - base) : 8;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if ((uint64_t)i < n) s[i] = __ldg(src + base + i);
+        p2_permute(s, c_p2);
+    }
+    if (last) {
+        ulonglong2* dst = reinterpret_cast<ulonglong2*>(digests + row * 8);
+#pragma unroll
+        for (int q = 0; q < 4; q++) dst[q] = make_ulonglong2(gl_canon(s[2 * q]), gl_canon(s[2 * q + 1]));
+    } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++) sp[q] = make_ulonglong2(s[2 * q], s[2 * q + 1]);
+    }
+}
+
 // Latency-bound shapes (few rows or nodes): the same leaf sponge and
 // compression with four threads per state (p2_permute_x4).  Lane g of each
 // aligned 4-lane group holds state lanes 4g..4g+3; g = 0, 1 hold the rate and
@@ -248,6 +292,16 @@ int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint
                                                                                      w);
     else
         k_leaf_rows<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0, row_end, w);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int launch_leaf_absorb(const uint64_t* mat, uint64_t ld, uint64_t c0, uint64_t cn, uint64_t h, uint64_t* states,
+                       uint64_t* digests, bool first, bool last, cudaStream_t s) {
+    if (h == 0) return 0;
+    if (!mat || !states || !digests || (c0 & 7) || cn == 0) return (int)cudaErrorInvalidValue;
+    k_leaf_absorb<<<(unsigned)ceil_div(h, kHashThreads), kHashThreads, 0, s>>>(mat, ld, c0, cn, h, states, digests,
+                                                                              first ? 1 : 0, last ? 1 : 0);
     ZK_LAUNCH_CHECK();
     return 0;
 }
