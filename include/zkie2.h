@@ -244,6 +244,31 @@ int zkie2_virtual_prove(const uint64_t *const *d_mles, uint32_t n_mles, uint32_t
                         const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms, const uint64_t *h_ch,
                         uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch, zkie_stream_t stream);
 
+/* ---- logUp GKR fraction tree (common/logup_gkr.rs) ------------------------------------ */
+/* prove_fractional_with_challenges (logup_gkr.rs:29-69) over device tables
+ * num, den of 2^lg_n values (read only), with lg_n challenges full_r and cs
+ * (host).  Layer l = 0 .. lg_n-1 is a prove_virtual over seven tables with
+ * lg_n - l - 1 rounds of 4 evaluations: h_rounds gets every layer's rounds
+ * concatenated (2 lg_n (lg_n - 1) values), h_finals 7 final evaluations per
+ * layer, h_final_nd the last layer's (num, den).  Synchronous. */
+uint64_t zkie2_fractional_scratch_elems(uint32_t lg_n);
+int zkie2_fractional_prove(const uint64_t *d_num, const uint64_t *d_den, uint32_t lg_n, const uint64_t *h_full_r,
+                           const uint64_t *h_cs, uint64_t *h_rounds, uint64_t *h_finals, uint64_t *h_final_nd,
+                           uint64_t *d_scratch, zkie_stream_t stream);
+/* Lookup columns num, den of zkie2_lookup_len(n, t, mode) values (device):
+ * mode 0 build_lookup_num_den (logup_gkr.rs:210-240: witness fractions, then
+ * the table with -multiplicity, multiplicities counted on the device;
+ * cudaErrorInvalidValue if some x >= t), 1 build_lookup_witness_num_den
+ * (:261-277), 2 the witness columns of prove_lookup_witness_batch_columns
+ * (:340-370: at least 32 rows, padding den = alpha), 3
+ * build_lookup_table_num_den (:285-301, multiplicities d_m from the caller).
+ * d_x is u32.  Mode 0 synchronizes on the stream to report a bad index. */
+uint64_t zkie2_lookup_len(uint64_t n, uint64_t t, uint32_t mode);
+uint64_t zkie2_lookup_scratch_elems(uint64_t t);
+int zkie2_lookup_num_den(const uint32_t *d_x, const uint64_t *d_y, uint64_t n, const uint64_t *d_table,
+                         const uint64_t *d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                         uint64_t *d_num, uint64_t *d_den, uint64_t *d_scratch, zkie_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

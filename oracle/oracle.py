@@ -91,6 +91,12 @@ def lib():
             "orc_op_matmul_prove": (None, [_pu64, _pu64, _pu64, _u64, _u64, _u64, C.POINTER(Challenger),
                                            _pu64, _pu64, _pu64, _pu64, _pu64, _pu64, _pu64]),
             "orc_shard_dag_child": (None, [_pu64, _u32, _u64, _u64, C.POINTER(Transcript)]),
+            "orc_fractional_prove": (None, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _pu64, _pu64]),
+            "orc_fractional_verify": (C.c_int, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _u64, _u64, _u64]),
+            "orc_fractional_chain_core": (C.c_int, [_u32, _pu64, _pu64, _pu64, _pu64]),
+            "orc_lookup_len": (_u64, [_u64, _u64, _u32]),
+            "orc_lookup_num_den": (_u64, [_pu32, _pu64, _u64, _pu64, _pu64, _u64, _u32, _u64, _u64, _pu64,
+                                          _pu64]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -459,3 +465,59 @@ def shard_dag_child(op_ids, ops_per_shard, shard_index):
     t = OracleTranscript(b"x")
     lib().orc_shard_dag_child(ptr(ids), ids.size // 3, ops_per_shard, shard_index, C.byref(t.t))
     return t
+
+
+# ---- logUp GKR fraction tree (logup_gkr.rs:29-164, 210-301) ---------------------------
+def fractional_prove(num, den, full_r, cs):
+    """-> (rounds: list of (t_l, 4) arrays, finals: (lg, 7), final_num, final_den)."""
+    nm, dn, fr, c = u64(num), u64(den), u64(full_r), u64(cs)
+    lg = nm.size.bit_length() - 1
+    rounds = np.zeros(max(2 * lg * (lg - 1), 1), dtype=np.uint64)
+    finals = np.zeros(max(7 * lg, 1), dtype=np.uint64)
+    fnd = np.zeros(2, dtype=np.uint64)
+    lib().orc_fractional_prove(ptr(nm), ptr(dn), lg, ptr(fr) if fr.size else None, ptr(c) if c.size else None,
+                               ptr(rounds), ptr(finals), ptr(fnd))
+    out, off = [], 0
+    for layer in range(lg):
+        t = lg - layer - 1
+        out.append(rounds[off:off + 4 * t].reshape(t, 4).copy())
+        off += 4 * t
+    return out, finals[:7 * lg].reshape(lg, 7).copy(), int(fnd[0]), int(fnd[1])
+
+
+def _flat_rounds(rounds):
+    parts = [np.asarray(r, dtype=np.uint64).reshape(-1) for r in rounds]
+    flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.uint64)
+    return np.ascontiguousarray(flat if flat.size else np.zeros(1, dtype=np.uint64))
+
+
+def fractional_verify(num, den, full_r, cs, rounds, final_num, final_den, claimed):
+    nm, dn, fr, c = u64(num), u64(den), u64(full_r), u64(cs)
+    lg = nm.size.bit_length() - 1
+    rf = _flat_rounds(rounds)
+    return bool(lib().orc_fractional_verify(ptr(nm), ptr(dn), lg, ptr(fr) if fr.size else None,
+                                            ptr(c) if c.size else None, ptr(rf), final_num, final_den, claimed))
+
+
+def fractional_chain_core(full_r, cs, rounds, finals):
+    fr, c = u64(full_r), u64(cs)
+    fin = np.ascontiguousarray(np.asarray(finals, dtype=np.uint64).reshape(-1))
+    rf = _flat_rounds(rounds)
+    return bool(lib().orc_fractional_chain_core(fr.size, ptr(fr) if fr.size else None, ptr(c) if c.size else None,
+                                                ptr(rf), ptr(fin) if fin.size else None))
+
+
+def lookup_num_den(x, y, table, m, mode, alpha, beta):
+    """mode 0 merged, 1 witness, 2 witness columns, 3 table; None if an index
+    is outside the table."""
+    xx = np.ascontiguousarray(np.asarray(x if x is not None else [], dtype=np.uint32).reshape(-1))
+    yy, tb = u64(y if y is not None else []), u64(table if table is not None else [])
+    mm = u64(m if m is not None else [])
+    n = xx.size if mode != 3 else 0
+    total = lib().orc_lookup_len(n, tb.size, mode)
+    num = np.zeros(total, dtype=np.uint64)
+    den = np.zeros(total, dtype=np.uint64)
+    got = lib().orc_lookup_num_den(xx.ctypes.data_as(_pu32) if xx.size else None, ptr(yy) if yy.size else None, n,
+                                   ptr(tb) if tb.size else None, ptr(mm) if mm.size else None, tb.size, mode,
+                                   int(alpha) % P, int(beta) % P, ptr(num), ptr(den))
+    return (num, den) if got else None

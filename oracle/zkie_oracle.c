@@ -960,3 +960,192 @@ void orc_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_pe
     }
     orc_transcript_absorb_u64(child, shard_index);
 }
+
+/* ============================================================================
+ * logUp GKR fraction tree (crates/zkie-core/src/common/logup_gkr.rs).
+ * Round messages of all layers are concatenated: layer l has lg - l - 1
+ * rounds of 4 evaluations; finals hold 7 evaluations per layer.
+ * ========================================================================== */
+
+/* build_terms (:19-28) over [eq, next_num, next_den, num_lo, num_hi, den_lo, den_hi] */
+static void frac_terms(uint64_t c, uint64_t coeffs[5], uint32_t off[6], uint32_t idx[13])
+{
+    static const uint32_t o[6] = {0, 2, 5, 8, 10, 13};
+    static const uint32_t ix[13] = {0, 1, 0, 3, 6, 0, 4, 5, 0, 2, 0, 5, 6};
+    uint64_t neg = orc_from_i64(-1);
+    coeffs[0] = 1;
+    coeffs[1] = neg;
+    coeffs[2] = neg;
+    coeffs[3] = canon(c);
+    coeffs[4] = orc_mul(neg, canon(c));
+    memcpy(off, o, sizeof(o));
+    memcpy(idx, ix, sizeof(ix));
+}
+
+/* Layer tables of one fraction-tree step (:43-58): mles = 7 x half, contiguous. */
+static void frac_layer_tables(const uint64_t *num, const uint64_t *den, uint64_t half, const uint64_t *r,
+                              uint32_t t, uint64_t *mles)
+{
+    uint64_t *eq = mles, *nn = mles + half, *nd = mles + 2 * half;
+    for (uint64_t s = 0; s < half; s++) {
+        nn[s] = orc_add(orc_mul(num[s], den[half + s]), orc_mul(num[half + s], den[s]));
+        nd[s] = orc_mul(den[s], den[half + s]);
+    }
+    orc_eq_evals(r, t, eq);
+    memcpy(mles + 3 * half, num, 8 * half);
+    memcpy(mles + 4 * half, num + half, 8 * half);
+    memcpy(mles + 5 * half, den, 8 * half);
+    memcpy(mles + 6 * half, den + half, 8 * half);
+}
+
+/* prove_fractional_with_challenges (:29-69). */
+void orc_fractional_prove(const uint64_t *num, const uint64_t *den, uint32_t lg, const uint64_t *full_r,
+                          const uint64_t *cs, uint64_t *rounds, uint64_t *finals, uint64_t final_nd[2])
+{
+    uint64_t n = 1ULL << lg;
+    uint64_t *cn = (uint64_t *)malloc(8 * n), *cd = (uint64_t *)malloc(8 * n);
+    uint64_t *mles = (uint64_t *)malloc(8 * 7 * (n / 2 ? n / 2 : 1));
+    for (uint64_t i = 0; i < n; i++) {
+        cn[i] = canon(num[i]);
+        cd[i] = canon(den[i]);
+    }
+    uint64_t roff = 0;
+    for (uint32_t l = 0; l < lg; l++) {
+        uint64_t half = n >> (l + 1);
+        uint32_t t = lg - l - 1;
+        uint64_t coeffs[5];
+        uint32_t off[6], idx[13];
+        frac_terms(cs[l], coeffs, off, idx);
+        frac_layer_tables(cn, cd, half, full_r, t, mles);
+        orc_virtual_prove(mles, 7, t, coeffs, off, idx, 5, full_r, rounds + roff, finals + 7ULL * l);
+        roff += 4ULL * t;
+        memcpy(cn, mles + half, 8 * half);
+        memcpy(cd, mles + 2 * half, 8 * half);
+    }
+    final_nd[0] = cn[0];
+    final_nd[1] = cd[0];
+    free(cn);
+    free(cd);
+    free(mles);
+}
+
+/* verify_fractional (:83-134): every layer's sumcheck against final
+ * evaluations recomputed from the tables, then final_num == claimed * final_den. */
+int orc_fractional_verify(const uint64_t *num, const uint64_t *den, uint32_t lg, const uint64_t *full_r,
+                          const uint64_t *cs, const uint64_t *rounds, uint64_t final_num, uint64_t final_den,
+                          uint64_t claimed)
+{
+    uint64_t n = 1ULL << lg;
+    uint64_t *cn = (uint64_t *)malloc(8 * n), *cd = (uint64_t *)malloc(8 * n);
+    uint64_t *mles = (uint64_t *)malloc(8 * 7 * (n / 2 ? n / 2 : 1));
+    for (uint64_t i = 0; i < n; i++) {
+        cn[i] = canon(num[i]);
+        cd[i] = canon(den[i]);
+    }
+    int ok = 1;
+    uint64_t roff = 0;
+    for (uint32_t l = 0; ok && l < lg; l++) {
+        uint64_t half = n >> (l + 1);
+        uint32_t t = lg - l - 1;
+        uint64_t coeffs[5], fe[7];
+        uint32_t off[6], idx[13];
+        frac_terms(cs[l], coeffs, off, idx);
+        frac_layer_tables(cn, cd, half, full_r, t, mles);
+        for (int j = 0; j < 7; j++) fe[j] = orc_mle_eval(mles + (uint64_t)j * half, t, full_r);
+        ok = orc_virtual_verify(rounds + roff, t, coeffs, off, idx, 5, 0, full_r, fe);
+        roff += 4ULL * t;
+        memcpy(cn, mles + half, 8 * half);
+        memcpy(cd, mles + 2 * half, 8 * half);
+    }
+    free(cn);
+    free(cd);
+    free(mles);
+    return ok && canon(final_num) == orc_mul(canon(claimed), canon(final_den));
+}
+
+/* verify_fractional_chain_core (:136-164): each layer's sumcheck against its
+ * own stored final evaluations, and the folding link between layers. */
+int orc_fractional_chain_core(uint32_t lg, const uint64_t *full_r, const uint64_t *cs, const uint64_t *rounds,
+                              const uint64_t *finals)
+{
+    uint64_t roff = 0;
+    for (uint32_t l = 0; l < lg; l++) {
+        uint32_t t = lg - l - 1;
+        uint64_t coeffs[5];
+        uint32_t off[6], idx[13];
+        frac_terms(cs[l], coeffs, off, idx);
+        if (!orc_virtual_verify(rounds + roff, t, coeffs, off, idx, 5, 0, full_r, finals + 7ULL * l)) return 0;
+        roff += 4ULL * t;
+    }
+    for (uint32_t l = 0; l + 1 < lg; l++) {
+        const uint64_t *prev = finals + 7ULL * l, *curr = finals + 7ULL * (l + 1);
+        uint32_t tp = lg - l - 1; /* prev.r = full_r[..tp] */
+        uint64_t rk = canon(full_r[tp - 1]), om = orc_sub(1, rk);
+        uint64_t fold_num = orc_add(orc_mul(om, curr[3]), orc_mul(rk, curr[4]));
+        uint64_t fold_den = orc_add(orc_mul(om, curr[5]), orc_mul(rk, curr[6]));
+        if (canon(prev[1]) != fold_num || canon(prev[2]) != fold_den) return 0;
+    }
+    return 1;
+}
+
+/* Lookup columns.  mode 0: build_lookup_num_den (:210-240); 1:
+ * build_lookup_witness_num_den (:261-277); 2: the columns of
+ * prove_lookup_witness_batch_columns (:340-370); 3: build_lookup_table_num_den
+ * (:285-301) with caller multiplicities m.  Returns the column length, or 0 if
+ * an index is out of the table (mode 0). */
+static uint64_t next_pow2_u64(uint64_t x)
+{
+    uint64_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+uint64_t orc_lookup_len(uint64_t n, uint64_t t, uint32_t mode)
+{
+    switch (mode) {
+    case 0: return next_pow2_u64(n + t);
+    case 1: return next_pow2_u64(n);
+    case 2: { uint64_t l = next_pow2_u64(n); return l < 32 ? 32 : l; }
+    case 3: return next_pow2_u64(t);
+    default: return 0;
+    }
+}
+
+uint64_t orc_lookup_num_den(const uint32_t *x, const uint64_t *y, uint64_t n, const uint64_t *table,
+                            const uint64_t *m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                            uint64_t *num, uint64_t *den)
+{
+    uint64_t total = orc_lookup_len(n, t, mode);
+    if (mode == 3) {
+        for (uint64_t j = 0; j < total; j++) {
+            uint64_t tj = j < t ? canon(table[j]) : 0;
+            num[j] = j < t ? canon(m[j]) : 0;
+            den[j] = orc_add(orc_add(canon(alpha), canon(j)), orc_mul(canon(beta), tj));
+        }
+        return total;
+    }
+    for (uint64_t i = 0; i < total; i++) {
+        num[i] = 0;
+        den[i] = mode == 2 ? canon(alpha) : 1;
+    }
+    for (uint64_t i = 0; i < n; i++) {
+        num[i] = 1;
+        den[i] = orc_add(orc_add(canon(alpha), x[i]), orc_mul(canon(beta), canon(y[i])));
+    }
+    if (mode == 0) {
+        uint64_t *cnt = (uint64_t *)calloc(t ? t : 1, 8);
+        for (uint64_t i = 0; i < n; i++) {
+            if (x[i] >= t) {
+                free(cnt);
+                return 0;
+            }
+            cnt[x[i]]++;
+        }
+        for (uint64_t j = 0; j < t; j++) {
+            num[n + j] = orc_from_i64(-(int64_t)cnt[j]);
+            den[n + j] = orc_add(orc_add(canon(alpha), canon(j)), orc_mul(canon(beta), canon(table[j])));
+        }
+        free(cnt);
+    }
+    return total;
+}

@@ -166,6 +166,23 @@ void orc_op_matmul_prove(const uint64_t *a, const uint64_t *b, const uint64_t *c
 void orc_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_per_shard,
                          uint64_t shard_index, orc_transcript *child);
 
+/* logUp GKR fraction tree (crates/zkie-core/src/common/logup_gkr.rs:29-164).
+ * rounds: layer l's lg - l - 1 rounds of 4 evaluations, concatenated;
+ * finals: 7 evaluations per layer. */
+void orc_fractional_prove(const uint64_t *num, const uint64_t *den, uint32_t lg, const uint64_t *full_r,
+                          const uint64_t *cs, uint64_t *rounds, uint64_t *finals, uint64_t final_nd[2]);
+int orc_fractional_verify(const uint64_t *num, const uint64_t *den, uint32_t lg, const uint64_t *full_r,
+                          const uint64_t *cs, const uint64_t *rounds, uint64_t final_num, uint64_t final_den,
+                          uint64_t claimed);
+int orc_fractional_chain_core(uint32_t lg, const uint64_t *full_r, const uint64_t *cs, const uint64_t *rounds,
+                              const uint64_t *finals);
+/* Lookup columns (logup_gkr.rs:210-301, 340-370); mode 0 merged, 1 witness,
+ * 2 witness as committed columns, 3 table with multiplicities m. */
+uint64_t orc_lookup_len(uint64_t n, uint64_t t, uint32_t mode);
+uint64_t orc_lookup_num_den(const uint32_t *x, const uint64_t *y, uint64_t n, const uint64_t *table,
+                            const uint64_t *m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                            uint64_t *num, uint64_t *den);
+
 #ifdef __cplusplus
 }
 #endif

@@ -249,6 +249,26 @@ ZK_HD void acc160_mac(Acc160& a, uint64_t x, uint64_t y) {
 #endif
 }
 
+// a += x
+ZK_HD void acc160_add(Acc160& a, uint64_t x) {
+#if defined(__CUDA_ARCH__)
+    asm("add.cc.u32  %0, %0, %5;\n\t"
+        "addc.cc.u32 %1, %1, %6;\n\t"
+        "addc.cc.u32 %2, %2, 0;\n\t"
+        "addc.cc.u32 %3, %3, 0;\n\t"
+        "addc.u32    %4, %4, 0;"
+        : "+r"(a.w[0]), "+r"(a.w[1]), "+r"(a.w[2]), "+r"(a.w[3]), "+r"(a.w[4])
+        : "r"((uint32_t)x), "r"((uint32_t)(x >> 32)));
+#else
+    uint64_t carry = x;
+    for (int i = 0; i < 5 && carry; i++) {
+        const uint64_t s = (uint64_t)a.w[i] + (uint32_t)carry;
+        a.w[i] = (uint32_t)s;
+        carry = (carry >> 32) + (s >> 32);
+    }
+#endif
+}
+
 // lo + mid * 2^64 + hi * 2^128 with 2^128 == -2^32 (mod p); hi * 2^32 < p.
 ZK_HD uint64_t acc160_reduce(const Acc160& a) {
     const uint64_t r = gl_reduce128(pack64(a.w[0], a.w[1]), pack64(a.w[2], a.w[3]));

@@ -60,6 +60,14 @@ int op_matmul_enqueue(const uint64_t* d_a, const uint64_t* d_b, const uint64_t* 
                       uint64_t n, const uint64_t* u, const uint64_t* v, const uint64_t* ch, uint64_t* d_scratch,
                       uint64_t** d_out, cudaStream_t s);
 
+// ---- virtual sumcheck and MLE pieces used by the LogUp fraction tree (logup.cu) -----
+uint64_t virtual_plan_elems(uint32_t n_mles, uint32_t t);
+int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
+                    const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
+                    uint64_t* d_rounds, uint64_t* d_finals, uint32_t* deg_out, uint64_t* d_scratch,
+                    cudaStream_t stream);
+int eq_table_dev(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s);
+
 // ---- host-side primitives (host.cpp) -------------------------------------------
 void p2_derive_constants_host(uint64_t seed, uint64_t rc_init[64], uint64_t rc_final[64],
                               uint64_t rc_internal[22], uint64_t* diag15);

@@ -1,0 +1,293 @@
+// logup.cu -- the logUp GKR fraction tree on the device: prove_fractional and
+// the lookup numerator / denominator columns it is run on.
+//
+// Reference: crates/zkie-core/src/common/logup_gkr.rs.
+// prove_fractional_with_challenges (:29-69) proves sum_i num[i] / den[i] one
+// layer at a time.  With the current layer split into halves (lo = [0, half),
+// hi = [half, 2 half)) the next layer is
+//     next_num = num_lo * den_hi + num_hi * den_lo,   next_den = den_lo * den_hi
+// (:45-51), and layer l is a virtual sumcheck (prove_virtual,
+// sumcheck.rs:378-438) over the seven tables
+//     [eq(r), next_num, next_den, num_lo, num_hi, den_lo, den_hi]
+// with r = full_r[0 .. lg n - l - 1] as both the eq point and the round
+// challenges, and the five terms of build_terms (:19-28):
+//     eq next_num - eq num_lo den_hi - eq num_hi den_lo + c eq next_den - c eq den_lo den_hi.
+// Here every layer stays in HBM: the halves are pointer offsets into the
+// current layer, the next layer comes from one fused kernel, the eq table
+// from the MLE kernel, and the round messages of all layers go to the host
+// in one copy at the end.
+#include "../../include/zkie2.h"
+#include "common.cuh"
+#include "gl64.cuh"
+#include "internal.h"
+
+namespace zk {
+
+namespace {
+
+constexpr int kFracThreads = 256;
+constexpr uint32_t kFracMles = 7, kFracTerms = 5, kFracDeg = 3;
+constexpr uint32_t kMaxLg = 40;
+
+// next_num[s] = num[s] den[s + half] + num[s + half] den[s] (one exact sum of
+// two 128-bit products, reduced once), next_den[s] = den[s] den[s + half].
+// Two consecutive s per thread when every pointer is 16-byte aligned.
+__device__ __forceinline__ void frac_pair(uint64_t a, uint64_t b, uint64_t c, uint64_t d, uint64_t& nn,
+                                          uint64_t& nd) {
+    Acc160 acc = acc160_zero();
+    acc160_mac(acc, a, d);
+    acc160_mac(acc, b, c);
+    nn = gl_canon(acc160_reduce(acc));
+    nd = gl_canon(gl_mul(c, d));
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kFracThreads)
+    k_fraction_layer(const uint64_t* __restrict__ num, const uint64_t* __restrict__ den, uint64_t half,
+                     uint64_t* __restrict__ nnum, uint64_t* __restrict__ nden) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    if (kVec) {
+        const ulonglong2* nl = reinterpret_cast<const ulonglong2*>(num);
+        const ulonglong2* nh = reinterpret_cast<const ulonglong2*>(num + half);
+        const ulonglong2* dl = reinterpret_cast<const ulonglong2*>(den);
+        const ulonglong2* dh = reinterpret_cast<const ulonglong2*>(den + half);
+        ulonglong2* on = reinterpret_cast<ulonglong2*>(nnum);
+        ulonglong2* od = reinterpret_cast<ulonglong2*>(nden);
+        for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < half / 2; i += stride) {
+            const ulonglong2 a = __ldg(nl + i), b = __ldg(nh + i), c = __ldg(dl + i), d = __ldg(dh + i);
+            uint64_t n0, d0, n1, d1;
+            frac_pair(a.x, b.x, c.x, d.x, n0, d0);
+            frac_pair(a.y, b.y, c.y, d.y, n1, d1);
+            on[i] = make_ulonglong2(n0, n1);
+            od[i] = make_ulonglong2(d0, d1);
+        }
+    } else {
+        for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < half; s += stride)
+            frac_pair(__ldg(num + s), __ldg(num + half + s), __ldg(den + s), __ldg(den + half + s), nnum[s], nden[s]);
+    }
+}
+
+__global__ void k_fraction_final(const uint64_t* num, const uint64_t* den, uint64_t* out) {
+    if (threadIdx.x == 0) {
+        out[0] = gl_canon(num[0]);
+        out[1] = gl_canon(den[0]);
+    }
+}
+
+unsigned frac_grid(uint64_t work) {
+    const uint64_t b = ceil_div(work, kFracThreads);
+    return (unsigned)(b < 148ull * 16 ? (b ? b : 1) : 148ull * 16);
+}
+
+int launch_fraction_layer(const uint64_t* num, const uint64_t* den, uint64_t half, uint64_t* nnum, uint64_t* nden,
+                          cudaStream_t s) {
+    const bool vec = half % 2 == 0 &&
+                     ((reinterpret_cast<uintptr_t>(num) | reinterpret_cast<uintptr_t>(den) |
+                       reinterpret_cast<uintptr_t>(nnum) | reinterpret_cast<uintptr_t>(nden)) & 15) == 0;
+    if (vec)
+        k_fraction_layer<true><<<frac_grid(half / 2), kFracThreads, 0, s>>>(num, den, half, nnum, nden);
+    else
+        k_fraction_layer<false><<<frac_grid(half), kFracThreads, 0, s>>>(num, den, half, nnum, nden);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+// Scratch layout of zkie2_fractional_prove for n = 2^lg (u64 offsets, every
+// region a multiple of two elements so 16-byte alignment carries through).
+struct FracScratch {
+    uint64_t *a_num, *a_den, *b_num, *b_den, *eq, *vscr, *rounds, *finals, *final_nd;
+};
+
+uint64_t even(uint64_t x) { return (x + 1) & ~1ull; }
+
+uint64_t frac_layout(uint32_t lg, FracScratch* fs, uint64_t* base) {
+    const uint64_t n = 1ull << lg;
+    uint64_t vmax = 0;
+    for (uint32_t l = 0; l < lg; l++) {
+        const uint64_t v = virtual_plan_elems(kFracMles, lg - l - 1);
+        vmax = v > vmax ? v : vmax;
+    }
+    uint64_t off = 0;
+    auto take = [&](uint64_t** p, uint64_t cnt) {
+        if (base) *p = base + off;
+        off += even(cnt);
+    };
+    FracScratch s{};
+    take(&s.a_num, n / 2);
+    take(&s.a_den, n / 2);
+    take(&s.b_num, n / 4);
+    take(&s.b_den, n / 4);
+    take(&s.eq, n / 2);
+    take(&s.vscr, vmax);
+    take(&s.rounds, 2ull * lg * (lg ? lg - 1 : 0) + 2);
+    take(&s.finals, (uint64_t)kFracMles * lg + 1);
+    take(&s.final_nd, 2);
+    if (fs) *fs = s;
+    return off;
+}
+
+// Lookup column modes (logup_gkr.rs): the merged witness + table columns
+// (build_lookup_num_den :210-240), the witness side alone
+// (build_lookup_witness_num_den :261-277, prove_lookup_witness_batch :317-339),
+// the witness side as committed columns (prove_lookup_witness_batch_columns
+// :340-370: at least 32 rows, padding rows get den = alpha), and the table
+// side with caller multiplicities (build_lookup_table_num_den :285-301).
+enum : uint32_t { kLookupMerged = 0, kLookupWitness = 1, kLookupWitnessColumns = 2, kLookupTable = 3 };
+
+uint64_t next_pow2(uint64_t x) {
+    uint64_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+uint64_t lookup_len(uint64_t n, uint64_t t, uint32_t mode) {
+    switch (mode) {
+        case kLookupMerged: return next_pow2(n + t);
+        case kLookupWitness: return next_pow2(n);
+        case kLookupWitnessColumns: {
+            const uint64_t l = next_pow2(n);
+            return l < 32 ? 32 : l;
+        }
+        case kLookupTable: return next_pow2(t);
+        default: return 0;
+    }
+}
+
+// m[x[i]] += 1 for i < n; an index at or above t raises *bad (the reference
+// would index out of bounds and panic).
+__global__ void k_lookup_hist(const uint32_t* __restrict__ x, uint64_t n, uint64_t t, uint32_t* __restrict__ m,
+                              uint32_t* __restrict__ bad) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint32_t xi = __ldg(x + i);
+        if (xi < t)
+            atomicAdd(m + xi, 1u);
+        else
+            atomicOr(bad, 1u);
+    }
+}
+
+// alpha + j + beta * v as a canonical field element
+__device__ __forceinline__ uint64_t lookup_den(uint64_t alpha, uint64_t j, uint64_t beta, uint64_t v) {
+    return gl_canon(gl_add(gl_add(alpha, j), gl_mul(beta, v)));
+}
+
+__global__ void k_lookup_fill(const uint32_t* __restrict__ x, const uint64_t* __restrict__ y, uint64_t n,
+                              const uint64_t* __restrict__ table, uint64_t t, const uint32_t* __restrict__ m32,
+                              const uint64_t* __restrict__ m64, uint32_t mode, uint64_t alpha, uint64_t beta,
+                              uint64_t total, uint64_t* __restrict__ num, uint64_t* __restrict__ den) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        uint64_t nv, dv;
+        if (mode == kLookupTable) {
+            const bool in = i < t;
+            nv = in ? gl_canon(__ldg(m64 + i)) : 0;
+            dv = lookup_den(alpha, i, beta, in ? __ldg(table + i) : 0);
+        } else if (i < n) {
+            nv = 1;
+            dv = lookup_den(alpha, __ldg(x + i), beta, __ldg(y + i));
+        } else if (mode == kLookupMerged && i - n < t) {
+            const uint64_t j = i - n;
+            const uint32_t c = __ldg(m32 + j);
+            nv = c ? GL_P - c : 0;  // from_i64(-m)
+            dv = lookup_den(alpha, j, beta, __ldg(table + j));
+        } else {
+            nv = 0;
+            dv = mode == kLookupWitnessColumns ? gl_canon(alpha) : 1;
+        }
+        num[i] = nv;
+        den[i] = dv;
+    }
+}
+
+}  // namespace
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+uint64_t zkie2_fractional_scratch_elems(uint32_t lg_n) { return lg_n > kMaxLg ? 0 : frac_layout(lg_n, nullptr, nullptr); }
+
+int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,
+                           const uint64_t* h_cs, uint64_t* h_rounds, uint64_t* h_finals, uint64_t* h_final_nd,
+                           uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_num || !d_den || !h_final_nd || !d_scratch || lg_n > kMaxLg ||
+        (lg_n && (!h_full_r || !h_cs || !h_finals)) || (lg_n > 1 && !h_rounds))
+        return (int)cudaErrorInvalidValue;
+    FracScratch fs;
+    frac_layout(lg_n, &fs, d_scratch);
+    const uint64_t n = 1ull << lg_n;
+    const uint32_t off[kFracTerms + 1] = {0, 2, 5, 8, 10, 13};
+    const uint32_t idx[13] = {0, 1, 0, 3, 6, 0, 4, 5, 0, 2, 0, 5, 6};
+    const uint64_t* cn = d_num;
+    const uint64_t* cd = d_den;
+    uint64_t roff = 0;
+    for (uint32_t l = 0; l < lg_n; l++) {
+        const uint64_t half = n >> (l + 1);
+        const uint32_t t = lg_n - l - 1;
+        uint64_t* nn = (l & 1) ? fs.b_num : fs.a_num;
+        uint64_t* nd = (l & 1) ? fs.b_den : fs.a_den;
+        int rc = launch_fraction_layer(cn, cd, half, nn, nd, stream);
+        if (rc) return rc;
+        rc = eq_table_dev(h_full_r, t, fs.eq, stream);
+        if (rc) return rc;
+        const uint64_t c = gl_canon(h_cs[l]);
+        const uint64_t coeffs[kFracTerms] = {1, GL_P - 1, GL_P - 1, c, gl_canon(GL_P - c)};
+        const uint64_t* mles[kFracMles] = {fs.eq, nn, nd, cn, cn + half, cd, cd + half};
+        rc = virtual_enqueue(mles, kFracMles, t, coeffs, off, idx, kFracTerms, h_full_r, fs.rounds + roff,
+                             fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr, stream);
+        if (rc) return rc;
+        roff += (uint64_t)(kFracDeg + 1) * t;
+        cn = nn;
+        cd = nd;
+    }
+    k_fraction_final<<<1, 32, 0, stream>>>(cn, cd, fs.final_nd);
+    ZK_LAUNCH_CHECK();
+    if (roff) ZK_TRY(cudaMemcpyAsync(h_rounds, fs.rounds, 8 * roff, cudaMemcpyDeviceToHost, stream));
+    if (lg_n)
+        ZK_TRY(cudaMemcpyAsync(h_finals, fs.finals, 8ull * kFracMles * lg_n, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaMemcpyAsync(h_final_nd, fs.final_nd, 16, cudaMemcpyDeviceToHost, stream));
+    ZK_TRY(cudaStreamSynchronize(stream));
+    return 0;
+}
+
+uint64_t zkie2_lookup_len(uint64_t n, uint64_t t, uint32_t mode) { return lookup_len(n, t, mode); }
+
+uint64_t zkie2_lookup_scratch_elems(uint64_t t) { return t / 2 + 2; }
+
+int zkie2_lookup_num_den(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, const uint64_t* d_table,
+                         const uint64_t* d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                         uint64_t* d_num, uint64_t* d_den, uint64_t* d_scratch, cudaStream_t stream) {
+    if (mode > kLookupTable || !d_num || !d_den) return (int)cudaErrorInvalidValue;
+    if (mode != kLookupTable && n && (!d_x || !d_y)) return (int)cudaErrorInvalidValue;
+    if ((mode == kLookupMerged || mode == kLookupTable) && t && !d_table) return (int)cudaErrorInvalidValue;
+    if (mode == kLookupTable && t && !d_m) return (int)cudaErrorInvalidValue;
+    if (mode == kLookupMerged && (!d_scratch || n > 0xFFFFFFFFull)) return (int)cudaErrorInvalidValue;
+    const uint64_t total = lookup_len(n, t, mode);
+    uint32_t* m32 = nullptr;
+    uint32_t* bad = nullptr;
+    if (mode == kLookupMerged) {
+        m32 = reinterpret_cast<uint32_t*>(d_scratch);
+        bad = m32 + 2 * (t / 2 + 1);
+        ZK_TRY(cudaMemsetAsync(d_scratch, 0, 8 * zkie2_lookup_scratch_elems(t), stream));
+        if (n) {
+            k_lookup_hist<<<frac_grid(n), kFracThreads, 0, stream>>>(d_x, n, t, m32, bad);
+            ZK_LAUNCH_CHECK();
+        }
+    }
+    k_lookup_fill<<<frac_grid(total), kFracThreads, 0, stream>>>(d_x, d_y, n, d_table, t, m32, d_m, mode,
+                                                                   gl_canon(alpha), gl_canon(beta), total, d_num,
+                                                                   d_den);
+    ZK_LAUNCH_CHECK();
+    if (mode == kLookupMerged) {
+        uint32_t h_bad = 0;
+        ZK_TRY(cudaMemcpyAsync(&h_bad, bad, 4, cudaMemcpyDeviceToHost, stream));
+        ZK_TRY(cudaStreamSynchronize(stream));
+        if (h_bad) return (int)cudaErrorInvalidValue;
+    }
+    return 0;
+}
+
+}  // extern "C"

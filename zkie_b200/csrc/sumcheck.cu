@@ -43,6 +43,39 @@ __global__ void k_eq_table(Point p, uint32_t d, uint64_t* __restrict__ out) {
     out[x] = gl_canon(acc);
 }
 
+// The same table for d >= 8 with about one multiplication per element: x
+// splits into hi = x >> 8 and lo = x & 255, eq(r, x) = eq(r_hi, hi) eq(r_lo, lo).
+// A 256-thread block builds the 256 low factors (8 products each) and the
+// high factors of its kEqHiPerBlock consecutive hi values (d - 8 each) in
+// shared memory, then writes kEqHiPerBlock rows of 256 with one product per
+// element (consecutive threads, consecutive addresses).
+constexpr uint32_t kEqHiPerBlock = 32;
+__global__ void __launch_bounds__(256) k_eq_table_split(Point p, uint32_t d, uint64_t* __restrict__ out) {
+    __shared__ uint64_t lo[256], hi[kEqHiPerBlock];
+    const uint32_t t = threadIdx.x;
+    const uint64_t nhi = 1ull << (d - 8);
+    const uint32_t per = nhi < kEqHiPerBlock ? (uint32_t)nhi : kEqHiPerBlock;
+    const uint64_t h0 = (uint64_t)blockIdx.x * per;
+    uint64_t a = 1;
+#pragma unroll
+    for (uint32_t j = 0; j < 8; j++) {
+        const uint64_t rj = p.r[j];
+        a = gl_mul(a, ((t >> j) & 1) ? rj : gl_sub(1, rj));
+    }
+    lo[t] = a;
+    if (t < per) {
+        const uint64_t h = h0 + t;
+        uint64_t b = 1;
+        for (uint32_t j = 8; j < d; j++) {
+            const uint64_t rj = p.r[j];
+            b = gl_mul(b, ((h >> (j - 8)) & 1) ? rj : gl_sub(1, rj));
+        }
+        hi[t] = b;
+    }
+    __syncthreads();
+    for (uint32_t i = 0; i < per; i++) out[((h0 + i) << 8) + t] = gl_canon(gl_mul(hi[i], lo[t]));
+}
+
 __device__ __forceinline__ uint64_t warp_sum(uint64_t v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = gl_add(v, __shfl_down_sync(0xffffffffu, v, o));
@@ -392,7 +425,14 @@ int eq_table(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s) {
     Point p{};
     for (uint32_t j = 0; j < d; j++) p.r[j] = h_r[j];
     const uint64_t n = 1ull << d;
-    k_eq_table<<<(unsigned)ceil_div(n, kThreads), kThreads, 0, s>>>(p, d, d_out);
+    if (d >= 8) {
+        const uint64_t nhi = 1ull << (d - 8);
+        const uint64_t blocks = nhi < kEqHiPerBlock ? 1 : nhi / kEqHiPerBlock;
+        if (blocks > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
+        k_eq_table_split<<<(unsigned)blocks, 256, 0, s>>>(p, d, d_out);
+    } else {
+        k_eq_table<<<(unsigned)ceil_div(n, kThreads), kThreads, 0, s>>>(p, d, d_out);
+    }
     ZK_LAUNCH_CHECK();
     return 0;
 }

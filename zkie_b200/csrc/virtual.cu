@@ -12,16 +12,20 @@
 // runs q <= 8 rounds on independent chunks of 2^q consecutive positions: one
 // 128-thread block stages its chunk of every table in shared memory, runs the
 // q rounds there (ping-pong buffers, one barrier per round) and writes
-// per-round partial sums plus one folded value per table.  A round is split
-// into (term, pair) work items rather than pairs, so the late rounds with few
-// pairs still spread over the block.  A second launch sums the partials of
-// all chunks.  The folded vectors (1/2^q of the input) feed the next level.
+// per-round partial sums plus one folded value per table.  A general term
+// list is split into (term, pair) work items, so the late rounds with few
+// pairs still spread over the block; the term shapes of the reference's
+// callers (eq times a linear combination, the logUp layer) have dedicated
+// pair-at-a-time evaluations with fewer products.  A second launch sums the
+// partials of all chunks.  The folded vectors (1/2^q of the input) feed the next level.
 // The input tables are read from HBM exactly once.
 //
 // f_j(k) for k = 0..d is formed incrementally (f0, f0 + (f1 - f0), ...), the
 // same field elements as k f1 - (k - 1) f0, and the last factor of every
 // term product is multiplied into an exact Acc160 sum (one reduction per
 // round and evaluation point instead of one per product).
+#include <atomic>
+
 #include "../../include/zkie2.h"
 #include "common.cuh"
 #include "gl64.cuh"
@@ -39,11 +43,26 @@ constexpr int kVMaxQ = 10;
 constexpr int kVQCap = 8;  // rounds per launch: 2^8 positions per 128-thread block
 constexpr uint32_t kVSmemBytes = 46 * 1024;  // dynamic part; the static reduction buffer rides on top
 
+// Term shapes with a dedicated evaluation, classified on the host:
+//  kShapeGeneric  any term list; (term, pair) work items.
+//  kShapeEqLinear degree 2, every term is [e, j] or [e] for one common table
+//                 e (Projection affine, projection.rs:74-83): g = f_e * I with
+//                 I = sum_i c_i f_{j_i} linear in k, so I is summed at k = 0, 1
+//                 only and g(2) = (2 e1 - e0)(2 I1 - I0).
+//  kShapeFraction the five terms of a logUp layer (logup_gkr.rs:19-28) over
+//                 [eq, nn, nd, nl, nh, dl, dh]: g = eq * I with
+//                 I = nn + c nd - nl dh - nh dl - c dl dh quadratic in k, so
+//                 I(3) = I(0) + 3 (I(2) - I(1)).
+// Both special shapes evaluate one pair per work item with every table's
+// pair read once; the values equal those of the term-by-term formula.
+enum : uint32_t { kShapeGeneric = 0, kShapeEqLinear = 1, kShapeFraction = 2 };
+
 struct VTerms {
     uint64_t coeff[kVMaxTerms];
     uint8_t off[kVMaxTerms + 1];
     uint8_t idx[kVMaxFactors];
-    uint32_t n_terms, n_mles, deg;
+    int8_t other[kVMaxTerms];  // kShapeEqLinear: the second table of term i, -1 for [e] alone
+    uint32_t n_terms, n_mles, deg, shape, common;
 };
 struct VIn {
     const uint64_t* p[kVMaxMles];
@@ -58,6 +77,45 @@ __device__ __forceinline__ uint64_t v_warp_sum(uint64_t v) {
     return v;
 }
 
+// Warp sums of V values at once (V a power of two <= 32): log2 V butterfly
+// steps each hand half of the remaining values to the partner lane, the
+// remaining steps reduce one value.  Afterwards lane k * (32 / V) holds the
+// total of value k.  V - 1 + 5 - log2 V shuffle-adds instead of 5 V.
+template <int V>
+__device__ __forceinline__ uint64_t warp_multi_sum(uint64_t (&v)[V]) {
+    const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+    for (int st = 0; st < 5; st++) {
+        const int n = 16 >> st, h = (V >> st) / 2;  // values held before this step: V >> st
+        if (h >= 1) {
+            const bool upper = (lane & n) != 0;
+#pragma unroll
+            for (int i = 0; i < h; i++) {
+                const uint64_t send = upper ? v[i] : v[i + h];
+                const uint64_t keep = upper ? v[i + h] : v[i];
+                v[i] = gl_add(keep, __shfl_xor_sync(0xffffffffu, send, n));
+            }
+        } else {
+            v[0] = gl_add(v[0], __shfl_xor_sync(0xffffffffu, v[0], n));
+        }
+    }
+    return v[0];
+}
+
+__host__ __device__ constexpr int pow2_ceil(int x) { return x <= 1 ? 1 : 2 * pow2_ceil((x + 1) / 2); }
+
+// I = nn + c nd - nl dh - nh dl - c dl dh (one exact sum per sign)
+__device__ __forceinline__ uint64_t frac_inner(uint64_t c, uint64_t nn, uint64_t nd, uint64_t nl, uint64_t nh,
+                                               uint64_t dl, uint64_t dh) {
+    Acc160 pos = acc160_zero(), neg = acc160_zero();
+    acc160_mac(pos, c, nd);
+    acc160_add(pos, nn);
+    acc160_mac(neg, nl, dh);
+    acc160_mac(neg, nh, dl);
+    acc160_mac(neg, gl_mul(c, dl), dh);
+    return gl_sub(acc160_reduce(pos), acc160_reduce(neg));
+}
+
 // One block per chunk of 2^q positions.  Shared memory: every table's chunk
 // (n_mles x 2^q) followed by a half-size buffer (n_mles x 2^(q-1)).
 // partials[(chunk * q + round) * (d + 1) + k]; out[j * out_stride + chunk] is
@@ -66,18 +124,23 @@ __device__ __forceinline__ uint64_t v_warp_sum(uint64_t v) {
 // instantiated for 2, 4 and 8 so the per-factor loops unroll to what the
 // terms need.  The term tables are copied to shared memory once per block,
 // where the per-pair lookups by term and factor index are cheap.
-template <int kF>
+template <int kF, uint32_t kShape>
 __global__ void __launch_bounds__(kVThreads)
     k_virtual_chunk(VIn in, uint32_t q, VTerms T, VChal ch, uint64_t* __restrict__ partials,
                     uint64_t* __restrict__ out, uint64_t out_stride) {
+    constexpr int kV = pow2_ceil(kF + 1);
     extern __shared__ __align__(16) uint64_t sm[];
     __shared__ uint64_t red[2][kVThreads / 32][kF + 1];
     __shared__ uint64_t s_coeff[kVMaxTerms];
     __shared__ uint32_t s_off[kVMaxTerms + 1], s_idx[kVMaxFactors];
+    __shared__ int32_t s_other[kVMaxTerms];
     __shared__ uint64_t s_ch[kVMaxQ];
     const uint32_t nm = T.n_mles, deg = T.deg, nt = T.n_terms, Q = 1u << q;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid < kVMaxTerms) s_coeff[tid] = T.coeff[tid];
+    if (tid < kVMaxTerms) {
+        s_coeff[tid] = T.coeff[tid];
+        s_other[tid] = T.other[tid];
+    }
     if (tid <= kVMaxTerms) s_off[tid] = T.off[tid];
     if (tid < kVMaxFactors) s_idx[tid] = T.idx[tid];
     if (tid < kVMaxQ) s_ch[tid] = ch.r[tid];
@@ -93,47 +156,94 @@ __global__ void __launch_bounds__(kVThreads)
     uint64_t* cur = sm;
     uint64_t* nxt = sm + (size_t)nm * Q;
     uint32_t sc = Q, sn = Q >> 1;
+    const uint32_t e = T.common;
+    const uint64_t fc = T.coeff[3];  // the logUp layer's c
     for (uint32_t rd = 0; rd < q; rd++) {
         const uint32_t lg_pairs = q - 1 - rd, pairs = 1u << lg_pairs;
         const uint64_t r = s_ch[rd];
         Acc160 acc[kF + 1];
 #pragma unroll
         for (int k = 0; k <= kF; k++) acc[k] = acc160_zero();
-        // work items (term ti, pair s), term-major: neighbouring threads take
-        // neighbouring pairs of one term, so their shared-memory reads are
-        // consecutive 16-byte pairs
-        const uint32_t items = nt << lg_pairs;
-        for (uint32_t it = tid; it < items; it += kVThreads) {
-            const uint32_t ti = it >> lg_pairs, s = it & (pairs - 1);
-            const uint32_t o0 = s_off[ti], nf = s_off[ti + 1] - o0;
-            const uint64_t c = s_coeff[ti];
-            uint64_t fv[kF], dv[kF];
-#pragma unroll
-            for (int f = 0; f < kF; f++) {
-                fv[f] = 1;
-                dv[f] = 0;
-                if ((uint32_t)f < nf) {
-                    const ulonglong2 pr = reinterpret_cast<const ulonglong2*>(cur + s_idx[o0 + f] * sc)[s];
-                    fv[f] = pr.x;
-                    dv[f] = gl_sub(pr.y, pr.x);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k <= kF; k++) {
-                if ((uint32_t)k <= deg) {
-                    // c * prod_{f < nf} f_f(k): all but the last factor reduced,
-                    // the last one multiplied into the exact sum
-                    uint64_t p = c, last = 1;
-#pragma unroll
-                    for (int f = 0; f < kF; f++) {
-                        if ((uint32_t)f + 1 < nf) p = gl_mul(p, fv[f]);
-                        else if ((uint32_t)f + 1 == nf) last = fv[f];
+        auto pair_of = [&](uint32_t j, uint32_t s) { return reinterpret_cast<const ulonglong2*>(cur + j * sc)[s]; };
+        uint32_t items;
+        if (kShape == kShapeEqLinear) {
+            items = pairs;
+            for (uint32_t s = tid; s < pairs; s += kVThreads) {
+                const ulonglong2 ep = pair_of(e, s);
+                Acc160 i0 = acc160_zero(), i1 = acc160_zero();
+                for (uint32_t ti = 0; ti < nt; ti++) {
+                    const int32_t o = s_other[ti];
+                    const uint64_t c = s_coeff[ti];
+                    if (o < 0) {
+                        acc160_add(i0, c);
+                        acc160_add(i1, c);
+                    } else {
+                        const ulonglong2 fp = pair_of((uint32_t)o, s);
+                        acc160_mac(i0, c, fp.x);
+                        acc160_mac(i1, c, fp.y);
                     }
-                    acc160_mac(acc[k], p, last);
-                    if ((uint32_t)k < deg) {
+                }
+                const uint64_t a0 = acc160_reduce(i0), a1 = acc160_reduce(i1);
+                acc160_mac(acc[0], ep.x, a0);
+                acc160_mac(acc[1], ep.y, a1);
+                acc160_mac(acc[2], gl_sub(gl_add(ep.y, ep.y), ep.x), gl_sub(gl_add(a1, a1), a0));
+            }
+        } else if (kShape == kShapeFraction) {
+            items = pairs;
+            for (uint32_t s = tid; s < pairs; s += kVThreads) {
+                const ulonglong2 eq = pair_of(0, s), nn = pair_of(1, s), nd = pair_of(2, s), nl = pair_of(3, s),
+                                 nh = pair_of(4, s), dl = pair_of(5, s), dh = pair_of(6, s);
+                const uint64_t i0 = frac_inner(fc, nn.x, nd.x, nl.x, nh.x, dl.x, dh.x);
+                const uint64_t i1 = frac_inner(fc, nn.y, nd.y, nl.y, nh.y, dl.y, dh.y);
+                // f(2) = f1 + (f1 - f0)
+                auto f2 = [](ulonglong2 v) { return gl_add(v.y, gl_sub(v.y, v.x)); };
+                const uint64_t i2 = frac_inner(fc, f2(nn), f2(nd), f2(nl), f2(nh), f2(dl), f2(dh));
+                const uint64_t d21 = gl_sub(i2, i1);
+                const uint64_t i3 = gl_add(i0, gl_add(gl_add(d21, d21), d21));
+                const uint64_t de = gl_sub(eq.y, eq.x);
+                const uint64_t e2 = gl_add(eq.y, de);
+                acc160_mac(acc[0], eq.x, i0);
+                acc160_mac(acc[1], eq.y, i1);
+                acc160_mac(acc[2], e2, i2);
+                acc160_mac(acc[3], gl_add(e2, de), i3);
+            }
+        } else {
+            // work items (term ti, pair s), term-major: neighbouring threads take
+            // neighbouring pairs of one term, so their shared-memory reads are
+            // consecutive 16-byte pairs
+            items = nt << lg_pairs;
+            for (uint32_t it = tid; it < items; it += kVThreads) {
+                const uint32_t ti = it >> lg_pairs, s = it & (pairs - 1);
+                const uint32_t o0 = s_off[ti], nf = s_off[ti + 1] - o0;
+                const uint64_t c = s_coeff[ti];
+                uint64_t fv[kF], dv[kF];
 #pragma unroll
-                        for (int f = 0; f < kF; f++)
-                            if ((uint32_t)f < nf) fv[f] = gl_add(fv[f], dv[f]);
+                for (int f = 0; f < kF; f++) {
+                    fv[f] = 1;
+                    dv[f] = 0;
+                    if ((uint32_t)f < nf) {
+                        const ulonglong2 pr = pair_of(s_idx[o0 + f], s);
+                        fv[f] = pr.x;
+                        dv[f] = gl_sub(pr.y, pr.x);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k <= kF; k++) {
+                    if ((uint32_t)k <= deg) {
+                        // c * prod_{f < nf} f_f(k): all but the last factor reduced,
+                        // the last one multiplied into the exact sum
+                        uint64_t p = c, last = 1;
+#pragma unroll
+                        for (int f = 0; f < kF; f++) {
+                            if ((uint32_t)f + 1 < nf) p = gl_mul(p, fv[f]);
+                            else if ((uint32_t)f + 1 == nf) last = fv[f];
+                        }
+                        acc160_mac(acc[k], p, last);
+                        if ((uint32_t)k < deg) {
+#pragma unroll
+                            for (int f = 0; f < kF; f++)
+                                if ((uint32_t)f < nf) fv[f] = gl_add(fv[f], dv[f]);
+                        }
                     }
                 }
             }
@@ -142,17 +252,16 @@ __global__ void __launch_bounds__(kVThreads)
         const uint32_t fitems = nm << lg_pairs;
         for (uint32_t it = tid; it < fitems; it += kVThreads) {
             const uint32_t j = it >> lg_pairs, s = it & (pairs - 1);
-            const ulonglong2 pr = reinterpret_cast<const ulonglong2*>(cur + j * sc)[s];
+            const ulonglong2 pr = pair_of(j, s);
             nxt[j * sn + s] = gl_add(pr.x, gl_mul(r, gl_sub(pr.y, pr.x)));
         }
         if (warp * 32 < items) {  // warp-uniform: warps past the last item hold zeros
+            uint64_t v[kV];
 #pragma unroll
-            for (int k = 0; k <= kF; k++) {
-                if ((uint32_t)k <= deg) {
-                    const uint64_t v = v_warp_sum(acc160_reduce(acc[k]));
-                    if (lane == 0) red[rd & 1][warp][k] = v;
-                }
-            }
+            for (int k = 0; k < kV; k++) v[k] = (k <= kF && (uint32_t)k <= deg) ? acc160_reduce(acc[k < kF + 1 ? k : 0]) : 0;
+            const uint64_t tot = warp_multi_sum<kV>(v);
+            const uint32_t k = lane / (32 / kV);
+            if (lane % (32 / kV) == 0 && k <= deg) red[rd & 1][warp][k] = tot;
         }
         __syncthreads();
         if (tid <= deg) {
@@ -188,6 +297,31 @@ __global__ void k_virtual_reduce(const uint64_t* __restrict__ partials, uint64_t
     }
 }
 
+// First stage of the round sums for many chunks: block b sums a contiguous
+// run of chunks for every (round, k) slot (S = q (d + 1) slots per chunk,
+// consecutive threads reading consecutive slots) and writes one row of S
+// sums in the partials layout, so k_virtual_reduce finishes over the blocks.
+constexpr uint32_t kVRedBlocks = 296;
+constexpr uint32_t kVRedThreads = 256;
+constexpr uint64_t kVRedMinChunks = 2048;
+__global__ void __launch_bounds__(kVRedThreads)
+    k_virtual_reduce_blocks(const uint64_t* __restrict__ partials, uint64_t G, uint32_t S,
+                            uint64_t* __restrict__ block_out) {
+    __shared__ uint64_t red[kVRedThreads];
+    const uint32_t t = threadIdx.x, groups = kVRedThreads / S, slot = t % S, grp = t / S;
+    const uint64_t per = (G + gridDim.x - 1) / gridDim.x;
+    const uint64_t c0 = (uint64_t)blockIdx.x * per, c1 = c0 + per < G ? c0 + per : G;
+    uint64_t v = 0;
+    if (grp < groups)
+        for (uint64_t c = c0 + grp; c < c1; c += groups) v = gl_add(v, __ldg(partials + c * S + slot));
+    red[t] = v;
+    __syncthreads();
+    if (t < S) {
+        for (uint32_t g = 1; g < groups; g++) v = gl_add(v, red[t + g * S]);
+        block_out[(uint64_t)blockIdx.x * S + t] = v;
+    }
+}
+
 __global__ void k_virtual_t0(VIn in, uint32_t nm, uint64_t* __restrict__ out) {
     const uint32_t j = threadIdx.x;
     if (j < nm) out[j] = gl_canon(in.p[j][0]);
@@ -214,11 +348,79 @@ VPlan v_plan(uint32_t nm, uint32_t t) {
     p.q1 = t < qm ? t : qm;
     p.g1 = 1ull << (t - p.q1);
     // two folded buffers (nm x g1, 16-byte aligned) + the first level's partials
-    p.elems = 2 * ((nm * p.g1 + 1) & ~1ull) + p.g1 * (p.q1 ? p.q1 : 1) * (kVMaxDeg + 1) + 8;
+    // + the first reduce stage's block sums
+    p.elems = 2 * ((nm * p.g1 + 1) & ~1ull) + p.g1 * (p.q1 ? p.q1 : 1) * (kVMaxDeg + 1) + 8 +
+              (uint64_t)kVRedBlocks * kVMaxQ * (kVMaxDeg + 1);
     return p;
 }
 
 }  // namespace
+
+// Launch of one chunk-kernel instantiation; the first launch on each device
+// asks for the largest shared-memory carveout (more resident blocks: a block
+// stages 12 bytes per table and position, e.g. 21 KB for seven tables).
+template <int kF, uint32_t kShape>
+int v_launch(unsigned G, size_t smem, cudaStream_t s, const VIn& in, uint32_t q, const VTerms& T, const VChal& ch,
+             uint64_t* partials, uint64_t* out, uint64_t out_stride) {
+    static std::atomic<bool> carved[kMaxDevices];
+    const int d = current_device();
+    if (d >= 0 && d < kMaxDevices && !carved[d].load(std::memory_order_relaxed)) {
+        ZK_TRY(cudaFuncSetAttribute(k_virtual_chunk<kF, kShape>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    (int)cudaSharedmemCarveoutMaxShared));
+        carved[d].store(true, std::memory_order_relaxed);
+    }
+    k_virtual_chunk<kF, kShape><<<G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+// Picks the term shape's evaluation (see kShapeGeneric ...).  T's
+// coefficients are canonical.
+void v_classify(VTerms& T) {
+    T.shape = kShapeGeneric;
+    T.common = 0;
+    for (int i = 0; i < kVMaxTerms; i++) T.other[i] = -1;
+    const uint32_t nt = T.n_terms;
+    // logUp layer: [eq, nn, nd, nl, nh, dl, dh] with terms 1*[0,1], -1*[0,3,6],
+    // -1*[0,4,5], c*[0,2], -c*[0,5,6]
+    static const uint8_t kFracOff[6] = {0, 2, 5, 8, 10, 13};
+    static const uint8_t kFracIdx[13] = {0, 1, 0, 3, 6, 0, 4, 5, 0, 2, 0, 5, 6};
+    if (T.n_mles == 7 && nt == 5 && T.deg == 3) {
+        bool same = true;
+        for (int i = 0; i < 6; i++) same = same && T.off[i] == kFracOff[i];
+        for (int i = 0; same && i < 13; i++) same = same && T.idx[i] == kFracIdx[i];
+        const uint64_t c = T.coeff[3];
+        if (same && T.coeff[0] == 1 && T.coeff[1] == GL_P - 1 && T.coeff[2] == GL_P - 1 &&
+            T.coeff[4] == (c ? GL_P - c : 0)) {
+            T.shape = kShapeFraction;
+            return;
+        }
+    }
+    // f_e times a linear combination: every term [e, j], [j, e] or [e]
+    if (T.deg != 2 || nt == 0) return;
+    const uint32_t o0 = T.off[0], n0 = T.off[1] - o0;
+    for (uint32_t cand = 0; cand < n0; cand++) {
+        const uint32_t e = T.idx[o0 + cand];
+        bool ok = true;
+        for (uint32_t i = 0; ok && i < nt; i++) {
+            const uint32_t o = T.off[i], nf = T.off[i + 1] - o;
+            if (nf == 1 && T.idx[o] == e)
+                T.other[i] = -1;
+            else if (nf == 2 && T.idx[o] == e)
+                T.other[i] = (int8_t)T.idx[o + 1];
+            else if (nf == 2 && T.idx[o + 1] == e)
+                T.other[i] = (int8_t)T.idx[o];
+            else
+                ok = false;
+        }
+        if (ok) {
+            T.shape = kShapeEqLinear;
+            T.common = e;
+            return;
+        }
+    }
+    for (int i = 0; i < kVMaxTerms; i++) T.other[i] = -1;
+}
 
 // All t rounds on the device; rounds (t x (d+1)) and finals (n_mles) go to
 // device memory.
@@ -236,6 +438,7 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
     const uint64_t bufsz = (nm * plan.g1 + 1) & ~1ull;
     uint64_t* buf[2] = {d_scratch, d_scratch + bufsz};
     uint64_t* partials = d_scratch + 2 * bufsz;
+    uint64_t* block_sums = partials + plan.g1 * (plan.q1 ? plan.q1 : 1) * (kVMaxDeg + 1) + 8;
     uint32_t done = 0, which = 0;
     while (done < t) {
         const uint32_t rem = t - done;
@@ -248,14 +451,27 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
         uint64_t* out = last ? d_finals : buf[which];
         const uint64_t out_stride = last ? 1 : G;
         const size_t smem = ((size_t)12 * nm) << q;  // nm x (2^q + 2^(q-1)) u64
-        if (T.deg <= 2)
-            k_virtual_chunk<2><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+        int rc;
+        if (T.shape == kShapeEqLinear)
+            rc = v_launch<2, kShapeEqLinear>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+        else if (T.shape == kShapeFraction)
+            rc = v_launch<3, kShapeFraction>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+        else if (T.deg <= 2)
+            rc = v_launch<2, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
         else if (T.deg <= 4)
-            k_virtual_chunk<4><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<4, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
         else
-            k_virtual_chunk<8><<<(unsigned)G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<8, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+        if (rc) return rc;
         ZK_LAUNCH_CHECK();
-        k_virtual_reduce<<<q * (T.deg + 1), kVThreads, 0, s>>>(partials, G, q, T.deg, d_rounds + (uint64_t)done * (T.deg + 1));
+        uint64_t* rounds = d_rounds + (uint64_t)done * (T.deg + 1);
+        if (G >= kVRedMinChunks) {
+            k_virtual_reduce_blocks<<<kVRedBlocks, kVRedThreads, 0, s>>>(partials, G, q * (T.deg + 1), block_sums);
+            ZK_LAUNCH_CHECK();
+            k_virtual_reduce<<<q * (T.deg + 1), kVThreads, 0, s>>>(block_sums, kVRedBlocks, q, T.deg, rounds);
+        } else {
+            k_virtual_reduce<<<q * (T.deg + 1), kVThreads, 0, s>>>(partials, G, q, T.deg, rounds);
+        }
         ZK_LAUNCH_CHECK();
         if (!last) {
             for (uint32_t j = 0; j < nm; j++) in.p[j] = out + j * G;
@@ -266,23 +482,20 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
     return 0;
 }
 
-}  // namespace zk
-
-using namespace zk;
-
-extern "C" {
-
-// plan scratch, then the round messages (t x at most kVMaxDeg + 1) and the finals
-uint64_t zkie2_virtual_scratch_elems(uint32_t n_mles, uint32_t t) {
+uint64_t virtual_plan_elems(uint32_t n_mles, uint32_t t) {
     if (n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40) return 0;
-    return v_plan(n_mles, t).elems + (uint64_t)t * (kVMaxDeg + 1) + kVMaxMles;
+    return v_plan(n_mles, t).elems;
 }
 
-int zkie2_virtual_prove(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
-                        const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
-                        uint64_t* h_rounds, uint64_t* h_finals, uint64_t* d_scratch, cudaStream_t stream) {
-    if (!d_mles || !h_finals || !d_scratch || n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40 ||
-        n_terms > (uint32_t)kVMaxTerms || (n_terms && (!coeffs || !idx_off)) || (t && (!h_ch || !h_rounds)))
+// Term-list validation plus all launches, no synchronization: the round
+// messages (t x (d + 1), d = the largest term) land in d_rounds and the
+// finals (n_mles) in d_finals, both device memory outside d_scratch.
+int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
+                    const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
+                    uint64_t* d_rounds, uint64_t* d_finals, uint32_t* deg_out, uint64_t* d_scratch,
+                    cudaStream_t stream) {
+    if (!d_mles || !d_finals || !d_scratch || n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40 ||
+        n_terms > (uint32_t)kVMaxTerms || (n_terms && (!coeffs || !idx_off)) || (t && (!h_ch || !d_rounds)))
         return (int)cudaErrorInvalidValue;
     VTerms T{};
     T.n_terms = n_terms;
@@ -306,12 +519,36 @@ int zkie2_virtual_prove(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t
         }
     }
     T.deg = deg;
+    v_classify(T);
     for (uint32_t j = 0; j < n_mles; j++)
         if (!d_mles[j]) return (int)cudaErrorInvalidValue;
+    if (deg_out) *deg_out = deg;
+    return virtual_dev(d_mles, n_mles, t, T, h_ch, d_rounds, d_finals, d_scratch, stream);
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+// plan scratch, then the round messages (t x at most kVMaxDeg + 1) and the finals
+uint64_t zkie2_virtual_scratch_elems(uint32_t n_mles, uint32_t t) {
+    if (n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40) return 0;
+    return v_plan(n_mles, t).elems + (uint64_t)t * (kVMaxDeg + 1) + kVMaxMles;
+}
+
+int zkie2_virtual_prove(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
+                        const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
+                        uint64_t* h_rounds, uint64_t* h_finals, uint64_t* d_scratch, cudaStream_t stream) {
+    if (!h_finals || !d_scratch || n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40 || (t && !h_rounds))
+        return (int)cudaErrorInvalidValue;
     // the round messages and the finals live behind the plan's scratch
     uint64_t* d_rounds = d_scratch + v_plan(n_mles, t).elems;
-    uint64_t* d_finals = d_rounds + (uint64_t)t * (deg + 1);
-    int rc = virtual_dev(d_mles, n_mles, t, T, h_ch, d_rounds, d_finals, d_scratch, stream);
+    uint64_t* d_finals = d_rounds + (uint64_t)t * (kVMaxDeg + 1);
+    uint32_t deg = 0;
+    int rc = virtual_enqueue(d_mles, n_mles, t, coeffs, idx_off, idx, n_terms, h_ch, d_rounds, d_finals, &deg,
+                             d_scratch, stream);
     if (rc) return rc;
     if (t) ZK_TRY(cudaMemcpyAsync(h_rounds, d_rounds, 8ull * t * (deg + 1), cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaMemcpyAsync(h_finals, d_finals, 8ull * n_mles, cudaMemcpyDeviceToHost, stream));

@@ -5,6 +5,7 @@
     python -m zkie_b200.perfcases matmul --m 512 --k 1024 --n 4096
     python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
     python -m zkie_b200.perfcases virtual --log-size 21
+    python -m zkie_b200.perfcases logup --log-size 24
     python -m zkie_b200.perfcases sop --log-size 20 --polys 4
     python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
     python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
@@ -138,6 +139,43 @@ def case_virtual(a):
             "gbs": (48 << t) / (ms / 1e3) / 1e9}
 
 
+def case_logup(a):
+    """The logUp fraction tree (prove_fractional_with_challenges) over 2^log_size
+    fractions, and the merged lookup columns of 2^(log_size-1) samples into a
+    2^(log_size-1) table.  Algorithmic bytes of the tree: every layer of N_l
+    fractions reads num and den once and writes the N_l / 2 next fractions
+    (24 N_l bytes), about 48 N over all layers."""
+    lg = a.log_size
+    n = 1 << lg
+    num, den = _rand(n, 40), _rand(n, 41)
+    full_r = np.arange(1, lg + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15 % P)
+    cs = np.arange(1, lg + 1, dtype=np.uint64) * np.uint64(0x5851F42D4C957F2D % P)
+    rounds = np.zeros(max(2 * lg * (lg - 1), 1), dtype=np.uint64)
+    finals = np.zeros(max(7 * lg, 1), dtype=np.uint64)
+    fnd = np.zeros(2, dtype=np.uint64)
+    scr = torch.empty(lib.zkie2_fractional_scratch_elems(lg), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        check(lib.zkie2_fractional_prove(num.data_ptr(), den.data_ptr(), lg, _p(full_r), _p(cs), _p(rounds),
+                                         _p(finals), _p(fnd), scr.data_ptr(), st), "fractional")
+    ms = _time(run, a.iters)
+    half = n // 2
+    x = torch.from_numpy(np.random.default_rng(43).integers(0, half, size=half).astype(np.uint32)).cuda()
+    table, y = _rand(half, 42), _rand(half, 44)
+    onum = torch.empty(n, dtype=torch.uint64, device="cuda")
+    oden = torch.empty(n, dtype=torch.uint64, device="cuda")
+    lscr = torch.empty(lib.zkie2_lookup_scratch_elems(half), dtype=torch.uint64, device="cuda")
+
+    def cols():
+        check(lib.zkie2_lookup_num_den(x.data_ptr(), y.data_ptr(), half, table.data_ptr(), None, half, 0, 3, 5,
+                                       onum.data_ptr(), oden.data_ptr(), lscr.data_ptr(), st), "lookup columns")
+    ms_cols = _time(cols, a.iters)
+    alg = 48 * n
+    return {"case": "logup_fraction_tree", "log_size": lg, "ms": ms, "bytes": alg, "gbs": alg / (ms / 1e3) / 1e9,
+            "lookup_columns_ms": ms_cols}
+
+
 def case_sop(a):
     """prove_sum_of_products over `polys` table pairs of 2^log_size."""
     t, n = a.log_size, a.polys
@@ -248,7 +286,8 @@ def case_commit(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep"])
+    ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
+                                         "logup"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -262,7 +301,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "sop": case_sop, "shard": case_shard, "split": case_split,
+           "virtual": case_virtual, "logup": case_logup, "sop": case_sop, "shard": case_shard, "split": case_split,
            "sweep": case_sweep}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
