@@ -244,6 +244,18 @@ int zkie2_virtual_prove(const uint64_t *const *d_mles, uint32_t n_mles, uint32_t
                         const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms, const uint64_t *h_ch,
                         uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch, zkie_stream_t stream);
 
+/* PoW grinding of the WHIR prover (challenger.grind, p3-whir src/pcs/prover/mod.rs:240-245,
+ * 355-358) on the transcript's DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>
+ * (pcs/whir.rs:42): the smallest w < p with check_witness(bits, w), i.e. observe(w) then
+ * sample_bits(bits) == 0, for the challenger whose sponge state is h_sponge (16 values)
+ * with len < 8 inputs h_input buffered.  The reference searches with find_any and keeps
+ * any valid witness; every valid witness verifies.  The caller then replays
+ * check_witness on its own challenger (one permutation), as the reference does.
+ * Batches of zkie2_grind_batch(bits) candidates per launch.  Synchronous. */
+uint64_t zkie2_grind_batch(uint32_t bits);
+int zkie2_grind(const uint64_t *h_sponge, const uint64_t *h_input, uint32_t len, uint32_t bits,
+                uint64_t *h_witness, zkie_stream_t stream);
+
 /* ---- logUp GKR fraction tree (common/logup_gkr.rs) ------------------------------------ */
 /* prove_fractional_with_challenges (logup_gkr.rs:29-69) over device tables
  * num, den of 2^lg_n values (read only), with lg_n challenges full_r and cs

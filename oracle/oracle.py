@@ -91,6 +91,8 @@ def lib():
             "orc_op_matmul_prove": (None, [_pu64, _pu64, _pu64, _u64, _u64, _u64, C.POINTER(Challenger),
                                            _pu64, _pu64, _pu64, _pu64, _pu64, _pu64, _pu64]),
             "orc_shard_dag_child": (None, [_pu64, _u32, _u64, _u64, C.POINTER(Transcript)]),
+            "orc_check_witness": (C.c_int, [C.POINTER(P2Consts), _pu64, _pu64, _u32, _u32, _u64]),
+            "orc_grind": (_u64, [C.POINTER(P2Consts), _pu64, _pu64, _u32, _u32, _u64, _u64]),
             "orc_fractional_prove": (None, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _pu64, _pu64]),
             "orc_fractional_verify": (C.c_int, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _u64, _u64, _u64]),
             "orc_fractional_chain_core": (C.c_int, [_u32, _pu64, _pu64, _pu64, _pu64]),
@@ -521,3 +523,16 @@ def lookup_num_den(x, y, table, m, mode, alpha, beta):
                                    ptr(tb) if tb.size else None, ptr(mm) if mm.size else None, tb.size, mode,
                                    int(alpha) % P, int(beta) % P, ptr(num), ptr(den))
     return (num, den) if got else None
+
+
+# ---- PoW grinding (DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>) --------------------
+def check_witness(consts, sponge, inputs, bits, w):
+    sp, inp = u64(sponge), u64(inputs if len(inputs) else [0])
+    return bool(lib().orc_check_witness(C.byref(consts), ptr(sp), ptr(inp), len(inputs), bits, w))
+
+
+def grind(consts, sponge, inputs, bits, start=0, limit=1 << 40):
+    """Smallest valid witness >= start (None if none below start + limit)."""
+    sp, inp = u64(sponge), u64(inputs if len(inputs) else [0])
+    w = lib().orc_grind(C.byref(consts), ptr(sp), ptr(inp), len(inputs), bits, start, limit)
+    return None if w == 0xFFFFFFFFFFFFFFFF else int(w)

@@ -1149,3 +1149,34 @@ uint64_t orc_lookup_num_den(const uint32_t *x, const uint64_t *y, uint64_t n, co
     }
     return total;
 }
+
+/* ============================================================================
+ * PoW grinding on DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>
+ * (pcs/whir.rs:42; grind called at p3-whir src/pcs/prover/mod.rs:240-245).
+ * p3-challenger 0.7.0 is not vendored; restated from its published duplex
+ * sponge: observe(v) clears the outputs and buffers v (a full rate of 8
+ * inputs duplexes at once); sample() duplexes when inputs are buffered or no
+ * output is left and pops the last output; a duplexing overwrites lanes
+ * [0, len) with the buffered inputs, permutes, and keeps lanes [0, 8) as
+ * outputs; sample_bits(b) = canonical(sample()) & (2^b - 1);
+ * check_witness(b, w) = observe(w); sample_bits(b) == 0.
+ * ========================================================================== */
+int orc_check_witness(const orc_p2_consts *c, const uint64_t sponge[16], const uint64_t *input, uint32_t len,
+                      uint32_t bits, uint64_t w)
+{
+    uint64_t st[16];
+    for (int i = 0; i < 16; i++) st[i] = canon(sponge[i]);
+    for (uint32_t i = 0; i < len; i++) st[i] = canon(input[i]);
+    st[len] = canon(w);
+    orc_p2_permute(c, st);
+    return (canon(st[7]) & ((1ULL << bits) - 1)) == 0;
+}
+
+/* The smallest valid witness in [start, start + limit), or UINT64_MAX. */
+uint64_t orc_grind(const orc_p2_consts *c, const uint64_t sponge[16], const uint64_t *input, uint32_t len,
+                   uint32_t bits, uint64_t start, uint64_t limit)
+{
+    for (uint64_t w = start; w - start < limit && w < ORC_P; w++)
+        if (orc_check_witness(c, sponge, input, len, bits, w)) return w;
+    return ~0ULL;
+}

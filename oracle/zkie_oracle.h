@@ -166,6 +166,14 @@ void orc_op_matmul_prove(const uint64_t *a, const uint64_t *b, const uint64_t *c
 void orc_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_per_shard,
                          uint64_t shard_index, orc_transcript *child);
 
+/* PoW grinding on DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>: validity of a
+ * witness for the challenger (sponge state, len < 8 buffered inputs), and the smallest
+ * valid witness of [start, start + limit) (UINT64_MAX if none). */
+int orc_check_witness(const orc_p2_consts *c, const uint64_t sponge[16], const uint64_t *input, uint32_t len,
+                      uint32_t bits, uint64_t w);
+uint64_t orc_grind(const orc_p2_consts *c, const uint64_t sponge[16], const uint64_t *input, uint32_t len,
+                   uint32_t bits, uint64_t start, uint64_t limit);
+
 /* logUp GKR fraction tree (crates/zkie-core/src/common/logup_gkr.rs:29-164).
  * rounds: layer l's lg - l - 1 rounds of 4 evaluations, concatenated;
  * finals: 7 evaluations per layer. */

@@ -118,3 +118,38 @@ def sumcheck_prove(f, h, ch):
         f = [(f[2 * s] + r * (f[2 * s + 1] - f[2 * s])) % P for s in range(len(f) // 2)]
         h = [(h[2 * s] + r * (h[2 * s + 1] - h[2 * s])) % P for s in range(len(h) // 2)]
     return rounds, f[0], h[0]
+
+
+class DuplexChallenger:
+    """DuplexChallenger<F, Perm, 16, 8> restated as a stateful object (the
+    p3-challenger duplex sponge the WHIR transcript uses, pcs/whir.rs:42)."""
+
+    def __init__(self, cp, state=None):
+        self.cp = cp
+        self.state = [x % P for x in (state if state is not None else [0] * 16)]
+        self.inp, self.out = [], []
+
+    def duplexing(self):
+        for i, v in enumerate(self.inp):
+            self.state[i] = v
+        self.inp = []
+        self.state = permute(self.state, *self.cp)
+        self.out = self.state[:8]
+
+    def observe(self, v):
+        self.out = []
+        self.inp.append(v % P)
+        if len(self.inp) == 8:
+            self.duplexing()
+
+    def sample(self):
+        if self.inp or not self.out:
+            self.duplexing()
+        return self.out.pop()
+
+    def sample_bits(self, bits):
+        return self.sample() & ((1 << bits) - 1)
+
+    def check_witness(self, bits, w):
+        self.observe(w)
+        return self.sample_bits(bits) == 0

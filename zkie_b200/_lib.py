@@ -91,6 +91,8 @@ SIGNATURES = {
     "zkie2_sum_of_products_prove": (i64, [vp, vp, u32, u32, pu64, pu64, pu64, vp, vp]),
     "zkie2_virtual_scratch_elems": (u64, [u32, u32]),
     "zkie2_virtual_prove": (i64, [C.POINTER(vp), u32, u32, pu64, pu32, pu32, u32, pu64, pu64, pu64, vp, vp]),
+    "zkie2_grind_batch": (u64, [u32]),
+    "zkie2_grind": (i64, [pu64, pu64, u32, u32, pu64, vp]),
     "zkie2_fractional_scratch_elems": (u64, [u32]),
     "zkie2_fractional_prove": (i64, [vp, vp, u32, pu64, pu64, pu64, pu64, pu64, vp, vp]),
     "zkie2_lookup_len": (u64, [u64, u64, u32]),

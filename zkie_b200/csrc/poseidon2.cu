@@ -245,6 +245,35 @@ __global__ void k_digest_interleave(const uint64_t* __restrict__ in, uint64_t G,
     out[idx] = __ldg(in + ((r * n + c) << 3) + (idx & 7));
 }
 
+// PoW grinding (challenger.grind in the WHIR prover, p3-whir
+// src/pcs/prover/mod.rs:240-245, 355-358) on the transcript's
+// DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8> (pcs/whir.rs:42).
+// check_witness(bits, w) = observe(w); sample_bits(bits) == 0.  With len < 8
+// inputs already buffered, observing w and sampling is one duplexing: the
+// sponge lanes [0, len) take the buffered inputs, lane len takes w, the other
+// lanes keep the sponge state, the state is permuted, and sample() pops the
+// last of the eight outputs, lane 7.  `b` is that state with lane len to be
+// replaced; w is valid when the canonical lane 7 has its low `bits` bits
+// clear.  The smallest valid w of [start, start + count) lands in *found
+// (atomicMin); a thread stops once a smaller witness is known.
+struct GrindBase {
+    uint64_t s[16];
+};
+__global__ void __launch_bounds__(kHashThreads)
+    k_grind(GrindBase b, uint32_t len, uint64_t mask, uint64_t start, uint64_t count,
+            unsigned long long* __restrict__ found) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const uint64_t w = start + i;
+        if (w >= *reinterpret_cast<volatile unsigned long long*>(found)) break;
+        uint64_t s[16];
+#pragma unroll
+        for (int q = 0; q < 16; q++) s[q] = (uint32_t)q == len ? w : b.s[q];
+        p2_permute(s, c_p2);
+        if ((gl_canon(s[7]) & mask) == 0) atomicMin(found, (unsigned long long)w);
+    }
+}
+
 uint64_t canon_host(uint64_t x) { return x >= GL_P ? x - GL_P : x; }
 
 }  // namespace
@@ -431,6 +460,54 @@ int zkie2_p2_permute(uint64_t* d_states, uint64_t n, uint32_t reps, cudaStream_t
     if (!p2_constants_ready()) return (int)cudaErrorInitializationError;
     k_permute<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, stream>>>(d_states, n, reps);
     ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+uint64_t zkie2_grind_batch(uint32_t bits) {
+    const uint32_t lg = bits + 2 < 16 ? 16 : (bits + 2 > 26 ? 26 : bits + 2);
+    return 1ull << lg;
+}
+
+int zkie2_grind(const uint64_t* h_sponge, const uint64_t* h_input, uint32_t len, uint32_t bits, uint64_t* h_witness,
+                cudaStream_t stream) {
+    if (!h_sponge || !h_witness || len >= 8 || (len && !h_input) || bits >= 63) return (int)cudaErrorInvalidValue;
+    int rc = p2_ensure_default();
+    if (rc) return rc;
+    GrindBase b{};
+    for (int q = 0; q < 16; q++) b.s[q] = gl_canon(h_sponge[q]);
+    for (uint32_t q = 0; q < len; q++) b.s[q] = gl_canon(h_input[q]);
+    const uint64_t mask = (1ull << bits) - 1;
+    unsigned long long* d_found = nullptr;
+    ZK_TRY(cudaMallocAsync((void**)&d_found, 8, stream));
+    // One wave of resident blocks: the grid-stride loop then walks the
+    // candidates in increasing order across all threads at once, so the
+    // search stops close to the smallest witness instead of finishing the
+    // ranges of the first resident blocks while later blocks wait.
+    int dev = 0, sms = 0, per_sm = 0;
+    ZK_TRY(cudaGetDevice(&dev));
+    ZK_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    ZK_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_grind, kHashThreads, 0));
+    const uint64_t resident = (uint64_t)(sms > 0 ? sms : 1) * (uint64_t)(per_sm > 0 ? per_sm : 1);
+    const uint64_t batch = zkie2_grind_batch(bits);
+    const uint64_t none = ~0ull;
+    uint64_t got = none;
+    // batches in increasing order: the first batch holding a witness yields the smallest one
+    for (uint64_t start = 0; !rc && got == none && start < GL_P; start += batch) {
+        const uint64_t count = GL_P - start < batch ? GL_P - start : batch;
+        rc = (int)cudaMemcpyAsync(d_found, &none, 8, cudaMemcpyHostToDevice, stream);
+        if (!rc) {
+            const uint64_t blocks = ceil_div(count, kHashThreads);
+            k_grind<<<(unsigned)(blocks < resident ? blocks : resident), kHashThreads, 0, stream>>>(b, len, mask, start,
+                                                                                            count, d_found);
+            rc = (int)cudaGetLastError();
+        }
+        if (!rc) rc = (int)cudaMemcpyAsync(&got, d_found, 8, cudaMemcpyDeviceToHost, stream);
+        if (!rc) rc = (int)cudaStreamSynchronize(stream);
+    }
+    cudaFreeAsync(d_found, stream);
+    if (rc) return rc;
+    if (got == none) return (int)cudaErrorInvalidValue;  // no witness in the field (not for bits < 63)
+    *h_witness = got;
     return 0;
 }
 

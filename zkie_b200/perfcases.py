@@ -6,6 +6,7 @@
     python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
     python -m zkie_b200.perfcases virtual --log-size 21
     python -m zkie_b200.perfcases logup --log-size 24
+    python -m zkie_b200.perfcases grind --log-size 24
     python -m zkie_b200.perfcases sop --log-size 20 --polys 4
     python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
     python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
@@ -176,6 +177,22 @@ def case_logup(a):
             "lookup_columns_ms": ms_cols}
 
 
+def case_grind(a):
+    """PoW grinding (zkie2_grind) at --log-size bits from a fixed challenger
+    state; the candidate count is data-dependent, so the rate is reported per
+    candidate tried (the smallest witness + 1, one permutation each)."""
+    from .pow import grind
+    sponge = [(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(16)]
+    w = {}
+
+    def run():
+        w["w"] = grind(sponge, [5, 6, 7], a.log_size)
+    ms = _time(run, a.iters)
+    perms = w["w"] + 1
+    return {"case": "grind", "bits": a.log_size, "ms": ms, "witness": w["w"],
+            "gperm_s_tried": perms / (ms / 1e3) / 1e9}
+
+
 def case_sop(a):
     """prove_sum_of_products over `polys` table pairs of 2^log_size."""
     t, n = a.log_size, a.polys
@@ -287,7 +304,7 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup"])
+                                         "logup", "grind"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -301,7 +318,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "logup": case_logup, "sop": case_sop, "shard": case_shard, "split": case_split,
+           "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "sop": case_sop, "shard": case_shard, "split": case_split,
            "sweep": case_sweep}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
