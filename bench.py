@@ -518,6 +518,8 @@ def main():
 
     # ---- MatMul shard prove (inputs resident) ----
     shard = shard_prove_ms(zk, dev) if rank == 0 else None
+    # ---- the next rows: logUp fraction tree and WHIR PoW grinding ----
+    extra = next_rows(want_cpu=rank == 0 and world == 1 and not args.no_cpu) if rank == 0 else None
 
     launches_per_step = ntt_passes(lg) + 1 + (lib.zkie2_merkle_num_layers(H) - 1)
     line = {
@@ -551,6 +553,8 @@ def main():
         line["e2e"] = e2e
     if shard:
         line["shard_prove"] = shard
+    if extra:
+        line.update(extra)
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(w, lg_b)
     if rank == 0:
@@ -559,6 +563,47 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def next_rows(want_cpu, lg_frac=22, grind_bits=24):
+    """The logUp fraction tree (prove_fractional_with_challenges, 2^22
+    fractions, inputs resident) and PoW grinding (24 bits) on the device, each
+    with the CPU oracle port timed beside it on a bounded sample (one thread:
+    a 2^18-fraction tree; a 16-bit grind)."""
+    import types
+
+    from zkie_b200.perfcases import case_grind, case_logup
+    lg = case_logup(types.SimpleNamespace(log_size=lg_frac, iters=5))
+    gr = case_grind(types.SimpleNamespace(log_size=grind_bits, iters=3))
+    out = {
+        "logup": {"config": f"prove_fractional_with_challenges over 2^{lg_frac} fractions (every layer on the device)",
+                  "ms": round(lg["ms"], 4), "value": round((1 << lg_frac) / (lg["ms"] / 1e3) / 1e6, 3),
+                  "unit": "Mfractions/s", "lookup_columns_ms": round(lg["lookup_columns_ms"], 4)},
+        "grind": {"config": f"WHIR PoW grind, {grind_bits} bits, DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>",
+                  "ms": round(gr["ms"], 4), "witness": gr["witness"], "value": round(gr["gperm_s_tried"] * 1e3, 3),
+                  "unit": "M candidates/s"},
+    }
+    if want_cpu:
+        import numpy as np
+
+        from oracle import oracle as orc
+        g = np.random.default_rng(1)
+        n = 1 << 18
+        num, den = g.integers(0, P, size=n, dtype=np.uint64), g.integers(1, P, size=n, dtype=np.uint64)
+        t0 = time.perf_counter()
+        orc.fractional_prove(num, den, list(range(3, 21)), list(range(5, 23)))
+        s_frac = time.perf_counter() - t0
+        out["logup"]["cpu_baseline"] = {"value": round(n / s_frac / 1e6, 4), "unit": "Mfractions/s", "cores": 1,
+                                        "kind": "port", "sample": "2^18-fraction tree, oracle/zkie_oracle.c"}
+        consts = orc.p2_constants(1)
+        sponge = [(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(16)]
+        t0 = time.perf_counter()
+        w = orc.grind(consts, sponge, [5, 6, 7], 16)
+        s_grind = time.perf_counter() - t0
+        out["grind"]["cpu_baseline"] = {"value": round((w + 1) / s_grind / 1e6, 4), "unit": "M candidates/s",
+                                        "cores": 1, "kind": "port",
+                                        "sample": f"16-bit grind from the same state ({w + 1} candidates)"}
+    return out
 
 
 def shard_prove_ms(zk, dev, iters=5):
