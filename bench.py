@@ -522,6 +522,7 @@ def main():
     extra = next_rows(want_cpu=rank == 0 and world == 1 and not args.no_cpu) if rank == 0 else None
 
     launches_per_step = ntt_passes(lg) + 1 + (lib.zkie2_merkle_num_layers(H) - 1)
+    traffic = measured_traffic(lg_l, w, lg_b, world)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
@@ -530,7 +531,8 @@ def main():
         "roofline": {
             "bound": "int", "kernel": f"k_leaf_rows (Poseidon2 leaf sponge, {(w + 7) // 8} permutations per row)",
             "achieved": round(leaf_rate * MULS_PER_PERM / 1e9, 2), "peak": round(mul_peak / 1e9, 2),
-            "unit": "G Goldilocks mul/s", "frac": round(leaf_rate * MULS_PER_PERM / mul_peak, 4), "traffic": None,
+            "unit": "G Goldilocks mul/s", "frac": round(leaf_rate * MULS_PER_PERM / mul_peak, 4),
+            "traffic": traffic["leaf"], "traffic_unit": "DRAM bytes per launch", "traffic_source": traffic["src"],
             "work_per_unit": f"{MULS_PER_PERM} field multiplications per Poseidon2-16 permutation "
                              "(8x16 + 22 S-boxes x^7 at 4 each, 22 diagonal products)",
             "peak_source": "measured live: zkie2_gl_mul_probe, independent register-resident multiply chains",
@@ -541,7 +543,8 @@ def main():
         "roofline_ntt": {
             "bound": "hbm", "kernel": f"k_ntt_pass2 x{ntt_passes(lg)} (register-radix passes, LDE 2^{lg_l} -> 2^{lg})",
             "achieved": round(ntt_gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(ntt_gbs / hbm_peak, 4),
-            "traffic": None, "algorithmic_bytes": ntt_bytes, "peak_source": hbm_src,
+            "traffic": traffic["ntt"], "traffic_unit": "DRAM bytes per LDE (both passes)",
+            "algorithmic_bytes": ntt_bytes, "peak_source": hbm_src,
             "ms_per_step": round(ntt_ms, 4), "share_of_step": round(ntt_ms / ms_per_step, 4),
         },
         "nodes_ms_per_step": round(node_ms, 4),
@@ -563,6 +566,16 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def measured_traffic(lg_l, w, lg_b, world):
+    """dram__bytes_read.sum + dram__bytes_write.sum of the dominant launches,
+    from one single-pass ncu capture of this exact workload (the command is in
+    profiles/traffic__bench_cfg2_256x2^20_b2.md); null for other workloads."""
+    if (lg_l, w, lg_b, world) == (20, 256, 1, 1):
+        return {"leaf": 4309188608 + 131260928, "ntt": 8609186560 + 4282861056 + 8590646784 + 4268069632,
+                "src": "ncu single-pass capture of this workload, profiles/traffic__bench_cfg2_256x2^20_b2.md"}
+    return {"leaf": None, "ntt": None, "src": None}
 
 
 def next_rows(want_cpu, lg_frac=22, grind_bits=24):
