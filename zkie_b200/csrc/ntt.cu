@@ -70,6 +70,7 @@ struct PassDesc {
     uint32_t logR;    // log2 of the tile lanes R (C * R = tile width)
     uint32_t tw_log;  // 0: no inter-pass twiddle; else multiply by W_{2^tw_log}^(f*k)
     uint32_t canon;   // canonicalize the output
+    uint32_t cgroups;  // k_ntt_pass2: column groups of 2^logC columns (fastest-varying block index)
     // Twiddle source of the reference-facing entry: the caller's top-stage
     // table tab[e] = W_{2^tab_log}^e, e < 2^(tab_log-1).
     const uint64_t* tab;
@@ -314,7 +315,7 @@ __device__ __forceinline__ uint32_t n2_out_base(const Sched& sc, uint32_t gam, u
 template <int L, bool kIn, bool kOut, typename IdxT>
 __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint32_t lgm, uint64_t* data,
                                         const uint64_t* tws, uint32_t q, uint32_t cc, uint32_t logC, bool cok,
-                                        IdxT row_in0, IdxT row_out0, uint64_t f) {
+                                        IdxT row_in0, IdxT row_out0, uint64_t f, uint64_t col0) {
     constexpr int R = 1 << L, G = kN2Elems / R;
     const uint32_t m = d.m, lgs = lgm - L;  // stride M_i / R
     const IdxT w = (IdxT)d.ld;  // row stride
@@ -328,7 +329,7 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
             // rows row_in0 + (base + e 2^lgs) jin of column c0 + cc
             const IdxT rstep = (IdxT)d.jin << lgs;
             const IdxT row_b = row_in0 + (IdxT)base * (IdxT)d.jin;
-            const uint64_t* g = d.in + ((uint64_t)blockIdx.y << logC) + cc + (uint64_t)row_b * w;
+            const uint64_t* g = d.in + col0 + cc + (uint64_t)row_b * w;
             const IdxT gstep = rstep * w;
 #pragma unroll
             for (int e = 0; e < R; e++) {
@@ -366,7 +367,7 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
                 for (int e = 0; e < R; e++) x[e] = gl_canon(x[e]);
             }
             if (cok) {
-                uint64_t* g = d.out + ((uint64_t)blockIdx.y << logC) + cc + (uint64_t)(row_out0 + (IdxT)kb * (IdxT)d.kout) * w;
+                uint64_t* g = d.out + col0 + cc + (uint64_t)(row_out0 + (IdxT)kb * (IdxT)d.kout) * w;
                 const IdxT gstep = ((IdxT)d.kout << (m - L)) * w;
 #pragma unroll
                 for (int e = 0; e < R; e++) g[(IdxT)e * gstep] = x[e];
@@ -381,10 +382,14 @@ __global__ void __launch_bounds__(kN2Threads, 2) k_ntt_pass2(PassDesc d, Sched s
     const uint32_t m = d.m, M = 1u << m, logC = d.logC;
     uint64_t* data = sm;                         // [M][C]
     uint64_t* tws = sm + ((size_t)M << logC);    // [M] powers of W_M
-    const uint64_t f = blockIdx.x % d.F;         // one lane per block
-    const uint64_t s_idx = blockIdx.x / d.F;
+    // Consecutive blocks take consecutive column groups of the same rows, so
+    // the row segments that neighbouring blocks read share DRAM bursts in L2.
+    const uint64_t cg = blockIdx.x % d.cgroups, bx = blockIdx.x / d.cgroups;
+    const uint64_t col0 = cg << logC;
+    const uint64_t f = bx % d.F;                 // one lane per block
+    const uint64_t s_idx = bx / d.F;
     const uint32_t tid = threadIdx.x, cc = tid & ((1u << logC) - 1), q = tid >> logC;
-    const bool cok = ((uint64_t)blockIdx.y << logC) + cc < d.w;
+    const bool cok = col0 + cc < d.w;
     for (uint32_t i = tid; i < M; i += blockDim.x) tws[i] = root_pow<false>(d, m, i);
     __syncthreads();
     const IdxT row_in0 = (IdxT)(f * d.fin + s_idx * d.sin);
@@ -392,21 +397,21 @@ __global__ void __launch_bounds__(kN2Threads, 2) k_ntt_pass2(PassDesc d, Sched s
     // The schedule (make_sched) is 4-bit steps with the remainder last, so
     // only the last step can have a radix below 16.
     if (sc.n == 1) {
-        n2_step<4, true, true, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+        n2_step<4, true, true, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
         return;
     }
-    n2_step<4, true, false, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+    n2_step<4, true, false, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
     __syncthreads();
     if (sc.n == 3) {
-        n2_step<4, false, false, IdxT>(d, sc, sc.lgm[1], data, tws, q, cc, logC, cok, row_in0, row_out0, f);
+        n2_step<4, false, false, IdxT>(d, sc, sc.lgm[1], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
         __syncthreads();
     }
     const uint32_t lgm = sc.n == 3 ? sc.lgm[2] : sc.lgm[1];
     switch (lgm) {
-        case 4: n2_step<4, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-        case 3: n2_step<3, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-        case 2: n2_step<2, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
-        default: n2_step<1, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f); break;
+        case 4: n2_step<4, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
+        case 3: n2_step<3, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
+        case 2: n2_step<2, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
+        default: n2_step<1, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
     }
 }
 
@@ -442,13 +447,14 @@ int run_pass2(PassDesc d, uint64_t S, cudaStream_t s) {
     d.logC = logC;
     d.logR = 0;
     const uint64_t blocks = d.F * S, cblocks = ceil_div(d.w, 1ull << logC);
-    if (blocks > 0x7FFFFFFFull || cblocks > 65535) return (int)cudaErrorInvalidConfiguration;
+    if (blocks * cblocks > 0x7FFFFFFFull) return (int)cudaErrorInvalidConfiguration;
+    d.cgroups = (uint32_t)cblocks;
     const size_t smem = 8ull * ((1ull << m) << logC) + 8ull * (1ull << m);
     if (smem > 48 * 1024)
         ZK_TRY(cudaFuncSetAttribute(k_ntt_pass2<IdxT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const Sched sc = make_sched(m);
     const uint32_t threads = (1u << (m - 4)) << logC;
-    k_ntt_pass2<IdxT><<<dim3((unsigned)blocks, (unsigned)cblocks), threads, smem, s>>>(d, sc);
+    k_ntt_pass2<IdxT><<<(unsigned)(blocks * cblocks), threads, smem, s>>>(d, sc);
     ZK_LAUNCH_CHECK();
     return 0;
 }
