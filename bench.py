@@ -72,10 +72,21 @@ def parse():
 
 
 # ---- CPU side (oracle) --------------------------------------------------------------------
+def host_threads():
+    """Cores this process may run on (torch.distributed.run sets
+    OMP_NUM_THREADS=1 for its ranks; the CPU baseline sets its own count)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_commit_rate(lg_rows, w, lg_b, seed=7):
-    """Oracle LDE + Merkle commit of a (2^lg_rows x w) sample; returns (Melem/s, seconds)."""
+    """Oracle LDE + Merkle commit of a (2^lg_rows x w) sample on every host
+    thread; returns (Melem/s, seconds)."""
     import numpy as np
     from oracle import oracle as orc
+    orc.set_threads(host_threads())
     consts = orc.p2_constants(1)
     m = np.random.default_rng(seed).integers(0, P, size=(1 << lg_rows, w), dtype=np.uint64)
     t0 = time.perf_counter()
@@ -94,9 +105,9 @@ def cpu_sample_rows(w, lg_b, target_s):
 def cpu_baseline(w, lg_b, target_s=10.0):
     lg_rows = cpu_sample_rows(w, lg_b, target_s)
     rate, dt = cpu_commit_rate(lg_rows, w, lg_b)
-    return {"value": round(rate, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+    return {"value": round(rate, 3), "unit": UNIT, "cores": host_threads(), "kind": "port",
             "sample": f"oracle/zkie_oracle.c LDE + Merkle of {w} polys x 2^{lg_rows} coeffs (blowup {1 << lg_b}), "
-                      f"OpenMP over {os.cpu_count()} host threads, {dt:.1f} s"}
+                      f"OpenMP over {host_threads()} host threads, {dt:.1f} s"}
 
 
 def run_reference(args):
@@ -118,7 +129,7 @@ def run_reference(args):
         "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3), "higher_is_better": True,
         "scaling": "weak" if args.gpus == 1 else "strong", "vs_baseline": None, "dtype": "u64 (Goldilocks)",
         "data": "synthetic", "impl": "reference", "config": cfg,
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": host_threads(), "kind": "port",
                          "sample": f"{args.polys} polys x 2^{lg_rows} coeffs per step (bounded sample of the "
                                    f"workload), oracle/zkie_oracle.c on all host threads"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

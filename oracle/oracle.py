@@ -91,6 +91,7 @@ def lib():
             "orc_op_matmul_prove": (None, [_pu64, _pu64, _pu64, _u64, _u64, _u64, C.POINTER(Challenger),
                                            _pu64, _pu64, _pu64, _pu64, _pu64, _pu64, _pu64]),
             "orc_shard_dag_child": (None, [_pu64, _u32, _u64, _u64, C.POINTER(Transcript)]),
+            "orc_set_threads": (None, [C.c_int]),
             "orc_check_witness": (C.c_int, [C.POINTER(P2Consts), _pu64, _pu64, _u32, _u32, _u64]),
             "orc_grind": (_u64, [C.POINTER(P2Consts), _pu64, _pu64, _u32, _u32, _u64, _u64]),
             "orc_fractional_prove": (None, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _pu64, _pu64]),
@@ -536,3 +537,8 @@ def grind(consts, sponge, inputs, bits, start=0, limit=1 << 40):
     sp, inp = u64(sponge), u64(inputs if len(inputs) else [0])
     w = lib().orc_grind(C.byref(consts), ptr(sp), ptr(inp), len(inputs), bits, start, limit)
     return None if w == 0xFFFFFFFFFFFFFFFF else int(w)
+
+
+def set_threads(n):
+    """OpenMP threads of the oracle's parallel loops."""
+    lib().orc_set_threads(int(n))

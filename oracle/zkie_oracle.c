@@ -1180,3 +1180,14 @@ uint64_t orc_grind(const orc_p2_consts *c, const uint64_t sponge[16], const uint
         if (orc_check_witness(c, sponge, input, len, bits, w)) return w;
     return ~0ULL;
 }
+
+/* Thread count of the OpenMP loops above (a launcher may have set
+ * OMP_NUM_THREADS=1 for its ranks; the CPU baseline wants every core). */
+void orc_set_threads(int n)
+{
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

@@ -166,6 +166,9 @@ void orc_op_matmul_prove(const uint64_t *a, const uint64_t *b, const uint64_t *c
 void orc_shard_dag_child(const uint64_t *op_ids, uint32_t n_ops, uint64_t ops_per_shard,
                          uint64_t shard_index, orc_transcript *child);
 
+/* Thread count of the oracle's OpenMP loops (n > 0). */
+void orc_set_threads(int n);
+
 /* PoW grinding on DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>: validity of a
  * witness for the challenger (sponge state, len < 8 buffered inputs), and the smallest
  * valid witness of [start, start + limit) (UINT64_MAX if none). */
