@@ -596,9 +596,10 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
     a 2^18-fraction tree; a 16-bit grind)."""
     import types
 
-    from zkie_b200.perfcases import case_grind, case_logup
+    from zkie_b200.perfcases import case_fixed, case_grind, case_logup
     lg = case_logup(types.SimpleNamespace(log_size=lg_frac, iters=5))
     gr = case_grind(types.SimpleNamespace(log_size=grind_bits, iters=3))
+    fm = case_fixed(types.SimpleNamespace(m=512, k=1024, n=4096, iters=5))
     out = {
         "logup": {"config": f"prove_fractional_with_challenges over 2^{lg_frac} fractions (every layer on the device)",
                   "ms": round(lg["ms"], 4), "value": round((1 << lg_frac) / (lg["ms"] / 1e3) / 1e6, 3),
@@ -606,6 +607,11 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
         "grind": {"config": f"WHIR PoW grind, {grind_bits} bits, DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>",
                   "ms": round(gr["ms"], 4), "witness": gr["witness"], "value": round(gr["gperm_s_tried"] * 1e3, 3),
                   "unit": "M candidates/s"},
+        "forward_matmul": {"config": "par::mm_par_fixed, 512 x 1024 @ 1024 x 4096 (a GPT-2 layer's FFN shape), "
+                                     "16-bit fixed-point entries, u8 x u8 -> s32 tcgen05 GEMMs",
+                           "ms": round(fm["ms"], 4), "path": "tensor cores" if fm["path"] == 0 else "field kernel",
+                           "field_kernel_ms": round(fm["field_kernel_ms"], 4), "equal_to_field_kernel": fm["equal"],
+                           "value": round(512 * 1024 * 4096 / (fm["ms"] / 1e3) / 1e9, 3), "unit": "G MAC/s"},
     }
     if want_cpu:
         import numpy as np
@@ -627,6 +633,17 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
         out["grind"]["cpu_baseline"] = {"value": round((w + 1) / s_grind / 1e6, 4), "unit": "M candidates/s",
                                         "cores": 1, "kind": "port",
                                         "sample": f"16-bit grind from the same state ({w + 1} candidates)"}
+        a = g.integers(-(1 << 15), 1 << 15, size=(16, 1024), dtype=np.int64)
+        b = g.integers(-(1 << 15), 1 << 15, size=(1024, 4096), dtype=np.int64)
+        fa = a.astype(np.uint64) + np.where(a < 0, np.uint64(P), np.uint64(0))
+        fb = b.astype(np.uint64) + np.where(b < 0, np.uint64(P), np.uint64(0))
+        orc.set_threads(host_threads())
+        t0 = time.perf_counter()
+        orc.matmul_field(fa, fb)
+        s_mm = time.perf_counter() - t0
+        out["forward_matmul"]["cpu_baseline"] = {"value": round(16 * 1024 * 4096 / s_mm / 1e9, 4), "unit": "G MAC/s",
+                                                 "cores": host_threads(), "kind": "port",
+                                                 "sample": "16 x 1024 @ 1024 x 4096, oracle field matmul (OpenMP)"}
     return out
 
 

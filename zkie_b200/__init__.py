@@ -12,7 +12,7 @@ from .commit import (  # noqa: F401
 from .device import P  # noqa: F401
 from .gkr import (  # noqa: F401
     MatmulProof, OpMatMulProof, SumcheckProof, SumcheckProofBatch, Transcript, VirtualProof, XorShift64, eq_evals,
-    matmul_field, matmul_prove, mle_eval, mle_partial_eval, op_matmul_prove, prove_sum_of_products, prove_virtual,
+    matmul_field, matmul_fixed, matmul_prove, mle_eval, mle_partial_eval, op_matmul_prove, prove_sum_of_products, prove_virtual,
     sha256, shard_dag_child, sumcheck_prove)
 from .gkr import ShardMatMulProof, ShardProver  # noqa: F401
 from .pow import grind  # noqa: F401

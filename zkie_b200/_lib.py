@@ -84,6 +84,8 @@ SIGNATURES = {
     "zkie2_op_matmul_prove": (i64, [vp, vp, vp, u64, u64, u64, PCh, pu64, pu64, pu64, pu64, pu64, pu64,
                                     pu64, vp, vp]),
     "zkie2_matmul_field": (i64, [vp, vp, u64, u64, u64, vp, vp]),
+    "zkie2_matmul_fixed_scratch_elems": (u64, [u64, u64, u64]),
+    "zkie2_matmul_fixed": (i64, [vp, vp, u64, u64, u64, vp, u32, pu32, vp, vp]),
     "zkie2_shard_prove_matmul_scratch_elems": (u64, [u64, u64, u64]),
     "zkie2_shard_prove_matmul": (i64, [vp, vp, u64, u64, u64, pu64, u64, u64, vp, pu64, pu64, pu64, pu64, pu64,
                                        vp, vp]),

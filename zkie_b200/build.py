@@ -18,7 +18,28 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libzkie_b200.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-diag-suppress", "550",
+
+
+def cutlass_include() -> list:
+    """-I flags of the CUTLASS/CuTe header tree (the tensor-core GEMM of the
+    fixed-point forward matmul instantiates its sm100 templates): the tree
+    vendored with the flashinfer package, or $CUTLASS_DIR."""
+    cands = []
+    if os.environ.get("CUTLASS_DIR"):
+        cands.append(os.environ["CUTLASS_DIR"])
+    try:
+        import site
+        for sp in site.getsitepackages():
+            cands.append(os.path.join(sp, "flashinfer", "data", "cutlass"))
+    except Exception:
+        pass
+    for c in cands:
+        if os.path.exists(os.path.join(c, "include", "cutlass", "gemm", "collective", "collective_builder.hpp")):
+            return ["-I" + os.path.join(c, "include"), "-I" + os.path.join(c, "tools", "util", "include")]
+    raise RuntimeError("CUTLASS headers not found (set CUTLASS_DIR to a CUTLASS 4.x checkout)")
+
+
+NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-diag-suppress", "550,20012",
                      "--expt-relaxed-constexpr", "-I" + INCLUDE]
 
 
@@ -39,7 +60,7 @@ def _headers():
 
 
 def _compile(src: str, obj: str, verbose_ptxas: bool) -> str:
-    cmd = [nvcc()] + NVCC_FLAGS + ["-c", src, "-o", obj]
+    cmd = [nvcc()] + NVCC_FLAGS + (cutlass_include() if src.endswith("_tc.cu") else []) + ["-c", src, "-o", obj]
     if verbose_ptxas and src.endswith(".cu"):
         cmd += ["-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)

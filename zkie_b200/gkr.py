@@ -7,6 +7,7 @@
 - ``op_matmul_prove``                        <- zkie-ops/src/compose.rs:1724-1747
 - ``prove_sum_of_products``                  <- common/sumcheck.rs:243-286
 - ``prove_virtual`` -> ``VirtualProof``      <- common/sumcheck.rs:378-438
+- ``matmul_fixed`` (forward witness)        <- zkie-ops/src/par.rs:41-89
 - ``shard_dag_child``                        <- zkie-ops/src/compose.rs:2276-2311
 """
 import ctypes as C
@@ -238,6 +239,23 @@ def matmul_field(a, b, m, k, n) -> torch.Tensor:
     dc = empty(m * n)
     check(lib.zkie2_matmul_field(ptr(da), ptr(db), m, k, n, ptr(dc), stream_handle()), "zkie2_matmul_field")
     return dc
+
+
+def matmul_fixed(a, b, m, k, n, force_tensor=False):
+    """par::mm_par_fixed: the same product as matmul_field, on the tensor cores when
+    every input is 16-bit fixed point (and, unless force_tensor, the product has at
+    least 2^27 multiply-adds); returns (C on the device, path) with path 0 = tensor
+    cores, 1 = the field kernel."""
+    da, db = to_dev(a).reshape(-1), to_dev(b).reshape(-1)
+    if da.numel() != m * k or db.numel() != k * n:
+        raise ValueError("matmul_fixed: shape mismatch")
+    dc = empty(m * n)
+    scr = empty(max(lib.zkie2_matmul_fixed_scratch_elems(m, k, n), 1))
+    path = C.c_uint32(0)
+    check(lib.zkie2_matmul_fixed(ptr(da), ptr(db), m, k, n, ptr(dc), 1 if force_tensor else 0, C.byref(path),
+                                 ptr(scr), stream_handle()),
+          "zkie2_matmul_fixed")
+    return dc, int(path.value)
 
 
 # ---- batch-opening and virtual-polynomial sumchecks -------------------------------------

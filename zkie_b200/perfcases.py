@@ -7,6 +7,7 @@
     python -m zkie_b200.perfcases virtual --log-size 21
     python -m zkie_b200.perfcases logup --log-size 24
     python -m zkie_b200.perfcases grind --log-size 24
+    python -m zkie_b200.perfcases fixed --m 512 --k 1024 --n 4096
     python -m zkie_b200.perfcases sop --log-size 20 --polys 4
     python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
     python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
@@ -193,6 +194,44 @@ def case_grind(a):
             "gperm_s_tried": perms / (ms / 1e3) / 1e9}
 
 
+def case_fixed(a):
+    """The fixed-point forward matmul (zkie2_matmul_fixed) on m x k @ k x n with
+    16-bit entries, against the exact field kernel on the same inputs;
+    tensor-core work = 4 m n k u8 MACs (three GEMMs, the middle one over 2k)."""
+    import ctypes as C
+    m, k, n = a.m, a.k, a.n
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+
+    def fx(cnt):
+        return _fx_field(torch.randint(-(1 << 15), 1 << 15, (cnt,), generator=g, device="cuda", dtype=torch.int64))
+    da, db = fx(m * k), fx(k * n)
+    dc = torch.empty(m * n, dtype=torch.uint64, device="cuda")
+    dc2 = torch.empty(m * n, dtype=torch.uint64, device="cuda")
+    scr = torch.empty(lib.zkie2_matmul_fixed_scratch_elems(m, k, n), dtype=torch.uint64, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    path = C.c_uint32(9)
+
+    def tc():
+        check(lib.zkie2_matmul_fixed(da.data_ptr(), db.data_ptr(), m, k, n, dc.data_ptr(), 0, C.byref(path),
+                                     scr.data_ptr(), st), "matmul_fixed")
+
+    def field():
+        check(lib.zkie2_matmul_field(da.data_ptr(), db.data_ptr(), m, k, n, dc2.data_ptr(), st), "matmul_field")
+    ms_tc = _time(tc, a.iters)
+    ms_f = _time(field, a.iters)
+    same = bool(torch.equal(dc.view(torch.int64), dc2.view(torch.int64)))
+    macs = 4 * m * n * k
+    return {"case": "matmul_fixed", "m": m, "k": k, "n": n, "path": int(path.value), "ms": ms_tc,
+            "field_kernel_ms": ms_f, "equal": same, "tops_u8": macs * 2 / (ms_tc / 1e3) / 1e12}
+
+
+def _fx_field(x):
+    """int64 values in (-2^62, 2^62) -> field elements (from_i64) as uint64 on the
+    device: p + x for x < 0 is x + 1 - 2^32 in 64-bit two's complement."""
+    return torch.where(x < 0, x + 1 - (1 << 32), x).view(torch.uint64)
+
+
 def case_sop(a):
     """prove_sum_of_products over `polys` table pairs of 2^log_size."""
     t, n = a.log_size, a.polys
@@ -304,7 +343,7 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup", "grind"])
+                                         "logup", "grind", "fixed"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -318,7 +357,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "sop": case_sop, "shard": case_shard, "split": case_split,
+           "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "sop": case_sop, "shard": case_shard, "split": case_split,
            "sweep": case_sweep}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
