@@ -269,6 +269,27 @@ uint64_t zkie2_grind_batch(uint32_t bits);
 int zkie2_grind(const uint64_t *h_sponge, const uint64_t *h_input, uint32_t len, uint32_t bits,
                 uint64_t *h_witness, zkie_stream_t stream);
 
+/* ---- ZKIEBCH2 weight cache --------------------------------------------------------- */
+/* The weight-cache file of a committed batch: header = bincode 1.3.3 of (b"ZKIEBCH2",
+ * BatchCacheMetadata, MerkleCap of the root) (pcs/cache.rs:7-70); then the committed
+ * matrix (Whir::serialize_batch_prover_data_into, pcs/whir.rs:542-559: u64 count 1,
+ * u64 width, u64 value count, values); then the digest layers (p3-merkle-tree
+ * write_digest_layers: u64 layer count, u64 per layer length, u64 arity 2 per step,
+ * digests).  All integers little-endian.  zkie2_cache_header returns the header length
+ * and writes it to out when out_cap is large enough (0 on a null argument). */
+uint64_t zkie2_cache_header(const char *model_id, const char *group_id, const char *const *table_ids,
+                            uint32_t num_tables, uint32_t table_arity, uint32_t security_level, uint32_t pow_bits,
+                            const uint8_t *source_digest, const uint64_t *root, uint8_t *out, uint64_t out_cap);
+/* Write the file: the header bytes, then the rows x width matrix d_lde and every digest
+ * layer of its rows-row tree (d_layers, the layout of zkie2_merkle_tree) streamed from the
+ * device through pinned staging buffers.  Synchronous. */
+int zkie2_cache_write(const char *path, const uint8_t *header, uint64_t header_len, const uint64_t *d_lde,
+                      uint64_t rows, uint64_t width, const uint64_t *d_layers, zkie_stream_t stream);
+/* Read the matrix and the digest layers of such a file (after its header_len header bytes)
+ * into device buffers, checking every count against rows x width.  Synchronous. */
+int zkie2_cache_read(const char *path, uint64_t header_len, uint64_t rows, uint64_t width, uint64_t *d_lde,
+                     uint64_t *d_layers, zkie_stream_t stream);
+
 /* ---- logUp GKR fraction tree (common/logup_gkr.rs) ------------------------------------ */
 /* prove_fractional_with_challenges (logup_gkr.rs:29-69) over device tables
  * num, den of 2^lg_n values (read only), with lg_n challenges full_r and cs

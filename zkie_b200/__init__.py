@@ -15,6 +15,7 @@ from .gkr import (  # noqa: F401
     matmul_field, matmul_fixed, matmul_prove, mle_eval, mle_partial_eval, op_matmul_prove, prove_sum_of_products, prove_virtual,
     sha256, shard_dag_child, sumcheck_prove)
 from .gkr import ShardMatMulProof, ShardProver  # noqa: F401
+from .cache import BatchCacheMetadata, header_bytes, read_cache, read_header, write_cache  # noqa: F401
 from .pow import grind  # noqa: F401
 from .logup import (  # noqa: F401
     FractionalLayer, FractionalProof, build_lookup_num_den, build_lookup_table_num_den, build_lookup_witness_num_den,

@@ -95,6 +95,10 @@ SIGNATURES = {
     "zkie2_virtual_prove": (i64, [C.POINTER(vp), u32, u32, pu64, pu32, pu32, u32, pu64, pu64, pu64, vp, vp]),
     "zkie2_grind_batch": (u64, [u32]),
     "zkie2_grind": (i64, [pu64, pu64, u32, u32, pu64, vp]),
+    "zkie2_cache_header": (u64, [C.c_char_p, C.c_char_p, C.POINTER(C.c_char_p), u32, u32, u32, u32, C.c_char_p, pu64,
+                                  C.c_char_p, u64]),
+    "zkie2_cache_write": (i64, [C.c_char_p, C.c_char_p, u64, vp, u64, u64, vp, vp]),
+    "zkie2_cache_read": (i64, [C.c_char_p, u64, u64, u64, vp, vp, vp]),
     "zkie2_fractional_scratch_elems": (u64, [u32]),
     "zkie2_fractional_prove": (i64, [vp, vp, u32, pu64, pu64, pu64, pu64, pu64, vp, vp]),
     "zkie2_lookup_len": (u64, [u64, u64, u32]),

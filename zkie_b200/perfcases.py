@@ -8,6 +8,7 @@
     python -m zkie_b200.perfcases logup --log-size 24
     python -m zkie_b200.perfcases grind --log-size 24
     python -m zkie_b200.perfcases fixed --m 512 --k 1024 --n 4096
+    python -m zkie_b200.perfcases cache --log-size 25
     python -m zkie_b200.perfcases sop --log-size 20 --polys 4
     python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
     python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
@@ -232,6 +233,35 @@ def _fx_field(x):
     return torch.where(x < 0, x + 1 - (1 << 32), x).view(torch.uint64)
 
 
+def case_cache(a):
+    """The ZKIEBCH2 cache file of a WHIR commit of 2^log_size evaluations,
+    written from and read back into device buffers (a temporary file)."""
+    import os
+    import tempfile
+    import time
+
+    from .cache import BatchCacheMetadata, read_cache, write_cache
+    from .commit import Whir
+    n = a.log_size
+    com = Whir(n).commit(_rand(1 << n, 50))
+    rows = com.lde.numel() // 32
+    meta = BatchCacheMetadata("model", "group", ["w"], n, 1, 90, 32, bytes(32))
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "batch.zkc")
+        write_cache(path, meta, com.root, com.lde, 32, com.layers)
+        t0 = time.perf_counter()
+        for _ in range(a.iters):
+            write_cache(path, meta, com.root, com.lde, 32, com.layers)
+        tw = (time.perf_counter() - t0) / a.iters
+        size = os.path.getsize(path)
+        t0 = time.perf_counter()
+        for _ in range(a.iters):
+            read_cache(path, rows, 32)
+        tr = (time.perf_counter() - t0) / a.iters
+    return {"case": "cache", "log_size": n, "bytes": size, "write_ms": 1e3 * tw, "read_ms": 1e3 * tr,
+            "write_gbs": size / tw / 1e9, "read_gbs": size / tr / 1e9}
+
+
 def case_sop(a):
     """prove_sum_of_products over `polys` table pairs of 2^log_size."""
     t, n = a.log_size, a.polys
@@ -343,7 +373,7 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup", "grind", "fixed"])
+                                         "logup", "grind", "fixed", "cache"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -357,7 +387,7 @@ def main(argv=None):
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
-           "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "sop": case_sop, "shard": case_shard, "split": case_split,
+           "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "cache": case_cache, "sop": case_sop, "shard": case_shard, "split": case_split,
            "sweep": case_sweep}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
