@@ -17,6 +17,7 @@ from .gkr import (  # noqa: F401
 from .gkr import ShardMatMulProof, ShardProver  # noqa: F401
 from .cache import BatchCacheMetadata, header_bytes, read_cache, read_header, write_cache  # noqa: F401
 from .pow import grind  # noqa: F401
+from .proofbytes import from_bincode, to_bincode  # noqa: F401
 from .logup import (  # noqa: F401
     FractionalLayer, FractionalProof, build_lookup_num_den, build_lookup_table_num_den, build_lookup_witness_num_den,
     fractional_leaf, lookup_multiplicity, merge_multiplicity, pad_table, prove_fractional,
