@@ -275,26 +275,49 @@ ZK_HD uint64_t acc160_reduce(const Acc160& a) {
     return gl_sub(r, (uint64_t)a.w[4] << 32);
 }
 
-// a^2: the cross product a0*a1 is formed once and added twice, so the square
-// takes three 32 x 32 -> 64 products instead of the four partial-product
-// chains of gl_mul.
+// a^2 = a0^2 + 2 a0 a1 2^32 + a1^2 2^64: the two squares as wide products and
+// the doubled cross term as two multiply-add carry chains.  Three fewer
+// multiplies than gl_mul and most of the additions on the multiply pipe
+// (the ALU pipe is the one that binds the Poseidon2 S-box).
 ZK_HD uint64_t gl_sqr(uint64_t a) {
 #if defined(__CUDA_ARCH__)
     const uint32_t a0 = (uint32_t)a, a1 = (uint32_t)(a >> 32);
-    const uint64_t ll = mul_wide32(a0, a0), hh = mul_wide32(a1, a1), c = mul_wide32(a0, a1);
+    const uint64_t ll = mul_wide32(a0, a0), hh = mul_wide32(a1, a1);
     uint32_t r0 = (uint32_t)ll, r1 = (uint32_t)(ll >> 32), r2 = (uint32_t)hh, r3 = (uint32_t)(hh >> 32);
-    const uint32_t c0 = (uint32_t)c, c1 = (uint32_t)(c >> 32);
-    asm("add.cc.u32  %0, %0, %3;\n\t"
-        "addc.cc.u32 %1, %1, %4;\n\t"
-        "addc.u32    %2, %2, 0;\n\t"
-        "add.cc.u32  %0, %0, %3;\n\t"
-        "addc.cc.u32 %1, %1, %4;\n\t"
-        "addc.u32    %2, %2, 0;"
+    asm("mad.lo.cc.u32  %0, %3, %4, %0;\n\t"
+        "madc.hi.cc.u32 %1, %3, %4, %1;\n\t"
+        "addc.u32       %2, %2, 0;\n\t"
+        "mad.lo.cc.u32  %0, %3, %4, %0;\n\t"
+        "madc.hi.cc.u32 %1, %3, %4, %1;\n\t"
+        "addc.u32       %2, %2, 0;"
         : "+r"(r1), "+r"(r2), "+r"(r3)
-        : "r"(c0), "r"(c1));
+        : "r"(a0), "r"(a1));
     return gl_reduce128(pack64(r0, r1), pack64(r2, r3));
 #else
     return gl_mul(a, a);
+#endif
+}
+
+// a * b with the diagonal products as wide multiplies and the two cross
+// products as multiply-add carry chains: fewer ALU instructions than gl_mul
+// (whose single carry chain suits the NTT better), for the S-box.
+ZK_HD uint64_t gl_mul_madc(uint64_t a, uint64_t b) {
+#if defined(__CUDA_ARCH__)
+    const uint32_t a0 = (uint32_t)a, a1 = (uint32_t)(a >> 32);
+    const uint32_t b0 = (uint32_t)b, b1 = (uint32_t)(b >> 32);
+    const uint64_t ll = mul_wide32(a0, b0), hh = mul_wide32(a1, b1);
+    uint32_t r0 = (uint32_t)ll, r1 = (uint32_t)(ll >> 32), r2 = (uint32_t)hh, r3 = (uint32_t)(hh >> 32);
+    asm("mad.lo.cc.u32  %0, %3, %6, %0;\n\t"
+        "madc.hi.cc.u32 %1, %3, %6, %1;\n\t"
+        "addc.u32       %2, %2, 0;\n\t"
+        "mad.lo.cc.u32  %0, %4, %5, %0;\n\t"
+        "madc.hi.cc.u32 %1, %4, %5, %1;\n\t"
+        "addc.u32       %2, %2, 0;"
+        : "+r"(r1), "+r"(r2), "+r"(r3)
+        : "r"(a0), "r"(a1), "r"(b0), "r"(b1));
+    return gl_reduce128(pack64(r0, r1), pack64(r2, r3));
+#else
+    return gl_mul(a, b);
 #endif
 }
 

@@ -7,7 +7,9 @@
 // and x^7 on lane 0, then state <- (1 + diag(V)) * state); 4 external rounds.
 //
 // Cost shape on sm_100a: the integer ALU pipe (additions, carry folding) is
-// the bottleneck, the multiply pipe has headroom.  So the linear layers add
+// the bottleneck, the multiply pipe has headroom.  So the S-box squares and
+// multiplies with products whose cross terms are multiply-add carry chains
+// (gl_sqr, gl_mul_madc: additions moved onto the multiply pipe), the linear layers add
 // into 96-bit accumulators (3 instructions per addition) and reduce each
 // output once, instead of reducing after every modular addition; and the
 // eight external rounds share one loop body, the internal rounds nested after
@@ -25,9 +27,9 @@ struct P2Const {
 
 ZK_HD uint64_t p2_sbox(uint64_t x) {
     const uint64_t x2 = gl_sqr(x);
-    const uint64_t x3 = gl_mul(x2, x);
+    const uint64_t x3 = gl_mul_madc(x2, x);
     const uint64_t x4 = gl_sqr(x2);
-    return gl_mul(x3, x4);
+    return gl_mul_madc(x3, x4);
 }
 
 // [2 3 1 1; 1 2 3 1; 1 1 2 3; 3 1 1 2] on one 4-lane block, unreduced
