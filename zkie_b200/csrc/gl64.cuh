@@ -193,6 +193,25 @@ ZK_HD Acc acc_add(Acc a, Acc b) {
 #endif
 }
 
+// a - b, for a >= b
+ZK_HD Acc acc_sub(Acc a, Acc b) {
+#if defined(__CUDA_ARCH__)
+    asm("sub.cc.u64 %0, %0, %2;\n\t"
+        "subc.u32 %1, %1, %3;"
+        : "+l"(a.lo), "+r"(a.hi)
+        : "l"(b.lo), "r"(b.hi));
+    return a;
+#else
+    return Acc{a.lo - b.lo, a.hi - b.hi - (a.lo < b.lo ? 1u : 0u)};
+#endif
+}
+
+// x * 2^K as an accumulator, 1 <= K <= 31
+template <int K>
+ZK_HD Acc acc_shl(uint64_t x) {
+    return Acc{x << K, (uint32_t)(x >> (64 - K))};
+}
+
 // x + y of two partially reduced elements, as an accumulator
 ZK_HD Acc acc_sum(uint64_t x, uint64_t y) { return acc_add(acc_of(x), y); }
 

@@ -69,28 +69,39 @@ ZK_HD void p2_mds_light(uint64_t s[16]) {
     for (int i = 0; i < 16; i++) s[i] = acc_reduce(acc_add(y[i], sum[i & 3]));
 }
 
+// sum - V s for V in {2, 3, 4}, given vs = V s: (V + 1) p exceeds V s, so
+// sum + (V + 1) p - V s is a non-negative accumulator below (V + 2) 2^64.
+template <int V>
+ZK_HD uint64_t p2_sum_minus(uint64_t sum, Acc vs) {
+    const Acc c = acc_add(Acc{(uint64_t)0 - (uint64_t)(V + 1) * GL_EPS, (uint32_t)V}, sum);
+    return acc_reduce(acc_sub(c, vs));
+}
+
 // Internal linear layer: s_i <- sum + V_i * s_i with
 // V = [-2, 1, 2, 1/2, 3, 4, -1/2, -3, -4, 1/2^3, 1/2^4, 1/2^5, -1/2^3,
 //      -1/2^4, -1/2^5, diag15] (poseidon2_merkle.cu:111-142).
 ZK_HD void p2_internal_linear(uint64_t s[16], uint64_t diag15) {
-    Acc acc = acc_sum(s[0], s[1]);
+    // the sum over the 32-bit halves (3-input additions), then recombined
+    uint64_t lo = 0, hi = 0;
 #pragma unroll
-    for (int i = 2; i < 16; i++) acc = acc_add(acc, s[i]);
+    for (int i = 0; i < 16; i++) {
+        lo += (uint32_t)s[i];
+        hi += s[i] >> 32;
+    }
+    // lo, hi < 2^36: lo + hi 2^32 < 2^69
+    const Acc acc = acc_add(Acc{hi << 32, (uint32_t)(hi >> 32)}, lo);
     // canonical, so that sum + x needs a single carry fold (gl_add_c)
     const uint64_t sum = gl_canon(acc_reduce(acc));
-    uint64_t t;
-    s[0] = gl_sub(sum, gl_add(s[0], s[0]));
+    // integer V: one accumulator expression and one reduction per lane
+    s[0] = p2_sum_minus<2>(sum, acc_shl<1>(s[0]));
     s[1] = gl_add_c(s[1], sum);
-    s[2] = gl_add_c(gl_add(s[2], s[2]), sum);
+    s[2] = acc_reduce(acc_add(acc_shl<1>(s[2]), sum));
     s[3] = gl_add_c(gl_div_pow2<1>(s[3]), sum);
     s[4] = acc_reduce(acc_add(acc_add(acc_sum(sum, s[4]), s[4]), s[4]));
-    t = gl_add(s[5], s[5]);
-    s[5] = gl_add_c(gl_add(t, t), sum);
+    s[5] = acc_reduce(acc_add(acc_shl<2>(s[5]), sum));
     s[6] = gl_sub(sum, gl_div_pow2<1>(s[6]));
-    t = acc_reduce(acc_add(acc_sum(s[7], s[7]), s[7]));
-    s[7] = gl_sub(sum, t);
-    t = gl_add(s[8], s[8]);
-    s[8] = gl_sub(sum, gl_add(t, t));
+    s[7] = p2_sum_minus<3>(sum, acc_add(acc_shl<1>(s[7]), s[7]));
+    s[8] = p2_sum_minus<4>(sum, acc_shl<2>(s[8]));
     s[9] = gl_add_c(gl_div_pow2<3>(s[9]), sum);
     s[10] = gl_add_c(gl_div_pow2<4>(s[10]), sum);
     s[11] = gl_add_c(gl_div_pow2<5>(s[11]), sum);
