@@ -19,6 +19,8 @@
 
 namespace zk {
 
+constexpr uint64_t kInv2Pow32 = 0xFFFFFFFE00000002ull;  // 1/2^32 mod p
+
 struct P2Const {
     uint64_t ext[8][16];  // rounds 0-3: initial external, 4-7: terminal external
     uint64_t internal[22];
@@ -108,7 +110,8 @@ ZK_HD void p2_internal_linear(uint64_t s[16], uint64_t diag15) {
     s[12] = gl_sub(sum, gl_div_pow2<3>(s[12]));
     s[13] = gl_sub(sum, gl_div_pow2<4>(s[13]));
     s[14] = gl_sub(sum, gl_div_pow2<5>(s[14]));
-    s[15] = gl_add_c(gl_mul(s[15], diag15), sum);
+    // V_15 = 1/2^32 for the reference's constants: a division, not a product
+    s[15] = gl_add_c(diag15 == kInv2Pow32 ? gl_div_pow2<32>(s[15]) : gl_mul(s[15], diag15), sum);
 }
 
 ZK_HD void p2_internal_round(uint64_t s[16], uint64_t rc, uint64_t diag15) {
