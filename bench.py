@@ -233,10 +233,10 @@ def int_peaks(zk, dev):
     mul_peak = n_thr * 8 * iters / (pe0.elapsed_time(pe1) / 1e3)
     check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 1, sh), "permute warmup")
     pe0.record(stream)
-    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 4, sh), "permute")
+    check(lib.zkie2_p2_permute(st.data_ptr(), n_thr, 16, sh), "permute")
     pe1.record(stream)
     torch.cuda.synchronize()
-    return mul_peak, n_thr * 4 / (pe0.elapsed_time(pe1) / 1e3)
+    return mul_peak, n_thr * 16 / (pe0.elapsed_time(pe1) / 1e3)
 
 
 def hbm_peak_gbs():
