@@ -71,6 +71,7 @@ struct PassDesc {
     uint32_t tw_log;  // 0: no inter-pass twiddle; else multiply by W_{2^tw_log}^(f*k)
     uint32_t canon;   // canonicalize the output
     uint32_t cgroups;  // k_ntt_pass2: column groups of 2^logC columns (fastest-varying block index)
+    uint32_t half_zero;  // k_ntt_pass2: inputs e >= 8 of every first-step group are padding rows
     // Twiddle source of the reference-facing entry: the caller's top-stage
     // table tab[e] = W_{2^tab_log}^e, e < 2^(tab_log-1).
     const uint64_t* tab;
@@ -292,6 +293,23 @@ __device__ __forceinline__ void dft_reg(uint64_t* x) {
     for (int i = 0; i < R; i++) x[i] = y[i];
 }
 
+template <int L, int... S>
+__device__ __forceinline__ void dit_stages_from2(uint64_t* y, std::integer_sequence<int, S...>) {
+    (dit_stage<S + 2>(y, std::make_integer_sequence<int, (1 << (L - 1))>{}), ...);
+}
+// dft_reg for inputs whose upper half is zero: after the bit reversal those
+// sit at the odd positions, so the first DIT stage (twiddle 1) is a copy.
+template <int L>
+__device__ __forceinline__ void dft_reg_half(uint64_t* x) {
+    constexpr int R = 1 << L;
+    uint64_t y[R];
+#pragma unroll
+    for (int i = 0; i < R; i += 2) y[i] = y[i + 1] = x[brev_c<L>(i)];
+    dit_stages_from2<L>(y, std::make_integer_sequence<int, L - 1>{});
+#pragma unroll
+    for (int i = 0; i < R; i++) x[i] = y[i];
+}
+
 // Output index of the last step's group gam: the digit of step i sits at bits
 // [lgm_i - lg_i, lgm_i) of the position and goes to bits
 // [lg_0 + ... + lg_{i-1}, ...) of k; the last step's own digit is added by
@@ -312,10 +330,10 @@ __device__ __forceinline__ uint32_t n2_out_base(const Sched& sc, uint32_t gam, u
 // One step with radix 2^L: the thread's 16 elements are G = 16 / 2^L groups.
 // kIn / kOut: the step reads from global memory (first step) or shared
 // memory, and writes to global memory (last step) or shared memory.
-template <int L, bool kIn, bool kOut, typename IdxT>
+template <int L, bool kIn, bool kOut, typename IdxT, bool kHalf = false>
 __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint32_t lgm, uint64_t* data,
-                                        const uint64_t* tws, uint32_t q, uint32_t cc, uint32_t logC, bool cok,
-                                        IdxT row_in0, IdxT row_out0, uint64_t f, uint64_t col0) {
+                                        const uint64_t* tws, const uint64_t* ptw, uint32_t q, uint32_t cc,
+                                        uint32_t logC, bool cok, IdxT row_in0, IdxT row_out0, uint64_t col0) {
     constexpr int R = 1 << L, G = kN2Elems / R;
     const uint32_t m = d.m, lgs = lgm - L;  // stride M_i / R
     const IdxT w = (IdxT)d.ld;  // row stride
@@ -334,7 +352,8 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
 #pragma unroll
             for (int e = 0; e < R; e++) {
                 x[e] = 0;
-                if (cok && (uint64_t)(row_b + (IdxT)e * rstep) < d.rows_valid) x[e] = __ldg(g + (IdxT)e * gstep);
+                if ((!kHalf || e < R / 2) && cok && (uint64_t)(row_b + (IdxT)e * rstep) < d.rows_valid)
+                    x[e] = __ldg(g + (IdxT)e * gstep);
             }
         } else {
             const uint64_t* p = data + (base << logC) + cc;
@@ -342,7 +361,10 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
 #pragma unroll
             for (int e = 0; e < R; e++) x[e] = p[e * st];
         }
-        dft_reg<L>(x);
+        if (kHalf)
+            dft_reg_half<L>(x);
+        else
+            dft_reg<L>(x);
         if (!kOut) {
             // W_{M_i}^(j' e) = W_M^(j' e 2^(m - lgm))
             const uint32_t tsh = m - lgm;
@@ -357,10 +379,8 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
             // k = kb + e 2^(m-L), row row_out0 + k kout
             const uint32_t kb = n2_out_base(sc, gam, L);
             if (d.tw_log) {
-                const uint64_t emask = (1ull << d.tw_log) - 1;
 #pragma unroll
-                for (int e = 0; e < R; e++)
-                    x[e] = gl_mul(x[e], root_pow<false>(d, d.tw_log, (f * (kb | ((uint32_t)e << (m - L)))) & emask));
+                for (int e = 0; e < R; e++) x[e] = gl_mul(x[e], ptw[kb | ((uint32_t)e << (m - L))]);
             }
             if (d.canon) {
 #pragma unroll
@@ -382,6 +402,7 @@ __global__ void __launch_bounds__(kN2Threads, 2) k_ntt_pass2(PassDesc d, Sched s
     const uint32_t m = d.m, M = 1u << m, logC = d.logC;
     uint64_t* data = sm;                         // [M][C]
     uint64_t* tws = sm + ((size_t)M << logC);    // [M] powers of W_M
+    uint64_t* ptw = tws + M;                     // [M] inter-pass twiddles (tw_log != 0)
     // Consecutive blocks take consecutive column groups of the same rows, so
     // the row segments that neighbouring blocks read share DRAM bursts in L2.
     const uint64_t cg = blockIdx.x % d.cgroups, bx = blockIdx.x / d.cgroups;
@@ -391,27 +412,36 @@ __global__ void __launch_bounds__(kN2Threads, 2) k_ntt_pass2(PassDesc d, Sched s
     const uint32_t tid = threadIdx.x, cc = tid & ((1u << logC) - 1), q = tid >> logC;
     const bool cok = col0 + cc < d.w;
     for (uint32_t i = tid; i < M; i += blockDim.x) tws[i] = root_pow<false>(d, m, i);
+    if (d.tw_log) {
+        // W_{2^tw_log}^(f k) for this block's lane f and every output k, once
+        // per block instead of once per element (the block's columns share them)
+        const uint64_t emask = (1ull << d.tw_log) - 1;
+        for (uint32_t i = tid; i < M; i += blockDim.x) ptw[i] = root_pow<false>(d, d.tw_log, (f * i) & emask);
+    }
     __syncthreads();
     const IdxT row_in0 = (IdxT)(f * d.fin + s_idx * d.sin);
     const IdxT row_out0 = (IdxT)(f * d.fout + s_idx * d.sout);
     // The schedule (make_sched) is 4-bit steps with the remainder last, so
     // only the last step can have a radix below 16.
     if (sc.n == 1) {
-        n2_step<4, true, true, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
+        n2_step<4, true, true, IdxT>(d, sc, sc.lgm[0], data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0);
         return;
     }
-    n2_step<4, true, false, IdxT>(d, sc, sc.lgm[0], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
+    if (d.half_zero)
+        n2_step<4, true, false, IdxT, true>(d, sc, sc.lgm[0], data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0);
+    else
+        n2_step<4, true, false, IdxT>(d, sc, sc.lgm[0], data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0);
     __syncthreads();
     if (sc.n == 3) {
-        n2_step<4, false, false, IdxT>(d, sc, sc.lgm[1], data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0);
+        n2_step<4, false, false, IdxT>(d, sc, sc.lgm[1], data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0);
         __syncthreads();
     }
     const uint32_t lgm = sc.n == 3 ? sc.lgm[2] : sc.lgm[1];
     switch (lgm) {
-        case 4: n2_step<4, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
-        case 3: n2_step<3, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
-        case 2: n2_step<2, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
-        default: n2_step<1, false, true, IdxT>(d, sc, lgm, data, tws, q, cc, logC, cok, row_in0, row_out0, f, col0); break;
+        case 4: n2_step<4, false, true, IdxT>(d, sc, lgm, data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0); break;
+        case 3: n2_step<3, false, true, IdxT>(d, sc, lgm, data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0); break;
+        case 2: n2_step<2, false, true, IdxT>(d, sc, lgm, data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0); break;
+        default: n2_step<1, false, true, IdxT>(d, sc, lgm, data, tws, ptw, q, cc, logC, cok, row_in0, row_out0, col0); break;
     }
 }
 
@@ -449,10 +479,13 @@ int run_pass2(PassDesc d, uint64_t S, cudaStream_t s) {
     const uint64_t blocks = d.F * S, cblocks = ceil_div(d.w, 1ull << logC);
     if (blocks * cblocks > 0x7FFFFFFFull) return (int)cudaErrorInvalidConfiguration;
     d.cgroups = (uint32_t)cblocks;
-    const size_t smem = 8ull * ((1ull << m) << logC) + 8ull * (1ull << m);
+    const size_t smem = 8ull * ((1ull << m) << logC) + 8ull * (1ull << m) * (d.tw_log ? 2 : 1);
     if (smem > 48 * 1024)
         ZK_TRY(cudaFuncSetAttribute(k_ntt_pass2<IdxT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const Sched sc = make_sched(m);
+    // first-step element e of a group reads row >= row_in0 + e 2^(m-4) jin, so
+    // with 2^(m-1) jin >= rows_valid every element e >= 8 is a padding row
+    d.half_zero = sc.n > 1 && (d.jin << (m - 1)) >= d.rows_valid ? 1u : 0u;
     const uint32_t threads = (1u << (m - 4)) << logC;
     k_ntt_pass2<IdxT><<<(unsigned)(blocks * cblocks), threads, smem, s>>>(d, sc);
     ZK_LAUNCH_CHECK();
