@@ -5,7 +5,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 SRC = os.path.join(HERE, "devcheck.cu")
 OUT = os.path.join(HERE, "_build", "libdevcheck.so")
-HDRS = [os.path.join(HERE, "..", "zkie_b200", "csrc", f) for f in ("gl64.cuh", "poseidon2.cuh")]
+HDRS = [os.path.join(HERE, "..", "zkie_b200", "csrc", f) for f in ("gl64.cuh", "poseidon2.cuh", "dft_reg.cuh")]
 
 
 def build() -> str:

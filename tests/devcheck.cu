@@ -9,6 +9,7 @@
 
 #include <cstdint>
 
+#include "../zkie_b200/csrc/dft_reg.cuh"
 #include "../zkie_b200/csrc/poseidon2.cuh"
 
 using namespace zk;
@@ -76,6 +77,19 @@ ZK_HD void state_op(int op, uint64_t s[16], const P2Const& c) {
             s[0] = a; s[1] = b; s[2] = x; s[3] = d;
             break;
         }
+        // in-register DFTs of the NTT passes: plain and lazy forms, radix 16
+        // (also with the upper half of the input zero), 8, 4 and 2 on
+        // consecutive groups of the state
+        case 110: dft_reg<4>(s); break;
+        case 111: dft_reg_lazy<4>(s); break;
+        case 112: dft_reg_half<4>(s); break;
+        case 113: dft_reg_half_lazy<4>(s); break;
+        case 114: dft_reg<3>(s); dft_reg<3>(s + 8); break;
+        case 115: dft_reg_lazy<3>(s); dft_reg_lazy<3>(s + 8); break;
+        case 116: for (int g = 0; g < 16; g += 4) dft_reg<2>(s + g); break;
+        case 117: for (int g = 0; g < 16; g += 4) dft_reg_lazy<2>(s + g); break;
+        case 118: for (int g = 0; g < 16; g += 2) dft_reg<1>(s + g); break;
+        case 119: for (int g = 0; g < 16; g += 2) dft_reg_lazy<1>(s + g); break;
         default: break;
     }
 }

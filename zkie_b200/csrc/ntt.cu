@@ -22,6 +22,7 @@
 #include "../../include/zkie_goldilocks_cuda.h"
 #include "../../include/zkie2.h"
 #include "common.cuh"
+#include "dft_reg.cuh"
 #include "gl64.cuh"
 #include "internal.h"
 
@@ -244,72 +245,6 @@ struct Sched {
     uint32_t lgm[4];  // log2 of the sub-problem size M_i at step i
 };
 
-template <int L>
-__device__ __forceinline__ constexpr int brev_c(int i) {
-    int r = 0;
-    for (int b = 0; b < L; b++)
-        if ((i >> b) & 1) r |= 1 << (L - 1 - b);
-    return r;
-}
-
-// Butterfly (a, b) <- (a + W b, a - W b) with W = 2^K.
-template <int K>
-__device__ __forceinline__ void bfly_pow2(uint64_t& a, uint64_t& b) {
-    const uint64_t t = GlPow2<K>::mag(b), u = a;
-    if (GlPow2<K>::neg) {
-        a = gl_sub(u, t);
-        b = gl_add(u, t);
-    } else {
-        a = gl_add(u, t);
-        b = gl_sub(u, t);
-    }
-}
-
-// Butterfly I of DIT stage S (1-based) of a 2^L-point transform on
-// bit-reversed input: rows a, a + 2^(S-1), twiddle W_{2^S}^j.
-template <int S, int I>
-__device__ __forceinline__ void dit_bfly(uint64_t* y) {
-    constexpr int h = 1 << (S - 1), j = I % h, a = (I / h) * 2 * h + j;
-    constexpr int K = ((39 << (6 - S)) * j) % 192;
-    bfly_pow2<K>(y[a], y[a + h]);
-}
-template <int S, int... I>
-__device__ __forceinline__ void dit_stage(uint64_t* y, std::integer_sequence<int, I...>) {
-    (dit_bfly<S, I>(y), ...);
-}
-template <int L, int... S>
-__device__ __forceinline__ void dit_stages(uint64_t* y, std::integer_sequence<int, S...>) {
-    (dit_stage<S + 1>(y, std::make_integer_sequence<int, (1 << (L - 1))>{}), ...);
-}
-// x[e] <- sum_d x[d] W_{2^L}^(d e), natural order in and out.
-template <int L>
-__device__ __forceinline__ void dft_reg(uint64_t* x) {
-    constexpr int R = 1 << L;
-    uint64_t y[R];
-#pragma unroll
-    for (int i = 0; i < R; i++) y[i] = x[brev_c<L>(i)];
-    dit_stages<L>(y, std::make_integer_sequence<int, L>{});
-#pragma unroll
-    for (int i = 0; i < R; i++) x[i] = y[i];
-}
-
-template <int L, int... S>
-__device__ __forceinline__ void dit_stages_from2(uint64_t* y, std::integer_sequence<int, S...>) {
-    (dit_stage<S + 2>(y, std::make_integer_sequence<int, (1 << (L - 1))>{}), ...);
-}
-// dft_reg for inputs whose upper half is zero: after the bit reversal those
-// sit at the odd positions, so the first DIT stage (twiddle 1) is a copy.
-template <int L>
-__device__ __forceinline__ void dft_reg_half(uint64_t* x) {
-    constexpr int R = 1 << L;
-    uint64_t y[R];
-#pragma unroll
-    for (int i = 0; i < R; i += 2) y[i] = y[i + 1] = x[brev_c<L>(i)];
-    dit_stages_from2<L>(y, std::make_integer_sequence<int, L - 1>{});
-#pragma unroll
-    for (int i = 0; i < R; i++) x[i] = y[i];
-}
-
 // Output index of the last step's group gam: the digit of step i sits at bits
 // [lgm_i - lg_i, lgm_i) of the position and goes to bits
 // [lg_0 + ... + lg_{i-1}, ...) of k; the last step's own digit is added by
@@ -362,9 +297,9 @@ __device__ __forceinline__ void n2_step(const PassDesc& d, const Sched& sc, uint
             for (int e = 0; e < R; e++) x[e] = p[e * st];
         }
         if (kHalf)
-            dft_reg_half<L>(x);
+            dft_reg_half_lazy<L>(x);
         else
-            dft_reg<L>(x);
+            dft_reg_lazy<L>(x);
         if (!kOut) {
             // W_{M_i}^(j' e) = W_M^(j' e 2^(m - lgm))
             const uint32_t tsh = m - lgm;
