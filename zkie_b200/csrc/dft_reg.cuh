@@ -79,10 +79,18 @@ ZK_HD void dft_reg_half(uint64_t* x) {
 // ---- lazy butterflies -----------------------------------------------------------------
 // The same DIT network on 96-bit accumulators: a butterfly adds and subtracts
 // without reducing, and only a value about to be multiplied by a shift
-// twiddle, and each output, is reduced.  Values entering stage S are below
+// twiddle (and only where the shifted value would not fit 128 bits), and
+// each output, is reduced.  Values entering stage S are below
 // B_S 2^64 with B_1 = 1 and B_(S+1) = 2 B_S + 1 (31 after four stages):
 // a difference u - t is formed as u + c p - t with c p > t, namely
 // c = B + 1 for an unreduced t < B 2^64 and c = 2 for a reduced t < 2^64.
+
+// ceil(log2(x)) for x >= 1
+ZK_HD constexpr int clog2_c(int x) {
+    int r = 0;
+    while ((1 << r) < x) r++;
+    return r;
+}
 
 // c p as an accumulator, 1 <= c <= 2^31: (c - 1) 2^64 + (2^64 - c (2^32 - 1))
 template <int C>
@@ -98,7 +106,14 @@ ZK_HD void bfly_lazy(Acc& a, Acc& b) {
         s = acc_add(u, b);                              // below 2B
         d = acc_sub(acc_add(u, acc_pmul<B + 1>()), b);  // below 2B + 1
     } else {
-        const uint64_t t = GlPow2<K>::mag(acc_reduce(b));
+        constexpr int Kp = K % 96;
+        uint64_t t;
+        if constexpr (Kp < 64 && Kp + clog2_c(B) <= 64) {
+            // b 2^Kp as a 128-bit value: its high word, below B 2^Kp, fits
+            t = gl_reduce128(b.lo << Kp, (b.lo >> (64 - Kp)) | ((uint64_t)b.hi << Kp));
+        } else {
+            t = GlPow2<K>::mag(acc_reduce(b));
+        }
         s = acc_add(u, t);                                   // below B + 1
         d = acc_sub(acc_add(u, acc_pmul<2>()), Acc{t, 0u});  // below B + 2
     }
