@@ -57,6 +57,31 @@ def test_split_commit_emulated_root(zk, lg_l, lg_b, w, G):
     assert np.array_equal(root, np.asarray(want, dtype=np.uint64))
 
 
+def test_split_committer_run_host_single_rank(zk):
+    """SplitCommitter.run_host without a process group (one rank): pinned
+    input slice in, the LDE downloaded on a side stream while the rows are
+    hashed, the digest layers back; two calls in a row, each equal to the
+    device commit."""
+    from zkie_b200.multigpu import SplitCommitter
+    lg_l, lg_b, w = 14, 1, 32
+    x = coeffs(77, 1 << lg_l, w)
+    want = zk.commit(torch.from_numpy(x).cuda(), lg_b)
+    want_lde = want.lde.reshape(-1).view(torch.int64).cpu()
+    want_layers = want.layers.view(torch.int64).cpu()
+    H = 1 << (lg_l + lg_b)
+    sc = SplitCommitter(lg_l, lg_b, w)
+    h_part = torch.from_numpy(x.view(np.int64).reshape(-1).copy()).pin_memory()
+    h_lde = torch.empty(H * w, dtype=torch.int64).pin_memory()
+    h_layers = torch.empty(zk.lib.zkie2_merkle_total_digests(H) * 8, dtype=torch.int64).pin_memory()
+    for _ in range(2):
+        h_lde.zero_()
+        h_layers.zero_()
+        root = sc.run_host(h_part, h_lde, h_layers)
+        assert torch.equal(h_lde, want_lde)
+        assert torch.equal(h_layers, want_layers)
+        assert np.array_equal(np.asarray(root).view(np.uint64), np.asarray(want.root, dtype=np.uint64))
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

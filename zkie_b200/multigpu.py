@@ -223,6 +223,8 @@ class SplitCommitter:
         self.roots = torch.empty(self.G * 8, dtype=torch.int64, device=self.lde.device)
         self.top = empty(lib.zkie2_merkle_total_digests(self.G) * 8)
         self.full_in = None
+        self.copy_stream = None
+        self.events = None
 
     def run(self, coeffs, events=None):
         """One split commit; events (if given) are recorded after the LDE, the
@@ -263,13 +265,22 @@ class SplitCommitter:
         if self.full_in is None:
             self.full_in = empty(L * self.w)
             self.part = empty(L * self.w // self.G)
+        if self.copy_stream is None:
+            self.copy_stream = torch.cuda.Stream(device=self.lde.device)
+            self.events = [torch.cuda.Event() for _ in range(4)]
+        cur = torch.cuda.current_stream()
         self.part.view(torch.int64).copy_(h_part.view(torch.int64), non_blocking=True)
         if self.G > 1:
             dist.all_gather_into_tensor(self.full_in.view(torch.int64), self.part.view(torch.int64), group=self.group)
         else:
             self.full_in.copy_(self.part)
-        self.run(self.full_in)
-        h_lde.view(torch.int64).copy_(self.lde.view(torch.int64), non_blocking=True)
+        self.run(self.full_in, self.events)
+        # the LDE download overlaps the hashing: the copy stream starts once
+        # the LDE is complete (events[0]); the hashing only reads the LDE
+        self.copy_stream.wait_event(self.events[0])
+        with torch.cuda.stream(self.copy_stream):
+            h_lde.view(torch.int64).copy_(self.lde.view(torch.int64), non_blocking=True)
         h_layers.view(torch.int64).copy_(self.layers.view(torch.int64), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        cur.synchronize()
+        self.copy_stream.synchronize()
         return self.root()
