@@ -27,11 +27,13 @@ bool g_p2_ready[kMaxDevices];
 
 constexpr int kHashThreads = 128;
 // Up to this many states per launch the four-threads-per-state kernels run:
-// 4 x 2^16 threads fit the GPU in under one wave, so the launch is bound by
-// one permutation's latency, which the cooperative form cuts by about 3x.
-// Larger launches are throughput-bound and take one thread per state
-// (fewer instructions per permutation).
-constexpr uint64_t kX4MaxStates = 1ull << 16;
+// such a launch is bound by one permutation's latency, which the
+// cooperative form cuts by about 3x.  Larger launches take one thread per
+// state (fewer instructions per permutation).  Measured on the bench's tree
+// and the configuration-1 shard: the crossover lies between 2^12 and 2^14
+// states (2^16 was 13 % slower on the shard, whose 2^16-row leaf launch is
+// throughput-bound).
+constexpr uint64_t kX4MaxStates = 1ull << 14;
 
 // Leaf digests of rows [row0, row_end): sponge with rate 8, overwrite mode,
 // one permutation per full 8-block and one after a partial tail
