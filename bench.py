@@ -584,7 +584,7 @@ def measured_traffic(lg_l, w, lg_b, world):
     from one single-pass ncu capture of this exact workload (the command is in
     profiles/traffic__bench_cfg2_256x2^20_b2.md); null for other workloads."""
     if (lg_l, w, lg_b, world) == (20, 256, 1, 1):
-        return {"leaf": 4309188608 + 131260928, "ntt": 2148577024 + 4261442048 + 4295237120 + 4255394304,
+        return {"leaf": 4310624256 + 131658752, "ntt": 2149098240 + 4298085632 + 4295429120 + 4260205056,
                 "src": "ncu single-pass capture of this workload, profiles/traffic__bench_cfg2_256x2^20_b2.md"}
     return {"leaf": None, "ntt": None, "src": None}
 
