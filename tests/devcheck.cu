@@ -90,6 +90,10 @@ ZK_HD void state_op(int op, uint64_t s[16], const P2Const& c) {
         case 117: for (int g = 0; g < 16; g += 4) dft_reg_lazy<2>(s + g); break;
         case 118: for (int g = 0; g < 16; g += 2) dft_reg<1>(s + g); break;
         case 119: for (int g = 0; g < 16; g += 2) dft_reg_lazy<1>(s + g); break;
+        // radix 16 with only the first 4, 2 or 1 inputs nonzero
+        case 120: dft_reg_zero_lazy<4, 2>(s); break;
+        case 121: dft_reg_zero_lazy<4, 3>(s); break;
+        case 122: dft_reg_zero_lazy<4, 4>(s); break;
         default: break;
     }
 }

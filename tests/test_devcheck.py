@@ -19,10 +19,11 @@ SCALAR_OPS = {0: "add", 1: "add_c", 2: "sub", 3: "mul", 4: "sqr", 5: "div2", 6: 
 POW2_K = {16: 1, 17: 33, 18: 63, 19: 64, 20: 95, 21: 96, 22: 120, 23: 156, 24: 191, 25: 39}
 STATE_OPS = {105: "mat4", 100: "mds_light", 101: "ext_round0", 102: "internal_linear", 103: "int_round0",
              104: "permute", 110: "dft16", 111: "dft16_lazy", 112: "dft16_half", 113: "dft16_half_lazy",
-             114: "dft8", 115: "dft8_lazy", 116: "dft4", 117: "dft4_lazy", 118: "dft2", 119: "dft2_lazy"}
-# state op -> (log2 radix, upper half of each group zero)
-DFT_OPS = {110: (4, False), 111: (4, False), 112: (4, True), 113: (4, True), 114: (3, False), 115: (3, False),
-           116: (2, False), 117: (2, False), 118: (1, False), 119: (1, False)}
+             114: "dft8", 115: "dft8_lazy", 116: "dft4", 117: "dft4_lazy", 118: "dft2", 119: "dft2_lazy",
+             120: "dft16_quarter_lazy", 121: "dft16_eighth_lazy", 122: "dft16_first_only_lazy"}
+# state op -> (log2 radix, log2 of the zero fraction: inputs e >= 2^lg >> z of each group are zero)
+DFT_OPS = {110: (4, 0), 111: (4, 0), 112: (4, 1), 113: (4, 1), 114: (3, 0), 115: (3, 0),
+           116: (2, 0), 117: (2, 0), 118: (1, 0), 119: (1, 0), 120: (4, 2), 121: (4, 3), 122: (4, 4)}
 
 
 @pytest.fixture(scope="module")
@@ -102,15 +103,16 @@ def test_host_permutation_matches_oracle(dc, orc):
         assert np.array_equal(np.array([x % P for x in out[i].tolist()], dtype=np.uint64), orc.p2_permute(cs, st[i]))
 
 
-def _dft_expected(x, lg, half):
-    """Natural-order DFT of each 2^lg group, W_(2^lg) = 2^(39 * 2^(6 - lg) mod 192)."""
+def _dft_expected(x, lg, z):
+    """Natural-order DFT of each 2^lg group, W_(2^lg) = 2^(39 * 2^(6 - lg) mod 192),
+    with the inputs e >= 2^lg >> z of each group taken as zero."""
     r = 1 << lg
     w = pow(2, (39 << (6 - lg)) % 192, P)
     out = []
     for g in range(0, 16, r):
         grp = [int(v) % P for v in x[g:g + r]]
-        if half:
-            grp = grp[:r // 2] + [0] * (r // 2)
+        if z:
+            grp = grp[:r >> z] + [0] * (r - (r >> z))
         out += [sum(grp[d] * pow(w, d * e, P) for d in range(r)) % P for e in range(r)]
     return out
 
@@ -126,12 +128,12 @@ def test_host_register_dfts_match_definition(dc, orc):
     st[2] = np.uint64(P - 1)
     st[3, ::2] = np.uint64(M64 - 1)
     st[4] = np.uint64(P)
-    for op, (lg, half) in DFT_OPS.items():
+    for op, (lg, z) in DFT_OPS.items():
         out = st.copy()
         dc.hostcheck_state(op, _p(out), 64, _p(c))
         for i in range(64):
             got = [int(v) % P for v in out[i].tolist()]
-            assert got == _dft_expected(st[i].tolist(), lg, half), (STATE_OPS[op], i)
+            assert got == _dft_expected(st[i].tolist(), lg, z), (STATE_OPS[op], i)
 
 
 @pytest.mark.gpu

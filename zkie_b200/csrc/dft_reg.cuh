@@ -153,16 +153,28 @@ ZK_HD void dft_reg_lazy(uint64_t* x) {
 #pragma unroll
     for (int i = 0; i < R; i++) x[i] = acc_reduce(y[i]);
 }
-// dft_reg_half on accumulators
-template <int L>
-ZK_HD void dft_reg_half_lazy(uint64_t* x) {
-    constexpr int R = 1 << L;
+// dft_reg_lazy for inputs e >= R / 2^Z all zero (1 <= Z <= L): after the bit
+// reversal the nonzero inputs sit at the positions whose low Z bits are
+// zero, and the first Z DIT stages spread each over its block of 2^Z (the
+// DFT of a delta is constant), so they are copies.
+template <int L, int Z>
+ZK_HD void dft_reg_zero_lazy(uint64_t* x) {
+    constexpr int R = 1 << L, S = 1 << Z;
     Acc y[R];
 #pragma unroll
-    for (int i = 0; i < R; i += 2) y[i] = y[i + 1] = acc_of(x[brev_c<L>(i)]);
-    dit_stages_lazy<2, L, 1>(y);
+    for (int i = 0; i < R; i += S) {
+        const Acc v = acc_of(x[brev_c<L>(i)]);
+#pragma unroll
+        for (int k = 0; k < S; k++) y[i + k] = v;
+    }
+    dit_stages_lazy<Z + 1, L, 1>(y);
 #pragma unroll
     for (int i = 0; i < R; i++) x[i] = acc_reduce(y[i]);
+}
+// the upper half zero
+template <int L>
+ZK_HD void dft_reg_half_lazy(uint64_t* x) {
+    dft_reg_zero_lazy<L, 1>(x);
 }
 
 }  // namespace zk
