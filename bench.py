@@ -41,6 +41,7 @@ UNIT = "Melem/s"
 P = 0xFFFFFFFF00000001
 LG_L, W, LG_B = 20, 256, 1
 HBM_FALLBACK_GBS = 6650.0
+CPU_LABEL = "C restatement, not the reference binary"
 MULS_PER_PERM = 8 * 16 * 4 + 22 * 4 + 22
 
 
@@ -105,7 +106,7 @@ def cpu_sample_rows(w, lg_b, target_s):
 def cpu_baseline(w, lg_b, target_s=10.0):
     lg_rows = cpu_sample_rows(w, lg_b, target_s)
     rate, dt = cpu_commit_rate(lg_rows, w, lg_b)
-    return {"value": round(rate, 3), "unit": UNIT, "cores": host_threads(), "kind": "port",
+    return {"value": round(rate, 3), "unit": UNIT, "cores": host_threads(), "kind": "port", "label": CPU_LABEL,
             "sample": f"oracle/zkie_oracle.c LDE + Merkle of {w} polys x 2^{lg_rows} coeffs (blowup {1 << lg_b}), "
                       f"OpenMP over {host_threads()} host threads, {dt:.1f} s"}
 
@@ -129,7 +130,7 @@ def run_reference(args):
         "warmup": args.warmup, "ms_per_step": round(1e3 * sum(times) / len(times), 3), "higher_is_better": True,
         "scaling": "weak" if args.gpus == 1 else "strong", "vs_baseline": None, "dtype": "u64 (Goldilocks)",
         "data": "synthetic", "impl": "reference", "config": cfg,
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": host_threads(), "kind": "port",
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": host_threads(), "kind": "port", "label": CPU_LABEL,
                          "sample": f"{args.polys} polys x 2^{lg_rows} coeffs per step (bounded sample of the "
                                    f"workload), oracle/zkie_oracle.c on all host threads"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -140,12 +141,16 @@ def run_reference(args):
 
 # ---- clocks ------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("timestamp,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi samples (every 200 ms) of the ONE GPU this rank runs on,
+    matched by UUID or PCI bus id; the median SM clock is taken over the
+    samples inside the timed region in which that GPU was busy."""
+    FIELDS = ("timestamp,uuid,pci.bus_id,utilization.gpu,clocks.sm,clocks.max.sm,power.draw,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, bus_id):
-        self.bus = bus_id.lower()[-12:] if bus_id else ""
+    def __init__(self, ident):
+        self.uuid, self.bus = ident
         self.proc = None
         self.rows = []
 
@@ -163,7 +168,7 @@ class ClockSampler:
         import datetime
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 11:
                 try:
                     ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
                 except ValueError:
@@ -173,25 +178,41 @@ class ClockSampler:
     def window(self, t0, t1):
         self.t0, self.t1 = t0, t1
 
+    def _mine(self, row):
+        uuid, bus = row[1].lower(), row[2].upper()
+        if self.uuid and uuid.endswith(self.uuid):
+            return True
+        return bool(self.bus) and bus.endswith(self.bus)
+
     def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "gpu_match": "nvidia-smi unavailable"}
         time.sleep(0.3)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        mine = [r for r in self.rows if not self.bus or r[1].lower().endswith(self.bus)] or self.rows
+        mine = [r for r in self.rows if self._mine(r)]
+        if not mine:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "gpu_match": "unmatched",
+                    "gpu": {"uuid": self.uuid, "pci_bus_id": self.bus}}
         t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", 1e30)
         inside = [r for r in mine if t0 - 0.25 <= r[0] <= t1 + 0.25]
-        use = inside or mine
-        sm = [float(r[2]) for r in use if r[2].replace(".", "").isdigit()]
-        mx = [float(r[3]) for r in use if r[3].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in use for i in range(4) if r[5 + i].lower() == "active"})
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        busy = [r for r in inside if (num(r[3]) or 0) > 0]
+        use = busy or inside or mine
+        sm = [v for v in (num(r[4]) for r in use) if v is not None]
+        mx = [v for v in (num(r[5]) for r in use) if v is not None]
+        reasons = sorted({self.REASONS[i] for r in use for i in range(4) if r[7 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples_in_timed_region": len(inside), "samples": len(use)}
+                "reasons": reasons, "samples_in_timed_region": len(inside), "samples_busy": len(busy),
+                "samples": len(use), "gpu_match": "uuid/pci", "gpu": {"uuid": self.uuid, "pci_bus_id": self.bus}}
 
 
 # ---- GPU side -------------------------------------------------------------------------------------
@@ -249,14 +270,18 @@ def hbm_peak_gbs():
     return HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
 
 
-def bus_id(dev):
+def gpu_ident(dev):
+    """(uuid, PCI bus id) of this rank's GPU in nvidia-smi's forms: torch's
+    pci_bus_id is the bus NUMBER, so the "DDDDDDDD:BB:DD.0" string is built
+    from the domain, bus and device numbers."""
     import torch
     props = torch.cuda.get_device_properties(dev)
-    bus = getattr(props, "pci_bus_id", None)
-    if bus is None:
-        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", 0),
-                                     getattr(props, "pci_device_id", 0))
-    return str(bus)
+    uuid = str(getattr(props, "uuid", "") or "").lower()
+    try:
+        bus = "%08X:%02X:%02X.0" % (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
+    except (AttributeError, TypeError, ValueError):
+        bus = ""
+    return uuid, bus
 
 
 def max_over_ranks(x, dev):
@@ -290,7 +315,7 @@ def main_split(args, zk, dev, world, rank):
     for _ in range(args.warmup):
         sc.run(d_in)
     torch.cuda.synchronize()
-    sampler = ClockSampler(bus_id(dev))
+    sampler = ClockSampler(gpu_ident(dev))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
@@ -459,7 +484,7 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    sampler = ClockSampler(bus_id(dev))
+    sampler = ClockSampler(gpu_ident(dev))
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -581,11 +606,12 @@ def main():
 
 def measured_traffic(lg_l, w, lg_b, world):
     """dram__bytes_read.sum + dram__bytes_write.sum of the dominant launches,
-    from one single-pass ncu capture of this exact workload (the command is in
-    profiles/traffic__bench_cfg2_256x2^20_b2.md); null for other workloads."""
+    from one single-pass ncu capture of this exact workload; null for other
+    workloads."""
     if (lg_l, w, lg_b, world) == (20, 256, 1, 1):
         return {"leaf": 4310624256 + 131658752, "ntt": 2149098240 + 4298085632 + 4295429120 + 4260205056,
-                "src": "ncu single-pass capture of this workload, profiles/traffic__bench_cfg2_256x2^20_b2.md"}
+                "src": "dram__bytes_read.sum + dram__bytes_write.sum from one single-pass ncu capture of this "
+                       "workload (a constant of that capture, not measured in this run)"}
     return {"leaf": None, "ntt": None, "src": None}
 
 
@@ -596,7 +622,7 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
     a 2^18-fraction tree; a 16-bit grind)."""
     import types
 
-    from zkie_b200.perfcases import case_fixed, case_grind, case_logup
+    from perfcases import case_fixed, case_grind, case_logup
     lg = case_logup(types.SimpleNamespace(log_size=lg_frac, iters=5))
     gr = case_grind(types.SimpleNamespace(log_size=grind_bits, iters=3))
     fm = case_fixed(types.SimpleNamespace(m=512, k=1024, n=4096, iters=5))
@@ -624,14 +650,14 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
         orc.fractional_prove(num, den, list(range(3, 21)), list(range(5, 23)))
         s_frac = time.perf_counter() - t0
         out["logup"]["cpu_baseline"] = {"value": round(n / s_frac / 1e6, 4), "unit": "Mfractions/s", "cores": 1,
-                                        "kind": "port", "sample": "2^18-fraction tree, oracle/zkie_oracle.c"}
+                                        "kind": "port", "label": CPU_LABEL, "sample": "2^18-fraction tree, oracle/zkie_oracle.c"}
         consts = orc.p2_constants(1)
         sponge = [(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(16)]
         t0 = time.perf_counter()
         w = orc.grind(consts, sponge, [5, 6, 7], 16)
         s_grind = time.perf_counter() - t0
         out["grind"]["cpu_baseline"] = {"value": round((w + 1) / s_grind / 1e6, 4), "unit": "M candidates/s",
-                                        "cores": 1, "kind": "port",
+                                        "cores": 1, "kind": "port", "label": CPU_LABEL,
                                         "sample": f"16-bit grind from the same state ({w + 1} candidates)"}
         a = g.integers(-(1 << 15), 1 << 15, size=(16, 1024), dtype=np.int64)
         b = g.integers(-(1 << 15), 1 << 15, size=(1024, 4096), dtype=np.int64)
@@ -642,7 +668,7 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
         orc.matmul_field(fa, fb)
         s_mm = time.perf_counter() - t0
         out["forward_matmul"]["cpu_baseline"] = {"value": round(16 * 1024 * 4096 / s_mm / 1e9, 4), "unit": "G MAC/s",
-                                                 "cores": host_threads(), "kind": "port",
+                                                 "cores": host_threads(), "kind": "port", "label": CPU_LABEL,
                                                  "sample": "16 x 1024 @ 1024 x 4096, oracle field matmul (OpenMP)"}
     return out
 

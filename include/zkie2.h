@@ -115,8 +115,11 @@ int zkie2_commit_extension(const uint64_t *d_evals, uint32_t n, uint32_t log_inv
 /* Host-buffer commit (the drop-in path of CudaDft::dft_batch followed by
  * CudaMerkleTreeMmcs::commit): h_coeffs L x w in, root (8 u64) out, plus the
  * LDE ((L << lg_blowup) x w) and all digest layers when those pointers are
- * non-null.  Synchronous.  Allocates its device buffers from the current
- * device's stream-ordered memory pool. */
+ * non-null.  Synchronous.  Allocates its device buffers from a memory pool
+ * the library creates for the current device on the first call (freed blocks
+ * stay cached in that pool for the next call; the device's default pool is
+ * left as it was).  Calls on one device are serialised inside the library:
+ * a second host thread blocks until the first call has returned. */
 int zkie2_commit_host(const uint64_t *h_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
                       uint64_t *h_lde, uint64_t *h_layers, uint64_t *h_root);
 

@@ -1,18 +1,19 @@
-"""Timed cases for the kernel families of libzkie_b200 (used for profiling).
+"""Timed cases for the kernel families of libzkie_b200: the reproduction recipe
+of the profiles (run from the repository root).
 
-    python -m zkie_b200.perfcases sumcheck --log-size 24
-    python -m zkie_b200.perfcases mle --log-size 24
-    python -m zkie_b200.perfcases matmul --m 512 --k 1024 --n 4096
-    python -m zkie_b200.perfcases commit --log-size 16 --polys 256 --lg-blowup 1
-    python -m zkie_b200.perfcases virtual --log-size 21
-    python -m zkie_b200.perfcases logup --log-size 24
-    python -m zkie_b200.perfcases grind --log-size 24
-    python -m zkie_b200.perfcases fixed --m 512 --k 1024 --n 4096
-    python -m zkie_b200.perfcases cache --log-size 25
-    python -m zkie_b200.perfcases sop --log-size 20 --polys 4
-    python -m zkie_b200.perfcases shard --m 16 --k 1024 --n 1024
-    python -m zkie_b200.perfcases split --log-size 18 --polys 32 --gpus 4
-    python -m zkie_b200.perfcases sweep
+    python perfcases.py sumcheck --log-size 24
+    python perfcases.py mle --log-size 24
+    python perfcases.py matmul --m 512 --k 1024 --n 4096
+    python perfcases.py commit --log-size 16 --polys 256 --lg-blowup 1
+    python perfcases.py virtual --log-size 21
+    python perfcases.py logup --log-size 24
+    python perfcases.py grind --log-size 24
+    python perfcases.py fixed --m 512 --k 1024 --n 4096
+    python perfcases.py cache --log-size 25
+    python perfcases.py sop --log-size 20 --polys 4
+    python perfcases.py shard --m 16 --k 1024 --n 1024
+    python perfcases.py split --log-size 18 --polys 32 --gpus 4
+    python perfcases.py sweep
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -21,13 +22,16 @@ uniform canonical field elements.
 """
 import argparse
 import json
+import os
 import sys
 
 import numpy as np
 import torch
 
-from . import _lib
-from ._lib import check, lib
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from zkie_b200 import _lib  # noqa: E402
+from zkie_b200._lib import check, lib  # noqa: E402
 
 P = 0xFFFFFFFF00000001
 
@@ -183,7 +187,7 @@ def case_grind(a):
     """PoW grinding (zkie2_grind) at --log-size bits from a fixed challenger
     state; the candidate count is data-dependent, so the rate is reported per
     candidate tried (the smallest witness + 1, one permutation each)."""
-    from .pow import grind
+    from zkie_b200.pow import grind
     sponge = [(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(16)]
     w = {}
 
@@ -240,8 +244,8 @@ def case_cache(a):
     import tempfile
     import time
 
-    from .cache import BatchCacheMetadata, read_cache, write_cache
-    from .commit import Whir
+    from zkie_b200.cache import BatchCacheMetadata, read_cache, write_cache
+    from zkie_b200.commit import Whir
     n = a.log_size
     com = Whir(n).commit(_rand(1 << n, 50))
     rows = com.lde.numel() // 32
@@ -285,7 +289,7 @@ def case_sop(a):
 def case_shard(a):
     """zkie2_shard_prove_matmul at BASELINE configuration 1 (16 x 1024 x 1024,
     entries uniform in [-2^15, 2^15) embedded in the field)."""
-    from .gkr import ShardProver
+    from zkie_b200.gkr import ShardProver
     m, k, n = a.m, a.k, a.n
     g = np.random.default_rng(5)
 
@@ -305,7 +309,7 @@ def case_shard(a):
 def case_split(a):
     """The split commit over `gpus` ranks emulated on this one GPU (every
     rank's coset LDE, leaf hashes, digest interleave and subtree in turn)."""
-    from .multigpu import split_commit_emulated
+    from zkie_b200.multigpu import split_commit_emulated
     lg_l, w, lb, G = a.log_size, a.polys, a.lg_blowup, a.gpus
     d_in = _rand((1 << lg_l) * w, 8)
 

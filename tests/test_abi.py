@@ -107,6 +107,10 @@ def test_scratch_queries(zk):
     assert L.zkie2_whir_scratch_elems(20) == 32 << 16
     assert L.zkie2_matmul_scratch_elems(16, 1024, 1024) > 0
     assert L.zkie2_matmul_scratch_elems(3, 4, 4) == 0        # not a power of two
+    # shapes the tensor path cannot take need no tensor-path scratch (field kernel)
+    assert L.zkie2_matmul_fixed_scratch_elems(16, 40, 16) == 1       # k % 16 != 0
+    assert L.zkie2_matmul_fixed_scratch_elems(16, 1 << 21, 16) == 1  # k / 32 = 65536 > grid.y limit
+    assert L.zkie2_matmul_fixed_scratch_elems(16, 65535 * 32, 16) > 1
 
 
 def test_device_count_without_gpu(zk):

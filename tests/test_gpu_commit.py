@@ -164,9 +164,11 @@ def test_whir_commit_batch_stacks_tables(zk, orc, consts):
 
 # ---- BASELINE-sized cases: size-independent checks ------------------------------------------------
 @pytest.mark.slow
-@pytest.mark.parametrize("lg_l,lb,w", [(16, 1, 256), (20, 1, 16), (16, 2, 16), (20, 2, 1), (24, 1, 1)])
+@pytest.mark.parametrize("lg_l,lb,w", [(16, 1, 256), (20, 1, 16), (16, 2, 16), (20, 2, 1), (24, 1, 1),
+                                        (20, 1, 256), (20, 2, 256), (24, 2, 16)])
 def test_commit_sweep_sampled(zk, orc, consts, lg_l, lb, w):
-    """Raw commit sweep shapes: sampled LDE rows against
+    """Raw commit sweep shapes (the benched 256 x 2^20 at
+    blowup 2 and the blowup-4 cases included): sampled LDE rows against
     Horner evaluation, sampled leaves against the oracle sponge, and the
     whole tree above the leaves rebuilt by the oracle from the GPU leaves."""
     m = rand_mat_fast(lg_l * 7 + lb + w, 1 << lg_l, w)

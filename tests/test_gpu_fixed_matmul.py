@@ -88,3 +88,15 @@ def test_unaligned_a_pointer_uses_field(zk):
                                        scr.data_ptr(), torch.cuda.current_stream().cuda_stream), "matmul_fixed")
     assert path.value == 1
     assert np.array_equal(dc.cpu().numpy(), zk.matmul_field(a, b, m, k, n).cpu().numpy())
+
+
+def test_tall_field_matmul_runs_in_row_blocks(zk, orc):
+    """More rows than one launch's grid.y (65535): the field kernel runs row
+    blocks, as the reference's field matmul computes any shape."""
+    m, k, n = 2 * 65535 + 3, 8, 4
+    a, b = fixed(14, (m, k)), fixed(15, (k, n))
+    got = zk.matmul_field(a, b, m, k, n).cpu().numpy().reshape(m, n)
+    assert np.array_equal(got, orc.matmul_field(a, b))
+    got, path = zk.matmul_fixed(a, b, m, k, n, force_tensor=True)
+    assert path == 1  # k % 16 != 0: the field kernel
+    assert np.array_equal(got.cpu().numpy().reshape(m, n), orc.matmul_field(a, b))

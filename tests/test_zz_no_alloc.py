@@ -4,9 +4,10 @@ It exists for callers that cannot allocate device memory (a prover living
 next to a framework allocator that already holds the GPU's memory, or a
 latency-critical caller that cannot take cudaFree's device-wide sync).  Its
 scratch is a fixed array inside the library, shared by every call.  This test
-calls it through the C ABI twice in a row, with different inputs each time so
-stale contents from the first call would show, and checks both results
-bit-exactly against the allocating entry point zkie2_sumcheck_prove.  It sits
+calls it through the C ABI several times in a row, with different inputs each
+time so stale contents from an earlier call would show, at sizes from no
+variables to the largest the array holds, and checks every result bit-exactly
+against the allocating entry point zkie2_sumcheck_prove.  It sits
 in its own file so that pytest collects it last."""
 import ctypes as C
 
@@ -30,9 +31,12 @@ def _p(a):
 def test_noalloc_sumcheck_matches_allocating_entry_point(zk):
     import torch
     lib = zk.lib
-    assert lib.zkie2_sumcheck_noalloc_max_vars() == 24
+    t_max = lib.zkie2_sumcheck_noalloc_max_vars()
+    assert t_max == 24
     stream = torch.cuda.current_stream().cuda_stream
-    for call, t in enumerate((18, 14)):
+    # t_max fills the fixed array to its end (round polynomials and finals sit
+    # last); t = 0 has no rounds, only the two canonicalised values
+    for call, t in enumerate((18, 14, 0, t_max)):
         f = _fields(10 + call, 1 << t)
         h = _fields(20 + call, 1 << t)
         ch = _fields(30 + call, t)

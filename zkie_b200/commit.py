@@ -147,20 +147,23 @@ class CudaMerkleTreeMmcs:
         layers = split_layers(flat, h)
         return MerkleTree(layers, layers[-1][0].copy())
 
-    def commit_reference_sequence(self, mat) -> MerkleTree:
+    def commit_reference_sequence(self, mat, ffi=None) -> MerkleTree:
+        """``ffi``: another library exporting the same seven C symbols (the
+        parity tests pass the reference's own kernels); default: this one."""
+        lib_ = lib if ffi is None else ffi
         mat = np.asarray(mat, dtype=np.uint64)
         h, w = mat.shape
         lens = merkle_layer_lengths(h)
         d_mat = to_dev(mat)
         d_layers = [torch.zeros(n * DIGEST_ELEMS, dtype=torch.uint64, device=d_mat.device) for n in lens]
         batches = h // 8
-        check(lib.zkie_p2_leaf_batch(ptr(d_mat), ptr(d_layers[0]), h, w), "zkie_p2_leaf_batch")
-        check(lib.zkie_p2_leaf_scalar(ptr(d_mat), ptr(d_layers[0]), batches * 8, h, w), "zkie_p2_leaf_scalar")
+        check(lib_.zkie_p2_leaf_batch(ptr(d_mat), ptr(d_layers[0]), h, w), "zkie_p2_leaf_batch")
+        check(lib_.zkie_p2_leaf_scalar(ptr(d_mat), ptr(d_layers[0]), batches * 8, h, w), "zkie_p2_leaf_scalar")
         for i in range(len(lens) - 1):
             raw = lens[i] // MERKLE_ARITY
-            check(lib.zkie_p2_compress_batch(ptr(d_layers[i]), ptr(d_layers[i + 1]), raw, MERKLE_ARITY),
+            check(lib_.zkie_p2_compress_batch(ptr(d_layers[i]), ptr(d_layers[i + 1]), raw, MERKLE_ARITY),
                   "zkie_p2_compress_batch")
-            check(lib.zkie_p2_compress_scalar(ptr(d_layers[i]), ptr(d_layers[i + 1]), raw // 8 * 8, raw,
+            check(lib_.zkie_p2_compress_scalar(ptr(d_layers[i]), ptr(d_layers[i + 1]), raw // 8 * 8, raw,
                                               MERKLE_ARITY), "zkie_p2_compress_scalar")
         torch.cuda.synchronize()
         layers = [to_host(l).reshape(-1, DIGEST_ELEMS) for l in d_layers]

@@ -18,10 +18,18 @@ namespace {
 
 constexpr int kMaxChunks = 8;  // column blocks of the pipelined host commit
 
+// Per-device state of zkie2_commit_host.  The streams and events are shared by
+// every call on the device, so `call` serialises whole calls: a second host
+// thread waits instead of re-recording an event between another call's record
+// and its wait.  `pool` is the library's own stream-ordered pool: it caches
+// freed blocks across calls without changing the device's default pool, which
+// the caller's allocator (torch, cudaMallocAsync users) may rely on.
 struct DevStreams {
     cudaStream_t compute = nullptr, copy = nullptr, copy_out = nullptr, hash = nullptr;
-    cudaEvent_t lde_ready = nullptr, done = nullptr, hashed = nullptr;
+    cudaEvent_t lde_ready = nullptr;
     cudaEvent_t in_ready[kMaxChunks] = {}, chunk_lde[kMaxChunks] = {};
+    cudaMemPool_t pool = nullptr;
+    std::mutex call;
     bool ready = false;
 };
 std::mutex g_streams_mu;
@@ -38,17 +46,17 @@ int get_streams(DevStreams** out) {
         ZK_TRY(cudaStreamCreateWithFlags(&s.copy_out, cudaStreamNonBlocking));
         ZK_TRY(cudaStreamCreateWithFlags(&s.hash, cudaStreamNonBlocking));
         ZK_TRY(cudaEventCreateWithFlags(&s.lde_ready, cudaEventDisableTiming));
-        ZK_TRY(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
-        ZK_TRY(cudaEventCreateWithFlags(&s.hashed, cudaEventDisableTiming));
         for (int i = 0; i < kMaxChunks; i++) {
             ZK_TRY(cudaEventCreateWithFlags(&s.in_ready[i], cudaEventDisableTiming));
             ZK_TRY(cudaEventCreateWithFlags(&s.chunk_lde[i], cudaEventDisableTiming));
         }
-        cudaMemPool_t pool;
-        if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
-            uint64_t thr = ~0ull;  // keep freed blocks cached across calls
-            cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
-        }
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = d;
+        ZK_TRY(cudaMemPoolCreate(&s.pool, &props));
+        uint64_t thr = ~0ull;  // keep freed blocks cached across calls (this pool only)
+        ZK_TRY(cudaMemPoolSetAttribute(s.pool, cudaMemPoolAttrReleaseThreshold, &thr));
         s.ready = true;
     }
     *out = &s;
@@ -126,16 +134,10 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
     DevStreams* st = nullptr;
     int rc = get_streams(&st);
     if (rc) return rc;
+    std::lock_guard<std::mutex> call_lock(st->call);
     const uint64_t L = 1ull << lg_l, H = L << lg_blowup;
     const MerkleGeom g = merkle_geometry(H);
     const uint64_t scratch = lde_scratch_elems(lg_l, lg_blowup, w);
-    uint64_t *d_in = nullptr, *d_lde = nullptr, *d_layers = nullptr, *d_scr = nullptr;
-    cudaStream_t cs = st->compute;
-    ZK_TRY(cudaMallocAsync((void**)&d_in, 8 * L * w, cs));
-    ZK_TRY(cudaMallocAsync((void**)&d_lde, 8 * H * w, cs));
-    ZK_TRY(cudaMallocAsync((void**)&d_layers, 64 * g.total, cs));
-    if (scratch) ZK_TRY(cudaMallocAsync((void**)&d_scr, 8 * scratch, cs));
-    rc = p2_ensure_default();
     // Pipeline over column blocks: block j is uploaded (copy stream), its LDE
     // computed (compute stream), downloaded (copy_out stream) and absorbed
     // into every row's sponge (hash stream) while block j + 1 is uploaded.
@@ -145,12 +147,22 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
     // the leaves follows the last block.
     const uint64_t cw = w >= 64 ? ((w + 3) / 4 + 7) / 8 * 8 : w;  // about four blocks, multiples of 8
     const uint64_t nchunks = (w + cw - 1) / cw;
-    uint64_t* d_states = nullptr;
-    if (nchunks > 1) ZK_TRY(cudaMallocAsync((void**)&d_states, 128 * H, cs));
-    cudaStream_t hs = st->hash;
-    ZK_TRY(cudaEventRecord(st->lde_ready, cs));  // the allocations above, in stream order
-    ZK_TRY(cudaStreamWaitEvent(st->copy, st->lde_ready, 0));
-    ZK_TRY(cudaStreamWaitEvent(hs, st->lde_ready, 0));
+    uint64_t *d_in = nullptr, *d_lde = nullptr, *d_layers = nullptr, *d_scr = nullptr, *d_states = nullptr;
+    cudaStream_t cs = st->compute, hs = st->hash;
+    // A failed allocation sets rc; every exit below goes through the frees and
+    // the stream synchronisation at the end, so nothing allocated stays behind.
+    auto alloc = [&](uint64_t** p, uint64_t bytes) {
+        if (!rc) rc = (int)cudaMallocFromPoolAsync((void**)p, bytes, st->pool, cs);
+    };
+    alloc(&d_in, 8 * L * w);
+    alloc(&d_lde, 8 * H * w);
+    alloc(&d_layers, 64 * g.total);
+    if (scratch) alloc(&d_scr, 8 * scratch);
+    if (nchunks > 1) alloc(&d_states, 128 * H);
+    if (!rc) rc = p2_ensure_default();
+    if (!rc) rc = (int)cudaEventRecord(st->lde_ready, cs);  // the allocations above, in stream order
+    if (!rc) rc = (int)cudaStreamWaitEvent(st->copy, st->lde_ready, 0);
+    if (!rc) rc = (int)cudaStreamWaitEvent(hs, st->lde_ready, 0);
     for (uint64_t j = 0; !rc && j < nchunks; j++) {
         const uint64_t c0 = j * cw, cn = (w - c0) < cw ? (w - c0) : cw;
         rc = (int)cudaMemcpy2DAsync(d_in + c0, 8 * w, h_coeffs + c0, 8 * w, 8 * cn, L, cudaMemcpyHostToDevice,
@@ -176,14 +188,14 @@ int zkie2_commit_host(const uint64_t* h_coeffs, uint32_t lg_l, uint32_t lg_blowu
         else
             rc = (int)cudaMemcpyAsync(h_root, d_layers + 8 * g.offset.back(), 64, cudaMemcpyDeviceToHost, hs);
     }
-    // join everything on the compute stream before the frees
-    if (cudaEventRecord(st->hashed, hs) == cudaSuccess) cudaStreamWaitEvent(cs, st->hashed, 0);
-    if (h_lde && cudaEventRecord(st->done, st->copy_out) == cudaSuccess) cudaStreamWaitEvent(cs, st->done, 0);
-    cudaFreeAsync(d_in, cs);
-    cudaFreeAsync(d_lde, cs);
-    cudaFreeAsync(d_layers, cs);
-    if (d_scr) cudaFreeAsync(d_scr, cs);
-    if (d_states) cudaFreeAsync(d_states, cs);
+    // Wait for the side streams (on every path, also after an error part-way)
+    // before the buffers they use go back to the pool on the compute stream.
+    for (cudaStream_t side : {hs, st->copy_out, st->copy}) {
+        cudaError_t e = cudaStreamSynchronize(side);
+        if (!rc && e != cudaSuccess) rc = (int)e;
+    }
+    for (uint64_t* p : {d_in, d_lde, d_layers, d_scr, d_states})
+        if (p) cudaFreeAsync(p, cs);
     cudaError_t e = cudaStreamSynchronize(cs);
     if (!rc && e != cudaSuccess) rc = (int)e;
     if (!rc && h_layers)

@@ -284,8 +284,10 @@ int sm_count_of(int dev) {
 }
 
 bool tc_shape_ok(uint64_t M, uint64_t K, uint64_t N) {
-    // TMA row strides of 16 bytes (u8 K, i32 N), int tile coordinates
-    return M && K && N && K % 16 == 0 && N % 4 == 0 && M < (1ull << 30) && N < (1ull << 30) && 2 * K < (1ull << 30);
+    // TMA row strides of 16 bytes (u8 K, i32 N), int tile coordinates; the
+    // plane kernel of B puts K / 32 in grid.y (at most 65535)
+    return M && K && N && K % 16 == 0 && N % 4 == 0 && M < (1ull << 30) && N < (1ull << 30) &&
+           2 * K < (1ull << 30) && ceil_div(K, 32) <= 65535;
 }
 
 }  // namespace

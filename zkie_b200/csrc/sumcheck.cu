@@ -631,11 +631,15 @@ int sum_of_products_dev(const uint64_t* d_w, const uint64_t* d_v, uint32_t n, ui
 int matmul_field_dev(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n,
                      uint64_t* d_c, cudaStream_t s) {
     if (m == 0 || n == 0) return 0;
-    if (m > 65535) return (int)cudaErrorInvalidValue;
     if (ceil_div(n, 32) > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
-    const dim3 grid((unsigned)ceil_div(n, 32), (unsigned)m), block(32, kMmSlices);
-    k_matmul_field<<<grid, block, 0, s>>>(d_a, d_b, m, k, n, d_c);
-    ZK_LAUNCH_CHECK();
+    // grid.y holds at most 65535 rows: taller products run as row blocks
+    constexpr uint64_t kRowsPerLaunch = 65535;
+    for (uint64_t r0 = 0; r0 < m; r0 += kRowsPerLaunch) {
+        const uint64_t rows = m - r0 < kRowsPerLaunch ? m - r0 : kRowsPerLaunch;
+        const dim3 grid((unsigned)ceil_div(n, 32), (unsigned)rows), block(32, kMmSlices);
+        k_matmul_field<<<grid, block, 0, s>>>(d_a + r0 * k, d_b, rows, k, n, d_c + r0 * n);
+        ZK_LAUNCH_CHECK();
+    }
     return 0;
 }
 
