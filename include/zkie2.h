@@ -112,6 +112,16 @@ int zkie2_whir_commit(const uint64_t *d_evals, uint32_t n, uint64_t *d_lde, uint
 uint64_t zkie2_commit_extension_scratch_elems(uint32_t n, uint32_t log_inv_rate);
 int zkie2_commit_extension(const uint64_t *d_evals, uint32_t n, uint32_t log_inv_rate, uint64_t *d_lde,
                            uint64_t *d_layers, uint64_t *d_scratch, zkie_stream_t stream);
+/* Commit (root and every digest layer, as zkie2_commit) of a matrix whose LDE
+ * need not fit in HBM: the LDE rows are computed one coset of 2^lg_c at a time
+ * (rows c, c + 2^lg_c, ...; 2 lg_c <= lg_l + lg_blowup), each coset hashed
+ * and its LDE buffer reused, and the leaf digests put in row order before the
+ * tree.  The LDE is not kept.  d_scratch holds
+ * zkie2_commit_cosets_scratch_elems u64 (0 = unsupported shape).  No reference
+ * counterpart: the reference keeps the whole LDE on one device. */
+uint64_t zkie2_commit_cosets_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_c);
+int zkie2_commit_cosets(const uint64_t *d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_c,
+                        uint64_t *d_layers, uint64_t *d_scratch, zkie_stream_t stream);
 /* Host-buffer commit (the drop-in path of CudaDft::dft_batch followed by
  * CudaMerkleTreeMmcs::commit): h_coeffs L x w in, root (8 u64) out, plus the
  * LDE ((L << lg_blowup) x w) and all digest layers when those pointers are

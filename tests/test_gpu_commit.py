@@ -195,6 +195,21 @@ def test_commit_sweep_sampled(zk, orc, consts, lg_l, lb, w):
     assert np.array_equal(com2.root, com.root)
 
 
+@pytest.mark.parametrize("lg_l,lb,w,lg_c", [(3, 1, 5, 0), (3, 1, 5, 1), (6, 1, 16, 2), (6, 2, 16, 3), (9, 1, 32, 3),
+                                             (10, 2, 9, 1), (12, 1, 256, 2), (13, 1, 3, 4), (15, 3, 2, 5)])
+def test_commit_cosets_matches_commit(zk, orc, consts, lg_l, lb, w, lg_c):
+    """zkie2_commit_cosets (the LDE one coset of rows at a time, 2^lg_c cosets
+    below, at and above the blowup, i.e. with and without folded inputs):
+    every digest layer equal to zkie2_commit's, the root to the oracle's."""
+    m = rand_mat_fast(lg_l * 41 + lb * 3 + w + lg_c, 1 << lg_l, w)
+    root, layers = zk.commit_cosets(m, lb, lg_c)
+    com = zk.commit(m, lb)
+    assert np.array_equal(layers.cpu().numpy(), com.layers.cpu().numpy())
+    assert np.array_equal(root, com.root)
+    if (w << (lg_l + lb)) <= (1 << 16):
+        assert np.array_equal(root, orc.merkle_tree(consts, orc.lde(m, lb))[1])
+
+
 @pytest.mark.parametrize("lg", [4, 5, 6, 7, 8, 9, 10, 13])
 @pytest.mark.parametrize("w", [1, 5, 64, 600])
 def test_dft_every_radix_schedule(zk, orc, lg, w):

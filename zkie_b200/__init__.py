@@ -7,7 +7,7 @@ missing -- there is no CPU fallback.
 """
 from ._lib import LIB_PATH, ZkieError, check, lib  # noqa: F401
 from .commit import (  # noqa: F401
-    Committed, CudaDft, CudaMerkleTreeMmcs, MerkleTree, Whir, commit, commit_host, init_default_constants,
+    Committed, CudaDft, CudaMerkleTreeMmcs, MerkleTree, Whir, commit, commit_cosets, commit_host, init_default_constants,
     make_twiddles, merkle_layer_lengths, p2_default_constants, padded_len, split_layers, upload_constants)
 from .device import P  # noqa: F401
 from .gkr import (  # noqa: F401

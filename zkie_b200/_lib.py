@@ -60,6 +60,8 @@ SIGNATURES = {
     "zkie2_whir_commit": (i64, [vp, u32, vp, vp, vp, vp]),
     "zkie2_commit_extension_scratch_elems": (u64, [u32, u32]),
     "zkie2_commit_extension": (i64, [vp, u32, u32, vp, vp, vp, vp]),
+    "zkie2_commit_cosets_scratch_elems": (u64, [u32, u32, u64, u32]),
+    "zkie2_commit_cosets": (i64, [vp, u32, u32, u64, u32, vp, vp, vp]),
     "zkie2_commit_host": (i64, [vp, u32, u32, u64, vp, vp, vp]),
     "zkie2_sha256": (None, [C.c_char_p, sz, C.c_char_p]),
     "zkie2_transcript_new": (None, [PTr, C.c_char_p, sz]),

@@ -202,6 +202,28 @@ def commit(coeffs, lg_blowup: int, stream=None) -> Committed:
     return Committed(root, d_lde.view(H, w), d_layers, H, w)
 
 
+def commit_cosets(coeffs, lg_blowup: int, lg_cosets: int, w: int = None, stream=None):
+    """zkie2_commit_cosets: the commit of an L x w coefficient matrix (device
+    tensor or host array) whose LDE need not fit in HBM, computed one coset of
+    the LDE rows at a time.  Returns (root, flat digest layers on the device);
+    same root and layers as ``commit``, the LDE is not kept."""
+    d_in = to_dev(coeffs)
+    if w is None:
+        w = d_in.shape[1] if d_in.dim() == 2 else 1
+    L = d_in.numel() // w
+    lg_l = _lg(L)
+    H = L << lg_blowup
+    ns = lib.zkie2_commit_cosets_scratch_elems(lg_l, lg_blowup, w, lg_cosets)
+    if ns == 0:
+        raise ValueError("commit_cosets needs (2^lg_cosets)^2 <= LDE rows")
+    d_layers = empty(lib.zkie2_merkle_total_digests(H) * DIGEST_ELEMS)
+    d_scr = empty(ns)
+    check(lib.zkie2_commit_cosets(ptr(d_in), lg_l, lg_blowup, w, lg_cosets, ptr(d_layers), ptr(d_scr),
+                                  stream_handle(stream)), "zkie2_commit_cosets")
+    del d_scr
+    return to_host(d_layers[-DIGEST_ELEMS:]).copy(), d_layers
+
+
 def commit_host(coeffs: np.ndarray, lg_blowup: int, want_lde=True, want_layers=True):
     """zkie2_commit_host: host buffers in and out (pinned buffers recommended)."""
     coeffs = np.ascontiguousarray(np.asarray(coeffs, dtype=np.uint64))

@@ -122,6 +122,45 @@ uint64_t zkie2_commit_extension_scratch_elems(uint32_t n, uint32_t log_inv_rate)
     return n < 5 ? 0 : lde_scratch_elems(n - 5, log_inv_rate, 64);
 }
 
+// Commit of a matrix whose LDE does not fit in HBM next to its inputs (the
+// 256 x 2^24 cases of the raw-commit sweep need 64-128 GiB of LDE plus the
+// same again of NTT scratch): the LDE rows are produced one coset at a time.
+// Coset c of C = 2^lg_c holds the rows i = c + C*i' (zkie2_lde_coset, the
+// per-rank step of the multi-GPU split commit); its leaf digests go to a
+// staging area in coset-major order, the coset's LDE buffer is reused for the
+// next coset, and one interleave puts the H digests in row order before the
+// tree.  Same root and layers as zkie2_commit; the LDE is not kept.
+uint64_t zkie2_commit_cosets_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_c) {
+    const uint32_t lg_h = lg_l + lg_blowup;
+    if (2 * lg_c > lg_h) return 0;
+    const uint64_t H = 1ull << lg_h;
+    return (H >> lg_c) * w + zkie2_lde_coset_scratch_elems(lg_l, lg_blowup, w, lg_c) + 8 * H;
+}
+
+int zkie2_commit_cosets(const uint64_t* d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w, uint32_t lg_c,
+                        uint64_t* d_layers, uint64_t* d_scratch, cudaStream_t stream) {
+    const uint32_t lg_h = lg_l + lg_blowup;
+    if (!d_coeffs || !d_layers || !d_scratch || w == 0 || 2 * lg_c > lg_h) return (int)cudaErrorInvalidValue;
+    int rc = p2_ensure_default();
+    if (rc) return rc;
+    const uint64_t H = 1ull << lg_h, rows = H >> lg_c, C = 1ull << lg_c;
+    uint64_t* d_lde = d_scratch;
+    uint64_t* d_ntt = d_lde + rows * w;
+    uint64_t* d_stage = d_ntt + zkie2_lde_coset_scratch_elems(lg_l, lg_blowup, w, lg_c);
+    for (uint64_t c = 0; c < C; c++) {
+        rc = zkie2_lde_coset(d_coeffs, d_lde, d_ntt, lg_l, lg_blowup, w, lg_c, c, stream);
+        if (!rc) rc = launch_leaf_rows(d_lde, d_stage + 8 * rows * c, 0, rows, w, stream);
+        if (rc) return rc;
+    }
+    if (C > 1) {
+        rc = zkie2_digests_interleave(d_stage, C, rows, d_layers, stream);
+    } else {
+        rc = (int)cudaMemcpyAsync(d_layers, d_stage, 64 * H, cudaMemcpyDeviceToDevice, stream);
+    }
+    if (rc) return rc;
+    return merkle_build_from_leaves(H, d_layers, stream);
+}
+
 // Host-buffer commit: the end-to-end path a drop-in caller of
 // CudaDft::dft_batch + CudaMerkleTreeMmcs::commit takes.  Copies the L x w
 // coefficient matrix in, runs LDE + tree, and copies back the root and --
