@@ -69,6 +69,7 @@ def parse():
     ap.add_argument("--lg-blowup", type=int, default=LG_B)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-big", action="store_true", help="skip the 256 x 2^24 and expert-stack commits")
     return ap.parse_args()
 
 
@@ -229,6 +230,18 @@ def synth_device(n, seed, device):
     return x.view(torch.uint64)
 
 
+def synth_into(out, seed):
+    """synth_device into a preallocated uint64 tensor in chunks of 2^26
+    elements, so that a 32 GiB input needs no 100 GiB of temporaries."""
+    import torch
+    n, chunk = out.numel(), 1 << 26
+    v = out.view(torch.int64)
+    for i, c0 in enumerate(range(0, n, chunk)):
+        c1 = min(n, c0 + chunk)
+        v[c0:c1].copy_(synth_device(c1 - c0, seed * 7919 + i, out.device).view(torch.int64))
+    return out
+
+
 def ntt_passes(lg):
     """Launches of k_ntt_pass per LDE (the plan in zkie_b200/csrc/ntt.cu)."""
     return 1 if lg <= 10 else (2 if lg <= 22 else 3)
@@ -382,6 +395,23 @@ def main_split(args, zk, dev, world, rank):
     lg_local = lg_l + lg_b - sc.lg_g
     launches = (1 + ntt_passes(lg_local)) + 1 + 1 + (lib.zkie2_merkle_num_layers(sc.n_local) - 1) + \
         (lib.zkie2_merkle_num_layers(world) - 1)
+    n_local = sc.n_local
+    del sc, d_in
+    torch.cuda.empty_cache()
+
+    # configuration 1 as replicas: every rank proves its own shard (shards
+    # are independent until the cross-shard binding); max over ranks
+    dist.barrier()
+    shard = shard_prove_ms(zk, dev)
+    shard.pop("inputs")
+    shard_ms = max_over_ranks(shard["ms"], dev)
+    shard_dev_ms = max_over_ranks(shard["device_ms"], dev)
+    shard.update({"ms": round(shard_ms, 3), "device_ms": round(shard_dev_ms, 3), "replicas": world,
+                  "value": round(world / (shard_ms / 1e3), 1), "unit": "shards/s (all GPUs)",
+                  "parallelism": f"replicas: one independent shard per GPU, max over {world} ranks"})
+    shard["roofline"] = shard_roofline(zk, dev, shard_dev_ms, perm_ceiling)
+    big = big_commits(zk, dev, rank, world) if not args.no_big else {}
+    split_sc = sumcheck_case(zk, dev, rank, world)
     cfg = workload_config(lg_l, w, lg_b, world)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -390,7 +420,7 @@ def main_split(args, zk, dev, world, rank):
         "config": cfg,
         "roofline": {
             "bound": "int", "kernel": f"k_leaf_rows (Poseidon2 leaf sponge, {(w + 7) // 8} permutations per row, "
-                                      f"{sc.n_local} rows per rank)",
+                                      f"{n_local} rows per rank)",
             "achieved": round(leaf_rate * MULS_PER_PERM / 1e9, 2), "peak": round(mul_peak / 1e9, 2),
             "unit": "G Goldilocks mul/s (per GPU)", "frac": round(leaf_rate * MULS_PER_PERM / mul_peak, 4),
             "traffic": None,
@@ -408,7 +438,7 @@ def main_split(args, zk, dev, world, rank):
             "ms_per_step": round(ntt_ms, 4), "share_of_step": round(ntt_ms / ms_per_step, 4),
         },
         "exchange_ms_per_step": round(exch_ms, 4),
-        "exchange_bytes_per_rank": 64 * sc.n_local * (world - 1) // world,
+        "exchange_bytes_per_rank": 64 * n_local * (world - 1) // world,
         "nodes_ms_per_step": round(tree_ms, 4),
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
@@ -417,6 +447,9 @@ def main_split(args, zk, dev, world, rank):
     }
     if e2e:
         line["e2e"] = e2e
+    line["shard_prove"] = shard
+    line.update(big)
+    line["split_sumcheck"] = split_sc
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -553,9 +586,19 @@ def main():
         del h_in, h_lde, h_layers
 
     # ---- MatMul shard prove (inputs resident) ----
-    shard = shard_prove_ms(zk, dev) if rank == 0 else None
+    shard = shard_prove_ms(zk, dev)
+    sa, sw = shard.pop("inputs")
+    shard["roofline"] = shard_roofline(zk, dev, shard["device_ms"], perm_ceiling)
+    if not args.no_cpu:
+        shard["cpu_baseline"] = shard_cpu_baseline(sa, sw)
     # ---- the next rows: logUp fraction tree and WHIR PoW grinding ----
-    extra = next_rows(want_cpu=rank == 0 and world == 1 and not args.no_cpu) if rank == 0 else None
+    extra = next_rows(want_cpu=not args.no_cpu)
+    extra["projection"] = projection_case(zk, dev, want_cpu=not args.no_cpu)
+    # ---- configurations 2 (256 x 2^24) and 5 (expert stack); the 2^28 sumcheck ----
+    del d_in, d_lde, d_layers, d_scr
+    torch.cuda.empty_cache()
+    big = big_commits(zk, dev, rank, world) if not args.no_big else {}
+    sumcheck = sumcheck_case(zk, dev, rank, world)
 
     launches_per_step = ntt_passes(lg) + 1 + (lib.zkie2_merkle_num_layers(H) - 1)
     traffic = measured_traffic(lg_l, w, lg_b, world)
@@ -594,6 +637,8 @@ def main():
         line["shard_prove"] = shard
     if extra:
         line.update(extra)
+    line.update(big)
+    line["sumcheck_2^28"] = sumcheck
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(w, lg_b)
     if rank == 0:
@@ -713,7 +758,317 @@ def shard_prove_ms(zk, dev, iters=5):
                       "+ 10-round GKR sumcheck, one zkie2_shard_prove_matmul call (four streams)",
             "ms": round(1e3 * statistics.median(times), 3),
             "device_ms": round(statistics.median(dev_times), 3),
-            "claimed": hex(res.proof.proof.claimed), "root_w": hex(int(res.roots[0][0]))}
+            "claimed": hex(res.proof.proof.claimed), "root_w": hex(int(res.roots[0][0])),
+            "inputs": (a, wt)}
+
+
+def projection_case(zk, dev, want_cpu, m=512, k=1024, n=4096, shift=16, iters=5):
+    """The projection block (crates/zkie-ops/src/projection.rs prove_projection)
+    at a GPT-2 layer's FFN up-projection shape, 16-bit fixed-point x and W
+    (scale 2^16), bias within 2^20: the whole prove (forward h = x W on the
+    tensor cores, MatMul GKR, affine virtual sumcheck, logUp range check into
+    the 2^16 table) with inputs resident; the proof alone (h given) beside it."""
+    import numpy as np
+    import torch
+
+    from zkie_b200.projection import projection_witness, prove_projection
+    g = np.random.default_rng(11)
+
+    def fx(size, lim):
+        x = g.integers(-lim, lim, size=size, dtype=np.int64)
+        return torch.from_numpy(x.astype(np.uint64) + np.where(x < 0, np.uint64(P), np.uint64(0))).to(dev)
+    x, w, b = fx(m * k, 1 << 15), fx(k * n, 1 << 15), fx(m * n, 1 << 20)
+    h, path = zk.matmul_fixed(x, w, m, k, n)
+    out, rem, idx = projection_witness(h, b, shift)
+    whole, proof_only = [], []
+    for it in range(iters + 2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3), idx=idx)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        p = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3), idx=idx, h=h)
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        if it >= 2:
+            whole.append(t1 - t0)
+            proof_only.append(t2 - t1)
+    ms, ms_p = 1e3 * statistics.median(whole), 1e3 * statistics.median(proof_only)
+    lg = (m * n + (1 << shift) - 1).bit_length()
+    # bytes the proof reads at least once: x, W, h (GKR); rem, h, out, bias
+    # (affine; eq and ones are generated); the lookup columns num / den of
+    # 2^lg fractions written and read once
+    proof_bytes = 8 * (m * k + k * n + m * n) + 8 * 4 * m * n + 2 * 16 * (1 << lg)
+    hbm_peak, hbm_src = hbm_peak_gbs()
+    out_d = {"config": f"prove_projection, x {m}x{k} @ W {k}x{n} (a GPT-2 layer's FFN up-projection), shift {shift}, "
+                       "16-bit fixed-point inputs, inputs resident",
+             "ms": round(ms, 3), "proof_only_ms": round(ms_p, 3), "forward_path": "tensor cores" if path == 0 else
+             "field kernel", "value": round(m * n / (ms / 1e3) / 1e6, 3), "unit": "M outputs/s",
+             "claimed": hex(p.matmul.claimed), "lookup_fractions": 1 << lg,
+             "roofline": {"bound": "hbm", "achieved": round(proof_bytes / (ms_p / 1e3) / 1e9, 1), "peak": hbm_peak,
+                          "unit": "GB/s", "frac": round(proof_bytes / (ms_p / 1e3) / 1e9 / hbm_peak, 4),
+                          "algorithmic_bytes": proof_bytes, "peak_source": hbm_src,
+                          "note": "proof part (h given); the logUp tree's ~2 lg serial rounds per layer make it "
+                                  "latency-bound, see logup"}}
+    if want_cpu:
+        from oracle import oracle as orc
+        orc.set_threads(host_threads())
+        xs, ws, bs, os_, rs = (t.cpu().numpy() for t in (x, w, b, out, rem))
+        t0 = time.perf_counter()
+        orc.projection_prove(xs, ws, bs, os_, rs, m, k, n, shift, orc.XorShift64(3))
+        dt = time.perf_counter() - t0
+        out_d["cpu_baseline"] = {"value": round(1e3 * dt, 1), "unit": "ms per projection", "cores": host_threads(),
+                                 "kind": "port", "label": CPU_LABEL,
+                                 "sample": "the same projection once by oracle/zkie_oracle.c (field matmul on all "
+                                           "threads, the sumchecks and the fraction tree on one)"}
+    del x, w, b, h, out, rem, idx
+    torch.cuda.empty_cache()
+    return out_d
+
+
+def shard_roofline(zk, dev, device_ms, perm_ceiling):
+    """Floor of the configuration-1 shard: the larger of (a) its dependency
+    chain, W's 4 leaf absorptions (32 columns, rate 8) then 16 tree levels, one
+    permutation each, at the measured latency of one permutation (one thread
+    per permutation where a launch has more than 2^14 states, four lanes per
+    permutation below), and (b) its permutation count at the measured
+    permutation throughput (the NTT, matmul and GKR bytes add < 10 us at HBM
+    speed).  Kernel-launch gaps between the dependent steps are not in the
+    floor."""
+    import torch
+    lib = zk.lib
+    st = synth_device(16, 77, dev)
+    reps = 4096
+    zk.check(lib.zkie2_p2_permute(st.data_ptr(), 1, 16, 0), "permute warmup")
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    zk.check(lib.zkie2_p2_permute(st.data_ptr(), 1, reps, s.cuda_stream), "permute latency")
+    e1.record(s)
+    torch.cuda.synchronize()
+    lat_us = 1e3 * e0.elapsed_time(e1) / reps
+    # launches of at most 2^14 states run each permutation on four lanes: the
+    # latency of that form from one row of 8 * 256 columns (256 dependent
+    # absorptions in one four-lane group)
+    absorb = 256
+    row = synth_device(8 * absorb, 78, dev)
+    dig = torch.empty(8, dtype=torch.uint64, device=dev)
+    zk.check(lib.zkie2_merkle_leaves(row.data_ptr(), 1, 8 * absorb, dig.data_ptr(), s.cuda_stream), "warmup")
+    e0.record(s)
+    zk.check(lib.zkie2_merkle_leaves(row.data_ptr(), 1, 8 * absorb, dig.data_ptr(), s.cuda_stream), "x4 latency")
+    e1.record(s)
+    torch.cuda.synchronize()
+    lat4_us = 1e3 * e0.elapsed_time(e1) / absorb
+    perms = 0
+    for n in (20, 14, 14):  # W, A, C
+        H = 1 << (n - 4)
+        perms += H * 4 + (lib.zkie2_merkle_total_digests(H) - H)
+    # W's chain: 4 absorptions of 2^16 rows and the 2^15-node level (one lane
+    # per permutation), then 15 levels of at most 2^14 nodes (four lanes)
+    chain = 4 + 16
+    chain_ms = ((4 + 1) * lat_us + 15 * lat4_us) / 1e3
+    thr_ms = perms / perm_ceiling * 1e3
+    floor = max(chain_ms, thr_ms)
+    return {"bound": "latency" if chain_ms >= thr_ms else "int", "achieved_ms": device_ms, "floor_ms": round(floor, 4),
+            "frac": round(floor / device_ms, 4), "unit": "ms",
+            "chain_floor_ms": round(chain_ms, 4), "chain_permutations": chain,
+            "permutation_latency_us": round(lat_us, 3), "permutation_latency_x4_us": round(lat4_us, 3),
+            "throughput_floor_ms": round(thr_ms, 4), "permutations": perms,
+            "perm_rate_gperm_s": round(perm_ceiling / 1e9, 4)}
+
+
+def shard_cpu_baseline(a, wt, m=16, k=1024, n=1024):
+    """The configuration-1 shard on the host cores: forward C = A W (field
+    matmul, OpenMP), the three WHIR commits (LDE + Merkle, OpenMP) and the
+    Op::MatMul proof with the shard's child transcript (single thread)."""
+    from oracle import oracle as orc
+    orc.set_threads(host_threads())
+    consts = orc.p2_constants(1)
+    t0 = time.perf_counter()
+    c = orc.matmul_field(a, wt)
+    for t in (wt, a, c):
+        orc.whir_commit(consts, t.reshape(-1))
+    orc.op_matmul_prove(a, wt, c, m, k, n, orc.shard_dag_child([[0, 1, 2]], 1, 0))
+    dt = time.perf_counter() - t0
+    return {"value": round(1e3 * dt, 3), "unit": "ms per shard", "cores": host_threads(), "kind": "port",
+            "label": CPU_LABEL, "sample": "the whole configuration-1 shard (forward, three WHIR commits, MatMul GKR) "
+                                          "by oracle/zkie_oracle.c, once"}
+
+
+# ---- the commits larger than one GPU's plain commit, and the split sumcheck --------------
+EXTRA_WARMUP, EXTRA_STEPS = 1, 2
+BIG_CASES = [
+    # name, lg_l, lg_blowup, w, description
+    ("cfg5_expert_stack", 23, 1, 32,
+     "cfg5: DeepSeek-V2-Lite routed-expert stack, N_ROUTED x H x MOE_PAD = 64 x 2048 x 2048 = 2^28 evaluations, "
+     "one WHIR base commit (group size 1: arity 28 > 26): 2^23 x 32 at blowup 2"),
+    ("cfg2_256x2^24_b2", 24, 1, 256, "cfg2: 256 polys x 2^24 coeffs, blowup 2 (LDE 64 GiB)"),
+    ("cfg2_256x2^24_b4", 24, 2, 256, "cfg2: 256 polys x 2^24 coeffs, blowup 4 (LDE 128 GiB)"),
+]
+
+
+def _timed(fn, stream, dev, world):
+    """EXTRA_WARMUP untimed calls, then EXTRA_STEPS calls between CUDA events on
+    the launching stream; ms per call, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(EXTRA_WARMUP):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(EXTRA_STEPS):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / EXTRA_STEPS
+    return max_over_ranks(ms, dev) if world > 1 else ms
+
+
+def _hex_root(root):
+    return [hex(int(x)) for x in root[:2]]
+
+
+def big_commits(zk, dev, rank, world):
+    """BASELINE configurations 2 (256 x 2^24, blowup 2 and 4) and 5 (the
+    routed-expert stack).  N = 1: the expert stack through the plain WHIR
+    commit (LDE kept), the 2^24 cases through zkie2_commit_cosets (LDE one
+    coset of rows at a time; 164 / 296 GiB would not fit otherwise).  N > 1:
+    every case as one commit split over the ranks (SplitCommitter), blowup 4 at
+    N >= 4 (at N = 2 a rank would hold 32 GiB of input plus 2 x 64 GiB).  Each
+    root is checked on rank 0 against a single-GPU commit of the same input
+    taken by another path: the plain commit for the expert stack, the coset
+    commit with a different coset count for the 2^24 cases."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from zkie_b200.device import empty
+    from zkie_b200.multigpu import SplitCommitter
+    lib, check = zk.lib, zk.check
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    lg_g = world.bit_length() - 1
+    out = {}
+    for idx, (name, lg_l, lg_b, w, desc) in enumerate(BIG_CASES):
+        if world == 2 and lg_b == 2:
+            continue
+        L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+        torch.cuda.empty_cache()
+        d_in = synth_into(torch.empty(L * w, dtype=torch.uint64, device=dev), 4242 + idx)
+        total = lib.zkie2_merkle_total_digests(H)
+        if world > 1:
+            sc = SplitCommitter(lg_l, lg_b, w)
+            ms = _timed(lambda: sc.run(d_in), stream, dev, world)
+            root = sc.root()
+            path = (f"split over {world} GPUs (coset LDE rows per rank, NCCL all-to-all of leaf digests, "
+                    "all-gather of subtree roots)")
+            del sc
+        elif name.startswith("cfg5"):
+            lde, layers = empty(H * w), empty(total * 8)
+            scr = empty(max(lib.zkie2_whir_scratch_elems(lg_l + 5), 1))
+            ms = _timed(lambda: check(lib.zkie2_whir_commit(d_in.data_ptr(), lg_l + 5, lde.data_ptr(),
+                                                            layers.data_ptr(), scr.data_ptr(), sh), "whir_commit"),
+                        stream, dev, world)
+            root = layers[-8:].cpu().numpy()
+            path = "zkie2_whir_commit on one GPU (LDE kept resident)"
+            del lde, layers, scr
+        else:
+            lg_c = 2 if lg_b == 1 else 3
+            layers = empty(total * 8)
+            scr = empty(lib.zkie2_commit_cosets_scratch_elems(lg_l, lg_b, w, lg_c))
+            ms = _timed(lambda: check(lib.zkie2_commit_cosets(d_in.data_ptr(), lg_l, lg_b, w, lg_c, layers.data_ptr(),
+                                                              scr.data_ptr(), sh), "commit_cosets"),
+                        stream, dev, world)
+            root = layers[-8:].cpu().numpy()
+            path = f"zkie2_commit_cosets on one GPU ({1 << lg_c} cosets of LDE rows, LDE not kept)"
+            del layers, scr
+        torch.cuda.empty_cache()
+        root_ok, check_path = None, None
+        if rank == 0:
+            if name.startswith("cfg5") and world > 1:
+                ref = zk.Whir.with_params(lg_l + 5, 90, 17).commit(d_in)
+                exp, check_path = np.asarray(ref.root, dtype=np.uint64), "zkie2_whir_commit on one GPU"
+                del ref
+            else:
+                lg_c = (lg_g + 1) if world > 1 else (2 if lg_b == 1 else 3) + 1
+                exp, layers = zk.commit_cosets(d_in, lg_b, lg_c, w=w)
+                check_path = f"zkie2_commit_cosets on one GPU with {1 << lg_c} cosets"
+                del layers
+            root_ok = bool((exp == root).all())
+            torch.cuda.empty_cache()
+        if world > 1:
+            dist.barrier()
+        del d_in
+        torch.cuda.empty_cache()
+        perms = H * ((w + 7) // 8) + (total - H)
+        out[name] = {"config": desc, "path": path, "ms": round(ms, 3), "steps": EXTRA_STEPS, "warmup": EXTRA_WARMUP,
+                     "value": round(L * w / (ms / 1e3) / 1e6, 3), "unit": "Melem/s (input elements, all GPUs)",
+                     "lde_melem_s": round(H * w / (ms / 1e3) / 1e6, 3),
+                     "gperm_s_per_gpu": round(perms / world / (ms / 1e3) / 1e9, 4),
+                     "root": _hex_root(root), "root_check": check_path, "root_ok": root_ok}
+    return out
+
+
+def sumcheck_case(zk, dev, rank, world, t=28):
+    """sumcheck::prove of f, h of 2^t elements, split over the ranks by the
+    high variables (zkie_b200.multigpu.split_sumcheck: local rounds, ONE
+    all-reduce of every local round message, an all-gather of the folded
+    values, the last log2 N rounds on every rank); at N = 1 the plain
+    single-GPU proof.  Rounds and finals are checked on rank 0 against the
+    single-GPU proof of the whole vectors."""
+    import numpy as np
+    import torch
+
+    from zkie_b200.multigpu import split_sumcheck
+    n_loc = (1 << t) // world
+    f = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 500 + rank)
+    h = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 600 + rank)
+    ch = np.array([(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(t)], dtype=np.uint64)
+    for _ in range(2):
+        split_sumcheck(f, h, t, ch)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        rounds, fe, he = split_sumcheck(f, h, t, ch)
+    torch.cuda.synchronize()
+    ms = 1e3 * (time.perf_counter() - t0) / reps
+    if world > 1:
+        ms = max_over_ranks(ms, dev)
+    ok = None
+    if rank == 0:
+        if world > 1:
+            F = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+            G = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+            for r in range(world):
+                synth_into(F[r * n_loc:(r + 1) * n_loc], 500 + r)
+                synth_into(G[r * n_loc:(r + 1) * n_loc], 600 + r)
+            ref = zk.sumcheck_prove(F, G, 0, ch)
+            ok = bool(np.array_equal(np.asarray(rounds).reshape(-1, 3), ref.rounds)
+                      and (fe, he) == (ref.f_eval, ref.h_eval))
+            del F, G
+        else:
+            ok = True
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    del f, h
+    torch.cuda.empty_cache()
+    hbm_peak, _ = hbm_peak_gbs()
+    gbs = 16 * n_loc / (ms / 1e3) / 1e9
+    return {"config": f"sumcheck::prove, f and h of 2^{t} elements" +
+                      (f" split over {world} GPUs by the high variables" if world > 1 else " on one GPU"),
+            "ms": round(ms, 4), "value": round((1 << t) / (ms / 1e3) / 1e6, 3), "unit": "Melem/s",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s per GPU",
+                         "frac": round(gbs / hbm_peak, 4),
+                         "note": "16 bytes per element (f and h read once), whole call incl. host round trips"},
+            "rounds_match": ok}
 
 
 if __name__ == "__main__":

@@ -235,6 +235,18 @@ uint64_t zkie2_matmul_fixed_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
 int zkie2_matmul_fixed(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
                        uint64_t *d_c, uint32_t policy, uint32_t *h_path, uint64_t *d_scratch,
                        zkie_stream_t stream);
+/* The projection block's witness columns (crates/zkie-ops/src/projection.rs, the
+ * out / rem_off construction of its tests, :136-176): for each of n elements,
+ * with a = to_i64(h) (h = x @ W) and b = to_i64(bias),
+ *   out = div_round(a, 2^shift) + b      (floor, plus one when the remainder >= 2^(shift-1)),
+ *   rem_off = a - (out - b) 2^shift + 2^(shift-1)   (in [0, 2^shift)),
+ * as field elements (from_i64), and, when d_idx is non-null, the lookup index
+ * to_i32(rem_off) as u32 of prove_projection (:94).  1 <= shift <= 30. */
+int zkie2_projection_witness(const uint64_t *d_h, const uint64_t *d_bias, uint64_t n, uint32_t shift,
+                             uint64_t *d_out, uint64_t *d_rem_off, uint32_t *d_idx, zkie_stream_t stream);
+/* to_i32(v) as u32 of n field elements (the lookup indices of a fixed-point
+ * column, fixed_point.rs to_i32). */
+int zkie2_lookup_index_i32(const uint64_t *d_v, uint64_t n, uint32_t *d_idx, zkie_stream_t stream);
 /* One MatMul shard in one call: C = A W into d_c
  * (m x n), WHIR base commits of W (k*n evaluations), A (m*k) and C (m*n)
  * (pcs/whir.rs:438-469, each >= 32 evaluations), and the Op::MatMul proof

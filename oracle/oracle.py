@@ -526,6 +526,88 @@ def lookup_num_den(x, y, table, m, mode, alpha, beta):
     return (num, den) if got else None
 
 
+# ---- projection block (crates/zkie-ops/src/projection.rs) -------------------------------
+def to_i64(v):
+    """fixed_point.rs to_i64."""
+    v = int(v) % P
+    return v if v <= 0x7FFFFFFFFFFFFFFF else -(P - v)
+
+
+def to_i32_index(v):
+    """to_i32(v) as u32 (fixed_point.rs): the low 32 bits of (P - v), negated."""
+    v = int(v) % P
+    if v <= 0x7FFFFFFF:
+        return v
+    return (-((P - v) & 0xFFFFFFFF)) & 0xFFFFFFFF
+
+
+def projection_terms(shift):
+    """prove_projection's terms over [eq, rem_off, h, out, bias, ones] (:71-81)."""
+    two, half, neg = 1 << shift, 1 << (shift - 1), P - 1
+    return [(1, [0, 1]), (neg, [0, 2]), (two, [0, 3]), (neg * two % P, [0, 4]), (neg * half % P, [0, 5])]
+
+
+def projection_witness(h, bias, shift):
+    """out and rem_off as the reference's tests build them (:136-176):
+    out = div_round(to_i64(h), 2^shift) + to_i64(bias), rem_off = h - (out - bias)
+    2^shift + 2^(shift-1), with div_round = floor plus one at remainder >= half."""
+    out, rem = [], []
+    for hv, bv in zip(np.asarray(h, dtype=np.uint64).reshape(-1), np.asarray(bias, dtype=np.uint64).reshape(-1)):
+        a, b = to_i64(hv), to_i64(bv)
+        q, r = divmod(a, 1 << shift)
+        if 2 * r >= (1 << shift):
+            q += 1
+        o = q + b
+        out.append(from_i64(o))
+        rem.append(from_i64(a - (o - b) * (1 << shift) + (1 << (shift - 1))))
+    return np.array(out, dtype=np.uint64), np.array(rem, dtype=np.uint64)
+
+
+def projection_prove(x, w, bias, out, rem_off, m, k, n, shift, challenger):
+    """prove_projection (projection.rs:44-101) over the oracle's parts: h = x w,
+    matmul::prove(x^T, w, h) with u, v, ch drawn in that order (the Op::MatMul
+    draw order), prove_virtual over [eq(v||u), rem_off, h, out, bias, ones],
+    then alpha, beta and prove_lookup_fractional of (to_i32(rem_off) as u32,
+    rem_off) into the table 0 .. 2^shift - 1 (full_r then cs per variable)."""
+    x = u64(x).reshape(m, k)
+    w = u64(w).reshape(k, n)
+    h = matmul_field(x, w).reshape(-1)
+    op = op_matmul_prove(x, w, h.reshape(m, n), m, k, n, challenger)
+    pt = np.concatenate([op["v"], op["u"]]).astype(np.uint64)
+    eq = eq_evals(pt)
+    ones = np.ones(m * n, dtype=np.uint64)
+    rem = u64(rem_off).reshape(-1)
+    a_rounds, a_finals = virtual_prove([eq, rem, h, u64(out).reshape(-1), u64(bias).reshape(-1), ones],
+                                       projection_terms(shift), pt)
+    alpha, beta = challenger.field(), challenger.field()
+    table = np.arange(1 << shift, dtype=np.uint64)
+    idx = [to_i32_index(v) for v in rem]
+    num, den = lookup_num_den(idx, rem, table, None, 0, alpha, beta)
+    lg = num.size.bit_length() - 1
+    full_r = [challenger.field() for _ in range(lg)]
+    cs = [challenger.field() for _ in range(lg)]
+    f_rounds, f_finals, fnum, fden = fractional_prove(num, den, full_r, cs)
+    return dict(h=h, claimed=op["claimed"], mm_rounds=op["rounds"], mm_finals=op["finals"], u=op["u"], v=op["v"],
+                ch=op["ch"], pt=pt, affine_rounds=a_rounds, affine_finals=a_finals, alpha=alpha, beta=beta,
+                full_r=np.array(full_r, dtype=np.uint64), cs=np.array(cs, dtype=np.uint64), frac_rounds=f_rounds,
+                frac_finals=f_finals, final_num=fnum, final_den=fden)
+
+
+def projection_verify(proof, shift):
+    """verify_projection (projection.rs:102-128): the affine virtual sumcheck
+    with h's final evaluation replaced by the matmul claim, the matmul
+    sumcheck, and the lookup's fraction chain with claimed sum 0."""
+    fe = np.array(proof["affine_finals"], dtype=np.uint64).copy()
+    fe[2] = np.uint64(proof["claimed"])
+    if not virtual_verify(proof["affine_rounds"], projection_terms(shift), 0, proof["pt"], fe):
+        return False
+    f_eval, h_eval = (int(v) for v in proof["mm_finals"])
+    if not sumcheck_verify(proof["mm_rounds"], proof["claimed"], proof["ch"], f_eval, h_eval):
+        return False
+    return (fractional_chain_core(proof["full_r"], proof["cs"], proof["frac_rounds"], proof["frac_finals"])
+            and proof["final_num"] == 0)
+
+
 # ---- PoW grinding (DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>) --------------------
 def check_witness(consts, sponge, inputs, bits, w):
     sp, inp = u64(sponge), u64(inputs if len(inputs) else [0])

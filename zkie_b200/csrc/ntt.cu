@@ -551,9 +551,55 @@ int dft_plan(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint32_t lg, 
 // y[j'][c] = sum_{m < nfold} x[j' + m*stride][c] * W_H^((j' + m*stride) * g)
 // for j' < R.  Rows of x at or past L are zero.  Then the coset is the
 // R-point DFT of y (zero-padded to H/G rows when R = L < H/G).
-__global__ void __launch_bounds__(256)
+//
+// The twist factor depends on the row only, so a block takes a tile of
+// kTwistRows rows: it computes the tile's kTwistRows * nfold factors once in
+// shared memory, then its threads walk the tile's (row, column) elements with
+// consecutive threads on consecutive columns (coalesced rows of x and y).
+// Each element costs nfold loads and one exact 160-bit dot product; the
+// factors cost one table product per row and fold term instead of one per
+// element.
+constexpr int kTwistThreads = 256;
+constexpr uint32_t kTwistRows = 8;
+constexpr uint32_t kTwistMaxFold = 512;  // kTwistRows * kTwistMaxFold factors = 32 KB of shared memory
+
+__device__ __forceinline__ uint64_t coset_factor(uint64_t j, uint64_t g, uint32_t lg_h) {
+    // W_H^(j g) with W_H = w32^(2^(32 - lg_h)): exponent of w32 mod 2^32
+    const uint32_t E = (uint32_t)(((j * g) << (32 - lg_h)) & 0xFFFFFFFFull);
+    return gl_mul(__ldg(g_tw_lo + (E & 0xFFFF)), __ldg(g_tw_hi + (E >> 16)));
+}
+
+__global__ void __launch_bounds__(kTwistThreads)
     k_coset_twist(const uint64_t* __restrict__ x, uint64_t L, uint64_t w, uint32_t lg_h, uint64_t g, uint64_t R,
                   uint64_t stride, uint32_t nfold, uint64_t* __restrict__ y) {
+    __shared__ uint64_t fac[kTwistRows * kTwistMaxFold];
+    const uint64_t r0 = (uint64_t)blockIdx.x * kTwistRows;
+    const uint32_t rows = (uint32_t)(R - r0 < kTwistRows ? R - r0 : kTwistRows);
+    for (uint32_t i = threadIdx.x; i < rows * nfold; i += kTwistThreads) {
+        const uint32_t r = i / nfold, m = i - r * nfold;
+        const uint64_t j = r0 + r + (uint64_t)m * stride;
+        fac[i] = j < L ? coset_factor(j, g, lg_h) : 0;
+    }
+    __syncthreads();
+    const uint64_t n = (uint64_t)rows * w;
+    for (uint64_t e = threadIdx.x; e < n; e += kTwistThreads) {
+        const uint32_t r = (uint32_t)(e / w);
+        const uint64_t c = e - (uint64_t)r * w, jp = r0 + r;
+        Acc160 acc = acc160_zero();
+        for (uint32_t m = 0; m < nfold; m++) {
+            const uint64_t j = jp + m * stride;
+            if (j >= L) break;
+            acc160_mac(acc, __ldg(x + j * w + c), fac[r * nfold + m]);
+        }
+        y[jp * w + c] = gl_canon(acc160_reduce(acc));
+    }
+}
+
+// The same for fold counts above kTwistMaxFold (very many cosets per
+// blowup): factors computed per element.
+__global__ void __launch_bounds__(kTwistThreads)
+    k_coset_twist_wide(const uint64_t* __restrict__ x, uint64_t L, uint64_t w, uint32_t lg_h, uint64_t g, uint64_t R,
+                       uint64_t stride, uint32_t nfold, uint64_t* __restrict__ y) {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= R * w) return;
     const uint64_t jp = idx / w, c = idx - jp * w;
@@ -561,10 +607,7 @@ __global__ void __launch_bounds__(256)
     for (uint32_t m = 0; m < nfold; m++) {
         const uint64_t j = jp + m * stride;
         if (j >= L) break;
-        // W_H^(j g) with W_H = w32^(2^(32 - lg_h)): exponent of w32 mod 2^32
-        const uint32_t E = (uint32_t)(((j * g) << (32 - lg_h)) & 0xFFFFFFFFull);
-        const uint64_t tw = gl_mul(__ldg(g_tw_lo + (E & 0xFFFF)), __ldg(g_tw_hi + (E >> 16)));
-        acc160_mac(acc, __ldg(x + j * w + c), tw);
+        acc160_mac(acc, __ldg(x + j * w + c), coset_factor(j, g, lg_h));
     }
     y[idx] = gl_canon(acc160_reduce(acc));
 }
@@ -619,8 +662,14 @@ int lde_coset_launch(const uint64_t* in, uint64_t* out, uint64_t* scratch, uint3
     uint64_t* y = scratch;
     uint64_t* sub = scratch + ((w << lg_y) + 1 & ~1ull);  // keep 16-byte alignment
     const uint64_t n = R * w;
-    k_coset_twist<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(in, 1ull << lg_l, w, lg_h, g, R, 1ull << (lg_h - lg_g),
-                                                              fold ? 1u << (lg_g - lg_blowup) : 1u, y);
+    const uint32_t nfold = fold ? 1u << (lg_g - lg_blowup) : 1u;
+    const uint64_t stride = 1ull << (lg_h - lg_g);
+    if (nfold <= kTwistMaxFold && ceil_div(R, kTwistRows) <= 0x7FFFFFFFull)
+        k_coset_twist<<<(unsigned)ceil_div(R, kTwistRows), kTwistThreads, 0, s>>>(in, 1ull << lg_l, w, lg_h, g, R,
+                                                                                  stride, nfold, y);
+    else
+        k_coset_twist_wide<<<(unsigned)ceil_div(n, kTwistThreads), kTwistThreads, 0, s>>>(in, 1ull << lg_l, w, lg_h,
+                                                                                           g, R, stride, nfold, y);
     ZK_LAUNCH_CHECK();
     if (fold) return dft_plan<false>(y, out, sub, lg_h - lg_g, w, w, ~0ull, nullptr, 0, s);
     return dft_plan<false>(y, out, sub, lg_h - lg_g, w, w, 1ull << lg_l, nullptr, 0, s);
