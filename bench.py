@@ -412,6 +412,7 @@ def main_split(args, zk, dev, world, rank):
     shard["roofline"] = shard_roofline(zk, dev, shard_dev_ms, perm_ceiling)
     big = big_commits(zk, dev, rank, world) if not args.no_big else {}
     split_sc = sumcheck_case(zk, dev, rank, world)
+    mg = mg_case(zk, dev, rank, world, lg_l, lg_b, w, root)
     cfg = workload_config(lg_l, w, lg_b, world)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -450,6 +451,7 @@ def main_split(args, zk, dev, world, rank):
     line["shard_prove"] = shard
     line.update(big)
     line["split_sumcheck"] = split_sc
+    line["mg_c_abi"] = mg
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -1009,6 +1011,90 @@ def big_commits(zk, dev, rank, world):
                      "lde_melem_s": round(H * w / (ms / 1e3) / 1e6, 3),
                      "gperm_s_per_gpu": round(perms / world / (ms / 1e3) / 1e9, 4),
                      "root": _hex_root(root), "root_check": check_path, "root_ok": root_ok}
+    return out
+
+
+def mg_case(zk, dev, rank, world, lg_l, lg_b, w, want_root, t=28):
+    """The same split commit and a 2^t split sumcheck through the library's
+    own multi-GPU context (zkie2_mg_init over a communicator the library
+    creates from an NCCL id broadcast by rank 0; zkie2_mg_split_commit,
+    zkie2_mg_split_sumcheck): the path a non-Python host drives.  ms per call
+    (CUDA events around the synchronous calls, max over ranks); the root is
+    compared with the torch-orchestrated split above, the proof with the
+    single-GPU sumcheck on rank 0."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    lib, check = zk.lib, zk.check
+    P64 = C.POINTER(C.c_uint64)
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        check(lib.zkie2_mg_unique_id(uid), "mg unique id")
+    box = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    uid = C.create_string_buffer(box[0], 128)
+    ctx = C.c_void_p()
+    check(lib.zkie2_mg_init(uid, world, rank, C.byref(ctx)), "mg init")
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    out = {}
+    try:
+        L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+        n_local = H // world
+        d_in = synth_device(L * w, 1234, dev)
+        lde = torch.empty(n_local * w, dtype=torch.uint64, device=dev)
+        layers = torch.empty(lib.zkie2_merkle_total_digests(n_local) * 8, dtype=torch.uint64, device=dev)
+        top = torch.empty(lib.zkie2_mg_top_digests(world) * 8, dtype=torch.uint64, device=dev)
+        scr = torch.empty(lib.zkie2_mg_split_commit_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
+                          device=dev)
+        root = np.zeros(8, dtype=np.uint64)
+
+        def commit():
+            check(lib.zkie2_mg_split_commit(ctx, d_in.data_ptr(), lg_l, lg_b, w, lde.data_ptr(), layers.data_ptr(),
+                                            top.data_ptr(), scr.data_ptr(), root.ctypes.data_as(P64), sh),
+                  "mg split commit")
+        ms = _timed(commit, stream, dev, world)
+        out["split_commit"] = {"ms": round(ms, 3), "value": round(L * w / (ms / 1e3) / 1e6, 3),
+                               "unit": "Melem/s (input elements, all GPUs)",
+                               "root_matches_torch_split": bool((root == want_root).all())}
+        del d_in, lde, layers, top, scr
+        torch.cuda.empty_cache()
+        n_loc = (1 << t) // world
+        f = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 500 + rank)
+        h = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 600 + rank)
+        ch = np.array([(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(t)], dtype=np.uint64)
+        scr = torch.empty(lib.zkie2_mg_split_sumcheck_scratch_elems(t, world), dtype=torch.uint64, device=dev)
+        rounds, fin = np.zeros((t, 3), dtype=np.uint64), np.zeros(2, dtype=np.uint64)
+
+        def sumcheck():
+            check(lib.zkie2_mg_split_sumcheck(ctx, f.data_ptr(), h.data_ptr(), t, ch.ctypes.data_as(P64),
+                                              rounds.ctypes.data_as(P64), fin.ctypes.data_as(P64), scr.data_ptr(),
+                                              sh), "mg split sumcheck")
+        ms = _timed(sumcheck, stream, dev, world)
+        ok = None
+        if rank == 0:
+            F = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+            G = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+            for r in range(world):
+                synth_into(F[r * n_loc:(r + 1) * n_loc], 500 + r)
+                synth_into(G[r * n_loc:(r + 1) * n_loc], 600 + r)
+            ref = zk.sumcheck_prove(F, G, 0, ch)
+            ok = bool(np.array_equal(rounds, ref.rounds) and (int(fin[0]), int(fin[1])) == (ref.f_eval, ref.h_eval))
+            del F, G
+        dist.barrier()
+        hbm_peak, _ = hbm_peak_gbs()
+        gbs = 16 * n_loc / (ms / 1e3) / 1e9
+        out["split_sumcheck"] = {"config": f"sumcheck::prove, f and h of 2^{t} elements split over {world} GPUs",
+                                 "ms": round(ms, 4), "value": round((1 << t) / (ms / 1e3) / 1e6, 3),
+                                 "unit": "Melem/s", "rounds_match": ok,
+                                 "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                                              "unit": "GB/s per GPU", "frac": round(gbs / hbm_peak, 4)}}
+        del f, h, scr
+        torch.cuda.empty_cache()
+    finally:
+        lib.zkie2_mg_destroy(ctx)
     return out
 
 

@@ -340,6 +340,56 @@ int zkie2_lookup_num_den(const uint32_t *d_x, const uint64_t *d_y, uint64_t n, c
                          const uint64_t *d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
                          uint64_t *d_num, uint64_t *d_den, uint64_t *d_scratch, zkie_stream_t stream);
 
+/* ---- multi-GPU context (NCCL) ------------------------------------------------------- */
+/* One split commit and one split sumcheck over an NCCL communicator, one
+ * process (or host thread) per GPU, G = a power of two ranks.  No reference
+ * counterpart: the reference commits and proves on one device.  NCCL is
+ * loaded at run time (libnccl.so.2); without it these calls return
+ * cudaErrorSharedObjectInitFailed and the rest of the library is unaffected.
+ * NCCL failures return ZKIE2_MG_NCCL_ERROR_BASE + the ncclResult_t.  Every
+ * rank calls the collective entry points in the same order with the same
+ * shapes; each call synchronizes its stream before returning. */
+#define ZKIE2_MG_NCCL_ERROR_BASE 10000
+#define ZKIE2_MG_UNIQUE_ID_BYTES 128
+typedef struct zkie2_mg_ctx zkie2_mg_ctx;
+/* 1 if NCCL could be loaded. */
+int zkie2_mg_available(void);
+/* ncclGetUniqueId into h_id (128 bytes), on one rank; the caller hands it to
+ * every rank (its own transport). */
+int zkie2_mg_unique_id(uint8_t *h_id);
+/* A context with a new communicator of nranks ranks (this process = rank) on
+ * the current device (the zkie2_mg_init(ncclComm_t[]) of the survey's
+ * additive entry points, per rank). */
+int zkie2_mg_init(const uint8_t *h_id, int nranks, int rank, zkie2_mg_ctx **out);
+/* A context around a communicator the caller created (an ncclComm_t, e.g.
+ * from its own NCCL binding); not destroyed by zkie2_mg_destroy. */
+int zkie2_mg_init_comm(void *nccl_comm, zkie2_mg_ctx **out);
+int zkie2_mg_destroy(zkie2_mg_ctx *ctx);
+int zkie2_mg_rank(const zkie2_mg_ctx *ctx);
+int zkie2_mg_size(const zkie2_mg_ctx *ctx);
+/* Split commit of the L x w coefficient matrix d_coeffs (replicated on every
+ * rank, L = 2^lg_l) at blowup 2^lg_blowup, H = L << lg_blowup rows,
+ * G^2 <= H: rank g leaves with its LDE rows g, g + G, ... in d_lde
+ * ((H/G) x w), the digest layers of its contiguous leaf block
+ * [g H/G, (g+1) H/G) in d_layers (zkie2_merkle_total_digests(H/G) x 8), the
+ * layers above the G subtree roots in d_top (zkie2_mg_top_digests(G) x 8) and
+ * the root of the single-device commit (zkie2_commit) in h_root (8 u64).
+ * d_scratch: zkie2_mg_split_commit_scratch_elems (0 = unsupported shape). */
+uint64_t zkie2_mg_split_commit_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, int nranks);
+uint64_t zkie2_mg_top_digests(int nranks);
+int zkie2_mg_split_commit(zkie2_mg_ctx *ctx, const uint64_t *d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
+                          uint64_t *d_lde, uint64_t *d_layers, uint64_t *d_top, uint64_t *d_scratch,
+                          uint64_t *h_root, zkie_stream_t stream);
+/* sumcheck::prove (common/sumcheck.rs:33-79) of f, h of 2^t elements split
+ * over the G ranks by the high variables: rank g passes its 2^t / G
+ * contiguous elements [g 2^t/G, (g+1) 2^t/G) of each; h_ch the t challenges
+ * (host, the same on every rank).  Every rank receives the single-device
+ * proof: h_rounds (t x 3), h_finals (f_eval, h_eval).  log2 G <= t. */
+uint64_t zkie2_mg_split_sumcheck_scratch_elems(uint32_t t, int nranks);
+int zkie2_mg_split_sumcheck(zkie2_mg_ctx *ctx, const uint64_t *d_f, const uint64_t *d_h, uint32_t t,
+                            const uint64_t *h_ch, uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch,
+                            zkie_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

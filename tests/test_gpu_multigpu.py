@@ -178,3 +178,109 @@ def test_split_sumcheck_nccl_two_ranks(orc, tmp_path):
     want = np.concatenate([np.asarray(rounds, dtype=np.uint64).reshape(-1), np.asarray(finals, dtype=np.uint64)])
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"sc{r}.npy"), want), r
+
+
+# ---- the C-ABI multi-GPU context (zkie2_mg_*) ------------------------------------------------
+MG_COMMIT_CASES = [(14, 1, 32), (12, 2, 9), (12, 0, 8), (10, 1, 256)]
+
+
+def _mg_check_rank(zk, ctx, rank, world):
+    """Split commits and split sumchecks through the C ABI on this rank,
+    each compared with the single-device result on this rank's GPU."""
+    import ctypes as C
+    lib = zk.lib
+    s = torch.cuda.current_stream().cuda_stream
+    ok = []
+    for lg_l, lg_b, w in MG_COMMIT_CASES:
+        H = 1 << (lg_l + lg_b)
+        x = torch.from_numpy(coeffs(lg_l * 7 + w, 1 << lg_l, w).reshape(-1)).cuda()
+        n_local = H // world
+        lde = torch.empty(n_local * w, dtype=torch.uint64, device="cuda")
+        layers = torch.empty(lib.zkie2_merkle_total_digests(n_local) * 8, dtype=torch.uint64, device="cuda")
+        top = torch.empty(lib.zkie2_mg_top_digests(world) * 8, dtype=torch.uint64, device="cuda")
+        scr = torch.empty(lib.zkie2_mg_split_commit_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
+                          device="cuda")
+        root = np.zeros(8, dtype=np.uint64)
+        for _ in range(2):  # two calls in a row on the same buffers
+            rc = lib.zkie2_mg_split_commit(ctx, x.data_ptr(), lg_l, lg_b, w, lde.data_ptr(), layers.data_ptr(),
+                                           top.data_ptr(), scr.data_ptr(), root.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                           s)
+            assert rc == 0, rc
+        want = zk.commit(x.reshape(1 << lg_l, w), lg_b)
+        want_rows = want.lde.reshape(H, w)[rank::world].reshape(-1)
+        ok.append(bool(np.array_equal(root, np.asarray(want.root, dtype=np.uint64))))
+        ok.append(bool(torch.equal(lde.view(torch.int64), want_rows.view(torch.int64))))
+    for t in (20, world.bit_length() - 1, 9):
+        f, h = coeffs(40 + t, 1 << t, 1).reshape(-1), coeffs(50 + t, 1 << t, 1).reshape(-1)
+        ch = coeffs(60 + t, max(t, 1), 1).reshape(-1)[:t].copy()
+        n = (1 << t) // world
+        df = torch.from_numpy(f[rank * n:(rank + 1) * n].copy()).cuda()
+        dh = torch.from_numpy(h[rank * n:(rank + 1) * n].copy()).cuda()
+        scr = torch.empty(lib.zkie2_mg_split_sumcheck_scratch_elems(t, world), dtype=torch.uint64, device="cuda")
+        rounds = np.zeros((max(t, 1), 3), dtype=np.uint64)
+        fin = np.zeros(2, dtype=np.uint64)
+        P64 = C.POINTER(C.c_uint64)
+        rc = lib.zkie2_mg_split_sumcheck(ctx, df.data_ptr(), dh.data_ptr(), t, ch.ctypes.data_as(P64),
+                                         rounds.ctypes.data_as(P64), fin.ctypes.data_as(P64), scr.data_ptr(), s)
+        assert rc == 0, rc
+        want = zk.sumcheck_prove(f, h, 0, ch)
+        ok.append(bool(np.array_equal(rounds[:t], want.rounds)))
+        ok.append((int(fin[0]), int(fin[1])) == (want.f_eval, want.h_eval))
+    return ok
+
+
+def test_mg_context_single_rank(zk):
+    """zkie2_mg_* with a one-rank communicator: the split commit and split
+    sumcheck entry points reduce to the single-device results."""
+    import ctypes as C
+    lib = zk.lib
+    assert lib.zkie2_mg_available() == 1
+    uid = C.create_string_buffer(128)
+    assert lib.zkie2_mg_unique_id(uid) == 0
+    ctx = C.c_void_p()
+    assert lib.zkie2_mg_init(uid, 1, 0, C.byref(ctx)) == 0
+    try:
+        assert (lib.zkie2_mg_rank(ctx), lib.zkie2_mg_size(ctx)) == (0, 1)
+        assert all(_mg_check_rank(zk, ctx, 0, 1))
+    finally:
+        assert lib.zkie2_mg_destroy(ctx) == 0
+
+
+def _mg_rank(rank, world, out_dir):
+    import ctypes as C
+    import time
+    torch.cuda.set_device(rank)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import zkie_b200 as zk
+    lib = zk.lib
+    path = os.path.join(out_dir, "uid.bin")
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        assert lib.zkie2_mg_unique_id(uid) == 0
+        with open(path + ".tmp", "wb") as fh:
+            fh.write(uid.raw)
+        os.replace(path + ".tmp", path)
+    else:
+        t0 = time.time()
+        while not os.path.exists(path):
+            assert time.time() - t0 < 60, "rank 0 never wrote the NCCL id"
+            time.sleep(0.05)
+        uid = C.create_string_buffer(open(path, "rb").read(), 128)
+    ctx = C.c_void_p()
+    assert lib.zkie2_mg_init(uid, world, rank, C.byref(ctx)) == 0
+    try:
+        ok = _mg_check_rank(zk, ctx, rank, world)
+        np.save(os.path.join(out_dir, f"mg{rank}.npy"), np.array(ok))
+    finally:
+        lib.zkie2_mg_destroy(ctx)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_mg_context_two_ranks(zk, tmp_path):
+    """zkie2_mg_split_commit / zkie2_mg_split_sumcheck over a two-rank NCCL
+    communicator made by the library (zkie2_mg_unique_id + zkie2_mg_init):
+    every rank's root, LDE rows and proof equal the single-device ones."""
+    mp.start_processes(_mg_rank, args=(2, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        ok = np.load(tmp_path / f"mg{r}.npy")
+        assert ok.all(), (r, ok)

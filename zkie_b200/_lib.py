@@ -108,6 +108,18 @@ SIGNATURES = {
     "zkie2_lookup_len": (u64, [u64, u64, u32]),
     "zkie2_lookup_scratch_elems": (u64, [u64]),
     "zkie2_lookup_num_den": (i64, [vp, vp, u64, vp, vp, u64, u32, u64, u64, vp, vp, vp, vp]),
+    "zkie2_mg_available": (i64, []),
+    "zkie2_mg_unique_id": (i64, [C.c_char_p]),
+    "zkie2_mg_init": (i64, [C.c_char_p, i64, i64, C.POINTER(vp)]),
+    "zkie2_mg_init_comm": (i64, [vp, C.POINTER(vp)]),
+    "zkie2_mg_destroy": (i64, [vp]),
+    "zkie2_mg_rank": (i64, [vp]),
+    "zkie2_mg_size": (i64, [vp]),
+    "zkie2_mg_split_commit_scratch_elems": (u64, [u32, u32, u64, i64]),
+    "zkie2_mg_top_digests": (u64, [i64]),
+    "zkie2_mg_split_commit": (i64, [vp, vp, u32, u32, u64, vp, vp, vp, vp, pu64, vp]),
+    "zkie2_mg_split_sumcheck_scratch_elems": (u64, [u32, i64]),
+    "zkie2_mg_split_sumcheck": (i64, [vp, vp, vp, u32, pu64, pu64, pu64, vp, vp]),
 }
 
 if not os.path.exists(LIB_PATH):

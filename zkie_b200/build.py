@@ -89,7 +89,7 @@ def build(force: bool = False, verbose_ptxas: bool = False, jobs: int = 8) -> st
         os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)
     if need_link:
         tmp = LIB + ".tmp"
-        cmd = [nvcc()] + ARCH + ["-shared", "--cudart", "static", "-o", tmp] + objs
+        cmd = [nvcc()] + ARCH + ["-shared", "--cudart", "static", "-o", tmp] + objs + ["-ldl"]
         subprocess.check_call(cmd)
         os.replace(tmp, LIB)
     if verbose_ptxas:
