@@ -2,10 +2,10 @@
 
 Compiles oracle/zkie_oracle.c into oracle/liboracle.so with gcc + OpenMP.
 
-The reference itself is not compiled here: its CUDA files include sppark
-headers (``ff/goldilocks.hpp``, ``util/exception.cuh``) that are not in this
-tree, and its host code is Rust with no toolchain present, so there is no
-``oracle/_ref`` build.
+The reference's host code is Rust, with no toolchain present, so this C
+restatement is the CPU oracle.  The reference's two CUDA files are built
+separately, against a stand-in for the three sppark names they include, by
+``oracle/build_ref.py`` (the GPU parity tests run them beside this library).
 """
 import os
 import subprocess
