@@ -297,6 +297,52 @@ def gpu_ident(dev):
     return uuid, bus
 
 
+def gpu_local_cpus(dev):
+    """The host CPUs of the NUMA node the GPU hangs off (sysfs), or None."""
+    import torch
+    try:
+        props = torch.cuda.get_device_properties(dev)
+        sysfs = "%04x:%02x:%02x.0" % (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
+        node = int(open(f"/sys/bus/pci/devices/{sysfs}/numa_node").read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        return cpus & os.sched_getaffinity(0) or None
+    except (OSError, ValueError, AttributeError, TypeError):
+        return None
+
+
+class NumaLocal:
+    """Context manager: the calling thread runs on the CPUs of the GPU's own
+    NUMA node while the end-to-end path allocates its pinned host buffers and
+    copies, so those pages sit in that node's memory (first touch) and the
+    PCIe transfers do not cross the socket interconnect; the previous CPU set
+    comes back on exit (the CPU-baseline legs keep every host thread).  A
+    host-thread setting only: nothing on the GPU changes."""
+
+    def __init__(self, dev):
+        self.local = gpu_local_cpus(dev)
+        self.prev = None
+
+    def __enter__(self):
+        if self.local:
+            self.prev = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.local)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev:
+            os.sched_setaffinity(0, self.prev)
+        return False
+
+    def describe(self):
+        return f"pinned buffers on the GPU's NUMA node ({len(self.local)} local CPUs)" if self.local else \
+            "NUMA node of the GPU unknown: default placement"
+
+
 def max_over_ranks(x, dev):
     import torch
     import torch.distributed as dist
@@ -372,24 +418,36 @@ def main_split(args, zk, dev, world, rank):
     e2e = None
     if not args.no_e2e:
         rows = L // world
-        h_part = torch.empty(rows * w, dtype=torch.uint64, pin_memory=True)
-        h_part.view(torch.int64).copy_(d_in.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w])
-        h_lde = torch.empty(sc.n_local * w, dtype=torch.uint64, pin_memory=True)
-        h_layers = torch.empty(sc.layers.numel(), dtype=torch.uint64, pin_memory=True)
-        for _ in range(max(1, args.warmup)):
-            sc.run_host(h_part, h_lde, h_layers)
-        k_e2e = max(1, min(args.steps, 5))
-        dist.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(k_e2e):
-            r = sc.run_host(h_part, h_lde, h_layers)
-        e2e_s = max_over_ranks((time.perf_counter() - t0) / k_e2e, dev)
-        assert (r == root).all(), "host-path root differs from the device-path root"
+        numa = NumaLocal(dev)
+        with numa:
+            h_part = torch.empty(rows * w, dtype=torch.uint64, pin_memory=True)
+            h_part.view(torch.int64).copy_(d_in.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w])
+            h_lde = torch.empty(sc.n_local * w, dtype=torch.uint64, pin_memory=True)
+            h_layers = torch.empty(sc.layers.numel(), dtype=torch.uint64, pin_memory=True)
+            for _ in range(max(1, args.warmup)):
+                sc.run_host(h_part, h_lde, h_layers)
+            k_e2e = max(1, min(args.steps, 5))
+            dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(k_e2e):
+                r = sc.run_host(h_part, h_lde, h_layers)
+            e2e_s = max_over_ranks((time.perf_counter() - t0) / k_e2e, dev)
+            assert (r == root).all(), "host-path root differs from the device-path root"
+            phases = []
+            sc.run_host(h_part, h_lde, h_layers, phases)   # one more call with phase events (not in the timing)
+        ph = {k: round(max_over_ranks(v, dev), 3) for k, v in phases[0].items()}
+        lde_b, lay_b, part_b = 8 * sc.n_local * w, 8 * sc.layers.numel(), 8 * rows * w
         e2e = {"value": round(n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
                "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 8 * world * sc.layers.numel(),
                "call": "SplitCommitter.run_host (per rank: pinned 1/N input slice in, NVLink all-gather, "
-                       "split commit, LDE rows + subtree layers back to pinned host)"}
+                       "split commit, LDE rows + subtree layers back to pinned host)",
+               "host_memory": numa.describe(),
+               "phases_ms_from_start_max_over_ranks": ph,
+               "per_rank_gbs": {"upload": round(part_b / max(ph["upload"], 1e-3) / 1e6, 1),
+                                "lde_download": round(lde_b / max(ph["lde_download"] - ph["lde_done"], 1e-3) / 1e6, 1),
+                                "layers_download": round(lay_b / max(ph["layers_download"] - ph["commit"], 1e-3)
+                                                         / 1e6, 1)}}
         del h_part, h_lde, h_layers
 
     lg_local = lg_l + lg_b - sc.lg_g
@@ -559,33 +617,36 @@ def main():
 
     # ---- e2e through the host-buffer C-ABI call ----
     e2e = None
+    numa = NumaLocal(dev)
     if not args.no_e2e:
-        h_in = torch.empty(n_in, dtype=torch.uint64, pin_memory=True)
-        h_in.copy_(d_in)
-        h_lde = torch.empty(H * w, dtype=torch.uint64, pin_memory=True)
-        h_layers = torch.empty(total_dig * 8, dtype=torch.uint64, pin_memory=True)
-        h_root = torch.empty(8, dtype=torch.uint64, pin_memory=True)
-        for _ in range(max(1, args.warmup)):
-            check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
-                                        h_root.data_ptr()), "commit_host")
-        k_e2e = max(1, min(args.steps, 5))
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(k_e2e):
-            check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
-                                        h_root.data_ptr()), "commit_host")
-        e2e_s = (time.perf_counter() - t0) / k_e2e
-        if world > 1:
-            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_s = float(t.item())
-        assert (h_root.numpy() == root).all(), "host-path root differs from the device-path root"
-        e2e = {"value": round(world * n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
-               "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 64 * total_dig,
-               "call": "zkie2_commit_host (pinned input; LDE + every digest layer + root back to pinned host)"}
-        del h_in, h_lde, h_layers
+        with numa:
+            h_in = torch.empty(n_in, dtype=torch.uint64, pin_memory=True)
+            h_in.copy_(d_in)
+            h_lde = torch.empty(H * w, dtype=torch.uint64, pin_memory=True)
+            h_layers = torch.empty(total_dig * 8, dtype=torch.uint64, pin_memory=True)
+            h_root = torch.empty(8, dtype=torch.uint64, pin_memory=True)
+            for _ in range(max(1, args.warmup)):
+                check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
+                                            h_root.data_ptr()), "commit_host")
+            k_e2e = max(1, min(args.steps, 5))
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(k_e2e):
+                check(lib.zkie2_commit_host(h_in.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(), h_layers.data_ptr(),
+                                            h_root.data_ptr()), "commit_host")
+            e2e_s = (time.perf_counter() - t0) / k_e2e
+            if world > 1:
+                t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                e2e_s = float(t.item())
+            assert (h_root.numpy() == root).all(), "host-path root differs from the device-path root"
+            e2e = {"value": round(world * n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
+                   "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 64 * total_dig,
+                   "call": "zkie2_commit_host (pinned input; LDE + every digest layer + root back to pinned host)",
+                   "host_memory": numa.describe()}
+            del h_in, h_lde, h_layers
 
     # ---- MatMul shard prove (inputs resident) ----
     shard = shard_prove_ms(zk, dev)

@@ -34,6 +34,9 @@ constexpr int kHashThreads = 128;
 // states (2^16 was 13 % slower on the shard, whose 2^16-row leaf launch is
 // throughput-bound).
 constexpr uint64_t kX4MaxStates = 1ull << 14;
+// Up to this many states the sixteen-threads-per-state kernels run (a
+// quarter of the four-thread form's latency per permutation).
+constexpr uint64_t kX16MaxStates = 1ull << 11;
 
 // Leaf digests of rows [row0, row_end): sponge with rate 8, overwrite mode,
 // one permutation per full 8-block and one after a partial tail
@@ -202,6 +205,42 @@ __global__ void __launch_bounds__(kHashThreads)
     }
 }
 
+// The same with sixteen threads per state (p2_permute_x16): lane l of each
+// aligned 16-lane group holds state element l; lanes 0-7 are the rate and the
+// digest.  Groups past the end still run the permutation (full-mask
+// shuffles) but load zeros and store nothing.  Each lane loads one element
+// per absorbed block, so a group reads 64 consecutive bytes of its row.
+__global__ void __launch_bounds__(kHashThreads)
+    k_leaf_rows_x16(const uint64_t* __restrict__ mat, uint64_t* __restrict__ digests, uint64_t row0,
+                    uint64_t row_end, uint64_t w) {
+    const uint64_t row = row0 + (((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4);
+    const uint32_t l = threadIdx.x & 15;
+    const bool ok = row < row_end;
+    const uint64_t* src = mat + (ok ? row : row0) * w;
+    uint64_t x = 0;
+    const uint64_t nblk = (w + 7) >> 3;
+    for (uint64_t b = 0; b < nblk; b++) {
+        const uint64_t base = b << 3;
+        const uint64_t n = (w - base) < 8 ? (w - base) : 8;
+        if (ok && l < n) x = __ldg(src + base + l);  // overwrite the rate; a partial tail keeps stale lanes
+        x = p2_permute_x16(x, l, c_p2);
+    }
+    if (ok && l < 8) digests[row * 8 + l] = gl_canon(x);
+}
+
+__global__ void __launch_bounds__(kHashThreads)
+    k_compress_x16(const uint64_t* __restrict__ prev, uint64_t* __restrict__ next, uint64_t from, uint64_t to,
+                   uint32_t step) {
+    const uint64_t i = from + (((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4);
+    const uint32_t l = threadIdx.x & 15;
+    const bool ok = i < to;
+    // state [left(8), right(8)] (step 2) or [child(8), 0(8)] (step 1): the
+    // children are consecutive digests, so lane l reads element l of them
+    uint64_t x = (ok && l < 8 * step) ? __ldg(prev + (uint64_t)step * i * 8 + l) : 0;
+    x = p2_permute_x16(x, l, c_p2);
+    if (ok && l < 8) next[i * 8 + l] = gl_canon(x);
+}
+
 // Full permutations of a batch of 16-element states (tests and the
 // permutation throughput probe used for the integer-pipe roofline).
 __global__ void __launch_bounds__(kHashThreads)
@@ -318,7 +357,10 @@ int launch_leaf_rows(const uint64_t* mat, uint64_t* digests, uint64_t row0, uint
     if (row_end <= row0) return 0;
     if (!digests || (!mat && w != 0)) return (int)cudaErrorInvalidValue;
     const uint64_t n = row_end - row0;
-    if (n <= kX4MaxStates)
+    if (n <= kX16MaxStates)
+        k_leaf_rows_x16<<<(unsigned)ceil_div(16 * n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0,
+                                                                                       row_end, w);
+    else if (n <= kX4MaxStates)
         k_leaf_rows_x4<<<(unsigned)ceil_div(4 * n, kHashThreads), kHashThreads, 0, s>>>(mat, digests, row0, row_end,
                                                                                      w);
     else
@@ -342,7 +384,10 @@ int launch_compress(const uint64_t* prev, uint64_t* next, uint64_t from, uint64_
     if (to <= from) return 0;
     if (!prev || !next || step < 1 || step > 2) return (int)cudaErrorInvalidValue;
     const uint64_t n = to - from;
-    if (n <= kX4MaxStates)
+    if (n <= kX16MaxStates)
+        k_compress_x16<<<(unsigned)ceil_div(16 * n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to,
+                                                                                        step);
+    else if (n <= kX4MaxStates)
         k_compress_x4<<<(unsigned)ceil_div(4 * n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);
     else
         k_compress<<<(unsigned)ceil_div(n, kHashThreads), kHashThreads, 0, s>>>(prev, next, from, to, step);

@@ -206,6 +206,50 @@ __device__ __forceinline__ void p2_permute_x4(uint64_t v[4], uint32_t g, const P
         }
     }
 }
+
+// ---- sixteen threads per permutation ------------------------------------------------
+// For the most latency-bound launches (the top levels of a tree, a few rows):
+// lane l (= lane & 15) of an aligned 16-lane group holds state element l.  An
+// external round is one S-box per lane, the 4x4 block row of the lane's
+// position from three in-block shuffles, and the per-residue column sum from
+// two xor-shuffle steps; an internal round is lane 0's S-box, a four-step
+// xor-shuffle sum and one product by the lane's diagonal entry V_l.  The
+// values equal the one-thread permutation's modulo p; the critical path is
+// about a quarter of the four-thread form's.  Every lane of the warp must
+// call this (full-mask shuffles, width 16).
+__device__ __forceinline__ uint64_t p2x16_mds_light(uint64_t x, uint32_t l) {
+    // block row of position k: out_k = 2 x_k + 3 x_{k+1} + x_{k+2} + x_{k+3} (circulant [2 3 1 1])
+    const uint32_t base = l & ~3u, k = l & 3u;
+    const uint64_t x1 = __shfl_sync(0xffffffffu, x, base | ((k + 1) & 3u), 16);
+    const uint64_t x2 = __shfl_sync(0xffffffffu, x, base | ((k + 2) & 3u), 16);
+    const uint64_t x3 = __shfl_sync(0xffffffffu, x, base | ((k + 3) & 3u), 16);
+    const Acc y = acc_add(acc_add(acc_add(acc_add(acc_add(acc_sum(x, x), x1), x1), x1), x2), x3);  // < 7 2^64
+    uint64_t c = acc_reduce(y);
+    c = gl_add(c, __shfl_xor_sync(0xffffffffu, c, 4, 16));
+    c = gl_add(c, __shfl_xor_sync(0xffffffffu, c, 8, 16));
+    return acc_reduce(acc_add(y, c));
+}
+
+__device__ __forceinline__ uint64_t p2_permute_x16(uint64_t x, uint32_t l, const P2Const& c) {
+    const uint64_t vd = p2_vdiag(l, c.diag15);
+    x = p2x16_mds_light(x, l);
+#pragma unroll 1
+    for (int r = 0; r < 8; r++) {
+        x = p2x16_mds_light(p2_sbox(gl_add_c(x, c.ext[r][l])), l);
+        if (r == 3) {
+#pragma unroll 1
+            for (int q = 0; q < 22; q++) {
+                if (l == 0) x = p2_sbox(gl_add_c(x, c.internal[q]));
+                uint64_t sum = gl_add(x, __shfl_xor_sync(0xffffffffu, x, 1, 16));
+                sum = gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 2, 16));
+                sum = gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 4, 16));
+                sum = gl_canon(gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 8, 16)));
+                x = gl_add_c(gl_mul(x, vd), sum);
+            }
+        }
+    }
+    return x;
+}
 #endif
 
 }  // namespace zk

@@ -258,9 +258,13 @@ class SplitCommitter:
         src = self.top if self.G > 1 else self.layers
         return src[-8:].cpu().numpy()
 
-    def run_host(self, h_part, h_lde, h_layers):
+    def run_host(self, h_part, h_lde, h_layers, phases=None):
         """h_part: this rank's rows [g*L/G, (g+1)*L/G) of the L x w input (pinned
-        host, int64 or uint64 view); h_lde / h_layers: pinned outputs."""
+        host, int64 or uint64 view); h_lde / h_layers: pinned outputs.  With a
+        list ``phases``, appends this call's phase times in ms (CUDA events):
+        upload of the slice, NVLink all-gather of the input, the LDE, the split
+        commit, and the end of the LDE download and of the layer download, each
+        from the start of the call."""
         L = 1 << self.lg_l
         if self.full_in is None:
             self.full_in = empty(L * self.w)
@@ -269,18 +273,36 @@ class SplitCommitter:
             self.copy_stream = torch.cuda.Stream(device=self.lde.device)
             self.events = [torch.cuda.Event() for _ in range(4)]
         cur = torch.cuda.current_stream()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if phases is not None else None
+        if ev:
+            ev[0].record(cur)
         self.part.view(torch.int64).copy_(h_part.view(torch.int64), non_blocking=True)
+        if ev:
+            ev[1].record(cur)
         if self.G > 1:
             dist.all_gather_into_tensor(self.full_in.view(torch.int64), self.part.view(torch.int64), group=self.group)
         else:
             self.full_in.copy_(self.part)
+        if ev:
+            ev[2].record(cur)
         self.run(self.full_in, self.events)
+        if ev:
+            ev[3].record(cur)
         # the LDE download overlaps the hashing: the copy stream starts once
         # the LDE is complete (events[0]); the hashing only reads the LDE
         self.copy_stream.wait_event(self.events[0])
         with torch.cuda.stream(self.copy_stream):
             h_lde.view(torch.int64).copy_(self.lde.view(torch.int64), non_blocking=True)
+            if ev:
+                ev[4].record(self.copy_stream)
         h_layers.view(torch.int64).copy_(self.layers.view(torch.int64), non_blocking=True)
+        if ev:
+            ev[5].record(cur)
         cur.synchronize()
         self.copy_stream.synchronize()
+        if ev:
+            phases.append({"upload": ev[0].elapsed_time(ev[1]), "allgather": ev[0].elapsed_time(ev[2]),
+                           "lde_done": ev[0].elapsed_time(self.events[0]),
+                           "commit": ev[0].elapsed_time(ev[3]), "lde_download": ev[0].elapsed_time(ev[4]),
+                           "layers_download": ev[0].elapsed_time(ev[5])})
         return self.root()
