@@ -43,6 +43,27 @@ LG_L, W, LG_B = 20, 256, 1
 HBM_FALLBACK_GBS = 6650.0
 CPU_LABEL = "C restatement, not the reference binary"
 MULS_PER_PERM = 8 * 16 * 4 + 22 * 4 + 22
+# ALU-pipe thread instructions per Poseidon2 permutation of k_leaf_rows:
+# sm__inst_executed_pipe_alu.sum (1,428,619,264 warp instructions) x 32 over the
+# 4,194,304 permutations of one ncu capture (2^21 rows x 16 columns).
+ALU_INST_PER_PERM = 1428619264 * 32 / 4194304
+ALU_WARP_INST_PER_SM_CYCLE = 2  # integer ALU pipe: 16 lanes per cycle in each of 4 sub-partitions
+
+
+def alu_pipe_roofline(dev, perm_rate, clocks):
+    """The leaf kernel against the integer ALU pipe's issue peak (the pipe ncu
+    shows binding): achieved ALU thread-instructions per second = permutations
+    per second x ALU instructions per permutation (from the capture); peak =
+    SMs x 64 lanes x the SM clock sampled under load (else the max clock)."""
+    import torch
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = (clocks or {}).get("sm_mhz") or (clocks or {}).get("sm_max_mhz") or 1965.0
+    peak = sms * ALU_WARP_INST_PER_SM_CYCLE * 32 * mhz * 1e6
+    ach = perm_rate * ALU_INST_PER_PERM
+    return {"achieved": round(ach / 1e12, 3), "peak": round(peak / 1e12, 3), "unit": "T ALU thread-instr/s",
+            "frac": round(ach / peak, 4), "inst_per_perm": round(ALU_INST_PER_PERM, 1), "sm_mhz": mhz,
+            "source": "sm__inst_executed_pipe_alu.sum of one ncu capture of k_leaf_rows / its permutations; "
+                      "peak = 2 warp instructions per SM per cycle"}
 
 
 def workload_config(lg_l, w, lg_b, n_gpus):
@@ -487,6 +508,7 @@ def main_split(args, zk, dev, world, rank):
             "peak_source": "measured live: zkie2_gl_mul_probe, independent register-resident multiply chains",
             "perm_rate_gperm_s": round(leaf_rate / 1e9, 4), "perm_ceiling_gperm_s": round(perm_ceiling / 1e9, 4),
             "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
+            "alu_pipe": alu_pipe_roofline(dev, leaf_rate, clocks),
         },
         "roofline_ntt": {
             "bound": "hbm", "kernel": f"k_coset_twist + k_ntt_pass2 x{ntt_passes(lg_local)} (coset LDE, "
@@ -681,6 +703,7 @@ def main():
             "perm_rate_gperm_s": round(leaf_rate / 1e9, 4),
             "perm_ceiling_gperm_s": round(perm_ceiling / 1e9, 4),
             "ms_per_launch": round(leaf_ms, 4), "share_of_step": round(leaf_ms / ms_per_step, 4),
+            "alu_pipe": alu_pipe_roofline(dev, leaf_rate, clocks),
         },
         "roofline_ntt": {
             "bound": "hbm", "kernel": f"k_ntt_pass2 x{ntt_passes(lg)} (register-radix passes, LDE 2^{lg_l} -> 2^{lg})",
@@ -847,10 +870,10 @@ def projection_case(zk, dev, want_cpu, m=512, k=1024, n=4096, shift=16, iters=5)
     for it in range(iters + 2):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3), idx=idx)
+        prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3))
         torch.cuda.synchronize()
         t1 = time.perf_counter()
-        p = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3), idx=idx, h=h)
+        p = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(3), h=h)
         torch.cuda.synchronize()
         t2 = time.perf_counter()
         if it >= 2:

@@ -247,6 +247,28 @@ int zkie2_projection_witness(const uint64_t *d_h, const uint64_t *d_bias, uint64
 /* to_i32(v) as u32 of n field elements (the lookup indices of a fixed-point
  * column, fixed_point.rs to_i32). */
 int zkie2_lookup_index_i32(const uint64_t *d_v, uint64_t n, uint32_t *d_idx, zkie_stream_t stream);
+/* prove_projection (crates/zkie-ops/src/projection.rs:44-101) in one call, for
+ * x (m x k), W (k x n), bias, out, rem_off (m x n) on the device, m, k, n
+ * powers of two, 1 <= shift <= 30: h = x W (zkie2_matmul_fixed; pass d_h to
+ * reuse an h already computed, else NULL), the MatMul GKR with u, v, ch drawn
+ * from src, prove_virtual over [eq(v||u), rem_off, h, out, bias, ones] with
+ * the five affine terms, alpha and beta from src, and the logUp range check
+ * of (to_i32(rem_off) as u32, rem_off) into the table 0 .. 2^shift - 1 with
+ * full_r then cs drawn from src (lg = zkie2_projection_lookup_vars of each).
+ * Host outputs: claimed (1), mm_rounds (log2 k x 3), mm_finals (2), u (log2 m),
+ * v (log2 n), ch (log2 k), aff_rounds (log2(m n) x 3), aff_finals (6),
+ * alpha_beta (2), full_r, cs (lg each), frac_rounds (2 lg (lg - 1)),
+ * frac_finals (7 lg), frac_nd (2): the fields of the reference's
+ * ProjectionProof.  d_scratch: zkie2_projection_scratch_elems.  Synchronous. */
+uint32_t zkie2_projection_lookup_vars(uint64_t m, uint64_t n, uint32_t shift);
+uint64_t zkie2_projection_scratch_elems(uint64_t m, uint64_t k, uint64_t n, uint32_t shift);
+int zkie2_projection_prove(const uint64_t *d_x, const uint64_t *d_w, const uint64_t *d_bias, const uint64_t *d_out,
+                           const uint64_t *d_rem_off, const uint64_t *d_h, uint64_t m, uint64_t k, uint64_t n,
+                           uint32_t shift, zkie2_challenger *src, uint64_t *h_claimed, uint64_t *h_mm_rounds,
+                           uint64_t *h_mm_finals, uint64_t *h_u, uint64_t *h_v, uint64_t *h_ch,
+                           uint64_t *h_aff_rounds, uint64_t *h_aff_finals, uint64_t *h_alpha_beta,
+                           uint64_t *h_full_r, uint64_t *h_cs, uint64_t *h_frac_rounds, uint64_t *h_frac_finals,
+                           uint64_t *h_frac_nd, uint64_t *d_scratch, zkie_stream_t stream);
 /* One MatMul shard in one call: C = A W into d_c
  * (m x n), WHIR base commits of W (k*n evaluations), A (m*k) and C (m*n)
  * (pcs/whir.rs:438-469, each >= 32 evaluations), and the Op::MatMul proof

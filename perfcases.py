@@ -14,6 +14,8 @@ of the profiles (run from the repository root).
     python perfcases.py shard --m 16 --k 1024 --n 1024
     python perfcases.py split --log-size 18 --polys 32 --gpus 4
     python perfcases.py sweep
+    python perfcases.py coset --log-size 20 --polys 256 --gpus 8
+    python perfcases.py projection --m 512 --k 1024 --n 4096
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -319,6 +321,48 @@ def case_split(a):
     return {"case": "split_commit_emulated", "log_size": lg_l, "polys": w, "blowup": 1 << lb, "ranks": G, "ms": ms}
 
 
+def case_coset(a):
+    """One coset of the LDE rows as one rank of a `gpus`-way split computes it
+    (zkie2_lde_coset: the twist of the replicated input, folded when the rank
+    count exceeds the blowup, then the sub-LDE)."""
+    lg_l, w, lb, G = a.log_size, a.polys, a.lg_blowup, a.gpus
+    lg_g = G.bit_length() - 1
+    d_in = _rand((1 << lg_l) * w, 8)
+    rows = 1 << (lg_l + lb - lg_g)
+    out = torch.empty(rows * w, dtype=torch.uint64, device="cuda")
+    scr = torch.empty(max(lib.zkie2_lde_coset_scratch_elems(lg_l, lb, w, lg_g), 2), dtype=torch.uint64,
+                      device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        check(lib.zkie2_lde_coset(d_in.data_ptr(), out.data_ptr(), scr.data_ptr(), lg_l, lb, w, lg_g, G - 1, s),
+              "lde_coset")
+    ms = _time(run, a.iters)
+    return {"case": "lde_coset", "log_size": lg_l, "polys": w, "blowup": 1 << lb, "ranks": G, "ms": ms,
+            "algorithmic_bytes": 8 * w * ((1 << lg_l) + rows)}
+
+
+def case_projection(a):
+    """prove_projection (the projection block) of x (m x k) @ W (k x n),
+    16-bit fixed-point inputs, shift 16, inputs and witness resident."""
+    from zkie_b200.gkr import XorShift64, matmul_fixed
+    from zkie_b200.projection import projection_witness, prove_projection
+    m, k, n, shift = a.m, a.k, a.n, 16
+    g = np.random.default_rng(11)
+
+    def fx(size, lim):
+        x = g.integers(-lim, lim, size=size, dtype=np.int64)
+        return torch.from_numpy(x.astype(np.uint64) + np.where(x < 0, np.uint64(P), np.uint64(0))).cuda()
+    x, w, b = fx(m * k, 1 << 15), fx(k * n, 1 << 15), fx(m * n, 1 << 20)
+    h, _ = matmul_fixed(x, w, m, k, n)
+    out, rem, idx = projection_witness(h, b, shift)
+
+    def run():
+        prove_projection(x, w, b, out, rem, m, k, n, shift, XorShift64(3))
+    ms = _time(run, a.iters)
+    return {"case": "prove_projection", "m": m, "k": k, "n": n, "shift": shift, "ms": ms}
+
+
 def case_sweep(a):
     """batches of 1, 16, 256 polynomials of 2^16,
     2^20, 2^24 coefficients at blowup 2 and 4.  One JSON line per case that
@@ -377,7 +421,7 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup", "grind", "fixed", "cache"])
+                                         "logup", "grind", "fixed", "cache", "coset", "projection"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -392,7 +436,7 @@ def main(argv=None):
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
            "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "cache": case_cache, "sop": case_sop, "shard": case_shard, "split": case_split,
-           "sweep": case_sweep}[a.case](a)
+           "sweep": case_sweep, "coset": case_coset, "projection": case_projection}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 

@@ -73,10 +73,16 @@ def test_split_committer_run_host_single_rank(zk):
     h_part = torch.from_numpy(x.view(np.int64).reshape(-1).copy()).pin_memory()
     h_lde = torch.empty(H * w, dtype=torch.int64).pin_memory()
     h_layers = torch.empty(zk.lib.zkie2_merkle_total_digests(H) * 8, dtype=torch.int64).pin_memory()
-    for _ in range(2):
+    for call in range(2):
         h_lde.zero_()
         h_layers.zero_()
-        root = sc.run_host(h_part, h_lde, h_layers)
+        phases = [] if call else None  # the second call also records its phase times
+        root = sc.run_host(h_part, h_lde, h_layers, phases)
+        if call:
+            ph = phases[0]
+            assert set(ph) == {"upload", "allgather", "lde_done", "commit", "lde_download", "layers_download"}
+            assert 0 <= ph["upload"] <= ph["allgather"] <= ph["lde_done"] <= ph["commit"] <= ph["layers_download"]
+            assert ph["lde_done"] <= ph["lde_download"]
         assert torch.equal(h_lde, want_lde)
         assert torch.equal(h_layers, want_layers)
         assert np.array_equal(np.asarray(root).view(np.uint64), np.asarray(want.root, dtype=np.uint64))

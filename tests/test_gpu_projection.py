@@ -97,7 +97,7 @@ def test_fixed_point_shapes_match_oracle(zk, orc, m, k, n, shift):
     h, _ = zk.matmul_fixed(x, w, m, k, n, force_tensor=True)
     out, rem, idx = projection_witness(h, b, shift)
     ids = [[7, 8, 9]]
-    got = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.shard_dag_child(ids, 1, 0), idx=idx, h=h)
+    got = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.shard_dag_child(ids, 1, 0), h=h)
     exp = orc.projection_prove(x, w, b, out.cpu().numpy(), rem.cpu().numpy(), m, k, n, shift,
                                orc.shard_dag_child(ids, 1, 0))
     assert np.array_equal(h.cpu().numpy(), exp["h"])
@@ -119,7 +119,7 @@ def test_gpt2_projection_shape(zk, orc):
     h, path = zk.matmul_fixed(x, w, m, k, n)
     assert path == 0
     out, rem, idx = projection_witness(h, b, shift)
-    got = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(5), idx=idx, h=h)
+    got = prove_projection(x, w, b, out, rem, m, k, n, shift, zk.XorShift64(5), h=h)
     assert got.matmul.claimed == orc.mle_eval(h.cpu().numpy(), got.pt)
     orng = orc.XorShift64(5)
     lg = (m * n + (1 << shift) - 1).bit_length()

@@ -89,6 +89,10 @@ SIGNATURES = {
     "zkie2_matmul_fixed_scratch_elems": (u64, [u64, u64, u64]),
     "zkie2_projection_witness": (i64, [vp, vp, u64, u32, vp, vp, vp, vp]),
     "zkie2_lookup_index_i32": (i64, [vp, u64, vp, vp]),
+    "zkie2_projection_lookup_vars": (u32, [u64, u64, u32]),
+    "zkie2_projection_scratch_elems": (u64, [u64, u64, u64, u32]),
+    "zkie2_projection_prove": (i64, [vp, vp, vp, vp, vp, vp, u64, u64, u64, u32, PCh, pu64, pu64, pu64, pu64, pu64,
+                                     pu64, pu64, pu64, pu64, pu64, pu64, pu64, pu64, pu64, vp, vp]),
     "zkie2_matmul_fixed": (i64, [vp, vp, u64, u64, u64, vp, u32, pu32, vp, vp]),
     "zkie2_shard_prove_matmul_scratch_elems": (u64, [u64, u64, u64]),
     "zkie2_shard_prove_matmul": (i64, [vp, vp, u64, u64, u64, pu64, u64, u64, vp, pu64, pu64, pu64, pu64, pu64,

@@ -581,17 +581,62 @@ __global__ void __launch_bounds__(kTwistThreads)
         fac[i] = j < L ? coset_factor(j, g, lg_h) : 0;
     }
     __syncthreads();
-    const uint64_t n = (uint64_t)rows * w;
-    for (uint64_t e = threadIdx.x; e < n; e += kTwistThreads) {
-        const uint32_t r = (uint32_t)(e / w);
-        const uint64_t c = e - (uint64_t)r * w, jp = r0 + r;
+    // walk the tile's elements with the row / column pair advanced by the
+    // stride (no division per element)
+    uint32_t r = 0;
+    uint64_t c = threadIdx.x;
+    while (c >= w && r < rows) {
+        c -= w;
+        r++;
+    }
+    if (nfold == 1) {
+        // no fold (G <= blowup): a pointwise twist; four elements per
+        // iteration so that four reads are in flight per thread
+        while (r < rows) {
+            uint32_t rr[4];
+            uint64_t cc[4], v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                rr[u] = r;
+                cc[u] = c;
+                if (r < rows) {
+                    const uint64_t j = r0 + r;
+                    v[u] = j < L ? __ldg(x + j * w + c) : 0ull;
+                    c += kTwistThreads;
+                    while (c >= w && r < rows) {
+                        c -= w;
+                        r++;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (rr[u] < rows) y[(r0 + rr[u]) * w + cc[u]] = gl_canon(gl_mul(v[u], fac[rr[u]]));
+        }
+        return;
+    }
+    for (; r < rows;) {
+        const uint64_t jp = r0 + r;
         Acc160 acc = acc160_zero();
-        for (uint32_t m = 0; m < nfold; m++) {
-            const uint64_t j = jp + m * stride;
-            if (j >= L) break;
-            acc160_mac(acc, __ldg(x + j * w + c), fac[r * nfold + m]);
+        // fold terms four at a time, their loads issued before the products
+        // (several reads in flight per thread; rows at or past L read nothing)
+        for (uint32_t m0 = 0; m0 < nfold; m0 += 4) {
+            uint64_t v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t j = jp + (uint64_t)(m0 + u) * stride;
+                v[u] = (m0 + u < nfold && j < L) ? __ldg(x + j * w + c) : 0ull;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (m0 + u < nfold) acc160_mac(acc, v[u], fac[r * nfold + m0 + u]);
         }
         y[jp * w + c] = gl_canon(acc160_reduce(acc));
+        c += kTwistThreads;
+        while (c >= w && r < rows) {
+            c -= w;
+            r++;
+        }
     }
 }
 

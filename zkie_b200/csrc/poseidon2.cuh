@@ -197,9 +197,17 @@ __device__ __forceinline__ void p2_permute_x4(uint64_t v[4], uint32_t g, const P
         if (r == 3) {
 #pragma unroll 1
             for (int q = 0; q < 22; q++) {
-                if (g == 0) v[0] = p2_sbox(gl_add_c(v[0], c.internal[q]));
-                const Acc a = acc_add(acc_add(acc_sum(v[0], v[1]), v[2]), v[3]);
-                const uint64_t sum = gl_canon(p2x4_group_sum(acc_reduce(a)));
+                // Lane 0's S-box and the sum of the other fifteen lanes are
+                // independent: every thread computes the S-box of its v[0]
+                // (only group lane g = 0's is used; the warp issues it either
+                // way) while the partial sum's shuffles run, then lane 0's
+                // result is broadcast and added.
+                const uint64_t t = p2_sbox(gl_add_c(v[0], c.internal[q]));
+                const Acc a = acc_add(acc_add(acc_sum(v[1], v[2]), v[3]), g ? v[0] : 0ull);
+                const uint64_t part = p2x4_group_sum(acc_reduce(a));
+                const uint64_t t0 = __shfl_sync(0xffffffffu, t, 0, 4);
+                const uint64_t sum = gl_canon(gl_add(part, t0));
+                if (g == 0) v[0] = t;
 #pragma unroll
                 for (int j = 0; j < 4; j++) v[j] = gl_add_c(gl_mul(v[j], vd[j]), sum);
             }
@@ -239,12 +247,16 @@ __device__ __forceinline__ uint64_t p2_permute_x16(uint64_t x, uint32_t l, const
         if (r == 3) {
 #pragma unroll 1
             for (int q = 0; q < 22; q++) {
-                if (l == 0) x = p2_sbox(gl_add_c(x, c.internal[q]));
-                uint64_t sum = gl_add(x, __shfl_xor_sync(0xffffffffu, x, 1, 16));
-                sum = gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 2, 16));
-                sum = gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 4, 16));
-                sum = gl_canon(gl_add(sum, __shfl_xor_sync(0xffffffffu, sum, 8, 16)));
-                x = gl_add_c(gl_mul(x, vd), sum);
+                // lane 0's S-box overlaps the shuffle sum of lanes 1-15 (as in
+                // the four-thread form), then is broadcast into the sum
+                const uint64_t t = p2_sbox(gl_add_c(x, c.internal[q]));
+                uint64_t part = l ? x : 0ull;
+                part = gl_add(part, __shfl_xor_sync(0xffffffffu, part, 1, 16));
+                part = gl_add(part, __shfl_xor_sync(0xffffffffu, part, 2, 16));
+                part = gl_add(part, __shfl_xor_sync(0xffffffffu, part, 4, 16));
+                part = gl_add(part, __shfl_xor_sync(0xffffffffu, part, 8, 16));
+                const uint64_t sum = gl_canon(gl_add(part, __shfl_sync(0xffffffffu, t, 0, 16)));
+                x = gl_add_c(gl_mul(l ? x : t, vd), sum);
             }
         }
     }

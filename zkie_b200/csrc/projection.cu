@@ -11,9 +11,12 @@
 // host with div_round (:136-176): q = floor(a / 2^shift), plus one when the
 // remainder is at least half.  Values are signed fixed point embedded in the
 // field (fixed_point.rs: from_i64 / to_i64 / to_i32).
+#include <cstring>
+
 #include "../../include/zkie2.h"
 #include "common.cuh"
 #include "gl64.cuh"
+#include "internal.h"
 
 namespace zk {
 
@@ -64,9 +67,57 @@ __global__ void k_lookup_index_i32(const uint64_t* __restrict__ v, uint64_t n, u
         idx[i] = to_i32_index(__ldg(v + i));
 }
 
+__global__ void k_fill_const(uint64_t* __restrict__ out, uint64_t n, uint64_t v) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = v;
+}
+
+__global__ void k_fill_iota(uint64_t* __restrict__ out, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = i;
+}
+
 unsigned grid_for(uint64_t n) {
     const uint64_t b = ceil_div(n, kThreads);
     return (unsigned)(b < 148ull * 16 ? b : 148ull * 16);
+}
+
+bool is_pow2(uint64_t x) { return x && !(x & (x - 1)); }
+
+uint32_t lg_of(uint64_t x) {
+    uint32_t r = 0;
+    while ((1ull << r) < x) r++;
+    return r;
+}
+
+// Scratch layout of zkie2_projection_prove (u64 elements, each region even-sized).
+struct ProjLayout {
+    uint64_t h, eq, ones, table, idx, num, den, fixed, op, virt, look, frac, total;
+};
+
+ProjLayout proj_layout(uint64_t m, uint64_t k, uint64_t n, uint32_t shift) {
+    ProjLayout L{};
+    uint64_t off = 0;
+    auto take = [&](uint64_t& at, uint64_t cnt) {
+        at = off;
+        off += (cnt + 1) & ~1ull;
+    };
+    const uint64_t mn = m * n, t = 1ull << shift;
+    const uint64_t frac_n = zkie2_lookup_len(mn, t, 0);
+    take(L.h, mn);
+    take(L.eq, mn);
+    take(L.ones, mn);
+    take(L.table, t);
+    take(L.idx, (mn + 1) / 2);
+    take(L.num, frac_n);
+    take(L.den, frac_n);
+    take(L.fixed, zkie2_matmul_fixed_scratch_elems(m, k, n));
+    take(L.op, zkie2_op_matmul_scratch_elems(m, k, n));
+    take(L.virt, zkie2_virtual_scratch_elems(6, lg_of(mn)));
+    take(L.look, zkie2_lookup_scratch_elems(t));
+    take(L.frac, zkie2_fractional_scratch_elems(lg_of(frac_n)));
+    L.total = off;
+    return L;
 }
 
 }  // namespace
@@ -93,6 +144,92 @@ int zkie2_lookup_index_i32(const uint64_t* d_v, uint64_t n, uint32_t* d_idx, cud
     k_lookup_index_i32<<<grid_for(n), kThreads, 0, stream>>>(d_v, n, d_idx);
     ZK_LAUNCH_CHECK();
     return 0;
+}
+
+uint32_t zkie2_projection_lookup_vars(uint64_t m, uint64_t n, uint32_t shift) {
+    if (shift < 1 || shift > 30) return 0;
+    return lg_of(zkie2_lookup_len(m * n, 1ull << shift, 0));
+}
+
+uint64_t zkie2_projection_scratch_elems(uint64_t m, uint64_t k, uint64_t n, uint32_t shift) {
+    if (!is_pow2(m) || !is_pow2(k) || !is_pow2(n) || shift < 1 || shift > 30) return 0;
+    return proj_layout(m, k, n, shift).total;
+}
+
+// prove_projection (crates/zkie-ops/src/projection.rs:44-101) in one call:
+//   h = x W (mm_par_fixed, unless the caller passes h), the MatMul GKR with u,
+//   v, ch drawn from src (matmul::prove(x^T, W, h, u, v, ch): the Op::MatMul
+//   kernels), prove_virtual over [eq(v||u), rem_off, h, out, bias, ones] with
+//   the five affine terms, alpha and beta from src, the merged lookup columns
+//   of (to_i32(rem_off) as u32, rem_off) into the table 0 .. 2^shift - 1 and
+//   their fraction tree (full_r then cs from src).  The challenger advances
+//   exactly as the reference's does.  Synchronous.
+int zkie2_projection_prove(const uint64_t* d_x, const uint64_t* d_w, const uint64_t* d_bias, const uint64_t* d_out,
+                           const uint64_t* d_rem_off, const uint64_t* d_h, uint64_t m, uint64_t k, uint64_t n,
+                           uint32_t shift, zkie2_challenger* src, uint64_t* h_claimed, uint64_t* h_mm_rounds,
+                           uint64_t* h_mm_finals, uint64_t* h_u, uint64_t* h_v, uint64_t* h_ch,
+                           uint64_t* h_aff_rounds, uint64_t* h_aff_finals, uint64_t* h_alpha_beta,
+                           uint64_t* h_full_r, uint64_t* h_cs, uint64_t* h_frac_rounds, uint64_t* h_frac_finals,
+                           uint64_t* h_frac_nd, uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_x || !d_w || !d_bias || !d_out || !d_rem_off || !src || !d_scratch || !h_claimed || !h_mm_finals ||
+        !h_aff_finals || !h_alpha_beta || !h_frac_nd)
+        return (int)cudaErrorInvalidValue;
+    if (!is_pow2(m) || !is_pow2(k) || !is_pow2(n) || shift < 1 || shift > 30) return (int)cudaErrorInvalidValue;
+    const uint64_t mn = m * n, t = 1ull << shift;
+    const uint32_t lm = lg_of(m), lk = lg_of(k), ln = lg_of(n), tv = lm + ln;
+    const uint64_t frac_n = zkie2_lookup_len(mn, t, 0);
+    const uint32_t lg = lg_of(frac_n);
+    if (lm > 32 || lk > 32 || ln > 32) return (int)cudaErrorInvalidValue;
+    if ((lk && (!h_mm_rounds || !h_ch)) || (lm && !h_u) || (ln && !h_v) || (tv && !h_aff_rounds) ||
+        (lg && (!h_full_r || !h_cs || !h_frac_finals)) || (lg > 1 && !h_frac_rounds))
+        return (int)cudaErrorInvalidValue;
+    const ProjLayout L = proj_layout(m, k, n, shift);
+    uint64_t* S = d_scratch;
+    const uint64_t* h = d_h;
+    int rc = 0;
+    if (!h) {
+        rc = zkie2_matmul_fixed(d_x, d_w, m, k, n, S + L.h, 0, nullptr, S + L.fixed, stream);
+        if (rc) return rc;
+        h = S + L.h;
+    }
+    uint64_t claims[3];
+    uint64_t u_buf[64], v_buf[64], ch_buf[64];
+    rc = zkie2_op_matmul_prove(d_x, d_w, h, m, k, n, src, u_buf, v_buf, ch_buf, h_claimed, h_mm_rounds, h_mm_finals,
+                               claims, S + L.op, stream);
+    if (rc) return rc;
+    if (lm) std::memcpy(h_u, u_buf, 8ull * lm);
+    if (ln) std::memcpy(h_v, v_buf, 8ull * ln);
+    if (lk) std::memcpy(h_ch, ch_buf, 8ull * lk);
+    // the affine constraint at pt = v || u
+    uint64_t pt[64];
+    for (uint32_t i = 0; i < ln; i++) pt[i] = v_buf[i];
+    for (uint32_t i = 0; i < lm; i++) pt[ln + i] = u_buf[i];
+    rc = zkie2_eq_evals(pt, tv, S + L.eq, stream);
+    if (rc) return rc;
+    k_fill_const<<<grid_for(mn), kThreads, 0, stream>>>(S + L.ones, mn, 1);
+    ZK_LAUNCH_CHECK();
+    const uint64_t neg = kP - 1, two = 1ull << shift, half = 1ull << (shift - 1);
+    const uint64_t coeffs[5] = {1, neg, two, gl_mul_host(neg, two), gl_mul_host(neg, half)};
+    const uint32_t idx_off[6] = {0, 2, 4, 6, 8, 10};
+    const uint32_t idx[10] = {0, 1, 0, 2, 0, 3, 0, 4, 0, 5};
+    const uint64_t* mles[6] = {S + L.eq, d_rem_off, h, d_out, d_bias, S + L.ones};
+    rc = zkie2_virtual_prove(mles, 6, tv, coeffs, idx_off, idx, 5, pt, h_aff_rounds, h_aff_finals, S + L.virt, stream);
+    if (rc) return rc;
+    // the range check: alpha, beta, then the fraction tree's own draws
+    h_alpha_beta[0] = zkie2_challenger_field(src);
+    h_alpha_beta[1] = zkie2_challenger_field(src);
+    k_fill_iota<<<grid_for(t), kThreads, 0, stream>>>(S + L.table, t);
+    ZK_LAUNCH_CHECK();
+    uint32_t* d_idx = reinterpret_cast<uint32_t*>(S + L.idx);
+    rc = zkie2_lookup_index_i32(d_rem_off, mn, d_idx, stream);
+    if (!rc)
+        rc = zkie2_lookup_num_den(d_idx, d_rem_off, mn, S + L.table, nullptr, t, 0, h_alpha_beta[0], h_alpha_beta[1],
+                                  S + L.num, S + L.den, S + L.look, stream);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < lg; i++) h_full_r[i] = zkie2_challenger_field(src);
+    for (uint32_t i = 0; i < lg; i++) h_cs[i] = zkie2_challenger_field(src);
+    return zkie2_fractional_prove(S + L.num, S + L.den, lg, h_full_r, h_cs, h_frac_rounds, h_frac_finals, h_frac_nd,
+                                  S + L.frac, stream);
 }
 
 }  // extern "C"

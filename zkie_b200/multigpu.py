@@ -271,7 +271,7 @@ class SplitCommitter:
             self.part = empty(L * self.w // self.G)
         if self.copy_stream is None:
             self.copy_stream = torch.cuda.Stream(device=self.lde.device)
-            self.events = [torch.cuda.Event() for _ in range(4)]
+            self.events = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         cur = torch.cuda.current_stream()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)] if phases is not None else None
         if ev:
