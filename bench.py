@@ -319,21 +319,42 @@ def gpu_ident(dev):
 
 
 def gpu_local_cpus(dev):
-    """The host CPUs of the NUMA node the GPU hangs off (sysfs), or None."""
+    """(host CPUs close to the GPU, how they were found), or (None, why not):
+    the NUMA node of the GPU's PCI function in sysfs, else NVML's CPU
+    affinity of the device (a read-only query)."""
     import torch
+    allowed = os.sched_getaffinity(0)
     try:
         props = torch.cuda.get_device_properties(dev)
-        sysfs = "%04x:%02x:%02x.0" % (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
-        node = int(open(f"/sys/bus/pci/devices/{sysfs}/numa_node").read().strip())
-        if node < 0:
-            return None
-        cpus = set()
-        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
-            lo, _, hi = part.partition("-")
-            cpus.update(range(int(lo), int(hi or lo) + 1))
-        return cpus & os.sched_getaffinity(0) or None
-    except (OSError, ValueError, AttributeError, TypeError):
-        return None
+        dom, bus, devn = int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id)
+    except (AttributeError, TypeError, ValueError):
+        return None, "no PCI id"
+    try:
+        node = int(open("/sys/bus/pci/devices/%04x:%02x:%02x.0/numa_node" % (dom, bus, devn)).read().strip())
+        if node >= 0:
+            cpus = set()
+            for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+            if cpus & allowed:
+                return cpus & allowed, f"sysfs NUMA node {node}"
+    except (OSError, ValueError):
+        pass
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(("%08X:%02X:%02X.0" % (dom, bus, devn)).encode())
+            words = (os.cpu_count() + 63) // 64
+            masks = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+            cpus = {64 * i + b for i, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+            if cpus & allowed and cpus & allowed != allowed:
+                return cpus & allowed, "NVML CPU affinity"
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # NVML absent or the query unsupported on this box
+        pass
+    return None, "no NUMA locality reported (sysfs numa_node -1, NVML affinity = all CPUs)"
 
 
 class NumaLocal:
@@ -345,7 +366,7 @@ class NumaLocal:
     host-thread setting only: nothing on the GPU changes."""
 
     def __init__(self, dev):
-        self.local = gpu_local_cpus(dev)
+        self.local, self.how = gpu_local_cpus(dev)
         self.prev = None
 
     def __enter__(self):
@@ -360,8 +381,9 @@ class NumaLocal:
         return False
 
     def describe(self):
-        return f"pinned buffers on the GPU's NUMA node ({len(self.local)} local CPUs)" if self.local else \
-            "NUMA node of the GPU unknown: default placement"
+        if self.local:
+            return f"pinned buffers allocated on {len(self.local)} CPUs close to the GPU ({self.how})"
+        return f"default placement: {self.how}"
 
 
 def max_over_ranks(x, dev):
@@ -433,13 +455,16 @@ def main_split(args, zk, dev, world, rank):
     ntt_bytes = 8 * w * (L + sc.n_local)
     ntt_gbs = ntt_bytes / (ntt_ms / 1e3) / 1e9
 
-    # e2e: each rank copies its 1/N row slice of the pinned host input in,
-    # the full input is all-gathered over NVLink, and each rank copies its LDE
-    # rows and subtree layers back to pinned host memory
-    e2e = None
+    # e2e through the C-ABI context (the headline host-buffer path), then the
+    # torch-orchestrated one with per-phase times: each rank copies its 1/N
+    # row slice of the pinned host input in, the full input is all-gathered
+    # over NVLink, and each rank copies its LDE rows and subtree layers back
+    ctx = mg_context(zk, rank, world)
+    e2e, e2e_torch = None, None
     if not args.no_e2e:
         rows = L // world
         numa = NumaLocal(dev)
+        e2e = e2e_mg(zk, dev, ctx, rank, world, lg_l, lg_b, w, d_in, root, numa, args.warmup, args.steps)
         with numa:
             h_part = torch.empty(rows * w, dtype=torch.uint64, pin_memory=True)
             h_part.view(torch.int64).copy_(d_in.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w])
@@ -459,10 +484,10 @@ def main_split(args, zk, dev, world, rank):
             sc.run_host(h_part, h_lde, h_layers, phases)   # one more call with phase events (not in the timing)
         ph = {k: round(max_over_ranks(v, dev), 3) for k, v in phases[0].items()}
         lde_b, lay_b, part_b = 8 * sc.n_local * w, 8 * sc.layers.numel(), 8 * rows * w
-        e2e = {"value": round(n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
+        e2e_torch = {"value": round(n_in / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
                "h2d_bytes_per_step": 8 * n_in, "d2h_bytes_per_step": 8 * H * w + 8 * world * sc.layers.numel(),
                "call": "SplitCommitter.run_host (per rank: pinned 1/N input slice in, NVLink all-gather, "
-                       "split commit, LDE rows + subtree layers back to pinned host)",
+                       "split commit, LDE rows + subtree layers back to pinned host; not pipelined)",
                "host_memory": numa.describe(),
                "phases_ms_from_start_max_over_ranks": ph,
                "per_rank_gbs": {"upload": round(part_b / max(ph["upload"], 1e-3) / 1e6, 1),
@@ -491,7 +516,8 @@ def main_split(args, zk, dev, world, rank):
     shard["roofline"] = shard_roofline(zk, dev, shard_dev_ms, perm_ceiling)
     big = big_commits(zk, dev, rank, world) if not args.no_big else {}
     split_sc = sumcheck_case(zk, dev, rank, world)
-    mg = mg_case(zk, dev, rank, world, lg_l, lg_b, w, root)
+    mg = mg_case(zk, dev, ctx, rank, world, lg_l, lg_b, w, root)
+    lib.zkie2_mg_destroy(ctx)
     cfg = workload_config(lg_l, w, lg_b, world)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -528,6 +554,8 @@ def main_split(args, zk, dev, world, rank):
     }
     if e2e:
         line["e2e"] = e2e
+    if e2e_torch:
+        line["e2e_torch_split"] = e2e_torch
     line["shard_prove"] = shard
     line.update(big)
     line["split_sumcheck"] = split_sc
@@ -1098,11 +1126,75 @@ def big_commits(zk, dev, rank, world):
     return out
 
 
-def mg_case(zk, dev, rank, world, lg_l, lg_b, w, want_root, t=28):
+def mg_context(zk, rank, world):
+    """The library's multi-GPU context over a communicator it makes from an
+    NCCL id that rank 0 creates and torch.distributed broadcasts."""
+    import ctypes as C
+
+    import torch.distributed as dist
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        zk.check(zk.lib.zkie2_mg_unique_id(uid), "mg unique id")
+    box = [uid.raw if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    uid = C.create_string_buffer(box[0], 128)
+    ctx = C.c_void_p()
+    zk.check(zk.lib.zkie2_mg_init(uid, world, rank, C.byref(ctx)), "mg init")
+    return ctx
+
+
+def e2e_mg(zk, dev, ctx, rank, world, lg_l, lg_b, w, d_in, want_root, numa, warmup, steps):
+    """The end-to-end split commit through the C-ABI context
+    (zkie2_mg_split_commit_host): per rank, its pinned 1/N row slice of the
+    input in, column blocks pipelined (upload, NVLink all-gather of the
+    block, coset LDE and leaf absorption, download of the block's LDE rows),
+    its LDE rows and subtree layers back to pinned host memory."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    lib = zk.lib
+    L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+    rows, n_local = L // world, H // world
+    with numa:
+        h_part = torch.empty(rows * w, dtype=torch.uint64, pin_memory=True)
+        h_part.view(torch.int64).copy_(d_in.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w])
+        h_lde = torch.empty(n_local * w, dtype=torch.uint64, pin_memory=True)
+        n_lay = lib.zkie2_merkle_total_digests(n_local) * 8
+        h_layers = torch.empty(n_lay, dtype=torch.uint64, pin_memory=True)
+        scr = torch.empty(lib.zkie2_mg_split_commit_host_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
+                          device=dev)
+        root = np.zeros(8, dtype=np.uint64)
+        rp = root.ctypes.data_as(C.POINTER(C.c_uint64))
+
+        def call():
+            zk.check(lib.zkie2_mg_split_commit_host(ctx, h_part.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(),
+                                                    h_layers.data_ptr(), rp, scr.data_ptr()), "mg split commit host")
+        for _ in range(max(1, warmup)):
+            call()
+        k_e2e = max(1, min(steps, 5))
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(k_e2e):
+            call()
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / k_e2e, dev)
+        assert (root == want_root).all(), "host-path root differs from the device-path root"
+    del h_part, h_lde, h_layers, scr
+    torch.cuda.empty_cache()
+    return {"value": round(L * w / e2e_s / 1e6, 3), "unit": UNIT, "ms_per_step": round(1e3 * e2e_s, 3),
+            "h2d_bytes_per_step": 8 * L * w, "d2h_bytes_per_step": 8 * H * w + 8 * world * n_lay,
+            "call": "zkie2_mg_split_commit_host (per rank: pinned 1/N row slice in, column blocks pipelined: "
+                    "upload, NVLink all-gather, coset LDE + leaf absorption, LDE rows down; subtree layers back "
+                    "to pinned host)",
+            "host_memory": numa.describe()}
+
+
+def mg_case(zk, dev, ctx, rank, world, lg_l, lg_b, w, want_root, t=28):
     """The same split commit and a 2^t split sumcheck through the library's
-    own multi-GPU context (zkie2_mg_init over a communicator the library
-    creates from an NCCL id broadcast by rank 0; zkie2_mg_split_commit,
-    zkie2_mg_split_sumcheck): the path a non-Python host drives.  ms per call
+    own multi-GPU context (zkie2_mg_split_commit, zkie2_mg_split_sumcheck):
+    the path a non-Python host drives.  ms per call
     (CUDA events around the synchronous calls, max over ranks); the root is
     compared with the torch-orchestrated split above, the proof with the
     single-GPU sumcheck on rank 0."""
@@ -1113,72 +1205,61 @@ def mg_case(zk, dev, rank, world, lg_l, lg_b, w, want_root, t=28):
     import torch.distributed as dist
     lib, check = zk.lib, zk.check
     P64 = C.POINTER(C.c_uint64)
-    uid = C.create_string_buffer(128)
-    if rank == 0:
-        check(lib.zkie2_mg_unique_id(uid), "mg unique id")
-    box = [uid.raw if rank == 0 else None]
-    dist.broadcast_object_list(box, src=0)
-    uid = C.create_string_buffer(box[0], 128)
-    ctx = C.c_void_p()
-    check(lib.zkie2_mg_init(uid, world, rank, C.byref(ctx)), "mg init")
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     out = {}
-    try:
-        L, H = 1 << lg_l, 1 << (lg_l + lg_b)
-        n_local = H // world
-        d_in = synth_device(L * w, 1234, dev)
-        lde = torch.empty(n_local * w, dtype=torch.uint64, device=dev)
-        layers = torch.empty(lib.zkie2_merkle_total_digests(n_local) * 8, dtype=torch.uint64, device=dev)
-        top = torch.empty(lib.zkie2_mg_top_digests(world) * 8, dtype=torch.uint64, device=dev)
-        scr = torch.empty(lib.zkie2_mg_split_commit_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
-                          device=dev)
-        root = np.zeros(8, dtype=np.uint64)
+    L, H = 1 << lg_l, 1 << (lg_l + lg_b)
+    n_local = H // world
+    d_in = synth_device(L * w, 1234, dev)
+    lde = torch.empty(n_local * w, dtype=torch.uint64, device=dev)
+    layers = torch.empty(lib.zkie2_merkle_total_digests(n_local) * 8, dtype=torch.uint64, device=dev)
+    top = torch.empty(lib.zkie2_mg_top_digests(world) * 8, dtype=torch.uint64, device=dev)
+    scr = torch.empty(lib.zkie2_mg_split_commit_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
+                      device=dev)
+    root = np.zeros(8, dtype=np.uint64)
 
-        def commit():
-            check(lib.zkie2_mg_split_commit(ctx, d_in.data_ptr(), lg_l, lg_b, w, lde.data_ptr(), layers.data_ptr(),
-                                            top.data_ptr(), scr.data_ptr(), root.ctypes.data_as(P64), sh),
-                  "mg split commit")
-        ms = _timed(commit, stream, dev, world)
-        out["split_commit"] = {"ms": round(ms, 3), "value": round(L * w / (ms / 1e3) / 1e6, 3),
-                               "unit": "Melem/s (input elements, all GPUs)",
-                               "root_matches_torch_split": bool((root == want_root).all())}
-        del d_in, lde, layers, top, scr
-        torch.cuda.empty_cache()
-        n_loc = (1 << t) // world
-        f = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 500 + rank)
-        h = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 600 + rank)
-        ch = np.array([(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(t)], dtype=np.uint64)
-        scr = torch.empty(lib.zkie2_mg_split_sumcheck_scratch_elems(t, world), dtype=torch.uint64, device=dev)
-        rounds, fin = np.zeros((t, 3), dtype=np.uint64), np.zeros(2, dtype=np.uint64)
+    def commit():
+        check(lib.zkie2_mg_split_commit(ctx, d_in.data_ptr(), lg_l, lg_b, w, lde.data_ptr(), layers.data_ptr(),
+                                        top.data_ptr(), scr.data_ptr(), root.ctypes.data_as(P64), sh),
+              "mg split commit")
+    ms = _timed(commit, stream, dev, world)
+    out["split_commit"] = {"ms": round(ms, 3), "value": round(L * w / (ms / 1e3) / 1e6, 3),
+                           "unit": "Melem/s (input elements, all GPUs)",
+                           "root_matches_torch_split": bool((root == want_root).all())}
+    del d_in, lde, layers, top, scr
+    torch.cuda.empty_cache()
+    n_loc = (1 << t) // world
+    f = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 500 + rank)
+    h = synth_into(torch.empty(n_loc, dtype=torch.uint64, device=dev), 600 + rank)
+    ch = np.array([(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(t)], dtype=np.uint64)
+    scr = torch.empty(lib.zkie2_mg_split_sumcheck_scratch_elems(t, world), dtype=torch.uint64, device=dev)
+    rounds, fin = np.zeros((t, 3), dtype=np.uint64), np.zeros(2, dtype=np.uint64)
 
-        def sumcheck():
-            check(lib.zkie2_mg_split_sumcheck(ctx, f.data_ptr(), h.data_ptr(), t, ch.ctypes.data_as(P64),
-                                              rounds.ctypes.data_as(P64), fin.ctypes.data_as(P64), scr.data_ptr(),
-                                              sh), "mg split sumcheck")
-        ms = _timed(sumcheck, stream, dev, world)
-        ok = None
-        if rank == 0:
-            F = torch.empty(1 << t, dtype=torch.uint64, device=dev)
-            G = torch.empty(1 << t, dtype=torch.uint64, device=dev)
-            for r in range(world):
-                synth_into(F[r * n_loc:(r + 1) * n_loc], 500 + r)
-                synth_into(G[r * n_loc:(r + 1) * n_loc], 600 + r)
-            ref = zk.sumcheck_prove(F, G, 0, ch)
-            ok = bool(np.array_equal(rounds, ref.rounds) and (int(fin[0]), int(fin[1])) == (ref.f_eval, ref.h_eval))
-            del F, G
-        dist.barrier()
-        hbm_peak, _ = hbm_peak_gbs()
-        gbs = 16 * n_loc / (ms / 1e3) / 1e9
-        out["split_sumcheck"] = {"config": f"sumcheck::prove, f and h of 2^{t} elements split over {world} GPUs",
-                                 "ms": round(ms, 4), "value": round((1 << t) / (ms / 1e3) / 1e6, 3),
-                                 "unit": "Melem/s", "rounds_match": ok,
-                                 "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
-                                              "unit": "GB/s per GPU", "frac": round(gbs / hbm_peak, 4)}}
-        del f, h, scr
-        torch.cuda.empty_cache()
-    finally:
-        lib.zkie2_mg_destroy(ctx)
+    def sumcheck():
+        check(lib.zkie2_mg_split_sumcheck(ctx, f.data_ptr(), h.data_ptr(), t, ch.ctypes.data_as(P64),
+                                          rounds.ctypes.data_as(P64), fin.ctypes.data_as(P64), scr.data_ptr(),
+                                          sh), "mg split sumcheck")
+    ms = _timed(sumcheck, stream, dev, world)
+    ok = None
+    if rank == 0:
+        F = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+        G = torch.empty(1 << t, dtype=torch.uint64, device=dev)
+        for r in range(world):
+            synth_into(F[r * n_loc:(r + 1) * n_loc], 500 + r)
+            synth_into(G[r * n_loc:(r + 1) * n_loc], 600 + r)
+        ref = zk.sumcheck_prove(F, G, 0, ch)
+        ok = bool(np.array_equal(rounds, ref.rounds) and (int(fin[0]), int(fin[1])) == (ref.f_eval, ref.h_eval))
+        del F, G
+    dist.barrier()
+    hbm_peak, _ = hbm_peak_gbs()
+    gbs = 16 * n_loc / (ms / 1e3) / 1e9
+    out["split_sumcheck"] = {"config": f"sumcheck::prove, f and h of 2^{t} elements split over {world} GPUs",
+                             "ms": round(ms, 4), "value": round((1 << t) / (ms / 1e3) / 1e6, 3),
+                             "unit": "Melem/s", "rounds_match": ok,
+                             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                                          "unit": "GB/s per GPU", "frac": round(gbs / hbm_peak, 4)}}
+    del f, h, scr
+    torch.cuda.empty_cache()
     return out
 
 

@@ -402,6 +402,20 @@ uint64_t zkie2_mg_top_digests(int nranks);
 int zkie2_mg_split_commit(zkie2_mg_ctx *ctx, const uint64_t *d_coeffs, uint32_t lg_l, uint32_t lg_blowup, uint64_t w,
                           uint64_t *d_lde, uint64_t *d_layers, uint64_t *d_top, uint64_t *d_scratch,
                           uint64_t *h_root, zkie_stream_t stream);
+/* The same split commit from host buffers (the end-to-end path of a rank):
+ * h_part holds this rank's rows [g L/G, (g+1) L/G) of the L x w coefficient
+ * matrix (pinned host memory for overlap); the root (8 u64) comes back in
+ * h_root, this rank's LDE rows g, g + G, ... in h_lde ((H/G) x w) and its
+ * subtree's digest layers in h_layers (zkie2_merkle_total_digests(H/G) x 8)
+ * when those are non-null.  Pipelined over about four column blocks on the
+ * context's own streams: the upload of block j + 1, the NVLink all-gather of
+ * block j's rows from every rank, its coset LDE and leaf-sponge absorption,
+ * and the download of its LDE rows overlap.  Synchronous; d_scratch:
+ * zkie2_mg_split_commit_host_scratch_elems (0 = unsupported shape). */
+uint64_t zkie2_mg_split_commit_host_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, int nranks);
+int zkie2_mg_split_commit_host(zkie2_mg_ctx *ctx, const uint64_t *h_part, uint32_t lg_l, uint32_t lg_blowup,
+                               uint64_t w, uint64_t *h_lde, uint64_t *h_layers, uint64_t *h_root,
+                               uint64_t *d_scratch);
 /* sumcheck::prove (common/sumcheck.rs:33-79) of f, h of 2^t elements split
  * over the G ranks by the high variables: rank g passes its 2^t / G
  * contiguous elements [g 2^t/G, (g+1) 2^t/G) of each; h_ch the t challenges

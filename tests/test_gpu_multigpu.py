@@ -187,7 +187,7 @@ def test_split_sumcheck_nccl_two_ranks(orc, tmp_path):
 
 
 # ---- the C-ABI multi-GPU context (zkie2_mg_*) ------------------------------------------------
-MG_COMMIT_CASES = [(14, 1, 32), (12, 2, 9), (12, 0, 8), (10, 1, 256)]
+MG_COMMIT_CASES = [(14, 1, 32), (12, 2, 9), (12, 0, 8), (10, 1, 256), (11, 1, 200)]
 
 
 def _mg_check_rank(zk, ctx, rank, world):
@@ -216,6 +216,22 @@ def _mg_check_rank(zk, ctx, rank, world):
         want_rows = want.lde.reshape(H, w)[rank::world].reshape(-1)
         ok.append(bool(np.array_equal(root, np.asarray(want.root, dtype=np.uint64))))
         ok.append(bool(torch.equal(lde.view(torch.int64), want_rows.view(torch.int64))))
+        # the host-buffer form: this rank's input rows in, LDE rows, subtree layers and root out
+        rows = (1 << lg_l) // world
+        h_part = x.view(torch.int64)[rank * rows * w:(rank + 1) * rows * w].cpu().pin_memory()
+        h_lde = torch.zeros(n_local * w, dtype=torch.int64).pin_memory()
+        h_layers = torch.zeros(layers.numel(), dtype=torch.int64).pin_memory()
+        hscr = torch.empty(lib.zkie2_mg_split_commit_host_scratch_elems(lg_l, lg_b, w, world), dtype=torch.uint64,
+                           device="cuda")
+        for _ in range(2):
+            root2 = np.zeros(8, dtype=np.uint64)
+            rc = lib.zkie2_mg_split_commit_host(ctx, h_part.data_ptr(), lg_l, lg_b, w, h_lde.data_ptr(),
+                                                h_layers.data_ptr(), root2.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                                hscr.data_ptr())
+            assert rc == 0, rc
+            ok.append(bool(np.array_equal(root2, root)))
+        ok.append(bool(torch.equal(h_lde, want_rows.view(torch.int64).cpu())))
+        ok.append(bool(torch.equal(h_layers, layers.view(torch.int64).cpu())))
     for t in (20, world.bit_length() - 1, 9):
         f, h = coeffs(40 + t, 1 << t, 1).reshape(-1), coeffs(50 + t, 1 << t, 1).reshape(-1)
         ch = coeffs(60 + t, max(t, 1), 1).reshape(-1)[:t].copy()

@@ -122,6 +122,8 @@ SIGNATURES = {
     "zkie2_mg_split_commit_scratch_elems": (u64, [u32, u32, u64, i64]),
     "zkie2_mg_top_digests": (u64, [i64]),
     "zkie2_mg_split_commit": (i64, [vp, vp, u32, u32, u64, vp, vp, vp, vp, pu64, vp]),
+    "zkie2_mg_split_commit_host_scratch_elems": (u64, [u32, u32, u64, i64]),
+    "zkie2_mg_split_commit_host": (i64, [vp, vp, u32, u32, u64, vp, vp, pu64, vp]),
     "zkie2_mg_split_sumcheck_scratch_elems": (u64, [u32, i64]),
     "zkie2_mg_split_sumcheck": (i64, [vp, vp, vp, u32, pu64, pu64, pu64, vp, vp]),
 }

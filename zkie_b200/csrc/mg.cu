@@ -147,6 +147,10 @@ struct zkie2_mg_ctx {
     int nranks = 0, rank = 0, device = -1;
     uint32_t lg_g = 0;
     bool owns = false;
+    // streams and events of the host-buffer split commit, made on first use
+    cudaStream_t s_in = nullptr, s_nccl = nullptr, s_comp = nullptr, s_out = nullptr;
+    cudaEvent_t ev_up[2] = {}, ev_gath[2] = {}, ev_lde[2] = {}, ev_down[2] = {}, ev_a = nullptr, ev_b = nullptr;
+    bool pipe_ready = false;
 };
 
 namespace {
@@ -228,6 +232,13 @@ int zkie2_mg_init_comm(void* nccl_comm, zkie2_mg_ctx** out) {
 int zkie2_mg_destroy(zkie2_mg_ctx* ctx) {
     if (!ctx) return 0;
     int rc = 0;
+    if (ctx->pipe_ready) {
+        for (cudaStream_t st : {ctx->s_in, ctx->s_nccl, ctx->s_comp, ctx->s_out}) cudaStreamDestroy(st);
+        for (int i = 0; i < 2; i++)
+            for (cudaEvent_t e : {ctx->ev_up[i], ctx->ev_gath[i], ctx->ev_lde[i], ctx->ev_down[i]}) cudaEventDestroy(e);
+        cudaEventDestroy(ctx->ev_a);
+        cudaEventDestroy(ctx->ev_b);
+    }
     if (ctx->owns && ctx->comm) {
         const ncclResult_t r = nccl()->comm_destroy(ctx->comm);
         if (r != ncclSuccess) rc = kZkMgNcclError + (int)r;
@@ -296,6 +307,185 @@ int zkie2_mg_split_commit(zkie2_mg_ctx* ctx, const uint64_t* d_coeffs, uint32_t 
     }
     ZK_TRY(cudaStreamSynchronize(stream));
     return 0;
+}
+
+// ---- host buffers in and out, pipelined over column blocks ----------------------------------
+// Block j of about four (multiples of 8 columns, the sponge rate): the upload
+// of this rank's row slice of the block (copy-in stream), the all-gather of
+// the block's rows from every rank (NCCL stream), the block's coset LDE and
+// its absorption into every local row's sponge (compute stream; sponge
+// states carried in HBM between blocks), and the download of the block's LDE
+// rows (copy-out stream) overlap across blocks, two buffer slots deep.  Then
+// the digest all-to-all, the subtree, the root all-gather and the top tree,
+// and the layers go back to the host.
+}  // extern "C"
+
+namespace {
+
+uint64_t mg_col_block(uint64_t w) { return w >= 64 ? ((w + 3) / 4 + 7) / 8 * 8 : w; }
+
+struct MgHostLayout {
+    uint64_t part, full, lde, coset, slot, states, dig, recv, layers, top, total;
+};
+
+MgHostLayout mg_host_layout(uint32_t lg_l, uint32_t lg_b, uint64_t w, uint32_t lg_g, int G) {
+    MgHostLayout L{};
+    const uint64_t cw = mg_col_block(w), rows = (1ull << lg_l) >> lg_g;
+    const uint64_t n_local = 1ull << (lg_l + lg_b - lg_g);
+    auto even = [](uint64_t x) { return (x + 1) & ~1ull; };
+    L.part = 0;
+    L.full = even(rows * cw);
+    L.lde = L.full + even((1ull << lg_l) * cw);
+    L.coset = L.lde + even(n_local * cw);
+    L.slot = L.coset + split_commit_coset_elems(lg_l, lg_b, cw, lg_g);
+    L.states = 2 * L.slot;
+    L.dig = L.states + (cw < w ? 16 * n_local : 0);
+    L.recv = L.dig + 8 * n_local;
+    L.layers = L.recv + 8 * n_local;
+    L.top = L.layers + 8 * zkie2_merkle_total_digests(n_local);
+    L.total = L.top + 8 * zkie2_merkle_total_digests((uint64_t)G);
+    return L;
+}
+
+int mg_pipe_ready(zkie2_mg_ctx* c) {
+    if (c->pipe_ready) return 0;
+    for (cudaStream_t* st : {&c->s_in, &c->s_nccl, &c->s_comp, &c->s_out})
+        ZK_TRY(cudaStreamCreateWithFlags(st, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; i++)
+        for (cudaEvent_t* e : {&c->ev_up[i], &c->ev_gath[i], &c->ev_lde[i], &c->ev_down[i]})
+            ZK_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    ZK_TRY(cudaEventCreateWithFlags(&c->ev_a, cudaEventDisableTiming));
+    ZK_TRY(cudaEventCreateWithFlags(&c->ev_b, cudaEventDisableTiming));
+    c->pipe_ready = true;
+    return 0;
+}
+
+// b waits for everything enqueued on a so far
+int mg_after(zkie2_mg_ctx* c, cudaStream_t a, cudaStream_t b) {
+    ZK_TRY(cudaEventRecord(c->ev_a, a));
+    ZK_TRY(cudaStreamWaitEvent(b, c->ev_a, 0));
+    return 0;
+}
+
+int mg_host_body(zkie2_mg_ctx* c, const uint64_t* h_part, uint32_t lg_l, uint32_t lg_b, uint64_t w,
+                 uint64_t* h_lde, uint64_t* h_layers, uint64_t* h_root, uint64_t* S) {
+    const NcclApi* api = nccl();
+    const int G = c->nranks;
+    const uint32_t lg_g = c->lg_g;
+    const MgHostLayout L = mg_host_layout(lg_l, lg_b, w, lg_g, G);
+    const uint64_t cw = mg_col_block(w), nblk = (w + cw - 1) / cw;
+    const uint64_t rows = (1ull << lg_l) >> lg_g, n_local = 1ull << (lg_l + lg_b - lg_g);
+    uint64_t* states = S + L.states;
+    uint64_t* dig = S + L.dig;
+    for (uint64_t j = 0; j < nblk; j++) {
+        const int s = (int)(j & 1);
+        uint64_t* slot = S + s * L.slot;
+        uint64_t *part = slot + L.part, *full = slot + L.full, *lde = slot + L.lde, *scr = slot + L.coset;
+        const uint64_t c0 = j * cw, cn = (w - c0) < cw ? (w - c0) : cw;
+        // upload this rank's rows of the block (part is free once block j-2 was gathered)
+        if (j >= 2) ZK_TRY(cudaStreamWaitEvent(c->s_in, c->ev_gath[s], 0));
+        ZK_TRY(cudaMemcpy2DAsync(part, 8 * cn, h_part + c0, 8 * w, 8 * cn, rows, cudaMemcpyHostToDevice, c->s_in));
+        ZK_TRY(cudaEventRecord(c->ev_up[s], c->s_in));
+        // every rank's rows of the block (full is free once block j-2's LDE read it)
+        ZK_TRY(cudaStreamWaitEvent(c->s_nccl, c->ev_up[s], 0));
+        if (j >= 2) ZK_TRY(cudaStreamWaitEvent(c->s_nccl, c->ev_lde[s], 0));
+        if (G > 1) {
+            ZK_NCCL(api->all_gather(part, full, rows * cn, ncclUint64, c->comm, c->s_nccl));
+        } else {
+            ZK_TRY(cudaMemcpyAsync(full, part, 8 * rows * cn, cudaMemcpyDeviceToDevice, c->s_nccl));
+        }
+        ZK_TRY(cudaEventRecord(c->ev_gath[s], c->s_nccl));
+        // the block's coset LDE (lde is free once block j-2's rows were downloaded), then its absorption
+        ZK_TRY(cudaStreamWaitEvent(c->s_comp, c->ev_gath[s], 0));
+        if (j >= 2 && h_lde) ZK_TRY(cudaStreamWaitEvent(c->s_comp, c->ev_down[s], 0));
+        int rc = lde_coset_launch(full, lde, scr, lg_l, lg_b, cn, lg_g, (uint64_t)c->rank, c->s_comp);
+        if (rc) return rc;
+        ZK_TRY(cudaEventRecord(c->ev_lde[s], c->s_comp));
+        rc = nblk > 1 ? launch_leaf_absorb(lde, cn, 0, cn, n_local, states, dig, j == 0, j + 1 == nblk, c->s_comp)
+                      : launch_leaf_rows(lde, dig, 0, n_local, cn, c->s_comp);
+        if (rc) return rc;
+        if (h_lde) {
+            ZK_TRY(cudaStreamWaitEvent(c->s_out, c->ev_lde[s], 0));
+            ZK_TRY(cudaMemcpy2DAsync(h_lde + c0, 8 * w, lde, 8 * cn, 8 * cn, n_local, cudaMemcpyDeviceToHost,
+                                     c->s_out));
+            ZK_TRY(cudaEventRecord(c->ev_down[s], c->s_out));
+        }
+    }
+    // the digest exchange, the subtree and the top levels
+    uint64_t* layers = S + L.layers;
+    uint64_t* top = S + L.top;
+    const uint64_t per = n_local >> lg_g;
+    int rc = 0;
+    if (G > 1) {
+        uint64_t* recv = S + L.recv;
+        rc = mg_after(c, c->s_comp, c->s_nccl);
+        if (rc) return rc;
+        ZK_NCCL(api->group_start());
+        for (int p = 0; p < G; p++) {
+            ncclResult_t r = api->send(dig + 8 * per * p, 8 * per, ncclUint64, p, c->comm, c->s_nccl);
+            if (r == ncclSuccess) r = api->recv(recv + 8 * per * p, 8 * per, ncclUint64, p, c->comm, c->s_nccl);
+            if (r != ncclSuccess) {
+                api->group_end();
+                return kZkMgNcclError + (int)r;
+            }
+        }
+        ZK_NCCL(api->group_end());
+        rc = mg_after(c, c->s_nccl, c->s_comp);
+        if (!rc) rc = zkie2_digests_interleave(recv, (uint64_t)G, per, layers, c->s_comp);
+    } else {
+        rc = (int)cudaMemcpyAsync(layers, dig, 64 * n_local, cudaMemcpyDeviceToDevice, c->s_comp);
+    }
+    if (!rc) rc = merkle_build_from_leaves(n_local, layers, c->s_comp);
+    if (rc) return rc;
+    const uint64_t sub_root = zkie2_merkle_total_digests(n_local) - 1;
+    if (G > 1) {
+        rc = mg_after(c, c->s_comp, c->s_nccl);
+        if (rc) return rc;
+        ZK_NCCL(api->all_gather(layers + 8 * sub_root, top, 8, ncclUint64, c->comm, c->s_nccl));
+        rc = mg_after(c, c->s_nccl, c->s_comp);
+        if (!rc) rc = merkle_build_from_leaves((uint64_t)G, top, c->s_comp);
+        if (rc) return rc;
+        const uint64_t top_root = zkie2_merkle_total_digests((uint64_t)G) - 1;
+        ZK_TRY(cudaMemcpyAsync(h_root, top + 8 * top_root, 64, cudaMemcpyDeviceToHost, c->s_comp));
+    } else {
+        ZK_TRY(cudaMemcpyAsync(h_root, layers + 8 * sub_root, 64, cudaMemcpyDeviceToHost, c->s_comp));
+    }
+    if (h_layers)
+        ZK_TRY(cudaMemcpyAsync(h_layers, layers, 64 * (sub_root + 1), cudaMemcpyDeviceToHost, c->s_comp));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t zkie2_mg_split_commit_host_scratch_elems(uint32_t lg_l, uint32_t lg_blowup, uint64_t w, int nranks) {
+    const uint32_t lg_g = exact_log2(nranks);
+    if (lg_g == 0xFFFFFFFFu || 2 * lg_g > lg_l + lg_blowup || lg_g > lg_l || w == 0) return 0;
+    return mg_host_layout(lg_l, lg_blowup, w, lg_g, nranks).total;
+}
+
+int zkie2_mg_split_commit_host(zkie2_mg_ctx* ctx, const uint64_t* h_part, uint32_t lg_l, uint32_t lg_blowup,
+                               uint64_t w, uint64_t* h_lde, uint64_t* h_layers, uint64_t* h_root,
+                               uint64_t* d_scratch) {
+    int rc = ctx_check(ctx);
+    if (rc) return rc;
+    const uint32_t lg_h = lg_l + lg_blowup;
+    if (!h_part || !h_root || !d_scratch || w == 0 || 2 * ctx->lg_g > lg_h || ctx->lg_g > lg_l || lg_h > 30)
+        return (int)cudaErrorInvalidValue;
+    rc = p2_ensure_default();
+    if (!rc) rc = mg_pipe_ready(ctx);
+    if (rc) return rc;
+    // the caller's earlier work on the legacy stream (e.g. filling the scratch) comes first
+    if (cudaEventRecord(ctx->ev_b, 0) == cudaSuccess)
+        for (cudaStream_t st : {ctx->s_in, ctx->s_nccl, ctx->s_comp, ctx->s_out}) cudaStreamWaitEvent(st, ctx->ev_b, 0);
+    rc = mg_host_body(ctx, h_part, lg_l, lg_blowup, w, h_lde, h_layers, h_root, d_scratch);
+    // every stream drains before returning, also after an error part-way
+    for (cudaStream_t st : {ctx->s_in, ctx->s_nccl, ctx->s_comp, ctx->s_out}) {
+        const cudaError_t e = cudaStreamSynchronize(st);
+        if (!rc && e != cudaSuccess) rc = (int)e;
+    }
+    return rc;
 }
 
 uint64_t zkie2_mg_split_sumcheck_scratch_elems(uint32_t t, int nranks) {
