@@ -163,13 +163,14 @@ def run_reference(args):
 
 # ---- clocks ------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) of the ONE GPU this rank runs on,
+    """nvidia-smi samples (every 50 ms) of the ONE GPU this rank runs on,
     matched by UUID or PCI bus id; the median SM clock is taken over the
     samples inside the timed region in which that GPU was busy."""
     FIELDS = ("timestamp,uuid,pci.bus_id,utilization.gpu,clocks.sm,clocks.max.sm,power.draw,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    PERIOD_MS = 50  # a split step at N = 8 takes about 10 ms: several samples even in a 0.1 s region
 
     def __init__(self, ident):
         self.uuid, self.bus = ident
@@ -179,7 +180,8 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
         except OSError:
             self.proc = None
             return
@@ -220,7 +222,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "gpu_match": "unmatched",
                     "gpu": {"uuid": self.uuid, "pci_bus_id": self.bus}}
         t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", 1e30)
-        inside = [r for r in mine if t0 - 0.25 <= r[0] <= t1 + 0.25]
+        inside = [r for r in mine if t0 - 0.1 <= r[0] <= t1 + 0.1]
 
         def num(x):
             try:
@@ -228,6 +230,8 @@ class ClockSampler:
             except ValueError:
                 return None
         busy = [r for r in inside if (num(r[3]) or 0) > 0]
+        if not busy:  # a region shorter than the sampling period: the busy samples next to it
+            busy = [r for r in mine if t0 - 1.0 <= r[0] <= t1 + 1.0 and (num(r[3]) or 0) > 0]
         use = busy or inside or mine
         sm = [v for v in (num(r[4]) for r in use) if v is not None]
         mx = [v for v in (num(r[5]) for r in use) if v is not None]
