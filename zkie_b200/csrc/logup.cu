@@ -16,6 +16,8 @@
 // current layer, the next layer comes from one fused kernel, the eq table
 // from the MLE kernel, and the round messages of all layers go to the host
 // in one copy at the end.
+#include <mutex>
+
 #include "../../include/zkie2.h"
 #include "common.cuh"
 #include "gl64.cuh"
@@ -93,37 +95,69 @@ int launch_fraction_layer(const uint64_t* num, const uint64_t* den, uint64_t hal
 }
 
 // Scratch layout of zkie2_fractional_prove for n = 2^lg (u64 offsets, every
-// region a multiple of two elements so 16-byte alignment carries through).
+// region a multiple of two elements so 16-byte alignment carries through):
+// every level of the fraction tree (level l + 1 = the next fractions of level
+// l, 2^(lg-l-1) values each of num and den), every layer's eq table and
+// virtual-sumcheck scratch, then the round messages and final evaluations.
+// All layers stay in HBM, so the layer sumchecks need not wait for each
+// other (their challenges are all given up front).
 struct FracScratch {
-    uint64_t *a_num, *a_den, *b_num, *b_den, *eq, *vscr, *rounds, *finals, *final_nd;
+    uint64_t *num[kMaxLg + 1], *den[kMaxLg + 1];  // levels 1 .. lg (level 0 is the caller's input)
+    uint64_t *eq[kMaxLg], *vscr[kMaxLg];
+    uint64_t *rounds, *finals, *final_nd;
 };
 
 uint64_t even(uint64_t x) { return (x + 1) & ~1ull; }
 
 uint64_t frac_layout(uint32_t lg, FracScratch* fs, uint64_t* base) {
-    const uint64_t n = 1ull << lg;
-    uint64_t vmax = 0;
-    for (uint32_t l = 0; l < lg; l++) {
-        const uint64_t v = virtual_plan_elems(kFracMles, lg - l - 1);
-        vmax = v > vmax ? v : vmax;
-    }
     uint64_t off = 0;
     auto take = [&](uint64_t** p, uint64_t cnt) {
         if (base) *p = base + off;
         off += even(cnt);
     };
     FracScratch s{};
-    take(&s.a_num, n / 2);
-    take(&s.a_den, n / 2);
-    take(&s.b_num, n / 4);
-    take(&s.b_den, n / 4);
-    take(&s.eq, n / 2);
-    take(&s.vscr, vmax);
+    for (uint32_t l = 1; l <= lg; l++) {
+        take(&s.num[l], 1ull << (lg - l));
+        take(&s.den[l], 1ull << (lg - l));
+    }
+    for (uint32_t l = 0; l < lg; l++) {
+        take(&s.eq[l], 1ull << (lg - l - 1));
+        take(&s.vscr[l], virtual_plan_elems(kFracMles, lg - l - 1));
+    }
     take(&s.rounds, 2ull * lg * (lg ? lg - 1 : 0) + 2);
     take(&s.finals, (uint64_t)kFracMles * lg + 1);
     take(&s.final_nd, 2);
     if (fs) *fs = s;
     return off;
+}
+
+// Side streams of the layer sumchecks, per device; a call holds the device's
+// mutex from the first enqueue to its final synchronization, so the shared
+// events are never re-recorded under another call.
+constexpr int kFracStreams = 4;
+struct FracStreams {
+    cudaStream_t s[kFracStreams] = {};
+    cudaEvent_t start = nullptr, level[kMaxLg + 1] = {}, done[kFracStreams] = {};
+    std::mutex call;
+    bool ready = false;
+};
+std::mutex g_frac_mu;
+FracStreams g_frac[kMaxDevices];
+
+int frac_streams(FracStreams** out) {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_frac_mu);
+    FracStreams& f = g_frac[d];
+    if (!f.ready) {
+        for (auto& st : f.s) ZK_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        ZK_TRY(cudaEventCreateWithFlags(&f.start, cudaEventDisableTiming));
+        for (auto& e : f.level) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        for (auto& e : f.done) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        f.ready = true;
+    }
+    *out = &f;
+    return 0;
 }
 
 // Lookup column modes (logup_gkr.rs): the merged witness + table columns
@@ -216,41 +250,65 @@ int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_
     if (!d_num || !d_den || !h_final_nd || !d_scratch || lg_n > kMaxLg ||
         (lg_n && (!h_full_r || !h_cs || !h_finals)) || (lg_n > 1 && !h_rounds))
         return (int)cudaErrorInvalidValue;
+    FracStreams* fst = nullptr;
+    int rc = frac_streams(&fst);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> call_lock(fst->call);
     FracScratch fs;
     frac_layout(lg_n, &fs, d_scratch);
     const uint64_t n = 1ull << lg_n;
     const uint32_t off[kFracTerms + 1] = {0, 2, 5, 8, 10, 13};
     const uint32_t idx[13] = {0, 1, 0, 3, 6, 0, 4, 5, 0, 2, 0, 5, 6};
-    const uint64_t* cn = d_num;
-    const uint64_t* cd = d_den;
+    // Level l + 1 of the tree from level l, all on the caller's stream; an
+    // event marks each level.  Layer l's sumcheck (over levels l and l + 1,
+    // its own eq table and scratch) runs on a side stream as soon as level
+    // l + 1 exists, concurrently with the other layers.
+    const uint64_t* lnum[kMaxLg + 1];
+    const uint64_t* lden[kMaxLg + 1];
+    lnum[0] = d_num;
+    lden[0] = d_den;
+    for (uint32_t l = 1; l <= lg_n; l++) {
+        lnum[l] = fs.num[l];
+        lden[l] = fs.den[l];
+    }
+    ZK_TRY(cudaEventRecord(fst->start, stream));
+    for (auto& ss : fst->s) ZK_TRY(cudaStreamWaitEvent(ss, fst->start, 0));
+    for (uint32_t l = 0; l < lg_n && !rc; l++) {
+        rc = launch_fraction_layer(lnum[l], lden[l], n >> (l + 1), fs.num[l + 1], fs.den[l + 1], stream);
+        if (!rc) rc = (int)cudaEventRecord(fst->level[l + 1], stream);
+    }
     uint64_t roff = 0;
-    for (uint32_t l = 0; l < lg_n; l++) {
+    for (uint32_t l = 0; l < lg_n && !rc; l++) {
+        cudaStream_t ss = fst->s[l % kFracStreams];
         const uint64_t half = n >> (l + 1);
         const uint32_t t = lg_n - l - 1;
-        uint64_t* nn = (l & 1) ? fs.b_num : fs.a_num;
-        uint64_t* nd = (l & 1) ? fs.b_den : fs.a_den;
-        int rc = launch_fraction_layer(cn, cd, half, nn, nd, stream);
-        if (rc) return rc;
-        rc = eq_table_dev(h_full_r, t, fs.eq, stream);
-        if (rc) return rc;
+        rc = eq_table_dev(h_full_r, t, fs.eq[l], ss);  // independent of the tree
+        if (!rc) rc = (int)cudaStreamWaitEvent(ss, fst->level[l + 1], 0);
+        if (rc) break;
         const uint64_t c = gl_canon(h_cs[l]);
         const uint64_t coeffs[kFracTerms] = {1, GL_P - 1, GL_P - 1, c, gl_canon(GL_P - c)};
-        const uint64_t* mles[kFracMles] = {fs.eq, nn, nd, cn, cn + half, cd, cd + half};
+        const uint64_t* mles[kFracMles] = {fs.eq[l], lnum[l + 1], lden[l + 1], lnum[l], lnum[l] + half,
+                                           lden[l], lden[l] + half};
         rc = virtual_enqueue(mles, kFracMles, t, coeffs, off, idx, kFracTerms, h_full_r, fs.rounds + roff,
-                             fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr, stream);
-        if (rc) return rc;
+                             fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr[l], ss);
         roff += (uint64_t)(kFracDeg + 1) * t;
-        cn = nn;
-        cd = nd;
     }
-    k_fraction_final<<<1, 32, 0, stream>>>(cn, cd, fs.final_nd);
-    ZK_LAUNCH_CHECK();
-    if (roff) ZK_TRY(cudaMemcpyAsync(h_rounds, fs.rounds, 8 * roff, cudaMemcpyDeviceToHost, stream));
-    if (lg_n)
-        ZK_TRY(cudaMemcpyAsync(h_finals, fs.finals, 8ull * kFracMles * lg_n, cudaMemcpyDeviceToHost, stream));
-    ZK_TRY(cudaMemcpyAsync(h_final_nd, fs.final_nd, 16, cudaMemcpyDeviceToHost, stream));
-    ZK_TRY(cudaStreamSynchronize(stream));
-    return 0;
+    // join the side streams (also after an error part-way, so that nothing
+    // still runs when the call returns)
+    for (int i = 0; i < kFracStreams; i++) {
+        if (cudaEventRecord(fst->done[i], fst->s[i]) == cudaSuccess) cudaStreamWaitEvent(stream, fst->done[i], 0);
+    }
+    if (!rc) {
+        k_fraction_final<<<1, 32, 0, stream>>>(lnum[lg_n], lden[lg_n], fs.final_nd);
+        rc = (int)cudaGetLastError();
+    }
+    if (!rc && roff) rc = (int)cudaMemcpyAsync(h_rounds, fs.rounds, 8 * roff, cudaMemcpyDeviceToHost, stream);
+    if (!rc && lg_n)
+        rc = (int)cudaMemcpyAsync(h_finals, fs.finals, 8ull * kFracMles * lg_n, cudaMemcpyDeviceToHost, stream);
+    if (!rc) rc = (int)cudaMemcpyAsync(h_final_nd, fs.final_nd, 16, cudaMemcpyDeviceToHost, stream);
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    if (!rc && e != cudaSuccess) rc = (int)e;
+    return rc;
 }
 
 uint64_t zkie2_lookup_len(uint64_t n, uint64_t t, uint32_t mode) { return lookup_len(n, t, mode); }
