@@ -67,6 +67,10 @@ int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, 
                     uint64_t* d_rounds, uint64_t* d_finals, uint32_t* deg_out, uint64_t* d_scratch,
                     cudaStream_t stream);
 int eq_table_dev(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s);
+// prove_fractional_with_challenges enqueued (logup.cu), outputs left in d_scratch
+int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,
+                       const uint64_t* h_cs, uint64_t* d_scratch, cudaStream_t stream, uint64_t** d_rounds,
+                       uint64_t** d_finals, uint64_t** d_nd, uint64_t* n_rounds);
 
 // ---- host-side primitives (host.cpp) -------------------------------------------
 void p2_derive_constants_host(uint64_t seed, uint64_t rc_init[64], uint64_t rc_final[64],

@@ -236,19 +236,16 @@ __global__ void k_lookup_fill(const uint32_t* __restrict__ x, const uint64_t* __
 
 }  // namespace
 
-}  // namespace zk
-
-using namespace zk;
-
-extern "C" {
-
-uint64_t zkie2_fractional_scratch_elems(uint32_t lg_n) { return lg_n > kMaxLg ? 0 : frac_layout(lg_n, nullptr, nullptr); }
-
-int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,
-                           const uint64_t* h_cs, uint64_t* h_rounds, uint64_t* h_finals, uint64_t* h_final_nd,
-                           uint64_t* d_scratch, cudaStream_t stream) {
-    if (!d_num || !d_den || !h_final_nd || !d_scratch || lg_n > kMaxLg ||
-        (lg_n && (!h_full_r || !h_cs || !h_finals)) || (lg_n > 1 && !h_rounds))
+// prove_fractional_with_challenges enqueued on `stream` (the tree's levels)
+// and the side streams (the layer sumchecks), joined back into `stream`
+// before returning; nothing is synchronized or copied to the host.  The
+// round messages (4 per round, layer after layer: *n_rounds values), the
+// finals (7 per layer) and the last level's (num, den) stay in d_scratch at
+// *d_rounds, *d_finals, *d_nd.
+int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,
+                       const uint64_t* h_cs, uint64_t* d_scratch, cudaStream_t stream, uint64_t** d_rounds,
+                       uint64_t** d_finals, uint64_t** d_nd, uint64_t* n_rounds) {
+    if (!d_num || !d_den || !d_scratch || lg_n > kMaxLg || (lg_n && (!h_full_r || !h_cs)))
         return (int)cudaErrorInvalidValue;
     FracStreams* fst = nullptr;
     int rc = frac_streams(&fst);
@@ -293,8 +290,8 @@ int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_
                              fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr[l], ss);
         roff += (uint64_t)(kFracDeg + 1) * t;
     }
-    // join the side streams (also after an error part-way, so that nothing
-    // still runs when the call returns)
+    // join the side streams (also after an error part-way, so that the
+    // caller's synchronization covers everything enqueued)
     for (int i = 0; i < kFracStreams; i++) {
         if (cudaEventRecord(fst->done[i], fst->s[i]) == cudaSuccess) cudaStreamWaitEvent(stream, fst->done[i], 0);
     }
@@ -302,10 +299,34 @@ int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_
         k_fraction_final<<<1, 32, 0, stream>>>(lnum[lg_n], lden[lg_n], fs.final_nd);
         rc = (int)cudaGetLastError();
     }
-    if (!rc && roff) rc = (int)cudaMemcpyAsync(h_rounds, fs.rounds, 8 * roff, cudaMemcpyDeviceToHost, stream);
+    *d_rounds = fs.rounds;
+    *d_finals = fs.finals;
+    *d_nd = fs.final_nd;
+    *n_rounds = roff;
+    return rc;
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+uint64_t zkie2_fractional_scratch_elems(uint32_t lg_n) { return lg_n > kMaxLg ? 0 : frac_layout(lg_n, nullptr, nullptr); }
+
+int zkie2_fractional_prove(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,
+                           const uint64_t* h_cs, uint64_t* h_rounds, uint64_t* h_finals, uint64_t* h_final_nd,
+                           uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_num || !d_den || !h_final_nd || !d_scratch || lg_n > kMaxLg ||
+        (lg_n && (!h_full_r || !h_cs || !h_finals)) || (lg_n > 1 && !h_rounds))
+        return (int)cudaErrorInvalidValue;
+    uint64_t *d_rounds = nullptr, *d_finals = nullptr, *d_nd = nullptr, roff = 0;
+    int rc = fractional_enqueue(d_num, d_den, lg_n, h_full_r, h_cs, d_scratch, stream, &d_rounds, &d_finals, &d_nd,
+                                &roff);
+    if (!rc && roff) rc = (int)cudaMemcpyAsync(h_rounds, d_rounds, 8 * roff, cudaMemcpyDeviceToHost, stream);
     if (!rc && lg_n)
-        rc = (int)cudaMemcpyAsync(h_finals, fs.finals, 8ull * kFracMles * lg_n, cudaMemcpyDeviceToHost, stream);
-    if (!rc) rc = (int)cudaMemcpyAsync(h_final_nd, fs.final_nd, 16, cudaMemcpyDeviceToHost, stream);
+        rc = (int)cudaMemcpyAsync(h_finals, d_finals, 8ull * kFracMles * lg_n, cudaMemcpyDeviceToHost, stream);
+    if (!rc) rc = (int)cudaMemcpyAsync(h_final_nd, d_nd, 16, cudaMemcpyDeviceToHost, stream);
     const cudaError_t e = cudaStreamSynchronize(stream);
     if (!rc && e != cudaSuccess) rc = (int)e;
     return rc;

@@ -12,6 +12,7 @@
 // remainder is at least half.  Values are signed fixed point embedded in the
 // field (fixed_point.rs: from_i64 / to_i64 / to_i32).
 #include <cstring>
+#include <mutex>
 
 #include "../../include/zkie2.h"
 #include "common.cuh"
@@ -84,6 +85,35 @@ unsigned grid_for(uint64_t n) {
 
 bool is_pow2(uint64_t x) { return x && !(x & (x - 1)); }
 
+// Side streams of the projection block: the MatMul GKR and the affine
+// sumcheck run on them while the caller's stream builds the lookup columns
+// and proves the fraction tree (the three proofs share no data beyond the
+// inputs, and every challenge is drawn on the host first).
+struct ProjStreams {
+    cudaStream_t gkr = nullptr, aff = nullptr;
+    cudaEvent_t start = nullptr, gkr_done = nullptr, aff_done = nullptr;
+    std::mutex call;
+    bool ready = false;
+};
+std::mutex g_proj_mu;
+ProjStreams g_proj[kMaxDevices];
+
+int proj_streams(ProjStreams** out) {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_proj_mu);
+    ProjStreams& p = g_proj[d];
+    if (!p.ready) {
+        ZK_TRY(cudaStreamCreateWithFlags(&p.gkr, cudaStreamNonBlocking));
+        ZK_TRY(cudaStreamCreateWithFlags(&p.aff, cudaStreamNonBlocking));
+        for (cudaEvent_t* e : {&p.start, &p.gkr_done, &p.aff_done})
+            ZK_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+        p.ready = true;
+    }
+    *out = &p;
+    return 0;
+}
+
 uint32_t lg_of(uint64_t x) {
     uint32_t r = 0;
     while ((1ull << r) < x) r++;
@@ -92,7 +122,7 @@ uint32_t lg_of(uint64_t x) {
 
 // Scratch layout of zkie2_projection_prove (u64 elements, each region even-sized).
 struct ProjLayout {
-    uint64_t h, eq, ones, table, idx, num, den, fixed, op, virt, look, frac, total;
+    uint64_t h, eq, ones, table, idx, num, den, fixed, op, virt, aff, look, frac, total;
 };
 
 ProjLayout proj_layout(uint64_t m, uint64_t k, uint64_t n, uint32_t shift) {
@@ -114,6 +144,7 @@ ProjLayout proj_layout(uint64_t m, uint64_t k, uint64_t n, uint32_t shift) {
     take(L.fixed, zkie2_matmul_fixed_scratch_elems(m, k, n));
     take(L.op, zkie2_op_matmul_scratch_elems(m, k, n));
     take(L.virt, zkie2_virtual_scratch_elems(6, lg_of(mn)));
+    take(L.aff, 3ull * lg_of(mn) + 6);
     take(L.look, zkie2_lookup_scratch_elems(t));
     take(L.frac, zkie2_fractional_scratch_elems(lg_of(frac_n)));
     L.total = off;
@@ -184,52 +215,89 @@ int zkie2_projection_prove(const uint64_t* d_x, const uint64_t* d_w, const uint6
         (lg && (!h_full_r || !h_cs || !h_frac_finals)) || (lg > 1 && !h_frac_rounds))
         return (int)cudaErrorInvalidValue;
     const ProjLayout L = proj_layout(m, k, n, shift);
+    ProjStreams* ps = nullptr;
+    int rc = proj_streams(&ps);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> call_lock(ps->call);
     uint64_t* S = d_scratch;
     const uint64_t* h = d_h;
-    int rc = 0;
     if (!h) {
         rc = zkie2_matmul_fixed(d_x, d_w, m, k, n, S + L.h, 0, nullptr, S + L.fixed, stream);
         if (rc) return rc;
         h = S + L.h;
     }
-    uint64_t claims[3];
-    uint64_t u_buf[64], v_buf[64], ch_buf[64];
-    rc = zkie2_op_matmul_prove(d_x, d_w, h, m, k, n, src, u_buf, v_buf, ch_buf, h_claimed, h_mm_rounds, h_mm_finals,
-                               claims, S + L.op, stream);
-    if (rc) return rc;
-    if (lm) std::memcpy(h_u, u_buf, 8ull * lm);
-    if (ln) std::memcpy(h_v, v_buf, 8ull * ln);
-    if (lk) std::memcpy(h_ch, ch_buf, 8ull * lk);
-    // the affine constraint at pt = v || u
-    uint64_t pt[64];
-    for (uint32_t i = 0; i < ln; i++) pt[i] = v_buf[i];
-    for (uint32_t i = 0; i < lm; i++) pt[ln + i] = u_buf[i];
-    rc = zkie2_eq_evals(pt, tv, S + L.eq, stream);
-    if (rc) return rc;
-    k_fill_const<<<grid_for(mn), kThreads, 0, stream>>>(S + L.ones, mn, 1);
-    ZK_LAUNCH_CHECK();
+    // every challenge in the reference's order: u, v, ch (the MatMul arm),
+    // alpha, beta, then full_r and cs of the fraction tree
+    uint64_t u[32], v[32], ch[32], pt[64];
+    for (uint32_t i = 0; i < lm; i++) u[i] = zkie2_challenger_field(src);
+    for (uint32_t i = 0; i < ln; i++) v[i] = zkie2_challenger_field(src);
+    for (uint32_t i = 0; i < lk; i++) ch[i] = zkie2_challenger_field(src);
+    h_alpha_beta[0] = zkie2_challenger_field(src);
+    h_alpha_beta[1] = zkie2_challenger_field(src);
+    for (uint32_t i = 0; i < lg; i++) h_full_r[i] = zkie2_challenger_field(src);
+    for (uint32_t i = 0; i < lg; i++) h_cs[i] = zkie2_challenger_field(src);
+    if (lm) std::memcpy(h_u, u, 8ull * lm);
+    if (ln) std::memcpy(h_v, v, 8ull * ln);
+    if (lk) std::memcpy(h_ch, ch, 8ull * lk);
+    for (uint32_t i = 0; i < ln; i++) pt[i] = v[i];
+    for (uint32_t i = 0; i < lm; i++) pt[ln + i] = u[i];
+    ZK_TRY(cudaEventRecord(ps->start, stream));  // h and the caller's inputs are ready
+    ZK_TRY(cudaStreamWaitEvent(ps->gkr, ps->start, 0));
+    ZK_TRY(cudaStreamWaitEvent(ps->aff, ps->start, 0));
+    // the MatMul GKR (matmul::prove(x^T, W, h, u, v, ch)) on its side stream
+    uint64_t* d_mm = nullptr;
+    rc = op_matmul_enqueue(d_x, d_w, h, m, k, n, u, v, ch, S + L.op, &d_mm, ps->gkr);
+    // the affine constraint at pt = v || u on the other
     const uint64_t neg = kP - 1, two = 1ull << shift, half = 1ull << (shift - 1);
     const uint64_t coeffs[5] = {1, neg, two, gl_mul_host(neg, two), gl_mul_host(neg, half)};
     const uint32_t idx_off[6] = {0, 2, 4, 6, 8, 10};
     const uint32_t idx[10] = {0, 1, 0, 2, 0, 3, 0, 4, 0, 5};
     const uint64_t* mles[6] = {S + L.eq, d_rem_off, h, d_out, d_bias, S + L.ones};
-    rc = zkie2_virtual_prove(mles, 6, tv, coeffs, idx_off, idx, 5, pt, h_aff_rounds, h_aff_finals, S + L.virt, stream);
-    if (rc) return rc;
-    // the range check: alpha, beta, then the fraction tree's own draws
-    h_alpha_beta[0] = zkie2_challenger_field(src);
-    h_alpha_beta[1] = zkie2_challenger_field(src);
-    k_fill_iota<<<grid_for(t), kThreads, 0, stream>>>(S + L.table, t);
-    ZK_LAUNCH_CHECK();
+    uint64_t* d_aff_rounds = S + L.aff;
+    uint64_t* d_aff_finals = d_aff_rounds + 3ull * tv;
+    if (!rc) rc = eq_table_dev(pt, tv, S + L.eq, ps->aff);
+    if (!rc) {
+        k_fill_const<<<grid_for(mn), kThreads, 0, ps->aff>>>(S + L.ones, mn, 1);
+        rc = (int)cudaGetLastError();
+    }
+    if (!rc)
+        rc = virtual_enqueue(mles, 6, tv, coeffs, idx_off, idx, 5, pt, d_aff_rounds, d_aff_finals, nullptr,
+                             S + L.virt, ps->aff);
+    // the range check on the caller's stream: the lookup columns (this step
+    // reads one flag back, which synchronizes only the caller's stream), then
+    // the fraction tree with its own side streams
+    uint64_t *d_fr = nullptr, *d_ff = nullptr, *d_nd = nullptr, roff = 0;
     uint32_t* d_idx = reinterpret_cast<uint32_t*>(S + L.idx);
-    rc = zkie2_lookup_index_i32(d_rem_off, mn, d_idx, stream);
+    if (!rc) {
+        k_fill_iota<<<grid_for(t), kThreads, 0, stream>>>(S + L.table, t);
+        rc = (int)cudaGetLastError();
+    }
+    if (!rc) rc = zkie2_lookup_index_i32(d_rem_off, mn, d_idx, stream);
     if (!rc)
         rc = zkie2_lookup_num_den(d_idx, d_rem_off, mn, S + L.table, nullptr, t, 0, h_alpha_beta[0], h_alpha_beta[1],
                                   S + L.num, S + L.den, S + L.look, stream);
-    if (rc) return rc;
-    for (uint32_t i = 0; i < lg; i++) h_full_r[i] = zkie2_challenger_field(src);
-    for (uint32_t i = 0; i < lg; i++) h_cs[i] = zkie2_challenger_field(src);
-    return zkie2_fractional_prove(S + L.num, S + L.den, lg, h_full_r, h_cs, h_frac_rounds, h_frac_finals, h_frac_nd,
-                                  S + L.frac, stream);
+    if (!rc)
+        rc = fractional_enqueue(S + L.num, S + L.den, lg, h_full_r, h_cs, S + L.frac, stream, &d_fr, &d_ff, &d_nd,
+                                &roff);
+    // join the side streams, then one round of copies to the host
+    if (cudaEventRecord(ps->gkr_done, ps->gkr) == cudaSuccess) cudaStreamWaitEvent(stream, ps->gkr_done, 0);
+    if (cudaEventRecord(ps->aff_done, ps->aff) == cudaSuccess) cudaStreamWaitEvent(stream, ps->aff_done, 0);
+    auto d2h = [&](void* dst, const void* src, uint64_t bytes) {
+        if (!rc && bytes) rc = (int)cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, stream);
+    };
+    if (!rc) {
+        d2h(h_claimed, d_mm, 8);
+        d2h(h_mm_rounds, d_mm + 1, 24ull * lk);
+        d2h(h_mm_finals, d_mm + 1 + 3ull * lk, 16);
+        d2h(h_aff_rounds, d_aff_rounds, 24ull * tv);
+        d2h(h_aff_finals, d_aff_finals, 48);
+        d2h(h_frac_rounds, d_fr, 8 * roff);
+        d2h(h_frac_finals, d_ff, 56ull * lg);
+        d2h(h_frac_nd, d_nd, 16);
+    }
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    if (!rc && e != cudaSuccess) rc = (int)e;
+    return rc;
 }
 
 }  // extern "C"
