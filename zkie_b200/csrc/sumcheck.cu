@@ -199,10 +199,10 @@ __global__ void k_sum_rows(const uint64_t* __restrict__ part, uint64_t nb, uint6
 // c1 = s - y1 - 3y0 and c2 = 2(y0 + y1) - s -- the same field elements with
 // two field additions per pair fewer and no halving.
 //
-// One warp owns a chunk of 2^9 consecutive elements of f and of h and runs all
-// nine rounds of it without shared memory: each lane holds 16 consecutive
-// elements and does rounds 0-3 in registers (the sums accumulate exactly in
-// Acc160 and reduce once per round), then rounds 4-8 pair lanes by shuffles.
+// One warp owns a chunk of 2^9 consecutive elements of f and of h: each lane
+// holds 16 consecutive elements and does rounds 0-3 in registers (the sums accumulate exactly in
+// Acc160 and reduce once per round); rounds 4-8 run on the 32 folded values
+// per chunk staged in shared memory, one pair per thread across the block.
 // The 27 per-round sums are reduced across the warp by a butterfly
 // reduce-scatter and across the block's 8 warps through shared memory, so each
 // block writes one row of 27 partial sums.
@@ -300,26 +300,36 @@ __global__ void __launch_bounds__(kThreads)
             fin_h = hv[0];
         }
     }
-    // rounds 4-8: lane l pairs with lane l + 2^k, active when l % 2^(k+1) == 0
-    uint64_t x = fv[0], z = hv[0];
+    // rounds 4-8 on the 32 folded values of each of the block's 8 chunks,
+    // staged in shared memory: round 4 + k has 16 >> k pairs per chunk and
+    // takes one pair per thread (the first 8 (16 >> k) threads), so no lane
+    // computes a pair that is not there (ping-pong buffers, one barrier per
+    // round)
+    __shared__ uint64_t sx[2][kChunkWarps][32], sz[2][kChunkWarps][32];
+    sx[0][warp][lane] = fv[0];
+    sz[0][warp][lane] = hv[0];
+    __syncthreads();
 #pragma unroll
     for (int k = 0; k < 5; k++) {
-        const int rd = 4 + k;
-        const uint32_t o = 1u << k;
-        const uint64_t x1 = __shfl_down_sync(0xffffffffu, x, o);
-        const uint64_t z1 = __shfl_down_sync(0xffffffffu, z, o);
-        if ((lane & (2 * o - 1)) == 0) {
-            vals[3 * rd] = gl_mul(x, z);
+        const int rd = 4 + k, lp = 4 - k;  // 2^lp pairs per chunk
+        const uint32_t tid = threadIdx.x;
+        if (tid < ((uint32_t)kChunkWarps << lp)) {
+            const uint32_t w = tid >> lp, pr = tid & ((1u << lp) - 1);
+            const uint64_t x0 = sx[k & 1][w][2 * pr], x1 = sx[k & 1][w][2 * pr + 1];
+            const uint64_t z0 = sz[k & 1][w][2 * pr], z1 = sz[k & 1][w][2 * pr + 1];
+            vals[3 * rd] = gl_mul(x0, z0);
             vals[3 * rd + 1] = gl_mul(x1, z1);
-            vals[3 * rd + 2] = gl_mul(gl_add(x, x1), gl_add(z, z1));
+            vals[3 * rd + 2] = gl_mul(gl_add(x0, x1), gl_add(z0, z1));
+            const uint64_t r = ch.r[rd];
+            sx[(k + 1) & 1][w][pr] = gl_add(x0, gl_mul(r, gl_sub(x1, x0)));
+            sz[(k + 1) & 1][w][pr] = gl_add(z0, gl_mul(r, gl_sub(z1, z0)));
         }
-        const uint64_t r = ch.r[rd];
-        x = gl_add(x, gl_mul(r, gl_sub(x1, x)));
-        z = gl_add(z, gl_mul(r, gl_sub(z1, z)));
-        if ((uint32_t)rd + 1 == q) {
-            fin_f = x;
-            fin_h = z;
-        }
+        __syncthreads();
+    }
+    // after round 4 + k the chunk's folded values sit in buffer (k + 1) & 1
+    if (q > 4) {
+        fin_f = sx[(q - 4) & 1][warp][0];
+        fin_h = sz[(q - 4) & 1][warp][0];
     }
     red[warp][lane] = warp_transpose_sum(vals);
     __syncthreads();
