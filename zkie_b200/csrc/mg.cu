@@ -309,6 +309,8 @@ int zkie2_mg_split_commit(zkie2_mg_ctx* ctx, const uint64_t* d_coeffs, uint32_t 
     return 0;
 }
 
+}  // extern "C"
+
 // ---- host buffers in and out, pipelined over column blocks ----------------------------------
 // Block j of about four (multiples of 8 columns, the sponge rate): the upload
 // of this rank's row slice of the block (copy-in stream), the all-gather of
@@ -318,8 +320,6 @@ int zkie2_mg_split_commit(zkie2_mg_ctx* ctx, const uint64_t* d_coeffs, uint32_t 
 // rows (copy-out stream) overlap across blocks, two buffer slots deep.  Then
 // the digest all-to-all, the subtree, the root all-gather and the top tree,
 // and the layers go back to the host.
-}  // extern "C"
-
 namespace {
 
 uint64_t mg_col_block(uint64_t w) { return w >= 64 ? ((w + 3) / 4 + 7) / 8 * 8 : w; }
