@@ -158,6 +158,10 @@ void zkie2_transcript_absorb_u64(zkie2_transcript *t, uint64_t x);
 uint64_t zkie2_transcript_field(zkie2_transcript *t);
 uint64_t zkie2_transcript_next_u64(zkie2_transcript *t);
 void zkie2_challenger_xorshift(zkie2_challenger *c, uint64_t seed);
+/* n XorShift64 draws from *state (advanced), each stored as
+ * from_i64((draw % mod) + offset): the weight draws of the reference's random
+ * model builders.  mod > 0. */
+void zkie2_xorshift_fill(uint64_t *state, uint64_t n, uint64_t mod, int64_t offset, uint64_t *out);
 uint64_t zkie2_challenger_field(zkie2_challenger *c);
 /* Child transcript of shard `shard_index` in prove_shard_dag
  * (zkie-ops/src/compose.rs:2276-2311) for a statement of MatMul ops given as
@@ -176,6 +180,9 @@ int zkie2_mle_partial_eval(const uint64_t *d_values, uint32_t t, const uint64_t 
 /* eval (common/mle.rs:8-23); synchronous, result to *h_out. */
 int zkie2_mle_eval(const uint64_t *d_values, uint32_t t, const uint64_t *h_point, uint64_t *h_out,
                    uint64_t *d_scratch, zkie_stream_t stream);
+/* The same with the value left in *d_out on the device (no synchronization). */
+int zkie2_mle_eval_async(const uint64_t *d_values, uint32_t t, const uint64_t *h_point, uint64_t *d_out,
+                         uint64_t *d_scratch, zkie_stream_t stream);
 /* sumcheck::prove (common/sumcheck.rs:33-79) over f, h of length 2^t with the
  * t challenges h_ch: h_rounds gets (c0, c1, c2) per round, h_finals (f, h)
  * after the last fold.  Synchronous. */
@@ -218,6 +225,12 @@ int zkie2_op_matmul_prove(const uint64_t *d_a, const uint64_t *d_b, const uint64
                           uint64_t *out_v, uint64_t *out_ch, uint64_t *out_claimed,
                           uint64_t *out_rounds, uint64_t *out_finals, uint64_t *out_claims,
                           uint64_t *d_scratch, zkie_stream_t stream);
+/* The same with u, v, ch from the caller and claimed | rounds (3 log2 k) |
+ * finals (2) left in d_proof on the device; no synchronization (the claims
+ * are left to zkie2_mle_eval_async). */
+int zkie2_op_matmul_prove_async(const uint64_t *d_a, const uint64_t *d_b, const uint64_t *d_c, uint64_t m,
+                                uint64_t k, uint64_t n, const uint64_t *h_u, const uint64_t *h_v,
+                                const uint64_t *h_ch, uint64_t *d_proof, uint64_t *d_scratch, zkie_stream_t stream);
 /* C = A @ B over the field (the forward witness of Op::MatMul,
  * zkie-ops/src/compose.rs:1327-1331, zkie-ops/src/par.rs:41-89). */
 int zkie2_matmul_field(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
@@ -269,6 +282,19 @@ int zkie2_projection_prove(const uint64_t *d_x, const uint64_t *d_w, const uint6
                            uint64_t *h_aff_rounds, uint64_t *h_aff_finals, uint64_t *h_alpha_beta,
                            uint64_t *h_full_r, uint64_t *h_cs, uint64_t *h_frac_rounds, uint64_t *h_frac_finals,
                            uint64_t *h_frac_nd, uint64_t *d_scratch, zkie_stream_t stream);
+/* The same with every challenge from the caller (u, v, ch, alpha, beta,
+ * full_r, cs) and the proof fields left on the device in d_proof
+ * (zkie2_projection_proof_elems u64: claimed | mm_rounds | mm_finals |
+ * aff_rounds | aff_finals | frac_rounds | frac_finals | frac_nd); a lookup
+ * index outside the table sets bit 1 of the device word *d_err.  No
+ * synchronization; d_scratch as above. */
+uint64_t zkie2_projection_proof_elems(uint64_t m, uint64_t k, uint64_t n, uint32_t shift);
+int zkie2_projection_prove_async(const uint64_t *d_x, const uint64_t *d_w, const uint64_t *d_bias,
+                                 const uint64_t *d_out, const uint64_t *d_rem_off, const uint64_t *d_h, uint64_t m,
+                                 uint64_t k, uint64_t n, uint32_t shift, const uint64_t *h_u, const uint64_t *h_v,
+                                 const uint64_t *h_ch, uint64_t alpha, uint64_t beta, const uint64_t *h_full_r,
+                                 const uint64_t *h_cs, uint64_t *d_proof, uint32_t *d_err, uint64_t *d_scratch,
+                                 zkie_stream_t stream);
 /* One MatMul shard in one call: C = A W into d_c
  * (m x n), WHIR base commits of W (k*n evaluations), A (m*k) and C (m*n)
  * (pcs/whir.rs:438-469, each >= 32 evaluations), and the Op::MatMul proof
@@ -303,6 +329,11 @@ uint64_t zkie2_virtual_scratch_elems(uint32_t n_mles, uint32_t t);
 int zkie2_virtual_prove(const uint64_t *const *d_mles, uint32_t n_mles, uint32_t t, const uint64_t *coeffs,
                         const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms, const uint64_t *h_ch,
                         uint64_t *h_rounds, uint64_t *h_finals, uint64_t *d_scratch, zkie_stream_t stream);
+/* The same with the rounds and finals left in device memory (d_rounds: t x
+ * (d + 1), d_finals: n_mles); no synchronization. */
+int zkie2_virtual_prove_async(const uint64_t *const *d_mles, uint32_t n_mles, uint32_t t, const uint64_t *coeffs,
+                              const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms, const uint64_t *h_ch,
+                              uint64_t *d_rounds, uint64_t *d_finals, uint64_t *d_scratch, zkie_stream_t stream);
 
 /* PoW grinding of the WHIR prover (challenger.grind, p3-whir src/pcs/prover/mod.rs:240-245,
  * 355-358) on the transcript's DuplexChallenger<Goldilocks, Poseidon2-16, 16, 8>
@@ -348,6 +379,12 @@ uint64_t zkie2_fractional_scratch_elems(uint32_t lg_n);
 int zkie2_fractional_prove(const uint64_t *d_num, const uint64_t *d_den, uint32_t lg_n, const uint64_t *h_full_r,
                            const uint64_t *h_cs, uint64_t *h_rounds, uint64_t *h_finals, uint64_t *h_final_nd,
                            uint64_t *d_scratch, zkie_stream_t stream);
+/* The same with rounds | finals | final (num, den) left in d_proof
+ * (zkie2_fractional_proof_elems u64); no synchronization. */
+uint64_t zkie2_fractional_proof_elems(uint32_t lg_n);
+int zkie2_fractional_prove_async(const uint64_t *d_num, const uint64_t *d_den, uint32_t lg_n,
+                                 const uint64_t *h_full_r, const uint64_t *h_cs, uint64_t *d_proof,
+                                 uint64_t *d_scratch, zkie_stream_t stream);
 /* Lookup columns num, den of zkie2_lookup_len(n, t, mode) values (device):
  * mode 0 build_lookup_num_den (logup_gkr.rs:210-240: witness fractions, then
  * the table with -multiplicity, multiplicities counted on the device;
@@ -361,6 +398,83 @@ uint64_t zkie2_lookup_scratch_elems(uint64_t t);
 int zkie2_lookup_num_den(const uint32_t *d_x, const uint64_t *d_y, uint64_t n, const uint64_t *d_table,
                          const uint64_t *d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
                          uint64_t *d_num, uint64_t *d_den, uint64_t *d_scratch, zkie_stream_t stream);
+/* The same without synchronization: in mode 0 an index at or past t sets
+ * bit 1 of the device word *d_err. */
+int zkie2_lookup_num_den_async(const uint32_t *d_x, const uint64_t *d_y, uint64_t n, const uint64_t *d_table,
+                               const uint64_t *d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                               uint64_t *d_num, uint64_t *d_den, uint64_t *d_scratch, uint32_t *d_err,
+                               zkie_stream_t stream);
+/* merge_multiplicity (logup_gkr.rs:251-260) on the device: d_m[j] (u64, t
+ * values) += the count of j in d_x[0 .. n) (zeroed first unless
+ * accumulate); an index at or past t sets bit 1 of *d_err. */
+int zkie2_lookup_multiplicity(const uint32_t *d_x, uint64_t n, uint64_t t, uint64_t *d_m, int accumulate,
+                              uint32_t *d_err, zkie_stream_t stream);
+
+/* ---- the op layer (crates/zkie-ops/src/compose.rs) ----------------------------------- */
+/* The forward witness of the op arms a GPT-2 layer uses (forward_ops,
+ * compose.rs:1174-1583) and the columns their proofs read.  Tensors are flat
+ * row-major device arrays of field elements (u64) or of u32 lookup indices.
+ * Fixed-point values are the field embedding of fixed_point.rs (to_i64 /
+ * from_i64), with the reference's wrapping i64 arithmetic.  Where the
+ * reference panics on data (an index outside a table, a zero softmax row
+ * sum), the kernels set a bit in the device word *d_err (1: index, 2:
+ * division) and carry on.  None of these synchronizes. */
+/* Op::Add: out = a + b over the field */
+int zkie2_op_add(const uint64_t *d_a, const uint64_t *d_b, uint64_t n, uint64_t *d_out, zkie_stream_t stream);
+/* Op::Scale: out = from_i64(round_div(to_i64(x) * factor, 2^shift)), shift <= 62 */
+int zkie2_op_scale(const uint64_t *d_x, uint64_t n, int64_t factor, uint32_t shift, uint64_t *d_out,
+                   zkie_stream_t stream);
+/* Op::Transpose: x (m x k) -> out (k x m) */
+int zkie2_op_transpose(const uint64_t *d_x, uint64_t m, uint64_t k, uint64_t *d_out, zkie_stream_t stream);
+/* Op::SoftmaxIndex: idx = (max(to_i64(x), 0) as u64) % table_len */
+int zkie2_op_softmax_index(const uint64_t *d_x, uint64_t n, uint64_t table_len, uint32_t *d_idx,
+                           zkie_stream_t stream);
+/* Op::GeluIndex: idx = clamp(to_i64(x) + offset, 0, table_len - 1) */
+int zkie2_op_gelu_index(const uint64_t *d_x, uint64_t n, int64_t offset, uint64_t table_len, uint32_t *d_idx,
+                        zkie_stream_t stream);
+/* Op::StableSoftmaxIndex: masked = x + mask, idx = clamp(to_i64(masked) -
+ * max over the row of to_i64(masked) + offset, 0, table_len - 1); m rows of n */
+int zkie2_op_stable_softmax_index(const uint64_t *d_x, const uint64_t *d_mask, uint64_t m, uint64_t n,
+                                  int64_t offset, uint64_t table_len, uint32_t *d_idx, zkie_stream_t stream);
+/* Op::Lookup: out = table[idx] */
+int zkie2_op_lookup(const uint32_t *d_idx, uint64_t n, const uint64_t *d_table, uint64_t t, uint64_t *d_out,
+                    uint32_t *d_err, zkie_stream_t stream);
+/* Op::Softmax: e = table[idx], sum = each row's field sum (into d_sum, m
+ * values, when non-null), out = from_i64(round_div(to_i64(e) 2^16, to_i64(sum))) */
+int zkie2_op_softmax(const uint32_t *d_idx, const uint64_t *d_table, uint64_t t, uint64_t m, uint64_t n,
+                     uint64_t *d_e, uint64_t *d_out, uint64_t *d_sum, uint32_t *d_err, zkie_stream_t stream);
+/* prove_softmax_rounded's columns (softmax_scaled.rs:69-80): sum_b = the row
+ * sum broadcast over its row, rem = from_i64(to_i64(e) 2^16 - to_i64(out) to_i64(sum_b)) */
+int zkie2_op_softmax_rem(const uint64_t *d_e, const uint64_t *d_out, const uint64_t *d_sum, uint64_t m, uint64_t n,
+                         uint64_t *d_sum_b, uint64_t *d_rem, zkie_stream_t stream);
+/* layer_norm_forward (layer_norm_centered.rs:42-120) of m rows of d values,
+ * the first n_real real, with rsqrt_index (compose.rs:884-896) into the
+ * table of t values.  d_outs (host array of 11 device pointers): mean (m),
+ * centered (m d), var (m), rstd (m), raw = centered rstd w (m d), out (m d),
+ * rem_out (m d), sum_mean (m), rem_mean (m), sum_var (m), rem_var (m);
+ * d_s_index (m u32). */
+int zkie2_op_layer_norm_centered(const uint64_t *d_x, const uint64_t *d_w, const uint64_t *d_b,
+                                 const uint64_t *d_table, uint64_t t, uint64_t m, uint64_t d, uint64_t n_real,
+                                 uint64_t *const *d_outs, uint32_t *d_s_index, uint32_t *d_err, zkie_stream_t stream);
+/* The Layernorm arm's forward (compose.rs:1467-1496): mean_sq (m), idx (m
+ * u32), rsqrt (m), scale (m d), out (m d) */
+int zkie2_op_layernorm(const uint64_t *d_x, const uint64_t *d_w, const uint64_t *d_b, const uint64_t *d_table,
+                       uint64_t t, uint64_t m, uint64_t d, uint64_t *d_mean_sq, uint32_t *d_idx, uint64_t *d_rsqrt,
+                       uint64_t *d_scale, uint64_t *d_out, zkie_stream_t stream);
+/* out[r n + j] = v[r] (m rows of n) */
+int zkie2_op_row_broadcast(const uint64_t *d_v, uint64_t m, uint64_t n, uint64_t *d_out, zkie_stream_t stream);
+/* out[r] = the field sum of x[r d .. r d + ncols) */
+int zkie2_op_row_sums(const uint64_t *d_x, uint64_t m, uint64_t d, uint64_t ncols, uint64_t *d_out,
+                      zkie_stream_t stream);
+/* out[i] = value */
+int zkie2_op_fill(uint64_t *d_out, uint64_t n, uint64_t value, zkie_stream_t stream);
+/* prove_same_poly (common/same_poly.rs:13-45) as one degree-2 virtual
+ * polynomial: every term of the reference's is c_i f eq(r_i, .), so its
+ * round messages are those of f E with E = sum_i c_i eq(r_i, .).  This
+ * builds E (2^t values) from c points r_i (h_points, c x t) and coefficients. */
+uint64_t zkie2_eq_combine_scratch_elems(uint32_t c, uint32_t t);
+int zkie2_eq_combine(const uint64_t *h_points, const uint64_t *h_coeffs, uint32_t c, uint32_t t, uint64_t *d_out,
+                     uint64_t *d_scratch, zkie_stream_t stream);
 
 /* ---- multi-GPU context (NCCL) ------------------------------------------------------- */
 /* One split commit and one split sumcheck over an NCCL communicator, one

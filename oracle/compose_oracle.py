@@ -1,0 +1,579 @@
+"""CPU restatement of zkie-ops' shard prover for the op arms of a GPT-2 layer.
+
+Test infrastructure, never part of the product: only tests/, smoke() and
+bench.py's CPU legs import it.  It restates, over the oracle's field,
+sumcheck and fraction-tree primitives (oracle.py over zkie_oracle.c) and
+numpy's wrapping int64 arithmetic (the reference's i64 arithmetic in a
+release build):
+
+- fixed_point.rs to_i64 / from_i64 (:53-70) and compose.rs round_div (:103-111)
+- forward_ops (compose.rs:1174-1583) for the arms a GPT-2 layer uses:
+  Transpose, Scale, MatMul, Projection, Add, Lookup, Softmax, SoftmaxIndex,
+  GeluIndex, StableSoftmaxIndex, Layernorm, LayerNormCentered
+- rsqrt_index (compose.rs:884-896), layer_norm_forward and
+  prove_layer_norm_centered (layer_norm_centered.rs:42-245)
+- prove_layernorm_chain (layernorm_chain.rs:24-93)
+- prove_softmax_rounded (softmax_scaled.rs:42-108)
+- prove_same_poly (common/same_poly.rs:13-45)
+- prove_lookup_witness_batch_columns, merge_multiplicity, prove_lookup_table,
+  prove_fractional, fractional_leaf (common/logup_gkr.rs:71-81, 193-201,
+  251-260, 340-383)
+- prove_shard_precomputed (compose.rs:1602-2091), prove_shard (:1589-1597),
+  absorb_statement and prove_shard_dag (:2276-2346)
+
+Ops are read by duck typing (``op.kind`` and the field names of the
+reference's Op enum); the store is a HostStore of numpy arrays.  Proofs come
+back as nested tuples of ints and numpy arrays, the layout the product's
+``canonical()`` methods produce, so a test compares the two directly.
+"""
+import numpy as np
+
+from . import oracle as o
+
+P = 0xFFFFFFFF00000001
+NEG = P - 1
+I64_MAX = 0x7FFFFFFFFFFFFFFF
+
+
+class HostStore:
+    """compose.rs Store: field tensors ``v`` and index tensors ``idx``."""
+
+    def __init__(self):
+        self.v = []
+        self.idx = []
+
+    def push(self, t):
+        self.v.append(None if t is None else o.u64(t).reshape(-1))
+        return len(self.v) - 1
+
+    def push_idx(self, t):
+        self.idx.append(None if t is None else np.asarray(t, dtype=np.uint32).reshape(-1))
+        return len(self.idx) - 1
+
+    def get(self, t):
+        return self.v[t]
+
+
+# ---- fixed point (fixed_point.rs:53-70, compose.rs:103-111) -----------------------------
+def to_i64(v):
+    v = np.asarray(v, dtype=np.uint64) % np.uint64(P)
+    neg = v > np.uint64(I64_MAX)
+    out = v.astype(np.int64)
+    out[neg] = -((np.uint64(P) - v[neg]).astype(np.int64))
+    return out
+
+
+def from_i64(x):
+    x = np.asarray(x, dtype=np.int64)
+    u = x.astype(np.uint64)
+    neg = x < 0
+    out = u.copy()
+    # P - |x| with |x| = 0 - u (mod 2^64), also for i64::MIN
+    out[neg] = np.uint64(P) - (np.uint64(0) - u[neg])
+    return out
+
+
+def round_div(a, b):
+    """q = a.div_euclid(b), r = a.rem_euclid(b), q + 1 when 2 r >= b (wrapping)."""
+    a = np.asarray(a, dtype=np.int64)
+    b = np.broadcast_to(np.asarray(b, dtype=np.int64), a.shape)
+    if (b == 0).any():
+        raise ZeroDivisionError("round_div by zero")
+    with np.errstate(over="ignore"):
+        ab = np.abs(b)
+        q = a // ab
+        r = a - q * ab
+        q = np.where(b < 0, -q, q)
+        return np.where(r * 2 >= b, q + 1, q)
+
+
+def rsqrt_index(var):
+    """compose.rs:884-896 on an int64 array."""
+    fine, coarse = 1 << 20, 1 << 22
+    coarse_end = fine + coarse * (1 << 8)
+    raw = round_div(var, 1 << 18)
+    with np.errstate(over="ignore"):
+        out = np.where(raw < fine, np.maximum(raw, 0),
+                       np.where(raw < coarse_end, fine + ((raw - fine) >> 8),
+                                fine + coarse + ((raw - coarse_end) >> 16)))
+    return (out.astype(np.int64).astype(np.uint64) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+
+
+def _lg(n):
+    n = int(n)
+    if n <= 0 or n & (n - 1):
+        raise ValueError(f"{n} is not a power of two")
+    return n.bit_length() - 1
+
+
+def _draw(rng, n):
+    return np.array([rng.field() for _ in range(n)], dtype=np.uint64)
+
+
+def _rows(v, m, d):
+    """v[r] broadcast over the d columns of row r."""
+    return np.repeat(o.u64(v).reshape(-1), d)
+
+
+def _gather(table, idx):
+    idx = np.asarray(idx, dtype=np.int64)
+    if idx.size and idx.max() >= table.size:
+        raise IndexError("lookup index outside the table")
+    return table[idx]
+
+
+# ---- forward (compose.rs:1174-1583) --------------------------------------------------------
+def layer_norm_forward(x, w, b, table, m, d, n_real):
+    """layer_norm_centered.rs:42-120 -> dict of its eleven outputs."""
+    x = o.u64(x).reshape(-1)
+    xi = to_i64(x).reshape(m, d)
+    with np.errstate(over="ignore"):
+        s = xi[:, :n_real].sum(axis=1)
+    mean = from_i64(round_div(s, n_real))
+    centered = o.vec_sub(x, _rows(mean, m, d))
+    c = to_i64(centered).reshape(m, d)[:, :n_real]
+    with np.errstate(over="ignore"):
+        sq = (c * c).sum(axis=1)
+    var = from_i64(round_div(sq, n_real))
+    s_index = rsqrt_index(to_i64(var))
+    if s_index.size and int(s_index.max()) >= table.size:
+        raise IndexError("rsqrt table too short for the forward pass")
+    rstd = table[s_index.astype(np.int64)]
+    raw = o.vec_mul(o.vec_mul(centered, _rows(rstd, m, d)), w)
+    bi = to_i64(b)
+    out = from_i64(round_div(to_i64(raw), 1 << 32) + bi)
+    with np.errstate(over="ignore"):
+        rem_out = from_i64(to_i64(raw) - (to_i64(out) - bi) * (1 << 32) + (1 << 31))
+        sum_mean = o.row_sums(x, m, d, n_real)
+        rem_mean = from_i64(to_i64(sum_mean) - to_i64(mean) * n_real + n_real // 2)
+        sum_var = o.row_sums(o.vec_mul(centered, centered), m, d, n_real)
+        rem_var = from_i64(to_i64(sum_var) - to_i64(var) * n_real + n_real // 2)
+    return dict(mean=mean, centered=centered, var=var, s_index=s_index, rstd=rstd, raw=raw, out=out,
+                rem_out=rem_out, sum_mean=sum_mean, rem_mean=rem_mean, sum_var=sum_var, rem_var=rem_var)
+
+
+def layernorm_forward(x, w, b, table, m, d):
+    """The Layernorm arm's forward (compose.rs:1467-1496, layernorm_chain.rs:34-44)."""
+    x = o.u64(x).reshape(-1)
+    mean_sq = o.row_sums(o.vec_mul(x, x), m, d, d)
+    idx = (np.maximum(to_i64(mean_sq), 0).astype(np.uint64) % np.uint64(table.size)).astype(np.uint32)
+    rsqrt = table[idx.astype(np.int64)]
+    scale = o.vec_mul(_rows(rsqrt, m, d), w)
+    out = o.vec_add(o.vec_mul(x, scale), b)
+    return dict(mean_sq=mean_sq, idx=idx, rsqrt=rsqrt, scale=scale, out=out)
+
+
+def softmax_forward(idx, table, m, n):
+    e = _gather(table, idx)
+    s = o.row_sums(e, m, n, n)
+    out = from_i64(round_div(to_i64(e) * (1 << 16), np.repeat(to_i64(s), n)))
+    return e, out, s
+
+
+def forward_ops(store, ops):
+    for op in ops:
+        k = op.kind
+        g = store.get
+        if k == "Transpose":
+            store.v[op.out] = np.ascontiguousarray(g(op.x).reshape(op.m, op.k).T).reshape(-1)
+        elif k == "Scale":
+            with np.errstate(over="ignore"):
+                store.v[op.out] = from_i64(round_div(to_i64(g(op.x)) * np.int64(op.factor), 1 << op.shift))
+        elif k == "MatMul":
+            store.v[op.c] = o.matmul_field(g(op.a).reshape(op.m, op.k), g(op.b).reshape(op.k, op.n)).reshape(-1)
+        elif k == "Projection":
+            h = to_i64(o.matmul_field(g(op.x).reshape(op.m, op.k), g(op.w).reshape(op.k, op.n)).reshape(-1))
+            bi = to_i64(g(op.bias))
+            out = from_i64(round_div(h, 1 << op.shift) + bi)
+            with np.errstate(over="ignore"):
+                rem = from_i64(h - (to_i64(out) - bi) * (1 << op.shift) + (1 << (op.shift - 1)))
+            store.v[op.out], store.v[op.rem] = out, rem
+        elif k == "Add":
+            store.v[op.c] = o.vec_add(g(op.a), g(op.b))
+        elif k == "Lookup":
+            store.v[op.out] = _gather(g(op.table), store.idx[op.idx])
+        elif k == "Softmax":
+            e, out, _ = softmax_forward(store.idx[op.idx], g(op.table), op.m, op.n)
+            store.v[op.e], store.v[op.out] = e, out
+        elif k == "SoftmaxIndex":
+            v = np.maximum(to_i64(g(op.x)), 0).astype(np.uint64)
+            store.idx[op.out] = (v % np.uint64(op.table_len)).astype(np.uint32)
+        elif k == "GeluIndex":
+            with np.errstate(over="ignore"):
+                v = to_i64(g(op.x)) + np.int64(op.offset)
+            store.idx[op.out] = np.clip(v, 0, op.table_len - 1).astype(np.uint32)
+        elif k == "StableSoftmaxIndex":
+            masked = to_i64(o.vec_add(g(op.x), g(op.mask))).reshape(op.m, op.n)
+            row_max = masked.max(axis=1, keepdims=True)
+            with np.errstate(over="ignore"):
+                v = (masked - row_max + np.int64(op.offset)).reshape(-1)
+            store.idx[op.out] = np.clip(v, 0, op.table_len - 1).astype(np.uint32)
+        elif k == "Layernorm":
+            store.v[op.out] = layernorm_forward(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d)["out"]
+        elif k == "LayerNormCentered":
+            store.v[op.out] = layer_norm_forward(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d,
+                                                 op.n_real)["out"]
+        else:
+            raise ValueError(f"op {k} is not restated")
+
+
+# ---- op arms -----------------------------------------------------------------------------
+def _vp(mles, terms, ch):
+    """prove_virtual -> (rounds, finals)."""
+    return o.virtual_prove([o.u64(t).reshape(-1) for t in mles], terms, ch)
+
+
+def prove_layer_norm_centered(x, w, b, table, m, d, n_real, rng):
+    """layer_norm_centered.rs:122-245.  The two reduction sumchecks whose
+    proofs the reference discards (:153-159, :193-201) only advance the
+    challenge source here; they contribute nothing to the proof."""
+    f = layer_norm_forward(x, w, b, table, m, d, n_real)
+    lm, lmd = _lg(m), _lg(m * d)
+    df, half_d = n_real % P, (n_real // 2) % P
+    r_mean = _draw(rng, lm)
+    _draw(rng, lmd)  # mean_ch of the discarded mean reduction
+    m_ch = _draw(rng, lm)
+    ones_m = np.ones(m, dtype=np.uint64)
+    trunc_terms = [(df, [0]), (1, [1]), (NEG, [2]), (NEG * half_d % P, [3])]
+    mean = _vp([f["mean"], f["rem_mean"], f["sum_mean"], ones_m], trunc_terms, m_ch)
+    centered_r = _draw(rng, lmd)
+    centered = _vp([x, _rows(f["mean"], m, d), f["centered"]], [(1, [2]), (NEG, [0]), (1, [1])], centered_r)
+    r_var = _draw(rng, lm)
+    _draw(rng, lmd)  # var_ch of the discarded variance reduction
+    v_ch = _draw(rng, lm)
+    var = _vp([f["var"], f["rem_var"], f["sum_var"], ones_m], trunc_terms, v_ch)
+    r_out = _draw(rng, lmd)
+    two32, half32 = 1 << 32, 1 << 31
+    out_terms = [(1, [0, 1, 2]), (NEG, [4]), (1, [4]), (NEG * two32 % P, [5]), (two32, [3]), (NEG, [6]),
+                 (half32, [7])]
+    out = _vp([f["centered"], _rows(f["rstd"], m, d), w, b, f["raw"], f["out"], f["rem_out"],
+               np.ones(m * d, dtype=np.uint64)], out_terms, r_out)
+    proof = ("LayerNormCentered", mean, centered, var, out, r_mean, m_ch, centered_r, r_var, v_ch, r_out)
+    return proof, f["s_index"], f["rstd"]
+
+
+def prove_layernorm_chain(x, w, b, table, m, d, rng):
+    """layernorm_chain.rs:24-93."""
+    f = layernorm_forward(x, w, b, table, m, d)
+    r_mean = _draw(rng, _lg(m))
+    eq_b = _rows(o.eq_evals(r_mean), m, d)
+    mean_claim = o.mle_eval(f["mean_sq"], r_mean)
+    mean_ch = _draw(rng, _lg(m * d))
+    mean_sq = _vp([eq_b, x], [(1, [0, 1, 1])], mean_ch)
+    r_out = _draw(rng, _lg(m * d))
+    out = _vp([x, f["scale"], b, f["out"]], [(1, [0, 1]), (1, [2]), (NEG, [3])], r_out)
+    return ("Layernorm", mean_sq, out, r_mean, mean_ch, r_out, mean_claim), f["idx"], f["rsqrt"]
+
+
+def prove_softmax_rounded(idx, e, out, table, m, n, rng):
+    """softmax_scaled.rs:42-108."""
+    s = o.row_sums(e, m, n, n)
+    r_sum = _draw(rng, _lg(m))
+    eq_b = _rows(o.eq_evals(r_sum), m, n)
+    sum_ch = _draw(rng, _lg(m * n))
+    claimed = o.mle_eval(s, r_sum)
+    row_sum = _vp([eq_b, e], [(1, [0, 1])], sum_ch)
+    sum_b = _rows(s, m, n)
+    with np.errstate(over="ignore"):
+        rem = from_i64(to_i64(e) * (1 << 16) - to_i64(out) * to_i64(sum_b))
+    r_scale = _draw(rng, _lg(m * n))
+    rescale = _vp([out, e, sum_b, rem], [(1, [0, 2]), (NEG * (1 << 16) % P, [1]), (1, [3])], r_scale)
+    return ("Softmax", row_sum, rescale, r_sum, sum_ch, r_scale, claimed)
+
+
+def prove_same_poly(f, claims, rng):
+    """same_poly.rs:13-45 -> (coeffs, (rounds, finals), merged_point, merged_eval)."""
+    t = _lg(len(f))
+    coeffs = _draw(rng, len(claims))
+    eqs = [o.eq_evals(pt) for pt, _ in claims]
+    terms = [(int(c), [0, i + 1]) for i, c in enumerate(coeffs)]
+    merged = _draw(rng, t)
+    rounds, finals = o.virtual_prove([f] + eqs, terms, merged)
+    return (coeffs, (rounds, finals), merged, int(finals[0]))
+
+
+def prove_fractional(num, den, rng):
+    """logup_gkr.rs:71-81 -> (layers, final_num, final_den, full_r); layer =
+    (r, c, rounds, finals)."""
+    lg = _lg(len(num))
+    full_r, cs = _draw(rng, lg), _draw(rng, lg)
+    rounds, finals, fnum, fden = o.fractional_prove(num, den, full_r, cs)
+    layers = tuple((full_r[:lg - l - 1].copy(), int(cs[l]), rounds[l], finals[l]) for l in range(lg))
+    return (layers, fnum, fden, full_r)
+
+
+def fractional_leaf(proof):
+    layers, _, _, full_r = proof
+    top = int(full_r[-1])
+    fe = [int(v) for v in layers[0][3]]
+    one_m = (1 - top) % P
+    return full_r.copy(), (one_m * fe[3] + top * fe[4]) % P, (one_m * fe[5] + top * fe[6]) % P
+
+
+def merge_multiplicity(xs, t):
+    m = np.zeros(t, dtype=np.uint64)
+    for x in xs:
+        x = np.asarray(x, dtype=np.int64)
+        if x.size and x.max() >= t:
+            raise IndexError("lookup index outside the table")
+        m += np.bincount(x, minlength=t).astype(np.uint64)
+    return m
+
+
+def prove_lookup_witness_batch_columns(xs, ys, alpha, beta, rng):
+    x = np.concatenate([np.asarray(v, dtype=np.uint32) for v in xs]) if xs else np.zeros(0, np.uint32)
+    y = np.concatenate([o.u64(v).reshape(-1) for v in ys]) if ys else np.zeros(0, np.uint64)
+    num, den = o.lookup_num_den(x, y, None, None, 2, alpha, beta)
+    x_flat = np.zeros(num.size, dtype=np.uint64)
+    y_flat = np.zeros(num.size, dtype=np.uint64)
+    x_flat[:x.size] = x
+    y_flat[:y.size] = y
+    return prove_fractional(num, den, rng), x_flat, y_flat, num
+
+
+def prove_lookup_table(m, table, alpha, beta, rng):
+    num, den = o.lookup_num_den(None, None, table, m, 3, alpha, beta)
+    return prove_fractional(num, den, rng)
+
+
+# ---- shard (compose.rs:1602-2091, 2276-2346) -------------------------------------------------
+ADD_TERMS = [(1, [2]), (NEG, [0]), (NEG, [1])]
+
+
+def prove_shard_precomputed(store, ops, boundary, rng):
+    """-> dict(ops, bound, binds, claims, witness_columns, table_columns)."""
+    g = store.get
+    claims, op_proofs, lookups = [], [], {}
+
+    def claim(t, pt):
+        pt = o.u64(pt).reshape(-1)
+        claims.append((t, pt, o.mle_eval(g(t), pt)))
+
+    for op in ops:
+        k = op.kind
+        if k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex"):
+            op_proofs.append((k,))
+        elif k == "MatMul":
+            r = o.op_matmul_prove(g(op.a).reshape(op.m, op.k), g(op.b).reshape(op.k, op.n),
+                                  g(op.c).reshape(op.m, op.n), op.m, op.k, op.n, rng)
+            fe = [int(v) for v in r["finals"]]
+            pts = [np.concatenate([r["ch"], r["u"]]), np.concatenate([r["v"], r["ch"]]),
+                   np.concatenate([r["v"], r["u"]])]
+            for t, pt, ev in zip((op.a, op.b, op.c), pts, r["claims"]):
+                claims.append((t, o.u64(pt), int(ev)))
+            op_proofs.append(("MatMul", r["claimed"], r["rounds"], fe[0], fe[1], r["u"], r["v"], r["ch"]))
+        elif k == "Projection":
+            p = o.projection_prove(g(op.x), g(op.w), g(op.bias), g(op.out), g(op.rem), op.m, op.k, op.n,
+                                   op.shift, rng)
+            claim(op.x, np.concatenate([p["ch"], p["u"]]))
+            claim(op.w, np.concatenate([p["v"], p["ch"]]))
+            claim(op.out, p["pt"])
+            claims.append((op.bias, o.u64(p["pt"]), int(p["affine_finals"][4])))
+            lg = len(p["full_r"])
+            layers = tuple((p["full_r"][:lg - l - 1].copy(), int(p["cs"][l]), p["frac_rounds"][l],
+                            p["frac_finals"][l]) for l in range(lg))
+            frac = (layers, p["final_num"], p["final_den"], p["full_r"])
+            mm = (p["claimed"], p["mm_rounds"], int(p["mm_finals"][0]), int(p["mm_finals"][1]))
+            op_proofs.append(("Projection", mm, (p["affine_rounds"], p["affine_finals"]), frac, p["alpha"],
+                              p["beta"], p["pt"], p["u"], p["v"], p["ch"]))
+        elif k == "Add":
+            r = _draw(rng, _lg(len(g(op.c))))
+            proof = _vp([g(op.a), g(op.b), g(op.c)], ADD_TERMS, r)
+            for t in (op.a, op.b, op.c):
+                claim(t, r)
+            op_proofs.append(("Add", proof, r))
+        elif k == "Lookup":
+            lookups.setdefault(op.table, []).append((store.idx[op.idx], g(op.out)))
+            op_proofs.append(("Lookup",))
+        elif k == "Softmax":
+            p = prove_softmax_rounded(store.idx[op.idx], g(op.e), g(op.out), g(op.table), op.m, op.n, rng)
+            claim(op.out, p[5])
+            lookups.setdefault(op.table, []).append((store.idx[op.idx], g(op.e)))
+            op_proofs.append(p)
+        elif k == "Layernorm":
+            p, ridx, rvals = prove_layernorm_chain(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d, rng)
+            lookups.setdefault(op.rsqrt_table, []).append((ridx, rvals))
+            for t in (op.out, op.w, op.b):
+                claim(t, p[5])
+            op_proofs.append(p)
+        elif k == "LayerNormCentered":
+            p, ridx, rvals = prove_layer_norm_centered(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m,
+                                                       op.d, op.n_real, rng)
+            lookups.setdefault(op.rsqrt_table, []).append((ridx, rvals))
+            claim(op.x, p[7])
+            for t in (op.out, op.w, op.b):
+                claim(t, p[10])
+            op_proofs.append(p)
+        else:
+            raise ValueError(f"op {k} is not restated")
+
+    by_tensor = {}
+    for t, pt, ev in claims:
+        by_tensor.setdefault(t, []).append((pt, ev))
+    bound, binds = [], []
+    for t in sorted(by_tensor):
+        cs = by_tensor[t]
+        if t in set(boundary) or len(cs) < 2:
+            continue
+        binds.append(prove_same_poly(g(t), cs, rng))
+        bound.append(t)
+
+    witness_columns, table_columns = [], []
+    for table in sorted(lookups):
+        alpha, beta = rng.field(), rng.field()
+        xs = [x for x, _ in lookups[table]]
+        ys = [y for _, y in lookups[table]]
+        proof, x_flat, y_flat, num = prove_lookup_witness_batch_columns(xs, ys, alpha, beta, rng)
+        point, nl, dl = fractional_leaf(proof)
+        m = merge_multiplicity(xs, len(g(table)))
+        tproof = prove_lookup_table(m, g(table), alpha, beta, rng)
+        tpoint, tnl, tdl = fractional_leaf(tproof)
+        witness_columns.append((proof, x_flat, y_flat, num, point, nl, dl, alpha, beta, table))
+        table_columns.append((tproof, table, m, alpha, beta, tpoint, tnl, tdl))
+    return dict(ops=op_proofs, bound=bound, binds=binds, claims=claims, witness_columns=witness_columns,
+                table_columns=table_columns)
+
+
+def prove_shard(store, ops, boundary, rng):
+    forward_ops(store, ops)
+    return prove_shard_precomputed(store, ops, boundary, rng)
+
+
+def shard_ranges(op_count, ops_per_shard):
+    ops_per_shard = max(ops_per_shard, 1)
+    return [(s, min(s + ops_per_shard, op_count)) for s in range(0, op_count, ops_per_shard)]
+
+
+def master_transcript(ops, ops_per_shard):
+    """Transcript::new("zkie-shard-dag-v1") with absorb_statement (compose.rs:2276-2287)."""
+    t = o.OracleTranscript(b"zkie-shard-dag-v1")
+    t.absorb_u64(ops_per_shard)
+    t.absorb_u64(len(ops))
+    for op in ops:
+        for i in op.reads():
+            t.absorb_u64(i)
+        for i in op.writes():
+            t.absorb_u64(i)
+    return t
+
+
+def prove_shard_dag(store, ops, ops_per_shard):
+    """compose.rs:2289-2346 -> dict(shards, cross_tensors, cross_binds)."""
+    forward_ops(store, ops)
+    master = master_transcript(ops, ops_per_shard)
+    shards = []
+    for si, (s, e) in enumerate(shard_ranges(len(ops), ops_per_shard)):
+        child = o.OracleTranscript(raw=master.t)
+        child.absorb_u64(si)
+        shards.append(prove_shard_precomputed(store, ops[s:e], [], child))
+    by_tensor, owners = {}, {}
+    for si, sh in enumerate(shards):
+        for t, pt, ev in sh["claims"]:
+            by_tensor.setdefault(t, []).append((pt, ev))
+            owners.setdefault(t, set()).add(si)
+    cross_tensors, cross_binds = [], []
+    for t in sorted(by_tensor):
+        if len(owners[t]) > 1:
+            cross_binds.append(prove_same_poly(store.get(t), by_tensor[t], master))
+            cross_tensors.append(t)
+    return dict(shards=shards, cross_tensors=cross_tensors, cross_binds=cross_binds)
+
+
+# ---- verify_shard_precomputed (compose.rs:2103-2239) ------------------------------------------
+def _verify_virtual(vp, terms, claimed, ch):
+    rounds, finals = vp
+    return o.virtual_verify(rounds, terms, claimed, ch, finals)
+
+
+def _chain_core(frac):
+    layers, _, _, full_r = frac
+    cs = [c for _, c, _, _ in layers]
+    return o.fractional_chain_core(full_r, cs, [r for _, _, r, _ in layers], [f for _, _, _, f in layers])
+
+
+def verify_lookup_split(wp, tp):
+    """logup_gkr.rs verify_lookup_split: both chains sound and the two sides'
+    fractional sums equal (cross-multiplied)."""
+    return (_chain_core(wp) and _chain_core(tp)
+            and (wp[1] * tp[2] - tp[1] * wp[2]) % P == 0)
+
+
+def verify_layer_norm_centered(p, n_real):
+    """layer_norm_centered.rs:247-310."""
+    _, mean, centered, var, out, _, mean_ch, centered_r, _, var_ch, r_out = p
+    trunc = [(n_real % P, [0]), (1, [1]), (NEG, [2]), (NEG * (n_real // 2) % P, [3])]
+    two32 = 1 << 32
+    out_terms = [(1, [0, 1, 2]), (NEG, [4]), (1, [4]), (NEG * two32 % P, [5]), (two32, [3]), (NEG, [6]),
+                 (1 << 31, [7])]
+    return (_verify_virtual(mean, trunc, 0, mean_ch)
+            and _verify_virtual(centered, [(1, [2]), (NEG, [0]), (1, [1])], 0, centered_r)
+            and _verify_virtual(var, trunc, 0, var_ch)
+            and _verify_virtual(out, out_terms, 0, r_out))
+
+
+def verify_layernorm_chain(p):
+    """layernorm_chain.rs:95-115."""
+    _, mean_sq, out, _, mean_ch, r_out, mean_claim = p
+    return (_verify_virtual(mean_sq, [(1, [0, 1, 1])], mean_claim, mean_ch)
+            and _verify_virtual(out, [(1, [0, 1]), (1, [2]), (NEG, [3])], 0, r_out))
+
+
+def verify_softmax_rounded(p):
+    """softmax_scaled.rs:110-135."""
+    _, row_sum, rescale, _, sum_ch, r_scale, claimed = p
+    return (_verify_virtual(row_sum, [(1, [0, 1])], claimed, sum_ch)
+            and _verify_virtual(rescale, [(1, [0, 2]), (NEG * (1 << 16) % P, [1]), (1, [3])], 0, r_scale))
+
+
+def verify_same_poly(sp, claims):
+    """same_poly.rs:46-70: the merged evaluation, or None."""
+    coeffs, vp, merged, merged_eval = sp
+    terms = [(int(c), [0, i + 1]) for i, c in enumerate(coeffs)]
+    claimed = sum(int(c) * int(y) for c, (_, y) in zip(coeffs, claims)) % P
+    return merged_eval if _verify_virtual(vp, terms, claimed, merged) else None
+
+
+def verify_shard(ops, proof):
+    """verify_shard_precomputed over the proof layout of prove_shard_precomputed."""
+    if len(proof["ops"]) != len(ops) or len(proof["bound"]) != len(proof["binds"]):
+        return False
+    wcols = {c[9]: c for c in proof["witness_columns"]}
+    tcols = {c[1]: c for c in proof["table_columns"]}
+    for op, p in zip(ops, proof["ops"]):
+        k = op.kind
+        if p[0] != k:
+            return False
+        if k == "MatMul":
+            _, claimed, rounds, f, h, _, _, ch = p
+            ok = o.sumcheck_verify(rounds, claimed, ch, f, h)
+        elif k == "Projection":
+            _, mm, aff, frac, alpha, beta, pt, u, v, ch = p
+            lg = len(frac[3])
+            ok = o.projection_verify(dict(claimed=mm[0], mm_rounds=mm[1], mm_finals=[mm[2], mm[3]], ch=ch,
+                                          affine_rounds=aff[0], affine_finals=aff[1], pt=pt, full_r=frac[3],
+                                          cs=[l[1] for l in frac[0]], frac_rounds=[l[2] for l in frac[0]],
+                                          frac_finals=[l[3] for l in frac[0]], final_num=frac[1]),
+                                     op.shift) if lg else False
+        elif k == "Add":
+            ok = _verify_virtual(p[1], ADD_TERMS, 0, p[2])
+        elif k == "Lookup":
+            w, t = wcols.get(op.table), tcols.get(op.table)
+            ok = w is not None and t is not None and verify_lookup_split(w[0], t[0])
+        elif k == "Softmax":
+            ok = verify_softmax_rounded(p)
+        elif k == "Layernorm":
+            ok = verify_layernorm_chain(p)
+        elif k == "LayerNormCentered":
+            ok = verify_layer_norm_centered(p, op.n_real)
+        else:
+            ok = k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex")
+        if not ok:
+            return False
+    by_tensor = {}
+    for t, pt, ev in proof["claims"]:
+        by_tensor.setdefault(t, []).append((pt, ev))
+    for t, sp in zip(proof["bound"], proof["binds"]):
+        cs = by_tensor.get(t, [])
+        if len(cs) < 2 or verify_same_poly(sp, cs) is None:
+            return False
+    return True

@@ -98,6 +98,10 @@ def lib():
             "orc_fractional_verify": (C.c_int, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _u64, _u64, _u64]),
             "orc_fractional_chain_core": (C.c_int, [_u32, _pu64, _pu64, _pu64, _pu64]),
             "orc_lookup_len": (_u64, [_u64, _u64, _u32]),
+            "orc_vec_add": (None, [_pu64, _pu64, _u64, _pu64]),
+            "orc_vec_sub": (None, [_pu64, _pu64, _u64, _pu64]),
+            "orc_vec_mul": (None, [_pu64, _pu64, _u64, _pu64]),
+            "orc_row_sums": (None, [_pu64, _u64, _u64, _u64, _pu64]),
             "orc_lookup_num_den": (_u64, [_pu32, _pu64, _u64, _pu64, _pu64, _u64, _u32, _u64, _u64, _pu64,
                                           _pu64]),
         }
@@ -128,6 +132,30 @@ def mul(a, b): return lib().orc_mul(a, b)
 def inv(a): return lib().orc_inv(a)
 def from_i64(x): return lib().orc_from_i64(int(x))
 def two_adic_generator(bits): return lib().orc_two_adic_generator(bits)
+
+
+def _vec(fn, a, b):
+    a, b = u64(a).reshape(-1), u64(b).reshape(-1)
+    if a.size != b.size:
+        raise ValueError("field vector lengths differ")
+    out = np.zeros(a.size, dtype=np.uint64)
+    if a.size:
+        fn(ptr(a), ptr(b), a.size, ptr(out))
+    return out
+
+
+def vec_add(a, b): return _vec(lib().orc_vec_add, a, b)
+def vec_sub(a, b): return _vec(lib().orc_vec_sub, a, b)
+def vec_mul(a, b): return _vec(lib().orc_vec_mul, a, b)
+
+
+def row_sums(x, m, d, ncols):
+    """Field sums of the first ncols entries of each of the m rows (d wide)."""
+    xx = u64(x).reshape(-1)
+    out = np.zeros(m, dtype=np.uint64)
+    if m:
+        lib().orc_row_sums(ptr(xx), m, d, ncols, ptr(out))
+    return out
 
 
 # ---- PRNG / transcript --------------------------------------------------------------

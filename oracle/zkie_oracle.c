@@ -1191,3 +1191,37 @@ void orc_set_threads(int n)
     (void)n;
 #endif
 }
+
+/* ============================================================================
+ * Elementwise field operations and row sums for the op-layer restatement
+ * (the Goldilocks +, -, * of crates/zkie-ops/src/compose.rs's forward and
+ * prove arms, over whole tensors).
+ * ========================================================================== */
+void orc_vec_add(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) out[i] = orc_add(canon(a[i]), canon(b[i]));
+}
+
+void orc_vec_sub(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) out[i] = orc_sub(canon(a[i]), canon(b[i]));
+}
+
+void orc_vec_mul(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)n; i++) out[i] = orc_mul(a[i], b[i]);
+}
+
+/* out[r] = sum_{j < ncols} x[r * d + j] over the field, r < m */
+void orc_row_sums(const uint64_t *x, uint64_t m, uint64_t d, uint64_t ncols, uint64_t *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < (int64_t)m; r++) {
+        uint64_t s = 0;
+        for (uint64_t j = 0; j < ncols; j++) s = orc_add(s, canon(x[r * d + j]));
+        out[r] = s;
+    }
+}

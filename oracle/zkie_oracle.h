@@ -194,6 +194,13 @@ uint64_t orc_lookup_num_den(const uint32_t *x, const uint64_t *y, uint64_t n, co
                             const uint64_t *m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
                             uint64_t *num, uint64_t *den);
 
+/* Elementwise field +, -, * and per-row field sums of the first ncols of each
+ * d-wide row (the op-layer restatement's tensor arithmetic). */
+void orc_vec_add(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out);
+void orc_vec_sub(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out);
+void orc_vec_mul(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out);
+void orc_row_sums(const uint64_t *x, uint64_t m, uint64_t d, uint64_t ncols, uint64_t *out);
+
 #ifdef __cplusplus
 }
 #endif

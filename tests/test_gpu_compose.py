@@ -1,0 +1,124 @@
+"""The op-layer shard prover on the GPU against its CPU restatement, bit for
+bit: every forward tensor, every proof field, every claim, every binding and
+every lookup column, for the reference's own layer test
+(build_gpt2_layer_roundtrip, compose.rs:6211-6259) and for GPT-2-shaped
+layers (models/gpt2/src/lib.rs build_layer) as prove_shard_dag shards; the
+device proofs are also accepted by the restated verifier."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import compose_oracle as co
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+P = co.P
+
+
+def assert_same(a, b, path="proof"):
+    if isinstance(a, dict):
+        assert isinstance(b, dict) and a.keys() == b.keys(), path
+        for k in a:
+            assert_same(a[k], b[k], f"{path}.{k}")
+    elif isinstance(a, (list, tuple)) and not isinstance(a, np.ndarray):
+        assert isinstance(b, (list, tuple)) and len(a) == len(b), f"{path}: {len(a)} vs {len(b)}"
+        for i, (x, y) in enumerate(zip(a, b)):
+            assert_same(x, y, f"{path}[{i}]")
+    elif isinstance(a, np.ndarray) or isinstance(b, np.ndarray):
+        x, y = np.asarray(a, dtype=np.uint64), np.asarray(b, dtype=np.uint64)
+        assert x.shape == y.shape and np.array_equal(x, y), f"{path}: arrays differ"
+    elif isinstance(a, str):
+        assert a == b, f"{path}: {a} vs {b}"
+    else:
+        assert int(a) % P == int(b) % P, f"{path}: {a} vs {b}"
+
+
+def _device_store(zk, host):
+    st = zk.compose.Store()
+    for v in host.v:
+        st.push(None if v is None else v.copy())
+    for i in host.idx:
+        st.push_idx(None if i is None else i.copy())
+    return st
+
+
+def _host_copy(host):
+    c = co.HostStore()
+    c.v = [None if v is None else v.copy() for v in host.v]
+    c.idx = [None if i is None else i.copy() for i in host.idx]
+    return c
+
+
+def _reference_case(zk):
+    from zkie_b200 import gpt2
+    from zkie_b200.gkr import XorShift64
+    host = co.HostStore()
+    ops, out, rng = gpt2.reference_layer_roundtrip_case(host, XorShift64)
+    orng = o.XorShift64(0)
+    orng.s.value = rng.c.xorshift_state
+    return host, ops, out, rng, orng
+
+
+def test_forward_matches_oracle_reference_case(zk):
+    host, ops, _, _, _ = _reference_case(zk)
+    dev = _device_store(zk, host)
+    zk.compose.forward_ops(dev, ops)
+    co.forward_ops(host, ops)
+    for i, v in enumerate(host.v):
+        assert np.array_equal(dev.v[i].cpu().numpy(), v), f"tensor {i}"
+    for i, v in enumerate(host.idx):
+        assert np.array_equal(dev.idx[i].cpu().numpy(), v), f"index tensor {i}"
+
+
+def test_prove_shard_matches_oracle_reference_case(zk):
+    """The reference's layer test: prove_shard(store, ops, [out], rng) with the
+    XorShift64 that drew the weights."""
+    host, ops, out, rng, orng = _reference_case(zk)
+    dev = _device_store(zk, host)
+    got = zk.compose.prove_shard(dev, ops, [out], rng).canonical()
+    want = co.prove_shard(host, ops, [out], orng)
+    assert_same(got, want)
+    assert co.verify_shard(ops, got)
+    assert rng.c.xorshift_state == orng.s.value
+
+
+def _layer(zk, shape):
+    from zkie_b200 import gpt2
+    host = co.HostStore()
+    ops, x, out = gpt2.gpt2_layer(host, shape)
+    return host, ops
+
+
+@pytest.mark.parametrize("name,ops_per_shard", [("small", 176), ("small", 12), ("medium", 176)])
+def test_gpt2_layer_shard_dag_matches_oracle(zk, name, ops_per_shard):
+    from zkie_b200 import gpt2
+    shape = {"small": gpt2.LayerShape(m=8, d=16, d_real=12, heads=2, dh=4, ffn=32, ffn_real=24, exp_bits=8,
+                                      gelu_bits=10, rsqrt_len=256),
+             "medium": gpt2.LayerShape(m=64, d=128, d_real=96, heads=6, dh=16, ffn=512, ffn_real=384, exp_bits=12,
+                                       gelu_bits=14, rsqrt_len=4096)}[name]
+    host, ops = _layer(zk, shape)
+    dev = _device_store(zk, host)
+    ref = _host_copy(host)
+    got = zk.compose.prove_shard_dag(dev, ops, ops_per_shard).canonical()
+    want = co.prove_shard_dag(ref, ops, ops_per_shard)
+    for i, v in enumerate(ref.v):
+        assert np.array_equal(dev.v[i].cpu().numpy(), v), f"forward tensor {i}"
+    assert_same(got, want)
+    for (s, e), sh in zip(co.shard_ranges(len(ops), ops_per_shard), got["shards"]):
+        assert co.verify_shard(ops[s:e], sh)
+
+
+def test_lookup_outside_table_is_an_error(zk):
+    """An index past the table end raises on the host (the reference panics);
+    the kernel bounds-checks every read."""
+    C = zk.compose
+    st = C.Store()
+    x = st.push(np.array([1, 2, 3, 70], dtype=np.uint64))
+    idx = st.push_idx(None)
+    table = st.push(np.arange(64, dtype=np.uint64))
+    out = st.push(None)
+    ops = [C.SoftmaxIndex(x, idx, 1 << 8), C.Lookup(idx, out, table)]
+    with pytest.raises(ValueError, match="outside its table"):
+        C.forward_ops(st, ops)
+    torch.cuda.synchronize()

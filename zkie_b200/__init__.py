@@ -24,3 +24,4 @@ from .logup import (  # noqa: F401
     prove_fractional_with_challenges, prove_lookup_fractional, prove_lookup_fractional_batch,
     prove_lookup_fractional_columns, prove_lookup_table, prove_lookup_witness, prove_lookup_witness_batch,
     prove_lookup_witness_batch_columns)
+from . import compose, gpt2, projection  # noqa: F401,E402

@@ -10,6 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libzkie_b200.so")
 
 u64, u32, i32, i64 = C.c_uint64, C.c_uint32, C.c_int32, C.c_int
+s64 = C.c_int64
 pu64 = C.POINTER(C.c_uint64)
 pu32 = C.POINTER(C.c_uint32)
 vp = C.c_void_p  # device pointers and streams travel as integers
@@ -112,6 +113,33 @@ SIGNATURES = {
     "zkie2_lookup_len": (u64, [u64, u64, u32]),
     "zkie2_lookup_scratch_elems": (u64, [u64]),
     "zkie2_lookup_num_den": (i64, [vp, vp, u64, vp, vp, u64, u32, u64, u64, vp, vp, vp, vp]),
+    "zkie2_xorshift_fill": (None, [pu64, u64, u64, s64, pu64]),
+    "zkie2_mle_eval_async": (i64, [vp, u32, pu64, vp, vp, vp]),
+    "zkie2_op_matmul_prove_async": (i64, [vp, vp, vp, u64, u64, u64, pu64, pu64, pu64, vp, vp, vp]),
+    "zkie2_projection_proof_elems": (u64, [u64, u64, u64, u32]),
+    "zkie2_projection_prove_async": (i64, [vp, vp, vp, vp, vp, vp, u64, u64, u64, u32, pu64, pu64, pu64, u64, u64,
+                                           pu64, pu64, vp, vp, vp, vp]),
+    "zkie2_virtual_prove_async": (i64, [C.POINTER(vp), u32, u32, pu64, pu32, pu32, u32, pu64, vp, vp, vp, vp]),
+    "zkie2_fractional_proof_elems": (u64, [u32]),
+    "zkie2_fractional_prove_async": (i64, [vp, vp, u32, pu64, pu64, vp, vp, vp]),
+    "zkie2_lookup_num_den_async": (i64, [vp, vp, u64, vp, vp, u64, u32, u64, u64, vp, vp, vp, vp, vp]),
+    "zkie2_lookup_multiplicity": (i64, [vp, u64, u64, vp, i64, vp, vp]),
+    "zkie2_op_add": (i64, [vp, vp, u64, vp, vp]),
+    "zkie2_op_scale": (i64, [vp, u64, s64, u32, vp, vp]),
+    "zkie2_op_transpose": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_op_softmax_index": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_op_gelu_index": (i64, [vp, u64, s64, u64, vp, vp]),
+    "zkie2_op_stable_softmax_index": (i64, [vp, vp, u64, u64, s64, u64, vp, vp]),
+    "zkie2_op_lookup": (i64, [vp, u64, vp, u64, vp, vp, vp]),
+    "zkie2_op_softmax": (i64, [vp, vp, u64, u64, u64, vp, vp, vp, vp, vp]),
+    "zkie2_op_softmax_rem": (i64, [vp, vp, vp, u64, u64, vp, vp, vp]),
+    "zkie2_op_layer_norm_centered": (i64, [vp, vp, vp, vp, u64, u64, u64, u64, C.POINTER(vp), vp, vp, vp]),
+    "zkie2_op_layernorm": (i64, [vp, vp, vp, vp, u64, u64, u64, vp, vp, vp, vp, vp, vp]),
+    "zkie2_op_row_broadcast": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_op_row_sums": (i64, [vp, u64, u64, u64, vp, vp]),
+    "zkie2_op_fill": (i64, [vp, u64, u64, vp]),
+    "zkie2_eq_combine_scratch_elems": (u64, [u32, u32]),
+    "zkie2_eq_combine": (i64, [pu64, pu64, u32, u32, vp, vp, vp]),
     "zkie2_mg_available": (i64, []),
     "zkie2_mg_unique_id": (i64, [C.c_char_p]),
     "zkie2_mg_init": (i64, [C.c_char_p, i64, i64, C.POINTER(vp)]),

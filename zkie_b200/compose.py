@@ -1,0 +1,988 @@
+"""The op layer of zkie-ops (crates/zkie-ops/src/compose.rs) on the device.
+
+Host-side mirror of the reference's op graph and shard prover for the arms a
+GPT-2 layer uses, over libzkie_b200.so:
+
+- the ``Op`` variants (compose.rs:560-800) with ``reads`` / ``writes``
+  (:955-1060), and ``Store`` (:525-560) holding device tensors;
+- ``forward_ops`` (:1174-1583): every arm's forward witness as device
+  kernels (the matmuls on the tensor cores where the inputs allow, as
+  par::mm_par_fixed);
+- ``prove_shard_precomputed`` (:1602-2091), ``prove_shard`` (:1589-1597) and
+  ``prove_shard_dag`` (:2289-2346), with the arms' provers:
+  prove_layer_norm_centered (layer_norm_centered.rs:122-245),
+  prove_layernorm_chain (layernorm_chain.rs:24-93), prove_softmax_rounded
+  (softmax_scaled.rs:42-108), prove_same_poly (common/same_poly.rs:13-45),
+  prove_projection (projection.rs:44-101), the Op::MatMul and Add arms, and
+  the per-table logUp of prove_lookup_witness_batch_columns and
+  prove_lookup_table (common/logup_gkr.rs:340-383).
+
+No prover in zkie-ops absorbs proof data into its challenge source: every
+challenge of a shard is a function of the statement alone.  The prover
+therefore draws each challenge on the host in the reference's order and
+enqueues the device work behind it without waiting; the proof, the claims'
+evaluations and the error word come back in one copy at the end.  The two
+reduction sumchecks of prove_layer_norm_centered whose proofs the reference
+discards (:153-159, :193-201) only advance the challenge source here.
+"""
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .device import P, device, empty, ptr, stream_handle, to_dev
+from .gkr import MatmulProof, OpMatMulProof, SumcheckProof, Transcript, VirtualProof
+from .logup import FractionalLayer, FractionalProof
+from .projection import ProjectionProof
+
+NEG = P - 1
+
+
+# ---- ops (compose.rs:560-800, reads/writes :955-1060) -------------------------------------
+class _Op:
+    kind = ""
+
+    def reads(self):
+        return [getattr(self, f) for f in self._reads]
+
+    def writes(self):
+        return [getattr(self, f) for f in self._writes]
+
+
+@dataclass
+class Transpose(_Op):
+    x: int
+    out: int
+    m: int
+    k: int
+    kind = "Transpose"
+    _reads, _writes = ("x",), ("out",)
+
+
+@dataclass
+class Scale(_Op):
+    x: int
+    out: int
+    factor: int
+    shift: int
+    kind = "Scale"
+    _reads, _writes = ("x",), ("out",)
+
+
+@dataclass
+class MatMul(_Op):
+    a: int
+    b: int
+    c: int
+    m: int
+    k: int
+    n: int
+    kind = "MatMul"
+    _reads, _writes = ("a", "b"), ("c",)
+
+
+@dataclass
+class Projection(_Op):
+    x: int
+    w: int
+    bias: int
+    out: int
+    rem: int
+    m: int
+    k: int
+    n: int
+    shift: int
+    kind = "Projection"
+    _reads, _writes = ("x", "w", "bias"), ("out", "rem")
+
+
+@dataclass
+class Add(_Op):
+    a: int
+    b: int
+    c: int
+    kind = "Add"
+    _reads, _writes = ("a", "b"), ("c",)
+
+
+@dataclass
+class Lookup(_Op):
+    idx: int
+    out: int
+    table: int
+    kind = "Lookup"
+    _reads, _writes = ("idx", "table"), ("out",)
+
+
+@dataclass
+class Softmax(_Op):
+    idx: int
+    e: int
+    out: int
+    table: int
+    m: int
+    n: int
+    kind = "Softmax"
+    _reads, _writes = ("idx", "table"), ("e", "out")
+
+
+@dataclass
+class SoftmaxIndex(_Op):
+    x: int
+    out: int
+    table_len: int
+    kind = "SoftmaxIndex"
+    _reads, _writes = ("x",), ("out",)
+
+
+@dataclass
+class GeluIndex(_Op):
+    x: int
+    out: int
+    offset: int
+    table_len: int
+    kind = "GeluIndex"
+    _reads, _writes = ("x",), ("out",)
+
+
+@dataclass
+class StableSoftmaxIndex(_Op):
+    x: int
+    mask: int
+    out: int
+    offset: int
+    table_len: int
+    m: int
+    n: int
+    kind = "StableSoftmaxIndex"
+    _reads, _writes = ("x", "mask"), ("out",)
+
+
+@dataclass
+class Layernorm(_Op):
+    x: int
+    w: int
+    b: int
+    out: int
+    rsqrt_table: int
+    m: int
+    d: int
+    kind = "Layernorm"
+    _reads, _writes = ("x", "w", "b", "rsqrt_table"), ("out",)
+
+
+@dataclass
+class LayerNormCentered(_Op):
+    x: int
+    w: int
+    b: int
+    out: int
+    rsqrt_table: int
+    m: int
+    d: int
+    n_real: int
+    kind = "LayerNormCentered"
+    _reads, _writes = ("x", "w", "b", "rsqrt_table"), ("out",)
+
+
+# ---- the store (compose.rs:525-560) -------------------------------------------------------
+class Store:
+    """Field tensors ``v`` and u32 index tensors ``idx`` on the device, two id
+    spaces as in the reference.  ``proj_h`` keeps each Projection's forward
+    product x W (by output id) so the prover need not recompute it."""
+
+    def __init__(self):
+        self.v: List[Optional[torch.Tensor]] = []
+        self.idx: List[Optional[torch.Tensor]] = []
+        self.proj_h = {}
+
+    def push(self, t=None) -> int:
+        self.v.append(None if t is None else to_dev(t).reshape(-1))
+        return len(self.v) - 1
+
+    def push_idx(self, t=None) -> int:
+        if t is not None:
+            t = torch.as_tensor(np.asarray(t, dtype=np.uint32) if not isinstance(t, torch.Tensor) else t)
+            t = t.to(device(), torch.uint32).reshape(-1).contiguous()
+        self.idx.append(t)
+        return len(self.idx) - 1
+
+    def get(self, t: int) -> torch.Tensor:
+        v = self.v[t]
+        if v is None:
+            raise ValueError(f"tensor {t} has no value (forward not run?)")
+        return v
+
+    def get_idx(self, t: int) -> torch.Tensor:
+        v = self.idx[t]
+        if v is None:
+            raise ValueError(f"index tensor {t} has no value (forward not run?)")
+        return v
+
+
+def _u32(n: int) -> torch.Tensor:
+    return torch.empty(max(n, 1), dtype=torch.uint32, device=device())
+
+
+def _err_word() -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device())
+
+
+_ERRORS = {1: "a lookup index outside its table", 2: "a softmax row sum of zero (round_div by zero)"}
+
+
+def _check_err(err: torch.Tensor, what: str):
+    code = int(err.item())
+    if code:
+        raise ValueError(f"{what}: " + ", ".join(v for k, v in _ERRORS.items() if code & k))
+
+
+def layer_norm_centered_columns(x, w, b, table, m, d, n_real, err):
+    """layer_norm_forward (layer_norm_centered.rs:42-120) on the device: a dict
+    of its outputs (mean, centered, var, rstd, raw, out, rem_out, sum_mean,
+    rem_mean, sum_var, rem_var, s_index)."""
+    names = ("mean", "centered", "var", "rstd", "raw", "out", "rem_out", "sum_mean", "rem_mean", "sum_var",
+             "rem_var")
+    sizes = (m, m * d, m, m, m * d, m * d, m * d, m, m, m, m)
+    outs = {k: empty(s) for k, s in zip(names, sizes)}
+    s_index = _u32(m)
+    arr = (_lib.vp * 11)(*[ptr(outs[k]) for k in names])
+    check(lib.zkie2_op_layer_norm_centered(ptr(x), ptr(w), ptr(b), ptr(table), table.numel(), m, d, n_real, arr,
+                                           s_index.data_ptr(), err.data_ptr(), stream_handle()),
+          "zkie2_op_layer_norm_centered")
+    outs["s_index"] = s_index[:m]
+    return outs
+
+
+def layernorm_columns(x, w, b, table, m, d):
+    """The Layernorm arm's forward (compose.rs:1467-1496): mean_sq, idx, rsqrt, scale, out."""
+    mean_sq, rsqrt, scale, out = empty(m), empty(m), empty(m * d), empty(m * d)
+    idx = _u32(m)
+    check(lib.zkie2_op_layernorm(ptr(x), ptr(w), ptr(b), ptr(table), table.numel(), m, d, ptr(mean_sq),
+                                 idx.data_ptr(), ptr(rsqrt), ptr(scale), ptr(out), stream_handle()),
+          "zkie2_op_layernorm")
+    return dict(mean_sq=mean_sq, idx=idx[:m], rsqrt=rsqrt, scale=scale, out=out)
+
+
+def softmax_columns(idx, table, m, n, err):
+    e, out, s = empty(m * n), empty(m * n), empty(m)
+    check(lib.zkie2_op_softmax(idx.data_ptr(), ptr(table), table.numel(), m, n, ptr(e), ptr(out), ptr(s),
+                               err.data_ptr(), stream_handle()), "zkie2_op_softmax")
+    return e, out, s
+
+
+def _matmul_fixed(a, b, m, k, n):
+    from .gkr import matmul_fixed
+    return matmul_fixed(a, b, m, k, n)[0]
+
+
+def forward_ops(store: Store, ops):
+    """forward_ops (compose.rs:1174-1583) on the device; raises where the
+    reference panics on the data (after the whole pass, one read-back)."""
+    err = _err_word()
+    sh = stream_handle()
+    for op in ops:
+        k = op.kind
+        g = store.get
+        if k == "Transpose":
+            out = empty(op.m * op.k)
+            check(lib.zkie2_op_transpose(ptr(g(op.x)), op.m, op.k, ptr(out), sh), "zkie2_op_transpose")
+            store.v[op.out] = out
+        elif k == "Scale":
+            x = g(op.x)
+            out = empty(x.numel())
+            check(lib.zkie2_op_scale(ptr(x), x.numel(), op.factor, op.shift, ptr(out), sh), "zkie2_op_scale")
+            store.v[op.out] = out
+        elif k == "MatMul":
+            store.v[op.c] = _matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n)
+        elif k == "Projection":
+            h = _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n)
+            out, rem = empty(op.m * op.n), empty(op.m * op.n)
+            check(lib.zkie2_projection_witness(ptr(h), ptr(g(op.bias)), op.m * op.n, op.shift, ptr(out), ptr(rem),
+                                               None, sh), "zkie2_projection_witness")
+            store.v[op.out], store.v[op.rem] = out, rem
+            store.proj_h[op.out] = h
+        elif k == "Add":
+            a, b = g(op.a), g(op.b)
+            out = empty(a.numel())
+            check(lib.zkie2_op_add(ptr(a), ptr(b), a.numel(), ptr(out), sh), "zkie2_op_add")
+            store.v[op.c] = out
+        elif k == "Lookup":
+            idx, table = store.get_idx(op.idx), g(op.table)
+            out = empty(idx.numel())
+            check(lib.zkie2_op_lookup(idx.data_ptr(), idx.numel(), ptr(table), table.numel(), ptr(out),
+                                      err.data_ptr(), sh), "zkie2_op_lookup")
+            store.v[op.out] = out
+        elif k == "Softmax":
+            e, out, _ = softmax_columns(store.get_idx(op.idx), g(op.table), op.m, op.n, err)
+            store.v[op.e], store.v[op.out] = e, out
+        elif k == "SoftmaxIndex":
+            x = g(op.x)
+            idx = _u32(x.numel())
+            check(lib.zkie2_op_softmax_index(ptr(x), x.numel(), op.table_len, idx.data_ptr(), sh),
+                  "zkie2_op_softmax_index")
+            store.idx[op.out] = idx[:x.numel()]
+        elif k == "GeluIndex":
+            x = g(op.x)
+            idx = _u32(x.numel())
+            check(lib.zkie2_op_gelu_index(ptr(x), x.numel(), op.offset, op.table_len, idx.data_ptr(), sh),
+                  "zkie2_op_gelu_index")
+            store.idx[op.out] = idx[:x.numel()]
+        elif k == "StableSoftmaxIndex":
+            idx = _u32(op.m * op.n)
+            check(lib.zkie2_op_stable_softmax_index(ptr(g(op.x)), ptr(g(op.mask)), op.m, op.n, op.offset,
+                                                    op.table_len, idx.data_ptr(), sh),
+                  "zkie2_op_stable_softmax_index")
+            store.idx[op.out] = idx[:op.m * op.n]
+        elif k == "Layernorm":
+            store.v[op.out] = layernorm_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d)["out"]
+        elif k == "LayerNormCentered":
+            store.v[op.out] = layer_norm_centered_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d,
+                                                          op.n_real, err)["out"]
+        else:
+            raise ValueError(f"op {k} is not supported")
+    _check_err(err, "forward_ops")
+
+
+# ---- proofs (compose.rs OpProof / OpShardProof, the arms' proof structs) -------------------
+def _vcanon(p: VirtualProof):
+    return (np.asarray(p.rounds, dtype=np.uint64), np.asarray(p.final_evals, dtype=np.uint64))
+
+
+def _frac_canon(p: FractionalProof):
+    layers = tuple((np.asarray(l.r, dtype=np.uint64), int(l.c), np.asarray(l.proof.rounds, dtype=np.uint64),
+                    np.asarray(l.proof.final_evals, dtype=np.uint64)) for l in p.layers)
+    return (layers, int(p.final_num), int(p.final_den), np.asarray(p.full_r, dtype=np.uint64))
+
+
+@dataclass
+class LayerNormCenteredProof:
+    """layer_norm_centered.rs:25-36."""
+    mean: VirtualProof
+    centered: VirtualProof
+    var: VirtualProof
+    out: VirtualProof
+    r_mean: np.ndarray
+    mean_ch: np.ndarray
+    centered_r: np.ndarray
+    r_var: np.ndarray
+    var_ch: np.ndarray
+    r_out: np.ndarray
+
+    def canonical(self):
+        return ("LayerNormCentered", _vcanon(self.mean), _vcanon(self.centered), _vcanon(self.var),
+                _vcanon(self.out), self.r_mean, self.mean_ch, self.centered_r, self.r_var, self.var_ch, self.r_out)
+
+
+@dataclass
+class LayernormChainProof:
+    """layernorm_chain.rs:14-22."""
+    mean_sq: VirtualProof
+    out: VirtualProof
+    r_mean: np.ndarray
+    mean_ch: np.ndarray
+    r_out: np.ndarray
+    mean_claim: int
+
+    def canonical(self):
+        return ("Layernorm", _vcanon(self.mean_sq), _vcanon(self.out), self.r_mean, self.mean_ch, self.r_out,
+                int(self.mean_claim))
+
+
+@dataclass
+class SoftmaxRoundedProof:
+    """softmax_scaled.rs:31-40."""
+    row_sum: VirtualProof
+    rescale: VirtualProof
+    r_sum: np.ndarray
+    sum_ch: np.ndarray
+    r_scale: np.ndarray
+    claimed: int
+
+    def canonical(self):
+        return ("Softmax", _vcanon(self.row_sum), _vcanon(self.rescale), self.r_sum, self.sum_ch, self.r_scale,
+                int(self.claimed))
+
+
+@dataclass
+class AddProof:
+    """OpProof::Add(proof, r)."""
+    proof: VirtualProof
+    r: np.ndarray
+
+    def canonical(self):
+        return ("Add", _vcanon(self.proof), self.r)
+
+
+@dataclass
+class MarkerProof:
+    """The arms with no proof of their own (Transpose, Scale, Lookup, the index ops)."""
+    kind: str
+
+    def canonical(self):
+        return (self.kind,)
+
+
+@dataclass
+class SamePolyProof:
+    """same_poly.rs:7-12."""
+    coeffs: np.ndarray
+    proof: VirtualProof
+    merged_point: np.ndarray
+    merged_eval: int
+
+    def canonical(self):
+        return (self.coeffs, _vcanon(self.proof), self.merged_point, int(self.merged_eval))
+
+
+@dataclass
+class WitnessColumn:
+    """compose.rs WitnessColumn: the witness side of one table's logUp."""
+    proof: FractionalProof
+    x: torch.Tensor
+    y: torch.Tensor
+    num: torch.Tensor
+    point: np.ndarray
+    num_leaf: int
+    den_leaf: int
+    alpha: int
+    beta: int
+    table: int
+
+    def canonical(self):
+        return (_frac_canon(self.proof), self.x.cpu().numpy(), self.y.cpu().numpy(), self.num.cpu().numpy(),
+                self.point, self.num_leaf, self.den_leaf, self.alpha, self.beta, self.table)
+
+
+@dataclass
+class TableColumn:
+    """compose.rs TableColumn: the table side with its merged multiplicities."""
+    proof: FractionalProof
+    table: int
+    m: torch.Tensor
+    alpha: int
+    beta: int
+    point: np.ndarray
+    num_leaf: int
+    den_leaf: int
+
+    def canonical(self):
+        return (_frac_canon(self.proof), self.table, self.m.cpu().numpy(), self.alpha, self.beta, self.point,
+                self.num_leaf, self.den_leaf)
+
+
+def _op_canon(p):
+    if isinstance(p, OpMatMulProof):
+        mm = p.proof
+        return ("MatMul", mm.claimed, np.asarray(mm.sumcheck.rounds, dtype=np.uint64), mm.sumcheck.f_eval,
+                mm.sumcheck.h_eval, p.u, p.v, p.ch)
+    if isinstance(p, ProjectionProof):
+        mm = p.matmul
+        return ("Projection", (mm.claimed, np.asarray(mm.sumcheck.rounds, dtype=np.uint64), mm.sumcheck.f_eval,
+                               mm.sumcheck.h_eval), _vcanon(p.affine), _frac_canon(p.frac), p.alpha, p.beta, p.pt,
+                p.u, p.v, p.ch)
+    return p.canonical()
+
+
+@dataclass
+class OpShardProof:
+    """compose.rs OpShardProof: per-op proofs, the same_poly bindings, every
+    raw claim (tensor, point, value) and the per-table logUp columns."""
+    ops: list
+    bound: List[int]
+    binds: List[SamePolyProof]
+    claims: list
+    witness_columns: List[WitnessColumn]
+    table_columns: List[TableColumn]
+
+    def canonical(self):
+        return dict(ops=[_op_canon(p) for p in self.ops], bound=list(self.bound),
+                    binds=[b.canonical() for b in self.binds],
+                    claims=[(t, np.asarray(pt, dtype=np.uint64), int(ev)) for t, pt, ev in self.claims],
+                    witness_columns=[c.canonical() for c in self.witness_columns],
+                    table_columns=[c.canonical() for c in self.table_columns])
+
+
+@dataclass
+class ShardDagProof:
+    """compose.rs ShardDagProof."""
+    shards: List[OpShardProof]
+    cross_tensors: List[int]
+    cross_binds: List[SamePolyProof]
+
+    def canonical(self):
+        return dict(shards=[s.canonical() for s in self.shards], cross_tensors=list(self.cross_tensors),
+                    cross_binds=[b.canonical() for b in self.cross_binds])
+
+
+# ---- the shard prover ---------------------------------------------------------------------
+def _terms_arrays(terms):
+    coeffs = np.array([int(c) % P for c, _ in terms] or [0], dtype=np.uint64)
+    off, idx = [0], []
+    for _, ids in terms:
+        idx.extend(int(i) for i in ids)
+        off.append(len(idx))
+    return (coeffs, np.array(off, dtype=np.uint32), np.array(idx or [0], dtype=np.uint32),
+            max((len(ids) for _, ids in terms), default=0))
+
+
+def _pp(a: np.ndarray):
+    return a.ctypes.data_as(_lib.pu64) if a.size else None
+
+
+def _lg(n: int) -> int:
+    n = int(n)
+    if n <= 0 or n & (n - 1):
+        raise ValueError(f"{n} is not a power of two")
+    return n.bit_length() - 1
+
+
+def _eq_at(r, x) -> int:
+    """eq(r, x) = prod_j (r_j x_j + (1 - r_j)(1 - x_j))."""
+    v = 1
+    for a, b in zip(r, x):
+        a, b = int(a), int(b)
+        v = v * ((a * b + (1 - a) * (1 - b)) % P) % P
+    return v
+
+
+ADD_TERMS = [(1, [2]), (NEG, [0]), (NEG, [1])]
+TRUNC_TERMS = lambda df, half: [(df % P, [0]), (1, [1]), (NEG, [2]), (NEG * half % P, [3])]  # noqa: E731
+CENTERED_TERMS = [(1, [2]), (NEG, [0]), (1, [1])]
+LNC_OUT_TERMS = [(1, [0, 1, 2]), (NEG, [4]), (1, [4]), (NEG * (1 << 32) % P, [5]), (1 << 32, [3]), (NEG, [6]),
+                 (1 << 31, [7])]
+LN_MEAN_TERMS = [(1, [0, 1, 1])]
+LN_OUT_TERMS = [(1, [0, 1]), (1, [2]), (NEG, [3])]
+SOFTMAX_SUM_TERMS = [(1, [0, 1])]
+SOFTMAX_RESCALE_TERMS = [(1, [0, 2]), (NEG * (1 << 16) % P, [1]), (1, [3])]
+PRODUCT_TERMS = [(1, [0, 1])]
+
+
+def _cat_u64(parts) -> torch.Tensor:
+    parts = [p.reshape(-1) for p in parts]
+    if len(parts) == 1:
+        return parts[0]
+    return torch.cat([p.view(torch.int64) for p in parts]).view(torch.uint64)
+
+
+class _Pending:
+    """Device outputs of one proof in flight: every buffer a prover writes is
+    registered here and fetched in one concatenated copy; ``host(h)`` then
+    returns buffer h as a numpy array."""
+
+    def __init__(self):
+        self.parts = []
+        self.arrays = None
+
+    def out(self, n: int):
+        t = empty(max(int(n), 1))
+        self.parts.append(t)
+        return len(self.parts) - 1, t
+
+    def fetch(self):
+        if self.parts:
+            flat = _cat_u64(self.parts).cpu().numpy()
+            sizes = np.cumsum([p.numel() for p in self.parts])[:-1]
+            self.arrays = np.split(flat, sizes)
+        else:
+            self.arrays = []
+
+    def host(self, h):
+        return self.arrays[h]
+
+    def value(self, ref):
+        """An int, or (buffer, index) into a fetched buffer."""
+        if isinstance(ref, tuple):
+            return int(self.arrays[ref[0]][ref[1]])
+        return int(ref)
+
+
+class OpShardProver:
+    """prove_shard_precomputed over a device Store (the witness already
+    materialised), with ``rng`` the shard's challenge source."""
+
+    def __init__(self, store: Store, rng):
+        self.store, self.rng = store, rng
+        self.pend = _Pending()
+        self.err = _err_word()
+        self.sh = stream_handle()
+        self.claims = []      # (tensor, point, value ref)
+        self.builders = []    # one per op: () -> proof object
+        self.lookups = {}     # table -> [(idx tensor, value tensor)]
+
+    # -- primitives ------------------------------------------------------------------------
+    def draw(self, n: int) -> np.ndarray:
+        return np.array([self.rng.field() for _ in range(n)], dtype=np.uint64)
+
+    def eval(self, values: torch.Tensor, point: np.ndarray):
+        t = point.size
+        h, d = self.pend.out(1)
+        scr = empty(max(lib.zkie2_mle_scratch_elems(t), 1))
+        check(lib.zkie2_mle_eval_async(ptr(values), t, _pp(point), ptr(d), ptr(scr), self.sh),
+              "zkie2_mle_eval_async")
+        return (h, 0)
+
+    def claim(self, t: int, point: np.ndarray, value=None):
+        point = np.ascontiguousarray(point, dtype=np.uint64)
+        self.claims.append((t, point, value if value is not None else self.eval(self.store.get(t), point)))
+
+    def virtual(self, mles, terms, ch: np.ndarray):
+        """prove_virtual enqueued -> a builder of the VirtualProof."""
+        n, t = len(mles), ch.size
+        coeffs, off, idx, deg = _terms_arrays(terms)
+        hr, dr = self.pend.out(t * (deg + 1))
+        hf, df = self.pend.out(n)
+        scr = empty(max(lib.zkie2_virtual_scratch_elems(n, t), 1))
+        arr = (_lib.vp * n)(*[ptr(m) for m in mles])
+        check(lib.zkie2_virtual_prove_async(arr, n, t, _pp(coeffs), off.ctypes.data_as(_lib.pu32),
+                                            idx.ctypes.data_as(_lib.pu32), len(terms), _pp(ch), ptr(dr), ptr(df),
+                                            ptr(scr), self.sh), "zkie2_virtual_prove_async")
+        pend = self.pend
+        return lambda: VirtualProof(pend.host(hr)[:t * (deg + 1)].reshape(t, deg + 1).copy(),
+                                    pend.host(hf)[:n].copy())
+
+    def fractional(self, num: torch.Tensor, den: torch.Tensor):
+        """prove_fractional (logup_gkr.rs:71-81): full_r then cs drawn."""
+        lg = _lg(num.numel())
+        full_r, cs = self.draw(lg), self.draw(lg)
+        h, d = self.pend.out(lib.zkie2_fractional_proof_elems(lg))
+        scr = empty(max(lib.zkie2_fractional_scratch_elems(lg), 2))
+        check(lib.zkie2_fractional_prove_async(ptr(num), ptr(den), lg, _pp(full_r), _pp(cs), ptr(d), ptr(scr),
+                                               self.sh), "zkie2_fractional_prove_async")
+        pend = self.pend
+
+        def build():
+            a = pend.host(h)
+            nr = 2 * lg * (lg - 1)
+            layers, off = [], 0
+            for l in range(lg):
+                t = lg - l - 1
+                layers.append(FractionalLayer(full_r[:t].copy(), int(cs[l]) % P,
+                                              VirtualProof(a[off:off + 4 * t].reshape(t, 4).copy(),
+                                                           a[nr + 7 * l:nr + 7 * l + 7].copy())))
+                off += 4 * t
+            return FractionalProof(layers, int(a[nr + 7 * lg]), int(a[nr + 7 * lg + 1]), full_r.copy())
+        return build
+
+    def ones(self, n: int) -> torch.Tensor:
+        o = empty(n)
+        check(lib.zkie2_op_fill(ptr(o), n, 1, self.sh), "zkie2_op_fill")
+        return o
+
+    def broadcast(self, v: torch.Tensor, m: int, n: int) -> torch.Tensor:
+        out = empty(m * n)
+        check(lib.zkie2_op_row_broadcast(ptr(v), m, n, ptr(out), self.sh), "zkie2_op_row_broadcast")
+        return out
+
+    def eq_table(self, r: np.ndarray) -> torch.Tensor:
+        out = empty(1 << r.size)
+        check(lib.zkie2_eq_evals(_pp(r), r.size, ptr(out), self.sh), "zkie2_eq_evals")
+        return out
+
+    # -- the arms --------------------------------------------------------------------------------
+    def op_matmul(self, op: MatMul):
+        g = self.store.get
+        lm, lk, ln = _lg(op.m), _lg(op.k), _lg(op.n)
+        u, v, ch = self.draw(lm), self.draw(ln), self.draw(lk)
+        h, d = self.pend.out(3 + 3 * lk)
+        scr = empty(max(lib.zkie2_op_matmul_scratch_elems(op.m, op.k, op.n), 1))
+        check(lib.zkie2_op_matmul_prove_async(ptr(g(op.a)), ptr(g(op.b)), ptr(g(op.c)), op.m, op.k, op.n, _pp(u),
+                                              _pp(v), _pp(ch), ptr(d), ptr(scr), self.sh),
+              "zkie2_op_matmul_prove_async")
+        refs = []
+        for t, pt in ((op.a, np.concatenate([ch, u])), (op.b, np.concatenate([v, ch])),
+                      (op.c, np.concatenate([v, u]))):
+            self.claim(t, pt)
+            refs.append(self.claims[-1][2])
+        pend = self.pend
+
+        def build():
+            a = pend.host(h)
+            mm = MatmulProof(int(a[0]), SumcheckProof(a[1:1 + 3 * lk].reshape(lk, 3).copy(), int(a[1 + 3 * lk]),
+                                                      int(a[2 + 3 * lk])))
+            return OpMatMulProof(mm, u, v, ch, np.array([pend.value(r) for r in refs], dtype=np.uint64))
+        return build
+
+    def op_projection(self, op: Projection):
+        g = self.store.get
+        m, k, n, shift = op.m, op.k, op.n, op.shift
+        lm, lk, ln = _lg(m), _lg(k), _lg(n)
+        lg = lib.zkie2_projection_lookup_vars(m, n, shift)
+        u, v, ch = self.draw(lm), self.draw(ln), self.draw(lk)
+        alpha, beta = self.rng.field(), self.rng.field()
+        full_r, cs = self.draw(lg), self.draw(lg)
+        hbuf = self.store.proj_h.get(op.out)
+        h, d = self.pend.out(lib.zkie2_projection_proof_elems(m, k, n, shift))
+        scr = empty(max(lib.zkie2_projection_scratch_elems(m, k, n, shift), 1))
+        check(lib.zkie2_projection_prove_async(ptr(g(op.x)), ptr(g(op.w)), ptr(g(op.bias)), ptr(g(op.out)),
+                                               ptr(g(op.rem)), ptr(hbuf) if hbuf is not None else None, m, k, n,
+                                               shift, _pp(u), _pp(v), _pp(ch), alpha, beta, _pp(full_r), _pp(cs),
+                                               ptr(d), self.err.data_ptr(), ptr(scr), self.sh),
+              "zkie2_projection_prove_async")
+        tv = lm + ln
+        o_mm, o_aff = 1, 1 + 3 * lk + 2
+        o_fr = o_aff + 3 * tv + 6
+        nr = 2 * lg * (lg - 1)
+        pt = np.concatenate([v, u])
+        self.claim(op.x, np.concatenate([ch, u]))
+        self.claim(op.w, np.concatenate([v, ch]))
+        self.claim(op.out, pt)
+        self.claim(op.bias, pt, (h, o_aff + 3 * tv + 4))
+        pend = self.pend
+
+        def build():
+            a = pend.host(h)
+            mm = MatmulProof(int(a[0]), SumcheckProof(a[o_mm:o_mm + 3 * lk].reshape(lk, 3).copy(),
+                                                      int(a[o_mm + 3 * lk]), int(a[o_mm + 3 * lk + 1])))
+            aff = VirtualProof(a[o_aff:o_aff + 3 * tv].reshape(tv, 3).copy(), a[o_aff + 3 * tv:o_aff + 3 * tv + 6].copy())
+            layers, off = [], 0
+            for l in range(lg):
+                t = lg - l - 1
+                layers.append(FractionalLayer(full_r[:t].copy(), int(cs[l]) % P,
+                                              VirtualProof(a[o_fr + off:o_fr + off + 4 * t].reshape(t, 4).copy(),
+                                                           a[o_fr + nr + 7 * l:o_fr + nr + 7 * l + 7].copy())))
+                off += 4 * t
+            base = o_fr + nr + 7 * lg
+            frac = FractionalProof(layers, int(a[base]), int(a[base + 1]), full_r.copy())
+            return ProjectionProof(mm, aff, frac, int(alpha), int(beta), pt, u, v, ch)
+        return build
+
+    def op_add(self, op: Add):
+        g = self.store.get
+        c = g(op.c)
+        r = self.draw(_lg(c.numel()))
+        vb = self.virtual([g(op.a), g(op.b), c], ADD_TERMS, r)
+        for t in (op.a, op.b, op.c):
+            self.claim(t, r)
+        return lambda: AddProof(vb(), r)
+
+    def _lookup(self, table: int, idx: torch.Tensor, vals: torch.Tensor):
+        self.lookups.setdefault(table, []).append((idx, vals))
+
+    def op_softmax(self, op: Softmax):
+        g = self.store.get
+        m, n = op.m, op.n
+        e, out = g(op.e), g(op.out)
+        s = empty(m)
+        check(lib.zkie2_op_row_sums(ptr(e), m, n, n, ptr(s), self.sh), "zkie2_op_row_sums")
+        r_sum = self.draw(_lg(m))
+        eq_b = self.broadcast(self.eq_table(r_sum), m, n)
+        sum_ch = self.draw(_lg(m * n))
+        claimed = self.eval(s, r_sum)
+        row_sum = self.virtual([eq_b, e], SOFTMAX_SUM_TERMS, sum_ch)
+        sum_b, rem = empty(m * n), empty(m * n)
+        check(lib.zkie2_op_softmax_rem(ptr(e), ptr(out), ptr(s), m, n, ptr(sum_b), ptr(rem), self.sh),
+              "zkie2_op_softmax_rem")
+        r_scale = self.draw(_lg(m * n))
+        rescale = self.virtual([out, e, sum_b, rem], SOFTMAX_RESCALE_TERMS, r_scale)
+        self.claim(op.out, r_scale)
+        self._lookup(op.table, self.store.get_idx(op.idx), e)
+        pend = self.pend
+        return lambda: SoftmaxRoundedProof(row_sum(), rescale(), r_sum, sum_ch, r_scale, pend.value(claimed))
+
+    def op_layernorm(self, op: Layernorm):
+        g = self.store.get
+        m, d = op.m, op.d
+        x, w, b = g(op.x), g(op.w), g(op.b)
+        cols = layernorm_columns(x, w, b, g(op.rsqrt_table), m, d)
+        r_mean = self.draw(_lg(m))
+        eq_b = self.broadcast(self.eq_table(r_mean), m, d)
+        mean_claim = self.eval(cols["mean_sq"], r_mean)
+        mean_ch = self.draw(_lg(m * d))
+        mean_sq = self.virtual([eq_b, x], LN_MEAN_TERMS, mean_ch)
+        r_out = self.draw(_lg(m * d))
+        out = self.virtual([x, cols["scale"], b, cols["out"]], LN_OUT_TERMS, r_out)
+        self._lookup(op.rsqrt_table, cols["idx"], cols["rsqrt"])
+        for t in (op.out, op.w, op.b):
+            self.claim(t, r_out)
+        pend = self.pend
+        return lambda: LayernormChainProof(mean_sq(), out(), r_mean, mean_ch, r_out, pend.value(mean_claim))
+
+    def op_layer_norm_centered(self, op: LayerNormCentered):
+        g = self.store.get
+        m, d, nr = op.m, op.d, op.n_real
+        x, w, b = g(op.x), g(op.w), g(op.b)
+        f = layer_norm_centered_columns(x, w, b, g(op.rsqrt_table), m, d, nr, self.err)
+        lm, lmd = _lg(m), _lg(m * d)
+        ones_m = self.ones(m)
+        trunc = TRUNC_TERMS(nr, nr // 2)
+        r_mean = self.draw(lm)
+        self.draw(lmd)  # mean_ch of the discarded mean reduction (:153-159)
+        m_ch = self.draw(lm)
+        mean = self.virtual([f["mean"], f["rem_mean"], f["sum_mean"], ones_m], trunc, m_ch)
+        centered_r = self.draw(lmd)
+        centered = self.virtual([x, self.broadcast(f["mean"], m, d), f["centered"]], CENTERED_TERMS, centered_r)
+        r_var = self.draw(lm)
+        self.draw(lmd)  # var_ch of the discarded variance reduction (:193-201)
+        v_ch = self.draw(lm)
+        var = self.virtual([f["var"], f["rem_var"], f["sum_var"], ones_m], trunc, v_ch)
+        r_out = self.draw(lmd)
+        out = self.virtual([f["centered"], self.broadcast(f["rstd"], m, d), w, b, f["raw"], f["out"], f["rem_out"],
+                            self.ones(m * d)], LNC_OUT_TERMS, r_out)
+        self._lookup(op.rsqrt_table, f["s_index"], f["rstd"])
+        self.claim(op.x, centered_r)
+        for t in (op.out, op.w, op.b):
+            self.claim(t, r_out)
+        return lambda: LayerNormCenteredProof(mean(), centered(), var(), out(), r_mean, m_ch, centered_r, r_var,
+                                              v_ch, r_out)
+
+    def same_poly(self, f: torch.Tensor, claims):
+        """prove_same_poly: coefficients then the merged point drawn; the
+        reference's virtual polynomial over [f, eq_1 .. eq_c] proved as f E."""
+        t = _lg(f.numel())
+        coeffs = self.draw(len(claims))
+        merged = self.draw(t)
+        pts = np.ascontiguousarray(np.concatenate([np.asarray(pt, dtype=np.uint64) for pt, _ in claims]))
+        E = empty(1 << t)
+        scr = empty(max(lib.zkie2_eq_combine_scratch_elems(len(claims), t), 1))
+        check(lib.zkie2_eq_combine(_pp(pts), _pp(coeffs), len(claims), t, ptr(E), ptr(scr), self.sh),
+              "zkie2_eq_combine")
+        vb = self.virtual([f, E], PRODUCT_TERMS, merged)
+        eq_finals = [_eq_at(pt, merged) for pt, _ in claims]
+
+        def build():
+            vp = vb()
+            finals = np.array([int(vp.final_evals[0])] + eq_finals, dtype=np.uint64)
+            return SamePolyProof(coeffs, VirtualProof(vp.rounds, finals), merged, int(vp.final_evals[0]))
+        return build
+
+    def lookup_table(self, table: int):
+        """The per-table logUp of prove_shard_precomputed (:2050-2080)."""
+        g = self.store.get
+        alpha, beta = self.rng.field(), self.rng.field()
+        pairs = self.lookups[table]
+        x = torch.cat([i.reshape(-1).view(torch.int32) for i, _ in pairs]).view(torch.uint32)
+        y = _cat_u64([v.reshape(-1) for _, v in pairs])
+        n = x.numel()
+        total = lib.zkie2_lookup_len(n, 0, 2)
+        num, den = empty(total), empty(total)
+        check(lib.zkie2_lookup_num_den_async(x.data_ptr(), ptr(y), n, None, None, 0, 2, alpha, beta, ptr(num),
+                                             ptr(den), None, self.err.data_ptr(), self.sh),
+              "zkie2_lookup_num_den_async")
+        x_flat = torch.zeros(total, dtype=torch.uint64, device=num.device)
+        y_flat = torch.zeros(total, dtype=torch.uint64, device=num.device)
+        x_flat[:n] = (x.view(torch.int32).to(torch.int64) & 0xFFFFFFFF).view(torch.uint64)
+        y_flat[:n] = y
+        wproof = self.fractional(num, den)
+        tab = g(table)
+        t = tab.numel()
+        mult = empty(max(t, 1))
+        for j, (i, _) in enumerate(pairs):
+            check(lib.zkie2_lookup_multiplicity(i.data_ptr(), i.numel(), t, ptr(mult), 1 if j else 0,
+                                                self.err.data_ptr(), self.sh), "zkie2_lookup_multiplicity")
+        ttotal = lib.zkie2_lookup_len(0, t, 3)
+        tnum, tden = empty(ttotal), empty(ttotal)
+        check(lib.zkie2_lookup_num_den_async(None, None, 0, ptr(tab), ptr(mult), t, 3, alpha, beta, ptr(tnum),
+                                             ptr(tden), None, self.err.data_ptr(), self.sh),
+              "zkie2_lookup_num_den_async")
+        tproof = self.fractional(tnum, tden)
+
+        def leaf(p: FractionalProof):
+            top = int(p.full_r[-1]) % P
+            fe = [int(v) for v in p.layers[0].proof.final_evals]
+            return p.full_r.copy(), ((1 - top) * fe[3] + top * fe[4]) % P, ((1 - top) * fe[5] + top * fe[6]) % P
+
+        def build():
+            wp, tp = wproof(), tproof()
+            pt, nl, dl = leaf(wp)
+            tpt, tnl, tdl = leaf(tp)
+            return (WitnessColumn(wp, x_flat, y_flat, num, pt, nl, dl, int(alpha), int(beta), table),
+                    TableColumn(tp, table, mult[:t], int(alpha), int(beta), tpt, tnl, tdl))
+        return build
+
+    # -- the shard ----------------------------------------------------------------------------
+    def prove(self, ops, boundary=()) -> OpShardProof:
+        arms = {"MatMul": self.op_matmul, "Projection": self.op_projection, "Add": self.op_add,
+                "Softmax": self.op_softmax, "Layernorm": self.op_layernorm,
+                "LayerNormCentered": self.op_layer_norm_centered}
+        for op in ops:
+            k = op.kind
+            if k in arms:
+                self.builders.append(arms[k](op))
+            elif k == "Lookup":
+                self._lookup(op.table, self.store.get_idx(op.idx), self.store.get(op.out))
+                self.builders.append(lambda k=k: MarkerProof(k))
+            elif k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex"):
+                self.builders.append(lambda k=k: MarkerProof(k))
+            else:
+                raise ValueError(f"op {k} is not supported")
+        by_tensor = {}
+        for t, pt, ref in self.claims:
+            by_tensor.setdefault(t, []).append((pt, ref))
+        bset = set(boundary)
+        bound, bind_builders = [], []
+        for t in sorted(by_tensor):
+            cs = by_tensor[t]
+            if t in bset or len(cs) < 2:
+                continue
+            bind_builders.append(self.same_poly(self.store.get(t), cs))
+            bound.append(t)
+        table_builders = [self.lookup_table(t) for t in sorted(self.lookups)]
+        # one copy back for everything
+        self.pend.parts.append(self.err.to(torch.int64).view(torch.uint64))
+        self.pend.fetch()
+        code = int(self.pend.arrays[-1][0])
+        if code:
+            raise ValueError("prove_shard: " + ", ".join(v for k, v in _ERRORS.items() if code & k))
+        op_proofs = [b() for b in self.builders]
+        binds = [b() for b in bind_builders]
+        claims = [(t, pt, self.pend.value(ref)) for t, pt, ref in self.claims]
+        cols = [b() for b in table_builders]
+        return OpShardProof(op_proofs, bound, binds, claims, [w for w, _ in cols], [tc for _, tc in cols])
+
+
+def prove_shard_precomputed(store: Store, ops, boundary, rng) -> OpShardProof:
+    """compose.rs:1602-2091 (the witness already in ``store``)."""
+    return OpShardProver(store, rng).prove(ops, boundary)
+
+
+def prove_shard(store: Store, ops, boundary, rng) -> OpShardProof:
+    """compose.rs:1589-1597: forward, then prove."""
+    forward_ops(store, ops)
+    return prove_shard_precomputed(store, ops, boundary, rng)
+
+
+def shard_ranges(op_count: int, ops_per_shard: int):
+    """compose.rs:2264-2274."""
+    ops_per_shard = max(ops_per_shard, 1)
+    return [(s, min(s + ops_per_shard, op_count)) for s in range(0, op_count, ops_per_shard)]
+
+
+def master_transcript(ops, ops_per_shard: int) -> Transcript:
+    """Transcript::new("zkie-shard-dag-v1") + absorb_statement (compose.rs:2276-2287)."""
+    t = Transcript(b"zkie-shard-dag-v1")
+    t.absorb_u64(ops_per_shard)
+    t.absorb_u64(len(ops))
+    for op in ops:
+        for i in op.reads():
+            t.absorb_u64(i)
+        for i in op.writes():
+            t.absorb_u64(i)
+    return t
+
+
+def prove_shard_dag(store: Store, ops, ops_per_shard: int) -> ShardDagProof:
+    """compose.rs:2289-2346: forward once, each shard proven with its child
+    transcript (master + the shard index), then the tensors claimed by more
+    than one shard bound with the master transcript."""
+    forward_ops(store, ops)
+    master = master_transcript(ops, ops_per_shard)
+    shards = []
+    for si, (s, e) in enumerate(shard_ranges(len(ops), ops_per_shard)):
+        child = master.clone()
+        child.absorb_u64(si)
+        shards.append(prove_shard_precomputed(store, ops[s:e], [], child))
+    by_tensor, owners = {}, {}
+    for si, sh in enumerate(shards):
+        for t, pt, ev in sh.claims:
+            by_tensor.setdefault(t, []).append((pt, ev))
+            owners.setdefault(t, set()).add(si)
+    cross = [t for t in sorted(by_tensor) if len(owners[t]) > 1]
+    prover = OpShardProver(store, master)
+    builders = [prover.same_poly(store.get(t), by_tensor[t]) for t in cross]
+    prover.pend.fetch()
+    return ShardDagProof(shards, cross, [b() for b in builders])

@@ -336,23 +336,24 @@ uint64_t zkie2_lookup_len(uint64_t n, uint64_t t, uint32_t mode) { return lookup
 
 uint64_t zkie2_lookup_scratch_elems(uint64_t t) { return t / 2 + 2; }
 
-int zkie2_lookup_num_den(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, const uint64_t* d_table,
-                         const uint64_t* d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
-                         uint64_t* d_num, uint64_t* d_den, uint64_t* d_scratch, cudaStream_t stream) {
+// Lookup columns enqueued without synchronization; an index at or past t
+// (mode 0) sets bit 1 of *d_bad.
+static int lookup_enqueue(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, const uint64_t* d_table,
+                          const uint64_t* d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                          uint64_t* d_num, uint64_t* d_den, uint64_t* d_scratch, uint32_t* d_bad,
+                          cudaStream_t stream) {
     if (mode > kLookupTable || !d_num || !d_den) return (int)cudaErrorInvalidValue;
     if (mode != kLookupTable && n && (!d_x || !d_y)) return (int)cudaErrorInvalidValue;
     if ((mode == kLookupMerged || mode == kLookupTable) && t && !d_table) return (int)cudaErrorInvalidValue;
     if (mode == kLookupTable && t && !d_m) return (int)cudaErrorInvalidValue;
-    if (mode == kLookupMerged && (!d_scratch || n > 0xFFFFFFFFull)) return (int)cudaErrorInvalidValue;
+    if (mode == kLookupMerged && (!d_scratch || !d_bad || n > 0xFFFFFFFFull)) return (int)cudaErrorInvalidValue;
     const uint64_t total = lookup_len(n, t, mode);
     uint32_t* m32 = nullptr;
-    uint32_t* bad = nullptr;
     if (mode == kLookupMerged) {
         m32 = reinterpret_cast<uint32_t*>(d_scratch);
-        bad = m32 + 2 * (t / 2 + 1);
-        ZK_TRY(cudaMemsetAsync(d_scratch, 0, 8 * zkie2_lookup_scratch_elems(t), stream));
+        ZK_TRY(cudaMemsetAsync(m32, 0, 4 * t, stream));
         if (n) {
-            k_lookup_hist<<<frac_grid(n), kFracThreads, 0, stream>>>(d_x, n, t, m32, bad);
+            k_lookup_hist<<<frac_grid(n), kFracThreads, 0, stream>>>(d_x, n, t, m32, d_bad);
             ZK_LAUNCH_CHECK();
         }
     }
@@ -360,12 +361,53 @@ int zkie2_lookup_num_den(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, c
                                                                    gl_canon(alpha), gl_canon(beta), total, d_num,
                                                                    d_den);
     ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_lookup_num_den(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, const uint64_t* d_table,
+                         const uint64_t* d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                         uint64_t* d_num, uint64_t* d_den, uint64_t* d_scratch, cudaStream_t stream) {
+    uint32_t* bad = nullptr;
+    if (mode == kLookupMerged) {
+        if (!d_scratch) return (int)cudaErrorInvalidValue;
+        bad = reinterpret_cast<uint32_t*>(d_scratch) + 2 * (t / 2 + 1);
+        ZK_TRY(cudaMemsetAsync(bad, 0, 4, stream));
+    }
+    int rc = lookup_enqueue(d_x, d_y, n, d_table, d_m, t, mode, alpha, beta, d_num, d_den, d_scratch, bad, stream);
+    if (rc) return rc;
     if (mode == kLookupMerged) {
         uint32_t h_bad = 0;
         ZK_TRY(cudaMemcpyAsync(&h_bad, bad, 4, cudaMemcpyDeviceToHost, stream));
         ZK_TRY(cudaStreamSynchronize(stream));
         if (h_bad) return (int)cudaErrorInvalidValue;
     }
+    return 0;
+}
+
+int zkie2_lookup_num_den_async(const uint32_t* d_x, const uint64_t* d_y, uint64_t n, const uint64_t* d_table,
+                               const uint64_t* d_m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
+                               uint64_t* d_num, uint64_t* d_den, uint64_t* d_scratch, uint32_t* d_err,
+                               cudaStream_t stream) {
+    if (mode == kLookupMerged && !d_err) return (int)cudaErrorInvalidValue;
+    return lookup_enqueue(d_x, d_y, n, d_table, d_m, t, mode, alpha, beta, d_num, d_den, d_scratch, d_err, stream);
+}
+
+uint64_t zkie2_fractional_proof_elems(uint32_t lg_n) {
+    if (lg_n > kMaxLg) return 0;
+    return 2ull * lg_n * (lg_n ? lg_n - 1 : 0) + 7ull * lg_n + 2;
+}
+
+int zkie2_fractional_prove_async(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n,
+                                 const uint64_t* h_full_r, const uint64_t* h_cs, uint64_t* d_proof,
+                                 uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_proof) return (int)cudaErrorInvalidValue;
+    uint64_t *d_rounds = nullptr, *d_finals = nullptr, *d_nd = nullptr, roff = 0;
+    int rc = fractional_enqueue(d_num, d_den, lg_n, h_full_r, h_cs, d_scratch, stream, &d_rounds, &d_finals, &d_nd,
+                                &roff);
+    if (rc) return rc;
+    if (roff) ZK_TRY(cudaMemcpyAsync(d_proof, d_rounds, 8 * roff, cudaMemcpyDeviceToDevice, stream));
+    if (lg_n) ZK_TRY(cudaMemcpyAsync(d_proof + roff, d_finals, 56ull * lg_n, cudaMemcpyDeviceToDevice, stream));
+    ZK_TRY(cudaMemcpyAsync(d_proof + roff + 7ull * lg_n, d_nd, 16, cudaMemcpyDeviceToDevice, stream));
     return 0;
 }
 

@@ -153,6 +153,12 @@ int zkie2_mle_eval(const uint64_t* d_values, uint32_t t, const uint64_t* h_point
     return 0;
 }
 
+int zkie2_mle_eval_async(const uint64_t* d_values, uint32_t t, const uint64_t* h_point, uint64_t* d_out,
+                         uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_values || !d_out || !d_scratch || (t && !h_point)) return (int)cudaErrorInvalidValue;
+    return eval_dev(d_values, t, h_point, d_out, d_scratch, stream);
+}
+
 uint64_t zkie2_sumcheck_scratch_elems(uint32_t t) { return sumcheck_scratch_elems(t) + 3ull * t + 4; }
 
 int zkie2_sumcheck_prove(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uint64_t* h_ch,
@@ -260,6 +266,22 @@ int zkie2_sum_of_products_prove(const uint64_t* d_weights, const uint64_t* d_val
     if (t) ZK_TRY(cudaMemcpyAsync(h_rounds, d_out, 24ull * t, cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaMemcpyAsync(h_b_eval, d_out + 3ull * t, 8, cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaStreamSynchronize(stream));
+    return 0;
+}
+
+// The Op::MatMul proof with the caller's u, v, ch, no synchronization:
+// claimed | rounds (3 log2 k) | finals (2) into d_proof on the device.
+int zkie2_op_matmul_prove_async(const uint64_t* d_a, const uint64_t* d_b, const uint64_t* d_c, uint64_t m,
+                                uint64_t k, uint64_t n, const uint64_t* h_u, const uint64_t* h_v,
+                                const uint64_t* h_ch, uint64_t* d_proof, uint64_t* d_scratch, cudaStream_t stream) {
+    if (!d_a || !d_b || !d_c || !d_proof || !d_scratch || !pow2(m) || !pow2(k) || !pow2(n))
+        return (int)cudaErrorInvalidValue;
+    const uint32_t lm = log2_exact(m), lk = log2_exact(k), ln = log2_exact(n);
+    if ((lm && !h_u) || (ln && !h_v) || (lk && !h_ch)) return (int)cudaErrorInvalidValue;
+    uint64_t* d_mm = nullptr;
+    int rc = op_matmul_enqueue(d_a, d_b, d_c, m, k, n, h_u, h_v, h_ch, d_scratch, &d_mm, stream);
+    if (rc) return rc;
+    ZK_TRY(cudaMemcpyAsync(d_proof, d_mm, 8ull * (3 + 3ull * lk), cudaMemcpyDeviceToDevice, stream));
     return 0;
 }
 

@@ -199,4 +199,20 @@ void zkie2_shard_dag_child(const uint64_t* op_ids, uint32_t n_ops, uint64_t ops_
     zkie2_transcript_absorb_u64(t, shard_index);
 }
 
+// n draws of XorShift64::next_u64 (common/field.rs:17-36) from *state (advanced
+// in place), each mapped to from_i64((draw % mod) + offset): the fixed-point
+// weight draws of the reference's random model builders (e.g. compose.rs
+// build_gpt2_layer, `from_i64((rng.next_u64() % 50) as i64)`).
+void zkie2_xorshift_fill(uint64_t* state, uint64_t n, uint64_t mod, int64_t offset, uint64_t* out) {
+    uint64_t x = *state;
+    for (uint64_t i = 0; i < n; i++) {
+        x ^= x << 13;
+        x ^= x >> 7;
+        x ^= x << 17;
+        const int64_t v = (int64_t)(x % mod) + offset;
+        out[i] = v >= 0 ? (uint64_t)v : kP - (0ull - (uint64_t)v);
+    }
+    *state = x;
+}
+
 }  // extern "C"

@@ -556,4 +556,13 @@ int zkie2_virtual_prove(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t
     return 0;
 }
 
+// prove_virtual with device outputs and no synchronization: rounds (t x
+// (d + 1), d the largest term) into d_rounds, the n_mles finals into d_finals.
+int zkie2_virtual_prove_async(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
+                              const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
+                              uint64_t* d_rounds, uint64_t* d_finals, uint64_t* d_scratch, cudaStream_t stream) {
+    return virtual_enqueue(d_mles, n_mles, t, coeffs, idx_off, idx, n_terms, h_ch, d_rounds, d_finals, nullptr,
+                           d_scratch, stream);
+}
+
 }  // extern "C"

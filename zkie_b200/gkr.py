@@ -43,6 +43,12 @@ class Transcript:
         self.t = _lib.Transcript()
         lib.zkie2_transcript_new(C.byref(self.t), domain, len(domain))
 
+    def clone(self) -> "Transcript":
+        c = Transcript.__new__(Transcript)
+        c.t = _lib.Transcript()
+        C.memmove(C.byref(c.t), C.byref(self.t), C.sizeof(_lib.Transcript))
+        return c
+
     def absorb(self, data: bytes):
         lib.zkie2_transcript_absorb(C.byref(self.t), data, len(data))
 
