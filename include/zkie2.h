@@ -163,6 +163,9 @@ void zkie2_challenger_xorshift(zkie2_challenger *c, uint64_t seed);
  * model builders.  mod > 0. */
 void zkie2_xorshift_fill(uint64_t *state, uint64_t n, uint64_t mod, int64_t offset, uint64_t *out);
 uint64_t zkie2_challenger_field(zkie2_challenger *c);
+/* n successive draws of zkie2_challenger_field / zkie2_transcript_field into out. */
+void zkie2_challenger_fields(zkie2_challenger *c, uint64_t n, uint64_t *out);
+void zkie2_transcript_fields(zkie2_transcript *t, uint64_t n, uint64_t *out);
 /* Child transcript of shard `shard_index` in prove_shard_dag
  * (zkie-ops/src/compose.rs:2276-2311) for a statement of MatMul ops given as
  * (a, b, c) tensor-id triples. */
@@ -183,6 +186,12 @@ int zkie2_mle_eval(const uint64_t *d_values, uint32_t t, const uint64_t *h_point
 /* The same with the value left in *d_out on the device (no synchronization). */
 int zkie2_mle_eval_async(const uint64_t *d_values, uint32_t t, const uint64_t *h_point, uint64_t *d_out,
                          uint64_t *d_scratch, zkie_stream_t stream);
+/* count evaluations in one call: table i (2^ts[i] values at d_values[i]) at
+ * the next ts[i] values of h_points, into d_out[i]; d_scratch holds
+ * zkie2_mle_eval_many_scratch_elems(max ts[i]) u64.  No synchronization. */
+uint64_t zkie2_mle_eval_many_scratch_elems(uint32_t max_t);
+int zkie2_mle_eval_many(const uint64_t *const *d_values, const uint32_t *ts, const uint64_t *h_points,
+                        uint32_t count, uint64_t *d_out, uint64_t *d_scratch, zkie_stream_t stream);
 /* sumcheck::prove (common/sumcheck.rs:33-79) over f, h of length 2^t with the
  * t challenges h_ch: h_rounds gets (c0, c1, c2) per round, h_finals (f, h)
  * after the last fold.  Synchronous. */
@@ -471,7 +480,9 @@ int zkie2_op_fill(uint64_t *d_out, uint64_t n, uint64_t value, zkie_stream_t str
 /* prove_same_poly (common/same_poly.rs:13-45) as one degree-2 virtual
  * polynomial: every term of the reference's is c_i f eq(r_i, .), so its
  * round messages are those of f E with E = sum_i c_i eq(r_i, .).  This
- * builds E (2^t values) from c points r_i (h_points, c x t) and coefficients. */
+ * builds E (2^t values) from c points r_i (h_points, c x t, t <= 40) and
+ * coefficients; the points travel as kernel parameters (no host copy, so the
+ * call can be recorded in a CUDA graph). */
 uint64_t zkie2_eq_combine_scratch_elems(uint32_t c, uint32_t t);
 int zkie2_eq_combine(const uint64_t *h_points, const uint64_t *h_coeffs, uint32_t c, uint32_t t, uint64_t *d_out,
                      uint64_t *d_scratch, zkie_stream_t stream);

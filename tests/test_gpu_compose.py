@@ -122,3 +122,40 @@ def test_lookup_outside_table_is_an_error(zk):
     with pytest.raises(ValueError, match="outside its table"):
         C.forward_ops(st, ops)
     torch.cuda.synchronize()
+
+
+def test_graph_prover_replays_for_a_new_witness(zk):
+    """GraphShardProver: the recorded prove equals the eager one, and after
+    new input values go into the same buffers (forward in place), a replay
+    proves the new witness exactly as the CPU restatement does."""
+    from zkie_b200 import gpt2
+    C = zk.compose
+    shape = gpt2.LayerShape(m=16, d=32, d_real=24, heads=3, dh=8, ffn=64, ffn_real=48, exp_bits=9, gelu_bits=11,
+                            rsqrt_len=512)
+    host = co.HostStore()
+    ops, x, out = gpt2.gpt2_layer(host, shape)
+    dev = _device_store(zk, host)
+    C.forward_ops(dev, ops)
+    master = C.master_transcript(ops, len(ops))
+
+    def make_rng():
+        c = master.clone()
+        c.absorb_u64(0)
+        return c
+    gp = C.GraphShardProver(dev, ops, [], make_rng)
+    eager = C.prove_shard_precomputed(dev, ops, [], make_rng()).canonical()
+    assert_same(gp.prove().canonical(), eager)
+    # a new layer input in the same buffer
+    g = np.random.default_rng(5)
+    new_x = np.zeros((shape.m, shape.d), dtype=np.uint64)
+    new_x[:, :shape.d_real] = g.integers(0, 50, size=(shape.m, shape.d_real)).astype(np.uint64)
+    dev.v[x].copy_(torch.from_numpy(new_x.reshape(-1)).cuda())
+    C.forward_ops(dev, ops)
+    got = gp.prove().canonical()
+    ref = _host_copy(host)
+    ref.v[x] = new_x.reshape(-1)
+    co.forward_ops(ref, ops)
+    om = co.master_transcript(ops, len(ops))
+    child = o.OracleTranscript(raw=om.t)
+    child.absorb_u64(0)
+    assert_same(got, co.prove_shard_precomputed(ref, ops, [], child))

@@ -115,6 +115,10 @@ SIGNATURES = {
     "zkie2_lookup_num_den": (i64, [vp, vp, u64, vp, vp, u64, u32, u64, u64, vp, vp, vp, vp]),
     "zkie2_xorshift_fill": (None, [pu64, u64, u64, s64, pu64]),
     "zkie2_mle_eval_async": (i64, [vp, u32, pu64, vp, vp, vp]),
+    "zkie2_mle_eval_many_scratch_elems": (u64, [u32]),
+    "zkie2_mle_eval_many": (i64, [C.POINTER(vp), pu32, pu64, u32, vp, vp, vp]),
+    "zkie2_challenger_fields": (None, [PCh, u64, pu64]),
+    "zkie2_transcript_fields": (None, [PTr, u64, pu64]),
     "zkie2_op_matmul_prove_async": (i64, [vp, vp, vp, u64, u64, u64, pu64, pu64, pu64, vp, vp, vp]),
     "zkie2_projection_proof_elems": (u64, [u64, u64, u64, u32]),
     "zkie2_projection_prove_async": (i64, [vp, vp, vp, vp, vp, vp, u64, u64, u64, u32, pu64, pu64, pu64, u64, u64,

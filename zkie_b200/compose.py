@@ -25,6 +25,7 @@ evaluations and the error word come back in one copy at the end.  The two
 reduction sumchecks of prove_layer_norm_centered whose proofs the reference
 discards (:153-159, :193-201) only advance the challenge source here.
 """
+import contextlib
 import ctypes as C
 from dataclasses import dataclass, field
 from typing import List, Optional
@@ -268,81 +269,93 @@ def layernorm_columns(x, w, b, table, m, d):
     return dict(mean_sq=mean_sq, idx=idx[:m], rsqrt=rsqrt, scale=scale, out=out)
 
 
-def softmax_columns(idx, table, m, n, err):
-    e, out, s = empty(m * n), empty(m * n), empty(m)
-    check(lib.zkie2_op_softmax(idx.data_ptr(), ptr(table), table.numel(), m, n, ptr(e), ptr(out), ptr(s),
-                               err.data_ptr(), stream_handle()), "zkie2_op_softmax")
-    return e, out, s
-
-
 def _matmul_fixed(a, b, m, k, n):
     from .gkr import matmul_fixed
     return matmul_fixed(a, b, m, k, n)[0]
 
 
+def _slot(store: Store, t: int, n: int) -> torch.Tensor:
+    """The output buffer of tensor t: its current buffer when it has the
+    right size (so a recorded proof graph keeps reading the same memory),
+    else a new one."""
+    v = store.v[t]
+    if v is None or v.numel() != n:
+        v = empty(n)
+        store.v[t] = v
+    return v
+
+
+def _islot(store: Store, t: int, n: int) -> torch.Tensor:
+    v = store.idx[t]
+    if v is None or v.numel() != n:
+        v = _u32(n)[:n]
+        store.idx[t] = v
+    return v
+
+
 def forward_ops(store: Store, ops):
-    """forward_ops (compose.rs:1174-1583) on the device; raises where the
-    reference panics on the data (after the whole pass, one read-back)."""
+    """forward_ops (compose.rs:1174-1583) on the device, writing every output
+    into its existing buffer where it has one; raises where the reference
+    panics on the data (after the whole pass, one read-back)."""
     err = _err_word()
     sh = stream_handle()
     for op in ops:
         k = op.kind
         g = store.get
         if k == "Transpose":
-            out = empty(op.m * op.k)
+            out = _slot(store, op.out, op.m * op.k)
             check(lib.zkie2_op_transpose(ptr(g(op.x)), op.m, op.k, ptr(out), sh), "zkie2_op_transpose")
-            store.v[op.out] = out
         elif k == "Scale":
             x = g(op.x)
-            out = empty(x.numel())
+            out = _slot(store, op.out, x.numel())
             check(lib.zkie2_op_scale(ptr(x), x.numel(), op.factor, op.shift, ptr(out), sh), "zkie2_op_scale")
-            store.v[op.out] = out
         elif k == "MatMul":
-            store.v[op.c] = _matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n)
+            _slot(store, op.c, op.m * op.n).copy_(_matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n))
         elif k == "Projection":
             h = _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n)
-            out, rem = empty(op.m * op.n), empty(op.m * op.n)
+            if op.out in store.proj_h and store.proj_h[op.out].numel() == h.numel():
+                store.proj_h[op.out].copy_(h)
+                h = store.proj_h[op.out]
+            store.proj_h[op.out] = h
+            out, rem = _slot(store, op.out, op.m * op.n), _slot(store, op.rem, op.m * op.n)
             check(lib.zkie2_projection_witness(ptr(h), ptr(g(op.bias)), op.m * op.n, op.shift, ptr(out), ptr(rem),
                                                None, sh), "zkie2_projection_witness")
-            store.v[op.out], store.v[op.rem] = out, rem
-            store.proj_h[op.out] = h
         elif k == "Add":
             a, b = g(op.a), g(op.b)
-            out = empty(a.numel())
+            out = _slot(store, op.c, a.numel())
             check(lib.zkie2_op_add(ptr(a), ptr(b), a.numel(), ptr(out), sh), "zkie2_op_add")
-            store.v[op.c] = out
         elif k == "Lookup":
             idx, table = store.get_idx(op.idx), g(op.table)
-            out = empty(idx.numel())
+            out = _slot(store, op.out, idx.numel())
             check(lib.zkie2_op_lookup(idx.data_ptr(), idx.numel(), ptr(table), table.numel(), ptr(out),
                                       err.data_ptr(), sh), "zkie2_op_lookup")
-            store.v[op.out] = out
         elif k == "Softmax":
-            e, out, _ = softmax_columns(store.get_idx(op.idx), g(op.table), op.m, op.n, err)
-            store.v[op.e], store.v[op.out] = e, out
+            idx, table = store.get_idx(op.idx), g(op.table)
+            e, out = _slot(store, op.e, op.m * op.n), _slot(store, op.out, op.m * op.n)
+            check(lib.zkie2_op_softmax(idx.data_ptr(), ptr(table), table.numel(), op.m, op.n, ptr(e), ptr(out),
+                                       None, err.data_ptr(), sh), "zkie2_op_softmax")
         elif k == "SoftmaxIndex":
             x = g(op.x)
-            idx = _u32(x.numel())
+            idx = _islot(store, op.out, x.numel())
             check(lib.zkie2_op_softmax_index(ptr(x), x.numel(), op.table_len, idx.data_ptr(), sh),
                   "zkie2_op_softmax_index")
-            store.idx[op.out] = idx[:x.numel()]
         elif k == "GeluIndex":
             x = g(op.x)
-            idx = _u32(x.numel())
+            idx = _islot(store, op.out, x.numel())
             check(lib.zkie2_op_gelu_index(ptr(x), x.numel(), op.offset, op.table_len, idx.data_ptr(), sh),
                   "zkie2_op_gelu_index")
-            store.idx[op.out] = idx[:x.numel()]
         elif k == "StableSoftmaxIndex":
-            idx = _u32(op.m * op.n)
+            idx = _islot(store, op.out, op.m * op.n)
             check(lib.zkie2_op_stable_softmax_index(ptr(g(op.x)), ptr(g(op.mask)), op.m, op.n, op.offset,
                                                     op.table_len, idx.data_ptr(), sh),
                   "zkie2_op_stable_softmax_index")
-            store.idx[op.out] = idx[:op.m * op.n]
         elif k == "Layernorm":
-            store.v[op.out] = layernorm_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d)["out"]
+            out = layernorm_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d)["out"]
+            _slot(store, op.out, out.numel()).copy_(out)
         elif k == "LayerNormCentered":
-            store.v[op.out] = layer_norm_centered_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d,
-                                                          op.n_real, err)["out"]
+            out = layer_norm_centered_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d, op.n_real,
+                                              err)["out"]
+            _slot(store, op.out, out.numel()).copy_(out)
         else:
             raise ValueError(f"op {k} is not supported")
     _check_err(err, "forward_ops")
@@ -583,20 +596,27 @@ class _Pending:
         self.parts.append(t)
         return len(self.parts) - 1, t
 
-    def fetch(self):
+    def gather(self) -> torch.Tensor:
+        """Every registered buffer in one device array (on the current stream)."""
+        return _cat_u64(self.parts) if self.parts else empty(1)
+
+    def download(self, flat: torch.Tensor):
         if self.parts:
-            flat = _cat_u64(self.parts).cpu().numpy()
+            host = flat.cpu().numpy()
             sizes = np.cumsum([p.numel() for p in self.parts])[:-1]
-            self.arrays = np.split(flat, sizes)
+            self.arrays = np.split(host, sizes)
         else:
             self.arrays = []
+
+    def fetch(self):
+        self.download(self.gather())
 
     def host(self, h):
         return self.arrays[h]
 
     def value(self, ref):
         """An int, or (buffer, index) into a fetched buffer."""
-        if isinstance(ref, tuple):
+        if isinstance(ref, (tuple, list)):
             return int(self.arrays[ref[0]][ref[1]])
         return int(ref)
 
@@ -605,26 +625,63 @@ class OpShardProver:
     """prove_shard_precomputed over a device Store (the witness already
     materialised), with ``rng`` the shard's challenge source."""
 
-    def __init__(self, store: Store, rng):
+    def __init__(self, store: Store, rng, streams: int = 8):
         self.store, self.rng = store, rng
         self.pend = _Pending()
         self.err = _err_word()
+        self.main = torch.cuda.current_stream()
+        self.streams = stream_pool(streams) if streams > 1 else [self.main]
+        self.turn = 0
         self.sh = stream_handle()
         self.claims = []      # (tensor, point, value ref)
         self.builders = []    # one per op: () -> proof object
-        self.lookups = {}     # table -> [(idx tensor, value tensor)]
+        self.lookups = {}     # table -> [(idx tensor, value tensor, event or None)]
+        self.evals = []       # evaluations waiting for flush_evals
+
+    @contextlib.contextmanager
+    def on(self, s):
+        """Enqueue on stream s (allocations included)."""
+        prev = self.sh
+        with torch.cuda.stream(s):
+            self.sh = s.cuda_stream
+            try:
+                yield
+                self.flush_evals()
+            finally:
+                self.sh = prev
+
+    def next_stream(self):
+        s = self.streams[self.turn % len(self.streams)]
+        self.turn += 1
+        return s
 
     # -- primitives ------------------------------------------------------------------------
     def draw(self, n: int) -> np.ndarray:
+        if hasattr(self.rng, "fields"):
+            return self.rng.fields(n)
         return np.array([self.rng.field() for _ in range(n)], dtype=np.uint64)
 
     def eval(self, values: torch.Tensor, point: np.ndarray):
-        t = point.size
-        h, d = self.pend.out(1)
-        scr = empty(max(lib.zkie2_mle_scratch_elems(t), 1))
-        check(lib.zkie2_mle_eval_async(ptr(values), t, _pp(point), ptr(d), ptr(scr), self.sh),
-              "zkie2_mle_eval_async")
-        return (h, 0)
+        """values(point), enqueued with the other evaluations of the current
+        arm in one call (flush_evals); returns a reference to the result."""
+        ref = [None, 0]
+        self.evals.append((values, np.ascontiguousarray(point, dtype=np.uint64), ref))
+        return ref
+
+    def flush_evals(self):
+        if not self.evals:
+            return
+        n = len(self.evals)
+        h, d = self.pend.out(n)
+        ts = np.array([pt.size for _, pt, _ in self.evals], dtype=np.uint32)
+        pts = np.ascontiguousarray(np.concatenate([pt for _, pt, _ in self.evals]))
+        vals = (_lib.vp * n)(*[ptr(v) for v, _, _ in self.evals])
+        scr = empty(max(lib.zkie2_mle_eval_many_scratch_elems(int(ts.max())), 1))
+        check(lib.zkie2_mle_eval_many(vals, ts.ctypes.data_as(_lib.pu32), _pp(pts), n, ptr(d), ptr(scr), self.sh),
+              "zkie2_mle_eval_many")
+        for i, (_, _, ref) in enumerate(self.evals):
+            ref[0], ref[1] = h, i
+        self.evals = []
 
     def claim(self, t: int, point: np.ndarray, value=None):
         point = np.ascontiguousarray(point, dtype=np.uint64)
@@ -760,8 +817,14 @@ class OpShardProver:
             self.claim(t, r)
         return lambda: AddProof(vb(), r)
 
-    def _lookup(self, table: int, idx: torch.Tensor, vals: torch.Tensor):
-        self.lookups.setdefault(table, []).append((idx, vals))
+    def _lookup(self, table: int, idx: torch.Tensor, vals: torch.Tensor, produced_here: bool = False):
+        """Register a lookup; columns computed by this prover carry an event
+        of the stream that wrote them."""
+        ev = None
+        if produced_here:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+        self.lookups.setdefault(table, []).append((idx, vals, ev))
 
     def op_softmax(self, op: Softmax):
         g = self.store.get
@@ -796,7 +859,7 @@ class OpShardProver:
         mean_sq = self.virtual([eq_b, x], LN_MEAN_TERMS, mean_ch)
         r_out = self.draw(_lg(m * d))
         out = self.virtual([x, cols["scale"], b, cols["out"]], LN_OUT_TERMS, r_out)
-        self._lookup(op.rsqrt_table, cols["idx"], cols["rsqrt"])
+        self._lookup(op.rsqrt_table, cols["idx"], cols["rsqrt"], produced_here=True)
         for t in (op.out, op.w, op.b):
             self.claim(t, r_out)
         pend = self.pend
@@ -823,7 +886,7 @@ class OpShardProver:
         r_out = self.draw(lmd)
         out = self.virtual([f["centered"], self.broadcast(f["rstd"], m, d), w, b, f["raw"], f["out"], f["rem_out"],
                             self.ones(m * d)], LNC_OUT_TERMS, r_out)
-        self._lookup(op.rsqrt_table, f["s_index"], f["rstd"])
+        self._lookup(op.rsqrt_table, f["s_index"], f["rstd"], produced_here=True)
         self.claim(op.x, centered_r)
         for t in (op.out, op.w, op.b):
             self.claim(t, r_out)
@@ -855,8 +918,11 @@ class OpShardProver:
         g = self.store.get
         alpha, beta = self.rng.field(), self.rng.field()
         pairs = self.lookups[table]
-        x = torch.cat([i.reshape(-1).view(torch.int32) for i, _ in pairs]).view(torch.uint32)
-        y = _cat_u64([v.reshape(-1) for _, v in pairs])
+        for _, _, ev in pairs:
+            if ev is not None:
+                torch.cuda.current_stream().wait_event(ev)
+        x = torch.cat([i.reshape(-1).view(torch.int32) for i, _, _ in pairs]).view(torch.uint32)
+        y = _cat_u64([v.reshape(-1) for _, v, _ in pairs])
         n = x.numel()
         total = lib.zkie2_lookup_len(n, 0, 2)
         num, den = empty(total), empty(total)
@@ -871,7 +937,7 @@ class OpShardProver:
         tab = g(table)
         t = tab.numel()
         mult = empty(max(t, 1))
-        for j, (i, _) in enumerate(pairs):
+        for j, (i, _, _) in enumerate(pairs):
             check(lib.zkie2_lookup_multiplicity(i.data_ptr(), i.numel(), t, ptr(mult), 1 if j else 0,
                                                 self.err.data_ptr(), self.sh), "zkie2_lookup_multiplicity")
         ttotal = lib.zkie2_lookup_len(0, t, 3)
@@ -895,14 +961,27 @@ class OpShardProver:
         return build
 
     # -- the shard ----------------------------------------------------------------------------
-    def prove(self, ops, boundary=()) -> OpShardProof:
+    def enqueue(self, ops, boundary=()):
+        """Every arm, then the bindings, then the per-table lookups, each
+        enqueued on the next of the prover's streams (they are independent
+        once the witness exists; the challenges are drawn in the reference's
+        order regardless), joined back into the caller's stream and gathered
+        into one device array.  Nothing here waits for the device, so the
+        whole call can be recorded as a CUDA graph."""
         arms = {"MatMul": self.op_matmul, "Projection": self.op_projection, "Add": self.op_add,
                 "Softmax": self.op_softmax, "Layernorm": self.op_layernorm,
                 "LayerNormCentered": self.op_layer_norm_centered}
+        self.err.zero_()
+        start = torch.cuda.Event()
+        start.record(self.main)
+        for st in self.streams:
+            if st is not self.main:
+                st.wait_event(start)
         for op in ops:
             k = op.kind
             if k in arms:
-                self.builders.append(arms[k](op))
+                with self.on(self.next_stream()):
+                    self.builders.append(arms[k](op))
             elif k == "Lookup":
                 self._lookup(op.table, self.store.get_idx(op.idx), self.store.get(op.out))
                 self.builders.append(lambda k=k: MarkerProof(k))
@@ -914,25 +993,91 @@ class OpShardProver:
         for t, pt, ref in self.claims:
             by_tensor.setdefault(t, []).append((pt, ref))
         bset = set(boundary)
-        bound, bind_builders = [], []
+        self.bound, self.bind_builders = [], []
         for t in sorted(by_tensor):
             cs = by_tensor[t]
             if t in bset or len(cs) < 2:
                 continue
-            bind_builders.append(self.same_poly(self.store.get(t), cs))
-            bound.append(t)
-        table_builders = [self.lookup_table(t) for t in sorted(self.lookups)]
-        # one copy back for everything
+            with self.on(self.next_stream()):
+                self.bind_builders.append(self.same_poly(self.store.get(t), cs))
+            self.bound.append(t)
+        self.table_builders = []
+        for t in sorted(self.lookups):
+            with self.on(self.next_stream()):
+                self.table_builders.append(self.lookup_table(t))
+        self.join()
         self.pend.parts.append(self.err.to(torch.int64).view(torch.uint64))
-        self.pend.fetch()
+        self.flat = self.pend.gather()
+
+    def collect(self) -> OpShardProof:
+        """One copy of the results to the host; the proof objects."""
+        self.pend.download(self.flat)
         code = int(self.pend.arrays[-1][0])
         if code:
             raise ValueError("prove_shard: " + ", ".join(v for k, v in _ERRORS.items() if code & k))
         op_proofs = [b() for b in self.builders]
-        binds = [b() for b in bind_builders]
+        binds = [b() for b in self.bind_builders]
         claims = [(t, pt, self.pend.value(ref)) for t, pt, ref in self.claims]
-        cols = [b() for b in table_builders]
-        return OpShardProof(op_proofs, bound, binds, claims, [w for w, _ in cols], [tc for _, tc in cols])
+        cols = [b() for b in self.table_builders]
+        return OpShardProof(op_proofs, list(self.bound), binds, claims, [w for w, _ in cols],
+                            [tc for _, tc in cols])
+
+    def prove(self, ops, boundary=()) -> OpShardProof:
+        self.enqueue(ops, boundary)
+        return self.collect()
+
+    def join(self):
+        for st in self.streams:
+            if st is not self.main:
+                ev = torch.cuda.Event()
+                ev.record(st)
+                self.main.wait_event(ev)
+
+
+class GraphShardProver:
+    """prove_shard_precomputed of one statement recorded once as a CUDA graph
+    and replayed.  Every challenge of a shard is fixed by the statement (the
+    op list and its tensor ids), and every launch's shape by the op shapes, so
+    the whole prove -- several thousand launches over the prover's streams
+    and the library's fan-out streams -- is the same graph for every witness:
+    write new witness values into the store's tensors (same buffers) and call
+    ``prove`` again.  ``make_rng`` returns the shard's challenge source at its
+    start (e.g. the child transcript); one eager proof warms the library's
+    streams and the allocator before the capture.  The device columns of a
+    returned proof (x, y, num, multiplicities) live in the graph's memory and
+    are overwritten by the next replay."""
+
+    def __init__(self, store: Store, ops, boundary, make_rng, streams: int = 8):
+        self.store, self.ops, self.boundary = store, list(ops), list(boundary)
+        OpShardProver(store, make_rng(), streams).prove(self.ops, self.boundary)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        self.prover = OpShardProver(store, make_rng(), streams)
+        with torch.cuda.graph(self.graph):
+            self.prover.main = torch.cuda.current_stream()
+            self.prover.sh = stream_handle()
+            self.prover.enqueue(self.ops, self.boundary)
+        torch.cuda.synchronize()
+
+    def replay(self):
+        """Enqueue the recorded prove on the current stream (no host work)."""
+        self.graph.replay()
+
+    def prove(self) -> OpShardProof:
+        self.replay()
+        return self.prover.collect()
+
+
+_STREAM_POOLS = {}
+
+
+def stream_pool(k: int):
+    """k side streams of the current device, created once and reused (the
+    library keeps its own fan-out streams per caller stream)."""
+    pool = _STREAM_POOLS.setdefault(torch.cuda.current_device(), [])
+    while len(pool) < k:
+        pool.append(torch.cuda.Stream())
+    return pool[:k]
 
 
 def prove_shard_precomputed(store: Store, ops, boundary, rng) -> OpShardProof:
@@ -982,7 +1127,7 @@ def prove_shard_dag(store: Store, ops, ops_per_shard: int) -> ShardDagProof:
             by_tensor.setdefault(t, []).append((pt, ev))
             owners.setdefault(t, set()).add(si)
     cross = [t for t in sorted(by_tensor) if len(owners[t]) > 1]
-    prover = OpShardProver(store, master)
+    prover = OpShardProver(store, master, streams=1)
     builders = [prover.same_poly(store.get(t), by_tensor[t]) for t in cross]
     prover.pend.fetch()
     return ShardDagProof(shards, cross, [b() for b in builders])

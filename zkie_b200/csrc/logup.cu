@@ -16,6 +16,8 @@
 // current layer, the next layer comes from one fused kernel, the eq table
 // from the MLE kernel, and the round messages of all layers go to the host
 // in one copy at the end.
+#include <map>
+#include <memory>
 #include <mutex>
 
 #include "../../include/zkie2.h"
@@ -131,32 +133,34 @@ uint64_t frac_layout(uint32_t lg, FracScratch* fs, uint64_t* base) {
     return off;
 }
 
-// Side streams of the layer sumchecks, per device; a call holds the device's
-// mutex from the first enqueue to its final synchronization, so the shared
-// events are never re-recorded under another call.
+// Side streams of the layer sumchecks, one set per (device, caller stream):
+// calls on different caller streams fan out on their own side streams and
+// run concurrently; calls on one caller stream share a set, and its mutex
+// covers an enqueue, so the shared events are never re-recorded under
+// another call.
 constexpr int kFracStreams = 4;
 struct FracStreams {
     cudaStream_t s[kFracStreams] = {};
     cudaEvent_t start = nullptr, level[kMaxLg + 1] = {}, done[kFracStreams] = {};
     std::mutex call;
-    bool ready = false;
 };
 std::mutex g_frac_mu;
-FracStreams g_frac[kMaxDevices];
+std::map<std::pair<int, cudaStream_t>, std::unique_ptr<FracStreams>> g_frac;
 
-int frac_streams(FracStreams** out) {
+int frac_streams(cudaStream_t caller, FracStreams** out) {
     const int d = current_device();
-    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    if (d < 0) return (int)cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> g(g_frac_mu);
-    FracStreams& f = g_frac[d];
-    if (!f.ready) {
-        for (auto& st : f.s) ZK_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
-        ZK_TRY(cudaEventCreateWithFlags(&f.start, cudaEventDisableTiming));
-        for (auto& e : f.level) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        for (auto& e : f.done) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        f.ready = true;
+    std::unique_ptr<FracStreams>& slot = g_frac[{d, caller}];
+    if (!slot) {
+        auto f = std::make_unique<FracStreams>();
+        for (auto& st : f->s) ZK_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        ZK_TRY(cudaEventCreateWithFlags(&f->start, cudaEventDisableTiming));
+        for (auto& e : f->level) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        for (auto& e : f->done) ZK_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        slot = std::move(f);
     }
-    *out = &f;
+    *out = slot.get();
     return 0;
 }
 
@@ -248,7 +252,7 @@ int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg
     if (!d_num || !d_den || !d_scratch || lg_n > kMaxLg || (lg_n && (!h_full_r || !h_cs)))
         return (int)cudaErrorInvalidValue;
     FracStreams* fst = nullptr;
-    int rc = frac_streams(&fst);
+    int rc = frac_streams(stream, &fst);
     if (rc) return rc;
     std::lock_guard<std::mutex> call_lock(fst->call);
     FracScratch fs;

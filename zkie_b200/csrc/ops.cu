@@ -362,15 +362,22 @@ __global__ void __launch_bounds__(kRowThreads) k_layernorm_fwd(const uint64_t* _
 // splits into a low table over tl bits and a high table over th bits (the
 // high one scaled by c_i), so an output costs two loads and one product per
 // claim.
-__global__ void k_eq_split_tables(const uint64_t* __restrict__ pts, const uint64_t* __restrict__ coeffs,
-                                  uint32_t c, uint32_t t, uint32_t tl, uint64_t* __restrict__ tabs) {
+// Points and coefficients of up to kEqChunk claims, passed by value so the
+// launch needs no host-to-device copy (and can be recorded in a CUDA graph).
+constexpr int kEqChunk = 8;
+constexpr int kEqMaxVars = 40;
+struct EqChunk {
+    uint64_t r[kEqChunk][kEqMaxVars];
+    uint64_t coeff[kEqChunk];
+};
+
+__global__ void k_eq_split_tables(EqChunk ck, uint32_t c, uint32_t t, uint32_t tl, uint64_t* __restrict__ tabs) {
     const uint32_t th = t - tl;
     const uint64_t nl = 1ull << tl, nh = 1ull << th, per = nl + nh;
     const uint64_t total = per * c;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += stride) {
         const uint64_t ci = g / per, e = g % per;
-        const uint64_t* r = pts + ci * t;
         uint64_t v;
         uint32_t bits, base;
         uint64_t x;
@@ -380,13 +387,13 @@ __global__ void k_eq_split_tables(const uint64_t* __restrict__ pts, const uint64
             base = 0;
             x = e;
         } else {
-            v = gl_canon(__ldg(coeffs + ci));
+            v = gl_canon(ck.coeff[ci]);
             bits = th;
             base = tl;
             x = e - nl;
         }
         for (uint32_t j = 0; j < bits; j++) {
-            const uint64_t rj = gl_canon(__ldg(r + base + j));
+            const uint64_t rj = gl_canon(ck.r[ci][base + j]);
             v = gl_mul(v, ((x >> j) & 1) ? rj : gl_sub(1, rj));
         }
         tabs[g] = gl_canon(v);
@@ -566,25 +573,29 @@ int zkie2_op_fill(uint64_t* d_out, uint64_t n, uint64_t value, cudaStream_t stre
 }
 
 uint64_t zkie2_eq_combine_scratch_elems(uint32_t c, uint32_t t) {
-    if (c == 0 || t > 40) return 0;
+    if (c == 0 || t > kEqMaxVars) return 0;
     const uint32_t tl = t / 2, th = t - tl;
-    return (uint64_t)c * (t + 1) + (uint64_t)c * ((1ull << tl) + (1ull << th)) + 2;
+    return (uint64_t)c * ((1ull << tl) + (1ull << th)) + 2;
 }
 
 int zkie2_eq_combine(const uint64_t* h_points, const uint64_t* h_coeffs, uint32_t c, uint32_t t, uint64_t* d_out,
                      uint64_t* d_scratch, cudaStream_t stream) {
-    if (c == 0 || t > 40 || !h_coeffs || !d_out || !d_scratch || (t && !h_points)) return (int)cudaErrorInvalidValue;
+    if (c == 0 || t > kEqMaxVars || !h_coeffs || !d_out || !d_scratch || (t && !h_points))
+        return (int)cudaErrorInvalidValue;
     const uint32_t tl = t / 2, th = t - tl;
-    uint64_t* d_pts = d_scratch;
-    uint64_t* d_co = d_pts + (uint64_t)c * t;
-    uint64_t* tabs = d_co + c;
-    if (t) ZK_TRY(cudaMemcpyAsync(d_pts, h_points, 8ull * c * t, cudaMemcpyHostToDevice, stream));
-    ZK_TRY(cudaMemcpyAsync(d_co, h_coeffs, 8ull * c, cudaMemcpyHostToDevice, stream));
-    const uint64_t ntab = (uint64_t)c * ((1ull << tl) + (1ull << th));
-    k_eq_split_tables<<<ew_grid(ntab), kOpThreads, 0, stream>>>(d_pts, d_co, c, t, tl, tabs);
-    ZK_LAUNCH_CHECK();
+    const uint64_t per = (1ull << tl) + (1ull << th);
+    for (uint32_t c0 = 0; c0 < c; c0 += kEqChunk) {
+        const uint32_t cn = c - c0 < (uint32_t)kEqChunk ? c - c0 : (uint32_t)kEqChunk;
+        EqChunk ck{};
+        for (uint32_t i = 0; i < cn; i++) {
+            for (uint32_t j = 0; j < t; j++) ck.r[i][j] = h_points[(uint64_t)(c0 + i) * t + j];
+            ck.coeff[i] = h_coeffs[c0 + i];
+        }
+        k_eq_split_tables<<<ew_grid(per * cn), kOpThreads, 0, stream>>>(ck, cn, t, tl, d_scratch + per * c0);
+        ZK_LAUNCH_CHECK();
+    }
     const uint64_t n = 1ull << t;
-    k_eq_combine<<<ew_grid(n), kOpThreads, 0, stream>>>(tabs, c, tl, th, n, d_out);
+    k_eq_combine<<<ew_grid(n), kOpThreads, 0, stream>>>(d_scratch, c, tl, th, n, d_out);
     ZK_LAUNCH_CHECK();
     return 0;
 }

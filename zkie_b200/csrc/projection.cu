@@ -12,6 +12,8 @@
 // remainder is at least half.  Values are signed fixed point embedded in the
 // field (fixed_point.rs: from_i64 / to_i64 / to_i32).
 #include <cstring>
+#include <map>
+#include <memory>
 #include <mutex>
 #include <vector>
 
@@ -70,29 +72,30 @@ bool is_pow2(uint64_t x) { return x && !(x & (x - 1)); }
 // Side streams of the projection block: the MatMul GKR and the affine
 // sumcheck run on them while the caller's stream builds the lookup columns
 // and proves the fraction tree (the three proofs share no data beyond the
-// inputs, and every challenge is drawn on the host first).
+// inputs, and every challenge is drawn on the host first).  One set per
+// (device, caller stream), so calls on different caller streams overlap.
 struct ProjStreams {
     cudaStream_t gkr = nullptr, aff = nullptr;
     cudaEvent_t start = nullptr, gkr_done = nullptr, aff_done = nullptr;
     std::mutex call;
-    bool ready = false;
 };
 std::mutex g_proj_mu;
-ProjStreams g_proj[kMaxDevices];
+std::map<std::pair<int, cudaStream_t>, std::unique_ptr<ProjStreams>> g_proj;
 
-int proj_streams(ProjStreams** out) {
+int proj_streams(cudaStream_t caller, ProjStreams** out) {
     const int d = current_device();
-    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    if (d < 0) return (int)cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> g(g_proj_mu);
-    ProjStreams& p = g_proj[d];
-    if (!p.ready) {
-        ZK_TRY(cudaStreamCreateWithFlags(&p.gkr, cudaStreamNonBlocking));
-        ZK_TRY(cudaStreamCreateWithFlags(&p.aff, cudaStreamNonBlocking));
-        for (cudaEvent_t* e : {&p.start, &p.gkr_done, &p.aff_done})
+    std::unique_ptr<ProjStreams>& slot = g_proj[{d, caller}];
+    if (!slot) {
+        auto p = std::make_unique<ProjStreams>();
+        ZK_TRY(cudaStreamCreateWithFlags(&p->gkr, cudaStreamNonBlocking));
+        ZK_TRY(cudaStreamCreateWithFlags(&p->aff, cudaStreamNonBlocking));
+        for (cudaEvent_t* e : {&p->start, &p->gkr_done, &p->aff_done})
             ZK_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
-        p.ready = true;
+        slot = std::move(p);
     }
-    *out = &p;
+    *out = slot.get();
     return 0;
 }
 
@@ -219,7 +222,7 @@ int projection_enqueue(const uint64_t* d_x, const uint64_t* d_w, const uint64_t*
     const ProjLayout L = proj_layout(m, k, n, shift);
     const ProjProofLayout PL = proj_proof_layout(lk, tv, lg);
     ProjStreams* ps = nullptr;
-    int rc = proj_streams(&ps);
+    int rc = proj_streams(stream, &ps);
     if (rc) return rc;
     std::lock_guard<std::mutex> call_lock(ps->call);
     uint64_t* S = d_scratch;

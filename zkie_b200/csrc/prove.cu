@@ -159,6 +159,23 @@ int zkie2_mle_eval_async(const uint64_t* d_values, uint32_t t, const uint64_t* h
     return eval_dev(d_values, t, h_point, d_out, d_scratch, stream);
 }
 
+uint64_t zkie2_mle_eval_many_scratch_elems(uint32_t max_t) { return eval_scratch_elems(max_t); }
+
+// eval of count tables at their points, one after another on the stream
+// (the scratch is reused: the launches are ordered), values into d_out.
+int zkie2_mle_eval_many(const uint64_t* const* d_values, const uint32_t* ts, const uint64_t* h_points,
+                        uint32_t count, uint64_t* d_out, uint64_t* d_scratch, cudaStream_t stream) {
+    if (count && (!d_values || !ts || !d_out || !d_scratch)) return (int)cudaErrorInvalidValue;
+    uint64_t off = 0;
+    for (uint32_t i = 0; i < count; i++) {
+        if (!d_values[i] || ts[i] > 40 || (ts[i] && !h_points)) return (int)cudaErrorInvalidValue;
+        int rc = eval_dev(d_values[i], ts[i], h_points + off, d_out + i, d_scratch, stream);
+        if (rc) return rc;
+        off += ts[i];
+    }
+    return 0;
+}
+
 uint64_t zkie2_sumcheck_scratch_elems(uint32_t t) { return sumcheck_scratch_elems(t) + 3ull * t + 4; }
 
 int zkie2_sumcheck_prove(const uint64_t* d_f, const uint64_t* d_h, uint32_t t, const uint64_t* h_ch,

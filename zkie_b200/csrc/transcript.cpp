@@ -215,4 +215,14 @@ void zkie2_xorshift_fill(uint64_t* state, uint64_t n, uint64_t mod, int64_t offs
     *state = x;
 }
 
+// n successive field draws of a challenge source into out (the reference's
+// `(0..n).map(|_| rng.field())`).
+void zkie2_challenger_fields(zkie2_challenger* c, uint64_t n, uint64_t* out) {
+    for (uint64_t i = 0; i < n; i++) out[i] = zkie2_challenger_field(c);
+}
+
+void zkie2_transcript_fields(zkie2_transcript* t, uint64_t n, uint64_t* out) {
+    for (uint64_t i = 0; i < n; i++) out[i] = zkie2_transcript_field(t);
+}
+
 }  // extern "C"

@@ -61,6 +61,11 @@ class Transcript:
     def field(self) -> int:
         return lib.zkie2_transcript_field(C.byref(self.t))
 
+    def fields(self, n: int) -> np.ndarray:
+        out = np.zeros(max(n, 1), dtype=np.uint64)
+        lib.zkie2_transcript_fields(C.byref(self.t), n, out.ctypes.data_as(_lib.pu64))
+        return out[:n]
+
     def next_u64(self) -> int:
         return lib.zkie2_transcript_next_u64(C.byref(self.t))
 
@@ -86,6 +91,11 @@ class XorShift64:
 
     def field(self) -> int:
         return lib.zkie2_challenger_field(C.byref(self.c))
+
+    def fields(self, n: int) -> np.ndarray:
+        out = np.zeros(max(n, 1), dtype=np.uint64)
+        lib.zkie2_challenger_fields(C.byref(self.c), n, out.ctypes.data_as(_lib.pu64))
+        return out[:n]
 
     def next_u64(self) -> int:
         x = self.c.xorshift_state
