@@ -180,9 +180,9 @@ def forward_ops(store, ops):
             with np.errstate(over="ignore"):
                 store.v[op.out] = from_i64(round_div(to_i64(g(op.x)) * np.int64(op.factor), 1 << op.shift))
         elif k == "MatMul":
-            store.v[op.c] = o.matmul_field(g(op.a).reshape(op.m, op.k), g(op.b).reshape(op.k, op.n)).reshape(-1)
+            store.v[op.c] = o.matmul_fixed(g(op.a).reshape(op.m, op.k), g(op.b).reshape(op.k, op.n)).reshape(-1)
         elif k == "Projection":
-            h = to_i64(o.matmul_field(g(op.x).reshape(op.m, op.k), g(op.w).reshape(op.k, op.n)).reshape(-1))
+            h = to_i64(o.matmul_fixed(g(op.x).reshape(op.m, op.k), g(op.w).reshape(op.k, op.n)).reshape(-1))
             bi = to_i64(g(op.bias))
             out = from_i64(round_div(h, 1 << op.shift) + bi)
             with np.errstate(over="ignore"):

@@ -98,6 +98,7 @@ def lib():
             "orc_fractional_verify": (C.c_int, [_pu64, _pu64, _u32, _pu64, _pu64, _pu64, _u64, _u64, _u64]),
             "orc_fractional_chain_core": (C.c_int, [_u32, _pu64, _pu64, _pu64, _pu64]),
             "orc_lookup_len": (_u64, [_u64, _u64, _u32]),
+            "orc_matmul_fixed": (None, [_pu64, _pu64, _u64, _u64, _u64, _pu64]),
             "orc_vec_add": (None, [_pu64, _pu64, _u64, _pu64]),
             "orc_vec_sub": (None, [_pu64, _pu64, _u64, _pu64]),
             "orc_vec_mul": (None, [_pu64, _pu64, _u64, _pu64]),
@@ -452,6 +453,16 @@ def matmul_field(a, b):
     return c
 
 
+def matmul_fixed(a, b):
+    """par::mm_par_fixed: the same field product as matmul_field, in i64 when it fits."""
+    a, b = u64(a), u64(b)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.zeros((m, n), dtype=np.uint64)
+    lib().orc_matmul_fixed(ptr(a), ptr(b), m, k, n, ptr(c))
+    return c
+
+
 def matmul_prove(at, b, c, m, k, n, u, v, ch):
     at, b, c, u, v, ch = map(u64, (at, b, c, u, v, ch))
     claimed = _u64(0)
@@ -569,6 +580,14 @@ def to_i32_index(v):
     return (-((P - v) & 0xFFFFFFFF)) & 0xFFFFFFFF
 
 
+def to_i32_indices(v):
+    """to_i32_index over an array (numpy, u32)."""
+    v = u64(v).reshape(-1) % np.uint64(P)
+    small = v <= np.uint64(0x7FFFFFFF)
+    low = ((np.uint64(P) - v) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    return np.where(small, v.astype(np.uint32), (np.uint32(0) - low).astype(np.uint32)).astype(np.uint32)
+
+
 def projection_terms(shift):
     """prove_projection's terms over [eq, rem_off, h, out, bias, ones] (:71-81)."""
     two, half, neg = 1 << shift, 1 << (shift - 1), P - 1
@@ -599,7 +618,7 @@ def projection_prove(x, w, bias, out, rem_off, m, k, n, shift, challenger):
     rem_off) into the table 0 .. 2^shift - 1 (full_r then cs per variable)."""
     x = u64(x).reshape(m, k)
     w = u64(w).reshape(k, n)
-    h = matmul_field(x, w).reshape(-1)
+    h = matmul_fixed(x, w).reshape(-1)
     op = op_matmul_prove(x, w, h.reshape(m, n), m, k, n, challenger)
     pt = np.concatenate([op["v"], op["u"]]).astype(np.uint64)
     eq = eq_evals(pt)
@@ -609,7 +628,7 @@ def projection_prove(x, w, bias, out, rem_off, m, k, n, shift, challenger):
                                        projection_terms(shift), pt)
     alpha, beta = challenger.field(), challenger.field()
     table = np.arange(1 << shift, dtype=np.uint64)
-    idx = [to_i32_index(v) for v in rem]
+    idx = to_i32_indices(rem)
     num, den = lookup_num_den(idx, rem, table, None, 0, alpha, beta)
     lg = num.size.bit_length() - 1
     full_r = [challenger.field() for _ in range(lg)]

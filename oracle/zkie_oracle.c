@@ -614,11 +614,19 @@ void orc_mle_partial_eval(const uint64_t *values, uint32_t t, const uint64_t *fi
 
 void orc_eq_evals(const uint64_t *r, uint32_t d, uint64_t *out)
 {
-    uint64_t n = 1ULL << d;
-    for (uint64_t i = 0; i < n; i++) out[i] = 1;
+    /* doubling, variable j on bit j: entries with bit j set take r_j, the
+     * others 1 - r_j (mle.rs eq_evals) */
+    out[0] = 1;
+    uint64_t size = 1;
     for (uint32_t j = 0; j < d; j++) {
-        uint64_t om = orc_sub(1, r[j]);
-        for (uint64_t i = 0; i < n; i++) out[i] = orc_mul(out[i], ((i >> j) & 1) ? r[j] : om);
+        const uint64_t rj = canon(r[j]), om = orc_sub(1, rj);
+#pragma omp parallel for schedule(static) if (size >= 4096)
+        for (int64_t i = 0; i < (int64_t)size; i++) {
+            const uint64_t v = out[i];
+            out[i + size] = orc_mul(v, rj);
+            out[i] = orc_mul(v, om);
+        }
+        size <<= 1;
     }
 }
 
@@ -785,7 +793,11 @@ void orc_sum_of_products_prove(const uint64_t *weights, const uint64_t *values, 
 }
 
 /* prove_virtual (:378-438).  Round message = evaluations at t = 0..max_deg via
- * k*f1 - (k-1)*f0; fold (1-r)*f0 + r*f1. */
+ * k*f1 - (k-1)*f0; fold (1-r)*f0 + r*f1.  As the reference's rayon loops, the
+ * pairs of a round are summed in parallel (field addition is associative, so
+ * the message does not depend on the split) and the fold writes a second
+ * buffer. */
+#define ORC_VMAX_DEG 16
 void orc_virtual_prove(const uint64_t *mles, uint32_t n_mles, uint32_t t, const uint64_t *coeffs,
                        const uint32_t *idx_off, const uint32_t *idx, uint32_t n_terms,
                        const uint64_t *ch, uint64_t *rounds, uint64_t *finals)
@@ -794,33 +806,58 @@ void orc_virtual_prove(const uint64_t *mles, uint32_t n_mles, uint32_t t, const 
     uint32_t max_deg = 0;
     for (uint32_t i = 0; i < n_terms; i++)
         if (idx_off[i + 1] - idx_off[i] > max_deg) max_deg = idx_off[i + 1] - idx_off[i];
-    uint64_t *bufs = (uint64_t *)malloc(8 * n * (n_mles ? n_mles : 1));
-    for (uint64_t i = 0; i < n * n_mles; i++) bufs[i] = canon(mles[i]);
+    if (max_deg > ORC_VMAX_DEG) max_deg = ORC_VMAX_DEG;
+    uint64_t nm = n_mles ? n_mles : 1;
+    uint64_t *cur = (uint64_t *)malloc(8 * n * nm), *nxt = (uint64_t *)malloc(8 * (n / 2 ? n / 2 : 1) * nm);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)(n * n_mles); i++) cur[i] = canon(mles[i]);
+    uint64_t kf[ORC_VMAX_DEG + 1], km1[ORC_VMAX_DEG + 1];
+    uint64_t *cf = (uint64_t *)malloc(8 * (n_terms ? n_terms : 1));
+    for (uint32_t k = 0; k <= max_deg; k++) {
+        kf[k] = orc_from_i64((int64_t)k);
+        km1[k] = orc_from_i64((int64_t)k - 1);
+    }
+    for (uint32_t ti = 0; ti < n_terms; ti++) cf[ti] = canon(coeffs[ti]);
     uint64_t len = n;
     for (uint32_t r = 0; r < t; r++) {
         uint64_t *p = rounds + (uint64_t)r * (max_deg + 1);
-        for (uint32_t k = 0; k <= max_deg; k++) p[k] = 0;
-        for (uint64_t s = 0; s < len / 2; s++)
-            for (uint32_t ti = 0; ti < n_terms; ti++)
-                for (uint32_t k = 0; k <= max_deg; k++) {
-                    uint64_t prod = canon(coeffs[ti]);
-                    uint64_t kf = orc_from_i64((int64_t)k), km1 = orc_from_i64((int64_t)k - 1);
-                    for (uint32_t q = idx_off[ti]; q < idx_off[ti + 1]; q++) {
-                        const uint64_t *b = bufs + (uint64_t)idx[q] * n;
-                        uint64_t fk = orc_sub(orc_mul(kf, b[2 * s + 1]), orc_mul(km1, b[2 * s]));
-                        prod = orc_mul(prod, fk);
+        uint64_t acc[ORC_VMAX_DEG + 1] = {0};
+        const uint64_t half = len / 2;
+#pragma omp parallel
+        {
+            uint64_t loc[ORC_VMAX_DEG + 1] = {0};
+#pragma omp for schedule(static)
+            for (int64_t s = 0; s < (int64_t)half; s++)
+                for (uint32_t ti = 0; ti < n_terms; ti++)
+                    for (uint32_t k = 0; k <= max_deg; k++) {
+                        uint64_t prod = cf[ti];
+                        for (uint32_t q = idx_off[ti]; q < idx_off[ti + 1]; q++) {
+                            const uint64_t *b = cur + (uint64_t)idx[q] * len;
+                            uint64_t fk = orc_sub(orc_mul(kf[k], b[2 * s + 1]), orc_mul(km1[k], b[2 * s]));
+                            prod = orc_mul(prod, fk);
+                        }
+                        loc[k] = orc_add(loc[k], prod);
                     }
-                    p[k] = orc_add(p[k], prod);
-                }
-        uint64_t rr = ch[r], om = orc_sub(1, rr);
-        for (uint32_t j = 0; j < n_mles; j++) {
-            uint64_t *b = bufs + (uint64_t)j * n;
-            for (uint64_t s = 0; s < len / 2; s++) b[s] = orc_add(orc_mul(om, b[2 * s]), orc_mul(rr, b[2 * s + 1]));
+#pragma omp critical
+            for (uint32_t k = 0; k <= max_deg; k++) acc[k] = orc_add(acc[k], loc[k]);
         }
-        len /= 2;
+        for (uint32_t k = 0; k <= max_deg; k++) p[k] = acc[k];
+        uint64_t rr = ch[r], om = orc_sub(1, rr);
+#pragma omp parallel for schedule(static) collapse(2)
+        for (uint32_t j = 0; j < n_mles; j++)
+            for (int64_t s = 0; s < (int64_t)half; s++) {
+                const uint64_t *b = cur + (uint64_t)j * len;
+                nxt[(uint64_t)j * half + s] = orc_add(orc_mul(om, b[2 * s]), orc_mul(rr, b[2 * s + 1]));
+            }
+        uint64_t *tmp = cur;
+        cur = nxt;
+        nxt = tmp;
+        len = half;
     }
-    for (uint32_t j = 0; j < n_mles; j++) finals[j] = bufs[(uint64_t)j * n];
-    free(bufs);
+    for (uint32_t j = 0; j < n_mles; j++) finals[j] = cur[(uint64_t)j * len];
+    free(cur);
+    free(nxt);
+    free(cf);
 }
 
 /* interpolate (:439-453) + verify_virtual (:454-484). */
@@ -909,6 +946,53 @@ void orc_matmul_field(const uint64_t *a, const uint64_t *b, uint64_t m, uint64_t
     (void)threads;
 }
 
+static int64_t to_i64_c(uint64_t v)
+{
+    v = canon(v);
+    return v <= (uint64_t)INT64_MAX ? (int64_t)v : -(int64_t)(ORC_P - v);
+}
+
+/* par::mm_par_fixed (crates/zkie-ops/src/par.rs:41-89): the field product,
+ * accumulated exactly in i64 (row-parallel, i-k-j order) when max|a| max|b| k
+ * < 2^63, else the field matmul. */
+void orc_matmul_fixed(const uint64_t *a, const uint64_t *b, uint64_t m, uint64_t k, uint64_t n, uint64_t *c)
+{
+    uint64_t max_a = 0, max_b = 0;
+    for (uint64_t i = 0; i < m * k; i++) {
+        const int64_t v = to_i64_c(a[i]);
+        const uint64_t u = v < 0 ? 0ULL - (uint64_t)v : (uint64_t)v;
+        if (u > max_a) max_a = u;
+    }
+    for (uint64_t i = 0; i < k * n; i++) {
+        const int64_t v = to_i64_c(b[i]);
+        const uint64_t u = v < 0 ? 0ULL - (uint64_t)v : (uint64_t)v;
+        if (u > max_b) max_b = u;
+    }
+    if ((u128)max_a * max_b * k >= ((u128)1 << 63)) {
+        orc_matmul_field(a, b, m, k, n, c, 0);
+        return;
+    }
+    int64_t *bi = (int64_t *)malloc(8 * (k * n != 0 ? k * n : 1));
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < (int64_t)(k * n); i++) bi[i] = to_i64_c(b[i]);
+#pragma omp parallel
+    {
+        int64_t *row = (int64_t *)malloc(8 * (n ? n : 1));
+#pragma omp for schedule(static)
+        for (int64_t i = 0; i < (int64_t)m; i++) {
+            for (uint64_t j = 0; j < n; j++) row[j] = 0;
+            for (uint64_t q = 0; q < k; q++) {
+                const int64_t av = to_i64_c(a[i * k + q]);
+                const int64_t *br = bi + q * n;
+                for (uint64_t j = 0; j < n; j++) row[j] += av * br[j];
+            }
+            for (uint64_t j = 0; j < n; j++) c[i * n + j] = orc_from_i64(row[j]);
+        }
+        free(row);
+    }
+    free(bi);
+}
+
 uint64_t orc_challenger_field(orc_challenger *s)
 {
     if (s->kind == 0) return orc_xorshift_field(&s->xs_state);
@@ -987,7 +1071,8 @@ static void frac_layer_tables(const uint64_t *num, const uint64_t *den, uint64_t
                               uint32_t t, uint64_t *mles)
 {
     uint64_t *eq = mles, *nn = mles + half, *nd = mles + 2 * half;
-    for (uint64_t s = 0; s < half; s++) {
+#pragma omp parallel for schedule(static)
+    for (int64_t s = 0; s < (int64_t)half; s++) {
         nn[s] = orc_add(orc_mul(num[s], den[half + s]), orc_mul(num[half + s], den[s]));
         nd[s] = orc_mul(den[s], den[half + s]);
     }

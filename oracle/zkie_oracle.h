@@ -194,6 +194,9 @@ uint64_t orc_lookup_num_den(const uint32_t *x, const uint64_t *y, uint64_t n, co
                             const uint64_t *m, uint64_t t, uint32_t mode, uint64_t alpha, uint64_t beta,
                             uint64_t *num, uint64_t *den);
 
+/* par::mm_par_fixed (zkie-ops/src/par.rs:41-89): exact i64 accumulation when
+ * max|a| max|b| k < 2^63, else the field matmul; the same field product. */
+void orc_matmul_fixed(const uint64_t *a, const uint64_t *b, uint64_t m, uint64_t k, uint64_t n, uint64_t *c);
 /* Elementwise field +, -, * and per-row field sums of the first ncols of each
  * d-wide row (the op-layer restatement's tensor arithmetic). */
 void orc_vec_add(const uint64_t *a, const uint64_t *b, uint64_t n, uint64_t *out);

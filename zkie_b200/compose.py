@@ -582,6 +582,17 @@ def _cat_u64(parts) -> torch.Tensor:
     return torch.cat([p.view(torch.int64) for p in parts]).view(torch.uint64)
 
 
+def frac_tree_bytes(lg: int) -> int:
+    """Bytes the fraction tree of 2^lg fractions touches once: each level
+    reads num / den of level l and writes level l + 1; layer l's sumcheck
+    reads its seven tables of 2^(lg - l - 1)."""
+    total = 0
+    for l in range(lg):
+        half = 1 << (lg - l - 1)
+        total += 8 * (4 * half + 2 * half) + 8 * 7 * half
+    return total
+
+
 class _Pending:
     """Device outputs of one proof in flight: every buffer a prover writes is
     registered here and fetched in one concatenated copy; ``host(h)`` then
@@ -637,6 +648,7 @@ class OpShardProver:
         self.builders = []    # one per op: () -> proof object
         self.lookups = {}     # table -> [(idx tensor, value tensor, event or None)]
         self.evals = []       # evaluations waiting for flush_evals
+        self.traffic = 0      # algorithmic bytes: every table a sub-proof reads, once
 
     @contextlib.contextmanager
     def on(self, s):
@@ -666,6 +678,7 @@ class OpShardProver:
         arm in one call (flush_evals); returns a reference to the result."""
         ref = [None, 0]
         self.evals.append((values, np.ascontiguousarray(point, dtype=np.uint64), ref))
+        self.traffic += 8 * values.numel()
         return ref
 
     def flush_evals(self):
@@ -690,6 +703,7 @@ class OpShardProver:
     def virtual(self, mles, terms, ch: np.ndarray):
         """prove_virtual enqueued -> a builder of the VirtualProof."""
         n, t = len(mles), ch.size
+        self.traffic += 8 * n << t
         coeffs, off, idx, deg = _terms_arrays(terms)
         hr, dr = self.pend.out(t * (deg + 1))
         hf, df = self.pend.out(n)
@@ -705,6 +719,7 @@ class OpShardProver:
     def fractional(self, num: torch.Tensor, den: torch.Tensor):
         """prove_fractional (logup_gkr.rs:71-81): full_r then cs drawn."""
         lg = _lg(num.numel())
+        self.traffic += frac_tree_bytes(lg)
         full_r, cs = self.draw(lg), self.draw(lg)
         h, d = self.pend.out(lib.zkie2_fractional_proof_elems(lg))
         scr = empty(max(lib.zkie2_fractional_scratch_elems(lg), 2))
@@ -746,6 +761,7 @@ class OpShardProver:
         lm, lk, ln = _lg(op.m), _lg(op.k), _lg(op.n)
         u, v, ch = self.draw(lm), self.draw(ln), self.draw(lk)
         h, d = self.pend.out(3 + 3 * lk)
+        self.traffic += 8 * (op.m * op.k + op.k * op.n + op.m * op.n)
         scr = empty(max(lib.zkie2_op_matmul_scratch_elems(op.m, op.k, op.n), 1))
         check(lib.zkie2_op_matmul_prove_async(ptr(g(op.a)), ptr(g(op.b)), ptr(g(op.c)), op.m, op.k, op.n, _pp(u),
                                               _pp(v), _pp(ch), ptr(d), ptr(scr), self.sh),
@@ -773,6 +789,9 @@ class OpShardProver:
         alpha, beta = self.rng.field(), self.rng.field()
         full_r, cs = self.draw(lg), self.draw(lg)
         hbuf = self.store.proj_h.get(op.out)
+        # GKR: x, W, h; affine: six tables of m n; lookup columns 2 x 2^lg
+        # written, then the fraction tree
+        self.traffic += 8 * (m * k + k * n + m * n) + 8 * 6 * m * n + 16 * (1 << lg) + frac_tree_bytes(lg)
         h, d = self.pend.out(lib.zkie2_projection_proof_elems(m, k, n, shift))
         scr = empty(max(lib.zkie2_projection_scratch_elems(m, k, n, shift), 1))
         check(lib.zkie2_projection_prove_async(ptr(g(op.x)), ptr(g(op.w)), ptr(g(op.bias)), ptr(g(op.out)),
