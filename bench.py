@@ -91,6 +91,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-big", action="store_true", help="skip the 256 x 2^24 and expert-stack commits")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the 12-layer GPT-2 shard DAG")
     return ap.parse_args()
 
 
@@ -522,6 +523,7 @@ def main_split(args, zk, dev, world, rank):
     split_sc = sumcheck_case(zk, dev, rank, world)
     mg = mg_case(zk, dev, ctx, rank, world, lg_l, lg_b, w, root)
     lib.zkie2_mg_destroy(ctx)
+    cfg4 = cfg4_case(zk, dev, rank, world) if not args.no_cfg4 else None
     cfg = workload_config(lg_l, w, lg_b, world)
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -564,6 +566,8 @@ def main_split(args, zk, dev, world, rank):
     line.update(big)
     line["split_sumcheck"] = split_sc
     line["mg_c_abi"] = mg
+    if cfg4:
+        line["cfg4_gpt2_12_layers"] = cfg4
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -712,6 +716,8 @@ def main():
     extra = next_rows(want_cpu=not args.no_cpu)
     extra["projection"] = projection_case(zk, dev, want_cpu=not args.no_cpu)
     extra["layer_shard"] = layer_case(zk, dev, want_cpu=not args.no_cpu)
+    if not args.no_cfg4:
+        extra["cfg4_gpt2_12_layers"] = cfg4_case(zk, dev, 0, 1)
     # ---- configurations 2 (256 x 2^24) and 5 (expert stack); the 2^28 sumcheck ----
     del d_in, d_lde, d_layers, d_scr
     torch.cuda.empty_cache()
@@ -945,32 +951,6 @@ def projection_case(zk, dev, want_cpu, m=512, k=1024, n=4096, shift=16, iters=5)
     return out_d
 
 
-def _proof_digest(canon) -> str:
-    """SHA-256 over every value of a proof's canonical form (arrays included)."""
-    import hashlib
-
-    import numpy as np
-    h = hashlib.sha256()
-
-    def walk(v):
-        if isinstance(v, dict):
-            for k in sorted(v):
-                h.update(k.encode())
-                walk(v[k])
-        elif isinstance(v, (list, tuple)):
-            h.update(b"[%d" % len(v))
-            for x in v:
-                walk(x)
-        elif isinstance(v, np.ndarray):
-            h.update(np.ascontiguousarray(v, dtype=np.uint64).tobytes())
-        elif isinstance(v, str):
-            h.update(v.encode())
-        else:
-            h.update(int(v).to_bytes(8, "little"))
-    walk(canon)
-    return h.hexdigest()[:16]
-
-
 def layer_case(zk, dev, want_cpu, iters=5):
     """Configuration 3: one GPT-2-small layer (models/gpt2 build_layer: 176 ops,
     m 512, D 1024 with 768 real, 12 heads x 64, FFN 4096 with 3072 real; the
@@ -984,6 +964,7 @@ def layer_case(zk, dev, want_cpu, iters=5):
 
     from zkie_b200 import compose as C
     from zkie_b200 import gpt2
+    from zkie_b200.dag import digest as _proof_digest
     shape = gpt2.GPT2_SMALL
     st = C.Store()
     ops, x, out = gpt2.gpt2_layer(st, shape)
@@ -1075,6 +1056,81 @@ def layer_case(zk, dev, want_cpu, iters=5):
                                            "over oracle/zkie_oracle.c (OpenMP loops on every host thread)"}
         out_d["proof_matches_cpu"] = out_d["cpu_baseline"]["proof_digest"] == digest
     del st, gp
+    torch.cuda.empty_cache()
+    return out_d
+
+
+def cfg4_case(zk, dev, rank, world, layers=12):
+    """Configuration 4: GPT-2-small's 12 layers chained as build_gpt2 chains
+    them (models/gpt2/src/lib.rs:367-372), proven as a shard DAG with one
+    layer per shard (ops_per_shard 176; compose.rs prove_shard_dag
+    :2289-2346): rank r proves the shards si % world == r, each recorded once
+    as a CUDA graph and replayed; rank 0 gathers the claims and binds the
+    tensors claimed by two shards (the layer boundaries) with the master
+    transcript.  Every rank holds the whole witness (the forward pass of all
+    12 layers).  Not assembled: the embedding lookup into the tied token
+    table, the final LayerNorm, the lm_head matmul and the argmax."""
+    import torch
+    import torch.distributed as dist
+
+    from zkie_b200 import compose as C
+    from zkie_b200 import dag, gpt2
+    t0 = time.perf_counter()
+    st = C.Store()
+    ops, x, out = gpt2.gpt2_layers(st, gpt2.GPT2_SMALL, layers)
+    build_s = time.perf_counter() - t0
+    fwd = []
+    for _ in range(2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        C.forward_ops(st, ops)
+        torch.cuda.synchronize()
+        fwd.append(time.perf_counter() - t0)
+    per = len(ops) // layers
+    gather = dag.torch_gather() if world > 1 else None
+    # timed passes gather only the claims; the digests come from one more
+    # replay afterwards (they download every shard's lookup columns)
+    provers = dag.device_provers(summary="none", graph=True)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    dag.prove_dag_ranks(st, ops, per, provers, rank, world, gather)
+    torch.cuda.synchronize()
+    record_s = time.perf_counter() - t0
+    times = []
+    for _ in range(3):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = dag.prove_dag_ranks(st, ops, per, provers, rank, world, gather)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.median(times)
+    fwd_ms = 1e3 * fwd[-1]
+    if world > 1:
+        ms = max_over_ranks(ms, dev)
+        fwd_ms = max_over_ranks(fwd_ms, dev)
+    if world > 1:
+        dist.barrier()
+    res = dag.prove_dag_ranks(st, ops, per, dag.device_provers(summary="digest", graph=True, graphs=provers.graphs),
+                              rank, world, gather)
+    out_d = None
+    if rank == 0:
+        check = dag.prove_dag_ranks(st, ops, per, dag.device_provers(summary="digest", graph=False))
+        out_d = {
+            "config": f"cfg4: GPT-2-small, {layers} layers of models/gpt2 build_layer chained (m 512, D 1024, "
+                      f"FFN 4096, 12 heads; synthetic weights), one layer per shard (ops_per_shard {per}), "
+                      f"shards round-robin over {world} GPU(s); embedding lookup, final LayerNorm, lm_head and "
+                      "argmax not assembled",
+            "ms": round(ms, 3), "unit": "ms per DAG proof (every shard + cross-shard bindings), max over ranks",
+            "layers_per_s": round(layers / (ms / 1e3), 2), "forward_ms": round(fwd_ms, 3),
+            "record_ms": round(1e3 * record_s, 1), "build_s": round(build_s, 2),
+            "shards": len(res.shards), "max_shards_per_gpu": -(-len(res.shards) // world),
+            "cross_tensors": len(res.cross_tensors), "digest": res.digest,
+            "digest_matches_eager_one_gpu": res.digest == check.digest,
+        }
+    del st, provers
     torch.cuda.empty_cache()
     return out_d
 

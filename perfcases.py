@@ -16,6 +16,7 @@ of the profiles (run from the repository root).
     python perfcases.py sweep
     python perfcases.py coset --log-size 20 --polys 256 --gpus 8
     python perfcases.py projection --m 512 --k 1024 --n 4096
+    python perfcases.py layer --trace
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -363,6 +364,49 @@ def case_projection(a):
     return {"case": "prove_projection", "m": m, "k": k, "n": n, "shift": shift, "ms": ms}
 
 
+def case_layer(a):
+    """One GPT-2-small layer shard (zkie_b200.gpt2.GPT2_SMALL, 176 ops) proven
+    by a recorded CUDA graph: the replay's device time, and with --trace the
+    kernels of one replay (torch.profiler / CUPTI: launches, the sum of kernel
+    times against the replay's span, the top kernels by total time)."""
+    import collections
+
+    from zkie_b200 import compose as C
+    from zkie_b200 import gpt2
+    st = C.Store()
+    ops, _, _ = gpt2.gpt2_layer(st, gpt2.GPT2_SMALL)
+    C.forward_ops(st, ops)
+    master = C.master_transcript(ops, len(ops))
+
+    def make_rng():
+        c = master.clone()
+        c.absorb_u64(0)
+        return c
+    gp = C.GraphShardProver(st, ops, [], make_rng)
+    ms = _time(gp.replay, a.iters)
+    res = {"case": "layer_shard_replay", "ops": len(ops), "ms": ms}
+    if a.trace:
+        from torch.profiler import ProfilerActivity, profile
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            gp.replay()
+            torch.cuda.synchronize()
+        evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        iv = sorted((e.time_range.start, e.time_range.end) for e in evs)
+        span = iv[-1][1] - iv[0][0]
+        total = sum(e - s for s, e in iv)
+        agg = collections.defaultdict(lambda: [0, 0.0])
+        for e in evs:
+            name = e.name.split("(")[0].replace("void ", "").replace("zk::(anonymous namespace)::", "")
+            agg[name][0] += 1
+            agg[name][1] += e.time_range.end - e.time_range.start
+        top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]
+        res.update({"launches": len(evs), "span_ms": span / 1e3, "kernel_time_sum_ms": total / 1e3,
+                    "mean_concurrency": total / max(span, 1),
+                    "top": [[k, n, round(t / 1e3, 3), round(t / total, 4)] for k, (n, t) in top]})
+    return res
+
+
 def case_sweep(a):
     """batches of 1, 16, 256 polynomials of 2^16,
     2^20, 2^24 coefficients at blowup 2 and 4.  One JSON line per case that
@@ -421,7 +465,7 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup", "grind", "fixed", "cache", "coset", "projection"])
+                                         "logup", "grind", "fixed", "cache", "coset", "projection", "layer"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -430,13 +474,14 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=1024)
     ap.add_argument("--n", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--trace", action="store_true", help="layer: list one replay's kernels")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("perfcases needs a CUDA device")
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
            "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "cache": case_cache, "sop": case_sop, "shard": case_shard, "split": case_split,
-           "sweep": case_sweep, "coset": case_coset, "projection": case_projection}[a.case](a)
+           "sweep": case_sweep, "coset": case_coset, "projection": case_projection, "layer": case_layer}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 

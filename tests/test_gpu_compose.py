@@ -159,3 +159,26 @@ def test_graph_prover_replays_for_a_new_witness(zk):
     child = o.OracleTranscript(raw=om.t)
     child.absorb_u64(0)
     assert_same(got, co.prove_shard_precomputed(ref, ops, [], child))
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_dag_ranks_device_matches_oracle(zk, graph):
+    """The shard-DAG orchestration (zkie_b200/dag.py) over the device prover,
+    eager and with recorded graphs, on a three-layer stack: the DAG digest of
+    the CPU restatement's prove_shard_dag."""
+    from zkie_b200 import dag, gpt2
+    shape = gpt2.LayerShape(m=8, d=16, d_real=12, heads=2, dh=4, ffn=32, ffn_real=24, exp_bits=8, gelu_bits=10,
+                            rsqrt_len=256)
+    host = co.HostStore()
+    ops, _, _ = gpt2.gpt2_layers(host, shape, 3)
+    dev = _device_store(zk, host)
+    zk.compose.forward_ops(dev, ops)
+    per = len(ops) // 3
+    provers = dag.device_provers(summary="digest", graph=graph)
+    got = dag.prove_dag_ranks(dev, ops, per, provers)
+    if graph:  # a second pass replays the recorded graphs
+        got = dag.prove_dag_ranks(dev, ops, per, provers)
+        assert len(provers.graphs) == 3
+    co.forward_ops(host, ops)
+    full = co.prove_shard_dag(host, ops, per)
+    assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"])

@@ -1,0 +1,182 @@
+"""prove_shard_dag (crates/zkie-ops/src/compose.rs:2289-2346) with its shards
+spread over ranks, one process per GPU.
+
+The reference proves the shards of a DAG in parallel on one host
+(`ranges.par_iter()`, :2305-2313): every shard's challenges come from its own
+child transcript (the master transcript over the statement, plus the shard
+index), so shards are independent once the witness exists, and only the
+tensors claimed by more than one shard are bound afterwards, with the master
+transcript (:2315-2345).  The split here is the same one, across GPUs: rank r
+proves the shards si with si % world == r (each rank holds the whole witness:
+the forward pass is cheap next to the proof), rank 0 gathers every shard's
+claims and proves the cross-shard bindings.  No collective touches the data
+path; the gather carries claims (points and values) and each shard's proof
+summary.
+
+The orchestration is host logic over a few callables, so the same code runs
+the device prover (``prove_dag_ranks`` with ``device_provers``) and, in the
+CPU tests, the CPU restatement under a gloo process group.
+"""
+import hashlib
+from dataclasses import dataclass
+from typing import Callable, List
+
+import numpy as np
+
+
+def shard_ranges(op_count: int, ops_per_shard: int):
+    """compose.rs:2264-2274."""
+    ops_per_shard = max(ops_per_shard, 1)
+    return [(s, min(s + ops_per_shard, op_count)) for s in range(0, op_count, ops_per_shard)]
+
+
+def shard_owner(si: int, world: int) -> int:
+    return si % world
+
+
+def digest(canon) -> str:
+    """SHA-256 (first 16 hex digits) over every value of a canonical proof
+    form: dict keys sorted, sequence lengths, arrays as little-endian u64."""
+    h = hashlib.sha256()
+
+    def walk(v):
+        if isinstance(v, dict):
+            for k in sorted(v):
+                h.update(str(k).encode())
+                walk(v[k])
+        elif isinstance(v, (list, tuple)):
+            h.update(b"[%d" % len(v))
+            for x in v:
+                walk(x)
+        elif isinstance(v, np.ndarray):
+            h.update(np.ascontiguousarray(v, dtype=np.uint64).tobytes())
+        elif isinstance(v, str):
+            h.update(v.encode())
+        else:
+            h.update(int(v).to_bytes(8, "little"))
+    walk(canon)
+    return h.hexdigest()[:16]
+
+
+@dataclass
+class DagProvers:
+    """What the orchestration needs from a prover: the master transcript of a
+    statement, a shard's child, a shard proof (store, ops, rng) -> proof, the
+    proof's raw claims [(tensor, point, value)], its summary for the gather
+    (the canonical form, or a digest of it), and the same_poly binding of one
+    tensor's claims with the master transcript."""
+    master: Callable
+    child: Callable
+    prove: Callable
+    claims: Callable
+    summary: Callable
+    same_poly: Callable
+
+
+@dataclass
+class DagResult:
+    """Rank 0's view: every shard's summary in shard order, the cross-shard
+    tensors and their bindings (canonical), and the DAG digest."""
+    shards: List
+    cross_tensors: List[int]
+    cross_binds: List
+    digest: str
+
+
+def dag_digest(shard_summaries, cross_tensors, cross_binds) -> str:
+    parts = [s if isinstance(s, str) or s is None else digest(s) for s in shard_summaries]
+    parts = ["" if s is None else s for s in parts]
+    return digest([parts, list(cross_tensors), [b for b in cross_binds]])
+
+
+def prove_dag_ranks(store, ops, ops_per_shard: int, provers: DagProvers, rank: int = 0, world: int = 1,
+                    gather=None):
+    """Prove the shards this rank owns; rank 0 returns the DagResult (other
+    ranks None).  ``gather(obj)`` returns every rank's obj (in rank order) on
+    rank 0 and None elsewhere; with world 1 it is not needed."""
+    ranges = shard_ranges(len(ops), ops_per_shard)
+    master = provers.master(ops, ops_per_shard)
+    mine = []
+    for si, (s, e) in enumerate(ranges):
+        if shard_owner(si, world) != rank:
+            continue
+        proof = provers.prove(store, ops[s:e], provers.child(master, si))
+        claims = [(int(t), np.asarray(pt, dtype=np.uint64), int(v)) for t, pt, v in provers.claims(proof)]
+        mine.append((si, claims, provers.summary(proof)))
+    everyone = gather(mine) if world > 1 else [mine]
+    if rank != 0:
+        return None
+    by_shard = sorted((x for part in everyone for x in part), key=lambda x: x[0])
+    assert [x[0] for x in by_shard] == list(range(len(ranges))), "a shard is missing from the gather"
+    by_tensor, owners = {}, {}
+    for si, claims, _ in by_shard:
+        for t, pt, v in claims:
+            by_tensor.setdefault(t, []).append((pt, v))
+            owners.setdefault(t, set()).add(si)
+    cross = [t for t in sorted(by_tensor) if len(owners[t]) > 1]
+    binds = [provers.same_poly(store, t, by_tensor[t], master) for t in cross]
+    summaries = [x[2] for x in by_shard]
+    return DagResult(summaries, cross, binds, dag_digest(summaries, cross, binds))
+
+
+def torch_gather(group=None):
+    """gather over torch.distributed (gather_object to rank 0)."""
+    import torch.distributed as dist
+
+    def gather(obj):
+        out = [None] * dist.get_world_size(group) if dist.get_rank(group) == 0 else None
+        dist.gather_object(obj, out, dst=0, group=group)
+        return out
+    return gather
+
+
+# ---- the device prover -----------------------------------------------------------------------
+def device_provers(summary: str = "digest", graph: bool = False, streams: int = 8, graphs=None) -> DagProvers:
+    """DagProvers over zkie_b200.compose.  summary "digest" keeps each shard's
+    proof on its rank (only claims and a digest of the proof travel; the
+    digest downloads the proof's lookup columns, hundreds of MB per GPT-2
+    layer), "canonical" gathers the whole canonical form (small statements),
+    "none" only the claims.  graph=True records each shard's prove as a CUDA
+    graph and replays it; the recorded graphs live in ``graphs`` (a dict,
+    shared between provers when given) and on the returned object."""
+    from . import compose as C
+
+    def master(ops, ops_per_shard):
+        return C.master_transcript(ops, ops_per_shard)
+
+    def child(m, si):
+        c = m.clone()
+        c.absorb_u64(si)
+        return c
+
+    graphs = {} if graphs is None else graphs
+
+    def prove(store, shard_ops, rng):
+        if not graph:
+            return C.OpShardProver(store, rng, streams).prove(shard_ops, [])
+        key = (shard_ops[0].__class__.__name__, id(shard_ops[0]), len(shard_ops))
+        gp = graphs.get(key)
+        if gp is None:
+            state = rng.clone()
+            gp = C.GraphShardProver(store, shard_ops, [], lambda: state.clone(), streams)
+            graphs[key] = gp
+        return gp.prove()
+
+    def claims(proof):
+        return proof.claims
+
+    def summ(proof):
+        if summary == "none":
+            return None
+        can = proof.canonical()
+        return digest(can) if summary == "digest" else can
+
+    def same_poly(store, t, cs, m):
+        pr = C.OpShardProver(store, m, streams=1)
+        b = pr.same_poly(store.get(t), cs)
+        pr.pend.fetch()
+        return b().canonical()
+
+    p = DagProvers(master, child, prove, claims, summ, same_poly)
+    p.graphs = graphs
+    return p

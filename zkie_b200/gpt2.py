@@ -215,16 +215,34 @@ def gpt2_layer(store, s: LayerShape, seed: int = 0x6B2):
     """A store holding one GPT-2 layer's inputs and the layer's ops:
     (ops, x, out).  The layer input x is drawn in [0, 50) on the real
     columns (zero padding), then the weights (synthetic_layer_weights)."""
+    return gpt2_layers(store, s, 1, seed)
+
+
+def gpt2_layers(store, s: LayerShape, layers: int, seed: int = 0x6B2):
+    """``layers`` GPT-2 layers chained as build_gpt2 chains them (the output
+    of layer l is the input of layer l + 1; models/gpt2/src/lib.rs:367-372),
+    sharing the tables and the mask: (ops, x, out).  The input x is drawn
+    first, then each layer's weights as the layer is built."""
     rng = XorShift64(seed)
-    m, D, DH = s.m, s.d, s.dh
-    x_host = _pad2(xorshift_fill(rng, m * s.d_real, 50).reshape(m, s.d_real), m, D).reshape(-1)
-    w = synthetic_layer_weights(rng, s)
-    bc = lambda v: np.tile(v, m)  # noqa: E731  broadcast a row vector over m rows
+    m = s.m
+    x_host = _pad2(xorshift_fill(rng, m * s.d_real, 50).reshape(m, s.d_real), m, s.d).reshape(-1)
     x = store.push(x_host)
     exp_t = store.push(exp_table(s.exp_bits))
     rsqrt_t = store.push(rsqrt_table(s.rsqrt_len))
     gelu_t = store.push(gelu_table(s.gelu_bits))
     mask_t = store.push(causal_mask(m))
+    ops, cur = [], x
+    for _ in range(layers):
+        layer_ops, cur = build_layer(store, s, cur, synthetic_layer_weights(rng, s), exp_t, rsqrt_t, gelu_t, mask_t)
+        ops += layer_ops
+    return ops, x, cur
+
+
+def build_layer(store, s: LayerShape, x, w, exp_t, rsqrt_t, gelu_t, mask_t):
+    """models/gpt2/src/lib.rs build_layer (:48-319) over weights w
+    (synthetic_layer_weights): -> (ops, out)."""
+    m, D, DH = s.m, s.d, s.dh
+    bc = lambda v: np.tile(v, m)  # noqa: E731  broadcast a row vector over m rows
     ops = []
     ln1_w, ln1_b = store.push(bc(w["ln1_w"])), store.push(bc(w["ln1_b"]))
     h = store.push(None)
@@ -272,4 +290,4 @@ def gpt2_layer(store, s: LayerShape, seed: int = 0x6B2):
             Projection(act, proj_w, proj_b, proj2, proj2_rem, m, s.ffn, D, s.shift)]
     out = store.push(None)
     ops.append(Add(x2, proj2, out))
-    return ops, x, out
+    return ops, out
