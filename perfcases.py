@@ -397,7 +397,7 @@ def case_layer(a):
         total = sum(e - s for s, e in iv)
         agg = collections.defaultdict(lambda: [0, 0.0])
         for e in evs:
-            name = e.name.split("(")[0].replace("void ", "").replace("zk::(anonymous namespace)::", "")
+            name = e.name.replace("void ", "").replace("zk::(anonymous namespace)::", "").split("(")[0]
             agg[name][0] += 1
             agg[name][1] += e.time_range.end - e.time_range.start
         top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]

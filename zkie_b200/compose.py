@@ -713,8 +713,11 @@ class OpShardProver:
                                             idx.ctypes.data_as(_lib.pu32), len(terms), _pp(ch), ptr(dr), ptr(df),
                                             ptr(scr), self.sh), "zkie2_virtual_prove_async")
         pend = self.pend
-        return lambda: VirtualProof(pend.host(hr)[:t * (deg + 1)].reshape(t, deg + 1).copy(),
-                                    pend.host(hf)[:n].copy())
+
+        def build():
+            return VirtualProof(pend.host(hr)[:t * (deg + 1)].reshape(t, deg + 1).copy(), pend.host(hf)[:n].copy())
+        build.final = lambda i: (hf, i)  # the folded value of table i: that table at the challenges
+        return build
 
     def fractional(self, num: torch.Tensor, den: torch.Tensor):
         """prove_fractional (logup_gkr.rs:71-81): full_r then cs drawn."""
@@ -766,11 +769,12 @@ class OpShardProver:
         check(lib.zkie2_op_matmul_prove_async(ptr(g(op.a)), ptr(g(op.b)), ptr(g(op.c)), op.m, op.k, op.n, _pp(u),
                                               _pp(v), _pp(ch), ptr(d), ptr(scr), self.sh),
               "zkie2_op_matmul_prove_async")
-        refs = []
-        for t, pt in ((op.a, np.concatenate([ch, u])), (op.b, np.concatenate([v, ch])),
-                      (op.c, np.concatenate([v, u]))):
-            self.claim(t, pt)
-            refs.append(self.claims[-1][2])
+        # the claims are the proof's own values: f_eval = eval(A, ch||u), h_eval =
+        # eval(B, v||ch) (the sumcheck's folded tables), claimed = eval(C, v||u)
+        refs = [(h, 1 + 3 * lk), (h, 2 + 3 * lk), (h, 0)]
+        for t, pt, ref in zip((op.a, op.b, op.c), (np.concatenate([ch, u]), np.concatenate([v, ch]),
+                                                   np.concatenate([v, u])), refs):
+            self.claim(t, pt, ref)
         pend = self.pend
 
         def build():
@@ -804,9 +808,11 @@ class OpShardProver:
         o_fr = o_aff + 3 * tv + 6
         nr = 2 * lg * (lg - 1)
         pt = np.concatenate([v, u])
-        self.claim(op.x, np.concatenate([ch, u]))
-        self.claim(op.w, np.concatenate([v, ch]))
-        self.claim(op.out, pt)
+        # x and W at the GKR sumcheck's folded values, out and bias at the
+        # affine sumcheck's finals (tables 3 and 4 at pt)
+        self.claim(op.x, np.concatenate([ch, u]), (h, o_mm + 3 * lk))
+        self.claim(op.w, np.concatenate([v, ch]), (h, o_mm + 3 * lk + 1))
+        self.claim(op.out, pt, (h, o_aff + 3 * tv + 3))
         self.claim(op.bias, pt, (h, o_aff + 3 * tv + 4))
         pend = self.pend
 
@@ -832,8 +838,8 @@ class OpShardProver:
         c = g(op.c)
         r = self.draw(_lg(c.numel()))
         vb = self.virtual([g(op.a), g(op.b), c], ADD_TERMS, r)
-        for t in (op.a, op.b, op.c):
-            self.claim(t, r)
+        for i, t in enumerate((op.a, op.b, op.c)):
+            self.claim(t, r, vb.final(i))
         return lambda: AddProof(vb(), r)
 
     def _lookup(self, table: int, idx: torch.Tensor, vals: torch.Tensor, produced_here: bool = False):
@@ -861,7 +867,7 @@ class OpShardProver:
               "zkie2_op_softmax_rem")
         r_scale = self.draw(_lg(m * n))
         rescale = self.virtual([out, e, sum_b, rem], SOFTMAX_RESCALE_TERMS, r_scale)
-        self.claim(op.out, r_scale)
+        self.claim(op.out, r_scale, rescale.final(0))
         self._lookup(op.table, self.store.get_idx(op.idx), e)
         pend = self.pend
         return lambda: SoftmaxRoundedProof(row_sum(), rescale(), r_sum, sum_ch, r_scale, pend.value(claimed))
@@ -879,8 +885,9 @@ class OpShardProver:
         r_out = self.draw(_lg(m * d))
         out = self.virtual([x, cols["scale"], b, cols["out"]], LN_OUT_TERMS, r_out)
         self._lookup(op.rsqrt_table, cols["idx"], cols["rsqrt"], produced_here=True)
-        for t in (op.out, op.w, op.b):
-            self.claim(t, r_out)
+        self.claim(op.out, r_out, out.final(3))
+        self.claim(op.w, r_out)
+        self.claim(op.b, r_out, out.final(2))
         pend = self.pend
         return lambda: LayernormChainProof(mean_sq(), out(), r_mean, mean_ch, r_out, pend.value(mean_claim))
 
@@ -906,9 +913,11 @@ class OpShardProver:
         out = self.virtual([f["centered"], self.broadcast(f["rstd"], m, d), w, b, f["raw"], f["out"], f["rem_out"],
                             self.ones(m * d)], LNC_OUT_TERMS, r_out)
         self._lookup(op.rsqrt_table, f["s_index"], f["rstd"], produced_here=True)
-        self.claim(op.x, centered_r)
-        for t in (op.out, op.w, op.b):
-            self.claim(t, r_out)
+        # x at the centering sumcheck's folded x; out, w, b at the output sumcheck's
+        self.claim(op.x, centered_r, centered.final(0))
+        self.claim(op.out, r_out, out.final(5))
+        self.claim(op.w, r_out, out.final(2))
+        self.claim(op.b, r_out, out.final(3))
         return lambda: LayerNormCenteredProof(mean(), centered(), var(), out(), r_mean, m_ch, centered_r, r_var,
                                               v_ch, r_out)
 

@@ -71,6 +71,110 @@ __global__ void __launch_bounds__(kFracThreads)
     }
 }
 
+// The tail of the tree in one launch: layer l with t = lg - l - 1 <= kSmallVars
+// variables is one block, which holds the layer's seven tables (eq from
+// full_r, the next level's num / den, the halves of level l) in shared
+// memory and runs all t rounds there: per round the four evaluations of
+//     I(k) = eq (next_num - num_lo den_hi - num_hi den_lo + c (next_den - den_lo den_hi))
+// at k = 0..3 (each table at f0 + k (f1 - f0)), summed over the pairs, then
+// the fold f <- f0 + r_j (f1 - f0).  The same sums as prove_virtual's,
+// without one eq-table launch and a few sumcheck launches per layer.
+constexpr uint32_t kSmallVars = 10;
+struct SmallTail {
+    uint64_t r[kMaxLg];
+    uint64_t c[kMaxLg];
+    const uint64_t* num[kMaxLg + 1];
+    const uint64_t* den[kMaxLg + 1];
+    uint64_t roff[kMaxLg];
+    uint32_t lg, l0;
+};
+
+__global__ void __launch_bounds__(kFracThreads) k_frac_small_layers(SmallTail T, uint64_t* __restrict__ rounds,
+                                                                    uint64_t* __restrict__ finals) {
+    extern __shared__ uint64_t sm[];
+    __shared__ uint64_t red[kFracThreads / 32][4];
+    const uint32_t l = T.l0 + blockIdx.x;
+    const uint32_t t = T.lg - l - 1;
+    const uint64_t half = 1ull << t;
+    uint64_t* tab[kFracMles];
+    for (uint32_t i = 0; i < kFracMles; i++) tab[i] = sm + i * half;
+    const uint64_t* num = T.num[l];
+    const uint64_t* den = T.den[l];
+    const uint64_t* nnum = T.num[l + 1];
+    const uint64_t* nden = T.den[l + 1];
+    for (uint64_t x = threadIdx.x; x < half; x += blockDim.x) {
+        uint64_t e = 1;
+        for (uint32_t j = 0; j < t; j++) {
+            const uint64_t rj = gl_canon(T.r[j]);
+            e = gl_mul(e, ((x >> j) & 1) ? rj : gl_sub(1, rj));
+        }
+        tab[0][x] = gl_canon(e);
+        tab[1][x] = gl_canon(nnum[x]);
+        tab[2][x] = gl_canon(nden[x]);
+        tab[3][x] = gl_canon(num[x]);
+        tab[4][x] = gl_canon(num[x + half]);
+        tab[5][x] = gl_canon(den[x]);
+        tab[6][x] = gl_canon(den[x + half]);
+    }
+    __syncthreads();
+    const uint64_t c = gl_canon(T.c[l]);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t len = half;
+    for (uint32_t j = 0; j < t; j++) {
+        const uint64_t pairs = len >> 1;
+        uint64_t acc[4] = {0, 0, 0, 0};
+        for (uint64_t q = threadIdx.x; q < pairs; q += blockDim.x) {
+            uint64_t v[kFracMles][4];
+            for (uint32_t i = 0; i < kFracMles; i++) {
+                const uint64_t a0 = tab[i][2 * q], a1 = tab[i][2 * q + 1];
+                const uint64_t d = gl_sub(a1, a0);
+                v[i][0] = a0;
+                v[i][1] = a1;
+                v[i][2] = gl_add(a1, d);
+                v[i][3] = gl_add(v[i][2], d);
+            }
+            for (int k = 0; k < 4; k++) {
+                const uint64_t dd = gl_mul(v[5][k], v[6][k]);
+                uint64_t in = gl_sub(v[1][k], gl_mul(v[3][k], v[6][k]));
+                in = gl_sub(in, gl_mul(v[4][k], v[5][k]));
+                in = gl_add(in, gl_mul(c, gl_sub(v[2][k], dd)));
+                acc[k] = gl_add(acc[k], gl_mul(v[0][k], in));
+            }
+        }
+        for (int k = 0; k < 4; k++) {
+            uint64_t a = acc[k];
+            for (int o = 16; o; o >>= 1) a = gl_add(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+            if (lane == 0) red[warp][k] = a;
+        }
+        __syncthreads();
+        if (threadIdx.x < 4) {
+            uint64_t a = 0;
+            for (int w = 0; w < kFracThreads / 32; w++) a = gl_add(a, red[w][threadIdx.x]);
+            rounds[T.roff[l] + 4ull * j + threadIdx.x] = gl_canon(a);
+        }
+        // fold: new values into registers, then one barrier, then the writes
+        const uint64_t rj = gl_canon(T.r[j]);
+        uint64_t nv[2][kFracMles];
+        for (int h = 0; h < 2; h++) {
+            const uint64_t x = threadIdx.x + (uint64_t)h * blockDim.x;
+            if (x < pairs)
+                for (uint32_t i = 0; i < kFracMles; i++) {
+                    const uint64_t a0 = tab[i][2 * x], a1 = tab[i][2 * x + 1];
+                    nv[h][i] = gl_canon(gl_add(a0, gl_mul(rj, gl_sub(a1, a0))));
+                }
+        }
+        __syncthreads();
+        for (int h = 0; h < 2; h++) {
+            const uint64_t x = threadIdx.x + (uint64_t)h * blockDim.x;
+            if (x < pairs)
+                for (uint32_t i = 0; i < kFracMles; i++) tab[i][x] = nv[h][i];
+        }
+        __syncthreads();
+        len = pairs;
+    }
+    if (threadIdx.x < kFracMles) finals[(uint64_t)kFracMles * l + threadIdx.x] = gl_canon(tab[threadIdx.x][0]);
+}
+
 __global__ void k_fraction_final(const uint64_t* num, const uint64_t* den, uint64_t* out) {
     if (threadIdx.x == 0) {
         out[0] = gl_canon(num[0]);
@@ -171,6 +275,23 @@ int frac_streams(cudaStream_t caller, FracStreams** out) {
 // :340-370: at least 32 rows, padding rows get den = alpha), and the table
 // side with caller multiplicities (build_lookup_table_num_den :285-301).
 enum : uint32_t { kLookupMerged = 0, kLookupWitness = 1, kLookupWitnessColumns = 2, kLookupTable = 3 };
+
+// the tail kernel's dynamic shared memory above 48 KB, set once per device
+std::mutex g_tail_mu;
+bool g_tail_ready[kMaxDevices];
+
+int small_tail_attr(size_t smem) {
+    if (smem <= 48 * 1024) return 0;
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_tail_mu);
+    if (!g_tail_ready[d]) {
+        ZK_TRY(cudaFuncSetAttribute(k_frac_small_layers, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)((size_t)kFracMles * (1ull << kSmallVars) * 8)));
+        g_tail_ready[d] = true;
+    }
+    return 0;
+}
 
 uint64_t next_pow2(uint64_t x) {
     uint64_t p = 1;
@@ -278,8 +399,17 @@ int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg
         rc = launch_fraction_layer(lnum[l], lden[l], n >> (l + 1), fs.num[l + 1], fs.den[l + 1], stream);
         if (!rc) rc = (int)cudaEventRecord(fst->level[l + 1], stream);
     }
+    // layers with more than kSmallVars variables: eq table and virtual
+    // sumcheck on a side stream each; the rest: one launch after the levels
+    const uint32_t l0 = lg_n > kSmallVars + 1 ? lg_n - kSmallVars - 1 : 0;
     uint64_t roff = 0;
+    SmallTail tail{};
     for (uint32_t l = 0; l < lg_n && !rc; l++) {
+        if (l >= l0) {
+            tail.roff[l] = roff;
+            roff += (uint64_t)(kFracDeg + 1) * (lg_n - l - 1);
+            continue;
+        }
         cudaStream_t ss = fst->s[l % kFracStreams];
         const uint64_t half = n >> (l + 1);
         const uint32_t t = lg_n - l - 1;
@@ -293,6 +423,25 @@ int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg
         rc = virtual_enqueue(mles, kFracMles, t, coeffs, off, idx, kFracTerms, h_full_r, fs.rounds + roff,
                              fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr[l], ss);
         roff += (uint64_t)(kFracDeg + 1) * t;
+    }
+    if (!rc && lg_n > l0) {
+        tail.lg = lg_n;
+        tail.l0 = l0;
+        for (uint32_t j = 0; j < lg_n; j++) {
+            tail.r[j] = h_full_r[j];
+            tail.c[j] = h_cs[j];
+        }
+        for (uint32_t l = 0; l <= lg_n; l++) {
+            tail.num[l] = lnum[l];
+            tail.den[l] = lden[l];
+        }
+        const uint32_t tmax = lg_n - l0 - 1;
+        const size_t smem = (size_t)kFracMles * (1ull << tmax) * 8;
+        rc = small_tail_attr(smem);
+        if (!rc) {
+            k_frac_small_layers<<<lg_n - l0, kFracThreads, smem, stream>>>(tail, fs.rounds, fs.finals);
+            rc = (int)cudaGetLastError();
+        }
     }
     // join the side streams (also after an error part-way, so that the
     // caller's synchronization covers everything enqueued)
