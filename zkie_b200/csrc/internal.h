@@ -65,7 +65,7 @@ uint64_t virtual_plan_elems(uint32_t n_mles, uint32_t t);
 int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
                     const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
                     uint64_t* d_rounds, uint64_t* d_finals, uint32_t* deg_out, uint64_t* d_scratch,
-                    cudaStream_t stream);
+                    cudaStream_t stream, bool tree_layer = false);
 int eq_table_dev(const uint64_t* h_r, uint32_t d, uint64_t* d_out, cudaStream_t s);
 // prove_fractional_with_challenges enqueued (logup.cu), outputs left in d_scratch
 int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg_n, const uint64_t* h_full_r,

@@ -133,12 +133,15 @@ __global__ void __launch_bounds__(kFracThreads) k_frac_small_layers(SmallTail T,
                 v[i][2] = gl_add(a1, d);
                 v[i][3] = gl_add(v[i][2], d);
             }
-            for (int k = 0; k < 4; k++) {
+            // in the layer's first round I vanishes at k = 0, 1 (the next level
+            // is the halves' fraction sum) and I(3) = 3 I(2)
+            for (int k = (j == 0 ? 2 : 0); k < (j == 0 ? 3 : 4); k++) {
                 const uint64_t dd = gl_mul(v[5][k], v[6][k]);
                 uint64_t in = gl_sub(v[1][k], gl_mul(v[3][k], v[6][k]));
                 in = gl_sub(in, gl_mul(v[4][k], v[5][k]));
                 in = gl_add(in, gl_mul(c, gl_sub(v[2][k], dd)));
                 acc[k] = gl_add(acc[k], gl_mul(v[0][k], in));
+                if (j == 0) acc[3] = gl_add(acc[3], gl_mul(v[0][3], gl_add(gl_add(in, in), in)));
             }
         }
         for (int k = 0; k < 4; k++) {
@@ -420,8 +423,9 @@ int fractional_enqueue(const uint64_t* d_num, const uint64_t* d_den, uint32_t lg
         const uint64_t coeffs[kFracTerms] = {1, GL_P - 1, GL_P - 1, c, gl_canon(GL_P - c)};
         const uint64_t* mles[kFracMles] = {fs.eq[l], lnum[l + 1], lden[l + 1], lnum[l], lnum[l] + half,
                                            lden[l], lden[l] + half};
+        // the next level was computed from this one: the first round's g(0), g(1) vanish
         rc = virtual_enqueue(mles, kFracMles, t, coeffs, off, idx, kFracTerms, h_full_r, fs.rounds + roff,
-                             fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr[l], ss);
+                             fs.finals + (uint64_t)kFracMles * l, nullptr, fs.vscr[l], ss, true);
         roff += (uint64_t)(kFracDeg + 1) * t;
     }
     if (!rc && lg_n > l0) {

@@ -63,6 +63,11 @@ struct VTerms {
     uint8_t idx[kVMaxFactors];
     int8_t other[kVMaxTerms];  // kShapeEqLinear: the second table of term i, -1 for [e] alone
     uint32_t n_terms, n_mles, deg, shape, common;
+    // kShapeFraction over a fraction-tree layer whose next-level tables were
+    // computed from its halves (nn = nl dh + nh dl, nd = dl dh at every
+    // boolean point): then I = 0 at every boolean point, so in the first
+    // round g(0) = g(1) = 0, I(3) = 3 I(2), and only I(2) is evaluated.
+    uint32_t tree_layer;
 };
 struct VIn {
     const uint64_t* p[kVMaxMles];
@@ -187,6 +192,18 @@ __global__ void __launch_bounds__(kVThreads)
                 acc160_mac(acc[0], ep.x, a0);
                 acc160_mac(acc[1], ep.y, a1);
                 acc160_mac(acc[2], gl_sub(gl_add(ep.y, ep.y), ep.x), gl_sub(gl_add(a1, a1), a0));
+            }
+        } else if (kShape == kShapeFraction && T.tree_layer && rd == 0) {
+            items = pairs;
+            for (uint32_t s = tid; s < pairs; s += kVThreads) {
+                const ulonglong2 eq = pair_of(0, s), nn = pair_of(1, s), nd = pair_of(2, s), nl = pair_of(3, s),
+                                 nh = pair_of(4, s), dl = pair_of(5, s), dh = pair_of(6, s);
+                auto f2 = [](ulonglong2 v) { return gl_add(v.y, gl_sub(v.y, v.x)); };
+                const uint64_t i2 = frac_inner(fc, f2(nn), f2(nd), f2(nl), f2(nh), f2(dl), f2(dh));
+                const uint64_t de = gl_sub(eq.y, eq.x);
+                const uint64_t e2 = gl_add(eq.y, de);
+                acc160_mac(acc[2], e2, i2);
+                acc160_mac(acc[3], gl_add(e2, de), gl_add(gl_add(i2, i2), i2));
             }
         } else if (kShape == kShapeFraction) {
             items = pairs;
@@ -447,21 +464,23 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
         if (G > 0x7FFFFFFFull) return (int)cudaErrorInvalidValue;
         VChal ch{};
         for (uint32_t i = 0; i < q; i++) ch.r[i] = h_ch[done + i];
+        VTerms Tl = T;
+        Tl.tree_layer = T.tree_layer && done == 0;
         const bool last = rem == q;
         uint64_t* out = last ? d_finals : buf[which];
         const uint64_t out_stride = last ? 1 : G;
         const size_t smem = ((size_t)12 * nm) << q;  // nm x (2^q + 2^(q-1)) u64
         int rc;
         if (T.shape == kShapeEqLinear)
-            rc = v_launch<2, kShapeEqLinear>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<2, kShapeEqLinear>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
         else if (T.shape == kShapeFraction)
-            rc = v_launch<3, kShapeFraction>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<3, kShapeFraction>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
         else if (T.deg <= 2)
-            rc = v_launch<2, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<2, kShapeGeneric>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
         else if (T.deg <= 4)
-            rc = v_launch<4, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<4, kShapeGeneric>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
         else
-            rc = v_launch<8, kShapeGeneric>((unsigned)G, smem, s, in, q, T, ch, partials, out, out_stride);
+            rc = v_launch<8, kShapeGeneric>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
         if (rc) return rc;
         ZK_LAUNCH_CHECK();
         uint64_t* rounds = d_rounds + (uint64_t)done * (T.deg + 1);
@@ -493,7 +512,7 @@ uint64_t virtual_plan_elems(uint32_t n_mles, uint32_t t) {
 int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, const uint64_t* coeffs,
                     const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
                     uint64_t* d_rounds, uint64_t* d_finals, uint32_t* deg_out, uint64_t* d_scratch,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, bool tree_layer) {
     if (!d_mles || !d_finals || !d_scratch || n_mles == 0 || n_mles > (uint32_t)kVMaxMles || t > 40 ||
         n_terms > (uint32_t)kVMaxTerms || (n_terms && (!coeffs || !idx_off)) || (t && (!h_ch || !d_rounds)))
         return (int)cudaErrorInvalidValue;
@@ -520,6 +539,7 @@ int virtual_enqueue(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t t, 
     }
     T.deg = deg;
     v_classify(T);
+    T.tree_layer = tree_layer && T.shape == kShapeFraction;
     for (uint32_t j = 0; j < n_mles; j++)
         if (!d_mles[j]) return (int)cudaErrorInvalidValue;
     if (deg_out) *deg_out = deg;
@@ -548,7 +568,7 @@ int zkie2_virtual_prove(const uint64_t* const* d_mles, uint32_t n_mles, uint32_t
     uint64_t* d_finals = d_rounds + (uint64_t)t * (kVMaxDeg + 1);
     uint32_t deg = 0;
     int rc = virtual_enqueue(d_mles, n_mles, t, coeffs, idx_off, idx, n_terms, h_ch, d_rounds, d_finals, &deg,
-                             d_scratch, stream);
+                             d_scratch, stream, false);
     if (rc) return rc;
     if (t) ZK_TRY(cudaMemcpyAsync(h_rounds, d_rounds, 8ull * t * (deg + 1), cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaMemcpyAsync(h_finals, d_finals, 8ull * n_mles, cudaMemcpyDeviceToHost, stream));
@@ -562,7 +582,7 @@ int zkie2_virtual_prove_async(const uint64_t* const* d_mles, uint32_t n_mles, ui
                               const uint32_t* idx_off, const uint32_t* idx, uint32_t n_terms, const uint64_t* h_ch,
                               uint64_t* d_rounds, uint64_t* d_finals, uint64_t* d_scratch, cudaStream_t stream) {
     return virtual_enqueue(d_mles, n_mles, t, coeffs, idx_off, idx, n_terms, h_ch, d_rounds, d_finals, nullptr,
-                           d_scratch, stream);
+                           d_scratch, stream, false);
 }
 
 }  // extern "C"
