@@ -24,7 +24,11 @@
 // same field elements as k f1 - (k - 1) f0, and the last factor of every
 // term product is multiplied into an exact Acc160 sum (one reduction per
 // round and evaluation point instead of one per product).
+#include <cuda_pipeline.h>
+
 #include <atomic>
+#include <map>
+#include <mutex>
 
 #include "../../include/zkie2.h"
 #include "common.cuh"
@@ -131,7 +135,7 @@ __device__ __forceinline__ uint64_t frac_inner(uint64_t c, uint64_t nn, uint64_t
 // where the per-pair lookups by term and factor index are cheap.
 template <int kF, uint32_t kShape>
 __global__ void __launch_bounds__(kVThreads)
-    k_virtual_chunk(VIn in, uint32_t q, VTerms T, VChal ch, uint64_t* __restrict__ partials,
+    k_virtual_chunk(VIn in, uint32_t q, uint64_t chunks, VTerms T, VChal ch, uint64_t* __restrict__ partials,
                     uint64_t* __restrict__ out, uint64_t out_stride) {
     constexpr int kV = pow2_ceil(kF + 1);
     extern __shared__ __align__(16) uint64_t sm[];
@@ -149,20 +153,45 @@ __global__ void __launch_bounds__(kVThreads)
     if (tid <= kVMaxTerms) s_off[tid] = T.off[tid];
     if (tid < kVMaxFactors) s_idx[tid] = T.idx[tid];
     if (tid < kVMaxQ) s_ch[tid] = ch.r[tid];
-    const uint64_t base = (uint64_t)blockIdx.x << q;
+    // Shared memory: two chunk buffers (nm x Q each) and one half-size
+    // buffer.  The block walks chunks blockIdx.x, + gridDim.x, ...; while it
+    // runs the rounds of one chunk out of one buffer (and the half buffer),
+    // cp.async fills the other with the next chunk.
+    uint64_t* const buf0 = sm;
+    uint64_t* const buf1 = sm + (size_t)nm * Q;
+    uint64_t* const half_buf = sm + 2 * (size_t)nm * Q;
+    const uint64_t n_chunks = chunks;
+    auto prefetch = [&](uint64_t chunk, uint64_t* dst) {
+        const uint64_t base = chunk << q;
 #pragma unroll
-    for (int j = 0; j < kVMaxMles; j++) {
-        if ((uint32_t)j < nm) {
+        for (uint32_t j = 0; j < (uint32_t)kVMaxMles; j++) {
+            if (j >= nm) break;
             const uint64_t* src = in.p[j] + base;
-            for (uint32_t i = tid; i < Q; i += kVThreads) sm[j * Q + i] = __ldg(src + i);
+            uint64_t* d = dst + (size_t)j * Q;
+            if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(d)) & 15) == 0) {
+                for (uint32_t i = 2 * tid; i < Q; i += 2 * kVThreads) __pipeline_memcpy_async(d + i, src + i, 16);
+            } else {
+                for (uint32_t i = tid; i < Q; i += kVThreads) __pipeline_memcpy_async(d + i, src + i, 8);
+            }
         }
-    }
-    __syncthreads();
-    uint64_t* cur = sm;
-    uint64_t* nxt = sm + (size_t)nm * Q;
-    uint32_t sc = Q, sn = Q >> 1;
+        __pipeline_commit();
+    };
     const uint32_t e = T.common;
     const uint64_t fc = T.coeff[3];  // the logUp layer's c
+    uint32_t which = 0;
+    if ((uint64_t)blockIdx.x < n_chunks) prefetch(blockIdx.x, buf0);
+    for (uint64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
+    const uint64_t next = chunk + gridDim.x;
+    if (next < n_chunks) {
+        prefetch(next, which ? buf0 : buf1);
+        __pipeline_wait_prior(1);
+    } else {
+        __pipeline_wait_prior(0);
+    }
+    __syncthreads();
+    uint64_t* cur = which ? buf1 : buf0;
+    uint64_t* nxt = half_buf;
+    uint32_t sc = Q, sn = Q >> 1;
     for (uint32_t rd = 0; rd < q; rd++) {
         const uint32_t lg_pairs = q - 1 - rd, pairs = 1u << lg_pairs;
         const uint64_t r = s_ch[rd];
@@ -285,7 +314,7 @@ __global__ void __launch_bounds__(kVThreads)
             const uint32_t nw = items >= (uint32_t)kVThreads ? kVThreads / 32 : (items + 31) / 32;
             uint64_t v = 0;  // no terms: every round sends zeros
             for (uint32_t w = 0; w < nw; w++) v = gl_add(v, red[rd & 1][w][tid]);
-            partials[((uint64_t)blockIdx.x * q + rd) * (deg + 1) + tid] = v;
+            partials[(chunk * q + rd) * (deg + 1) + tid] = v;
         }
         uint64_t* t = cur;
         cur = nxt;
@@ -294,7 +323,10 @@ __global__ void __launch_bounds__(kVThreads)
         sc = sn;
         sn = ts;
     }
-    if (tid < nm) out[tid * out_stride + blockIdx.x] = gl_canon(cur[(size_t)tid * sc]);
+    if (tid < nm) out[tid * out_stride + chunk] = gl_canon(cur[(size_t)tid * sc]);
+    __syncthreads();  // the buffers are reused by the next chunk
+    which ^= 1;
+    }
 }
 
 // rounds[rd * (d + 1) + k] = sum over the G chunks of their partial sums.
@@ -344,12 +376,12 @@ __global__ void k_virtual_t0(VIn in, uint32_t nm, uint64_t* __restrict__ out) {
     if (j < nm) out[j] = gl_canon(in.p[j][0]);
 }
 
-// Rounds per launch for n_mles tables: the chunk and its half-size ping-pong
-// buffer (12 bytes per table per position) fit in 46 KB of dynamic shared
-// memory (under the 48 KB default limit together with the static part).
+// Rounds per launch for n_mles tables: two chunk buffers and a half-size
+// ping-pong buffer (20 bytes per table per position) fit in 46 KB of dynamic
+// shared memory (under the 48 KB default limit together with the static part).
 uint32_t v_qmax(uint32_t nm) {
     uint32_t q = 1;
-    while (q < (uint32_t)kVQCap && 12ull * nm * (2ull << q) <= kVSmemBytes) q++;
+    while (q < (uint32_t)kVQCap && 20ull * nm * (2ull << q) <= kVSmemBytes) q++;
     return q;
 }
 
@@ -376,17 +408,37 @@ VPlan v_plan(uint32_t nm, uint32_t t) {
 // Launch of one chunk-kernel instantiation; the first launch on each device
 // asks for the largest shared-memory carveout (more resident blocks: a block
 // stages 12 bytes per table and position, e.g. 21 KB for seven tables).
+// The grid is one wave of resident blocks (the occupancy of this shared
+// memory size, queried once per device and size), each walking its chunks.
 template <int kF, uint32_t kShape>
 int v_launch(unsigned G, size_t smem, cudaStream_t s, const VIn& in, uint32_t q, const VTerms& T, const VChal& ch,
              uint64_t* partials, uint64_t* out, uint64_t out_stride) {
     static std::atomic<bool> carved[kMaxDevices];
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, unsigned> waves;
     const int d = current_device();
     if (d >= 0 && d < kMaxDevices && !carved[d].load(std::memory_order_relaxed)) {
         ZK_TRY(cudaFuncSetAttribute(k_virtual_chunk<kF, kShape>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     (int)cudaSharedmemCarveoutMaxShared));
         carved[d].store(true, std::memory_order_relaxed);
     }
-    k_virtual_chunk<kF, kShape><<<G, kVThreads, smem, s>>>(in, q, T, ch, partials, out, out_stride);
+    unsigned wave = 0;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = waves.find({d, smem});
+        if (it == waves.end()) {
+            int per_sm = 0, sms = 0;
+            ZK_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_virtual_chunk<kF, kShape>, kVThreads,
+                                                                 smem));
+            ZK_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d));
+            wave = (unsigned)((per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 1));
+            waves[{d, smem}] = wave;
+        } else {
+            wave = it->second;
+        }
+    }
+    const unsigned grid = G < wave ? G : wave;
+    k_virtual_chunk<kF, kShape><<<grid, kVThreads, smem, s>>>(in, q, G, T, ch, partials, out, out_stride);
     ZK_LAUNCH_CHECK();
     return 0;
 }
@@ -469,7 +521,7 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
         const bool last = rem == q;
         uint64_t* out = last ? d_finals : buf[which];
         const uint64_t out_stride = last ? 1 : G;
-        const size_t smem = ((size_t)12 * nm) << q;  // nm x (2^q + 2^(q-1)) u64
+        const size_t smem = ((size_t)20 * nm) << q;  // nm x (2 x 2^q + 2^(q-1)) u64
         int rc;
         if (T.shape == kShapeEqLinear)
             rc = v_launch<2, kShapeEqLinear>((unsigned)G, smem, s, in, q, Tl, ch, partials, out, out_stride);
