@@ -27,7 +27,7 @@ def assert_same(got, ref):
     assert (got.final_num, got.final_den) == (fn, fd)
 
 
-@pytest.mark.parametrize("lg", [0, 1, 2, 3, 6, 9, 10, 11, 13, 16])
+@pytest.mark.parametrize("lg", [0, 1, 2, 3, 6, 9, 10, 11, 13, 16, 18, 20])
 def test_fractional_matches_oracle(zk, orc, lg):
     n = 1 << lg
     num, den = fields(10 + lg, n, noncanon=True), fields(20 + lg, n, noncanon=True)

@@ -376,6 +376,170 @@ __global__ void k_virtual_t0(VIn in, uint32_t nm, uint64_t* __restrict__ out) {
     if (j < nm) out[j] = gl_canon(in.p[j][0]);
 }
 
+// The early rounds of a large set of tables, one launch per round: thread s
+// evaluates pair s of every table straight from HBM (16-byte loads, pair s
+// of table j at p_j[2s], p_j[2s + 1]), adds its share of the round message
+// and writes the pair's folded value of every table; each block writes one
+// partial per evaluation point.  Every thread has a pair, so these rounds
+// stream at memory speed, where the chunk kernel's later in-chunk rounds
+// leave most of a block idle.  The per-pair values are the chunk kernel's.
+constexpr int kSThreads = 256;
+constexpr uint32_t kStreamMinVars = 16;  // rounds over more than 2^16 positions stream
+constexpr unsigned kSMaxBlocks = 148 * 8;
+
+template <int kF, uint32_t kShape>
+__global__ void __launch_bounds__(kSThreads)
+    k_virtual_stream(VIn in, uint64_t pairs, VTerms T, uint64_t r, uint64_t* __restrict__ partials,
+                     uint64_t* __restrict__ out) {
+    constexpr int kV = pow2_ceil(kF + 1);
+    __shared__ uint64_t red[kSThreads / 32][kF + 1];
+    __shared__ const uint64_t* s_p[kVMaxMles];
+    __shared__ uint64_t s_coeff[kVMaxTerms];
+    __shared__ uint32_t s_off[kVMaxTerms + 1], s_idx[kVMaxFactors];
+    __shared__ int32_t s_other[kVMaxTerms];
+    const uint32_t nm = T.n_mles, deg = T.deg, nt = T.n_terms;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid < kVMaxMles) s_p[tid] = in.p[tid];
+    if (tid < kVMaxTerms) {
+        s_coeff[tid] = T.coeff[tid];
+        s_other[tid] = T.other[tid];
+    }
+    if (tid <= kVMaxTerms) s_off[tid] = T.off[tid];
+    if (tid < kVMaxFactors) s_idx[tid] = T.idx[tid];
+    __syncthreads();
+    Acc160 acc[kF + 1];
+#pragma unroll
+    for (int k = 0; k <= kF; k++) acc[k] = acc160_zero();
+    const uint64_t fc = T.coeff[3];
+    const bool tree0 = kShape == kShapeFraction && T.tree_layer;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + tid; s < pairs; s += stride) {
+        auto pr = [&](uint32_t j) { return __ldg(reinterpret_cast<const ulonglong2*>(s_p[j]) + s); };
+        if (kShape == kShapeFraction) {
+            const ulonglong2 eq = pr(0), nn = pr(1), nd = pr(2), nl = pr(3), nh = pr(4), dl = pr(5), dh = pr(6);
+            auto f2 = [](ulonglong2 v) { return gl_add(v.y, gl_sub(v.y, v.x)); };
+            const uint64_t i2 = frac_inner(fc, f2(nn), f2(nd), f2(nl), f2(nh), f2(dl), f2(dh));
+            const uint64_t de = gl_sub(eq.y, eq.x);
+            const uint64_t e2 = gl_add(eq.y, de);
+            if (tree0) {
+                acc160_mac(acc[2], e2, i2);
+                acc160_mac(acc[3], gl_add(e2, de), gl_add(gl_add(i2, i2), i2));
+            } else {
+                const uint64_t i0 = frac_inner(fc, nn.x, nd.x, nl.x, nh.x, dl.x, dh.x);
+                const uint64_t i1 = frac_inner(fc, nn.y, nd.y, nl.y, nh.y, dl.y, dh.y);
+                const uint64_t d21 = gl_sub(i2, i1);
+                const uint64_t i3 = gl_add(i0, gl_add(gl_add(d21, d21), d21));
+                acc160_mac(acc[0], eq.x, i0);
+                acc160_mac(acc[1], eq.y, i1);
+                acc160_mac(acc[2], e2, i2);
+                acc160_mac(acc[3], gl_add(e2, de), i3);
+            }
+        } else if (kShape == kShapeEqLinear) {
+            const ulonglong2 ep = pr(T.common);
+            Acc160 i0 = acc160_zero(), i1 = acc160_zero();
+            for (uint32_t ti = 0; ti < nt; ti++) {
+                const int32_t o = s_other[ti];
+                const uint64_t c = s_coeff[ti];
+                if (o < 0) {
+                    acc160_add(i0, c);
+                    acc160_add(i1, c);
+                } else {
+                    const ulonglong2 fp = pr((uint32_t)o);
+                    acc160_mac(i0, c, fp.x);
+                    acc160_mac(i1, c, fp.y);
+                }
+            }
+            const uint64_t a0 = acc160_reduce(i0), a1 = acc160_reduce(i1);
+            acc160_mac(acc[0], ep.x, a0);
+            acc160_mac(acc[1], ep.y, a1);
+            acc160_mac(acc[2], gl_sub(gl_add(ep.y, ep.y), ep.x), gl_sub(gl_add(a1, a1), a0));
+        } else {
+            for (uint32_t ti = 0; ti < nt; ti++) {
+                const uint32_t o0 = s_off[ti], nf = s_off[ti + 1] - o0;
+                const uint64_t c = s_coeff[ti];
+                uint64_t fv[kF], dv[kF];
+#pragma unroll
+                for (int f = 0; f < kF; f++) {
+                    fv[f] = 1;
+                    dv[f] = 0;
+                    if ((uint32_t)f < nf) {
+                        const ulonglong2 pp = pr(s_idx[o0 + f]);
+                        fv[f] = pp.x;
+                        dv[f] = gl_sub(pp.y, pp.x);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k <= kF; k++) {
+                    if ((uint32_t)k <= deg) {
+                        uint64_t p = c, last = 1;
+#pragma unroll
+                        for (int f = 0; f < kF; f++) {
+                            if ((uint32_t)f + 1 < nf) p = gl_mul(p, fv[f]);
+                            else if ((uint32_t)f + 1 == nf) last = fv[f];
+                        }
+                        acc160_mac(acc[k], p, last);
+                        if ((uint32_t)k < deg) {
+#pragma unroll
+                            for (int f = 0; f < kF; f++)
+                                if ((uint32_t)f < nf) fv[f] = gl_add(fv[f], dv[f]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < (uint32_t)kVMaxMles; j++) {
+            if (j >= nm) break;
+            const ulonglong2 pp = pr(j);
+            out[(uint64_t)j * pairs + s] = gl_canon(gl_add(pp.x, gl_mul(r, gl_sub(pp.y, pp.x))));
+        }
+    }
+    uint64_t v[kV];
+#pragma unroll
+    for (int k = 0; k < kV; k++) v[k] = (k <= kF && (uint32_t)k <= deg) ? acc160_reduce(acc[k < kF + 1 ? k : 0]) : 0;
+    const uint64_t tot = warp_multi_sum<kV>(v);
+    const uint32_t kk = lane / (32 / kV);
+    if (lane % (32 / kV) == 0 && kk <= deg) red[warp][kk] = tot;
+    __syncthreads();
+    if (tid <= deg) {
+        uint64_t a = 0;
+        for (int w = 0; w < kSThreads / 32; w++) a = gl_add(a, red[w][tid]);
+        partials[(uint64_t)blockIdx.x * (deg + 1) + tid] = a;
+    }
+}
+
+// One wave of resident blocks of a streaming kernel (queried once per device).
+template <int kF, uint32_t kShape>
+unsigned s_wave() {
+    static std::atomic<unsigned> wave[kMaxDevices];
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return kSMaxBlocks;
+    unsigned w = wave[d].load(std::memory_order_relaxed);
+    if (!w) {
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_virtual_stream<kF, kShape>, kSThreads, 0) !=
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess)
+            return kSMaxBlocks;
+        w = (unsigned)((per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 1));
+        w = w < kSMaxBlocks ? w : kSMaxBlocks;
+        wave[d].store(w, std::memory_order_relaxed);
+    }
+    return w;
+}
+
+template <int kF, uint32_t kShape>
+int s_launch(uint64_t pairs, cudaStream_t s, const VIn& in, const VTerms& T, uint64_t r, uint64_t* partials,
+             uint64_t* out, unsigned* grid_out) {
+    const uint64_t want = (pairs + kSThreads - 1) / kSThreads;
+    const unsigned wave = s_wave<kF, kShape>();
+    const unsigned grid = (unsigned)(want < wave ? want : wave);
+    k_virtual_stream<kF, kShape><<<grid, kSThreads, 0, s>>>(in, pairs, T, r, partials, out);
+    *grid_out = grid;
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
 // Rounds per launch for n_mles tables: two chunk buffers and a half-size
 // ping-pong buffer (20 bytes per table per position) fit in 46 KB of dynamic
 // shared memory (under the 48 KB default limit together with the static part).
@@ -386,19 +550,26 @@ uint32_t v_qmax(uint32_t nm) {
 }
 
 struct VPlan {
-    uint64_t g1;     // chunks of the first level (= folded length it leaves)
-    uint32_t q1;     // rounds of the first level
-    uint64_t elems;  // scratch u64
+    uint64_t g1;            // chunks of the first chunk level (= folded length it leaves)
+    uint32_t q1;            // rounds of the first chunk level
+    uint64_t stream_elems;  // the streaming rounds' two folded buffers and partials (0: none)
+    uint64_t elems;         // scratch u64
 };
 
+// The scratch: the streaming region (when t > kStreamMinVars: folded
+// buffers of nm x 2^(t-1) and nm x 2^(t-2), then kSMaxBlocks partials per
+// evaluation point), then the chunk region, sized for t (it also serves the
+// fallback without streaming).
 VPlan v_plan(uint32_t nm, uint32_t t) {
     VPlan p{};
     const uint32_t qm = v_qmax(nm);
     p.q1 = t < qm ? t : qm;
     p.g1 = 1ull << (t - p.q1);
+    if (t > kStreamMinVars)
+        p.stream_elems = (uint64_t)nm * (3ull << (t - 2)) + (uint64_t)kSMaxBlocks * (kVMaxDeg + 1) + 8;
     // two folded buffers (nm x g1, 16-byte aligned) + the first level's partials
     // + the first reduce stage's block sums
-    p.elems = 2 * ((nm * p.g1 + 1) & ~1ull) + p.g1 * (p.q1 ? p.q1 : 1) * (kVMaxDeg + 1) + 8 +
+    p.elems = p.stream_elems + 2 * ((nm * p.g1 + 1) & ~1ull) + p.g1 * (p.q1 ? p.q1 : 1) * (kVMaxDeg + 1) + 8 +
               (uint64_t)kVRedBlocks * kVMaxQ * (kVMaxDeg + 1);
     return p;
 }
@@ -504,11 +675,47 @@ int virtual_dev(const uint64_t* const* d_mles, uint32_t nm, uint32_t t, const VT
     }
     const VPlan plan = v_plan(nm, t);
     const uint32_t qm = v_qmax(nm);
+    uint32_t done = 0;
+    // the streaming rounds (16-byte aligned tables only)
+    bool aligned = true;
+    for (uint32_t j = 0; j < nm; j++) aligned = aligned && (reinterpret_cast<uintptr_t>(in.p[j]) & 15) == 0;
+    if (plan.stream_elems && aligned) {
+        uint64_t* sbuf[2] = {d_scratch, d_scratch + (uint64_t)nm * (1ull << (t - 1))};
+        uint64_t* spart = d_scratch + (uint64_t)nm * (3ull << (t - 2));
+        uint32_t sw = 0;
+        while (t - done > kStreamMinVars) {
+            const uint64_t pairs = 1ull << (t - done - 1);
+            VTerms Tl = T;
+            Tl.tree_layer = T.tree_layer && done == 0;
+            uint64_t* out = sbuf[sw];
+            const uint64_t r = h_ch[done];
+            unsigned grid = 0;
+            int rc;
+            if (T.shape == kShapeEqLinear)
+                rc = s_launch<2, kShapeEqLinear>(pairs, s, in, Tl, r, spart, out, &grid);
+            else if (T.shape == kShapeFraction)
+                rc = s_launch<3, kShapeFraction>(pairs, s, in, Tl, r, spart, out, &grid);
+            else if (T.deg <= 2)
+                rc = s_launch<2, kShapeGeneric>(pairs, s, in, Tl, r, spart, out, &grid);
+            else if (T.deg <= 4)
+                rc = s_launch<4, kShapeGeneric>(pairs, s, in, Tl, r, spart, out, &grid);
+            else
+                rc = s_launch<8, kShapeGeneric>(pairs, s, in, Tl, r, spart, out, &grid);
+            if (rc) return rc;
+            k_virtual_reduce<<<T.deg + 1, kVThreads, 0, s>>>(spart, grid, 1, T.deg,
+                                                             d_rounds + (uint64_t)done * (T.deg + 1));
+            ZK_LAUNCH_CHECK();
+            for (uint32_t j = 0; j < nm; j++) in.p[j] = out + j * pairs;
+            sw ^= 1;
+            done++;
+        }
+    }
+    uint64_t* const chunk_base = d_scratch + plan.stream_elems;
     const uint64_t bufsz = (nm * plan.g1 + 1) & ~1ull;
-    uint64_t* buf[2] = {d_scratch, d_scratch + bufsz};
-    uint64_t* partials = d_scratch + 2 * bufsz;
+    uint64_t* buf[2] = {chunk_base, chunk_base + bufsz};
+    uint64_t* partials = chunk_base + 2 * bufsz;
     uint64_t* block_sums = partials + plan.g1 * (plan.q1 ? plan.q1 : 1) * (kVMaxDeg + 1) + 8;
-    uint32_t done = 0, which = 0;
+    uint32_t which = 0;
     while (done < t) {
         const uint32_t rem = t - done;
         const uint32_t q = rem < qm ? rem : qm;
