@@ -788,8 +788,8 @@ def measured_traffic(lg_l, w, lg_b, world):
 def next_rows(want_cpu, lg_frac=22, grind_bits=24):
     """The logUp fraction tree (prove_fractional_with_challenges, 2^22
     fractions, inputs resident) and PoW grinding (24 bits) on the device, each
-    with the CPU oracle port timed beside it on a bounded sample (one thread:
-    a 2^18-fraction tree; a 16-bit grind)."""
+    with the CPU oracle port timed beside it on a bounded sample (a
+    2^18-fraction tree on every host thread; a 16-bit grind on one)."""
     import types
 
     from perfcases import case_fixed, case_grind, case_logup
@@ -816,10 +816,12 @@ def next_rows(want_cpu, lg_frac=22, grind_bits=24):
         g = np.random.default_rng(1)
         n = 1 << 18
         num, den = g.integers(0, P, size=n, dtype=np.uint64), g.integers(1, P, size=n, dtype=np.uint64)
+        orc.set_threads(host_threads())
         t0 = time.perf_counter()
         orc.fractional_prove(num, den, list(range(3, 21)), list(range(5, 23)))
         s_frac = time.perf_counter() - t0
-        out["logup"]["cpu_baseline"] = {"value": round(n / s_frac / 1e6, 4), "unit": "Mfractions/s", "cores": 1,
+        out["logup"]["cpu_baseline"] = {"value": round(n / s_frac / 1e6, 4), "unit": "Mfractions/s",
+                                        "cores": host_threads(),
                                         "kind": "port", "label": CPU_LABEL, "sample": "2^18-fraction tree, oracle/zkie_oracle.c"}
         consts = orc.p2_constants(1)
         sponge = [(0x9E3779B97F4A7C15 * (i + 1)) % P for i in range(16)]
@@ -944,8 +946,8 @@ def projection_case(zk, dev, want_cpu, m=512, k=1024, n=4096, shift=16, iters=5)
         dt = time.perf_counter() - t0
         out_d["cpu_baseline"] = {"value": round(1e3 * dt, 1), "unit": "ms per projection", "cores": host_threads(),
                                  "kind": "port", "label": CPU_LABEL,
-                                 "sample": "the same projection once by oracle/zkie_oracle.c (field matmul on all "
-                                           "threads, the sumchecks and the fraction tree on one)"}
+                                 "sample": "the same projection once by oracle/zkie_oracle.c (fixed-point matmul, "
+                                           "sumcheck rounds and fraction layers on every host thread)"}
     del x, w, b, h, out, rem, idx
     torch.cuda.empty_cache()
     return out_d
