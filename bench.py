@@ -1069,9 +1069,11 @@ def cfg4_case(zk, dev, rank, world, layers=12):
     :2289-2346): rank r proves the shards si % world == r, each recorded once
     as a CUDA graph and replayed; rank 0 gathers the claims and binds the
     tensors claimed by two shards (the layer boundaries) with the master
-    transcript.  Every rank holds the whole witness (the forward pass of all
-    12 layers).  Not assembled: the embedding lookup into the tied token
-    table, the final LayerNorm, the lm_head matmul and the argmax."""
+    transcript and commits each of them as prove_committed_shard_dag does
+    (Whir::with_params(arity, 90, 17)).  Every rank holds the whole witness
+    (the forward pass of all 12 layers).  Not assembled: the embedding lookup
+    into the tied token table, the final LayerNorm, the lm_head matmul and the
+    argmax; not built: the WHIR openings of the committed path."""
     import torch
     import torch.distributed as dist
 
@@ -1129,7 +1131,10 @@ def cfg4_case(zk, dev, rank, world, layers=12):
             "layers_per_s": round(layers / (ms / 1e3), 2), "forward_ms": round(fwd_ms, 3),
             "record_ms": round(1e3 * record_s, 1), "build_s": round(build_s, 2),
             "shards": len(res.shards), "max_shards_per_gpu": -(-len(res.shards) // world),
-            "cross_tensors": len(res.cross_tensors), "digest": res.digest,
+            "cross_tensors": len(res.cross_tensors),
+            "boundary_commits": f"{len(res.boundary_roots)} WHIR base commits of the cross-shard tensors "
+                                "(prove_committed_shard_dag's boundary commitments; their openings are not built)",
+            "digest": res.digest,
             "digest_matches_eager_one_gpu": res.digest == check.digest,
         }
     del st, provers

@@ -23,11 +23,13 @@ def oracle_provers():
         c = o.OracleTranscript(raw=m.t)
         c.absorb_u64(si)
         return c
+    consts = o.p2_constants(1)
     return dag.DagProvers(
         master=co.master_transcript, child=child,
         prove=lambda store, ops, rng: co.prove_shard_precomputed(store, ops, [], rng),
         claims=lambda p: p["claims"], summary=lambda p: p,
-        same_poly=lambda store, t, cs, m: co.prove_same_poly(store.get(t), cs, m))
+        same_poly=lambda store, t, cs, m: co.prove_same_poly(store.get(t), cs, m),
+        commit=lambda store, t: o.whir_commit(consts, store.get(t))[1])
 
 
 def stack(layers):
@@ -40,7 +42,9 @@ def stack(layers):
 def _want(layers, ops_per_shard):
     st, ops = stack(layers)
     full = co.prove_shard_dag(st, ops, ops_per_shard)
-    return dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"]), full
+    consts = o.p2_constants(1)
+    roots = [o.whir_commit(consts, st.get(t))[1] for t in full["cross_tensors"]]
+    return dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"], roots), full
 
 
 def test_layers_chain():

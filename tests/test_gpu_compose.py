@@ -181,4 +181,7 @@ def test_dag_ranks_device_matches_oracle(zk, graph):
         assert len(provers.graphs) == 3
     co.forward_ops(host, ops)
     full = co.prove_shard_dag(host, ops, per)
-    assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"])
+    consts = o.p2_constants(1)
+    roots = [o.whir_commit(consts, host.get(t))[1] for t in full["cross_tensors"]]
+    assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"], roots)
+    assert len(got.boundary_roots) == len(full["cross_tensors"])

@@ -71,22 +71,29 @@ class DagProvers:
     claims: Callable
     summary: Callable
     same_poly: Callable
+    commit: Callable = None  # (store, tensor) -> the WHIR base commitment's root (8 values)
 
 
 @dataclass
 class DagResult:
     """Rank 0's view: every shard's summary in shard order, the cross-shard
-    tensors and their bindings (canonical), and the DAG digest."""
+    tensors and their bindings (canonical), the roots of the cross-shard
+    tensors' WHIR base commitments (when the provers commit), and the DAG
+    digest."""
     shards: List
     cross_tensors: List[int]
     cross_binds: List
     digest: str
+    boundary_roots: List = None
 
 
-def dag_digest(shard_summaries, cross_tensors, cross_binds) -> str:
+def dag_digest(shard_summaries, cross_tensors, cross_binds, boundary_roots=None) -> str:
     parts = [s if isinstance(s, str) or s is None else digest(s) for s in shard_summaries]
     parts = ["" if s is None else s for s in parts]
-    return digest([parts, list(cross_tensors), [b for b in cross_binds]])
+    body = [parts, list(cross_tensors), [b for b in cross_binds]]
+    if boundary_roots is not None:
+        body.append([np.asarray(r, dtype=np.uint64) for r in boundary_roots])
+    return digest(body)
 
 
 def prove_dag_ranks(store, ops, ops_per_shard: int, provers: DagProvers, rank: int = 0, world: int = 1,
@@ -116,7 +123,11 @@ def prove_dag_ranks(store, ops, ops_per_shard: int, provers: DagProvers, rank: i
     cross = [t for t in sorted(by_tensor) if len(owners[t]) > 1]
     binds = [provers.same_poly(store, t, by_tensor[t], master) for t in cross]
     summaries = [x[2] for x in by_shard]
-    return DagResult(summaries, cross, binds, dag_digest(summaries, cross, binds))
+    # prove_committed_shard_dag (compose.rs:2796-2806) commits every
+    # cross-shard tensor with Whir::with_params(arity, 90, 17); its openings
+    # (committed_cross_bind) are not part of this prover
+    roots = [provers.commit(store, t) for t in cross] if provers.commit else None
+    return DagResult(summaries, cross, binds, dag_digest(summaries, cross, binds, roots), roots)
 
 
 def torch_gather(group=None):
@@ -177,6 +188,11 @@ def device_provers(summary: str = "digest", graph: bool = False, streams: int = 
         pr.pend.fetch()
         return b().canonical()
 
-    p = DagProvers(master, child, prove, claims, summ, same_poly)
+    def commit(store, t):
+        from .commit import Whir
+        v = store.get(t)
+        return Whir.with_params(v.numel().bit_length() - 1, 90, 17).commit(v).root
+
+    p = DagProvers(master, child, prove, claims, summ, same_poly, commit)
     p.graphs = graphs
     return p
