@@ -567,7 +567,7 @@ def main_split(args, zk, dev, world, rank):
     line["split_sumcheck"] = split_sc
     line["mg_c_abi"] = mg
     if cfg4:
-        line["cfg4_gpt2_12_layers"] = cfg4
+        line["cfg4_gpt2_model"] = cfg4
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
@@ -717,7 +717,7 @@ def main():
     extra["projection"] = projection_case(zk, dev, want_cpu=not args.no_cpu)
     extra["layer_shard"] = layer_case(zk, dev, want_cpu=not args.no_cpu)
     if not args.no_cfg4:
-        extra["cfg4_gpt2_12_layers"] = cfg4_case(zk, dev, 0, 1)
+        extra["cfg4_gpt2_model"] = cfg4_case(zk, dev, 0, 1)
     # ---- configurations 2 (256 x 2^24) and 5 (expert stack); the 2^28 sumcheck ----
     del d_in, d_lde, d_layers, d_scr
     torch.cuda.empty_cache()
@@ -1063,17 +1063,18 @@ def layer_case(zk, dev, want_cpu, iters=5):
 
 
 def cfg4_case(zk, dev, rank, world, layers=12):
-    """Configuration 4: GPT-2-small's 12 layers chained as build_gpt2 chains
-    them (models/gpt2/src/lib.rs:367-372), proven as a shard DAG with one
-    layer per shard (ops_per_shard 176; compose.rs prove_shard_dag
-    :2289-2346): rank r proves the shards si % world == r, each recorded once
-    as a CUDA graph and replayed; rank 0 gathers the claims and binds the
-    tensors claimed by two shards (the layer boundaries) with the master
-    transcript and commits each of them as prove_committed_shard_dag does
-    (Whir::with_params(arity, 90, 17)).  Every rank holds the whole witness
-    (the forward pass of all 12 layers).  Not assembled: the embedding lookup
-    into the tied token table, the final LayerNorm, the lm_head matmul and the
-    argmax; not built: the WHIR openings of the committed path."""
+    """Configuration 4: the GPT-2-small graph of build_gpt2 (models/gpt2/src/
+    lib.rs:321-436: the embedding lookup into the tied 1024 x 65536 table,
+    12 layers, the final LayerNorm, the lm_head matmul, the vocabulary mask)
+    proven as a shard DAG of 176-op shards (13 shards, as the reference's
+    GPT-2 512 proof; compose.rs prove_shard_dag :2289-2346): rank r proves
+    the shards si % world == r, each recorded once as a CUDA graph and
+    replayed; rank 0 gathers the claims, binds the tensors claimed by two
+    shards with the master transcript and commits each of them as
+    prove_committed_shard_dag does (Whir::with_params(arity, 90, 17)).  Every
+    rank holds the whole witness (the forward pass of the whole graph).  Not
+    built: the closing Argmax arm (topk.rs) and the WHIR openings of the
+    committed path."""
     import torch
     import torch.distributed as dist
 
@@ -1081,7 +1082,7 @@ def cfg4_case(zk, dev, rank, world, layers=12):
     from zkie_b200 import dag, gpt2
     t0 = time.perf_counter()
     st = C.Store()
-    ops, x, out = gpt2.gpt2_layers(st, gpt2.GPT2_SMALL, layers)
+    ops, _, _ = gpt2.gpt2_model(st, gpt2.GPT2_SMALL, layers)
     build_s = time.perf_counter() - t0
     fwd = []
     for _ in range(2):
@@ -1090,7 +1091,7 @@ def cfg4_case(zk, dev, rank, world, layers=12):
         C.forward_ops(st, ops)
         torch.cuda.synchronize()
         fwd.append(time.perf_counter() - t0)
-    per = len(ops) // layers
+    per = 176
     gather = dag.torch_gather() if world > 1 else None
     # timed passes gather only the claims; the digests come from one more
     # replay afterwards (they download every shard's lookup columns)
@@ -1123,12 +1124,12 @@ def cfg4_case(zk, dev, rank, world, layers=12):
     if rank == 0:
         check = dag.prove_dag_ranks(st, ops, per, dag.device_provers(summary="digest", graph=False))
         out_d = {
-            "config": f"cfg4: GPT-2-small, {layers} layers of models/gpt2 build_layer chained (m 512, D 1024, "
-                      f"FFN 4096, 12 heads; synthetic weights), one layer per shard (ops_per_shard {per}), "
-                      f"shards round-robin over {world} GPU(s); embedding lookup, final LayerNorm, lm_head and "
-                      "argmax not assembled",
+            "config": f"cfg4: GPT-2-small graph of models/gpt2 build_gpt2 up to the masked logits ({len(ops)} ops: "
+                      f"embedding lookup into the tied 1024 x 65536 table, {layers} layers (m 512, D 1024, FFN 4096, "
+                      f"12 heads), final LayerNorm, lm_head, vocabulary mask; synthetic weights and tokens), "
+                      f"ops_per_shard {per}, shards round-robin over {world} GPU(s); the Argmax arm is not built",
             "ms": round(ms, 3), "unit": "ms per DAG proof (every shard + cross-shard bindings), max over ranks",
-            "layers_per_s": round(layers / (ms / 1e3), 2), "forward_ms": round(fwd_ms, 3),
+            "layers_per_s": round(layers / (ms / 1e3), 2), "forward_ms": round(fwd_ms, 3), "ops": len(ops),
             "record_ms": round(1e3 * record_s, 1), "build_s": round(build_s, 2),
             "shards": len(res.shards), "max_shards_per_gpu": -(-len(res.shards) // world),
             "cross_tensors": len(res.cross_tensors),

@@ -17,6 +17,7 @@ of the profiles (run from the repository root).
     python perfcases.py coset --log-size 20 --polys 256 --gpus 8
     python perfcases.py projection --m 512 --k 1024 --n 4096
     python perfcases.py layer --trace
+    python perfcases.py model
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -407,6 +408,15 @@ def case_layer(a):
     return res
 
 
+def case_model(a):
+    """BASELINE configuration 4 on one GPU: the GPT-2-small graph up to the
+    masked logits proven as a DAG of 176-op shards by recorded graphs (the
+    bench's cfg4 case)."""
+    import bench
+    import zkie_b200 as zk
+    return {"case": "gpt2_model_dag", **bench.cfg4_case(zk, torch.device("cuda", 0), 0, 1)}
+
+
 def case_sweep(a):
     """batches of 1, 16, 256 polynomials of 2^16,
     2^20, 2^24 coefficients at blowup 2 and 4.  One JSON line per case that
@@ -465,7 +475,8 @@ def case_commit(a):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
-                                         "logup", "grind", "fixed", "cache", "coset", "projection", "layer"])
+                                         "logup", "grind", "fixed", "cache", "coset", "projection", "layer",
+                                         "model"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -481,7 +492,8 @@ def main(argv=None):
     check(lib.zkie2_p2_init_default(), "constants")
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
            "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "cache": case_cache, "sop": case_sop, "shard": case_shard, "split": case_split,
-           "sweep": case_sweep, "coset": case_coset, "projection": case_projection, "layer": case_layer}[a.case](a)
+           "sweep": case_sweep, "coset": case_coset, "projection": case_projection, "layer": case_layer,
+           "model": case_model}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 

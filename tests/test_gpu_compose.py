@@ -185,3 +185,22 @@ def test_dag_ranks_device_matches_oracle(zk, graph):
     roots = [o.whir_commit(consts, host.get(t))[1] for t in full["cross_tensors"]]
     assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"], roots)
     assert len(got.boundary_roots) == len(full["cross_tensors"])
+
+
+def test_gpt2_model_dag_device_matches_oracle(zk):
+    """The GPT-2 model graph (embedding lookup into the tied table, two small
+    layers, final LayerNorm, lm_head, vocabulary mask) as a DAG of 35-op
+    shards on the device: the CPU restatement's DAG digest."""
+    from zkie_b200 import dag, gpt2
+    shape = gpt2.LayerShape(m=8, d=16, d_real=12, heads=2, dh=4, ffn=32, ffn_real=24, exp_bits=8, gelu_bits=10,
+                            rsqrt_len=256, vocab=64, vocab_real=50)
+    host = co.HostStore()
+    ops, _, _ = gpt2.gpt2_model(host, shape, 2)
+    dev = _device_store(zk, host)
+    zk.compose.forward_ops(dev, ops)
+    got = dag.prove_dag_ranks(dev, ops, 35, dag.device_provers(summary="digest", graph=True))
+    co.forward_ops(host, ops)
+    full = co.prove_shard_dag(host, ops, 35)
+    consts = o.p2_constants(1)
+    roots = [o.whir_commit(consts, host.get(t))[1] for t in full["cross_tensors"]]
+    assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"], roots)

@@ -174,6 +174,8 @@ class LayerShape:
     exp_bits: int = 21      # StableSoftmaxIndex offset / table length 2^21
     gelu_bits: int = 24     # GeluIndex offset 2^23, table 2^24
     rsqrt_len: int = RSQRT_TABLE_LEN
+    vocab: int = 65536      # the padded vocabulary of the tied embedding / lm_head (50257 real)
+    vocab_real: int = 50257
 
 
 GPT2_SMALL = LayerShape()
@@ -291,3 +293,51 @@ def build_layer(store, s: LayerShape, x, w, exp_t, rsqrt_t, gelu_t, mask_t):
     out = store.push(None)
     ops.append(Add(x2, proj2, out))
     return ops, out
+
+
+def gpt2_model(store, s: LayerShape, layers: int = 12, seed: int = 0x6B2):
+    """The GPT-2 graph of build_gpt2 (models/gpt2/src/lib.rs:321-436) up to the
+    masked logits: the token embedding as a Lookup into the tied lm_head
+    table (emb_idx[i D + d] = d vocab + token_i) plus the position
+    embedding, ``layers`` layers, the final LayerNormCentered, the lm_head
+    MatMul and the vocabulary mask Add.  The closing Argmax arm (topk.rs) is
+    not built, so the graph ends at the masked logits.  Synthetic inputs: the
+    tokens (below vocab_real), the position embedding, the lm_head weights
+    (d_real x vocab_real, zero-padded) and the final norm's scale and shift,
+    drawn after the layers' weights.  Returns (ops, tokens index id, logits
+    id)."""
+    rng = XorShift64(seed)
+    m, D, V = s.m, s.d, s.vocab
+    tokens = np.array([int(t) % s.vocab_real for t in xorshift_fill(rng, m, 1 << 30)], dtype=np.uint32)
+    lm_w = _pad2(xorshift_fill(rng, s.d_real * s.vocab_real, 50).reshape(s.d_real, s.vocab_real), D, V)
+    pos = _pad2(xorshift_fill(rng, m * s.d_real, 50).reshape(m, s.d_real), m, D).reshape(-1)
+    tok_t = store.push_idx(tokens)
+    emb_idx = (np.arange(D, dtype=np.uint64)[None, :] * V + tokens.astype(np.uint64)[:, None]).reshape(-1)
+    emb_t = store.push_idx(emb_idx.astype(np.uint32))
+    wte = store.push(lm_w.reshape(-1))
+    token_emb = store.push(None)
+    ops = [Lookup(emb_t, token_emb, wte)]
+    pos_t = store.push(pos)
+    x0 = store.push(None)
+    ops.append(Add(token_emb, pos_t, x0))
+    exp_t = store.push(exp_table(s.exp_bits))
+    rsqrt_t = store.push(rsqrt_table(s.rsqrt_len))
+    gelu_t = store.push(gelu_table(s.gelu_bits))
+    mask_t = store.push(causal_mask(m))
+    cur = x0
+    for _ in range(layers):
+        layer_ops, cur = build_layer(store, s, cur, synthetic_layer_weights(rng, s), exp_t, rsqrt_t, gelu_t, mask_t)
+        ops += layer_ops
+    bc = lambda v: np.tile(v, m)  # noqa: E731
+    lnf_w = store.push(bc(_pad1(xorshift_fill(rng, s.d_real, 5, 1), D)))
+    lnf_b = store.push(bc(_pad1(xorshift_fill(rng, s.d_real, 10, -5), D)))
+    h_final = store.push(None)
+    ops.append(LayerNormCentered(cur, lnf_w, lnf_b, h_final, rsqrt_t, m, D, s.d_real))
+    lm_t = store.push(lm_w.reshape(-1))
+    logits = store.push(None)
+    ops.append(MatMul(h_final, lm_t, logits, m, D, V))
+    vmask = from_i64(np.where(np.arange(V) < s.vocab_real, 0, -(1 << 41)))
+    mask_v = store.push(np.tile(vmask, m))
+    logits_masked = store.push(None)
+    ops.append(Add(logits, mask_v, logits_masked))
+    return ops, tok_t, logits_masked
