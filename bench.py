@@ -1065,16 +1065,15 @@ def layer_case(zk, dev, want_cpu, iters=5):
 def cfg4_case(zk, dev, rank, world, layers=12):
     """Configuration 4: the GPT-2-small graph of build_gpt2 (models/gpt2/src/
     lib.rs:321-436: the embedding lookup into the tied 1024 x 65536 table,
-    12 layers, the final LayerNorm, the lm_head matmul, the vocabulary mask)
-    proven as a shard DAG of 176-op shards (13 shards, as the reference's
+    12 layers, the final LayerNorm, the lm_head matmul, the vocabulary mask,
+    the Argmax) proven as a shard DAG of 176-op shards (13 shards, as the reference's
     GPT-2 512 proof; compose.rs prove_shard_dag :2289-2346): rank r proves
     the shards si % world == r, each recorded once as a CUDA graph and
     replayed; rank 0 gathers the claims, binds the tensors claimed by two
     shards with the master transcript and commits each of them as
     prove_committed_shard_dag does (Whir::with_params(arity, 90, 17)).  Every
     rank holds the whole witness (the forward pass of the whole graph).  Not
-    built: the closing Argmax arm (topk.rs) and the WHIR openings of the
-    committed path."""
+    built: the WHIR openings of the committed path."""
     import torch
     import torch.distributed as dist
 
@@ -1124,10 +1123,10 @@ def cfg4_case(zk, dev, rank, world, layers=12):
     if rank == 0:
         check = dag.prove_dag_ranks(st, ops, per, dag.device_provers(summary="digest", graph=False))
         out_d = {
-            "config": f"cfg4: GPT-2-small graph of models/gpt2 build_gpt2 up to the masked logits ({len(ops)} ops: "
-                      f"embedding lookup into the tied 1024 x 65536 table, {layers} layers (m 512, D 1024, FFN 4096, "
-                      f"12 heads), final LayerNorm, lm_head, vocabulary mask; synthetic weights and tokens), "
-                      f"ops_per_shard {per}, shards round-robin over {world} GPU(s); the Argmax arm is not built",
+            "config": f"cfg4: GPT-2-small graph of models/gpt2 build_gpt2 ({len(ops)} ops: embedding lookup into "
+                      f"the tied 1024 x 65536 table, {layers} layers (m 512, D 1024, FFN 4096, 12 heads), final "
+                      f"LayerNorm, lm_head, vocabulary mask, Argmax over the 65536 logits of every position; "
+                      f"synthetic weights and tokens), ops_per_shard {per}, shards round-robin over {world} GPU(s)",
             "ms": round(ms, 3), "unit": "ms per DAG proof (every shard + cross-shard bindings), max over ranks",
             "layers_per_s": round(layers / (ms / 1e3), 2), "forward_ms": round(fwd_ms, 3), "ops": len(ops),
             "record_ms": round(1e3 * record_s, 1), "build_s": round(build_s, 2),

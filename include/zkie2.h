@@ -477,6 +477,26 @@ int zkie2_op_row_sums(const uint64_t *d_x, uint64_t m, uint64_t d, uint64_t ncol
                       zkie_stream_t stream);
 /* out[i] = value */
 int zkie2_op_fill(uint64_t *d_out, uint64_t n, uint64_t value, zkie_stream_t stream);
+/* out[i] = i (the range tables of the top-k proofs) */
+int zkie2_op_iota(uint64_t *d_out, uint64_t n, zkie_stream_t stream);
+/* The TopKSelect / Argmax arms' forward (topk.rs:41-80 topk_forward,
+ * :272-297 argmax_forward; compose.rs:1543-1583): x is m rows of n; per row
+ * the entries ordered by to_i64 value descending, ties by position
+ * ascending; thr (m) = the k-th, sel (m n) = 1 on the first k, gate = x sel,
+ * d1 = sel (x - thr), d2 = (1 - sel) (thr - x) (wrapping i64).  d_out (m
+ * u32, Argmax only, k = 1) receives each row's first position of its
+ * maximum.  k = 1 takes any n < 2^32; k > 1 needs n <= 4096 (the row is
+ * ranked in shared memory); k = 0 or k > n is rejected, as the reference
+ * would panic. */
+int zkie2_op_topk(const uint64_t *d_x, uint64_t m, uint64_t n, uint64_t k, uint64_t *d_thr, uint64_t *d_sel,
+                  uint64_t *d_gate, uint64_t *d_d1, uint64_t *d_d2, uint32_t *d_out, zkie_stream_t stream);
+/* The lookup columns of prove_topk (topk.rs:141-154) and prove_range_decomp
+ * (:395-419) over n entries: to_i32(sel) and to_i32(d1) as u32 indices, and
+ * the 16-bit limbs c0, c1, c2 of to_i64(d2) as u64, each as field values
+ * (d_limbs, 3 n: limb c at c n) and as u32 indices (d_limb_idx, 3 n). */
+int zkie2_op_topk_limbs(const uint64_t *d_sel, const uint64_t *d_d1, const uint64_t *d_d2, uint64_t n,
+                        uint32_t *d_sel_idx, uint32_t *d_d1_idx, uint64_t *d_limbs, uint32_t *d_limb_idx,
+                        zkie_stream_t stream);
 /* prove_same_poly (common/same_poly.rs:13-45) as one degree-2 virtual
  * polynomial: every term of the reference's is c_i f eq(r_i, .), so its
  * round messages are those of f E with E = sum_i c_i eq(r_i, .).  This

@@ -9,7 +9,7 @@ release build):
 - fixed_point.rs to_i64 / from_i64 (:53-70) and compose.rs round_div (:103-111)
 - forward_ops (compose.rs:1174-1583) for the arms a GPT-2 layer uses:
   Transpose, Scale, MatMul, Projection, Add, Lookup, Softmax, SoftmaxIndex,
-  GeluIndex, StableSoftmaxIndex, Layernorm, LayerNormCentered
+  GeluIndex, StableSoftmaxIndex, Layernorm, LayerNormCentered, TopKSelect, Argmax
 - rsqrt_index (compose.rs:884-896), layer_norm_forward and
   prove_layer_norm_centered (layer_norm_centered.rs:42-245)
 - prove_layernorm_chain (layernorm_chain.rs:24-93)
@@ -213,8 +213,102 @@ def forward_ops(store, ops):
         elif k == "LayerNormCentered":
             store.v[op.out] = layer_norm_forward(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d,
                                                  op.n_real)["out"]
+        elif k == "TopKSelect":
+            (store.v[op.thr], store.v[op.sel], store.v[op.gate], store.v[op.d1],
+             store.v[op.d2]) = topk_forward(g(op.x), op.m, op.n, op.k)
+        elif k == "Argmax":
+            (store.v[op.thr], store.v[op.sel], store.v[op.gate], store.v[op.d1], store.v[op.d2],
+             store.idx[op.out]) = argmax_forward(g(op.x), op.m, op.n)
         else:
             raise ValueError(f"op {k} is not restated")
+
+
+# ---- top-k selection and argmax (topk.rs) ------------------------------------------------
+GATE_TERMS = [(1, [0, 1]), (NEG, [2])]
+D1_TERMS = [(1, [0, 1]), (NEG, [0, 2]), (NEG, [3])]
+D2_TERMS = [(1, [2]), (NEG, [1]), (NEG, [0, 2]), (1, [0, 1]), (NEG, [3])]
+ROW_SUM_TERMS = [(1, [0, 1])]
+RECOMPOSE_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2]), (NEG * (1 << 32) % P, [3])]
+
+
+def topk_forward(x, m, n, k):
+    """topk.rs:41-80 -> (thr, sel, gate, d1, d2): per row the entries ordered
+    by value (to_i64) descending, ties by position ascending; the first k
+    selected, thr the k-th; gate = x sel, d1 = sel (x - thr), d2 = (1 - sel)
+    (thr - x) in wrapping i64."""
+    xv = o.u64(x).reshape(m, n) % np.uint64(P)
+    xi = to_i64(xv.reshape(-1)).reshape(m, n)
+    order = np.argsort(~xi, axis=1, kind="stable")  # ~v = -v - 1: descending, stable on ties
+    rows = np.arange(m)
+    thr_i = xi[rows, order[:, k - 1]]
+    sel = np.zeros((m, n), dtype=np.uint64)
+    sel[rows[:, None], order[:, :k]] = 1
+    s = sel.astype(bool)
+    with np.errstate(over="ignore"):
+        d1 = np.where(s, from_i64((xi - thr_i[:, None]).reshape(-1)).reshape(m, n), np.uint64(0))
+        d2 = np.where(s, np.uint64(0), from_i64((thr_i[:, None] - xi).reshape(-1)).reshape(m, n))
+    gate = np.where(s, xv, np.uint64(0))
+    return (xv[rows, order[:, k - 1]].copy(), sel.reshape(-1), gate.reshape(-1), d1.reshape(-1).astype(np.uint64),
+            d2.reshape(-1).astype(np.uint64))
+
+
+def argmax_forward(x, m, n):
+    """topk.rs:272-297 -> (thr, sel, gate, d1, d2, out): top-1 plus the first
+    position of each row's maximum."""
+    thr, sel, gate, d1, d2 = topk_forward(x, m, n, 1)
+    out = np.argmax(to_i64(x).reshape(m, n), axis=1).astype(np.uint32)
+    return thr, sel, gate, d1, d2, out
+
+
+def prove_lookup_fractional(idx, vals, table, alpha, beta, rng):
+    """logup_gkr.rs:390-401: the merged witness / table fraction columns, then
+    prove_fractional."""
+    cols = o.lookup_num_den(idx, vals, table, None, 0, alpha, beta)
+    if cols is None:
+        raise IndexError("lookup index outside the table")
+    return prove_fractional(cols[0], cols[1], rng)
+
+
+def prove_range_decomp(values, rng):
+    """topk.rs:391-448: to_i64(v) as u64 in three 16-bit limbs, each looked up
+    in the 2^16 table, then the recomposition sumcheck."""
+    v = to_i64(values).astype(np.uint64)
+    limbs = [(v >> np.uint64(s)) & np.uint64(0xFFFF) for s in (0, 16, 32)]
+    table = np.arange(1 << 16, dtype=np.uint64)
+    ab = _draw(rng, 6)
+    ranges = [prove_lookup_fractional(c.astype(np.uint32), c, table, int(ab[2 * i]), int(ab[2 * i + 1]), rng)
+              for i, c in enumerate(limbs)]
+    r = _draw(rng, _lg(len(v)))
+    recompose = _vp([values] + limbs, RECOMPOSE_TERMS, r)
+    return (ranges[0], ranges[1], ranges[2], recompose) + tuple(int(a) for a in ab) + (r,)
+
+
+def prove_topk(x, sel, thr, gate, d1, d2, m, n, k, range_bits, rng):
+    """topk.rs:82-176 -> ("TopKSelect", gate_rel, d1_rel, d2_rel, row_sum,
+    sel_range, d1_range, d2_decomp, r, r_row, a_sel, b_sel, a_d1, b_d1,
+    range_bits, sel)."""
+    r = _draw(rng, _lg(m * n))
+    gate_rel = _vp([x, sel, gate], GATE_TERMS, r)
+    thr_b = _rows(thr, m, n)
+    d1_rel = _vp([sel, x, thr_b, d1], D1_TERMS, r)
+    d2_rel = _vp([sel, x, thr_b, d2], D2_TERMS, r)
+    r_row = _draw(rng, _lg(m))
+    row_sum = _vp([sel, _rows(o.eq_evals(r_row), m, n)], ROW_SUM_TERMS, r)
+    a_sel, b_sel = rng.field(), rng.field()
+    sel_range = prove_lookup_fractional(o.to_i32_indices(sel), sel, np.array([0, 1], dtype=np.uint64), a_sel, b_sel,
+                                        rng)
+    a_d1, b_d1 = rng.field(), rng.field()
+    d1_range = prove_lookup_fractional(o.to_i32_indices(d1), d1, np.arange(1 << range_bits, dtype=np.uint64), a_d1,
+                                       b_d1, rng)
+    d2_decomp = prove_range_decomp(d2, rng)
+    return ("TopKSelect", gate_rel, d1_rel, d2_rel, row_sum, sel_range, d1_range, d2_decomp, r, r_row, int(a_sel),
+            int(b_sel), int(a_d1), int(b_d1), range_bits, o.u64(sel).reshape(-1).copy())
+
+
+def prove_argmax(x, sel, thr, gate, d1, d2, out, m, n, range_bits, rng):
+    """topk.rs:299-318 -> ("Argmax", topk proof, out, sel_evals = ())."""
+    return ("Argmax", prove_topk(x, sel, thr, gate, d1, d2, m, n, 1, range_bits, rng),
+            np.asarray(out, dtype=np.uint32).copy(), ())
 
 
 # ---- op arms -----------------------------------------------------------------------------
@@ -404,6 +498,17 @@ def prove_shard_precomputed(store, ops, boundary, rng):
             for t in (op.out, op.w, op.b):
                 claim(t, p[10])
             op_proofs.append(p)
+        elif k in ("TopKSelect", "Argmax"):
+            args = (g(op.x), g(op.sel), g(op.thr), g(op.gate), g(op.d1), g(op.d2))
+            if k == "TopKSelect":  # compose.rs:1968-1996 (range_bits 22)
+                p = prove_topk(*args, op.m, op.n, op.k, 22, rng)
+                tk = p
+            else:  # :1997-2025 (range_bits 16)
+                p = prove_argmax(*args, store.idx[op.out], op.m, op.n, 16, rng)
+                tk = p[1]
+            for t in (op.x, op.sel, op.gate):
+                claim(t, tk[8])
+            op_proofs.append(p)
         else:
             raise ValueError(f"op {k} is not restated")
 
@@ -525,6 +630,43 @@ def verify_softmax_rounded(p):
             and _verify_virtual(rescale, [(1, [0, 2]), (NEG * (1 << 16) % P, [1]), (1, [3])], 0, r_scale))
 
 
+def verify_lookup_fractional_chain(frac):
+    """logup_gkr.rs:450-452: the chain sound and the fraction sum zero."""
+    return _chain_core(frac) and int(frac[1]) % P == 0
+
+
+def verify_range_decomp(p):
+    """topk.rs:450-470."""
+    return (all(verify_lookup_fractional_chain(f) for f in p[:3])
+            and _verify_virtual(p[3], RECOMPOSE_TERMS, 0, p[10]))
+
+
+def verify_topk(p, k):
+    """topk.rs:178-240."""
+    _, gate_rel, d1_rel, d2_rel, row_sum, sel_range, d1_range, d2_decomp, r = p[:9]
+    return (_verify_virtual(gate_rel, GATE_TERMS, 0, r) and _verify_virtual(d1_rel, D1_TERMS, 0, r)
+            and _verify_virtual(d2_rel, D2_TERMS, 0, r) and _verify_virtual(row_sum, ROW_SUM_TERMS, k % P, r)
+            and verify_lookup_fractional_chain(sel_range) and verify_lookup_fractional_chain(d1_range)
+            and verify_range_decomp(d2_decomp))
+
+
+def verify_argmax(p, m, n):
+    """topk.rs:320-343: the top-1 proof, then sel = 1 at every row's output
+    position."""
+    _, tk, out, sel_evals = p
+    if not verify_topk(tk, 1):
+        return False
+    sel = tk[15]
+    for i in range(m):
+        j = int(out[i])
+        if j >= n:
+            return False
+        v = int(sel_evals[i]) if len(sel_evals) else int(sel[i * n + j])
+        if v != 1:
+            return False
+    return True
+
+
 def verify_same_poly(sp, claims):
     """same_poly.rs:46-70: the merged evaluation, or None."""
     coeffs, vp, merged, merged_eval = sp
@@ -565,6 +707,10 @@ def verify_shard(ops, proof):
             ok = verify_layernorm_chain(p)
         elif k == "LayerNormCentered":
             ok = verify_layer_norm_centered(p, op.n_real)
+        elif k == "TopKSelect":
+            ok = verify_topk(p, op.k)
+        elif k == "Argmax":
+            ok = verify_argmax(p, op.m, op.n)
         else:
             ok = k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex")
         if not ok:

@@ -409,9 +409,9 @@ def case_layer(a):
 
 
 def case_model(a):
-    """BASELINE configuration 4 on one GPU: the GPT-2-small graph up to the
-    masked logits proven as a DAG of 176-op shards by recorded graphs (the
-    bench's cfg4 case)."""
+    """BASELINE configuration 4 on one GPU: the GPT-2-small graph (embedding
+    lookup to Argmax) proven as a DAG of 176-op shards by recorded graphs
+    (the bench's cfg4 case)."""
     import bench
     import zkie_b200 as zk
     return {"case": "gpt2_model_dag", **bench.cfg4_case(zk, torch.device("cuda", 0), 0, 1)}

@@ -159,3 +159,112 @@ def test_gpt2_layer_shard_dag_verifies():
                     by.setdefault(t, []).append((pt, ev))
             for t, sp in zip(dag["cross_tensors"], dag["cross_binds"]):
                 assert co.verify_same_poly(sp, by[t]) is not None
+
+
+def _topk_rows(x, m, n, k):
+    """The top-k order restated independently: per row a Python sort on
+    (-value, position)."""
+    xi = co.to_i64(x).reshape(m, n)
+    sel = np.zeros((m, n), dtype=np.uint64)
+    thr = np.zeros(m, dtype=np.int64)
+    for t in range(m):
+        order = sorted(range(n), key=lambda e: (-int(xi[t, e]), e))
+        sel[t, order[:k]] = 1
+        thr[t] = xi[t, order[k - 1]]
+    return sel.reshape(-1), thr
+
+
+@pytest.mark.parametrize("m,n,k", [(4, 8, 3), (4, 8, 1), (2, 64, 6), (8, 16, 16)])
+def test_topk_forward_order_and_ties(m, n, k):
+    """topk_forward (topk.rs:41-80): ties broken by position, d1 and d2 the
+    signed distances to the threshold on either side."""
+    rng = np.random.default_rng(m * n + k)
+    vals = rng.integers(-4, 4, size=m * n)  # many ties
+    vals[::5] = rng.integers(-(1 << 40), 1 << 40, size=vals[::5].size)
+    x = co.from_i64(vals)
+    thr, sel, gate, d1, d2 = co.topk_forward(x, m, n, k)
+    want_sel, want_thr = _topk_rows(x, m, n, k)
+    assert np.array_equal(sel, want_sel) and np.array_equal(co.to_i64(thr), want_thr)
+    assert (sel.reshape(m, n).sum(axis=1) == k).all()
+    s = sel.astype(bool)
+    xi, ti = co.to_i64(x), np.repeat(want_thr, n)
+    assert np.array_equal(co.to_i64(gate), np.where(s, xi, 0))
+    assert np.array_equal(co.to_i64(d1), np.where(s, xi - ti, 0)) and (co.to_i64(d1) >= 0).all()
+    assert np.array_equal(co.to_i64(d2), np.where(s, 0, ti - xi)) and (co.to_i64(d2) >= 0).all()
+
+
+def test_reference_topk_roundtrip():
+    """topk.rs tests::topk_roundtrip (:247-259): seed 0x7777, x_i = (i mod 53)
+    - 26 over 4 x 8, k 3, range_bits 16; a corrupted sel-range leaf fails."""
+    m, n, k = 4, 8, 3
+    x = co.from_i64(np.array([(i % 53) - 26 for i in range(m * n)]))
+    thr, sel, gate, d1, d2 = co.topk_forward(x, m, n, k)
+    p = co.prove_topk(x, sel, thr, gate, d1, d2, m, n, k, 16, o.XorShift64(0x7777))
+    assert co.verify_topk(p, k)
+    bad = copy.deepcopy(p)
+    layers, fnum, fden, full_r = bad[5]
+    l0 = list(layers[0])
+    l0[3] = l0[3].copy()
+    l0[3][3] = (int(l0[3][3]) + 1) % P
+    bad = bad[:5] + (((tuple(l0),) + tuple(layers[1:]), fnum, fden, full_r),) + bad[6:]
+    assert not co.verify_topk(bad, k)
+    assert not co.verify_topk(p, k + 1)  # the row-sum claim is k
+
+
+def test_reference_argmax_roundtrip():
+    """topk.rs argmax_tests::argmax_roundtrip (:347-369): seed 0x9999; the
+    output positions are each row's first maximum, the proof verifies, and a
+    moved output position fails the index binding."""
+    m, n = 4, 8
+    x = co.from_i64(np.array([(i % 53) - 26 for i in range(m * n)]))
+    thr, sel, gate, d1, d2, out = co.argmax_forward(x, m, n)
+    xi = co.to_i64(x).reshape(m, n)
+    for i in range(m):
+        best = 0
+        for j in range(1, n):
+            if xi[i, j] > xi[i, best]:
+                best = j
+        assert out[i] == best and sel[i * n + best] == 1
+    p = co.prove_argmax(x, sel, thr, gate, d1, d2, out, m, n, 16, o.XorShift64(0x9999))
+    assert co.verify_argmax(p, m, n)
+    moved = out.copy()
+    moved[0] = (moved[0] + 1) % n
+    assert not co.verify_argmax((p[0], p[1], moved, p[3]), m, n)
+
+
+def test_range_decomp_wide_differences():
+    """prove_range_decomp (topk.rs:391-448) over 48-bit values verifies; a
+    value of 2^48 loses its top bits in the limbs and fails the
+    recomposition."""
+    vals = np.array([0, 1, 0xFFFF, 0x10000, (1 << 48) - 1, 12345678901, 7, 1 << 47], dtype=np.int64)
+    p = co.prove_range_decomp(co.from_i64(vals), o.XorShift64(3))
+    assert co.verify_range_decomp(p)
+    vals[3] = 1 << 48
+    assert not co.verify_range_decomp(co.prove_range_decomp(co.from_i64(vals), o.XorShift64(3)))
+
+
+def test_topk_and_argmax_shard_verifies():
+    """Op::TopKSelect (range_bits 22) and Op::Argmax (16) inside
+    prove_shard_precomputed: claims of x, sel and gate at the gate relation's
+    point, bound to x's other claim (an Add producing it) by same_poly."""
+    m, n = 4, 16
+    st = co.HostStore()
+    rng = np.random.default_rng(5)
+    a = st.push(co.from_i64(rng.integers(-1000, 1000, size=m * n)))
+    b = st.push(co.from_i64(rng.integers(-1000, 1000, size=m * n)))
+    x = st.push(None)
+    ts = [st.push(None) for _ in range(10)]
+    out = st.push_idx(None)
+    ops = [co_op("Add", a=a, b=b, c=x),
+           co_op("TopKSelect", x=x, sel=ts[0], thr=ts[1], gate=ts[2], d1=ts[3], d2=ts[4], m=m, n=n, k=3),
+           co_op("Argmax", x=x, sel=ts[5], thr=ts[6], gate=ts[7], d1=ts[8], d2=ts[9], out=out, m=m, n=n)]
+    proof = co.prove_shard(st, ops, [], o.XorShift64(11))
+    assert co.verify_shard(ops, proof)
+    assert x in proof["bound"]
+    assert np.array_equal(st.idx[out], co.to_i64(st.v[x]).reshape(m, n).argmax(axis=1))
+
+
+def co_op(kind, **fields):
+    """An op object of the product's op classes (read by duck typing)."""
+    from zkie_b200 import compose as C
+    return getattr(C, kind)(**fields)

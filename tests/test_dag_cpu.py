@@ -117,20 +117,23 @@ def test_gloo_dag_ranks(tmp_path, world):
 
 def test_gpt2_model_graph_shard_dag():
     """The model graph (embedding Lookup into the tied table, the layers, the
-    final LayerNorm, the lm_head MatMul, the vocabulary mask): 13 shards of
-    176 ops at GPT-2's 12 layers; here 2 small layers in shards of 35 ops,
-    each shard and each cross-shard binding accepted."""
+    final LayerNorm, the lm_head MatMul, the vocabulary mask, the Argmax):
+    13 shards of 176 ops at GPT-2's 12 layers; here 2 small layers in shards
+    of 35 ops, each shard and each cross-shard binding accepted, and the
+    Argmax output the first maximum of every masked-logit row."""
     small = gpt2.LayerShape(m=8, d=16, d_real=12, heads=2, dh=4, ffn=32, ffn_real=24, exp_bits=8, gelu_bits=10,
                             rsqrt_len=256, vocab=64, vocab_real=50)
     st = co.HostStore()
-    ops, tokens, logits = gpt2.gpt2_model(st, small, 2)
-    assert [o.kind for o in ops[:2]] == ["Lookup", "Add"] and [o.kind for o in ops[-3:]] == [
-        "LayerNormCentered", "MatMul", "Add"]
-    assert st.v[ops[0].table].size == small.d * small.vocab == st.v[ops[-2].b].size
+    ops, tokens, nxt = gpt2.gpt2_model(st, small, 2)
+    assert [o.kind for o in ops[:2]] == ["Lookup", "Add"] and [o.kind for o in ops[-4:]] == [
+        "LayerNormCentered", "MatMul", "Add", "Argmax"]
+    assert st.v[ops[0].table].size == small.d * small.vocab == st.v[ops[-3].b].size
     assert max(st.idx[tokens]) < small.vocab_real
-    full_ops = 2 + 12 * 176 + 3
+    full_ops = 2 + 12 * 176 + 4
     assert len(dag.shard_ranges(full_ops, 176)) == 13
     co.forward_ops(st, ops)
+    logits = co.to_i64(st.v[ops[-1].x]).reshape(small.m, small.vocab)
+    assert (st.idx[nxt] == logits.argmax(axis=1)).all() and (st.idx[nxt] < small.vocab_real).all()
     res = dag.prove_dag_ranks(st, ops, 35, oracle_provers())
     for (s, e), sh in zip(dag.shard_ranges(len(ops), 35), res.shards):
         assert co.verify_shard(ops[s:e], sh)

@@ -189,7 +189,7 @@ def test_dag_ranks_device_matches_oracle(zk, graph):
 
 def test_gpt2_model_dag_device_matches_oracle(zk):
     """The GPT-2 model graph (embedding lookup into the tied table, two small
-    layers, final LayerNorm, lm_head, vocabulary mask) as a DAG of 35-op
+    layers, final LayerNorm, lm_head, vocabulary mask, Argmax) as a DAG of 35-op
     shards on the device: the CPU restatement's DAG digest."""
     from zkie_b200 import dag, gpt2
     shape = gpt2.LayerShape(m=8, d=16, d_real=12, heads=2, dh=4, ffn=32, ffn_real=24, exp_bits=8, gelu_bits=10,
@@ -204,3 +204,88 @@ def test_gpt2_model_dag_device_matches_oracle(zk):
     consts = o.p2_constants(1)
     roots = [o.whir_commit(consts, host.get(t))[1] for t in full["cross_tensors"]]
     assert got.digest == dag.dag_digest(full["shards"], full["cross_tensors"], full["cross_binds"], roots)
+
+
+def _topk_case(m, n, seed, wide=False):
+    rng = np.random.default_rng(seed)
+    vals = rng.integers(-4, 4, size=m * n)  # ties in every row
+    if wide:
+        vals[::3] = rng.integers(-(1 << 41), 1 << 30, size=vals[::3].size)
+    return co.from_i64(vals)
+
+
+@pytest.mark.parametrize("m,n,k", [(4, 8, 1), (4, 8, 3), (8, 64, 6), (2, 4096, 5), (3, 1 << 17, 1), (16, 16, 16)])
+def test_topk_forward_matches_oracle(zk, m, n, k):
+    """zkie2_op_topk against topk_forward / argmax_forward: the k-th entry,
+    the one-hot selection (ties by position), gate, d1, d2 and the Argmax
+    output positions."""
+    x = _topk_case(m, n, m + n + k, wide=True)
+    host = co.HostStore()
+    xi = host.push(x)
+    ts = [host.push(None) for _ in range(5)]
+    out = host.push_idx(None)
+    C = zk.compose
+    op = (C.Argmax(xi, *ts, out, m, n) if k == 1 else C.TopKSelect(xi, *ts, m, n, k))
+    dev = _device_store(zk, host)
+    C.forward_ops(dev, [op])
+    co.forward_ops(host, [op])
+    for t in ts:
+        assert np.array_equal(dev.get(t).cpu().numpy(), host.v[t]), t
+    if k == 1:
+        assert np.array_equal(dev.get_idx(out).cpu().numpy(), host.idx[out])
+
+
+def test_topk_rejects_unsupported_k(zk):
+    from zkie_b200.device import to_dev
+    x = to_dev(_topk_case(2, 8, 1))
+    bufs = [torch.empty(16, dtype=torch.uint64, device="cuda") for _ in range(5)]
+    lib = zk.lib
+    for k in (0, 9):
+        assert lib.zkie2_op_topk(x.data_ptr(), 2, 8, k, *[b.data_ptr() for b in bufs], None, 0) != 0
+
+
+@pytest.mark.parametrize("n", [16, 1024])
+def test_topk_argmax_shard_matches_oracle(zk, n):
+    """Op::TopKSelect (range_bits 22) and Op::Argmax (16) in one shard on the
+    device prover: the CPU restatement's proof, value for value, and it
+    verifies."""
+    C = zk.compose
+    host, ops = _topk_shard(C, 4, n, 1000)
+    dev = _device_store(zk, host)
+    C.forward_ops(dev, ops)
+    got = C.prove_shard_precomputed(dev, ops, [], zk.gkr.XorShift64(21)).canonical()
+    want = co.prove_shard(host, ops, [], o.XorShift64(21))
+    assert_same(got, want)
+    assert co.verify_shard(ops, want)
+
+
+def _topk_shard(C, m, n, spread):
+    """x = a + b with a quarter of the entries 2^40 below the rest (never
+    among the top 6: d2 needs all three 16-bit limbs); the others within
+    +-spread, so the selected entries' distances d1 stay below 2^22 when
+    spread is small."""
+    host = co.HostStore()
+    rng = np.random.default_rng(n + spread)
+    a = host.push(co.from_i64(rng.integers(-spread, spread, size=m * n)))
+    bv = rng.integers(-1000, 1000, size=m * n)
+    bv[::4] = -(1 << 40)
+    b = host.push(co.from_i64(bv))
+    x = host.push(None)
+    ts = [host.push(None) for _ in range(10)]
+    out = host.push_idx(None)
+    return host, [C.Add(a, b, x), C.TopKSelect(x, *ts[:5], m, n, 6), C.Argmax(x, *ts[5:], out, m, n)]
+
+
+def test_topk_selected_spread_outside_the_range_table(zk):
+    """Selected entries further than 2^22 from the threshold: d1 falls
+    outside TopKSelect's range table, where the reference's multiplicity
+    count would panic; the device prover reports the lookup error and the
+    CPU restatement raises."""
+    C = zk.compose
+    host, ops = _topk_shard(C, 2, 16, 1 << 30)
+    dev = _device_store(zk, host)
+    C.forward_ops(dev, ops)
+    with pytest.raises(ValueError, match="lookup index"):
+        C.prove_shard_precomputed(dev, ops, [], zk.gkr.XorShift64(1))
+    with pytest.raises(IndexError):
+        co.prove_shard(host, ops, [], o.XorShift64(1))

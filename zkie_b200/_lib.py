@@ -142,6 +142,9 @@ SIGNATURES = {
     "zkie2_op_row_broadcast": (i64, [vp, u64, u64, vp, vp]),
     "zkie2_op_row_sums": (i64, [vp, u64, u64, u64, vp, vp]),
     "zkie2_op_fill": (i64, [vp, u64, u64, vp]),
+    "zkie2_op_iota": (i64, [vp, u64, vp]),
+    "zkie2_op_topk": (i64, [vp, u64, u64, u64, vp, vp, vp, vp, vp, vp, vp]),
+    "zkie2_op_topk_limbs": (i64, [vp, vp, vp, u64, vp, vp, vp, vp, vp]),
     "zkie2_eq_combine_scratch_elems": (u64, [u32, u32]),
     "zkie2_eq_combine": (i64, [pu64, pu64, u32, u32, vp, vp, vp]),
     "zkie2_mg_available": (i64, []),

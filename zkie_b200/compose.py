@@ -1,7 +1,7 @@
 """The op layer of zkie-ops (crates/zkie-ops/src/compose.rs) on the device.
 
 Host-side mirror of the reference's op graph and shard prover for the arms a
-GPT-2 layer uses, over libzkie_b200.so:
+GPT-2 model uses, over libzkie_b200.so:
 
 - the ``Op`` variants (compose.rs:560-800) with ``reads`` / ``writes``
   (:955-1060), and ``Store`` (:525-560) holding device tensors;
@@ -13,7 +13,9 @@ GPT-2 layer uses, over libzkie_b200.so:
   prove_layer_norm_centered (layer_norm_centered.rs:122-245),
   prove_layernorm_chain (layernorm_chain.rs:24-93), prove_softmax_rounded
   (softmax_scaled.rs:42-108), prove_same_poly (common/same_poly.rs:13-45),
-  prove_projection (projection.rs:44-101), the Op::MatMul and Add arms, and
+  prove_projection (projection.rs:44-101), prove_topk / prove_argmax /
+  prove_range_decomp (topk.rs:82-176, 299-318, 391-448), the Op::MatMul and
+  Add arms, and
   the per-table logUp of prove_lookup_witness_batch_columns and
   prove_lookup_table (common/logup_gkr.rs:340-383).
 
@@ -190,6 +192,36 @@ class LayerNormCentered(_Op):
     _reads, _writes = ("x", "w", "b", "rsqrt_table"), ("out",)
 
 
+@dataclass
+class TopKSelect(_Op):
+    x: int
+    sel: int
+    thr: int
+    gate: int
+    d1: int
+    d2: int
+    m: int
+    n: int
+    k: int
+    kind = "TopKSelect"
+    _reads, _writes = ("x",), ("sel", "thr", "gate", "d1", "d2")
+
+
+@dataclass
+class Argmax(_Op):
+    x: int
+    sel: int
+    thr: int
+    gate: int
+    d1: int
+    d2: int
+    out: int  # an index tensor
+    m: int
+    n: int
+    kind = "Argmax"
+    _reads, _writes = ("x",), ("sel", "thr", "gate", "d1", "d2")
+
+
 # ---- the store (compose.rs:525-560) -------------------------------------------------------
 class Store:
     """Field tensors ``v`` and u32 index tensors ``idx`` on the device, two id
@@ -356,6 +388,14 @@ def forward_ops(store: Store, ops):
             out = layer_norm_centered_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d, op.n_real,
                                               err)["out"]
             _slot(store, op.out, out.numel()).copy_(out)
+        elif k in ("TopKSelect", "Argmax"):
+            mn = op.m * op.n
+            thr = _slot(store, op.thr, op.m)
+            sel, gate, d1, d2 = (_slot(store, t, mn) for t in (op.sel, op.gate, op.d1, op.d2))
+            out = _islot(store, op.out, op.m) if k == "Argmax" else None
+            check(lib.zkie2_op_topk(ptr(g(op.x)), op.m, op.n, op.k if k == "TopKSelect" else 1, ptr(thr), ptr(sel),
+                                    ptr(gate), ptr(d1), ptr(d2), out.data_ptr() if out is not None else None, sh),
+                  "zkie2_op_topk")
         else:
             raise ValueError(f"op {k} is not supported")
     _check_err(err, "forward_ops")
@@ -488,6 +528,64 @@ class TableColumn:
                 self.num_leaf, self.den_leaf)
 
 
+@dataclass
+class RangeDecompProof:
+    """topk.rs:377-389."""
+    c0_range: FractionalProof
+    c1_range: FractionalProof
+    c2_range: FractionalProof
+    recompose: VirtualProof
+    a0: int
+    b0: int
+    a1: int
+    b1: int
+    a2: int
+    b2: int
+    r: np.ndarray
+
+    def canonical(self):
+        return (_frac_canon(self.c0_range), _frac_canon(self.c1_range), _frac_canon(self.c2_range),
+                _vcanon(self.recompose), self.a0, self.b0, self.a1, self.b1, self.a2, self.b2, self.r)
+
+
+@dataclass
+class TopKSelectProof:
+    """topk.rs:22-39; ``sel`` is the one-hot witness the reference's proof
+    carries (a device tensor here, read back by canonical())."""
+    gate_rel: VirtualProof
+    d1_rel: VirtualProof
+    d2_rel: VirtualProof
+    row_sum: VirtualProof
+    sel_range: FractionalProof
+    d1_range: FractionalProof
+    d2_decomp: RangeDecompProof
+    r: np.ndarray
+    r_row: np.ndarray
+    a_sel: int
+    b_sel: int
+    a_d1: int
+    b_d1: int
+    range_bits: int
+    sel: torch.Tensor
+
+    def canonical(self):
+        return ("TopKSelect", _vcanon(self.gate_rel), _vcanon(self.d1_rel), _vcanon(self.d2_rel),
+                _vcanon(self.row_sum), _frac_canon(self.sel_range), _frac_canon(self.d1_range),
+                self.d2_decomp.canonical(), self.r, self.r_row, self.a_sel, self.b_sel, self.a_d1, self.b_d1,
+                self.range_bits, self.sel.cpu().numpy())
+
+
+@dataclass
+class ArgmaxProof:
+    """topk.rs:265-270: the top-1 proof, the public output positions and the
+    (uncommitted path: empty) opened sel values."""
+    topk: TopKSelectProof
+    out: torch.Tensor
+
+    def canonical(self):
+        return ("Argmax", self.topk.canonical(), self.out.cpu().numpy(), ())
+
+
 def _op_canon(p):
     if isinstance(p, OpMatMulProof):
         mm = p.proof
@@ -573,6 +671,11 @@ LN_OUT_TERMS = [(1, [0, 1]), (1, [2]), (NEG, [3])]
 SOFTMAX_SUM_TERMS = [(1, [0, 1])]
 SOFTMAX_RESCALE_TERMS = [(1, [0, 2]), (NEG * (1 << 16) % P, [1]), (1, [3])]
 PRODUCT_TERMS = [(1, [0, 1])]
+GATE_TERMS = [(1, [0, 1]), (NEG, [2])]                                        # topk.rs:101
+D1_TERMS = [(1, [0, 1]), (NEG, [0, 2]), (NEG, [3])]                           # :111-115
+D2_TERMS = [(1, [2]), (NEG, [1]), (NEG, [0, 2]), (1, [0, 1]), (NEG, [3])]     # :119-125
+ROW_SUM_TERMS = [(1, [0, 1])]                                                 # :137
+RECOMPOSE_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2]), (NEG * (1 << 32) % P, [3])]  # :428-433
 
 
 def _cat_u64(parts) -> torch.Tensor:
@@ -649,6 +752,7 @@ class OpShardProver:
         self.lookups = {}     # table -> [(idx tensor, value tensor, event or None)]
         self.evals = []       # evaluations waiting for flush_evals
         self.traffic = 0      # algorithmic bytes: every table a sub-proof reads, once
+        self.keep = []        # columns read on streams other than the one that allocated them
 
     @contextlib.contextmanager
     def on(self, s):
@@ -758,7 +862,78 @@ class OpShardProver:
         check(lib.zkie2_eq_evals(_pp(r), r.size, ptr(out), self.sh), "zkie2_eq_evals")
         return out
 
+    def lookup_fractional(self, idx: torch.Tensor, vals: torch.Tensor, table: torch.Tensor, alpha: int, beta: int):
+        """prove_lookup_fractional (logup_gkr.rs:390-401): the merged witness /
+        table columns (an index outside the table sets the error word), then
+        the fraction tree."""
+        n, t = idx.numel(), table.numel()
+        total = lib.zkie2_lookup_len(n, t, 0)
+        num, den = empty(total), empty(total)
+        scr = empty(max(lib.zkie2_lookup_scratch_elems(t), 1))
+        self.traffic += 12 * n + 8 * t + 16 * total
+        check(lib.zkie2_lookup_num_den_async(idx.data_ptr(), ptr(vals), n, ptr(table), None, t, 0, alpha, beta,
+                                             ptr(num), ptr(den), ptr(scr), self.err.data_ptr(), self.sh),
+              "zkie2_lookup_num_den_async")
+        return self.fractional(num, den)
+
+    def range_table(self, bits: int) -> torch.Tensor:
+        """0, 1, .., 2^bits - 1 on the current stream."""
+        out = empty(1 << bits)
+        check(lib.zkie2_op_iota(ptr(out), 1 << bits, self.sh), "zkie2_op_iota")
+        return out
+
     # -- the arms --------------------------------------------------------------------------------
+    def op_topk(self, op):
+        """prove_topk (topk.rs:82-176) for Op::TopKSelect (range_bits 22,
+        compose.rs:1968-1996) and, with k = 1, prove_argmax (topk.rs:299-318)
+        for Op::Argmax (range_bits 16, compose.rs:1997-2025); x, sel and gate
+        claimed at r from the gate relation's folded tables."""
+        g = self.store.get
+        argmax = op.kind == "Argmax"
+        m, n = op.m, op.n
+        k, rb, mn = (1, 16, m * n) if argmax else (op.k, 22, m * n)
+        x, sel, thr, gate, d1, d2 = (g(t) for t in (op.x, op.sel, op.thr, op.gate, op.d1, op.d2))
+        r = self.draw(_lg(mn))
+        gate_rel = self.virtual([x, sel, gate], GATE_TERMS, r)
+        thr_b = self.broadcast(thr, m, n)
+        d1_rel = self.virtual([sel, x, thr_b, d1], D1_TERMS, r)
+        d2_rel = self.virtual([sel, x, thr_b, d2], D2_TERMS, r)
+        r_row = self.draw(_lg(m))
+        row_sum = self.virtual([sel, self.broadcast(self.eq_table(r_row), m, n)], ROW_SUM_TERMS, r)
+        sel_idx, d1_idx, limb_idx = _u32(mn), _u32(mn), _u32(3 * mn)
+        limbs = empty(3 * mn)
+        check(lib.zkie2_op_topk_limbs(ptr(sel), ptr(d1), ptr(d2), mn, sel_idx.data_ptr(), d1_idx.data_ptr(),
+                                      ptr(limbs), limb_idx.data_ptr(), self.sh), "zkie2_op_topk_limbs")
+        # the five range lookups are independent: each on a stream of its own
+        # behind the columns (which live as long as the prover)
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream())
+        self.keep += [sel_idx, d1_idx, limb_idx, limbs]
+
+        def lookup(idx, vals, bits, alpha, beta):
+            with self.on(self.next_stream()):
+                torch.cuda.current_stream().wait_event(ready)
+                return self.lookup_fractional(idx, vals, self.range_table(bits), alpha, beta)
+        a_sel, b_sel = self.rng.field(), self.rng.field()
+        sel_range = lookup(sel_idx, sel, 1, a_sel, b_sel)
+        a_d1, b_d1 = self.rng.field(), self.rng.field()
+        d1_range = lookup(d1_idx, d1, rb, a_d1, b_d1)
+        ab = [int(v) for v in self.draw(6)]
+        parts = [(limb_idx[c * mn:(c + 1) * mn], limbs[c * mn:(c + 1) * mn]) for c in range(3)]
+        ranges = [lookup(i, v, 16, ab[2 * c], ab[2 * c + 1]) for c, (i, v) in enumerate(parts)]
+        r2 = self.draw(_lg(mn))
+        recompose = self.virtual([d2] + [v for _, v in parts], RECOMPOSE_TERMS, r2)
+        for i, t in enumerate((op.x, op.sel, op.gate)):
+            self.claim(t, r, gate_rel.final(i))
+        out = self.store.get_idx(op.out) if argmax else None
+
+        def build():
+            dec = RangeDecompProof(ranges[0](), ranges[1](), ranges[2](), recompose(), *ab, r2)
+            tk = TopKSelectProof(gate_rel(), d1_rel(), d2_rel(), row_sum(), sel_range(), d1_range(), dec, r, r_row,
+                                 int(a_sel), int(b_sel), int(a_d1), int(b_d1), rb, sel)
+            return ArgmaxProof(tk, out) if argmax else tk
+        return build
+
     def op_matmul(self, op: MatMul):
         g = self.store.get
         lm, lk, ln = _lg(op.m), _lg(op.k), _lg(op.n)
@@ -998,7 +1173,8 @@ class OpShardProver:
         whole call can be recorded as a CUDA graph."""
         arms = {"MatMul": self.op_matmul, "Projection": self.op_projection, "Add": self.op_add,
                 "Softmax": self.op_softmax, "Layernorm": self.op_layernorm,
-                "LayerNormCentered": self.op_layer_norm_centered}
+                "LayerNormCentered": self.op_layer_norm_centered, "TopKSelect": self.op_topk,
+                "Argmax": self.op_topk}
         self.err.zero_()
         start = torch.cuda.Event()
         start.record(self.main)

@@ -23,6 +23,7 @@
 #include "../../include/zkie2.h"
 #include "common.cuh"
 #include "gl64.cuh"
+#include "hist.cuh"
 #include "internal.h"
 
 namespace zk {
@@ -315,18 +316,10 @@ uint64_t lookup_len(uint64_t n, uint64_t t, uint32_t mode) {
     }
 }
 
-// m[x[i]] += 1 for i < n; an index at or above t raises *bad (the reference
-// would index out of bounds and panic).
+// m[x[i]] += 1 for i < n; an index at or above t raises *bad (hist.cuh)
 __global__ void k_lookup_hist(const uint32_t* __restrict__ x, uint64_t n, uint64_t t, uint32_t* __restrict__ m,
                               uint32_t* __restrict__ bad) {
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint32_t xi = __ldg(x + i);
-        if (xi < t)
-            atomicAdd(m + xi, 1u);
-        else
-            atomicOr(bad, 1u);
-    }
+    hist_grid(x, n, t, m, bad, 1u);
 }
 
 // alpha + j + beta * v as a canonical field element

@@ -1,8 +1,8 @@
 // ops.cu -- the op layer of zkie-ops on the device: the forward witness of
-// the arms a GPT-2 layer uses (crates/zkie-ops/src/compose.rs forward_ops,
+// the arms a GPT-2 model uses (crates/zkie-ops/src/compose.rs forward_ops,
 // :1174-1583) and the columns their proofs read (the arms of
 // prove_shard_precomputed, :1602-2091; layer_norm_centered.rs,
-// layernorm_chain.rs, softmax_scaled.rs, common/same_poly.rs).
+// layernorm_chain.rs, softmax_scaled.rs, topk.rs, common/same_poly.rs).
 //
 // Every tensor is a flat row-major array of field elements (u64, canonical on
 // output) or of u32 lookup indices, as in the reference's Store.  Rows are
@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "fixed.cuh"
 #include "gl64.cuh"
+#include "hist.cuh"
 #include "internal.h"
 
 namespace zk {
@@ -418,14 +419,125 @@ __global__ void k_eq_combine(const uint64_t* __restrict__ tabs, uint32_t c, uint
 // ---- lookup multiplicities (common/logup_gkr.rs:251-260) ----------------------------------
 __global__ void k_multiplicity(const uint32_t* __restrict__ x, uint64_t n, uint64_t t,
                                unsigned long long* __restrict__ m, uint32_t* __restrict__ err) {
+    hist_grid(x, n, t, m, err, kErrIndex);
+}
+
+// ---- top-k selection and argmax (topk.rs:41-80, 272-297) -----------------------------------
+constexpr uint64_t kTopkMaxCols = 4096;  // a row held in shared memory when k > 1
+
+// topk_forward's order within a row: the larger value (to_i64) first, the
+// smaller position first among equal values
+__device__ __forceinline__ bool ranks_before(int64_t va, uint64_t ja, int64_t vb, uint64_t jb) {
+    return va > vb || (va == vb && ja < jb);
+}
+
+// Op::TopKSelect / Op::Argmax forward, one block per row: thr = the k-th
+// entry in that order, sel = 1 on the first k entries, gate = x sel, d1 =
+// sel (x - thr), d2 = (1 - sel) (thr - x) in wrapping i64; out[r] (given for
+// k = 1) = the row's first position of its maximum.  k = 1 is a block
+// reduction over any row length; k > 1 ranks every entry of a row of at most
+// kTopkMaxCols held in shared memory (writing sel in that pass).
+__global__ void __launch_bounds__(kRowThreads) k_topk_rows(const uint64_t* __restrict__ x, uint64_t m, uint64_t n,
+                                                           uint64_t k, uint64_t* __restrict__ thr,
+                                                           uint64_t* __restrict__ sel, uint64_t* __restrict__ gate,
+                                                           uint64_t* __restrict__ d1, uint64_t* __restrict__ d2,
+                                                           uint32_t* __restrict__ out) {
+    extern __shared__ int64_t row[];
+    __shared__ int64_t sv[kRowWarps];
+    __shared__ uint64_t sj[kRowWarps];
+    __shared__ uint64_t s_kth;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint64_t r = blockIdx.x; r < m; r += gridDim.x) {
+        const uint64_t* xr = x + r * n;
+        uint64_t tj;
+        __syncthreads();  // the previous row's shared values are no longer read
+        if (k == 1) {
+            int64_t bv = INT64_MIN;
+            uint64_t bj = UINT64_MAX;  // ranks after every entry
+            for (uint64_t j = threadIdx.x; j < n; j += blockDim.x) {
+                const int64_t v = fx_to_i64(gl_canon(__ldg(xr + j)));
+                if (ranks_before(v, j, bv, bj)) {
+                    bv = v;
+                    bj = j;
+                }
+            }
+            for (int o = 16; o; o >>= 1) {
+                const int64_t ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+                const uint64_t oj = __shfl_xor_sync(0xFFFFFFFFu, bj, o);
+                if (ranks_before(ov, oj, bv, bj)) {
+                    bv = ov;
+                    bj = oj;
+                }
+            }
+            if (lane == 0) {
+                sv[warp] = bv;
+                sj[warp] = bj;
+            }
+            __syncthreads();
+            bv = sv[0];
+            bj = sj[0];
+            for (int w = 1; w < kRowWarps; w++) {
+                if (ranks_before(sv[w], sj[w], bv, bj)) {
+                    bv = sv[w];
+                    bj = sj[w];
+                }
+            }
+            tj = bj;
+        } else {
+            for (uint64_t j = threadIdx.x; j < n; j += blockDim.x) row[j] = fx_to_i64(gl_canon(__ldg(xr + j)));
+            __syncthreads();
+            for (uint64_t j = threadIdx.x; j < n; j += blockDim.x) {
+                const int64_t v = row[j];
+                uint64_t rank = 0;
+                for (uint64_t i = 0; i < n; i++) rank += ranks_before(row[i], i, v, j) ? 1 : 0;
+                sel[r * n + j] = rank < k ? 1 : 0;
+                if (rank == k - 1) s_kth = j;
+            }
+            __syncthreads();
+            tj = s_kth;
+        }
+        const uint64_t tval = gl_canon(__ldg(xr + tj));
+        const int64_t ti = fx_to_i64(tval);
+        if (threadIdx.x == 0) {
+            thr[r] = tval;
+            if (out) out[r] = (uint32_t)tj;
+        }
+        for (uint64_t j = threadIdx.x; j < n; j += blockDim.x) {
+            const uint64_t o = r * n + j;
+            const uint64_t xv = gl_canon(__ldg(xr + j));
+            const int64_t xi = fx_to_i64(xv);
+            const bool s = k == 1 ? j == tj : sel[o] != 0;  // k > 1: this thread's own write above
+            if (k == 1) sel[o] = s ? 1 : 0;
+            gate[o] = s ? xv : 0;
+            d1[o] = s ? fx_from_i64(fx_wsub(xi, ti)) : 0;
+            d2[o] = s ? 0 : fx_from_i64(fx_wsub(ti, xi));
+        }
+    }
+}
+
+// The lookup columns of prove_topk (topk.rs:141-154) and prove_range_decomp
+// (:395-419): to_i32(v) as u32 of sel and d1, and the three 16-bit limbs of
+// to_i64(d2) as u64 (values and indices, limb c at offset c n)
+__global__ void k_topk_limbs(const uint64_t* __restrict__ sel, const uint64_t* __restrict__ d1,
+                             const uint64_t* __restrict__ d2, uint64_t n, uint32_t* __restrict__ sel_idx,
+                             uint32_t* __restrict__ d1_idx, uint64_t* __restrict__ limbs,
+                             uint32_t* __restrict__ limb_idx) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint32_t j = __ldg(x + i);
-        if (j < t)
-            atomicAdd(m + j, 1ull);
-        else
-            atomicOr(err, kErrIndex);
+        sel_idx[i] = fx_to_i32_index(__ldg(sel + i));
+        d1_idx[i] = fx_to_i32_index(__ldg(d1 + i));
+        const uint64_t v = (uint64_t)fx_to_i64(gl_canon(__ldg(d2 + i)));
+        for (int c = 0; c < 3; c++) {
+            const uint64_t l = (v >> (16 * c)) & 0xFFFFull;
+            limbs[c * n + i] = l;
+            limb_idx[c * n + i] = (uint32_t)l;
+        }
     }
+}
+
+__global__ void k_iota(uint64_t* __restrict__ out, uint64_t n) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) out[i] = i;
 }
 
 }  // namespace
@@ -560,6 +672,38 @@ int zkie2_op_row_sums(const uint64_t* d_x, uint64_t m, uint64_t d, uint64_t ncol
     if (m == 0) return 0;
     if (ncols > d || !d_x || !d_out) return (int)cudaErrorInvalidValue;
     k_row_sums<<<row_grid(m), kRowThreads, 0, stream>>>(d_x, m, d, ncols, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_topk(const uint64_t* d_x, uint64_t m, uint64_t n, uint64_t k, uint64_t* d_thr, uint64_t* d_sel,
+                  uint64_t* d_gate, uint64_t* d_d1, uint64_t* d_d2, uint32_t* d_out, cudaStream_t stream) {
+    if (k == 0 || k > n || (k > 1 && (n > kTopkMaxCols || d_out)) || n > 0xFFFFFFFFull)
+        return (int)cudaErrorInvalidValue;
+    if (m == 0) return 0;
+    if (!d_x || !d_thr || !d_sel || !d_gate || !d_d1 || !d_d2) return (int)cudaErrorInvalidValue;
+    const size_t shared = k > 1 ? 8 * n : 0;
+    k_topk_rows<<<row_grid(m), kRowThreads, shared, stream>>>(d_x, m, n, k, d_thr, d_sel, d_gate, d_d1, d_d2, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_topk_limbs(const uint64_t* d_sel, const uint64_t* d_d1, const uint64_t* d_d2, uint64_t n,
+                        uint32_t* d_sel_idx, uint32_t* d_d1_idx, uint64_t* d_limbs, uint32_t* d_limb_idx,
+                        cudaStream_t stream) {
+    if (n == 0) return 0;
+    if (!d_sel || !d_d1 || !d_d2 || !d_sel_idx || !d_d1_idx || !d_limbs || !d_limb_idx)
+        return (int)cudaErrorInvalidValue;
+    k_topk_limbs<<<ew_grid(n), kOpThreads, 0, stream>>>(d_sel, d_d1, d_d2, n, d_sel_idx, d_d1_idx, d_limbs,
+                                                          d_limb_idx);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_iota(uint64_t* d_out, uint64_t n, cudaStream_t stream) {
+    if (n == 0) return 0;
+    if (!d_out) return (int)cudaErrorInvalidValue;
+    k_iota<<<ew_grid(n), kOpThreads, 0, stream>>>(d_out, n);
     ZK_LAUNCH_CHECK();
     return 0;
 }

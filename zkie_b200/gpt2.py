@@ -31,7 +31,7 @@ import numpy as np
 from . import _lib
 from ._lib import lib
 from .gkr import XorShift64
-from .compose import (Add, GeluIndex, Layernorm, LayerNormCentered, Lookup, MatMul, Projection, Scale, Softmax,
+from .compose import (Add, Argmax, GeluIndex, Layernorm, LayerNormCentered, Lookup, MatMul, Projection, Scale, Softmax,
                       SoftmaxIndex, StableSoftmaxIndex, Transpose)
 
 P = 0xFFFFFFFF00000001
@@ -296,16 +296,15 @@ def build_layer(store, s: LayerShape, x, w, exp_t, rsqrt_t, gelu_t, mask_t):
 
 
 def gpt2_model(store, s: LayerShape, layers: int = 12, seed: int = 0x6B2):
-    """The GPT-2 graph of build_gpt2 (models/gpt2/src/lib.rs:321-436) up to the
-    masked logits: the token embedding as a Lookup into the tied lm_head
-    table (emb_idx[i D + d] = d vocab + token_i) plus the position
-    embedding, ``layers`` layers, the final LayerNormCentered, the lm_head
-    MatMul and the vocabulary mask Add.  The closing Argmax arm (topk.rs) is
-    not built, so the graph ends at the masked logits.  Synthetic inputs: the
-    tokens (below vocab_real), the position embedding, the lm_head weights
-    (d_real x vocab_real, zero-padded) and the final norm's scale and shift,
-    drawn after the layers' weights.  Returns (ops, tokens index id, logits
-    id)."""
+    """The GPT-2 graph of build_gpt2 (models/gpt2/src/lib.rs:321-436): the
+    token embedding as a Lookup into the tied lm_head table (emb_idx[i D + d]
+    = d vocab + token_i) plus the position embedding, ``layers`` layers, the
+    final LayerNormCentered, the lm_head MatMul, the vocabulary mask Add and
+    the Argmax over the masked logits (the next token of every position, a
+    public index tensor).  Synthetic inputs: the tokens (below vocab_real),
+    the position embedding, the lm_head weights (d_real x vocab_real,
+    zero-padded) and the final norm's scale and shift, drawn after the
+    layers' weights.  Returns (ops, tokens index id, argmax index id)."""
     rng = XorShift64(seed)
     m, D, V = s.m, s.d, s.vocab
     tokens = np.array([int(t) % s.vocab_real for t in xorshift_fill(rng, m, 1 << 30)], dtype=np.uint32)
@@ -340,4 +339,7 @@ def gpt2_model(store, s: LayerShape, layers: int = 12, seed: int = 0x6B2):
     mask_v = store.push(np.tile(vmask, m))
     logits_masked = store.push(None)
     ops.append(Add(logits, mask_v, logits_masked))
-    return ops, tok_t, logits_masked
+    sel, thr, gate, d1, d2 = (store.push(None) for _ in range(5))
+    out = store.push_idx(None)
+    ops.append(Argmax(logits_masked, sel, thr, gate, d1, d2, out, m, V))
+    return ops, tok_t, out
