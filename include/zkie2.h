@@ -490,6 +490,88 @@ int zkie2_op_iota(uint64_t *d_out, uint64_t n, zkie_stream_t stream);
  * would panic. */
 int zkie2_op_topk(const uint64_t *d_x, uint64_t m, uint64_t n, uint64_t k, uint64_t *d_thr, uint64_t *d_sel,
                   uint64_t *d_gate, uint64_t *d_d1, uint64_t *d_d2, uint32_t *d_out, zkie_stream_t stream);
+/* ---- the arms of an MLA attention / MoE layer (compose.rs:1193-1293, rms_norm.rs,
+ * rope.rs, scatter.rs, gather.rs, zkie-core common/batched_matmul.rs) ---- */
+/* The RmsNorm arm's forward (rms_norm.rs:37-95) over m rows of d, the first
+ * n_real of each averaged: d_outs = {ms (m), rstd (m), raw, out, rem_out,
+ * rem_lo, rem_hi (m d each), sum_sq (m), rem_s (m)}; d_s_index (m u32).  An
+ * rsqrt index at or past t sets bit 1 of *d_err. */
+int zkie2_op_rms_norm(const uint64_t *d_x, const uint64_t *d_w, const uint64_t *d_table, uint64_t t, uint64_t m,
+                      uint64_t d, uint64_t n_real, uint64_t *const *d_outs, uint32_t *d_s_index, uint32_t *d_err,
+                      zkie_stream_t stream);
+/* ScaleVec (compose.rs:1193-1212): out[i] = from_i64(round_div(to_i64(x[i])
+ * to_i64(scale[i % len]), 2^shift)), wrapping i64, shift <= 62. */
+int zkie2_op_scale_vec(const uint64_t *d_x, uint64_t n, const uint64_t *d_scale, uint64_t len, uint32_t shift,
+                       uint64_t *d_out, zkie_stream_t stream);
+/* BroadcastScale (:1284-1293): out[i] = x[i] scale[i / h] (field); scale
+ * holds len >= ceil(n / h) values. */
+int zkie2_op_broadcast_scale(const uint64_t *d_x, uint64_t n, const uint64_t *d_scale, uint64_t len, uint64_t h,
+                             uint64_t *d_out, zkie_stream_t stream);
+/* IdxBroadcast (:1258-1267): out[i b + j] = base[i] b + j (u32, wrapping). */
+int zkie2_op_idx_broadcast(const uint32_t *d_base, uint64_t nb, uint32_t b, uint32_t *d_out, zkie_stream_t stream);
+/* CombineIdx (:1268-1278): out[i] = a[i] scale + b[i] (u32, wrapping). */
+int zkie2_op_combine_idx(const uint32_t *d_a, const uint32_t *d_b, uint64_t n, uint32_t scale, uint32_t *d_out,
+                         zkie_stream_t stream);
+/* PadIdx (:1279-1283): out = base resized to len (zeros past nb). */
+int zkie2_op_pad_idx(const uint32_t *d_base, uint64_t nb, uint64_t len, uint32_t *d_out, zkie_stream_t stream);
+/* RoPE forward (rope.rs:87-124): x is m x heads x d (n values, d even), cos /
+ * sin m x d/2; rotate-half in wrapping i64, rounded by 2^shift. */
+int zkie2_op_rope(const uint64_t *d_x, uint64_t n, const uint64_t *d_cos, const uint64_t *d_sin, uint64_t m,
+                  uint64_t d, uint32_t shift, uint64_t *d_out, zkie_stream_t stream);
+/* The columns prove_rope reads (rope.rs:126-150), n / 2 values each:
+ * d_cols = {x_f, x_s, out_f, out_s, cos_b, sin_b, rem_f, rem_s}. */
+int zkie2_op_rope_columns(const uint64_t *d_x, const uint64_t *d_out, uint64_t n, const uint64_t *d_cos,
+                          const uint64_t *d_sin, uint64_t m, uint64_t d, uint32_t shift, uint64_t *const *d_cols,
+                          zkie_stream_t stream);
+/* Ones of the m x n one-hot sel (field value 1) per token row (by_token, m
+ * counts) or per expert column (n counts), u32. */
+int zkie2_op_sel_counts(const uint64_t *d_sel, uint64_t m, uint64_t n, uint32_t by_token, uint32_t *d_cnt,
+                        zkie_stream_t stream);
+/* scatter_forward (scatter.rs:12-25): for each expert in order, the tokens
+ * routed to it; d_expert_cnt from zkie2_op_sel_counts(by_token = 0); the
+ * outputs hold sum(d_expert_cnt) entries. */
+int zkie2_op_scatter(const uint64_t *d_sel, uint64_t m, uint64_t n, const uint32_t *d_expert_cnt,
+                     uint32_t *d_token_id, uint32_t *d_expert_of, zkie_stream_t stream);
+/* prove_scatter's multisets (scatter.rs:27-55): d_a (room for m n values) =
+ * the source encodings t n + e in token-major order (d_token_cnt from
+ * sel_counts(by_token = 1)), d_b[pos] = token_id[pos] n + expert_of[pos] for
+ * s positions.  Ones in sel other than s set bit 1 of *d_err (the reference
+ * asserts equal lengths). */
+int zkie2_op_scatter_encodings(const uint64_t *d_sel, uint64_t m, uint64_t n, const uint32_t *d_token_cnt,
+                               const uint32_t *d_token_id, const uint32_t *d_expert_of, uint64_t s, uint64_t *d_a,
+                               uint64_t *d_b, uint32_t *d_err, zkie_stream_t stream);
+/* build_perm_num_den (common/logup_gkr.rs:807-820) into total entries: num 1,
+ * den alpha - v for i < len, then 0 / alpha. */
+int zkie2_perm_num_den(const uint64_t *d_v, uint64_t len, uint64_t total, uint64_t alpha, uint64_t *d_num,
+                       uint64_t *d_den, zkie_stream_t stream);
+/* gather_forward (gather.rs:36-52): out[t] (h values) = the field sum over
+ * the positions routed to t of weighted[pos] gate[pos]; s positions, m
+ * tokens; scratch zkie2_op_gather_scratch_u32(s, m) u32 values.  A token id
+ * at or past m sets bit 1 of *d_err. */
+uint64_t zkie2_op_gather_scratch_u32(uint64_t s, uint64_t m);
+int zkie2_op_gather(const uint64_t *d_weighted, const uint32_t *d_token_id, const uint64_t *d_gate, uint64_t s,
+                    uint64_t m, uint64_t h, uint64_t *d_out, uint32_t *d_scratch_u32, uint32_t *d_err,
+                    zkie_stream_t stream);
+/* prove_scatter_add's columns (gather.rs:70-141) into total entries: with
+ * token ids and gate (the source side, rows = s positions) num = gamma[d]
+ * vals gate[pos], den = alpha - token_id[pos]; without (the target side,
+ * rows = m tokens) num = gamma[d] vals, den = alpha - t; then 0 / alpha.
+ * d_cols = {num, den, gamma_b, gate_b (source side only), vals_pad}. */
+int zkie2_scatter_add_columns(const uint64_t *d_vals, const uint64_t *d_gate, const uint32_t *d_token_id,
+                              const uint64_t *d_gamma, uint64_t rows, uint64_t h, uint64_t total, uint64_t alpha,
+                              uint64_t *const *d_cols, zkie_stream_t stream);
+/* gather_w_v's gather step (batched_matmul.rs:219-245): out[pos k + d] =
+ * wv[expert_of[pos] k + d] with wv the experts' weights contracted with
+ * eq(v) (zkie2_mle_partial_eval); an expert id at or past n_experts sets bit
+ * 1 of *d_err. */
+int zkie2_expert_rows(const uint64_t *d_wv, const uint32_t *d_expert_of, uint64_t s, uint64_t k, uint64_t n_experts,
+                      uint64_t *d_out, uint32_t *d_err, zkie_stream_t stream);
+/* expert_counts and expert_table_evals (batched_matmul.rs:247-277):
+ * counts[e] = sum over positions of expert e of eq_pos[pos]; table[e] = sum_d
+ * eq_d[d] wv[e k + d]. */
+int zkie2_expert_open(const uint32_t *d_expert_of, uint64_t s, const uint64_t *d_eq_pos, const uint64_t *d_wv,
+                      uint64_t k, const uint64_t *d_eq_d, uint64_t n_experts, uint64_t *d_counts, uint64_t *d_table,
+                      zkie_stream_t stream);
 /* The lookup columns of prove_topk (topk.rs:141-154) and prove_range_decomp
  * (:395-419) over n entries: to_i32(sel) and to_i32(d1) as u32 indices, and
  * the 16-bit limbs c0, c1, c2 of to_i64(d2) as u64, each as field values

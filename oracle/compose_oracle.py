@@ -213,6 +213,38 @@ def forward_ops(store, ops):
         elif k == "LayerNormCentered":
             store.v[op.out] = layer_norm_forward(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d,
                                                  op.n_real)["out"]
+        elif k == "ScaleVec":  # compose.rs:1193-1212
+            x, sv = g(op.x), g(op.scale)
+            sc = np.resize(to_i64(sv), x.size)
+            with np.errstate(over="ignore"):
+                store.v[op.out] = from_i64(round_div(to_i64(x) * sc, 1 << op.shift))
+        elif k == "BroadcastScale":  # :1284-1293
+            store.v[op.out] = o.vec_mul(g(op.x), np.repeat(g(op.scale), op.h)[:g(op.x).size])
+        elif k == "IdxBroadcast":  # :1258-1267
+            base = store.idx[op.base].astype(np.uint64)
+            v = base[:, None] * np.uint64(op.b) + np.arange(op.b, dtype=np.uint64)[None, :]
+            store.idx[op.out] = (v & np.uint64(0xFFFFFFFF)).astype(np.uint32).reshape(-1)
+        elif k == "CombineIdx":  # :1268-1278
+            a, b = store.idx[op.a].astype(np.uint64), store.idx[op.b].astype(np.uint64)
+            if a.size != b.size:
+                raise ValueError("CombineIdx: lengths differ")
+            store.idx[op.out] = ((a * np.uint64(op.scale) + b) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+        elif k == "PadIdx":  # :1279-1283
+            out = np.zeros(op.len, dtype=np.uint32)
+            base = store.idx[op.base][:op.len]
+            out[:base.size] = base
+            store.idx[op.out] = out
+        elif k == "Scatter":  # :1213-1223
+            store.idx[op.token_id], store.idx[op.expert_of] = scatter_forward(g(op.sel), op.m, op.n)
+        elif k == "Gather":  # :1224-1240
+            store.v[op.out] = gather_forward(g(op.weighted), store.idx[op.token_id], g(op.gate), op.m, op.h)
+        elif k == "GatherMatMul":  # :1245-1257
+            store.v[op.c] = gather_matmul_forward(g(op.a), store.idx[op.expert_of], g(op.w), op.s, op.k, op.n,
+                                                  op.n_experts)
+        elif k == "RmsNorm":  # :1509-1528
+            store.v[op.out] = rms_norm_forward(g(op.x), g(op.w), g(op.rsqrt_table), op.m, op.d, op.n_real)["out"]
+        elif k == "RoPE":  # :1529-1542
+            store.v[op.out] = rope_forward(g(op.x), g(op.cos), g(op.sin), op.m, op.d, op.shift)[0]
         elif k == "TopKSelect":
             (store.v[op.thr], store.v[op.sel], store.v[op.gate], store.v[op.d1],
              store.v[op.d2]) = topk_forward(g(op.x), op.m, op.n, op.k)
@@ -309,6 +341,239 @@ def prove_argmax(x, sel, thr, gate, d1, d2, out, m, n, range_bits, rng):
     """topk.rs:299-318 -> ("Argmax", topk proof, out, sel_evals = ())."""
     return ("Argmax", prove_topk(x, sel, thr, gate, d1, d2, m, n, 1, range_bits, rng),
             np.asarray(out, dtype=np.uint32).copy(), ())
+
+
+# ---- the arms of an MLA / MoE layer (rms_norm.rs, rope.rs, scatter.rs, gather.rs,
+# common/batched_matmul.rs, compose.rs:1193-1293) ------------------------------------------
+def rms_norm_forward(x, w, table, m, d, n_real):
+    """rms_norm.rs:37-95 -> dict(ms, s_index, rstd, raw, out, rem_out, rem_lo,
+    rem_hi, sum_sq, rem_s): ms = round(sum x^2 / n_real) in wrapping i64, the
+    rsqrt lookup, out = round(x rstd w / 2^32) and its remainder split in
+    16-bit halves (arithmetic shift for the high one)."""
+    x = o.u64(x).reshape(-1)
+    xi = to_i64(x).reshape(m, d)[:, :n_real]
+    with np.errstate(over="ignore"):
+        sq = (xi * xi).sum(axis=1)
+    ms = from_i64(round_div(sq, n_real))
+    s_index = rsqrt_index(to_i64(ms))
+    if s_index.size and int(s_index.max()) >= table.size:
+        raise IndexError("rsqrt table too short for the forward pass")
+    rstd = table[s_index.astype(np.int64)]
+    raw = o.vec_mul(o.vec_mul(x, _rows(rstd, m, d)), w)
+    ri = to_i64(raw)
+    out = from_i64(round_div(ri, 1 << 32))
+    with np.errstate(over="ignore"):
+        rem_i = ri - to_i64(out) * (1 << 32) + (1 << 31)
+        sum_sq = o.row_sums(o.vec_mul(x, x), m, d, n_real)
+        rem_s = from_i64(to_i64(sum_sq) - to_i64(ms) * n_real + n_real // 2)
+    rem_out = from_i64(rem_i)
+    ro = to_i64(rem_out)
+    return dict(ms=ms, s_index=s_index, rstd=rstd, raw=raw, out=out, rem_out=rem_out,
+                rem_lo=from_i64(ro & 0xFFFF), rem_hi=from_i64(ro >> 16), sum_sq=sum_sq, rem_s=rem_s)
+
+
+RMS_OUT_TERMS = [(1, [0, 1, 2]), (NEG, [3]), (1, [3]), (NEG * (1 << 32) % P, [4]), (NEG, [5]), (1 << 31, [6])]
+REM_SPLIT_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2])]
+
+
+def rms_trunc_terms(n_real):
+    return [(n_real % P, [0]), (1, [1]), (NEG, [2]), (NEG * (n_real // 2) % P, [3])]
+
+
+def prove_rms_norm(x, w, table, m, d, n_real, rng):
+    """rms_norm.rs:97-174 -> (("RmsNorm", trunc, out, rem_split, trunc_ch,
+    r_out, rem_split_ch), forward dict)."""
+    f = rms_norm_forward(x, w, table, m, d, n_real)
+    trunc_ch = _draw(rng, _lg(m))
+    trunc = _vp([f["ms"], f["rem_s"], f["sum_sq"], np.ones(m, dtype=np.uint64)], rms_trunc_terms(n_real), trunc_ch)
+    r_out = _draw(rng, _lg(m * d))
+    out = _vp([x, _rows(f["rstd"], m, d), w, f["raw"], f["out"], f["rem_out"], np.ones(m * d, dtype=np.uint64)],
+              RMS_OUT_TERMS, r_out)
+    rem_split_ch = _draw(rng, _lg(m * d))
+    rem_split = _vp([f["rem_out"], f["rem_lo"], f["rem_hi"]], REM_SPLIT_TERMS, rem_split_ch)
+    return ("RmsNorm", trunc, out, rem_split, trunc_ch, r_out, rem_split_ch), f
+
+
+def _rope_halves(v, m, d):
+    """extract_first / extract_second (rope.rs:47-71): [m, heads, d] split into
+    its two d/2 halves, each [m, heads, d/2] flattened."""
+    v = o.u64(v).reshape(m, -1, d)
+    return np.ascontiguousarray(v[:, :, :d // 2]).reshape(-1), np.ascontiguousarray(v[:, :, d // 2:]).reshape(-1)
+
+
+def _rope_pair(table, m, d, heads):
+    """broadcast_pair (rope.rs:73-85): [m, d/2] repeated over the heads."""
+    return np.repeat(o.u64(table).reshape(m, 1, d // 2), heads, axis=1).reshape(-1)
+
+
+def rope_forward(x, cos, sin, m, d, shift):
+    """rope.rs:87-124 -> (out, rem_f, rem_s): rotate-half in wrapping i64,
+    each product rounded by 2^shift, remainders offset by 2^(shift-1)."""
+    heads = o.u64(x).size // (m * d)
+    xf, xs = (to_i64(h).reshape(m, heads, d // 2) for h in _rope_halves(x, m, d))
+    c = to_i64(cos).reshape(m, 1, d // 2)
+    sn = to_i64(sin).reshape(m, 1, d // 2)
+    with np.errstate(over="ignore"):
+        raw_f = xf * c - xs * sn
+        raw_s = xs * c + xf * sn
+        of = round_div(raw_f.reshape(-1), 1 << shift).reshape(raw_f.shape)
+        os_ = round_div(raw_s.reshape(-1), 1 << shift).reshape(raw_s.shape)
+        rem_f = from_i64((raw_f - of * (1 << shift) + (1 << (shift - 1))).reshape(-1))
+        rem_s = from_i64((raw_s - os_ * (1 << shift) + (1 << (shift - 1))).reshape(-1))
+    out = np.concatenate([from_i64(of.reshape(-1)).reshape(m, heads, d // 2),
+                          from_i64(os_.reshape(-1)).reshape(m, heads, d // 2)], axis=2).reshape(-1)
+    return out, rem_f, rem_s
+
+
+def rope_terms(shift, second):
+    two, half = 1 << shift, 1 << (shift - 1)
+    return [(1, [0, 1]), ((1 if second else NEG), [2, 3]), (NEG * two % P, [4]), (NEG, [5]), (half, [6])]
+
+
+def prove_rope(x, cos, sin, out, m, d, shift, rng):
+    """rope.rs:126-196 -> (("RoPE", first, second, r_first, r_second, r_out),
+    rem_f, rem_s)."""
+    heads = o.u64(x).size // (m * d)
+    _, rem_f, rem_s = rope_forward(x, cos, sin, m, d, shift)
+    x_f, x_s = _rope_halves(x, m, d)
+    o_f, o_s = _rope_halves(out, m, d)
+    cos_b, sin_b = _rope_pair(cos, m, d, heads), _rope_pair(sin, m, d, heads)
+    n = m * heads * (d // 2)
+    ones = np.ones(n, dtype=np.uint64)
+    r_f = _draw(rng, _lg(n))
+    first = _vp([x_f, cos_b, x_s, sin_b, o_f, rem_f, ones], rope_terms(shift, False), r_f)
+    r_s = _draw(rng, _lg(n))
+    second = _vp([x_s, cos_b, x_f, sin_b, o_s, rem_s, ones], rope_terms(shift, True), r_s)
+    r_out = _draw(rng, _lg(o.u64(out).size))
+    return ("RoPE", first, second, r_f, r_s, r_out), rem_f, rem_s
+
+
+def scatter_forward(sel, m, n):
+    """scatter.rs:12-25 -> (token_id, expert_of) in expert-major order."""
+    s = (o.u64(sel).reshape(m, n) == 1)
+    e_idx, t_idx = np.nonzero(s.T)
+    return t_idx.astype(np.uint32), e_idx.astype(np.uint32)
+
+
+def _perm_num_den(values, alpha):
+    """build_perm_num_den (logup_gkr.rs:807-820): num 1, den alpha - value,
+    padded to max(next power of two, 32) with 0 / alpha."""
+    v = o.u64(values).reshape(-1)
+    total = max(1 << max(v.size - 1, 0).bit_length(), 32)
+    num = np.zeros(total, dtype=np.uint64)
+    den = np.full(total, int(alpha) % P, dtype=np.uint64)
+    num[:v.size] = 1
+    den[:v.size] = o.vec_sub(np.full(v.size, int(alpha) % P, dtype=np.uint64), v)
+    return num, den
+
+
+def prove_permutation(a, b, rng):
+    """logup_gkr.rs:822-840 -> (a_side, b_side, alpha, a, b)."""
+    alpha = rng.field()
+    na, da = _perm_num_den(a, alpha)
+    nb, db = _perm_num_den(b, alpha)
+    a_side = prove_fractional(na, da, rng)
+    b_side = prove_fractional(nb, db, rng)
+    return (a_side, b_side, int(alpha), o.u64(a).reshape(-1).copy(), o.u64(b).reshape(-1).copy())
+
+
+def prove_scatter(sel, token_id, expert_of, m, n, rng):
+    """scatter.rs:39-55: the source encodings t n + e in token-major order
+    against token_id n + expert_of, as a permutation."""
+    s = (o.u64(sel).reshape(m, n) == 1)
+    t_idx, e_idx = np.nonzero(s)
+    a = (t_idx * n + e_idx).astype(np.uint64)
+    b = np.asarray(token_id, dtype=np.uint64) * np.uint64(n) + np.asarray(expert_of, dtype=np.uint64)
+    return ("Scatter", prove_permutation(a, b, rng))
+
+
+def gather_forward(weighted, token_id, gate, m, h):
+    """gather.rs:36-52: out[t] = sum over positions routed to t of
+    weighted[pos] gate[pos] (field)."""
+    tid = np.asarray(token_id, dtype=np.int64)
+    wg = o.vec_mul(o.u64(weighted).reshape(-1), np.repeat(o.u64(gate).reshape(-1), h))
+    out = np.zeros(m * h, dtype=np.uint64)
+    for pos, t in enumerate(tid):
+        out[t * h:(t + 1) * h] = o.vec_add(out[t * h:(t + 1) * h], wg[pos * h:(pos + 1) * h])
+    return out
+
+
+def _pow2(n):
+    return 1 << max(int(n) - 1, 0).bit_length()
+
+
+def prove_scatter_add(weighted, token_id, gate, out, m, h, rng):
+    """gather.rs:54-157 -> ("Gather", source_side, target_side, alpha, gamma,
+    num_source, den_source, num_target, den_target, prod_source, prod_target,
+    r_prod_source, r_prod_target, weighted, gate, out, token_id)."""
+    weighted, gate, out = (o.u64(v).reshape(-1) for v in (weighted, gate, out))
+    tid = np.asarray(token_id, dtype=np.uint64)
+    s = tid.size
+    alpha = int(rng.field()) % P
+    gamma = _draw(rng, h)
+    st, tt = _pow2(s * h), _pow2(m * h)
+    gamma_s = np.zeros(st, dtype=np.uint64)
+    gamma_s[:s * h] = np.tile(gamma, s)
+    gate_b = np.zeros(st, dtype=np.uint64)
+    gate_b[:s * h] = np.repeat(gate, h)
+    w_pad = np.zeros(st, dtype=np.uint64)
+    w_pad[:s * h] = weighted
+    num_s = o.vec_mul(o.vec_mul(gamma_s, w_pad), gate_b)
+    den_s = np.full(st, alpha, dtype=np.uint64)
+    den_s[:s * h] = o.vec_sub(den_s[:s * h], np.repeat(tid, h))
+    gamma_t = np.zeros(tt, dtype=np.uint64)
+    gamma_t[:m * h] = np.tile(gamma, m)
+    o_pad = np.zeros(tt, dtype=np.uint64)
+    o_pad[:m * h] = out
+    num_t = o.vec_mul(gamma_t, o_pad)
+    den_t = np.full(tt, alpha, dtype=np.uint64)
+    den_t[:m * h] = o.vec_sub(den_t[:m * h], np.repeat(np.arange(m, dtype=np.uint64), h))
+    source_side = prove_fractional(num_s, den_s, rng)
+    target_side = prove_fractional(num_t, den_t, rng)
+    r_ps = _draw(rng, _lg(st))
+    prod_source = _vp([o.eq_evals(r_ps), num_s, gamma_s, w_pad, gate_b], SCATTER_ADD_SOURCE_TERMS, r_ps)
+    r_pt = _draw(rng, _lg(tt))
+    prod_target = _vp([o.eq_evals(r_pt), num_t, gamma_t, o_pad], SCATTER_ADD_TARGET_TERMS, r_pt)
+    return ("Gather", source_side, target_side, alpha, gamma, num_s, den_s, num_t, den_t, prod_source, prod_target,
+            r_ps, r_pt, weighted.copy(), gate.copy(), out.copy(), tid.astype(np.uint32))
+
+
+SCATTER_ADD_SOURCE_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3, 4])]
+SCATTER_ADD_TARGET_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3])]
+BMM_TERMS = [(1, [0, 1, 2])]
+
+
+def gather_matmul_forward(seg, expert_of, w_all, s, k, n, n_experts):
+    """batched_matmul.rs:331-357: g[pos] = seg[pos] W_all[expert_of[pos]] (field)."""
+    seg = o.u64(seg).reshape(s, k)
+    w_all = o.u64(w_all).reshape(n_experts, k, n)
+    g = np.zeros((s, n), dtype=np.uint64)
+    e_of = np.asarray(expert_of, dtype=np.int64)
+    for e in np.unique(e_of):
+        rows = np.nonzero(e_of == e)[0]
+        g[rows] = o.matmul_field(seg[rows], w_all[e])
+    return g.reshape(-1)
+
+
+def prove_gather_matmul(seg, expert_of, w_all, g, s, k, n, n_experts, u, v, ch):
+    """batched_matmul.rs:359-390 (prove_streaming) and :469-494 -> (claimed,
+    (rounds, finals), counts, table): the eq-selector sumcheck over [seg,
+    w_v, eq(u) per row], w_v the experts' weights contracted with eq(v)."""
+    w_all = o.u64(w_all).reshape(n_experts, k, n)
+    e_of = np.asarray(expert_of, dtype=np.int64)
+    eq_v = o.eq_evals(v)
+    wv = np.stack([o.matmul_field(w_all[e], eq_v.reshape(n, 1)).reshape(-1) for e in range(n_experts)])
+    w_v = wv[e_of].reshape(-1)
+    eq_b = np.repeat(o.eq_evals(u), k)
+    claimed = o.mle_eval(g, np.concatenate([v, u]))
+    sc = _vp([seg, w_v, eq_b], BMM_TERMS, ch)
+    kb = _lg(k)
+    eq_pos = o.eq_evals(ch[kb:])
+    counts = np.zeros(n_experts, dtype=np.uint64)
+    for pos, e in enumerate(e_of):
+        counts[e] = (int(counts[e]) + int(eq_pos[pos])) % P
+    table = np.array([int(o.mle_eval(wv[e], ch[:kb])) for e in range(n_experts)], dtype=np.uint64)
+    return (int(claimed), sc, counts, table)
 
 
 # ---- op arms -----------------------------------------------------------------------------
@@ -432,6 +697,9 @@ def prove_lookup_table(m, table, alpha, beta, rng):
 
 # ---- shard (compose.rs:1602-2091, 2276-2346) -------------------------------------------------
 ADD_TERMS = [(1, [2]), (NEG, [0]), (NEG, [1])]
+# the arms with no proof of their own (compose.rs:1623-1723)
+MARKER_KINDS = ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "ScaleVec", "IdxBroadcast",
+                "CombineIdx", "PadIdx", "BroadcastScale")
 
 
 def prove_shard_precomputed(store, ops, boundary, rng):
@@ -445,7 +713,7 @@ def prove_shard_precomputed(store, ops, boundary, rng):
 
     for op in ops:
         k = op.kind
-        if k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex"):
+        if k in MARKER_KINDS:
             op_proofs.append((k,))
         elif k == "MatMul":
             r = o.op_matmul_prove(g(op.a).reshape(op.m, op.k), g(op.b).reshape(op.k, op.n),
@@ -497,6 +765,33 @@ def prove_shard_precomputed(store, ops, boundary, rng):
             claim(op.x, p[7])
             for t in (op.out, op.w, op.b):
                 claim(t, p[10])
+            op_proofs.append(p)
+        elif k == "Scatter":  # compose.rs:1632-1648
+            op_proofs.append(prove_scatter(g(op.sel), store.idx[op.token_id], store.idx[op.expert_of], op.m, op.n,
+                                           rng))
+        elif k == "Gather":  # :1649-1667
+            op_proofs.append(prove_scatter_add(g(op.weighted), store.idx[op.token_id], g(op.gate), g(op.out), op.m,
+                                               op.h, rng))
+        elif k == "GatherMatMul":  # :1682-1705
+            u, v, ch = _draw(rng, _lg(op.s)), _draw(rng, _lg(op.n)), _draw(rng, _lg(op.s * op.k))
+            p = prove_gather_matmul(g(op.a), store.idx[op.expert_of], g(op.w), g(op.c), op.s, op.k, op.n,
+                                    op.n_experts, u, v, ch)
+            claims.append((op.a, ch.copy(), int(p[1][1][0])))
+            claims.append((op.c, np.concatenate([v, u]), p[0]))
+            op_proofs.append(("GatherMatMul", p, u, v, ch))
+        elif k == "RmsNorm":  # :1898-1934
+            p, f = prove_rms_norm(g(op.x), g(op.w), g(op.rsqrt_table), op.m, op.d, op.n_real, rng)
+            lookups.setdefault(op.rsqrt_table, []).append((f["s_index"], f["rstd"]))
+            for part in ("rem_lo", "rem_hi"):
+                lookups.setdefault(op.limb_table, []).append((o.to_i32_indices(f[part]), f[part]))
+            claim(op.out, p[5])
+            claim(op.w, p[5])
+            op_proofs.append(p)
+        elif k == "RoPE":  # :1935-1967
+            p, rem_f, rem_s = prove_rope(g(op.x), g(op.cos), g(op.sin), g(op.out), op.m, op.d, op.shift, rng)
+            for rem in (rem_f, rem_s):
+                lookups.setdefault(op.range_table, []).append((o.to_i32_indices(rem), rem))
+            claim(op.out, p[5])
             op_proofs.append(p)
         elif k in ("TopKSelect", "Argmax"):
             args = (g(op.x), g(op.sel), g(op.thr), g(op.gate), g(op.d1), g(op.d2))
@@ -667,6 +962,45 @@ def verify_argmax(p, m, n):
     return True
 
 
+def verify_rms_norm(p, n_real):
+    """rms_norm.rs:176-222."""
+    _, trunc, out, rem_split, trunc_ch, r_out, rem_split_ch = p
+    return (_verify_virtual(trunc, rms_trunc_terms(n_real), 0, trunc_ch)
+            and _verify_virtual(out, RMS_OUT_TERMS, 0, r_out)
+            and _verify_virtual(rem_split, REM_SPLIT_TERMS, 0, rem_split_ch))
+
+
+def verify_rope(p, shift):
+    """rope.rs:198-230."""
+    _, first, second, r_f, r_s, _ = p
+    return (_verify_virtual(first, rope_terms(shift, False), 0, r_f)
+            and _verify_virtual(second, rope_terms(shift, True), 0, r_s))
+
+
+def verify_scatter(p):
+    """scatter.rs:57-59 / logup_gkr.rs:842-844."""
+    a_side, b_side = p[1][0], p[1][1]
+    return verify_lookup_split(a_side, b_side)
+
+
+def verify_scatter_add(p):
+    """gather.rs:159-186."""
+    return (verify_lookup_split(p[1], p[2])
+            and _verify_virtual(p[9], SCATTER_ADD_SOURCE_TERMS, 0, p[11])
+            and _verify_virtual(p[10], SCATTER_ADD_TARGET_TERMS, 0, p[12]))
+
+
+def verify_gather_matmul(p, s, k):
+    """batched_matmul.rs:496-513: the sumcheck with the public eq(u) selector's
+    final value recomputed, then the weight claim against sum_e counts table."""
+    _, (claimed, (rounds, finals), counts, table), u, _, ch = p
+    eq_final = o.mle_eval(np.repeat(o.eq_evals(u), k), ch)
+    fin = np.array([int(finals[0]), int(finals[1]), int(eq_final)], dtype=np.uint64)
+    if not o.virtual_verify(rounds, BMM_TERMS, claimed, ch, fin):
+        return False
+    return int(finals[1]) % P == sum(int(c) * int(t) for c, t in zip(counts, table)) % P
+
+
 def verify_same_poly(sp, claims):
     """same_poly.rs:46-70: the merged evaluation, or None."""
     coeffs, vp, merged, merged_eval = sp
@@ -707,12 +1041,22 @@ def verify_shard(ops, proof):
             ok = verify_layernorm_chain(p)
         elif k == "LayerNormCentered":
             ok = verify_layer_norm_centered(p, op.n_real)
+        elif k == "RmsNorm":
+            ok = verify_rms_norm(p, op.n_real)
+        elif k == "RoPE":
+            ok = verify_rope(p, op.shift)
+        elif k == "Scatter":
+            ok = verify_scatter(p)
+        elif k == "Gather":
+            ok = verify_scatter_add(p)
+        elif k == "GatherMatMul":
+            ok = verify_gather_matmul(p, op.s, op.k)
         elif k == "TopKSelect":
             ok = verify_topk(p, op.k)
         elif k == "Argmax":
             ok = verify_argmax(p, op.m, op.n)
         else:
-            ok = k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex")
+            ok = k in MARKER_KINDS
         if not ok:
             return False
     by_tensor = {}

@@ -1,0 +1,103 @@
+"""The MLA / MoE arms on the device (zkie_b200/csrc/moe.cu, the RmsNorm,
+RoPE, Scatter, Gather, GatherMatMul and index arms of zkie_b200/compose.py)
+against the CPU restatement: a DeepSeek-V2-Lite-shaped MoE layer's forward
+witness tensor for tensor, and its shard proof value for value."""
+import numpy as np
+import pytest
+
+from oracle import compose_oracle as co
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(m=8, h=16, heads=2, qk_nope=4, qk_rope=4, v_head=4, kv_lora=8, n_routed=8, top_k=2, moe=8, moe_real=6,
+             shared=16, shared_real=12, exp_bits=8, silu_bits=12, rsqrt_len=1 << 12, w_mod=1 << 12, router_mod=1 << 10)
+MEDIUM = dict(m=32, h=256, heads=2, qk_nope=16, qk_rope=8, v_head=16, kv_lora=32, n_routed=16, top_k=3, moe=64,
+              moe_real=48, shared=128, shared_real=96, exp_bits=12, silu_bits=16, rsqrt_len=1 << 16, w_mod=1 << 8,
+              router_mod=1 << 10)
+
+
+def _stores(zk, shape):
+    from zkie_b200 import deepseek as ds
+    host = co.HostStore()
+    ops, x, out = ds.moe_layer(host, ds.MoeShape(**shape))
+    dev = zk.compose.Store()
+    for v in host.v:
+        dev.push(None if v is None else v.copy())
+    for i in host.idx:
+        dev.push_idx(None if i is None else i.copy())
+    return host, dev, ops, out
+
+
+def _assert_same(a, b, path="proof"):
+    if isinstance(a, dict):
+        assert a.keys() == b.keys(), path
+        for k in a:
+            _assert_same(a[k], b[k], f"{path}.{k}")
+    elif isinstance(a, (list, tuple)):
+        assert isinstance(b, (list, tuple)) and len(a) == len(b), f"{path}: {len(a)} vs {len(b)}"
+        for i, (x, y) in enumerate(zip(a, b)):
+            _assert_same(x, y, f"{path}[{i}]")
+    elif isinstance(a, np.ndarray) or isinstance(b, np.ndarray):
+        x, y = np.asarray(a, dtype=np.uint64), np.asarray(b, dtype=np.uint64)
+        assert x.shape == y.shape and np.array_equal(x, y), f"{path}: arrays differ"
+    elif isinstance(a, str):
+        assert a == b, f"{path}: {a} vs {b}"
+    else:
+        assert int(a) % co.P == int(b) % co.P, f"{path}: {a} vs {b}"
+
+
+@pytest.mark.parametrize("shape", [SMALL, MEDIUM], ids=["small", "medium"])
+def test_moe_layer_forward_matches_oracle(zk, shape):
+    host, dev, ops, out = _stores(zk, shape)
+    zk.compose.forward_ops(dev, ops)
+    co.forward_ops(host, ops)
+    for t, v in enumerate(host.v):
+        if v is not None:
+            assert np.array_equal(dev.get(t).cpu().numpy(), v), f"tensor {t}"
+    for t, v in enumerate(host.idx):
+        if v is not None:
+            assert np.array_equal(dev.get_idx(t).cpu().numpy(), v), f"index tensor {t}"
+    assert np.count_nonzero(host.v[out])
+
+
+@pytest.mark.parametrize("shape", [SMALL, MEDIUM], ids=["small", "medium"])
+def test_moe_layer_shard_matches_oracle(zk, shape):
+    host, dev, ops, _ = _stores(zk, shape)
+    zk.compose.forward_ops(dev, ops)
+    got = zk.compose.prove_shard_precomputed(dev, ops, [], zk.gkr.XorShift64(33)).canonical()
+    want = co.prove_shard(host, ops, [], o.XorShift64(33))
+    _assert_same(got, want)
+    assert co.verify_shard(ops, want)
+
+
+def test_moe_layer_graph_replay(zk):
+    """The MoE layer's proof recorded once as a CUDA graph and replayed: the
+    eager proof's digest."""
+    from zkie_b200 import dag
+    host, dev, ops, _ = _stores(zk, MEDIUM)
+    C = zk.compose
+    C.forward_ops(dev, ops)
+    master = C.master_transcript(ops, len(ops))
+
+    def make_rng():
+        c = master.clone()
+        c.absorb_u64(0)
+        return c
+    eager = dag.digest(C.prove_shard_precomputed(dev, ops, [], make_rng()).canonical())
+    gp = C.GraphShardProver(dev, ops, [], make_rng)
+    gp.replay()
+    assert dag.digest(gp.prove().canonical()) == eager
+
+
+def test_gather_token_outside_is_an_error(zk):
+    import torch
+    C = zk.compose
+    st = C.Store()
+    w = st.push(np.arange(8, dtype=np.uint64))
+    tid = st.push_idx(np.array([0, 5], dtype=np.uint32))  # 5 >= m
+    g = st.push(np.ones(2, dtype=np.uint64))
+    out = st.push(None)
+    with pytest.raises(ValueError, match="lookup index"):
+        C.forward_ops(st, [C.Gather(w, tid, g, out, 4, 4)])
+    torch.cuda.synchronize()

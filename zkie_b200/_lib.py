@@ -145,6 +145,23 @@ SIGNATURES = {
     "zkie2_op_iota": (i64, [vp, u64, vp]),
     "zkie2_op_topk": (i64, [vp, u64, u64, u64, vp, vp, vp, vp, vp, vp, vp]),
     "zkie2_op_topk_limbs": (i64, [vp, vp, vp, u64, vp, vp, vp, vp, vp]),
+    "zkie2_op_rms_norm": (i64, [vp, vp, vp, u64, u64, u64, u64, vp, vp, vp, vp]),
+    "zkie2_op_scale_vec": (i64, [vp, u64, vp, u64, u32, vp, vp]),
+    "zkie2_op_broadcast_scale": (i64, [vp, u64, vp, u64, u64, vp, vp]),
+    "zkie2_op_idx_broadcast": (i64, [vp, u64, u32, vp, vp]),
+    "zkie2_op_combine_idx": (i64, [vp, vp, u64, u32, vp, vp]),
+    "zkie2_op_pad_idx": (i64, [vp, u64, u64, vp, vp]),
+    "zkie2_op_rope": (i64, [vp, u64, vp, vp, u64, u64, u32, vp, vp]),
+    "zkie2_op_rope_columns": (i64, [vp, vp, u64, vp, vp, u64, u64, u32, vp, vp]),
+    "zkie2_op_sel_counts": (i64, [vp, u64, u64, u32, vp, vp]),
+    "zkie2_op_scatter": (i64, [vp, u64, u64, vp, vp, vp, vp]),
+    "zkie2_op_scatter_encodings": (i64, [vp, u64, u64, vp, vp, vp, u64, vp, vp, vp, vp]),
+    "zkie2_perm_num_den": (i64, [vp, u64, u64, u64, vp, vp, vp]),
+    "zkie2_op_gather_scratch_u32": (u64, [u64, u64]),
+    "zkie2_op_gather": (i64, [vp, vp, vp, u64, u64, u64, vp, vp, vp, vp]),
+    "zkie2_scatter_add_columns": (i64, [vp, vp, vp, vp, u64, u64, u64, u64, vp, vp]),
+    "zkie2_expert_rows": (i64, [vp, vp, u64, u64, u64, vp, vp, vp]),
+    "zkie2_expert_open": (i64, [vp, u64, vp, vp, u64, vp, u64, vp, vp, vp]),
     "zkie2_eq_combine_scratch_elems": (u64, [u32, u32]),
     "zkie2_eq_combine": (i64, [pu64, pu64, u32, u32, vp, vp, vp]),
     "zkie2_mg_available": (i64, []),

@@ -222,6 +222,119 @@ class Argmax(_Op):
     _reads, _writes = ("x",), ("sel", "thr", "gate", "d1", "d2")
 
 
+@dataclass
+class ScaleVec(_Op):
+    x: int
+    scale: int
+    out: int
+    shift: int
+    kind = "ScaleVec"
+    _reads, _writes = ("x", "scale"), ("out",)
+
+
+@dataclass
+class BroadcastScale(_Op):
+    x: int
+    scale: int
+    out: int
+    h: int
+    kind = "BroadcastScale"
+    _reads, _writes = ("x", "scale"), ("out",)
+
+
+@dataclass
+class IdxBroadcast(_Op):
+    base: int  # index tensors in and out
+    out: int
+    b: int
+    kind = "IdxBroadcast"
+    _reads, _writes = ("base",), ("out",)
+
+
+@dataclass
+class CombineIdx(_Op):
+    a: int  # index tensors in and out
+    b: int
+    out: int
+    scale: int
+    kind = "CombineIdx"
+    _reads, _writes = ("a", "b"), ("out",)
+
+
+@dataclass
+class PadIdx(_Op):
+    base: int  # index tensors in and out
+    out: int
+    len: int
+    kind = "PadIdx"
+    _reads, _writes = ("base",), ("out",)
+
+
+@dataclass
+class RmsNorm(_Op):
+    x: int
+    w: int
+    out: int
+    rsqrt_table: int
+    limb_table: int
+    m: int
+    d: int
+    n_real: int
+    kind = "RmsNorm"
+    _reads, _writes = ("x", "w", "rsqrt_table", "limb_table"), ("out",)
+
+
+@dataclass
+class RoPE(_Op):
+    x: int
+    cos: int
+    sin: int
+    out: int
+    range_table: int
+    m: int
+    d: int
+    shift: int
+    kind = "RoPE"
+    _reads, _writes = ("x", "cos", "sin", "range_table"), ("out",)
+
+
+@dataclass
+class Scatter(_Op):
+    sel: int
+    token_id: int  # index tensors out
+    expert_of: int
+    m: int
+    n: int
+    kind = "Scatter"
+    _reads, _writes = ("sel",), ("token_id", "expert_of")
+
+
+@dataclass
+class Gather(_Op):
+    weighted: int
+    token_id: int  # an index tensor
+    gate: int
+    out: int
+    m: int
+    h: int
+    kind = "Gather"
+    _reads, _writes = ("weighted", "token_id", "gate"), ("out",)
+
+
+@dataclass
+class GatherMatMul(_Op):
+    a: int
+    expert_of: int  # an index tensor
+    w: int
+    c: int
+    s: int
+    k: int
+    n: int
+    n_experts: int
+    kind = "GatherMatMul"
+    _reads, _writes = ("a", "expert_of", "w"), ("c",)
+
+
 # ---- the store (compose.rs:525-560) -------------------------------------------------------
 class Store:
     """Field tensors ``v`` and u32 index tensors ``idx`` on the device, two id
@@ -289,6 +402,49 @@ def layer_norm_centered_columns(x, w, b, table, m, d, n_real, err):
           "zkie2_op_layer_norm_centered")
     outs["s_index"] = s_index[:m]
     return outs
+
+
+def rms_norm_columns(x, w, table, m, d, n_real, err):
+    """rms_norm_forward (rms_norm.rs:37-95) on the device: a dict of ms, rstd,
+    raw, out, rem_out, rem_lo, rem_hi, sum_sq, rem_s and s_index."""
+    names = ("ms", "rstd", "raw", "out", "rem_out", "rem_lo", "rem_hi", "sum_sq", "rem_s")
+    sizes = (m, m, m * d, m * d, m * d, m * d, m * d, m, m)
+    outs = {k: empty(sz) for k, sz in zip(names, sizes)}
+    s_index = _u32(m)
+    arr = (_lib.vp * 9)(*[ptr(outs[k]) for k in names])
+    check(lib.zkie2_op_rms_norm(ptr(x), ptr(w), ptr(table), table.numel(), m, d, n_real, arr, s_index.data_ptr(),
+                                err.data_ptr(), stream_handle()), "zkie2_op_rms_norm")
+    outs["s_index"] = s_index[:m]
+    return outs
+
+
+def _index_i32(v: torch.Tensor) -> torch.Tensor:
+    """to_i32(v) as u32 of every value."""
+    idx = _u32(v.numel())
+    check(lib.zkie2_lookup_index_i32(ptr(v), v.numel(), idx.data_ptr(), stream_handle()), "zkie2_lookup_index_i32")
+    return idx[:v.numel()]
+
+
+def _gather_matmul_forward(store: Store, op, err):
+    """gather_matmul_forward (batched_matmul.rs:331-357): the positions of
+    each run of equal experts times that expert's K x N block (the exact
+    field product, on the tensor cores where the inputs are 16-bit)."""
+    a, eof, w = store.get(op.a), store.get_idx(op.expert_of), store.get(op.w)
+    s, k, n, ne = op.s, op.k, op.n, op.n_experts
+    if a.numel() != s * k or eof.numel() != s or w.numel() != ne * k * n:
+        raise ValueError("GatherMatMul: tensor sizes do not match s, k, n, n_experts")
+    c = _slot(store, op.c, s * n)
+    e = eof.cpu().numpy().astype(np.int64)
+    if e.size and int(e.max()) >= ne:
+        raise ValueError("GatherMatMul: an expert index outside the weights")
+    p0 = 0
+    while p0 < s:
+        p1 = p0 + 1
+        while p1 < s and e[p1] == e[p0]:
+            p1 += 1
+        blk = w[int(e[p0]) * k * n:(int(e[p0]) + 1) * k * n]
+        c[p0 * n:p1 * n].copy_(_matmul_fixed(a[p0 * k:p1 * k], blk, p1 - p0, k, n))
+        p0 = p1
 
 
 def layernorm_columns(x, w, b, table, m, d):
@@ -388,6 +544,59 @@ def forward_ops(store: Store, ops):
             out = layer_norm_centered_columns(g(op.x), g(op.w), g(op.b), g(op.rsqrt_table), op.m, op.d, op.n_real,
                                               err)["out"]
             _slot(store, op.out, out.numel()).copy_(out)
+        elif k == "RmsNorm":
+            out = rms_norm_columns(g(op.x), g(op.w), g(op.rsqrt_table), op.m, op.d, op.n_real, err)["out"]
+            _slot(store, op.out, out.numel()).copy_(out)
+        elif k == "RoPE":
+            x = g(op.x)
+            out = _slot(store, op.out, x.numel())
+            check(lib.zkie2_op_rope(ptr(x), x.numel(), ptr(g(op.cos)), ptr(g(op.sin)), op.m, op.d, op.shift, ptr(out),
+                                    sh), "zkie2_op_rope")
+        elif k == "ScaleVec":
+            x, sv = g(op.x), g(op.scale)
+            out = _slot(store, op.out, x.numel())
+            check(lib.zkie2_op_scale_vec(ptr(x), x.numel(), ptr(sv), sv.numel(), op.shift, ptr(out), sh),
+                  "zkie2_op_scale_vec")
+        elif k == "BroadcastScale":
+            x, sv = g(op.x), g(op.scale)
+            out = _slot(store, op.out, x.numel())
+            check(lib.zkie2_op_broadcast_scale(ptr(x), x.numel(), ptr(sv), sv.numel(), op.h, ptr(out), sh),
+                  "zkie2_op_broadcast_scale")
+        elif k == "IdxBroadcast":
+            base = store.get_idx(op.base)
+            out = _islot(store, op.out, base.numel() * op.b)
+            check(lib.zkie2_op_idx_broadcast(base.data_ptr(), base.numel(), op.b, out.data_ptr(), sh),
+                  "zkie2_op_idx_broadcast")
+        elif k == "CombineIdx":
+            a, b = store.get_idx(op.a), store.get_idx(op.b)
+            if a.numel() != b.numel():
+                raise ValueError("CombineIdx: index tensors differ in length")
+            out = _islot(store, op.out, a.numel())
+            check(lib.zkie2_op_combine_idx(a.data_ptr(), b.data_ptr(), a.numel(), op.scale, out.data_ptr(), sh),
+                  "zkie2_op_combine_idx")
+        elif k == "PadIdx":
+            base = store.get_idx(op.base)
+            out = _islot(store, op.out, op.len)
+            check(lib.zkie2_op_pad_idx(base.data_ptr(), base.numel(), op.len, out.data_ptr(), sh), "zkie2_op_pad_idx")
+        elif k == "Scatter":
+            sel = g(op.sel)
+            cnt = _u32(op.n)
+            check(lib.zkie2_op_sel_counts(ptr(sel), op.m, op.n, 0, cnt.data_ptr(), sh), "zkie2_op_sel_counts")
+            total = int(cnt[:op.n].to(torch.int64).sum().item())
+            tid, eof = _islot(store, op.token_id, total), _islot(store, op.expert_of, total)
+            check(lib.zkie2_op_scatter(ptr(sel), op.m, op.n, cnt.data_ptr(), tid.data_ptr(), eof.data_ptr(), sh),
+                  "zkie2_op_scatter")
+        elif k == "Gather":
+            wt, tid, gate = g(op.weighted), store.get_idx(op.token_id), g(op.gate)
+            s_ = tid.numel()
+            if gate.numel() != s_ or wt.numel() != s_ * op.h:
+                raise ValueError("Gather: weighted, token_id and gate lengths do not match")
+            out = _slot(store, op.out, op.m * op.h)
+            scr = _u32(lib.zkie2_op_gather_scratch_u32(s_, op.m))
+            check(lib.zkie2_op_gather(ptr(wt), tid.data_ptr(), ptr(gate), s_, op.m, op.h, ptr(out), scr.data_ptr(),
+                                      err.data_ptr(), sh), "zkie2_op_gather")
+        elif k == "GatherMatMul":
+            _gather_matmul_forward(store, op, err)
         elif k in ("TopKSelect", "Argmax"):
             mn = op.m * op.n
             thr = _slot(store, op.thr, op.m)
@@ -586,6 +795,101 @@ class ArgmaxProof:
         return ("Argmax", self.topk.canonical(), self.out.cpu().numpy(), ())
 
 
+@dataclass
+class RmsNormProof:
+    """rms_norm.rs:25-33."""
+    trunc: VirtualProof
+    out: VirtualProof
+    rem_split: VirtualProof
+    trunc_ch: np.ndarray
+    r_out: np.ndarray
+    rem_split_ch: np.ndarray
+
+    def canonical(self):
+        return ("RmsNorm", _vcanon(self.trunc), _vcanon(self.out), _vcanon(self.rem_split), self.trunc_ch,
+                self.r_out, self.rem_split_ch)
+
+
+@dataclass
+class RoPEProof:
+    """rope.rs:33-40."""
+    first: VirtualProof
+    second: VirtualProof
+    r_first: np.ndarray
+    r_second: np.ndarray
+    r_out: np.ndarray
+
+    def canonical(self):
+        return ("RoPE", _vcanon(self.first), _vcanon(self.second), self.r_first, self.r_second, self.r_out)
+
+
+@dataclass
+class PermutationProof:
+    """common/logup_gkr.rs:799-805; the multisets as device tensors."""
+    a_side: FractionalProof
+    b_side: FractionalProof
+    alpha: int
+    a: torch.Tensor
+    b: torch.Tensor
+
+    def canonical(self):
+        return (_frac_canon(self.a_side), _frac_canon(self.b_side), self.alpha, self.a.cpu().numpy(),
+                self.b.cpu().numpy())
+
+
+@dataclass
+class ScatterProof:
+    """scatter.rs:7-10."""
+    perm: PermutationProof
+
+    def canonical(self):
+        return ("Scatter", self.perm.canonical())
+
+
+@dataclass
+class ScatterAddProof:
+    """gather.rs:12-30 (OpProof::Gather); the columns as device tensors."""
+    source_side: FractionalProof
+    target_side: FractionalProof
+    alpha: int
+    gamma: np.ndarray
+    num_source: torch.Tensor
+    den_source: torch.Tensor
+    num_target: torch.Tensor
+    den_target: torch.Tensor
+    prod_source: VirtualProof
+    prod_target: VirtualProof
+    r_prod_source: np.ndarray
+    r_prod_target: np.ndarray
+    weighted: torch.Tensor
+    gate: torch.Tensor
+    out: torch.Tensor
+    token_id: torch.Tensor
+
+    def canonical(self):
+        h = lambda t: t.cpu().numpy()  # noqa: E731
+        return ("Gather", _frac_canon(self.source_side), _frac_canon(self.target_side), self.alpha, self.gamma,
+                h(self.num_source), h(self.den_source), h(self.num_target), h(self.den_target),
+                _vcanon(self.prod_source), _vcanon(self.prod_target), self.r_prod_source, self.r_prod_target,
+                h(self.weighted), h(self.gate), h(self.out), h(self.token_id))
+
+
+@dataclass
+class GatherMatMulOpProof:
+    """OpProof::GatherMatMul(GatherMatMulProof, u, v, ch) (batched_matmul.rs:462-467)."""
+    claimed: int
+    sumcheck: VirtualProof
+    counts: np.ndarray
+    table: np.ndarray
+    u: np.ndarray
+    v: np.ndarray
+    ch: np.ndarray
+
+    def canonical(self):
+        return ("GatherMatMul", (int(self.claimed), _vcanon(self.sumcheck), self.counts, self.table), self.u, self.v,
+                self.ch)
+
+
 def _op_canon(p):
     if isinstance(p, OpMatMulProof):
         mm = p.proof
@@ -675,6 +979,16 @@ GATE_TERMS = [(1, [0, 1]), (NEG, [2])]                                        # 
 D1_TERMS = [(1, [0, 1]), (NEG, [0, 2]), (NEG, [3])]                           # :111-115
 D2_TERMS = [(1, [2]), (NEG, [1]), (NEG, [0, 2]), (1, [0, 1]), (NEG, [3])]     # :119-125
 ROW_SUM_TERMS = [(1, [0, 1])]                                                 # :137
+RMS_OUT_TERMS = [(1, [0, 1, 2]), (NEG, [3]), (1, [3]), (NEG * (1 << 32) % P, [4]), (NEG, [5]), (1 << 31, [6])]  # rms_norm.rs:132-142
+REM_SPLIT_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2])]                  # :150-154
+ROPE_TERMS = lambda shift, second: [(1, [0, 1]), ((1 if second else NEG), [2, 3]), (NEG * (1 << shift) % P, [4]),  # noqa: E731,E501
+                                    (NEG, [5]), (1 << (shift - 1), [6])]          # rope.rs:152-177
+SCATTER_ADD_SOURCE_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3, 4])]                      # gather.rs:103-110
+SCATTER_ADD_TARGET_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3])]                         # :128-135
+BMM_TERMS = [(1, [0, 1, 2])]                                                       # batched_matmul.rs:40-42
+# the arms with no proof of their own (compose.rs:1623-1723)
+MARKER_KINDS = ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "ScaleVec", "IdxBroadcast",
+                "CombineIdx", "PadIdx", "BroadcastScale")
 RECOMPOSE_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2]), (NEG * (1 << 32) % P, [3])]  # :428-433
 
 
@@ -882,7 +1196,144 @@ class OpShardProver:
         check(lib.zkie2_op_iota(ptr(out), 1 << bits, self.sh), "zkie2_op_iota")
         return out
 
+    def upload(self, host: np.ndarray) -> torch.Tensor:
+        """A host array (challenges) on the device, copied on the current
+        stream from pinned memory both of which live as long as the prover
+        (so a recorded graph copies it again on every replay)."""
+        pinned = torch.from_numpy(np.ascontiguousarray(host, dtype=np.uint64).view(np.int64)).pin_memory()
+        dev = torch.empty(pinned.numel(), dtype=torch.int64, device=device())
+        dev.copy_(pinned, non_blocking=True)
+        self.keep += [pinned, dev]
+        return dev.view(torch.uint64)
+
+    def permutation(self, a: torch.Tensor, b: torch.Tensor, n: int):
+        """prove_permutation (logup_gkr.rs:822-840) over the first n values of
+        a and b."""
+        alpha = self.rng.field()
+        total = max(1 << max(n - 1, 0).bit_length(), 32)
+        cols = []
+        for v in (a, b):
+            num, den = empty(total), empty(total)
+            check(lib.zkie2_perm_num_den(ptr(v), n, total, alpha, ptr(num), ptr(den), self.sh), "zkie2_perm_num_den")
+            cols.append((num, den))
+        a_side = self.fractional(*cols[0])
+        b_side = self.fractional(*cols[1])
+        return lambda: PermutationProof(a_side(), b_side(), int(alpha) % P, a[:n], b[:n])
+
     # -- the arms --------------------------------------------------------------------------------
+    def op_rms_norm(self, op: RmsNorm):
+        """prove_rms_norm (rms_norm.rs:97-174) and its lookups (compose.rs:1898-1934)."""
+        g = self.store.get
+        m, d, nr = op.m, op.d, op.n_real
+        x, w = g(op.x), g(op.w)
+        f = rms_norm_columns(x, w, g(op.rsqrt_table), m, d, nr, self.err)
+        trunc_ch = self.draw(_lg(m))
+        trunc = self.virtual([f["ms"], f["rem_s"], f["sum_sq"], self.ones(m)], TRUNC_TERMS(nr, nr // 2), trunc_ch)
+        r_out = self.draw(_lg(m * d))
+        out = self.virtual([x, self.broadcast(f["rstd"], m, d), w, f["raw"], f["out"], f["rem_out"], self.ones(m * d)],
+                           RMS_OUT_TERMS, r_out)
+        rsc = self.draw(_lg(m * d))
+        rem_split = self.virtual([f["rem_out"], f["rem_lo"], f["rem_hi"]], REM_SPLIT_TERMS, rsc)
+        self._lookup(op.rsqrt_table, f["s_index"], f["rstd"], produced_here=True)
+        for part in ("rem_lo", "rem_hi"):
+            self._lookup(op.limb_table, _index_i32(f[part]), f[part], produced_here=True)
+        self.claim(op.out, r_out, out.final(4))
+        self.claim(op.w, r_out, out.final(2))
+        return lambda: RmsNormProof(trunc(), out(), rem_split(), trunc_ch, r_out, rsc)
+
+    def op_rope(self, op: RoPE):
+        """prove_rope (rope.rs:126-196) and its lookups (compose.rs:1935-1967)."""
+        g = self.store.get
+        x, out = g(op.x), g(op.out)
+        n = x.numel()
+        cols = [empty(n // 2) for _ in range(8)]  # x_f x_s o_f o_s cos_b sin_b rem_f rem_s
+        check(lib.zkie2_op_rope_columns(ptr(x), ptr(out), n, ptr(g(op.cos)), ptr(g(op.sin)), op.m, op.d, op.shift,
+                                        (_lib.vp * 8)(*[ptr(c) for c in cols]), self.sh), "zkie2_op_rope_columns")
+        x_f, x_s, o_f, o_s, cos_b, sin_b, rem_f, rem_s = cols
+        ones = self.ones(n // 2)
+        r_f = self.draw(_lg(n // 2))
+        first = self.virtual([x_f, cos_b, x_s, sin_b, o_f, rem_f, ones], ROPE_TERMS(op.shift, False), r_f)
+        r_s = self.draw(_lg(n // 2))
+        second = self.virtual([x_s, cos_b, x_f, sin_b, o_s, rem_s, ones], ROPE_TERMS(op.shift, True), r_s)
+        r_out = self.draw(_lg(n))
+        for rem in (rem_f, rem_s):
+            self._lookup(op.range_table, _index_i32(rem), rem, produced_here=True)
+        self.claim(op.out, r_out)
+        return lambda: RoPEProof(first(), second(), r_f, r_s, r_out)
+
+    def op_scatter(self, op: Scatter):
+        """prove_scatter (scatter.rs:39-55)."""
+        sel = self.store.get(op.sel)
+        tid, eof = self.store.get_idx(op.token_id), self.store.get_idx(op.expert_of)
+        m, n, s_ = op.m, op.n, tid.numel()
+        tcnt = _u32(m)
+        check(lib.zkie2_op_sel_counts(ptr(sel), m, n, 1, tcnt.data_ptr(), self.sh), "zkie2_op_sel_counts")
+        a, b = empty(m * n), empty(max(s_, 1))
+        check(lib.zkie2_op_scatter_encodings(ptr(sel), m, n, tcnt.data_ptr(), tid.data_ptr(), eof.data_ptr(), s_,
+                                             ptr(a), ptr(b), self.err.data_ptr(), self.sh),
+              "zkie2_op_scatter_encodings")
+        perm = self.permutation(a, b, s_)
+        return lambda: ScatterProof(perm())
+
+    def op_gather(self, op: Gather):
+        """prove_scatter_add (gather.rs:54-157)."""
+        g = self.store.get
+        wt, tid, gate, out = g(op.weighted), self.store.get_idx(op.token_id), g(op.gate), g(op.out)
+        m, h, s_ = op.m, op.h, tid.numel()
+        alpha = int(self.rng.field()) % P
+        gamma = self.draw(h)
+        gd = self.upload(gamma)
+        st, tt = 1 << max(s_ * h - 1, 0).bit_length(), 1 << max(m * h - 1, 0).bit_length()
+        src = [empty(st) for _ in range(5)]  # num den gamma_b gate_b w_pad
+        check(lib.zkie2_scatter_add_columns(ptr(wt), ptr(gate), tid.data_ptr(), ptr(gd), s_, h, st, alpha,
+                                            (_lib.vp * 5)(*[ptr(c) for c in src]), self.sh),
+              "zkie2_scatter_add_columns")
+        tgt = [empty(tt) for _ in range(4)]  # num den gamma_b o_pad
+        check(lib.zkie2_scatter_add_columns(ptr(out), None, None, ptr(gd), m, h, tt, alpha,
+                                            (_lib.vp * 5)(ptr(tgt[0]), ptr(tgt[1]), ptr(tgt[2]), None, ptr(tgt[3])),
+                                            self.sh), "zkie2_scatter_add_columns")
+        source_side = self.fractional(src[0], src[1])
+        target_side = self.fractional(tgt[0], tgt[1])
+        r_ps = self.draw(_lg(st))
+        prod_source = self.virtual([self.eq_table(r_ps), src[0], src[2], src[4], src[3]], SCATTER_ADD_SOURCE_TERMS,
+                                   r_ps)
+        r_pt = self.draw(_lg(tt))
+        prod_target = self.virtual([self.eq_table(r_pt), tgt[0], tgt[2], tgt[3]], SCATTER_ADD_TARGET_TERMS, r_pt)
+        return lambda: ScatterAddProof(source_side(), target_side(), alpha, gamma, src[0], src[1], tgt[0], tgt[1],
+                                       prod_source(), prod_target(), r_ps, r_pt, wt, gate, out, tid)
+
+    def op_gather_matmul(self, op: GatherMatMul):
+        """prove_gather_matmul (batched_matmul.rs:469-494, prove_streaming
+        :359-390; compose.rs:1682-1705): the experts' weights contracted with
+        eq(v) once (a partial evaluation over every expert), gathered per
+        position, the eq-selector sumcheck, and the per-expert counts and
+        table openings."""
+        g = self.store.get
+        a, eof, w, c = g(op.a), self.store.get_idx(op.expert_of), g(op.w), g(op.c)
+        s_, k, n, ne = op.s, op.k, op.n, op.n_experts
+        ls, lk, ln = _lg(s_), _lg(k), _lg(n)
+        u, v, ch = self.draw(ls), self.draw(ln), self.draw(ls + lk)
+        self.traffic += 8 * (ne * k * n + 3 * s_ * k + s_ * n)
+        wv = empty(ne * k)
+        scr = empty(max(lib.zkie2_mle_scratch_elems(lk + ln), 1))
+        for e in range(ne):  # expert blocks are powers of two; the expert count need not be
+            check(lib.zkie2_mle_partial_eval(ptr(w[e * k * n:(e + 1) * k * n]), lk + ln, _pp(v), ln,
+                                             ptr(wv[e * k:(e + 1) * k]), ptr(scr), self.sh), "zkie2_mle_partial_eval")
+        w_v = empty(s_ * k)
+        check(lib.zkie2_expert_rows(ptr(wv), eof.data_ptr(), s_, k, ne, ptr(w_v), self.err.data_ptr(), self.sh),
+              "zkie2_expert_rows")
+        claimed = self.eval(c, np.concatenate([v, u]))
+        sc = self.virtual([a, w_v, self.broadcast(self.eq_table(u), s_, k)], BMM_TERMS, ch)
+        hc, dc = self.pend.out(ne)
+        ht, dt = self.pend.out(ne)
+        check(lib.zkie2_expert_open(eof.data_ptr(), s_, ptr(self.eq_table(ch[lk:])), ptr(wv), k,
+                                    ptr(self.eq_table(ch[:lk])), ne, ptr(dc), ptr(dt), self.sh), "zkie2_expert_open")
+        self.claim(op.a, ch, sc.final(0))
+        self.claim(op.c, np.concatenate([v, u]), claimed)
+        pend = self.pend
+        return lambda: GatherMatMulOpProof(pend.value(claimed), sc(), pend.host(hc)[:ne].copy(),
+                                           pend.host(ht)[:ne].copy(), u, v, ch)
+
     def op_topk(self, op):
         """prove_topk (topk.rs:82-176) for Op::TopKSelect (range_bits 22,
         compose.rs:1968-1996) and, with k = 1, prove_argmax (topk.rs:299-318)
@@ -1174,7 +1625,8 @@ class OpShardProver:
         arms = {"MatMul": self.op_matmul, "Projection": self.op_projection, "Add": self.op_add,
                 "Softmax": self.op_softmax, "Layernorm": self.op_layernorm,
                 "LayerNormCentered": self.op_layer_norm_centered, "TopKSelect": self.op_topk,
-                "Argmax": self.op_topk}
+                "Argmax": self.op_topk, "RmsNorm": self.op_rms_norm, "RoPE": self.op_rope, "Scatter": self.op_scatter,
+                "Gather": self.op_gather, "GatherMatMul": self.op_gather_matmul}
         self.err.zero_()
         start = torch.cuda.Event()
         start.record(self.main)
@@ -1189,7 +1641,7 @@ class OpShardProver:
             elif k == "Lookup":
                 self._lookup(op.table, self.store.get_idx(op.idx), self.store.get(op.out))
                 self.builders.append(lambda k=k: MarkerProof(k))
-            elif k in ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex"):
+            elif k in MARKER_KINDS:
                 self.builders.append(lambda k=k: MarkerProof(k))
             else:
                 raise ValueError(f"op {k} is not supported")

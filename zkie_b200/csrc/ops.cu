@@ -319,6 +319,66 @@ __global__ void __launch_bounds__(kRowThreads) k_ln_centered_fwd(const uint64_t*
     }
 }
 
+// The RmsNorm arm (rms_norm.rs:37-95), one block per row: ms =
+// round_div(sum of to_i64(x)^2 over n_real, n_real) in wrapping i64, rstd =
+// table[rsqrt_index(ms)], raw = x rstd w (field), out = round_div(to_i64(raw),
+// 2^32), rem_out = to_i64(raw) - to_i64(out) 2^32 + 2^31 split into rem_lo =
+// rem_out & 0xFFFF and rem_hi = rem_out >> 16 (arithmetic); sum_sq = the
+// field sum of x^2 over n_real, rem_s = sum_sq - ms n_real + n_real / 2.
+struct RmsOut {
+    uint64_t *ms, *rstd, *raw, *out, *rem_out, *rem_lo, *rem_hi, *sum_sq, *rem_s;
+    uint32_t* s_index;
+};
+
+__global__ void __launch_bounds__(kRowThreads) k_rms_norm_fwd(const uint64_t* __restrict__ x,
+                                                              const uint64_t* __restrict__ w,
+                                                              const uint64_t* __restrict__ table, uint64_t t,
+                                                              uint64_t m, uint64_t d, uint64_t n_real, RmsOut o,
+                                                              uint32_t* __restrict__ err) {
+    __shared__ uint64_t sh[kRowWarps];
+    const int64_t nr = (int64_t)n_real;
+    for (uint64_t r = blockIdx.x; r < m; r += gridDim.x) {
+        const uint64_t* xr = x + r * d;
+        uint64_t qi = 0, qf = 0;
+        for (uint64_t j = threadIdx.x; j < n_real; j += blockDim.x) {
+            const uint64_t v = gl_canon(__ldg(xr + j));
+            const int64_t vi = fx_to_i64(v);
+            qi += (uint64_t)fx_wmul(vi, vi);
+            qf = gl_add(qf, gl_mul(v, v));
+        }
+        qi = block_reduce(qi, WrapAdd{}, sh);
+        qf = gl_canon(block_reduce(qf, FieldAdd{}, sh));
+        int64_t q = 0;
+        fx_round_div((int64_t)qi, nr, &q);
+        const uint64_t ms = fx_from_i64(q);
+        const uint32_t sidx = rsqrt_index(fx_to_i64(ms));
+        uint64_t rstd = 0;
+        if (sidx < t)
+            rstd = __ldg(table + sidx);
+        else if (threadIdx.x == 0)
+            atomicOr(err, kErrIndex);
+        if (threadIdx.x == 0) {
+            o.ms[r] = ms;
+            o.s_index[r] = sidx;
+            o.rstd[r] = rstd;
+            o.sum_sq[r] = qf;
+            o.rem_s[r] = fx_from_i64(fx_wadd(fx_wsub(fx_to_i64(qf), fx_wmul(fx_to_i64(ms), nr)), nr / 2));
+        }
+        for (uint64_t j = threadIdx.x; j < d; j += blockDim.x) {
+            const uint64_t i = r * d + j;
+            const uint64_t raw = gl_canon(gl_mul(gl_mul(__ldg(xr + j), rstd), __ldg(w + i)));
+            const int64_t ri = fx_to_i64(raw);
+            const int64_t oi = fx_round_div_pow2(ri, 32);
+            const int64_t rem = fx_wadd(fx_wsub(ri, fx_wmul(oi, 1ll << 32)), 1ll << 31);
+            o.raw[i] = raw;
+            o.out[i] = fx_from_i64(oi);
+            o.rem_out[i] = fx_from_i64(rem);
+            o.rem_lo[i] = fx_from_i64(rem & 0xFFFF);
+            o.rem_hi[i] = fx_from_i64(rem >> 16);
+        }
+    }
+}
+
 // The Layernorm arm (compose.rs:1467-1496, layernorm_chain.rs:34-44):
 // mean_sq = sum_j x^2, idx = max(to_i64(mean_sq), 0) % len, rsqrt =
 // table[idx], scale = rsqrt w, out = x scale + b
@@ -672,6 +732,21 @@ int zkie2_op_row_sums(const uint64_t* d_x, uint64_t m, uint64_t d, uint64_t ncol
     if (m == 0) return 0;
     if (ncols > d || !d_x || !d_out) return (int)cudaErrorInvalidValue;
     k_row_sums<<<row_grid(m), kRowThreads, 0, stream>>>(d_x, m, d, ncols, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_rms_norm(const uint64_t* d_x, const uint64_t* d_w, const uint64_t* d_table, uint64_t t, uint64_t m,
+                      uint64_t d, uint64_t n_real, uint64_t* const* d_outs, uint32_t* d_s_index, uint32_t* d_err,
+                      cudaStream_t stream) {
+    if (n_real == 0 || n_real > d) return (int)cudaErrorInvalidValue;
+    if (m == 0 || d == 0) return 0;
+    if (!d_x || !d_w || !d_table || !d_outs || !d_s_index || !d_err) return (int)cudaErrorInvalidValue;
+    for (int i = 0; i < 9; i++)
+        if (!d_outs[i]) return (int)cudaErrorInvalidValue;
+    RmsOut o{d_outs[0], d_outs[1], d_outs[2], d_outs[3], d_outs[4], d_outs[5], d_outs[6], d_outs[7], d_outs[8],
+             d_s_index};
+    k_rms_norm_fwd<<<row_grid(m), kRowThreads, 0, stream>>>(d_x, d_w, d_table, t, m, d, n_real, o, d_err);
     ZK_LAUNCH_CHECK();
     return 0;
 }
