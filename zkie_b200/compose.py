@@ -1326,8 +1326,9 @@ class OpShardProver:
         sc = self.virtual([a, w_v, self.broadcast(self.eq_table(u), s_, k)], BMM_TERMS, ch)
         hc, dc = self.pend.out(ne)
         ht, dt = self.pend.out(ne)
-        check(lib.zkie2_expert_open(eof.data_ptr(), s_, ptr(self.eq_table(ch[lk:])), ptr(wv), k,
-                                    ptr(self.eq_table(ch[:lk])), ne, ptr(dc), ptr(dt), self.sh), "zkie2_expert_open")
+        eq_pos, eq_d = self.eq_table(ch[lk:]), self.eq_table(ch[:lk])  # both alive across the call
+        check(lib.zkie2_expert_open(eof.data_ptr(), s_, ptr(eq_pos), ptr(wv), k, ptr(eq_d), ne, ptr(dc), ptr(dt),
+                                    self.sh), "zkie2_expert_open")
         self.claim(op.a, ch, sc.final(0))
         self.claim(op.c, np.concatenate([v, u]), claimed)
         pend = self.pend
