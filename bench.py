@@ -92,6 +92,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-big", action="store_true", help="skip the 256 x 2^24 and expert-stack commits")
     ap.add_argument("--no-cfg4", action="store_true", help="skip the 12-layer GPT-2 shard DAG")
+    ap.add_argument("--no-moe", action="store_true", help="skip the DeepSeek-V2-Lite-shaped MoE layer shard")
+    ap.add_argument("--cpu-moe", action="store_true", help="also time the MoE layer on the CPU restatement (minutes)")
     return ap.parse_args()
 
 
@@ -716,6 +718,8 @@ def main():
     extra = next_rows(want_cpu=not args.no_cpu)
     extra["projection"] = projection_case(zk, dev, want_cpu=not args.no_cpu)
     extra["layer_shard"] = layer_case(zk, dev, want_cpu=not args.no_cpu)
+    if not args.no_moe:
+        extra["cfg5_moe_layer"] = moe_case(zk, dev, want_cpu=args.cpu_moe)
     if not args.no_cfg4:
         extra["cfg4_gpt2_model"] = cfg4_case(zk, dev, 0, 1)
     # ---- configurations 2 (256 x 2^24) and 5 (expert stack); the 2^28 sumcheck ----
@@ -958,18 +962,45 @@ def layer_case(zk, dev, want_cpu, iters=5):
     m 512, D 1024 with 768 real, 12 heads x 64, FFN 4096 with 3072 real; the
     exp 2^21, rsqrt 7.3 M and gelu 2^24 tables) proven as one shard of
     prove_shard_dag: the forward witness, then the shard proof (every arm,
-    53 same_poly bindings, the three tables' logUp).  The proof is recorded
-    once as a CUDA graph (its challenges and launch shapes depend on the
-    statement only) and replayed; the eager proof (host orchestration of every
-    launch) is reported beside it."""
+    53 same_poly bindings, the three tables' logUp)."""
+    from zkie_b200 import gpt2
+    return shard_case(zk, lambda st: gpt2.gpt2_layer(st, gpt2.GPT2_SMALL),
+                      "GPT-2-small layer shard (models/gpt2/src/lib.rs build_layer, 176 ops: m 512, D 1024 (768 real), "
+                      "12 heads x 64, FFN 4096 (3072 real), shift 16; synthetic weights in the random builder's ranges; "
+                      "exp 2^21 / rsqrt 7.3M / gelu 2^24 tables), one shard of prove_shard_dag, inputs resident",
+                      want_cpu, iters)
+
+
+def moe_case(zk, dev, want_cpu, iters=3):
+    """Configuration 5: one DeepSeek-V2-Lite-shaped MoE layer
+    (models/deepseek-v2-lite build_attention + build_moe, zkie_b200.deepseek:
+    hidden 2048, MLA with 16 heads, kv_lora 512, 64 routed experts top-6 with
+    the expert FFN 2048 (1408 real), the shared experts 4096 (2816 real),
+    sequence 512) proven as one shard.  The CPU restatement of this layer
+    takes minutes, so it runs only on request (--cpu-moe)."""
+    from zkie_b200 import deepseek
+    return shard_case(zk, lambda st: deepseek.moe_layer(st, deepseek.DSV2_LITE),
+                      "DeepSeek-V2-Lite-shaped MoE layer shard (models/deepseek-v2-lite/src/lib.rs build_attention + "
+                      "build_moe as one layer: hidden 2048, MLA 16 heads (nope 128, rope 64, v 128, kv_lora 512), "
+                      "64 routed experts top-6 (FFN 2048, 1408 real) expert-major via Scatter / GatherMatMul / Gather, "
+                      "shared experts 4096 (2816 real), m 512, shift 16; synthetic weights; exp 2^21 / rsqrt 7.3M / "
+                      "SiLU 2^24 / limb 2^16 tables), one shard, inputs resident",
+                      want_cpu, iters)
+
+
+def shard_case(zk, build, config, want_cpu, iters):
+    """One op-graph shard on one GPU: the forward witness, then the shard
+    proof, recorded once as a CUDA graph (its challenges and launch shapes
+    depend on the statement only) and replayed; the eager proof (host
+    orchestration of every launch) is reported beside it, with its digest."""
     import torch
 
     from zkie_b200 import compose as C
-    from zkie_b200 import gpt2
     from zkie_b200.dag import digest as _proof_digest
-    shape = gpt2.GPT2_SMALL
     st = C.Store()
-    ops, x, out = gpt2.gpt2_layer(st, shape)
+    t0 = time.perf_counter()
+    ops, x, out = build(st)
+    build_s = time.perf_counter() - t0
     fwd = []
     for it in range(iters + 2):
         torch.cuda.synchronize()
@@ -1020,14 +1051,12 @@ def layer_case(zk, dev, want_cpu, iters=5):
     prove_ms = statistics.median(replay)
     hbm_peak, hbm_src = hbm_peak_gbs()
     out_d = {
-        "config": "GPT-2-small layer shard (models/gpt2/src/lib.rs build_layer, 176 ops: m 512, D 1024 (768 real), "
-                  "12 heads x 64, FFN 4096 (3072 real), shift 16; synthetic weights in the random builder's ranges; "
-                  "exp 2^21 / rsqrt 7.3M / gelu 2^24 tables), one shard of prove_shard_dag, inputs resident",
+        "config": config,
         "ms": round(1e3 * statistics.median(whole), 3), "unit": "ms per layer shard (forward + prove + proof to host)",
         "forward_ms": round(1e3 * statistics.median(fwd), 3), "prove_ms": round(prove_ms, 3),
         "collect_ms": round(1e3 * statistics.median(collect), 3),
         "eager_prove_ms": round(1e3 * statistics.median(eager), 3), "capture_ms": round(1e3 * capture_s, 1),
-        "ops": len(ops), "same_poly_binds": len(sh.binds), "claims": len(sh.claims),
+        "build_s": round(build_s, 2), "ops": len(ops), "same_poly_binds": len(sh.binds), "claims": len(sh.claims),
         "lookup_tables": len(sh.table_columns), "proof_digest": digest, "replay_equals_eager": digest == eager_digest,
         "roofline": {"bound": "hbm", "achieved": round(traffic / (prove_ms / 1e3) / 1e9, 1), "peak": hbm_peak,
                      "unit": "GB/s", "frac": round(traffic / (prove_ms / 1e3) / 1e9 / hbm_peak, 4),
@@ -1041,7 +1070,7 @@ def layer_case(zk, dev, want_cpu, iters=5):
         from oracle import oracle as orc
         orc.set_threads(host_threads())
         host = co.HostStore()
-        gpt2.gpt2_layer(host, shape)
+        build(host)
         t0 = time.perf_counter()
         co.forward_ops(host, ops)
         t1 = time.perf_counter()

@@ -18,6 +18,7 @@ of the profiles (run from the repository root).
     python perfcases.py projection --m 512 --k 1024 --n 4096
     python perfcases.py layer --trace
     python perfcases.py model
+    python perfcases.py moe [--cpu]
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -417,6 +418,15 @@ def case_model(a):
     return {"case": "gpt2_model_dag", **bench.cfg4_case(zk, torch.device("cuda", 0), 0, 1)}
 
 
+def case_moe(a):
+    """BASELINE configuration 5 on one GPU: the DeepSeek-V2-Lite-shaped MoE
+    layer proven as one shard by a recorded graph (the bench's cfg5 case);
+    with --cpu also the CPU restatement of the same shard."""
+    import bench
+    import zkie_b200 as zk
+    return {"case": "moe_layer_shard", **bench.moe_case(zk, torch.device("cuda", 0), a.cpu, a.iters)}
+
+
 def case_sweep(a):
     """batches of 1, 16, 256 polynomials of 2^16,
     2^20, 2^24 coefficients at blowup 2 and 4.  One JSON line per case that
@@ -476,7 +486,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["sumcheck", "mle", "matmul", "commit", "virtual", "sop", "shard", "split", "sweep",
                                          "logup", "grind", "fixed", "cache", "coset", "projection", "layer",
-                                         "model"])
+                                         "model", "moe"])
     ap.add_argument("--gpus", type=int, default=4, help="ranks of the emulated split commit")
     ap.add_argument("--log-size", type=int, default=20)
     ap.add_argument("--polys", type=int, default=16)
@@ -486,6 +496,7 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--trace", action="store_true", help="layer: list one replay's kernels")
+    ap.add_argument("--cpu", action="store_true", help="moe: also time the CPU restatement")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("perfcases needs a CUDA device")
@@ -493,7 +504,7 @@ def main(argv=None):
     res = {"sumcheck": case_sumcheck, "mle": case_mle, "matmul": case_matmul, "commit": case_commit,
            "virtual": case_virtual, "logup": case_logup, "grind": case_grind, "fixed": case_fixed, "cache": case_cache, "sop": case_sop, "shard": case_shard, "split": case_split,
            "sweep": case_sweep, "coset": case_coset, "projection": case_projection, "layer": case_layer,
-           "model": case_model}[a.case](a)
+           "model": case_model, "moe": case_moe}[a.case](a)
     print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in res.items()}), flush=True)
     return 0
 
