@@ -18,7 +18,7 @@ of the profiles (run from the repository root).
     python perfcases.py projection --m 512 --k 1024 --n 4096
     python perfcases.py layer --trace
     python perfcases.py model
-    python perfcases.py moe [--cpu]
+    python perfcases.py moe [--cpu | --trace]
 
 Each case prints one JSON line (the sweep one per configuration-2 case):
 time per call (CUDA events on the launching stream, after warm-up) and,
@@ -371,8 +371,6 @@ def case_layer(a):
     by a recorded CUDA graph: the replay's device time, and with --trace the
     kernels of one replay (torch.profiler / CUPTI: launches, the sum of kernel
     times against the replay's span, the top kernels by total time)."""
-    import collections
-
     from zkie_b200 import compose as C
     from zkie_b200 import gpt2
     st = C.Store()
@@ -388,25 +386,34 @@ def case_layer(a):
     ms = _time(gp.replay, a.iters)
     res = {"case": "layer_shard_replay", "ops": len(ops), "ms": ms}
     if a.trace:
-        from torch.profiler import ProfilerActivity, profile
-        torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            gp.replay()
-            torch.cuda.synchronize()
-        evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
-        iv = sorted((e.time_range.start, e.time_range.end) for e in evs)
-        span = iv[-1][1] - iv[0][0]
-        total = sum(e - s for s, e in iv)
-        agg = collections.defaultdict(lambda: [0, 0.0])
-        for e in evs:
-            name = e.name.replace("void ", "").replace("zk::(anonymous namespace)::", "").split("(")[0]
-            agg[name][0] += 1
-            agg[name][1] += e.time_range.end - e.time_range.start
-        top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]
-        res.update({"launches": len(evs), "span_ms": span / 1e3, "kernel_time_sum_ms": total / 1e3,
-                    "mean_concurrency": total / max(span, 1),
-                    "top": [[k, n, round(t / 1e3, 3), round(t / total, 4)] for k, (n, t) in top]})
+        res.update(_trace(gp.replay))
     return res
+
+
+def _trace(fn, top_n=12):
+    """The kernels of one call of fn (torch.profiler / CUPTI): launches, the
+    span first start -> last end, the sum of kernel durations, the top
+    kernels by total time."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    evs = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    iv = sorted((e.time_range.start, e.time_range.end) for e in evs)
+    span = iv[-1][1] - iv[0][0]
+    total = sum(e - s for s, e in iv)
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in evs:
+        name = e.name.replace("void ", "").replace("zk::(anonymous namespace)::", "").split("(")[0]
+        agg[name][0] += 1
+        agg[name][1] += e.time_range.end - e.time_range.start
+    top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:top_n]
+    return {"launches": len(evs), "span_ms": span / 1e3, "kernel_time_sum_ms": total / 1e3,
+            "mean_concurrency": total / max(span, 1),
+            "top": [[k, n, round(t / 1e3, 3), round(t / total, 4)] for k, (n, t) in top]}
 
 
 def case_model(a):
@@ -424,6 +431,22 @@ def case_moe(a):
     with --cpu also the CPU restatement of the same shard."""
     import bench
     import zkie_b200 as zk
+    if a.trace:
+        from zkie_b200 import compose as C
+        from zkie_b200 import deepseek
+        st = C.Store()
+        ops, _, _ = deepseek.moe_layer(st, deepseek.DSV2_LITE)
+        C.forward_ops(st, ops)
+        fwd = _trace(lambda: C.forward_ops(st, ops))
+        master = C.master_transcript(ops, len(ops))
+
+        def make_rng():
+            c = master.clone()
+            c.absorb_u64(0)
+            return c
+        gp = C.GraphShardProver(st, ops, [], make_rng)
+        gp.replay()
+        return {"case": "moe_layer_trace", "forward": fwd, "prove_replay": _trace(gp.replay)}
     return {"case": "moe_layer_shard", **bench.moe_case(zk, torch.device("cuda", 0), a.cpu, a.iters)}
 
 

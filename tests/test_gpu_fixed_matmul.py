@@ -1,8 +1,9 @@
 """GPU parity of the fixed-point forward matmul on the tensor cores
 (zkie2_matmul_fixed, par::mm_par_fixed of zkie-ops/src/par.rs:41-89) with the
 exact field matmul (zkie2_matmul_field) and, on small shapes, the CPU oracle:
-bit-exact, across tile edges, K split into i64-combined chunks, the extreme
-16-bit values, and the field fallback for values outside 16 bits."""
+bit-exact, across tile edges, K split into chunks, the extreme 16- and
+24-bit values (two or three byte planes per operand), and the field
+fallback for values outside 24 bits."""
 import numpy as np
 import pytest
 
@@ -41,7 +42,41 @@ def test_matches_oracle_and_extremes(zk, orc):
         assert np.array_equal(got.cpu().numpy(), zk.matmul_field(a, b, m, k, n).cpu().numpy())
 
 
-@pytest.mark.parametrize("bad", [1 << 15, P - (1 << 15) - 1, 12345678901234])
+@pytest.mark.parametrize("bits_a,bits_b", [(24, 16), (16, 24), (24, 24), (17, 17)])
+@pytest.mark.parametrize("m,k,n", [(48, 2048, 2048), (130, 160, 260), (3, 8208, 12), (8, 16384, 64)])
+def test_three_plane_operands_match_field(zk, bits_a, bits_b, m, k, n):
+    """Operands beyond 16 bits take three byte planes (five plane-sum GEMMs
+    for 3 x 3): the exact field product."""
+    a = fixed(m + k + bits_a, (m, k), -(1 << (bits_a - 1)), 1 << (bits_a - 1))
+    b = fixed(n + k + bits_b, (k, n), -(1 << (bits_b - 1)), 1 << (bits_b - 1))
+    got, path = zk.matmul_fixed(a, b, m, k, n, force_tensor=True)
+    assert path == 0
+    assert np.array_equal(got.cpu().numpy(), zk.matmul_field(a, b, m, k, n).cpu().numpy())
+
+
+def test_three_plane_extremes(zk):
+    """Every product at the 24-bit extremes: sums of +-2^46 over k = 4096."""
+    m, k, n = 64, 4096, 64
+    for va, vb in ((-(1 << 23), -(1 << 23)), ((1 << 23) - 1, -(1 << 23)), ((1 << 23) - 1, (1 << 23) - 1),
+                   (-(1 << 23), (1 << 15) - 1)):
+        a = fixed(0, (m, k), va, va + 1)
+        b = fixed(0, (k, n), vb, vb + 1)
+        got, path = zk.matmul_fixed(a, b, m, k, n, force_tensor=True)
+        assert path == 0
+        assert np.array_equal(got.cpu().numpy(), zk.matmul_field(a, b, m, k, n).cpu().numpy())
+
+
+@pytest.mark.parametrize("odd", [1 << 15, P - (1 << 15) - 1, (1 << 23) - 1, P - (1 << 23)])
+def test_values_past_16_bits_stay_on_the_tensor_path(zk, odd):
+    m, k, n = 32, 256, 64
+    a, b = fixed(3, (m, k)), fixed(4, (k, n))
+    a[7, 9] = np.uint64(odd)
+    got, path = zk.matmul_fixed(a, b, m, k, n, force_tensor=True)
+    assert path == 0
+    assert np.array_equal(got.cpu().numpy(), zk.matmul_field(a, b, m, k, n).cpu().numpy())
+
+
+@pytest.mark.parametrize("bad", [1 << 23, P - (1 << 23) - 1, 12345678901234])
 def test_out_of_range_falls_back_to_field(zk, bad):
     m, k, n = 32, 256, 64
     a, b = fixed(3, (m, k)), fixed(4, (k, n))

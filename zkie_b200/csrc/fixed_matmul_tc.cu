@@ -5,17 +5,20 @@
 // are negative), takes exact i64 dot products and maps them back (from_i64);
 // the result equals the field matmul, and it falls back to the field matmul
 // when the i64 sums could overflow.  Here, when every input lies in
-// [-2^15, 2^15) (16-bit fixed point, the inference witness range), the
-// products run on the 5th-generation tensor cores as u8 x u8 -> s32 GEMMs:
-//   a' = a + 2^15 in [0, 2^16) splits into bytes a' = 256 a_h + a_l, so
-//   sum_k a'b' = 2^16 (A_h B_h) + 2^8 (A_h B_l + A_l B_h) + A_l B_l,
-// the middle term as ONE GEMM over a doubled K ([A_h | A_l] times [B_l ; B_h]),
-// and the offset comes off exactly:
-//   sum_k a b = sum_k a'b' - 2^15 (rowsum_i(A') + colsum_j(B')) + K 2^30.
-// Every s32 sum stays below 2 * 8192 * 255^2 < 2^31 by splitting K into
-// chunks of at most 8192 (partial results add up in i64).  Inputs outside
-// 16 bits, or a K or N that TMA cannot address (K % 16, N % 4), take the
-// exact field kernel instead, so the output always equals the field matmul.
+// [-2^23, 2^23) (fixed point up to 24 bits: the inference witness range,
+// 16-bit weights against Q16 activations), the products run on the
+// 5th-generation tensor cores as u8 x u8 -> s32 GEMMs.  Each operand takes
+// P = 2 or 3 byte planes (2 when all its values lie in [-2^15, 2^15)):
+//   a' = a + 2^(8 P_a - 1) in [0, 2^(8 P_a)), a' = sum_q 2^(8q) a_q, so
+//   sum_k a'b' = sum_s 2^(8s) sum_{q_a + q_b = s} A_{q_a} B_{q_b},
+// each plane-sum s as ONE GEMM over the pairs' planes concatenated along K
+// (three GEMMs for 2 x 2 planes, five for 3 x 3), and the offsets come off
+// exactly:  sum_k a b = sum_k a'b' - o_b rowsum_i(A') - o_a colsum_j(B')
+// + K o_a o_b, in wrapping u64 arithmetic (|sum_k a b| < K 2^46 < 2^63).
+// Every s32 sum stays below 3 * 8192 * 255^2 < 2^31 by splitting K into
+// chunks of at most 8192.  Inputs outside 24 bits, or a K or N that TMA
+// cannot address (K % 16, N % 4), take the exact field kernel instead, so
+// the output always equals the field matmul.
 //
 // The GEMMs are CUTLASS sm100 collectives (tcgen05.mma kind::i8 issued by one
 // thread, operands staged by TMA, accumulators in TMEM), 128 x 128 x 128
@@ -55,62 +58,96 @@ using TcMainloop = typename cutlass::gemm::collective::CollectiveBuilder<
 using TcKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, TcMainloop, TcEpilogue>;
 using TcGemm = cutlass::gemm::device::GemmUniversalAdapter<TcKernel>;
 
-constexpr uint64_t kKChunk = 8192;  // 2 * kKChunk * 255^2 < 2^31
-constexpr uint64_t kOffset = 1ull << 15;
+constexpr uint64_t kKChunk = 8192;  // 3 * kKChunk * 255^2 < 2^31
 constexpr int kThr = 256;
+constexpr uint32_t kMaxPlanes = 3;
 
-// to_i64(x) + 2^15 when to_i64(x) is in [-2^15, 2^15), else sets *bad
-__device__ __forceinline__ uint32_t shifted16(uint64_t x, uint32_t* bad) {
-    x = gl_canon(x);
-    if (x < kOffset) return (uint32_t)(x + kOffset);
-    if (x >= GL_P - kOffset) return (uint32_t)(x - (GL_P - kOffset));
-    atomicOr(bad, 1u);
-    return 0;
+// The byte planes of an operand whose values all lie in [-2^(8P-1), 2^(8P-1)):
+// v' = to_i64(v) + 2^(8P-1) in [0, 2^(8P)), plane q = byte q of v'.  Products
+// group by s = q_a + q_b: G_s = sum over the pairs (q_a, s - q_a) of the
+// plane products, one GEMM per s over the pairs' planes concatenated along K
+// (per K chunk), and sum_k a'b' = sum_s 2^(8s) G_s.
+
+// pair p of plane-sum s (p-th q_a from max(0, s - PB + 1)); count of pairs
+__host__ __device__ __forceinline__ uint32_t pair_lo(uint32_t s, uint32_t pb) { return s + 1 > pb ? s + 1 - pb : 0; }
+__host__ __device__ __forceinline__ uint32_t pair_count(uint32_t s, uint32_t pa, uint32_t pb) {
+    const uint32_t lo = pair_lo(s, pb), hi = s < pa - 1 ? s : pa - 1;
+    return hi + 1 - lo;
+}
+// byte offset of region s in a packed operand of `rows` rows (regions in s order)
+__host__ __device__ __forceinline__ uint64_t region_off(uint32_t s, uint32_t pa, uint32_t pb, uint64_t rows,
+                                                        uint64_t K) {
+    uint64_t off = 0;
+    for (uint32_t q = 0; q < s; q++) off += pair_count(q, pa, pb) * rows * K;
+    return off;
 }
 
-// Column of chunk layout: element k of a row lands at 2 * kc0 + (k - kc0) for
-// the high (or first) plane and at 2 * kc0 + kc + (k - kc0) for the other,
-// kc0 = the chunk start, kc = the chunk width.
-__device__ __forceinline__ void cat_cols(uint64_t k, uint64_t K, uint64_t& first, uint64_t& second) {
+// column of element k (chunk c0, width kc) for pair p of a region with `cnt`
+// pairs: per chunk the pairs' planes side by side
+__device__ __forceinline__ uint64_t cat_col(uint64_t k, uint64_t K, uint32_t cnt, uint32_t p) {
     const uint64_t c0 = k / kKChunk * kKChunk;
     const uint64_t kc = K - c0 < kKChunk ? K - c0 : kKChunk;
-    first = 2 * c0 + (k - c0);
-    second = first + kc;
+    return cnt * c0 + p * kc + (k - c0);
 }
 
-// A (M x K field, row-major) -> AH, AL (M x K bytes), ACAT (M x 2K: per chunk
-// [a_h | a_l]), rowsum[i] = sum_k a'.  One thread per 16 consecutive elements
-// of a row (K % 16 == 0, and chunk widths are multiples of 16): 16-byte loads
-// and 16-byte stores of each plane.
+// bit 0: a value outside [-2^15, 2^15); bit 1: outside [-2^23, 2^23)
+__global__ void k_tc_range(const uint64_t* __restrict__ v, uint64_t n, uint32_t* __restrict__ flags) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    uint32_t f = 0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t x = gl_canon(__ldg(v + i));
+        const uint64_t mag = x <= GL_P / 2 ? x : GL_P - x;  // |to_i64(x)|, with the negative side's one extra value
+        const bool neg = x > GL_P / 2;
+        if (neg ? mag > (1ull << 15) : mag >= (1ull << 15)) f |= 1u;
+        if (neg ? mag > (1ull << 23) : mag >= (1ull << 23)) f |= 2u;
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if ((threadIdx.x & 31) == 0 && f) atomicOr(flags, f);
+}
+
+__device__ __forceinline__ uint32_t shifted(uint64_t x, uint64_t off) {
+    x = gl_canon(x);
+    return (uint32_t)(x < off ? x + off : x - (GL_P - off));
+}
+
+// A (M x K field, row-major) -> its PA planes placed in every region pair
+// they take part in (row stride cnt_s K in region s), rowsum[i] = sum_k a'.
+// One thread per 16 consecutive elements of a row (K % 16 == 0, chunk widths
+// multiples of 16): 16-byte loads and 16-byte stores of each plane.
 __global__ void __launch_bounds__(kThr)
-    k_planes_a(const uint64_t* __restrict__ a, uint64_t M, uint64_t K, uint8_t* __restrict__ ah,
-               uint8_t* __restrict__ al, uint8_t* __restrict__ acat, unsigned long long* __restrict__ rowsum,
-               uint32_t* __restrict__ bad) {
+    k_pack_a(const uint64_t* __restrict__ a, uint64_t M, uint64_t K, uint32_t pa, uint32_t pb,
+             uint8_t* __restrict__ acat, unsigned long long* __restrict__ rowsum) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t groups = M * K / 16, span = (groups + 31) & ~31ull;  // warp-uniform trip count
+    const uint64_t off = 1ull << (8 * pa - 1);
     for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < span; gi += stride) {
         const bool in = gi < groups;
         const uint64_t idx = in ? gi * 16 : 0, i = idx / K, k = idx - i * K;
         unsigned long long sum = 0;
         if (in) {
-        const ulonglong2* src = reinterpret_cast<const ulonglong2*>(a + idx);
-        uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+            const ulonglong2* src = reinterpret_cast<const ulonglong2*>(a + idx);
+            uint32_t w[kMaxPlanes][4] = {};
 #pragma unroll
-        for (int q = 0; q < 8; q++) {
-            const ulonglong2 pr = __ldg(src + q);
-            const uint32_t v0 = shifted16(pr.x, bad), v1 = shifted16(pr.y, bad);
-            sum += v0 + v1;
-            const int e = 2 * q, w = e >> 2, sh = (e & 3) * 8;
-            hw[w] |= ((v0 >> 8) << sh) | ((v1 >> 8) << (sh + 8));
-            lw[w] |= ((v0 & 255u) << sh) | ((v1 & 255u) << (sh + 8));
-        }
-        const uint4 h = make_uint4(hw[0], hw[1], hw[2], hw[3]), l = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        *reinterpret_cast<uint4*>(ah + idx) = h;
-        *reinterpret_cast<uint4*>(al + idx) = l;
-        uint64_t c1, c2;
-        cat_cols(k, K, c1, c2);
-        *reinterpret_cast<uint4*>(acat + i * 2 * K + c1) = h;
-        *reinterpret_cast<uint4*>(acat + i * 2 * K + c2) = l;
+            for (int q = 0; q < 8; q++) {
+                const ulonglong2 pr = __ldg(src + q);
+                const uint32_t v0 = shifted(pr.x, off), v1 = shifted(pr.y, off);
+                sum += v0 + v1;
+                const int e = 2 * q, wi = e >> 2, sh = (e & 3) * 8;
+#pragma unroll
+                for (uint32_t pl = 0; pl < kMaxPlanes; pl++)
+                    w[pl][wi] |= (((v0 >> (8 * pl)) & 255u) << sh) | (((v1 >> (8 * pl)) & 255u) << (sh + 8));
+            }
+            const uint4 pl0 = make_uint4(w[0][0], w[0][1], w[0][2], w[0][3]);
+            const uint4 pl1 = make_uint4(w[1][0], w[1][1], w[1][2], w[1][3]);
+            const uint4 pl2 = make_uint4(w[2][0], w[2][1], w[2][2], w[2][3]);
+            for (uint32_t s = 0; s + 1 < pa + pb; s++) {
+                const uint32_t lo = pair_lo(s, pb), cnt = pair_count(s, pa, pb);
+                uint8_t* reg = acat + region_off(s, pa, pb, M, K) + i * cnt * K;
+                for (uint32_t p = 0; p < cnt; p++) {
+                    const uint32_t qa = lo + p;  // selects, not an indexed (local-memory) array
+                    *reinterpret_cast<uint4*>(reg + cat_col(k, K, cnt, p)) = qa == 0 ? pl0 : qa == 1 ? pl1 : pl2;
+                }
+            }
         }
         // one atomic per warp when its 32 groups share a row
         const uint64_t i0 = __shfl_sync(0xffffffffu, i, 0);
@@ -124,21 +161,21 @@ __global__ void __launch_bounds__(kThr)
     }
 }
 
-// B (K x N field, row-major) -> transposed planes BH, BL (N x K bytes) and
-// BCAT (N x 2K: per chunk [b_l | b_h]), colsum[j] = sum_k b'; 32 x 32 tiles
-// through shared memory so the field reads run along rows of B and the byte
-// writes (four bytes per store) along rows of the transposes.  One atomic per
-// column per tile.
+// B (K x N field, row-major) -> its PB planes transposed (N x K bytes) into
+// every region pair they take part in (pair p of region s uses plane s -
+// q_a); colsum[j] = sum_k b'.  32 x 32 tiles through shared memory so the
+// field reads run along rows of B and the byte writes (four bytes per
+// store) along rows of the transposes; one atomic per column per tile.
 __global__ void __launch_bounds__(kThr)
-    k_planes_b(const uint64_t* __restrict__ b, uint64_t K, uint64_t N, uint8_t* __restrict__ bh,
-               uint8_t* __restrict__ bl, uint8_t* __restrict__ bcat, unsigned long long* __restrict__ colsum,
-               uint32_t* __restrict__ bad) {
+    k_pack_b(const uint64_t* __restrict__ b, uint64_t K, uint64_t N, uint32_t pa, uint32_t pb,
+             uint8_t* __restrict__ bcat, unsigned long long* __restrict__ colsum) {
     __shared__ uint32_t tile[32][33];
     const uint64_t k0 = (uint64_t)blockIdx.y * 32, n0 = (uint64_t)blockIdx.x * 32;
     const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    const uint64_t off = 1ull << (8 * pb - 1);
     for (uint32_t r = ty; r < 32; r += 8) {
         const uint64_t k = k0 + r, n = n0 + tx;
-        tile[r][tx] = (k < K && n < N) ? shifted16(__ldg(b + k * N + n), bad) : 0;
+        tile[r][tx] = (k < K && n < N) ? shifted(__ldg(b + k * N + n), off) : 0;
     }
     __syncthreads();
     if (ty == 0 && n0 + tx < N) {
@@ -151,45 +188,44 @@ __global__ void __launch_bounds__(kThr)
     const uint32_t nr = threadIdx.x >> 3, kq = (threadIdx.x & 7) * 4;
     const uint64_t n = n0 + nr, k = k0 + kq;
     if (n < N && k < K) {  // K % 16 == 0: the four bytes are all inside
-        uint32_t h = 0, l = 0;
+        uint32_t w[kMaxPlanes] = {};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const uint32_t v = tile[kq + e][nr];
-            h |= (v >> 8) << (8 * e);
-            l |= (v & 255u) << (8 * e);
+#pragma unroll
+            for (uint32_t pl = 0; pl < kMaxPlanes; pl++) w[pl] |= ((v >> (8 * pl)) & 255u) << (8 * e);
         }
-        *reinterpret_cast<uint32_t*>(bh + n * K + k) = h;
-        *reinterpret_cast<uint32_t*>(bl + n * K + k) = l;
-        uint64_t c1, c2;
-        cat_cols(k, K, c1, c2);
-        *reinterpret_cast<uint32_t*>(bcat + n * 2 * K + c1) = l;
-        *reinterpret_cast<uint32_t*>(bcat + n * 2 * K + c2) = h;
+        for (uint32_t s = 0; s + 1 < pa + pb; s++) {
+            const uint32_t lo = pair_lo(s, pb), cnt = pair_count(s, pa, pb);
+            uint8_t* reg = bcat + region_off(s, pa, pb, N, K) + n * cnt * K;
+            for (uint32_t p = 0; p < cnt; p++) {
+                const uint32_t qb = s - (lo + p);
+                *reinterpret_cast<uint32_t*>(reg + cat_col(k, K, cnt, p)) = qb == 0 ? w[0] : qb == 1 ? w[1] : w[2];
+            }
+        }
     }
 }
 
-// acc (+)= 2^16 hh + 2^8 x + ll
-__global__ void k_tc_accumulate(const int32_t* __restrict__ hh, const int32_t* __restrict__ x,
-                                const int32_t* __restrict__ ll, uint64_t mn, int64_t* __restrict__ acc, int first) {
+// acc (+)= g << shift (u64, wrapping)
+__global__ void k_tc_add(const int32_t* __restrict__ g, uint64_t mn, uint32_t shift, uint64_t* __restrict__ acc,
+                         int first) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += stride) {
-        const int64_t v = ((int64_t)hh[i] << 16) + ((int64_t)x[i] << 8) + (int64_t)ll[i];
+        const uint64_t v = (uint64_t)(int64_t)g[i] << shift;
         acc[i] = first ? v : acc[i] + v;
     }
 }
 
-// c = from_i64(sum - 2^15 (rowsum_i + colsum_j) + K 2^30), with sum either the
-// i64 accumulator or, for one chunk, 2^16 hh + 2^8 x + ll directly.
-__global__ void k_tc_finish(const int32_t* __restrict__ hh, const int32_t* __restrict__ x,
-                            const int32_t* __restrict__ ll, const int64_t* __restrict__ acc,
-                            const unsigned long long* __restrict__ rowsum,
+// c = from_i64(sum a'b' - oB rowsum_i - oA colsum_j + K oA oB), in wrapping
+// u64 arithmetic: the true value sum a b has |.| < K 2^46 < 2^63.
+__global__ void k_tc_finish(const uint64_t* __restrict__ acc, const unsigned long long* __restrict__ rowsum,
                             const unsigned long long* __restrict__ colsum, uint64_t M, uint64_t N, uint64_t K,
-                            uint64_t* __restrict__ c) {
+                            uint64_t oa, uint64_t ob, uint64_t* __restrict__ c) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < M * N; idx += stride) {
         const uint64_t i = idx / N, j = idx - i * N;
-        const int64_t s = acc ? acc[idx] : ((int64_t)hh[idx] << 16) + ((int64_t)x[idx] << 8) + (int64_t)ll[idx];
-        const int64_t v = s - (int64_t)((rowsum[i] + colsum[j]) << 15) + (int64_t)(K << 30);
-        c[idx] = v >= 0 ? (uint64_t)v : GL_P - (uint64_t)(-v);  // from_i64; |v| < 2^62
+        const int64_t v = (int64_t)(acc[idx] - ob * rowsum[i] - oa * colsum[j] + K * oa * ob);
+        c[idx] = v >= 0 ? (uint64_t)v : GL_P - (uint64_t)(-v);  // from_i64
     }
 }
 
@@ -198,13 +234,14 @@ unsigned tc_grid(uint64_t work) {
     return (unsigned)(b < 148ull * 16 ? (b ? b : 1) : 148ull * 16);
 }
 
-// Scratch layout in bytes (regions 256-byte aligned).
+// Scratch layout in bytes (regions 256-byte aligned), sized for three planes
+// on each side (nine plane pairs).
 struct TcScratch {
-    uint8_t *ah, *al, *acat, *bh, *bl, *bcat;
-    int32_t *hh, *x, *ll;
-    int64_t* acc;
+    uint8_t *acat, *bcat;
+    int32_t* g;
+    uint64_t* acc;
     unsigned long long *rowsum, *colsum;
-    uint32_t* bad;
+    uint32_t* flags;
     void* ws;
     uint64_t ws_bytes;
 };
@@ -216,19 +253,14 @@ uint64_t tc_layout(uint64_t M, uint64_t K, uint64_t N, uint64_t ws_bytes, TcScra
         off += (bytes + 255) & ~255ull;
     };
     TcScratch s{};
-    take(&s.ah, M * K);
-    take(&s.al, M * K);
-    take(&s.acat, 2 * M * K);
-    take(&s.bh, N * K);
-    take(&s.bl, N * K);
-    take(&s.bcat, 2 * N * K);
-    take(&s.hh, 4 * M * N);
-    take(&s.x, 4 * M * N);
-    take(&s.ll, 4 * M * N);
-    take(&s.acc, K > kKChunk ? 8 * M * N : 0);
+    const uint64_t pairs = (uint64_t)kMaxPlanes * kMaxPlanes;
+    take(&s.acat, pairs * M * K);
+    take(&s.bcat, pairs * N * K);
+    take(&s.g, 4 * M * N);
+    take(&s.acc, 8 * M * N);
     take(&s.rowsum, 8 * M);
     take(&s.colsum, 8 * N);
-    take(&s.bad, 8);
+    take(&s.flags, 8);
     take(&s.ws, ws_bytes);
     s.ws_bytes = ws_bytes;
     if (t) *t = s;
@@ -250,11 +282,11 @@ typename TcGemm::Arguments tc_args(const uint8_t* a, uint64_t lda, const uint8_t
                                       {{1, 0}, nullptr, sd, d, sd}, hw};
 }
 
-// workspace of the largest of the three GEMM shapes
+// workspace of the largest of the GEMM shapes (one to three plane pairs)
 uint64_t tc_ws_bytes(uint64_t M, uint64_t K, uint64_t N) {
     const int kc = (int)(K < kKChunk ? K : kKChunk);
     uint64_t w = 0;
-    for (int kk : {kc, 2 * kc}) {
+    for (int kk : {kc, 2 * kc, 3 * kc}) {
         auto args = tc_args(nullptr, K, nullptr, K, nullptr, (int)M, (int)N, kk, 148, 0);
         const uint64_t b = TcGemm::get_workspace_size(args);
         w = b > w ? b : w;
@@ -287,7 +319,7 @@ bool tc_shape_ok(uint64_t M, uint64_t K, uint64_t N) {
     // TMA row strides of 16 bytes (u8 K, i32 N), int tile coordinates; the
     // plane kernel of B puts K / 32 in grid.y (at most 65535)
     return M && K && N && K % 16 == 0 && N % 4 == 0 && M < (1ull << 30) && N < (1ull << 30) &&
-           2 * K < (1ull << 30) && ceil_div(K, 32) <= 65535;
+           3 * K < (1ull << 30) && ceil_div(K, 32) <= 65535 && K < (1ull << 17);
 }
 
 }  // namespace
@@ -323,35 +355,42 @@ int zkie2_matmul_fixed(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uin
     tc_layout(m, k, n, tc_ws_bytes(m, k, n), &s, reinterpret_cast<uint8_t*>(d_scratch));
     ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * m, stream));
     ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
-    ZK_TRY(cudaMemsetAsync(s.bad, 0, 4, stream));
-    k_planes_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, s.ah, s.al, s.acat, s.rowsum, s.bad);
+    ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
+    k_tc_range<<<tc_grid(m * k), kThr, 0, stream>>>(d_a, m * k, s.flags);
     ZK_LAUNCH_CHECK();
-    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
-    if (gb.y > 65535) return (int)cudaErrorInvalidValue;
-    k_planes_b<<<gb, kThr, 0, stream>>>(d_b, k, n, s.bh, s.bl, s.bcat, s.colsum, s.bad);
+    k_tc_range<<<tc_grid(k * n), kThr, 0, stream>>>(d_b, k * n, s.flags + 1);
     ZK_LAUNCH_CHECK();
-    uint32_t bad = 0;
-    ZK_TRY(cudaMemcpyAsync(&bad, s.bad, 4, cudaMemcpyDeviceToHost, stream));
+    uint32_t flags[2] = {0, 0};
+    ZK_TRY(cudaMemcpyAsync(flags, s.flags, 8, cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaStreamSynchronize(stream));
-    if (bad) {  // a value outside 16-bit fixed point: the exact field kernel
+    if ((flags[0] | flags[1]) & 2u) {  // a value outside 24-bit fixed point: the exact field kernel
         if (h_path) *h_path = 1;
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
+    const uint32_t pa = flags[0] ? 3 : 2, pb = flags[1] ? 3 : 2;
+    k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum);
+    ZK_LAUNCH_CHECK();
+    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
+    k_pack_b<<<gb, kThr, 0, stream>>>(d_b, k, n, pa, pb, s.bcat, s.colsum);
+    ZK_LAUNCH_CHECK();
     const int sms = g_sm_count[dev];
     const uint64_t chunks = ceil_div(k, kKChunk);
+    bool first = true;
     for (uint64_t c = 0; c < chunks; c++) {
         const uint64_t c0 = c * kKChunk, kc = k - c0 < kKChunk ? k - c0 : kKChunk;
-        rc = run_gemm(s.ah + c0, k, s.bh + c0, k, s.hh, m, n, kc, s, sms, dev, stream);
-        if (!rc) rc = run_gemm(s.acat + 2 * c0, 2 * k, s.bcat + 2 * c0, 2 * k, s.x, m, n, 2 * kc, s, sms, dev, stream);
-        if (!rc) rc = run_gemm(s.al + c0, k, s.bl + c0, k, s.ll, m, n, kc, s, sms, dev, stream);
-        if (rc) return rc;
-        if (chunks > 1) {
-            k_tc_accumulate<<<tc_grid(m * n), kThr, 0, stream>>>(s.hh, s.x, s.ll, m * n, s.acc, c == 0);
+        for (uint32_t sp = 0; sp + 1 < pa + pb; sp++) {
+            const uint64_t cnt = pair_count(sp, pa, pb);
+            const uint8_t* ar = s.acat + region_off(sp, pa, pb, m, k) + cnt * c0;
+            const uint8_t* br = s.bcat + region_off(sp, pa, pb, n, k) + cnt * c0;
+            rc = run_gemm(ar, cnt * k, br, cnt * k, s.g, m, n, cnt * kc, s, sms, dev, stream);
+            if (rc) return rc;
+            k_tc_add<<<tc_grid(m * n), kThr, 0, stream>>>(s.g, m * n, 8 * sp, s.acc, first ? 1 : 0);
             ZK_LAUNCH_CHECK();
+            first = false;
         }
     }
-    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(s.hh, s.x, s.ll, chunks > 1 ? s.acc : nullptr, s.rowsum, s.colsum,
-                                                     m, n, k, d_c);
+    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(s.acc, s.rowsum, s.colsum, m, n, k, 1ull << (8 * pa - 1),
+                                                     1ull << (8 * pb - 1), d_c);
     ZK_LAUNCH_CHECK();
     if (h_path) *h_path = 0;
     return 0;

@@ -259,7 +259,7 @@ def matmul_field(a, b, m, k, n) -> torch.Tensor:
 
 def matmul_fixed(a, b, m, k, n, force_tensor=False):
     """par::mm_par_fixed: the same product as matmul_field, on the tensor cores when
-    every input is 16-bit fixed point (and, unless force_tensor, the product has at
+    every input is fixed point of at most 24 bits (and, unless force_tensor, the product has at
     least 2^27 multiply-adds); returns (C on the device, path) with path 0 = tensor
     cores, 1 = the field kernel."""
     da, db = to_dev(a).reshape(-1), to_dev(b).reshape(-1)
