@@ -263,20 +263,47 @@ __global__ void k_token_fill(const uint32_t* __restrict__ tid, uint64_t s, uint6
 }
 
 // out[t h + d] = sum over the token's positions of weighted[pos h + d]
-// gate[pos] (field sums: the list order does not matter)
-__global__ void k_gather_rows(const uint64_t* __restrict__ weighted, const uint64_t* __restrict__ gate, uint64_t h,
-                              const uint32_t* __restrict__ off, const uint32_t* __restrict__ list, uint64_t m,
-                              uint64_t* __restrict__ out) {
+// gate[pos] (field sums: the list order does not matter).  Block (t, y)
+// covers columns y 256 .. + 255 of token t, one column per thread; the
+// token's positions and gates are staged in shared memory 256 at a time, so
+// a long list (the padding positions all route to token 0) costs one
+// coalesced load per position and column, four in flight per thread.
+__global__ void __launch_bounds__(kMoeThreads) k_gather_rows(const uint64_t* __restrict__ weighted,
+                                                             const uint64_t* __restrict__ gate, uint64_t h,
+                                                             const uint32_t* __restrict__ off,
+                                                             const uint32_t* __restrict__ list, uint64_t m,
+                                                             uint64_t* __restrict__ out) {
+    __shared__ uint32_t s_pos[kMoeThreads];
+    __shared__ uint64_t s_gate[kMoeThreads];
+    const uint64_t d = (uint64_t)blockIdx.y * kMoeThreads + threadIdx.x;
     for (uint64_t t = blockIdx.x; t < m; t += gridDim.x) {
         const uint32_t q0 = off[t], q1 = off[t + 1];
-        for (uint64_t d = threadIdx.x; d < h; d += blockDim.x) {
-            uint64_t acc = 0;
-            for (uint32_t q = q0; q < q1; q++) {
-                const uint64_t pos = list[q];
-                acc = gl_add(acc, gl_mul(__ldg(weighted + pos * h + d), __ldg(gate + pos)));
+        uint64_t acc = 0;
+        for (uint32_t c0 = q0; c0 < q1; c0 += kMoeThreads) {
+            const uint32_t cn = q1 - c0 < (uint32_t)kMoeThreads ? q1 - c0 : (uint32_t)kMoeThreads;
+            __syncthreads();  // the previous chunk is no longer read
+            if (threadIdx.x < cn) {
+                const uint32_t pos = list[c0 + threadIdx.x];
+                s_pos[threadIdx.x] = pos;
+                s_gate[threadIdx.x] = __ldg(gate + pos);
             }
-            out[t * h + d] = gl_canon(acc);
+            __syncthreads();
+            if (d < h) {
+                uint32_t q = 0;
+                for (; q + 4 <= cn; q += 4) {
+                    const uint64_t w0 = __ldg(weighted + (uint64_t)s_pos[q] * h + d);
+                    const uint64_t w1 = __ldg(weighted + (uint64_t)s_pos[q + 1] * h + d);
+                    const uint64_t w2 = __ldg(weighted + (uint64_t)s_pos[q + 2] * h + d);
+                    const uint64_t w3 = __ldg(weighted + (uint64_t)s_pos[q + 3] * h + d);
+                    acc = gl_add(acc, gl_mul(w0, s_gate[q]));
+                    acc = gl_add(acc, gl_mul(w1, s_gate[q + 1]));
+                    acc = gl_add(acc, gl_mul(w2, s_gate[q + 2]));
+                    acc = gl_add(acc, gl_mul(w3, s_gate[q + 3]));
+                }
+                for (; q < cn; q++) acc = gl_add(acc, gl_mul(__ldg(weighted + (uint64_t)s_pos[q] * h + d), s_gate[q]));
+            }
         }
+        if (d < h) out[t * h + d] = gl_canon(acc);
     }
 }
 
@@ -501,7 +528,10 @@ int zkie2_op_gather(const uint64_t* d_weighted, const uint32_t* d_token_id, cons
         k_token_fill<<<moe_grid(s), kMoeThreads, 0, stream>>>(d_token_id, s, m, off, cursor, list);
         ZK_LAUNCH_CHECK();
     }
-    k_gather_rows<<<block_grid(m), kMoeThreads, 0, stream>>>(d_weighted, d_gate, h, off, list, m, d_out);
+    const uint64_t dblocks = ceil_div(h, kMoeThreads);
+    if (dblocks > 65535) return (int)cudaErrorInvalidValue;
+    const dim3 grid(m < 65535ull * 16 ? (unsigned)m : 65535u * 16, (unsigned)dblocks);
+    k_gather_rows<<<grid, kMoeThreads, 0, stream>>>(d_weighted, d_gate, h, off, list, m, d_out);
     ZK_LAUNCH_CHECK();
     return 0;
 }
