@@ -101,3 +101,34 @@ def test_gather_token_outside_is_an_error(zk):
     with pytest.raises(ValueError, match="lookup index"):
         C.forward_ops(st, [C.Gather(w, tid, g, out, 4, 4)])
     torch.cuda.synchronize()
+
+
+def test_index_and_scale_ops_edge_cases(zk):
+    """The no-proof arms against the CPU restatement where the reference's
+    semantics bite: PadIdx truncating (len below the base's length),
+    IdxBroadcast and CombineIdx wrapping in u32, ScaleVec with a scale
+    shorter than x (cycled) and negative products, BroadcastScale over rows."""
+    C = zk.compose
+    host = co.HostStore()
+    rng = np.random.default_rng(7)
+    base = host.push_idx(rng.integers(0, 1 << 32, size=12, dtype=np.uint64).astype(np.uint32))
+    bb = host.push_idx(rng.integers(0, 1 << 32, size=12, dtype=np.uint32))
+    x = host.push(co.from_i64(rng.integers(-(1 << 30), 1 << 30, size=24)))
+    sv = host.push(co.from_i64(rng.integers(-(1 << 20), 1 << 20, size=5)))
+    rows = host.push(co.from_i64(rng.integers(-1000, 1000, size=6)))
+    outs = [host.push_idx(None) for _ in range(4)] + [host.push(None), host.push(None)]
+    ops = [C.PadIdx(base, outs[0], 7), C.PadIdx(base, outs[1], 20), C.IdxBroadcast(base, outs[2], 3000),
+           C.CombineIdx(base, bb, outs[3], 1 << 20), C.ScaleVec(x, sv, outs[4], 7),
+           C.BroadcastScale(x, rows, outs[5], 4)]
+    dev = zk.compose.Store()
+    for v in host.v:
+        dev.push(None if v is None else v.copy())
+    for i in host.idx:
+        dev.push_idx(None if i is None else i.copy())
+    C.forward_ops(dev, ops)
+    co.forward_ops(host, ops)
+    for t in outs[:4]:
+        assert np.array_equal(dev.get_idx(t).cpu().numpy(), host.idx[t]), t
+    for t in outs[4:]:
+        assert np.array_equal(dev.get(t).cpu().numpy(), host.v[t]), t
+    assert host.idx[outs[0]].size == 7 and host.idx[outs[1]].size == 20
