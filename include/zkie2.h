@@ -508,6 +508,16 @@ int zkie2_op_scale_vec(const uint64_t *d_x, uint64_t n, const uint64_t *d_scale,
  * holds len >= ceil(n / h) values. */
 int zkie2_op_broadcast_scale(const uint64_t *d_x, uint64_t n, const uint64_t *d_scale, uint64_t len, uint64_t h,
                              uint64_t *d_out, zkie_stream_t stream);
+/* ScaleGate (:1294-1318): out[i] = from_i64(round_div(to_i64(x[i])
+ * to_i64(gate[(i / h) n + col]), 2^shift)); gate holds gate_len values. */
+int zkie2_op_scale_gate(const uint64_t *d_x, uint64_t len, const uint64_t *d_gate, uint64_t gate_len, uint64_t col,
+                        uint64_t n, uint64_t h, uint32_t shift, uint64_t *d_out, zkie_stream_t stream);
+/* Relu (:1319-1326): x where to_i64(x) > 0, else 0. */
+int zkie2_op_relu(const uint64_t *d_x, uint64_t n, uint64_t *d_out, zkie_stream_t stream);
+/* BatchedMatMul's forward (batched_matmul.rs:112-134): c[pos] (n values) =
+ * a[pos] (k values) times w[pos] (k x n), s positions, field arithmetic. */
+int zkie2_op_batched_matmul(const uint64_t *d_a, const uint64_t *d_w, uint64_t s, uint64_t k, uint64_t n,
+                            uint64_t *d_c, zkie_stream_t stream);
 /* IdxBroadcast (:1258-1267): out[i b + j] = base[i] b + j (u32, wrapping). */
 int zkie2_op_idx_broadcast(const uint32_t *d_base, uint64_t nb, uint32_t b, uint32_t *d_out, zkie_stream_t stream);
 /* CombineIdx (:1268-1278): out[i] = a[i] scale + b[i] (u32, wrapping). */

@@ -234,6 +234,16 @@ def forward_ops(store, ops):
             base = store.idx[op.base][:op.len]
             out[:base.size] = base
             store.idx[op.out] = out
+        elif k == "ScaleGate":  # :1294-1318
+            x, gv = g(op.x), to_i64(g(op.gate))
+            sc = gv[(np.arange(x.size) // op.h) * op.n + op.col]
+            with np.errstate(over="ignore"):
+                store.v[op.out] = from_i64(round_div(to_i64(x) * sc, 1 << op.shift))
+        elif k == "Relu":  # :1319-1326
+            x = g(op.x)
+            store.v[op.out] = np.where(to_i64(x) > 0, x % np.uint64(P), np.uint64(0)).astype(np.uint64)
+        elif k == "BatchedMatMul":  # :1241-1244
+            store.v[op.c] = batched_matmul_forward(g(op.a), g(op.w), op.s, op.k, op.n)
         elif k == "Scatter":  # :1213-1223
             store.idx[op.token_id], store.idx[op.expert_of] = scatter_forward(g(op.sel), op.m, op.n)
         elif k == "Gather":  # :1224-1240
@@ -543,6 +553,29 @@ SCATTER_ADD_TARGET_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3])]
 BMM_TERMS = [(1, [0, 1, 2])]
 
 
+def batched_matmul_forward(a, w, s, k, n):
+    """batched_matmul.rs:112-134: g[pos] = a[pos] w[pos] (field), w S x K x N."""
+    a, w = o.u64(a).reshape(s, k), o.u64(w).reshape(s, k, n)
+    return np.concatenate([o.matmul_field(a[p:p + 1], w[p]).reshape(-1) for p in range(s)])
+
+
+def prove_batched_matmul(a, w, g, s, k, n, u, v, ch):
+    """batched_matmul.rs:51-83 -> (claimed, (rounds, finals)): the eq-selector
+    sumcheck over [a, w contracted with eq(v), eq(u) per row]."""
+    w_v = o.mle_partial_eval(o.u64(w).reshape(-1), v)
+    eq_b = np.repeat(o.eq_evals(u), k)
+    claimed = o.mle_eval(g, np.concatenate([v, u]))
+    return (int(claimed), _vp([a, w_v, eq_b], BMM_TERMS, ch))
+
+
+def verify_batched_matmul(p, s, k):
+    """batched_matmul.rs:85-110."""
+    _, (claimed, (rounds, finals)), u, _, ch = p
+    eq_final = o.mle_eval(np.repeat(o.eq_evals(u), k), ch)
+    fin = np.array([int(finals[0]), int(finals[1]), int(eq_final)], dtype=np.uint64)
+    return o.virtual_verify(rounds, BMM_TERMS, claimed, ch, fin)
+
+
 def gather_matmul_forward(seg, expert_of, w_all, s, k, n, n_experts):
     """batched_matmul.rs:331-357: g[pos] = seg[pos] W_all[expert_of[pos]] (field)."""
     seg = o.u64(seg).reshape(s, k)
@@ -699,7 +732,7 @@ def prove_lookup_table(m, table, alpha, beta, rng):
 ADD_TERMS = [(1, [2]), (NEG, [0]), (NEG, [1])]
 # the arms with no proof of their own (compose.rs:1623-1723)
 MARKER_KINDS = ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "ScaleVec", "IdxBroadcast",
-                "CombineIdx", "PadIdx", "BroadcastScale")
+                "CombineIdx", "PadIdx", "BroadcastScale", "ScaleGate", "Relu")
 
 
 def prove_shard_precomputed(store, ops, boundary, rng):
@@ -772,6 +805,13 @@ def prove_shard_precomputed(store, ops, boundary, rng):
         elif k == "Gather":  # :1649-1667
             op_proofs.append(prove_scatter_add(g(op.weighted), store.idx[op.token_id], g(op.gate), g(op.out), op.m,
                                                op.h, rng))
+        elif k == "BatchedMatMul":  # :1668-1681
+            u, v, ch = _draw(rng, _lg(op.s)), _draw(rng, _lg(op.n)), _draw(rng, _lg(op.s * op.k))
+            p = prove_batched_matmul(g(op.a), g(op.w), g(op.c), op.s, op.k, op.n, u, v, ch)
+            claim(op.a, ch)
+            claim(op.w, np.concatenate([v, ch]))
+            claim(op.c, np.concatenate([v, u]))
+            op_proofs.append(("BatchedMatMul", p, u, v, ch))
         elif k == "GatherMatMul":  # :1682-1705
             u, v, ch = _draw(rng, _lg(op.s)), _draw(rng, _lg(op.n)), _draw(rng, _lg(op.s * op.k))
             p = prove_gather_matmul(g(op.a), store.idx[op.expert_of], g(op.w), g(op.c), op.s, op.k, op.n,
@@ -1051,6 +1091,8 @@ def verify_shard(ops, proof):
             ok = verify_scatter_add(p)
         elif k == "GatherMatMul":
             ok = verify_gather_matmul(p, op.s, op.k)
+        elif k == "BatchedMatMul":
+            ok = verify_batched_matmul(p, op.s, op.k)
         elif k == "TopKSelect":
             ok = verify_topk(p, op.k)
         elif k == "Argmax":

@@ -132,3 +132,23 @@ def test_index_and_scale_ops_edge_cases(zk):
     for t in outs[4:]:
         assert np.array_equal(dev.get(t).cpu().numpy(), host.v[t]), t
     assert host.idx[outs[0]].size == 7 and host.idx[outs[1]].size == 20
+
+
+def test_relu_scale_gate_batched_matmul_shard_matches_oracle(zk):
+    """The arms only the Gemma / TimesFM graphs use (Relu, ScaleGate,
+    BatchedMatMul): forward and shard proof equal to the CPU restatement's."""
+    from test_moe_oracle import relu_gate_bmm_shard
+    C = zk.compose
+    host = co.HostStore()
+    ops = relu_gate_bmm_shard(C, host, s=16, k=64, n=32, m=4, h=128)
+    dev = C.Store()
+    for v in host.v:
+        dev.push(None if v is None else v.copy())
+    C.forward_ops(dev, ops)
+    got = C.prove_shard_precomputed(dev, ops, [], zk.gkr.XorShift64(8)).canonical()
+    want = co.prove_shard(host, ops, [], o.XorShift64(8))
+    for op in ops:
+        t = op.writes()[0]
+        assert np.array_equal(dev.get(t).cpu().numpy(), host.v[t]), op.kind
+    _assert_same(got, want)
+    assert co.verify_shard(ops, want)

@@ -194,3 +194,46 @@ def test_moe_layer_shard_verifies():
     res = next(op for op in ops if op.kind == "Add" and op.c == out)
     assert not np.array_equal(st.v[out], st.v[res.a])
     assert proof["bound"], "no tensor was bound by same_poly"
+
+
+def test_reference_batched_matmul_roundtrip():
+    """batched_matmul.rs tests::batched_matmul_roundtrip (:164-215): seed
+    0xbeef, s 4, k 4, n 2, the weights gathered from 3 experts; the endpoint
+    evaluations are a at ch and w contracted with eq(v) at ch; a tampered
+    claim fails."""
+    s, k, n, ne = 4, 4, 2, 3
+    w_all = np.array([(i % 7) + 1 for i in range(ne * k * n)], dtype=np.uint64).reshape(ne, k, n)
+    e_of = np.array([i % ne for i in range(s)])
+    w = w_all[e_of].reshape(-1)
+    seg = np.array([(i % 11) + 1 for i in range(s * k)], dtype=np.uint64)
+    g = co.batched_matmul_forward(seg, w, s, k, n)
+    assert np.array_equal(g, co.gather_matmul_forward(seg, e_of.astype(np.uint32), w_all.reshape(-1), s, k, n, ne))
+    rng = o.XorShift64(0xbeef)
+    u, v, ch = rng.fields(2), rng.fields(1), rng.fields(4)
+    p = co.prove_batched_matmul(seg, w, g, s, k, n, u, v, ch)
+    assert co.verify_batched_matmul(("BatchedMatMul", p, u, v, ch), s, k)
+    claimed, (rounds, finals) = p
+    assert int(finals[0]) == int(o.mle_eval(seg, ch))
+    assert int(finals[1]) == int(o.mle_eval(o.mle_partial_eval(w, v), ch))
+    assert not co.verify_batched_matmul(("BatchedMatMul", ((claimed + 1) % P, (rounds, finals)), u, v, ch), s, k)
+
+
+def relu_gate_bmm_shard(C, store, s=8, k=16, n=4, m=2, h=8):
+    """Relu, ScaleGate and BatchedMatMul chained (the arms of the Gemma /
+    TimesFM graphs): -> ops."""
+    rng = np.random.default_rng(s + k)
+    x = store.push(co.from_i64(rng.integers(-(1 << 20), 1 << 20, size=s * k)))
+    w = store.push(co.from_i64(rng.integers(-(1 << 12), 1 << 12, size=s * k * n)))
+    gate = store.push(co.from_i64(rng.integers(-(1 << 16), 1 << 16, size=m * n)))
+    r, c, sg = store.push(None), store.push(None), store.push(None)
+    return [C.Relu(x, r), C.BatchedMatMul(r, w, c, s, k, n), C.ScaleGate(c, gate, 1, sg, m, n, (s * n) // m, 8)]
+
+
+def test_relu_scale_gate_batched_matmul_shard_verifies():
+    from zkie_b200 import compose as C
+    st = co.HostStore()
+    ops = relu_gate_bmm_shard(C, st)
+    proof = co.prove_shard(st, ops, [], o.XorShift64(4))
+    assert co.verify_shard(ops, proof)
+    xi = co.to_i64(st.v[ops[0].x])
+    assert np.array_equal(co.to_i64(st.v[ops[0].out]), np.maximum(xi, 0))

@@ -147,6 +147,9 @@ SIGNATURES = {
     "zkie2_op_topk_limbs": (i64, [vp, vp, vp, u64, vp, vp, vp, vp, vp]),
     "zkie2_op_rms_norm": (i64, [vp, vp, vp, u64, u64, u64, u64, vp, vp, vp, vp]),
     "zkie2_op_scale_vec": (i64, [vp, u64, vp, u64, u32, vp, vp]),
+    "zkie2_op_scale_gate": (i64, [vp, u64, vp, u64, u64, u64, u64, u32, vp, vp]),
+    "zkie2_op_relu": (i64, [vp, u64, vp, vp]),
+    "zkie2_op_batched_matmul": (i64, [vp, vp, u64, u64, u64, vp, vp]),
     "zkie2_op_broadcast_scale": (i64, [vp, u64, vp, u64, u64, vp, vp]),
     "zkie2_op_idx_broadcast": (i64, [vp, u64, u32, vp, vp]),
     "zkie2_op_combine_idx": (i64, [vp, vp, u64, u32, vp, vp]),

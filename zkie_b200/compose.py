@@ -271,6 +271,40 @@ class PadIdx(_Op):
 
 
 @dataclass
+class ScaleGate(_Op):
+    x: int
+    gate: int
+    col: int
+    out: int
+    m: int
+    n: int
+    h: int
+    shift: int
+    kind = "ScaleGate"
+    _reads, _writes = ("x", "gate"), ("out",)
+
+
+@dataclass
+class Relu(_Op):
+    x: int
+    out: int
+    kind = "Relu"
+    _reads, _writes = ("x",), ("out",)
+
+
+@dataclass
+class BatchedMatMul(_Op):
+    a: int
+    w: int
+    c: int
+    s: int
+    k: int
+    n: int
+    kind = "BatchedMatMul"
+    _reads, _writes = ("a", "w"), ("c",)
+
+
+@dataclass
 class RmsNorm(_Op):
     x: int
     w: int
@@ -597,6 +631,22 @@ def forward_ops(store: Store, ops):
                                       err.data_ptr(), sh), "zkie2_op_gather")
         elif k == "GatherMatMul":
             _gather_matmul_forward(store, op, err)
+        elif k == "ScaleGate":
+            x, gate = g(op.x), g(op.gate)
+            out = _slot(store, op.out, x.numel())
+            check(lib.zkie2_op_scale_gate(ptr(x), x.numel(), ptr(gate), gate.numel(), op.col, op.n, op.h, op.shift,
+                                          ptr(out), sh), "zkie2_op_scale_gate")
+        elif k == "Relu":
+            x = g(op.x)
+            out = _slot(store, op.out, x.numel())
+            check(lib.zkie2_op_relu(ptr(x), x.numel(), ptr(out), sh), "zkie2_op_relu")
+        elif k == "BatchedMatMul":
+            a, w = g(op.a), g(op.w)
+            if a.numel() != op.s * op.k or w.numel() != op.s * op.k * op.n:
+                raise ValueError("BatchedMatMul: tensor sizes do not match s, k, n")
+            out = _slot(store, op.c, op.s * op.n)
+            check(lib.zkie2_op_batched_matmul(ptr(a), ptr(w), op.s, op.k, op.n, ptr(out), sh),
+                  "zkie2_op_batched_matmul")
         elif k in ("TopKSelect", "Argmax"):
             mn = op.m * op.n
             thr = _slot(store, op.thr, op.m)
@@ -875,6 +925,19 @@ class ScatterAddProof:
 
 
 @dataclass
+class BatchedMatMulOpProof:
+    """OpProof::BatchedMatMul(BatchedMatmulProof, u, v, ch) (batched_matmul.rs:24-28)."""
+    claimed: int
+    sumcheck: VirtualProof
+    u: np.ndarray
+    v: np.ndarray
+    ch: np.ndarray
+
+    def canonical(self):
+        return ("BatchedMatMul", (int(self.claimed), _vcanon(self.sumcheck)), self.u, self.v, self.ch)
+
+
+@dataclass
 class GatherMatMulOpProof:
     """OpProof::GatherMatMul(GatherMatMulProof, u, v, ch) (batched_matmul.rs:462-467)."""
     claimed: int
@@ -988,7 +1051,7 @@ SCATTER_ADD_TARGET_TERMS = [(1, [0, 1]), (NEG, [0, 2, 3])]                      
 BMM_TERMS = [(1, [0, 1, 2])]                                                       # batched_matmul.rs:40-42
 # the arms with no proof of their own (compose.rs:1623-1723)
 MARKER_KINDS = ("Transpose", "Scale", "SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "ScaleVec", "IdxBroadcast",
-                "CombineIdx", "PadIdx", "BroadcastScale")
+                "CombineIdx", "PadIdx", "BroadcastScale", "ScaleGate", "Relu")
 RECOMPOSE_TERMS = [(1, [0]), (NEG, [1]), (NEG * (1 << 16) % P, [2]), (NEG * (1 << 32) % P, [3])]  # :428-433
 
 
@@ -1301,6 +1364,28 @@ class OpShardProver:
         prod_target = self.virtual([self.eq_table(r_pt), tgt[0], tgt[2], tgt[3]], SCATTER_ADD_TARGET_TERMS, r_pt)
         return lambda: ScatterAddProof(source_side(), target_side(), alpha, gamma, src[0], src[1], tgt[0], tgt[1],
                                        prod_source(), prod_target(), r_ps, r_pt, wt, gate, out, tid)
+
+    def op_batched_matmul(self, op: BatchedMatMul):
+        """The Op::BatchedMatMul arm (compose.rs:1668-1681, batched_matmul.rs:51-83):
+        w contracted with eq(v) (one partial evaluation), the eq-selector
+        sumcheck; a, w and c claimed at ch, v || ch and v || u."""
+        g = self.store.get
+        a, w, c = g(op.a), g(op.w), g(op.c)
+        s_, k, n = op.s, op.k, op.n
+        ls, lk, ln = _lg(s_), _lg(k), _lg(n)
+        u, v, ch = self.draw(ls), self.draw(ln), self.draw(ls + lk)
+        self.traffic += 8 * (s_ * k * n + 3 * s_ * k + s_ * n)
+        w_v = empty(s_ * k)
+        scr = empty(max(lib.zkie2_mle_scratch_elems(ls + lk + ln), 1))
+        check(lib.zkie2_mle_partial_eval(ptr(w), ls + lk + ln, _pp(v), ln, ptr(w_v), ptr(scr), self.sh),
+              "zkie2_mle_partial_eval")
+        claimed = self.eval(c, np.concatenate([v, u]))
+        sc = self.virtual([a, w_v, self.broadcast(self.eq_table(u), s_, k)], BMM_TERMS, ch)
+        self.claim(op.a, ch, sc.final(0))
+        self.claim(op.w, np.concatenate([v, ch]), sc.final(1))
+        self.claim(op.c, np.concatenate([v, u]), claimed)
+        pend = self.pend
+        return lambda: BatchedMatMulOpProof(pend.value(claimed), sc(), u, v, ch)
 
     def op_gather_matmul(self, op: GatherMatMul):
         """prove_gather_matmul (batched_matmul.rs:469-494, prove_streaming
@@ -1627,7 +1712,8 @@ class OpShardProver:
                 "Softmax": self.op_softmax, "Layernorm": self.op_layernorm,
                 "LayerNormCentered": self.op_layer_norm_centered, "TopKSelect": self.op_topk,
                 "Argmax": self.op_topk, "RmsNorm": self.op_rms_norm, "RoPE": self.op_rope, "Scatter": self.op_scatter,
-                "Gather": self.op_gather, "GatherMatMul": self.op_gather_matmul}
+                "Gather": self.op_gather, "GatherMatMul": self.op_gather_matmul,
+                "BatchedMatMul": self.op_batched_matmul}
         self.err.zero_()
         start = torch.cuda.Event()
         start.record(self.main)

@@ -83,6 +83,42 @@ __global__ void k_combine_idx(const uint32_t* __restrict__ a, const uint32_t* __
         out[i] = __ldg(a + i) * scale + __ldg(b + i);
 }
 
+// ScaleGate (compose.rs:1294-1318): out[i] = from_i64(round_div(to_i64(x[i])
+// to_i64(gate[(i / h) n + col]), 2^shift))
+__global__ void k_scale_gate(const uint64_t* __restrict__ x, uint64_t len, const uint64_t* __restrict__ gate,
+                             uint64_t col, uint64_t n, uint64_t h, uint32_t shift, uint64_t* __restrict__ out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += stride) {
+        const int64_t g = fx_to_i64(gl_canon(__ldg(gate + (i / h) * n + col)));
+        out[i] = fx_from_i64(fx_round_div_pow2(fx_wmul(fx_to_i64(gl_canon(__ldg(x + i))), g), shift));
+    }
+}
+
+// Relu (compose.rs:1319-1326): x where to_i64(x) > 0, else 0
+__global__ void k_relu(const uint64_t* __restrict__ x, uint64_t n, uint64_t* __restrict__ out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const uint64_t v = gl_canon(__ldg(x + i));
+        out[i] = fx_to_i64(v) > 0 ? v : 0;
+    }
+}
+
+// BatchedMatMul forward (batched_matmul.rs:112-134): g[pos n + j] = sum_d
+// a[pos k + d] w[pos k n + d n + j] (field); one thread per output, the
+// reads of w along j coalesced, every element of w read once
+__global__ void k_batched_matmul(const uint64_t* __restrict__ a, const uint64_t* __restrict__ w, uint64_t s,
+                                 uint64_t k, uint64_t n, uint64_t* __restrict__ g) {
+    const uint64_t total = s * n, stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t o = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += stride) {
+        const uint64_t pos = o / n, j = o % n;
+        const uint64_t* ap = a + pos * k;
+        const uint64_t* wp = w + pos * k * n + j;
+        uint64_t acc = 0;
+        for (uint64_t d = 0; d < k; d++) acc = gl_add(acc, gl_mul(__ldg(ap + d), __ldg(wp + d * n)));
+        g[o] = gl_canon(acc);
+    }
+}
+
 // ---- RoPE (rope.rs:87-124 forward, :126-196 the prover's columns) ------------------------
 struct RopeCols {
     uint64_t *x_f, *x_s, *o_f, *o_s, *cos_b, *sin_b, *rem_f, *rem_s;
@@ -389,6 +425,34 @@ int zkie2_op_scale_vec(const uint64_t* d_x, uint64_t n, const uint64_t* d_scale,
     if (n == 0) return 0;
     if (!d_x || !d_scale || !d_out) return (int)cudaErrorInvalidValue;
     k_scale_vec<<<moe_grid(n), kMoeThreads, 0, stream>>>(d_x, n, d_scale, len, shift, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_scale_gate(const uint64_t* d_x, uint64_t len, const uint64_t* d_gate, uint64_t gate_len, uint64_t col,
+                        uint64_t n, uint64_t h, uint32_t shift, uint64_t* d_out, cudaStream_t stream) {
+    if (shift > 62 || h == 0 || col >= n || (len && ((len - 1) / h) * n + col >= gate_len))
+        return (int)cudaErrorInvalidValue;
+    if (len == 0) return 0;
+    if (!d_x || !d_gate || !d_out) return (int)cudaErrorInvalidValue;
+    k_scale_gate<<<moe_grid(len), kMoeThreads, 0, stream>>>(d_x, len, d_gate, col, n, h, shift, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_relu(const uint64_t* d_x, uint64_t n, uint64_t* d_out, cudaStream_t stream) {
+    if (n == 0) return 0;
+    if (!d_x || !d_out) return (int)cudaErrorInvalidValue;
+    k_relu<<<moe_grid(n), kMoeThreads, 0, stream>>>(d_x, n, d_out);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+int zkie2_op_batched_matmul(const uint64_t* d_a, const uint64_t* d_w, uint64_t s, uint64_t k, uint64_t n,
+                            uint64_t* d_c, cudaStream_t stream) {
+    if (s == 0 || n == 0) return 0;
+    if (!d_c || (k && (!d_a || !d_w))) return (int)cudaErrorInvalidValue;
+    k_batched_matmul<<<moe_grid(s * n), kMoeThreads, 0, stream>>>(d_a, d_w, s, k, n, d_c);
     ZK_LAUNCH_CHECK();
     return 0;
 }
