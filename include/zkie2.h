@@ -247,9 +247,10 @@ int zkie2_matmul_field(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uin
 /* The forward witness of a fixed-point matmul (par::mm_par_fixed, zkie-ops/src/par.rs:41-89):
  * d_c (m x n) = d_a (m x k) times d_b (k x n), row-major field elements, exactly as
  * zkie2_matmul_field.  When every input lies in [-2^23, 2^23) (to_i64 of the field element)
- * and k % 16 == 0, n % 4 == 0, k < 2^17, the products run on the tensor cores (u8 x u8 -> s32
- * tcgen05 GEMMs over two or three byte planes per operand, two where its values lie in
- * [-2^15, 2^15), offset to unsigned and recombined exactly); otherwise the exact field kernel
+ * and k % 16 == 0, n % 4 == 0 (and k < 2^17 once an operand needs 24 bits), the products run
+ * on the tensor cores (u8 x u8 -> s32 tcgen05 GEMMs over two or three byte planes per operand,
+ * two where its values lie in [-2^15, 2^15), offset to unsigned and recombined exactly);
+ * otherwise the exact field kernel
  * runs, as the reference falls back to its field matmul.  policy 0: the field kernel also
  * below 2^27 multiply-adds, where it is faster; policy 1: the tensor cores whenever the inputs
  * allow.  *h_path (optional) = 0 tensor cores, 1 field kernel.  The tensor path reads two

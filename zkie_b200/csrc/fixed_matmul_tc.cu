@@ -14,7 +14,8 @@
 // each plane-sum s as ONE GEMM over the pairs' planes concatenated along K
 // (three GEMMs for 2 x 2 planes, five for 3 x 3), and the offsets come off
 // exactly:  sum_k a b = sum_k a'b' - o_b rowsum_i(A') - o_a colsum_j(B')
-// + K o_a o_b, in wrapping u64 arithmetic (|sum_k a b| < K 2^46 < 2^63).
+// + K o_a o_b, in wrapping u64 arithmetic (|sum_k a b| <= K 2^(8 (P_a + P_b) - 2)
+// < 2^63: K < 2^17 for three planes on both sides, the field kernel past it).
 // Every s32 sum stays below 3 * 8192 * 255^2 < 2^31 by splitting K into
 // chunks of at most 8192.  Inputs outside 24 bits, or a K or N that TMA
 // cannot address (K % 16, N % 4), take the exact field kernel instead, so
@@ -217,7 +218,7 @@ __global__ void k_tc_add(const int32_t* __restrict__ g, uint64_t mn, uint32_t sh
 }
 
 // c = from_i64(sum a'b' - oB rowsum_i - oA colsum_j + K oA oB), in wrapping
-// u64 arithmetic: the true value sum a b has |.| < K 2^46 < 2^63.
+// u64 arithmetic: the true value sum a b has |.| < 2^63 (the caller's K bound).
 __global__ void k_tc_finish(const uint64_t* __restrict__ acc, const unsigned long long* __restrict__ rowsum,
                             const unsigned long long* __restrict__ colsum, uint64_t M, uint64_t N, uint64_t K,
                             uint64_t oa, uint64_t ob, uint64_t* __restrict__ c) {
@@ -319,7 +320,7 @@ bool tc_shape_ok(uint64_t M, uint64_t K, uint64_t N) {
     // TMA row strides of 16 bytes (u8 K, i32 N), int tile coordinates; the
     // plane kernel of B puts K / 32 in grid.y (at most 65535)
     return M && K && N && K % 16 == 0 && N % 4 == 0 && M < (1ull << 30) && N < (1ull << 30) &&
-           3 * K < (1ull << 30) && ceil_div(K, 32) <= 65535 && K < (1ull << 17);
+           3 * K < (1ull << 30) && ceil_div(K, 32) <= 65535;
 }
 
 }  // namespace
@@ -368,6 +369,12 @@ int zkie2_matmul_fixed(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uin
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
     const uint32_t pa = flags[0] ? 3 : 2, pb = flags[1] ? 3 : 2;
+    // |sum_k a b| <= K 2^(8 (pa + pb) - 2) must stay below 2^63 for the
+    // wrapping recombination: K < 2^(65 - 8 (pa + pb)) (2^17 for 3 x 3 planes)
+    if (k >= (1ull << (65 - 8 * (pa + pb)))) {
+        if (h_path) *h_path = 1;
+        return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
+    }
     k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum);
     ZK_LAUNCH_CHECK();
     const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
