@@ -137,10 +137,15 @@ def test_index_and_scale_ops_edge_cases(zk):
 def test_relu_scale_gate_batched_matmul_shard_matches_oracle(zk):
     """The arms only the Gemma / TimesFM graphs use (Relu, ScaleGate,
     BatchedMatMul): forward and shard proof equal to the CPU restatement's."""
-    from test_moe_oracle import relu_gate_bmm_shard
     C = zk.compose
     host = co.HostStore()
-    ops = relu_gate_bmm_shard(C, host, s=16, k=64, n=32, m=4, h=128)
+    s, k, n, m = 16, 64, 32, 4
+    rng = np.random.default_rng(s + k)
+    x = host.push(co.from_i64(rng.integers(-(1 << 20), 1 << 20, size=s * k)))
+    w = host.push(co.from_i64(rng.integers(-(1 << 12), 1 << 12, size=s * k * n)))
+    gate = host.push(co.from_i64(rng.integers(-(1 << 16), 1 << 16, size=m * n)))
+    r, c, sg = host.push(None), host.push(None), host.push(None)
+    ops = [C.Relu(x, r), C.BatchedMatMul(r, w, c, s, k, n), C.ScaleGate(c, gate, 1, sg, m, n, (s * n) // m, 8)]
     dev = C.Store()
     for v in host.v:
         dev.push(None if v is None else v.copy())
