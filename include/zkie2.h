@@ -259,6 +259,20 @@ uint64_t zkie2_matmul_fixed_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
 int zkie2_matmul_fixed(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
                        uint64_t *d_c, uint32_t policy, uint32_t *h_path, uint64_t *d_scratch,
                        zkie_stream_t stream);
+/* The same product for runs of rows that each multiply one block of a
+ * stack (GatherMatMul's forward, batched_matmul.rs:331-357, with the
+ * positions of one expert consecutive): h_runs holds n_runs triples
+ * (expert e, first row r0, rows), consecutive from row 0; rows r0 .. r0 +
+ * rows - 1 of d_a (k columns) times block e of d_w (n_experts x k x n) into
+ * the same rows of d_c (n columns).  One range pass over all rows and the
+ * whole stack and one read-back, then per run the tensor path (or the field
+ * kernel for runs below 2^27 multiply-adds or operands past 24 bits) with no
+ * further synchronization.  Scratch: zkie2_matmul_fixed_runs_scratch_elems
+ * of the longest run. */
+uint64_t zkie2_matmul_fixed_runs_scratch_elems(uint64_t rows, uint64_t k, uint64_t n);
+int zkie2_matmul_fixed_runs(const uint64_t *d_a, const uint64_t *d_w, uint64_t n_experts, uint64_t k, uint64_t n,
+                            const uint64_t *h_runs, uint64_t n_runs, uint64_t *d_c, uint64_t *d_scratch,
+                            zkie_stream_t stream);
 /* The projection block's witness columns (crates/zkie-ops/src/projection.rs, the
  * out / rem_off construction of its tests, :136-176): for each of n elements,
  * with a = to_i64(h) (h = x @ W) and b = to_i64(bias),

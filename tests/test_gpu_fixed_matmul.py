@@ -135,3 +135,38 @@ def test_tall_field_matmul_runs_in_row_blocks(zk, orc):
     got, path = zk.matmul_fixed(a, b, m, k, n, force_tensor=True)
     assert path == 1  # k % 16 != 0: the field kernel
     assert np.array_equal(got.cpu().numpy().reshape(m, n), orc.matmul_field(a, b))
+
+
+@pytest.mark.parametrize("bits", [16, 24, 30])
+def test_runs_entry_matches_field(zk, bits):
+    """zkie2_matmul_fixed_runs (the GatherMatMul forward): consecutive runs of
+    rows, each times one block of a stack of expert matrices, short runs on
+    the field kernel and long ones on the tensor path (or all on the field
+    kernel for 30-bit operands): every row equal to its field product."""
+    import torch
+
+    from zkie_b200._lib import check, lib, pu64
+    from zkie_b200.device import ptr, stream_handle, to_dev
+    ne, k, n = 5, 2048, 512
+    sizes = [300, 7, 1, 160, 40, 0, 200]
+    experts = [3, 0, 4, 3, 1, 2, 0]
+    runs, r0 = [], 0
+    for e, nr in zip(experts, sizes):
+        if nr:
+            runs += [e, r0, nr]
+            r0 += nr
+    rows = r0
+    a = fixed(bits, (rows, k), -(1 << (bits - 1)), 1 << (bits - 1))
+    w = fixed(bits + 1, (ne, k, n), -(1 << 15), 1 << 15)
+    da, dw = to_dev(a).reshape(-1), to_dev(w).reshape(-1)
+    dc = torch.empty(rows * n, dtype=torch.uint64, device="cuda")
+    h_runs = np.array(runs, dtype=np.uint64)
+    scr = torch.empty(max(lib.zkie2_matmul_fixed_runs_scratch_elems(int(h_runs[2::3].max()), k, n), 1),
+                      dtype=torch.uint64, device="cuda")
+    check(lib.zkie2_matmul_fixed_runs(ptr(da), ptr(dw), ne, k, n, h_runs.ctypes.data_as(pu64), len(runs) // 3,
+                                      ptr(dc), ptr(scr), stream_handle()), "zkie2_matmul_fixed_runs")
+    got = dc.cpu().numpy().reshape(rows, n)
+    for q in range(len(runs) // 3):
+        e, r, nr = runs[3 * q:3 * q + 3]
+        want = zk.matmul_field(a[r:r + nr], w[e], nr, k, n).cpu().numpy().reshape(nr, n)
+        assert np.array_equal(got[r:r + nr], want), (e, r, nr)

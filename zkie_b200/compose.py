@@ -471,14 +471,20 @@ def _gather_matmul_forward(store: Store, op, err):
     e = eof.cpu().numpy().astype(np.int64)
     if e.size and int(e.max()) >= ne:
         raise ValueError("GatherMatMul: an expert index outside the weights")
-    p0 = 0
+    runs, p0 = [], 0
     while p0 < s:
         p1 = p0 + 1
         while p1 < s and e[p1] == e[p0]:
             p1 += 1
-        blk = w[int(e[p0]) * k * n:(int(e[p0]) + 1) * k * n]
-        c[p0 * n:p1 * n].copy_(_matmul_fixed(a[p0 * k:p1 * k], blk, p1 - p0, k, n))
+        runs += [int(e[p0]), p0, p1 - p0]
         p0 = p1
+    if not runs:
+        return
+    h_runs = np.array(runs, dtype=np.uint64)
+    longest = int(h_runs[2::3].max())
+    scr = empty(max(lib.zkie2_matmul_fixed_runs_scratch_elems(longest, k, n), 1))
+    check(lib.zkie2_matmul_fixed_runs(ptr(a), ptr(w), ne, k, n, _pp(h_runs), len(runs) // 3, ptr(c), ptr(scr),
+                                      stream_handle()), "zkie2_matmul_fixed_runs")
 
 
 def layernorm_columns(x, w, b, table, m, d):

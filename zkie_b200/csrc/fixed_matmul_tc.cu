@@ -323,6 +323,46 @@ bool tc_shape_ok(uint64_t M, uint64_t K, uint64_t N) {
            3 * K < (1ull << 30) && ceil_div(K, 32) <= 65535;
 }
 
+// The tensor path once the plane counts are known: the K bound, the packing,
+// one GEMM per plane-sum and K chunk, the recombination.  rowsum / colsum of
+// the scratch must be zero on entry.
+int tc_product(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n, uint64_t* d_c,
+               uint32_t pa, uint32_t pb, const TcScratch& s, int dev, uint32_t* h_path, cudaStream_t stream) {
+    int rc = 0;
+    // |sum_k a b| <= K 2^(8 (pa + pb) - 2) must stay below 2^63 for the
+    // wrapping recombination: K < 2^(65 - 8 (pa + pb)) (2^17 for 3 x 3 planes)
+    if (k >= (1ull << (65 - 8 * (pa + pb)))) {
+        if (h_path) *h_path = 1;
+        return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
+    }
+    k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum);
+    ZK_LAUNCH_CHECK();
+    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
+    k_pack_b<<<gb, kThr, 0, stream>>>(d_b, k, n, pa, pb, s.bcat, s.colsum);
+    ZK_LAUNCH_CHECK();
+    const int sms = g_sm_count[dev];
+    const uint64_t chunks = ceil_div(k, kKChunk);
+    bool first = true;
+    for (uint64_t c = 0; c < chunks; c++) {
+        const uint64_t c0 = c * kKChunk, kc = k - c0 < kKChunk ? k - c0 : kKChunk;
+        for (uint32_t sp = 0; sp + 1 < pa + pb; sp++) {
+            const uint64_t cnt = pair_count(sp, pa, pb);
+            const uint8_t* ar = s.acat + region_off(sp, pa, pb, m, k) + cnt * c0;
+            const uint8_t* br = s.bcat + region_off(sp, pa, pb, n, k) + cnt * c0;
+            rc = run_gemm(ar, cnt * k, br, cnt * k, s.g, m, n, cnt * kc, s, sms, dev, stream);
+            if (rc) return rc;
+            k_tc_add<<<tc_grid(m * n), kThr, 0, stream>>>(s.g, m * n, 8 * sp, s.acc, first ? 1 : 0);
+            ZK_LAUNCH_CHECK();
+            first = false;
+        }
+    }
+    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(s.acc, s.rowsum, s.colsum, m, n, k, 1ull << (8 * pa - 1),
+                                                     1ull << (8 * pb - 1), d_c);
+    ZK_LAUNCH_CHECK();
+    if (h_path) *h_path = 0;
+    return 0;
+}
+
 }  // namespace
 
 }  // namespace zk
@@ -369,37 +409,66 @@ int zkie2_matmul_fixed(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uin
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
     const uint32_t pa = flags[0] ? 3 : 2, pb = flags[1] ? 3 : 2;
-    // |sum_k a b| <= K 2^(8 (pa + pb) - 2) must stay below 2^63 for the
-    // wrapping recombination: K < 2^(65 - 8 (pa + pb)) (2^17 for 3 x 3 planes)
-    if (k >= (1ull << (65 - 8 * (pa + pb)))) {
-        if (h_path) *h_path = 1;
-        return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
+    return tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, h_path, stream);
+}
+
+uint64_t zkie2_matmul_fixed_runs_scratch_elems(uint64_t rows, uint64_t k, uint64_t n) {
+    return zkie2_matmul_fixed_scratch_elems(rows, k, n);
+}
+
+int zkie2_matmul_fixed_runs(const uint64_t* d_a, const uint64_t* d_w, uint64_t n_experts, uint64_t k, uint64_t n,
+                            const uint64_t* h_runs, uint64_t n_runs, uint64_t* d_c, uint64_t* d_scratch,
+                            cudaStream_t stream) {
+    if (!d_a || !d_w || !d_c || !h_runs || !k || !n) return (int)cudaErrorInvalidValue;
+    uint64_t rows = 0, max_rows = 0;
+    for (uint64_t r = 0; r < n_runs; r++) {
+        const uint64_t e = h_runs[3 * r], r0 = h_runs[3 * r + 1], nr = h_runs[3 * r + 2];
+        if (e >= n_experts || r0 != rows || nr == 0) return (int)cudaErrorInvalidValue;  // consecutive runs
+        rows += nr;
+        max_rows = nr > max_rows ? nr : max_rows;
     }
-    k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum);
-    ZK_LAUNCH_CHECK();
-    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
-    k_pack_b<<<gb, kThr, 0, stream>>>(d_b, k, n, pa, pb, s.bcat, s.colsum);
-    ZK_LAUNCH_CHECK();
-    const int sms = g_sm_count[dev];
-    const uint64_t chunks = ceil_div(k, kKChunk);
-    bool first = true;
-    for (uint64_t c = 0; c < chunks; c++) {
-        const uint64_t c0 = c * kKChunk, kc = k - c0 < kKChunk ? k - c0 : kKChunk;
-        for (uint32_t sp = 0; sp + 1 < pa + pb; sp++) {
-            const uint64_t cnt = pair_count(sp, pa, pb);
-            const uint8_t* ar = s.acat + region_off(sp, pa, pb, m, k) + cnt * c0;
-            const uint8_t* br = s.bcat + region_off(sp, pa, pb, n, k) + cnt * c0;
-            rc = run_gemm(ar, cnt * k, br, cnt * k, s.g, m, n, cnt * kc, s, sms, dev, stream);
-            if (rc) return rc;
-            k_tc_add<<<tc_grid(m * n), kThr, 0, stream>>>(s.g, m * n, 8 * sp, s.acc, first ? 1 : 0);
-            ZK_LAUNCH_CHECK();
-            first = false;
+    if (rows == 0) return 0;
+    // every run's rows start 16-byte aligned when d_a is (k % 16 == 0)
+    const bool tc_ok = tc_shape_ok(max_rows, k, n) && (reinterpret_cast<uintptr_t>(d_a) & 15) == 0 && d_scratch;
+    uint32_t pa = 0, pb = 0;
+    TcScratch s{};
+    const int dev = current_device();
+    if (tc_ok) {
+        if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+        int rc = sm_count_of(dev);
+        if (rc) return rc;
+        tc_layout(max_rows, k, n, tc_ws_bytes(max_rows, k, n), &s, reinterpret_cast<uint8_t*>(d_scratch));
+        // one range pass over every row and every expert block, one read-back
+        ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
+        k_tc_range<<<tc_grid(rows * k), kThr, 0, stream>>>(d_a, rows * k, s.flags);
+        ZK_LAUNCH_CHECK();
+        k_tc_range<<<tc_grid(n_experts * k * n), kThr, 0, stream>>>(d_w, n_experts * k * n, s.flags + 1);
+        ZK_LAUNCH_CHECK();
+        uint32_t flags[2] = {0, 0};
+        ZK_TRY(cudaMemcpyAsync(flags, s.flags, 8, cudaMemcpyDeviceToHost, stream));
+        ZK_TRY(cudaStreamSynchronize(stream));
+        if (!((flags[0] | flags[1]) & 2u)) {
+            pa = flags[0] ? 3 : 2;
+            pb = flags[1] ? 3 : 2;
+            if (k >= (1ull << (65 - 8 * (pa + pb)))) pa = pb = 0;
         }
     }
-    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(s.acc, s.rowsum, s.colsum, m, n, k, 1ull << (8 * pa - 1),
-                                                     1ull << (8 * pb - 1), d_c);
-    ZK_LAUNCH_CHECK();
-    if (h_path) *h_path = 0;
+    for (uint64_t r = 0; r < n_runs; r++) {
+        const uint64_t e = h_runs[3 * r], r0 = h_runs[3 * r + 1], nr = h_runs[3 * r + 2];
+        const uint64_t* a = d_a + r0 * k;
+        const uint64_t* w = d_w + e * k * n;
+        uint64_t* c = d_c + r0 * n;
+        const bool small = (double)nr * (double)k * (double)n < (double)(1ull << 27);
+        int rc;
+        if (pa && !small) {
+            ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * nr, stream));
+            ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
+            rc = tc_product(a, w, nr, k, n, c, pa, pb, s, dev, nullptr, stream);
+        } else {
+            rc = matmul_field_dev(a, w, nr, k, n, c, stream);
+        }
+        if (rc) return rc;
+    }
     return 0;
 }
 
