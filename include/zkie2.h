@@ -555,17 +555,17 @@ int zkie2_op_sel_counts(const uint64_t *d_sel, uint64_t m, uint64_t n, uint32_t 
                         zkie_stream_t stream);
 /* scatter_forward (scatter.rs:12-25): for each expert in order, the tokens
  * routed to it; d_expert_cnt from zkie2_op_sel_counts(by_token = 0); the
- * outputs hold sum(d_expert_cnt) entries. */
+ * outputs hold sum(d_expert_cnt) entries; d_scratch: n u64. */
 int zkie2_op_scatter(const uint64_t *d_sel, uint64_t m, uint64_t n, const uint32_t *d_expert_cnt,
-                     uint32_t *d_token_id, uint32_t *d_expert_of, zkie_stream_t stream);
+                     uint32_t *d_token_id, uint32_t *d_expert_of, uint64_t *d_scratch, zkie_stream_t stream);
 /* prove_scatter's multisets (scatter.rs:27-55): d_a (room for m n values) =
  * the source encodings t n + e in token-major order (d_token_cnt from
  * sel_counts(by_token = 1)), d_b[pos] = token_id[pos] n + expert_of[pos] for
- * s positions.  Ones in sel other than s set bit 1 of *d_err (the reference
- * asserts equal lengths). */
+ * s positions; d_scratch: m u64.  Ones in sel other than s set bit 1 of
+ * *d_err (the reference asserts equal lengths). */
 int zkie2_op_scatter_encodings(const uint64_t *d_sel, uint64_t m, uint64_t n, const uint32_t *d_token_cnt,
                                const uint32_t *d_token_id, const uint32_t *d_expert_of, uint64_t s, uint64_t *d_a,
-                               uint64_t *d_b, uint32_t *d_err, zkie_stream_t stream);
+                               uint64_t *d_b, uint64_t *d_scratch, uint32_t *d_err, zkie_stream_t stream);
 /* build_perm_num_den (common/logup_gkr.rs:807-820) into total entries: num 1,
  * den alpha - v for i < len, then 0 / alpha. */
 int zkie2_perm_num_den(const uint64_t *d_v, uint64_t len, uint64_t total, uint64_t alpha, uint64_t *d_num,

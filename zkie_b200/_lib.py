@@ -159,8 +159,8 @@ SIGNATURES = {
     "zkie2_op_rope": (i64, [vp, u64, vp, vp, u64, u64, u32, vp, vp]),
     "zkie2_op_rope_columns": (i64, [vp, vp, u64, vp, vp, u64, u64, u32, vp, vp]),
     "zkie2_op_sel_counts": (i64, [vp, u64, u64, u32, vp, vp]),
-    "zkie2_op_scatter": (i64, [vp, u64, u64, vp, vp, vp, vp]),
-    "zkie2_op_scatter_encodings": (i64, [vp, u64, u64, vp, vp, vp, u64, vp, vp, vp, vp]),
+    "zkie2_op_scatter": (i64, [vp, u64, u64, vp, vp, vp, vp, vp]),
+    "zkie2_op_scatter_encodings": (i64, [vp, u64, u64, vp, vp, vp, u64, vp, vp, vp, vp, vp]),
     "zkie2_perm_num_den": (i64, [vp, u64, u64, u64, vp, vp, vp]),
     "zkie2_op_gather_scratch_u32": (u64, [u64, u64]),
     "zkie2_op_gather": (i64, [vp, vp, vp, u64, u64, u64, vp, vp, vp, vp]),

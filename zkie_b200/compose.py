@@ -624,8 +624,9 @@ def forward_ops(store: Store, ops):
             check(lib.zkie2_op_sel_counts(ptr(sel), op.m, op.n, 0, cnt.data_ptr(), sh), "zkie2_op_sel_counts")
             total = int(cnt[:op.n].to(torch.int64).sum().item())
             tid, eof = _islot(store, op.token_id, total), _islot(store, op.expert_of, total)
-            check(lib.zkie2_op_scatter(ptr(sel), op.m, op.n, cnt.data_ptr(), tid.data_ptr(), eof.data_ptr(), sh),
-                  "zkie2_op_scatter")
+            first = empty(op.n)
+            check(lib.zkie2_op_scatter(ptr(sel), op.m, op.n, cnt.data_ptr(), tid.data_ptr(), eof.data_ptr(),
+                                       ptr(first), sh), "zkie2_op_scatter")
         elif k == "Gather":
             wt, tid, gate = g(op.weighted), store.get_idx(op.token_id), g(op.gate)
             s_ = tid.numel()
@@ -1337,9 +1338,9 @@ class OpShardProver:
         m, n, s_ = op.m, op.n, tid.numel()
         tcnt = _u32(m)
         check(lib.zkie2_op_sel_counts(ptr(sel), m, n, 1, tcnt.data_ptr(), self.sh), "zkie2_op_sel_counts")
-        a, b = empty(m * n), empty(max(s_, 1))
+        a, b, first = empty(m * n), empty(max(s_, 1)), empty(m)
         check(lib.zkie2_op_scatter_encodings(ptr(sel), m, n, tcnt.data_ptr(), tid.data_ptr(), eof.data_ptr(), s_,
-                                             ptr(a), ptr(b), self.err.data_ptr(), self.sh),
+                                             ptr(a), ptr(b), ptr(first), self.err.data_ptr(), self.sh),
               "zkie2_op_scatter_encodings")
         perm = self.permutation(a, b, s_)
         return lambda: ScatterProof(perm())

@@ -204,17 +204,13 @@ __global__ void k_sel_counts(const uint64_t* __restrict__ sel, uint64_t lines, u
 // the ones of the lines before it.  expert-major: token_id = r, expert_of =
 // c; token-major: enc = c n + r (the source encodings t n + e).
 __global__ void k_sel_compact(const uint64_t* __restrict__ sel, uint64_t lines, uint64_t len, uint64_t lstride,
-                              uint64_t estride, const uint32_t* __restrict__ cnt, uint32_t* __restrict__ token_id,
+                              uint64_t estride, const uint64_t* __restrict__ first, uint32_t* __restrict__ token_id,
                               uint32_t* __restrict__ expert_of, uint64_t* __restrict__ enc, uint64_t n) {
     __shared__ uint32_t warp_cnt[kMoeWarps];
     __shared__ uint64_t base;
     for (uint64_t c = blockIdx.x; c < lines; c += gridDim.x) {
         __syncthreads();
-        if (threadIdx.x == 0) {
-            uint64_t b = 0;
-            for (uint64_t q = 0; q < c; q++) b += cnt[q];
-            base = b;
-        }
+        if (threadIdx.x == 0) base = first[c];
         __syncthreads();
         for (uint64_t r0 = 0; r0 < len; r0 += blockDim.x) {
             const uint64_t r = r0 + threadIdx.x;
@@ -233,13 +229,18 @@ __global__ void k_sel_compact(const uint64_t* __restrict__ sel, uint64_t lines, 
     }
 }
 
-// *err |= 1 unless sum(cnt) == s (the multisets of a permutation have one length)
-__global__ void k_check_total(const uint32_t* __restrict__ cnt, uint64_t lines, uint64_t s,
-                              uint32_t* __restrict__ err) {
+// first[c] = cnt[0] + .. + cnt[c - 1] (one thread: the lines are tokens or
+// experts); with err given, *err |= 1 unless the total is s (the multisets
+// of a permutation have one length)
+__global__ void k_line_offsets(const uint32_t* __restrict__ cnt, uint64_t lines, uint64_t* __restrict__ first,
+                               uint64_t s, uint32_t* __restrict__ err) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         uint64_t a = 0;
-        for (uint64_t c = 0; c < lines; c++) a += cnt[c];
-        if (a != s) atomicOr(err, kErrIndex);
+        for (uint64_t c = 0; c < lines; c++) {
+            first[c] = a;
+            a += cnt[c];
+        }
+        if (err && a != s) atomicOr(err, kErrIndex);
     }
 }
 
@@ -532,24 +533,26 @@ int zkie2_op_sel_counts(const uint64_t* d_sel, uint64_t m, uint64_t n, uint32_t 
 }
 
 int zkie2_op_scatter(const uint64_t* d_sel, uint64_t m, uint64_t n, const uint32_t* d_expert_cnt,
-                     uint32_t* d_token_id, uint32_t* d_expert_of, cudaStream_t stream) {
+                     uint32_t* d_token_id, uint32_t* d_expert_of, uint64_t* d_scratch, cudaStream_t stream) {
     if (m == 0 || n == 0) return 0;
-    if (!d_sel || !d_expert_cnt || !d_token_id || !d_expert_of) return (int)cudaErrorInvalidValue;
-    k_sel_compact<<<block_grid(n), kMoeThreads, 0, stream>>>(d_sel, n, m, 1, n, d_expert_cnt, d_token_id,
-                                                              d_expert_of, nullptr, n);
+    if (!d_sel || !d_expert_cnt || !d_token_id || !d_expert_of || !d_scratch) return (int)cudaErrorInvalidValue;
+    k_line_offsets<<<1, 32, 0, stream>>>(d_expert_cnt, n, d_scratch, 0, nullptr);
+    ZK_LAUNCH_CHECK();
+    k_sel_compact<<<block_grid(n), kMoeThreads, 0, stream>>>(d_sel, n, m, 1, n, d_scratch, d_token_id, d_expert_of,
+                                                              nullptr, n);
     ZK_LAUNCH_CHECK();
     return 0;
 }
 
 int zkie2_op_scatter_encodings(const uint64_t* d_sel, uint64_t m, uint64_t n, const uint32_t* d_token_cnt,
                                const uint32_t* d_token_id, const uint32_t* d_expert_of, uint64_t s, uint64_t* d_a,
-                               uint64_t* d_b, uint32_t* d_err, cudaStream_t stream) {
+                               uint64_t* d_b, uint64_t* d_scratch, uint32_t* d_err, cudaStream_t stream) {
     if (m == 0 || n == 0) return 0;
-    if (!d_sel || !d_token_cnt || !d_a || !d_b || !d_err || (s && (!d_token_id || !d_expert_of)))
+    if (!d_sel || !d_token_cnt || !d_a || !d_b || !d_scratch || !d_err || (s && (!d_token_id || !d_expert_of)))
         return (int)cudaErrorInvalidValue;
-    k_check_total<<<1, 32, 0, stream>>>(d_token_cnt, m, s, d_err);
+    k_line_offsets<<<1, 32, 0, stream>>>(d_token_cnt, m, d_scratch, s, d_err);
     ZK_LAUNCH_CHECK();
-    k_sel_compact<<<block_grid(m), kMoeThreads, 0, stream>>>(d_sel, m, n, n, 1, d_token_cnt, nullptr, nullptr, d_a,
+    k_sel_compact<<<block_grid(m), kMoeThreads, 0, stream>>>(d_sel, m, n, n, 1, d_scratch, nullptr, nullptr, d_a,
                                                               n);
     ZK_LAUNCH_CHECK();
     if (s) {
