@@ -1098,9 +1098,11 @@ class _Pending:
         """Every registered buffer in one device array (on the current stream)."""
         return _cat_u64(self.parts) if self.parts else empty(1)
 
-    def download(self, flat: torch.Tensor):
+    def download(self, flat: torch.Tensor, host: Optional[np.ndarray] = None):
+        """Split the gathered results into the registered buffers: copied from
+        ``flat`` now, or taken from ``host`` (a copy already made)."""
         if self.parts:
-            host = flat.cpu().numpy()
+            host = flat.cpu().numpy() if host is None else host
             sizes = np.cumsum([p.numel() for p in self.parts])[:-1]
             self.arrays = np.split(host, sizes)
         else:
@@ -1759,9 +1761,10 @@ class OpShardProver:
         self.pend.parts.append(self.err.to(torch.int64).view(torch.uint64))
         self.flat = self.pend.gather()
 
-    def collect(self) -> OpShardProof:
-        """One copy of the results to the host; the proof objects."""
-        self.pend.download(self.flat)
+    def collect(self, host: Optional[np.ndarray] = None) -> OpShardProof:
+        """One copy of the results to the host (or the copy ``host`` already
+        made of them); the proof objects."""
+        self.pend.download(self.flat, host)
         code = int(self.pend.arrays[-1][0])
         if code:
             raise ValueError("prove_shard: " + ", ".join(v for k, v in _ERRORS.items() if code & k))
@@ -1816,6 +1819,28 @@ class GraphShardProver:
     def prove(self) -> OpShardProof:
         self.replay()
         return self.prover.collect()
+
+    def start(self):
+        """Enqueue the recorded prove and, on a side stream behind it, the copy
+        of its results into pinned host memory; nothing waits, so the host can
+        collect an earlier shard while this one runs."""
+        self.graph.replay()
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream())
+        flat = self.prover.flat
+        if getattr(self, "_host", None) is None:
+            self._host = torch.empty(flat.numel(), dtype=torch.int64).pin_memory()
+            self._copy_stream = torch.cuda.Stream()
+        self._copy_stream.wait_event(done)
+        with torch.cuda.stream(self._copy_stream):
+            self._host.copy_(flat.view(torch.int64), non_blocking=True)
+        self._copied = torch.cuda.Event()
+        self._copied.record(self._copy_stream)
+
+    def finish(self) -> OpShardProof:
+        """The proof of the last ``start`` (waits for its copy only)."""
+        self._copied.synchronize()
+        return self.prover.collect(self._host.numpy().view(np.uint64).copy())
 
 
 _STREAM_POOLS = {}

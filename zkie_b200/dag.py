@@ -72,6 +72,11 @@ class DagProvers:
     summary: Callable
     same_poly: Callable
     commit: Callable = None  # (store, tensor) -> the WHIR base commitment's root (8 values)
+    # optional split of prove: start(store, ops, rng) enqueues and returns a
+    # handle, finish(handle) returns the proof; all of a rank's shards are
+    # started before the first is finished
+    start: Callable = None
+    finish: Callable = None
 
 
 @dataclass
@@ -104,12 +109,20 @@ def prove_dag_ranks(store, ops, ops_per_shard: int, provers: DagProvers, rank: i
     ranges = shard_ranges(len(ops), ops_per_shard)
     master = provers.master(ops, ops_per_shard)
     mine = []
-    for si, (s, e) in enumerate(ranges):
-        if shard_owner(si, world) != rank:
-            continue
-        proof = provers.prove(store, ops[s:e], provers.child(master, si))
+    owned = [si for si in range(len(ranges)) if shard_owner(si, world) == rank]
+
+    def record(si, proof):
         claims = [(int(t), np.asarray(pt, dtype=np.uint64), int(v)) for t, pt, v in provers.claims(proof)]
         mine.append((si, claims, provers.summary(proof)))
+    if provers.start is not None:
+        handles = [(si, provers.start(store, ops[ranges[si][0]:ranges[si][1]], provers.child(master, si)))
+                   for si in owned]
+        for si, h in handles:
+            record(si, provers.finish(h))
+    else:
+        for si in owned:
+            s, e = ranges[si]
+            record(si, provers.prove(store, ops[s:e], provers.child(master, si)))
     everyone = gather(mine) if world > 1 else [mine]
     if rank != 0:
         return None
@@ -162,16 +175,27 @@ def device_provers(summary: str = "digest", graph: bool = False, streams: int = 
 
     graphs = {} if graphs is None else graphs
 
-    def prove(store, shard_ops, rng):
-        if not graph:
-            return C.OpShardProver(store, rng, streams).prove(shard_ops, [])
+    def recorded(store, shard_ops, rng):
         key = (shard_ops[0].__class__.__name__, id(shard_ops[0]), len(shard_ops))
         gp = graphs.get(key)
         if gp is None:
             state = rng.clone()
             gp = C.GraphShardProver(store, shard_ops, [], lambda: state.clone(), streams)
             graphs[key] = gp
-        return gp.prove()
+        return gp
+
+    def prove(store, shard_ops, rng):
+        if not graph:
+            return C.OpShardProver(store, rng, streams).prove(shard_ops, [])
+        return recorded(store, shard_ops, rng).prove()
+
+    def start(store, shard_ops, rng):
+        gp = recorded(store, shard_ops, rng)
+        gp.start()
+        return gp
+
+    def finish(gp):
+        return gp.finish()
 
     def claims(proof):
         return proof.claims
@@ -193,6 +217,7 @@ def device_provers(summary: str = "digest", graph: bool = False, streams: int = 
         v = store.get(t)
         return Whir.with_params(v.numel().bit_length() - 1, 90, 17).commit(v).root
 
-    p = DagProvers(master, child, prove, claims, summ, same_poly, commit)
+    p = DagProvers(master, child, prove, claims, summ, same_poly, commit,
+                   start if graph else None, finish if graph else None)
     p.graphs = graphs
     return p
