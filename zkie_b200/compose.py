@@ -521,15 +521,72 @@ def _islot(store: Store, t: int, n: int) -> torch.Tensor:
     return v
 
 
+# arms whose outputs are index tensors (a separate id space)
+_INDEX_WRITERS = ("SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "Scatter", "PadIdx", "IdxBroadcast", "CombineIdx")
+
+
+def _projection_groups(ops):
+    """Projections that read the same x (same m, k) and whose weights and
+    biases no op writes at or after the first of them: {first index: [the
+    group's indices]} (groups of two or more).  Their products x W_j are one
+    matmul against the weights side by side, done at the first one."""
+    written = {}
+    for i, op in enumerate(ops):
+        if op.kind not in _INDEX_WRITERS:
+            for t in op.writes():
+                written.setdefault(t, i)
+    groups, taken = {}, set()
+    for i, op in enumerate(ops):
+        if op.kind != "Projection" or i in taken:
+            continue
+        grp = [i]
+        for j in range(i + 1, len(ops)):
+            o = ops[j]
+            if (o.kind == "Projection" and j not in taken and o.x == op.x and o.m == op.m and o.k == op.k
+                    and all(written.get(t, -1) < i for t in (o.w, o.bias))):
+                grp.append(j)
+        if len(grp) > 1:
+            taken.update(grp)
+            groups[i] = grp
+    return groups
+
+
+def _projection_witness(store: Store, op, h: torch.Tensor, sh):
+    """out / rem of one Projection from its product h (kept for the prover)."""
+    if op.out in store.proj_h and store.proj_h[op.out].numel() == h.numel():
+        store.proj_h[op.out].copy_(h)
+        h = store.proj_h[op.out]
+    store.proj_h[op.out] = h
+    out, rem = _slot(store, op.out, op.m * op.n), _slot(store, op.rem, op.m * op.n)
+    check(lib.zkie2_projection_witness(ptr(h), ptr(store.get(op.bias)), op.m * op.n, op.shift, ptr(out), ptr(rem),
+                                       None, sh), "zkie2_projection_witness")
+
+
 def forward_ops(store: Store, ops):
     """forward_ops (compose.rs:1174-1583) on the device, writing every output
     into its existing buffer where it has one; raises where the reference
-    panics on the data (after the whole pass, one read-back)."""
+    panics on the data (after the whole pass, one read-back).  Projections
+    sharing their input x are multiplied as one wide matmul."""
     err = _err_word()
     sh = stream_handle()
-    for op in ops:
+    groups = _projection_groups(ops)
+    grouped = {j for grp in groups.values() for j in grp}
+    for i, op in enumerate(ops):
         k = op.kind
         g = store.get
+        if i in groups:
+            grp = [ops[j] for j in groups[i]]
+            w_cat = torch.cat([g(o.w).view(torch.int64).reshape(op.k, o.n) for o in grp], dim=1).contiguous()
+            total = sum(o.n for o in grp)
+            h_all = _matmul_fixed(g(op.x), w_cat.view(torch.uint64).reshape(-1), op.m, op.k, total)
+            h2 = h_all.view(torch.int64).reshape(op.m, total)
+            c0 = 0
+            for o in grp:
+                _projection_witness(store, o, h2[:, c0:c0 + o.n].contiguous().view(torch.uint64).reshape(-1), sh)
+                c0 += o.n
+            continue
+        if i in grouped:
+            continue  # computed with its group
         if k == "Transpose":
             out = _slot(store, op.out, op.m * op.k)
             check(lib.zkie2_op_transpose(ptr(g(op.x)), op.m, op.k, ptr(out), sh), "zkie2_op_transpose")
@@ -540,14 +597,7 @@ def forward_ops(store: Store, ops):
         elif k == "MatMul":
             _slot(store, op.c, op.m * op.n).copy_(_matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n))
         elif k == "Projection":
-            h = _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n)
-            if op.out in store.proj_h and store.proj_h[op.out].numel() == h.numel():
-                store.proj_h[op.out].copy_(h)
-                h = store.proj_h[op.out]
-            store.proj_h[op.out] = h
-            out, rem = _slot(store, op.out, op.m * op.n), _slot(store, op.rem, op.m * op.n)
-            check(lib.zkie2_projection_witness(ptr(h), ptr(g(op.bias)), op.m * op.n, op.shift, ptr(out), ptr(rem),
-                                               None, sh), "zkie2_projection_witness")
+            _projection_witness(store, op, _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n), sh)
         elif k == "Add":
             a, b = g(op.a), g(op.b)
             out = _slot(store, op.c, a.numel())
