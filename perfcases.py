@@ -387,6 +387,7 @@ def case_layer(a):
     res = {"case": "layer_shard_replay", "ops": len(ops), "ms": ms}
     if a.trace:
         res.update(_trace(gp.replay))
+        res["forward"] = _trace(lambda: C.forward_ops(st, ops))
     return res
 
 

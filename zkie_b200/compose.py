@@ -535,18 +535,15 @@ def _projection_groups(ops):
         if op.kind not in _INDEX_WRITERS:
             for t in op.writes():
                 written.setdefault(t, i)
-    groups, taken = {}, set()
+    by_input = {}
     for i, op in enumerate(ops):
-        if op.kind != "Projection" or i in taken:
-            continue
-        grp = [i]
-        for j in range(i + 1, len(ops)):
-            o = ops[j]
-            if (o.kind == "Projection" and j not in taken and o.x == op.x and o.m == op.m and o.k == op.k
-                    and all(written.get(t, -1) < i for t in (o.w, o.bias))):
-                grp.append(j)
+        if op.kind == "Projection":
+            by_input.setdefault((op.x, op.m, op.k), []).append(i)
+    groups = {}
+    for members in by_input.values():
+        i = members[0]
+        grp = [i] + [j for j in members[1:] if all(written.get(t, -1) < i for t in (ops[j].w, ops[j].bias))]
         if len(grp) > 1:
-            taken.update(grp)
             groups[i] = grp
     return groups
 
