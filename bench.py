@@ -1001,11 +1001,17 @@ def shard_case(zk, build, config, want_cpu, iters):
     t0 = time.perf_counter()
     ops, x, out = build(st)
     build_s = time.perf_counter() - t0
+    # the forward recorded as a CUDA graph where the graph allows it (no
+    # routing read back to the host), else eager
+    t0 = time.perf_counter()
+    gf = None if any(op.kind in ("Scatter", "GatherMatMul") for op in ops) else C.GraphForward(st, ops)
+    fwd_capture_s = time.perf_counter() - t0
+    forward = gf.run if gf is not None else (lambda: C.forward_ops(st, ops))
     fwd = []
     for it in range(iters + 2):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        C.forward_ops(st, ops)
+        forward()
         torch.cuda.synchronize()
         if it >= 2:
             fwd.append(time.perf_counter() - t0)
@@ -1032,7 +1038,7 @@ def shard_case(zk, build, config, want_cpu, iters):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        C.forward_ops(st, ops)
+        forward()
         e0.record(stream)
         gp.replay()
         e1.record(stream)
@@ -1053,7 +1059,10 @@ def shard_case(zk, build, config, want_cpu, iters):
     out_d = {
         "config": config,
         "ms": round(1e3 * statistics.median(whole), 3), "unit": "ms per layer shard (forward + prove + proof to host)",
-        "forward_ms": round(1e3 * statistics.median(fwd), 3), "prove_ms": round(prove_ms, 3),
+        "forward_ms": round(1e3 * statistics.median(fwd), 3),
+        "forward": ("CUDA graph (GraphForward, recorded in %.0f ms)" % (1e3 * fwd_capture_s)) if gf is not None
+                   else "eager (routing read back to the host)",
+        "prove_ms": round(prove_ms, 3),
         "collect_ms": round(1e3 * statistics.median(collect), 3),
         "eager_prove_ms": round(1e3 * statistics.median(eager), 3), "capture_ms": round(1e3 * capture_s, 1),
         "build_s": round(build_s, 2), "ops": len(ops), "same_poly_binds": len(sh.binds), "claims": len(sh.claims),
@@ -1112,11 +1121,12 @@ def cfg4_case(zk, dev, rank, world, layers=12):
     st = C.Store()
     ops, _, _ = gpt2.gpt2_model(st, gpt2.GPT2_SMALL, layers)
     build_s = time.perf_counter() - t0
+    gf = C.GraphForward(st, ops)  # the whole graph's forward, recorded once
     fwd = []
-    for _ in range(2):
+    for _ in range(3):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        C.forward_ops(st, ops)
+        gf.run()
         torch.cuda.synchronize()
         fwd.append(time.perf_counter() - t0)
     per = 176

@@ -259,6 +259,20 @@ uint64_t zkie2_matmul_fixed_scratch_elems(uint64_t m, uint64_t k, uint64_t n);
 int zkie2_matmul_fixed(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
                        uint64_t *d_c, uint32_t policy, uint32_t *h_path, uint64_t *d_scratch,
                        zkie_stream_t stream);
+/* zkie2_matmul_fixed reporting its choices: h_plan = {path (0 tensor cores, 1 field kernel),
+ * planes of A, planes of B}. */
+int zkie2_matmul_fixed_ex(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
+                          uint64_t *d_c, uint32_t policy, uint32_t *h_plan, uint64_t *d_scratch,
+                          zkie_stream_t stream);
+/* The product with the choices of an earlier call fixed (h_plan as above),
+ * no read-back and no synchronization, so it can be recorded in a CUDA graph:
+ * the operands' widths are still checked on the device, and operands that
+ * need more planes than planned (or more than 24 bits) set bit 3 (value 4) of
+ * *d_err, in which case d_c is not the product and the caller recomputes it
+ * with zkie2_matmul_fixed. */
+int zkie2_matmul_fixed_planned(const uint64_t *d_a, const uint64_t *d_b, uint64_t m, uint64_t k, uint64_t n,
+                               uint64_t *d_c, const uint32_t *h_plan, uint64_t *d_scratch, uint32_t *d_err,
+                               zkie_stream_t stream);
 /* The same product for runs of rows that each multiply one block of a
  * stack (GatherMatMul's forward, batched_matmul.rs:331-357, with the
  * positions of one expert consecutive): h_runs holds n_runs triples

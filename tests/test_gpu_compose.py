@@ -289,3 +289,37 @@ def test_topk_selected_spread_outside_the_range_table(zk):
         C.prove_shard_precomputed(dev, ops, [], zk.gkr.XorShift64(1))
     with pytest.raises(IndexError):
         co.prove_shard(host, ops, [], o.XorShift64(1))
+
+
+def test_graph_forward_replays_new_witnesses_and_falls_back(zk):
+    """GraphForward: the forward of a GPT-2-shaped layer whose wide products
+    take the tensor path, recorded once; a new witness in the same buffers
+    replays to the CPU restatement's forward, and a witness whose FFN weights
+    outgrow the recorded byte planes is detected on the device and recomputed
+    eagerly, again equal to the restatement."""
+    from zkie_b200 import gpt2
+    from zkie_b200.device import to_dev
+    shape = gpt2.LayerShape(m=256, d=512, d_real=384, heads=8, dh=64, ffn=2048, ffn_real=1536, exp_bits=16,
+                            gelu_bits=18, rsqrt_len=1 << 16)
+    host, ops = _layer(zk, shape)
+    dev = _device_store(zk, host)
+    gf = zk.compose.GraphForward(dev, ops)
+    assert any(int(h[0]) == 0 for _, h in gf.plan.steps), "no product took the tensor path"
+    x = ops[0].x
+    rng = np.random.default_rng(3)
+    for step in range(2):
+        if step == 0:
+            new = np.zeros((shape.m, shape.d), dtype=np.uint64)
+            new[:, :shape.d_real] = rng.integers(0, 50, size=(shape.m, shape.d_real)).astype(np.uint64)
+            t = x
+        else:  # the FFN weights past 16 bits
+            t = next(op for op in ops if op.kind == "Projection" and op.n == shape.ffn).w
+            new = co.from_i64(rng.integers(-(1 << 20), 1 << 20, size=host.v[t].size))
+        host.v[t] = new.reshape(-1)
+        dev.get(t).copy_(to_dev(host.v[t]).reshape(-1))
+        gf.run()
+        co.forward_ops(host, ops)
+        for i, v in enumerate(host.v):
+            if v is not None:
+                assert np.array_equal(dev.get(i).cpu().numpy(), v), f"step {step}: tensor {i}"
+        assert gf.fallbacks == step

@@ -148,6 +148,8 @@ SIGNATURES = {
     "zkie2_op_rms_norm": (i64, [vp, vp, vp, u64, u64, u64, u64, vp, vp, vp, vp]),
     "zkie2_op_scale_vec": (i64, [vp, u64, vp, u64, u32, vp, vp]),
     "zkie2_matmul_fixed_runs_scratch_elems": (u64, [u64, u64, u64]),
+    "zkie2_matmul_fixed_ex": (i64, [vp, vp, u64, u64, u64, vp, u32, pu32, vp, vp]),
+    "zkie2_matmul_fixed_planned": (i64, [vp, vp, u64, u64, u64, vp, pu32, vp, vp, vp]),
     "zkie2_matmul_fixed_runs": (i64, [vp, vp, u64, u64, u64, pu64, u64, vp, vp, vp]),
     "zkie2_op_scale_gate": (i64, [vp, u64, vp, u64, u64, u64, u64, u32, vp, vp]),
     "zkie2_op_relu": (i64, [vp, u64, vp, vp]),

@@ -497,9 +497,36 @@ def layernorm_columns(x, w, b, table, m, d):
     return dict(mean_sq=mean_sq, idx=idx[:m], rsqrt=rsqrt, scale=scale, out=out)
 
 
-def _matmul_fixed(a, b, m, k, n):
+class _MatmulPlan:
+    """The tensor path's choice for every product of one forward pass, in
+    order: recorded by an eager pass (``record``), then issued without
+    read-backs for a CUDA-graph capture (``replay``; a product whose
+    operands outgrow its recorded planes sets bit 3 of the error word)."""
+
+    def __init__(self):
+        self.mode, self.steps, self.pos = "record", [], 0
+
+
+def _matmul_fixed(a, b, m, k, n, plan: Optional[_MatmulPlan] = None, err: Optional[torch.Tensor] = None):
     from .gkr import matmul_fixed
-    return matmul_fixed(a, b, m, k, n)[0]
+    if plan is None:
+        return matmul_fixed(a, b, m, k, n)[0]
+    da, db = a.reshape(-1), b.reshape(-1)
+    dc = empty(m * n)
+    scr = empty(max(lib.zkie2_matmul_fixed_scratch_elems(m, k, n), 1))
+    if plan.mode == "record":
+        h = np.zeros(3, dtype=np.uint32)
+        check(lib.zkie2_matmul_fixed_ex(ptr(da), ptr(db), m, k, n, ptr(dc), 0, h.ctypes.data_as(_lib.pu32), ptr(scr),
+                                        stream_handle()), "zkie2_matmul_fixed_ex")
+        plan.steps.append(((m, k, n), h))
+    else:
+        shape, h = plan.steps[plan.pos]
+        plan.pos += 1
+        if shape != (m, k, n):
+            raise ValueError("recorded matmul plan does not match the ops")
+        check(lib.zkie2_matmul_fixed_planned(ptr(da), ptr(db), m, k, n, ptr(dc), h.ctypes.data_as(_lib.pu32),
+                                             ptr(scr), err.data_ptr(), stream_handle()), "zkie2_matmul_fixed_planned")
+    return dc
 
 
 def _slot(store: Store, t: int, n: int) -> torch.Tensor:
@@ -521,6 +548,10 @@ def _islot(store: Store, t: int, n: int) -> torch.Tensor:
     return v
 
 
+# arms whose forward reads data back to the host (routing): not recordable
+_HOST_READ_KINDS = ("Scatter", "GatherMatMul")
+# error-word bit of a planned product whose operands outgrew its plan
+ERR_PLAN = 4
 # arms whose outputs are index tensors (a separate id space)
 _INDEX_WRITERS = ("SoftmaxIndex", "GeluIndex", "StableSoftmaxIndex", "Scatter", "PadIdx", "IdxBroadcast", "CombineIdx")
 
@@ -559,13 +590,18 @@ def _projection_witness(store: Store, op, h: torch.Tensor, sh):
                                        None, sh), "zkie2_projection_witness")
 
 
-def forward_ops(store: Store, ops):
+def forward_ops(store: Store, ops, plan: Optional[_MatmulPlan] = None, err: Optional[torch.Tensor] = None):
     """forward_ops (compose.rs:1174-1583) on the device, writing every output
     into its existing buffer where it has one; raises where the reference
-    panics on the data (after the whole pass, one read-back).  Projections
-    sharing their input x are multiplied as one wide matmul."""
-    err = _err_word()
+    panics on the data (after the whole pass, one read-back; with ``err``
+    given the caller reads that error word instead).  Projections sharing
+    their input x are multiplied as one wide matmul.  ``plan`` records or
+    replays the products' tensor-path choices (GraphForward)."""
+    own_err = err is None
+    err = _err_word() if own_err else err
     sh = stream_handle()
+    if plan is not None and plan.mode == "replay" and any(op.kind in _HOST_READ_KINDS for op in ops):
+        raise ValueError("forward_ops: Scatter and GatherMatMul read routing data back and cannot be recorded")
     groups = _projection_groups(ops)
     grouped = {j for grp in groups.values() for j in grp}
     for i, op in enumerate(ops):
@@ -575,7 +611,7 @@ def forward_ops(store: Store, ops):
             grp = [ops[j] for j in groups[i]]
             w_cat = torch.cat([g(o.w).view(torch.int64).reshape(op.k, o.n) for o in grp], dim=1).contiguous()
             total = sum(o.n for o in grp)
-            h_all = _matmul_fixed(g(op.x), w_cat.view(torch.uint64).reshape(-1), op.m, op.k, total)
+            h_all = _matmul_fixed(g(op.x), w_cat.view(torch.uint64).reshape(-1), op.m, op.k, total, plan, err)
             h2 = h_all.view(torch.int64).reshape(op.m, total)
             c0 = 0
             for o in grp:
@@ -592,9 +628,9 @@ def forward_ops(store: Store, ops):
             out = _slot(store, op.out, x.numel())
             check(lib.zkie2_op_scale(ptr(x), x.numel(), op.factor, op.shift, ptr(out), sh), "zkie2_op_scale")
         elif k == "MatMul":
-            _slot(store, op.c, op.m * op.n).copy_(_matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n))
+            _slot(store, op.c, op.m * op.n).copy_(_matmul_fixed(g(op.a), g(op.b), op.m, op.k, op.n, plan, err))
         elif k == "Projection":
-            _projection_witness(store, op, _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n), sh)
+            _projection_witness(store, op, _matmul_fixed(g(op.x), g(op.w), op.m, op.k, op.n, plan, err), sh)
         elif k == "Add":
             a, b = g(op.a), g(op.b)
             out = _slot(store, op.c, a.numel())
@@ -711,7 +747,8 @@ def forward_ops(store: Store, ops):
                   "zkie2_op_topk")
         else:
             raise ValueError(f"op {k} is not supported")
-    _check_err(err, "forward_ops")
+    if own_err:
+        _check_err(err, "forward_ops")
 
 
 # ---- proofs (compose.rs OpProof / OpShardProof, the arms' proof structs) -------------------
@@ -1832,6 +1869,41 @@ class OpShardProver:
                 ev = torch.cuda.Event()
                 ev.record(st)
                 self.main.wait_event(ev)
+
+
+class GraphForward:
+    """forward_ops of one statement recorded once as a CUDA graph and
+    replayed (the forward's launch sequence depends on the op shapes only,
+    once each product's tensor-path choice is fixed).  An eager pass records
+    those choices and allocates every output; ``run`` replays the graph and
+    reads the error word once: a witness whose products need more byte planes
+    than recorded is recomputed by the eager forward.  Graphs with Scatter or
+    GatherMatMul (routing read back to the host) stay eager."""
+
+    def __init__(self, store: Store, ops):
+        self.store, self.ops = store, list(ops)
+        self.plan = _MatmulPlan()
+        forward_ops(store, self.ops, plan=self.plan)
+        torch.cuda.synchronize()
+        self.plan.mode = "replay"
+        self.err = _err_word()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.plan.pos = 0
+            self.err.zero_()
+            forward_ops(store, self.ops, plan=self.plan, err=self.err)
+        torch.cuda.synchronize()
+        self.fallbacks = 0
+
+    def run(self):
+        """The forward for the witness now in the store's inputs."""
+        self.graph.replay()
+        code = int(self.err.item())
+        if code & ERR_PLAN:
+            self.fallbacks += 1
+            forward_ops(self.store, self.ops)
+        elif code:
+            raise ValueError("forward_ops: " + ", ".join(v for k, v in _ERRORS.items() if code & k))
 
 
 class GraphShardProver:

@@ -207,6 +207,16 @@ __global__ void __launch_bounds__(kThr)
     }
 }
 
+// A planned product whose operands need more planes than planned (or more
+// than 24 bits) sets bit 3 (value 4) of *err: its result is not the product.
+__global__ void k_tc_plan_check(const uint32_t* __restrict__ flags, uint32_t pa, uint32_t pb,
+                                uint32_t* __restrict__ err) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const uint32_t fa = flags[0], fb = flags[1];
+        if (((fa | fb) & 2u) || (pa == 2 && (fa & 1u)) || (pb == 2 && (fb & 1u))) atomicOr(err, 4u);
+    }
+}
+
 // acc (+)= g << shift (u64, wrapping)
 __global__ void k_tc_add(const int32_t* __restrict__ g, uint64_t mn, uint32_t shift, uint64_t* __restrict__ acc,
                          int first) {
@@ -378,6 +388,19 @@ uint64_t zkie2_matmul_fixed_scratch_elems(uint64_t m, uint64_t k, uint64_t n) {
 
 int zkie2_matmul_fixed(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n, uint64_t* d_c,
                        uint32_t policy, uint32_t* h_path, uint64_t* d_scratch, cudaStream_t stream) {
+    uint32_t plan[3] = {1, 0, 0};
+    const int rc = zkie2_matmul_fixed_ex(d_a, d_b, m, k, n, d_c, policy, plan, d_scratch, stream);
+    if (!rc && h_path) *h_path = plan[0];
+    return rc;
+}
+
+int zkie2_matmul_fixed_ex(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n,
+                          uint64_t* d_c, uint32_t policy, uint32_t* h_plan, uint64_t* d_scratch,
+                          cudaStream_t stream) {
+    if (!h_plan) return (int)cudaErrorInvalidValue;
+    h_plan[0] = 1;
+    h_plan[1] = h_plan[2] = 0;
+    uint32_t* h_path = h_plan;
     if (!d_a || !d_b || !d_c || !m || !k || !n || policy > 1) return (int)cudaErrorInvalidValue;
     // below ~2^27 multiply-adds the field kernel beats the tensor path's fixed
     // cost (range check read-back, plane packing, three GEMM launches)
@@ -409,7 +432,40 @@ int zkie2_matmul_fixed(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uin
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
     const uint32_t pa = flags[0] ? 3 : 2, pb = flags[1] ? 3 : 2;
-    return tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, h_path, stream);
+    rc = tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, h_path, stream);
+    if (!rc && h_plan[0] == 0) {
+        h_plan[1] = pa;
+        h_plan[2] = pb;
+    }
+    return rc;
+}
+
+int zkie2_matmul_fixed_planned(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n,
+                               uint64_t* d_c, const uint32_t* h_plan, uint64_t* d_scratch, uint32_t* d_err,
+                               cudaStream_t stream) {
+    if (!d_a || !d_b || !d_c || !m || !k || !n || !h_plan) return (int)cudaErrorInvalidValue;
+    if (h_plan[0] != 0) return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
+    const uint32_t pa = h_plan[1], pb = h_plan[2];
+    if (pa < 2 || pa > 3 || pb < 2 || pb > 3 || !d_scratch || !d_err || !tc_shape_ok(m, k, n) ||
+        (reinterpret_cast<uintptr_t>(d_a) & 15) != 0)
+        return (int)cudaErrorInvalidValue;
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    int rc = sm_count_of(dev);
+    if (rc) return rc;
+    TcScratch s;
+    tc_layout(m, k, n, tc_ws_bytes(m, k, n), &s, reinterpret_cast<uint8_t*>(d_scratch));
+    ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * m, stream));
+    ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
+    ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
+    k_tc_range<<<tc_grid(m * k), kThr, 0, stream>>>(d_a, m * k, s.flags);
+    ZK_LAUNCH_CHECK();
+    k_tc_range<<<tc_grid(k * n), kThr, 0, stream>>>(d_b, k * n, s.flags + 1);
+    ZK_LAUNCH_CHECK();
+    k_tc_plan_check<<<1, 32, 0, stream>>>(s.flags, pa, pb, d_err);
+    ZK_LAUNCH_CHECK();
+    uint32_t path = 0;
+    return tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, &path, stream);
 }
 
 uint64_t zkie2_matmul_fixed_runs_scratch_elems(uint64_t rows, uint64_t k, uint64_t n) {
