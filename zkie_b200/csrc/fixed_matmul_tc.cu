@@ -91,17 +91,20 @@ __device__ __forceinline__ uint64_t cat_col(uint64_t k, uint64_t K, uint32_t cnt
     return cnt * c0 + p * kc + (k - c0);
 }
 
+// bit 0: outside [-2^15, 2^15); bit 1: outside [-2^23, 2^23)
+__device__ __forceinline__ uint32_t width_flags(uint64_t x) {
+    x = gl_canon(x);
+    const bool neg = x > GL_P / 2;
+    const uint64_t mag = neg ? GL_P - x : x;
+    return ((neg ? mag > (1ull << 15) : mag >= (1ull << 15)) ? 1u : 0u) |
+           ((neg ? mag > (1ull << 23) : mag >= (1ull << 23)) ? 2u : 0u);
+}
+
 // bit 0: a value outside [-2^15, 2^15); bit 1: outside [-2^23, 2^23)
 __global__ void k_tc_range(const uint64_t* __restrict__ v, uint64_t n, uint32_t* __restrict__ flags) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint32_t f = 0;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const uint64_t x = gl_canon(__ldg(v + i));
-        const uint64_t mag = x <= GL_P / 2 ? x : GL_P - x;  // |to_i64(x)|, with the negative side's one extra value
-        const bool neg = x > GL_P / 2;
-        if (neg ? mag > (1ull << 15) : mag >= (1ull << 15)) f |= 1u;
-        if (neg ? mag > (1ull << 23) : mag >= (1ull << 23)) f |= 2u;
-    }
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) f |= width_flags(__ldg(v + i));
     f = __reduce_or_sync(0xffffffffu, f);
     if ((threadIdx.x & 31) == 0 && f) atomicOr(flags, f);
 }
@@ -117,10 +120,11 @@ __device__ __forceinline__ uint32_t shifted(uint64_t x, uint64_t off) {
 // multiples of 16): 16-byte loads and 16-byte stores of each plane.
 __global__ void __launch_bounds__(kThr)
     k_pack_a(const uint64_t* __restrict__ a, uint64_t M, uint64_t K, uint32_t pa, uint32_t pb,
-             uint8_t* __restrict__ acat, unsigned long long* __restrict__ rowsum) {
+             uint8_t* __restrict__ acat, unsigned long long* __restrict__ rowsum, uint32_t* __restrict__ flags) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t groups = M * K / 16, span = (groups + 31) & ~31ull;  // warp-uniform trip count
     const uint64_t off = 1ull << (8 * pa - 1);
+    uint32_t wf = 0;
     for (uint64_t gi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < span; gi += stride) {
         const bool in = gi < groups;
         const uint64_t idx = in ? gi * 16 : 0, i = idx / K, k = idx - i * K;
@@ -131,6 +135,7 @@ __global__ void __launch_bounds__(kThr)
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 const ulonglong2 pr = __ldg(src + q);
+                wf |= width_flags(pr.x) | width_flags(pr.y);
                 const uint32_t v0 = shifted(pr.x, off), v1 = shifted(pr.y, off);
                 sum += v0 + v1;
                 const int e = 2 * q, wi = e >> 2, sh = (e & 3) * 8;
@@ -160,6 +165,8 @@ __global__ void __launch_bounds__(kThr)
             atomicAdd(rowsum + i, sum);
         }
     }
+    wf = __reduce_or_sync(0xffffffffu, wf);  // every lane runs the same trip count
+    if ((threadIdx.x & 31) == 0 && wf) atomicOr(flags, wf);
 }
 
 // B (K x N field, row-major) -> its PB planes transposed (N x K bytes) into
@@ -169,15 +176,24 @@ __global__ void __launch_bounds__(kThr)
 // store) along rows of the transposes; one atomic per column per tile.
 __global__ void __launch_bounds__(kThr)
     k_pack_b(const uint64_t* __restrict__ b, uint64_t K, uint64_t N, uint32_t pa, uint32_t pb,
-             uint8_t* __restrict__ bcat, unsigned long long* __restrict__ colsum) {
+             uint8_t* __restrict__ bcat, unsigned long long* __restrict__ colsum, uint32_t* __restrict__ flags) {
     __shared__ uint32_t tile[32][33];
     const uint64_t k0 = (uint64_t)blockIdx.y * 32, n0 = (uint64_t)blockIdx.x * 32;
     const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
     const uint64_t off = 1ull << (8 * pb - 1);
+    uint32_t wf = 0;
     for (uint32_t r = ty; r < 32; r += 8) {
         const uint64_t k = k0 + r, n = n0 + tx;
-        tile[r][tx] = (k < K && n < N) ? shifted(__ldg(b + k * N + n), off) : 0;
+        uint32_t v = 0;
+        if (k < K && n < N) {
+            const uint64_t x = __ldg(b + k * N + n);
+            wf |= width_flags(x);
+            v = shifted(x, off);
+        }
+        tile[r][tx] = v;
     }
+    wf = __reduce_or_sync(0xffffffffu, wf);
+    if (tx == 0 && wf) atomicOr(flags, wf);
     __syncthreads();
     if (ty == 0 && n0 + tx < N) {
         unsigned long long sum = 0;
@@ -217,25 +233,42 @@ __global__ void k_tc_plan_check(const uint32_t* __restrict__ flags, uint32_t pa,
     }
 }
 
-// acc (+)= g << shift (u64, wrapping)
-__global__ void k_tc_add(const int32_t* __restrict__ g, uint64_t mn, uint32_t shift, uint64_t* __restrict__ acc,
-                         int first) {
+// The plane-sum GEMMs' s32 outputs (one per s, at most five)
+constexpr uint32_t kMaxSums = 2 * kMaxPlanes - 1;
+struct PlaneSums {
+    const int32_t* g[kMaxSums];
+    uint32_t count;
+};
+
+__device__ __forceinline__ uint64_t plane_sum(const PlaneSums& ps, uint64_t i) {
+    uint64_t v = 0;
+#pragma unroll
+    for (uint32_t q = 0; q < kMaxSums; q++)
+        if (q < ps.count) v += (uint64_t)(int64_t)ps.g[q][i] << (8 * q);
+    return v;
+}
+
+// acc (+)= sum_s 2^(8s) G_s (u64, wrapping): one K chunk of a long K
+__global__ void k_tc_accumulate(PlaneSums ps, uint64_t mn, uint64_t* __restrict__ acc, int first) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += stride) {
-        const uint64_t v = (uint64_t)(int64_t)g[i] << shift;
+        const uint64_t v = plane_sum(ps, i);
         acc[i] = first ? v : acc[i] + v;
     }
 }
 
 // c = from_i64(sum a'b' - oB rowsum_i - oA colsum_j + K oA oB), in wrapping
-// u64 arithmetic: the true value sum a b has |.| < 2^63 (the caller's K bound).
-__global__ void k_tc_finish(const uint64_t* __restrict__ acc, const unsigned long long* __restrict__ rowsum,
+// u64 arithmetic (the true value sum a b has |.| < 2^63: the caller's K
+// bound), with sum a'b' the accumulator or, for one K chunk, the plane sums.
+__global__ void k_tc_finish(PlaneSums ps, const uint64_t* __restrict__ acc,
+                            const unsigned long long* __restrict__ rowsum,
                             const unsigned long long* __restrict__ colsum, uint64_t M, uint64_t N, uint64_t K,
                             uint64_t oa, uint64_t ob, uint64_t* __restrict__ c) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < M * N; idx += stride) {
         const uint64_t i = idx / N, j = idx - i * N;
-        const int64_t v = (int64_t)(acc[idx] - ob * rowsum[i] - oa * colsum[j] + K * oa * ob);
+        const uint64_t sum = acc ? acc[idx] : plane_sum(ps, idx);
+        const int64_t v = (int64_t)(sum - ob * rowsum[i] - oa * colsum[j] + K * oa * ob);
         c[idx] = v >= 0 ? (uint64_t)v : GL_P - (uint64_t)(-v);  // from_i64
     }
 }
@@ -249,7 +282,7 @@ unsigned tc_grid(uint64_t work) {
 // on each side (nine plane pairs).
 struct TcScratch {
     uint8_t *acat, *bcat;
-    int32_t* g;
+    int32_t* g[kMaxSums];
     uint64_t* acc;
     unsigned long long *rowsum, *colsum;
     uint32_t* flags;
@@ -267,8 +300,8 @@ uint64_t tc_layout(uint64_t M, uint64_t K, uint64_t N, uint64_t ws_bytes, TcScra
     const uint64_t pairs = (uint64_t)kMaxPlanes * kMaxPlanes;
     take(&s.acat, pairs * M * K);
     take(&s.bcat, pairs * N * K);
-    take(&s.g, 4 * M * N);
-    take(&s.acc, 8 * M * N);
+    for (uint32_t q = 0; q < kMaxSums; q++) take(&s.g[q], 4 * M * N);
+    take(&s.acc, K > kKChunk ? 8 * M * N : 0);
     take(&s.rowsum, 8 * M);
     take(&s.colsum, 8 * N);
     take(&s.flags, 8);
@@ -333,11 +366,27 @@ bool tc_shape_ok(uint64_t M, uint64_t K, uint64_t N) {
            3 * K < (1ull << 30) && ceil_div(K, 32) <= 65535;
 }
 
-// The tensor path once the plane counts are known: the K bound, the packing,
-// one GEMM per plane-sum and K chunk, the recombination.  rowsum / colsum of
-// the scratch must be zero on entry.
+// Zero the row / column sums and the width flags, then pack both operands
+// for pa x pb planes (the flags record the operands' widths on the way).
+int tc_pack(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n, uint32_t pa, uint32_t pb,
+            const TcScratch& s, cudaStream_t stream) {
+    ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * m, stream));
+    ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
+    ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
+    k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum, s.flags);
+    ZK_LAUNCH_CHECK();
+    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
+    k_pack_b<<<gb, kThr, 0, stream>>>(d_b, k, n, pa, pb, s.bcat, s.colsum, s.flags + 1);
+    ZK_LAUNCH_CHECK();
+    return 0;
+}
+
+// The tensor path once the plane counts are known: the K bound, the packing
+// (unless already done for these plane counts), one GEMM per plane-sum and K
+// chunk, the recombination.
 int tc_product(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k, uint64_t n, uint64_t* d_c,
-               uint32_t pa, uint32_t pb, const TcScratch& s, int dev, uint32_t* h_path, cudaStream_t stream) {
+               uint32_t pa, uint32_t pb, const TcScratch& s, int dev, uint32_t* h_path, cudaStream_t stream,
+               bool packed = false) {
     int rc = 0;
     // |sum_k a b| <= K 2^(8 (pa + pb) - 2) must stay below 2^63 for the
     // wrapping recombination: K < 2^(65 - 8 (pa + pb)) (2^17 for 3 x 3 planes)
@@ -345,29 +394,31 @@ int tc_product(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, uint64_t k,
         if (h_path) *h_path = 1;
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
-    k_pack_a<<<tc_grid(m * k / 16), kThr, 0, stream>>>(d_a, m, k, pa, pb, s.acat, s.rowsum);
-    ZK_LAUNCH_CHECK();
-    const dim3 gb((unsigned)ceil_div(n, 32), (unsigned)ceil_div(k, 32));
-    k_pack_b<<<gb, kThr, 0, stream>>>(d_b, k, n, pa, pb, s.bcat, s.colsum);
-    ZK_LAUNCH_CHECK();
+    if (!packed) {
+        rc = tc_pack(d_a, d_b, m, k, n, pa, pb, s, stream);
+        if (rc) return rc;
+    }
     const int sms = g_sm_count[dev];
     const uint64_t chunks = ceil_div(k, kKChunk);
-    bool first = true;
+    PlaneSums ps{};
+    ps.count = pa + pb - 1;
+    for (uint32_t q = 0; q < ps.count; q++) ps.g[q] = s.g[q];
     for (uint64_t c = 0; c < chunks; c++) {
         const uint64_t c0 = c * kKChunk, kc = k - c0 < kKChunk ? k - c0 : kKChunk;
         for (uint32_t sp = 0; sp + 1 < pa + pb; sp++) {
             const uint64_t cnt = pair_count(sp, pa, pb);
             const uint8_t* ar = s.acat + region_off(sp, pa, pb, m, k) + cnt * c0;
             const uint8_t* br = s.bcat + region_off(sp, pa, pb, n, k) + cnt * c0;
-            rc = run_gemm(ar, cnt * k, br, cnt * k, s.g, m, n, cnt * kc, s, sms, dev, stream);
+            rc = run_gemm(ar, cnt * k, br, cnt * k, s.g[sp], m, n, cnt * kc, s, sms, dev, stream);
             if (rc) return rc;
-            k_tc_add<<<tc_grid(m * n), kThr, 0, stream>>>(s.g, m * n, 8 * sp, s.acc, first ? 1 : 0);
+        }
+        if (chunks > 1) {
+            k_tc_accumulate<<<tc_grid(m * n), kThr, 0, stream>>>(ps, m * n, s.acc, c == 0 ? 1 : 0);
             ZK_LAUNCH_CHECK();
-            first = false;
         }
     }
-    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(s.acc, s.rowsum, s.colsum, m, n, k, 1ull << (8 * pa - 1),
-                                                     1ull << (8 * pb - 1), d_c);
+    k_tc_finish<<<tc_grid(m * n), kThr, 0, stream>>>(ps, chunks > 1 ? s.acc : nullptr, s.rowsum, s.colsum, m, n, k,
+                                                     1ull << (8 * pa - 1), 1ull << (8 * pb - 1), d_c);
     ZK_LAUNCH_CHECK();
     if (h_path) *h_path = 0;
     return 0;
@@ -417,13 +468,10 @@ int zkie2_matmul_fixed_ex(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, 
     if (rc) return rc;
     TcScratch s;
     tc_layout(m, k, n, tc_ws_bytes(m, k, n), &s, reinterpret_cast<uint8_t*>(d_scratch));
-    ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * m, stream));
-    ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
-    ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
-    k_tc_range<<<tc_grid(m * k), kThr, 0, stream>>>(d_a, m * k, s.flags);
-    ZK_LAUNCH_CHECK();
-    k_tc_range<<<tc_grid(k * n), kThr, 0, stream>>>(d_b, k * n, s.flags + 1);
-    ZK_LAUNCH_CHECK();
+    // pack for 16-bit operands (two planes) while recording their widths;
+    // repack for three planes where a width needs it
+    rc = tc_pack(d_a, d_b, m, k, n, 2, 2, s, stream);
+    if (rc) return rc;
     uint32_t flags[2] = {0, 0};
     ZK_TRY(cudaMemcpyAsync(flags, s.flags, 8, cudaMemcpyDeviceToHost, stream));
     ZK_TRY(cudaStreamSynchronize(stream));
@@ -432,7 +480,8 @@ int zkie2_matmul_fixed_ex(const uint64_t* d_a, const uint64_t* d_b, uint64_t m, 
         return matmul_field_dev(d_a, d_b, m, k, n, d_c, stream);
     }
     const uint32_t pa = flags[0] ? 3 : 2, pb = flags[1] ? 3 : 2;
-    rc = tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, h_path, stream);
+    const bool packed = pa == 2 && pb == 2;
+    rc = tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, h_path, stream, packed);
     if (!rc && h_plan[0] == 0) {
         h_plan[1] = pa;
         h_plan[2] = pb;
@@ -455,17 +504,12 @@ int zkie2_matmul_fixed_planned(const uint64_t* d_a, const uint64_t* d_b, uint64_
     if (rc) return rc;
     TcScratch s;
     tc_layout(m, k, n, tc_ws_bytes(m, k, n), &s, reinterpret_cast<uint8_t*>(d_scratch));
-    ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * m, stream));
-    ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
-    ZK_TRY(cudaMemsetAsync(s.flags, 0, 8, stream));
-    k_tc_range<<<tc_grid(m * k), kThr, 0, stream>>>(d_a, m * k, s.flags);
-    ZK_LAUNCH_CHECK();
-    k_tc_range<<<tc_grid(k * n), kThr, 0, stream>>>(d_b, k * n, s.flags + 1);
-    ZK_LAUNCH_CHECK();
+    rc = tc_pack(d_a, d_b, m, k, n, pa, pb, s, stream);
+    if (rc) return rc;
     k_tc_plan_check<<<1, 32, 0, stream>>>(s.flags, pa, pb, d_err);
     ZK_LAUNCH_CHECK();
     uint32_t path = 0;
-    return tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, &path, stream);
+    return tc_product(d_a, d_b, m, k, n, d_c, pa, pb, s, dev, &path, stream, true);
 }
 
 uint64_t zkie2_matmul_fixed_runs_scratch_elems(uint64_t rows, uint64_t k, uint64_t n) {
@@ -517,9 +561,8 @@ int zkie2_matmul_fixed_runs(const uint64_t* d_a, const uint64_t* d_w, uint64_t n
         const bool small = (double)nr * (double)k * (double)n < (double)(1ull << 27);
         int rc;
         if (pa && !small) {
-            ZK_TRY(cudaMemsetAsync(s.rowsum, 0, 8 * nr, stream));
-            ZK_TRY(cudaMemsetAsync(s.colsum, 0, 8 * n, stream));
-            rc = tc_product(a, w, nr, k, n, c, pa, pb, s, dev, nullptr, stream);
+            uint32_t path = 0;
+            rc = tc_product(a, w, nr, k, n, c, pa, pb, s, dev, &path, stream);
         } else {
             rc = matmul_field_dev(a, w, nr, k, n, c, stream);
         }
