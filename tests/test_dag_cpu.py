@@ -144,3 +144,25 @@ def test_gpt2_model_graph_shard_dag():
     assert res.cross_tensors
     for t, sp in zip(res.cross_tensors, res.cross_binds):
         assert co.verify_same_poly(sp, by[t]) is not None
+
+
+def test_projection_groups_follow_the_data_dependencies():
+    """The forward's wide products: Projections that read the same input with
+    weights and biases no op writes at or after the first of them form one
+    group at that first op; a Projection whose weight is produced later, or
+    whose input or shape differs, stays on its own."""
+    from zkie_b200 import compose as C
+    P_ = C.Projection
+    ops = [P_(0, 1, 2, 10, 11, 4, 8, 4, 16),      # x 0: the group's first
+           C.Add(3, 3, 12),                        # writes 12
+           P_(0, 5, 6, 13, 14, 4, 8, 8, 16),       # x 0, constant weights: joins
+           P_(0, 12, 6, 15, 16, 4, 8, 4, 16),      # weight 12 written after op 0: alone
+           P_(7, 1, 2, 17, 18, 4, 8, 4, 16),       # another input
+           P_(0, 1, 2, 19, 20, 4, 16, 4, 16)]      # same x, another k
+    assert C._projection_groups(ops) == {0: [0, 2]}
+    st = co.HostStore()
+    lops, _, _ = gpt2.gpt2_layer(st, gpt2.LayerShape(m=8, d=16, d_real=12, heads=3, dh=4, ffn=32, ffn_real=24,
+                                                     exp_bits=8, gelu_bits=10, rsqrt_len=256))
+    groups = C._projection_groups(lops)
+    assert [len(g) for g in groups.values()] == [9]  # q, k, v of every head read the first LayerNorm's output
+    assert all(lops[j].x == lops[i].x for i, g in groups.items() for j in g)
