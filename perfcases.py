@@ -382,9 +382,9 @@ def case_layer(a):
         c = master.clone()
         c.absorb_u64(0)
         return c
-    gp = C.GraphShardProver(st, ops, [], make_rng)
+    gp = C.GraphShardProver(st, ops, [], make_rng, a.streams)
     ms = _time(gp.replay, a.iters)
-    res = {"case": "layer_shard_replay", "ops": len(ops), "ms": ms}
+    res = {"case": "layer_shard_replay", "ops": len(ops), "streams": a.streams, "ms": ms}
     if a.trace:
         res.update(_trace(gp.replay))
         res["forward"] = _trace(lambda: C.forward_ops(st, ops))
@@ -445,9 +445,10 @@ def case_moe(a):
             c = master.clone()
             c.absorb_u64(0)
             return c
-        gp = C.GraphShardProver(st, ops, [], make_rng)
+        gp = C.GraphShardProver(st, ops, [], make_rng, a.streams)
         gp.replay()
-        return {"case": "moe_layer_trace", "forward": fwd, "prove_replay": _trace(gp.replay)}
+        return {"case": "moe_layer_trace", "streams": a.streams, "replay_ms": _time(gp.replay, a.iters),
+                "forward": fwd, "prove_replay": _trace(gp.replay)}
     return {"case": "moe_layer_shard", **bench.moe_case(zk, torch.device("cuda", 0), a.cpu, a.iters)}
 
 
@@ -521,6 +522,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--trace", action="store_true", help="layer: list one replay's kernels")
     ap.add_argument("--cpu", action="store_true", help="moe: also time the CPU restatement")
+    ap.add_argument("--streams", type=int, default=8, help="layer / moe --trace: the prover's streams")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("perfcases needs a CUDA device")
