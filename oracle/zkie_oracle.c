@@ -23,28 +23,33 @@ typedef unsigned __int128 u128;
  * Semantics of p3-goldilocks `Goldilocks` (re-exported at
  * crates/zkie-core/src/common/field.rs:10-14).
  * ========================================================================== */
+/* a + b and a - b of canonical inputs, canonical; the conditions are masks,
+ * not branches (they are coin flips on random data). */
 uint64_t orc_add(uint64_t a, uint64_t b)
 {
     uint64_t s = a + b;
-    if (s < a) return s + EPS;          /* wrapped: +2^64 == +EPS, result < p */
-    return s >= ORC_P ? s - ORC_P : s;
+    const uint64_t wrapped = 0 - (uint64_t)(s < a); /* +2^64 == +EPS, result < p */
+    s += EPS & wrapped;
+    return s - (ORC_P & ~wrapped & (0 - (uint64_t)(s >= ORC_P)));
 }
 
 uint64_t orc_sub(uint64_t a, uint64_t b)
 {
-    return a >= b ? a - b : a - b + ORC_P;
+    return a - b + (ORC_P & (0 - (uint64_t)(a < b)));
 }
 
-static uint64_t reduce128(u128 x)
+/* x mod p for any 128-bit x: 2^64 = EPS and 2^96 = -1 (mod p).  Written
+ * without data-dependent branches (the conditions become masks). */
+static inline uint64_t reduce128(u128 x)
 {
     uint64_t lo = (uint64_t)x, hi = (uint64_t)(x >> 64);
     uint64_t hh = hi >> 32, hl = hi & 0xFFFFFFFFULL;
     uint64_t t0 = lo - hh;
-    if (lo < hh) t0 -= EPS;
+    t0 -= EPS & (0 - (uint64_t)(lo < hh));
     uint64_t t1 = hl * EPS;
     uint64_t t2 = t0 + t1;
-    if (t2 < t1) t2 += EPS;
-    return t2 >= ORC_P ? t2 - ORC_P : t2;
+    t2 += EPS & (0 - (uint64_t)(t2 < t1));
+    return t2 - (ORC_P & (0 - (uint64_t)(t2 >= ORC_P)));
 }
 
 uint64_t orc_mul(uint64_t a, uint64_t b) { return reduce128((u128)a * b); }
@@ -248,23 +253,36 @@ static uint32_t bitrev(uint32_t x, uint32_t bits)
     return r;
 }
 
-static void dft_column(uint64_t *v, uint32_t lg)
+/* tw = the twiddles of every stage, stage s (half = 2^(s-1)) at offset
+ * half - 1: w_{2^s}^j for j < half (2^lg - 1 values in all). */
+static uint64_t *dft_twiddles(uint32_t lg)
+{
+    uint64_t *tw = (uint64_t *)malloc(sizeof(uint64_t) * ((1ULL << lg) > 1 ? (1ULL << lg) : 2));
+    for (uint32_t s = 1; s <= lg; s++) {
+        uint64_t half = 1ULL << (s - 1), root = orc_two_adic_generator(s);
+        uint64_t *t = tw + half - 1;
+        t[0] = 1;
+        for (uint64_t j = 1; j < half; j++) t[j] = orc_mul(t[j - 1], root);
+    }
+    return tw;
+}
+
+/* Radix-2 decimation in time on one column, natural order in and out; rev
+ * = the bit-reversal permutation of lg bits. */
+static void dft_column(uint64_t *v, uint32_t lg, const uint64_t *tw_all, const uint32_t *rev)
 {
     uint64_t n = 1ULL << lg;
     for (uint64_t i = 0; i < n; i++) {
-        uint64_t j = bitrev((uint32_t)i, lg);
+        uint64_t j = rev[i];
         if (j > i) {
             uint64_t t = v[i];
             v[i] = v[j];
             v[j] = t;
         }
     }
-    uint64_t *tw = (uint64_t *)malloc(sizeof(uint64_t) * (n / 2 + 1));
     for (uint32_t s = 1; s <= lg; s++) {
         uint64_t half = 1ULL << (s - 1);
-        uint64_t root = orc_two_adic_generator(s);
-        tw[0] = 1;
-        for (uint64_t j = 1; j < half; j++) tw[j] = orc_mul(tw[j - 1], root);
+        const uint64_t *tw = tw_all + half - 1;
         for (uint64_t base = 0; base < n; base += 2 * half)
             for (uint64_t j = 0; j < half; j++) {
                 uint64_t u = v[base + j];
@@ -273,9 +291,12 @@ static void dft_column(uint64_t *v, uint32_t lg)
                 v[base + j + half] = orc_sub(u, x);
             }
     }
-    free(tw);
 }
 
+/* Columns go through in blocks of eight (one 64-byte line of a row holds a
+ * block's values), each gathered into contiguous buffers, transformed and
+ * scattered back; the twiddles are built once. */
+#define DFT_BLOCK 8
 void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w)
 {
     if (lg_h == 0 || w == 0) {
@@ -283,17 +304,26 @@ void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w)
         return;
     }
     uint64_t h = 1ULL << lg_h;
+    uint64_t *tw = dft_twiddles(lg_h);
+    uint32_t *rev = (uint32_t *)malloc(sizeof(uint32_t) * h);
+    for (uint64_t i = 0; i < h; i++) rev[i] = bitrev((uint32_t)i, lg_h);
+    int64_t blocks = (int64_t)((w + DFT_BLOCK - 1) / DFT_BLOCK);
 #pragma omp parallel
     {
-        uint64_t *col = (uint64_t *)malloc(sizeof(uint64_t) * h);
+        uint64_t *col = (uint64_t *)malloc(sizeof(uint64_t) * h * DFT_BLOCK);
 #pragma omp for schedule(dynamic, 1)
-        for (int64_t c = 0; c < (int64_t)w; c++) {
-            for (uint64_t i = 0; i < h; i++) col[i] = canon(mat[i * w + c]);
-            dft_column(col, lg_h);
-            for (uint64_t i = 0; i < h; i++) mat[i * w + c] = col[i];
+        for (int64_t blk = 0; blk < blocks; blk++) {
+            uint64_t c0 = (uint64_t)blk * DFT_BLOCK, nc = w - c0 < DFT_BLOCK ? w - c0 : DFT_BLOCK;
+            for (uint64_t i = 0; i < h; i++)
+                for (uint64_t c = 0; c < nc; c++) col[c * h + i] = canon(mat[i * w + c0 + c]);
+            for (uint64_t c = 0; c < nc; c++) dft_column(col + c * h, lg_h, tw, rev);
+            for (uint64_t i = 0; i < h; i++)
+                for (uint64_t c = 0; c < nc; c++) mat[i * w + c0 + c] = col[c * h + i];
         }
         free(col);
     }
+    free(tw);
+    free(rev);
 }
 
 void orc_dft_naive(const uint64_t *in, uint64_t *out, uint32_t lg_h, uint64_t w)
@@ -340,26 +370,27 @@ static uint64_t sbox7(uint64_t x)
     return orc_mul(x3, x4);
 }
 
-/* [2 3 1 1; 1 2 3 1; 1 1 2 3; 3 1 1 2] (poseidon2_merkle.cu:61-76). */
-static void mat4(uint64_t *x)
+/* [2 3 1 1; 1 2 3 1; 1 1 2 3; 3 1 1 2] (poseidon2_merkle.cu:61-76) on one
+ * 4-lane block of canonical inputs, unreduced: each output is a sum of seven
+ * inputs, below 7 p < 2^67, so the sums run in 128 bits. */
+static inline void mat4_acc(const uint64_t *x, u128 *y)
 {
-    uint64_t a = x[0], b = x[1], c = x[2], d = x[3];
-    uint64_t two_a = orc_add(a, a), two_b = orc_add(b, b), two_c = orc_add(c, c),
-             two_d = orc_add(d, d);
-    x[0] = orc_add(orc_add(two_a, orc_add(two_b, b)), orc_add(c, d));
-    x[1] = orc_add(orc_add(a, two_b), orc_add(orc_add(two_c, c), d));
-    x[2] = orc_add(orc_add(a, b), orc_add(two_c, orc_add(two_d, d)));
-    x[3] = orc_add(orc_add(orc_add(two_a, a), b), orc_add(c, two_d));
+    u128 a = x[0], b = x[1], c = x[2], d = x[3];
+    y[0] = 2 * a + 3 * b + c + d;
+    y[1] = a + 2 * b + 3 * c + d;
+    y[2] = a + b + 2 * c + 3 * d;
+    y[3] = 3 * a + b + c + 2 * d;
 }
 
-/* mds_light16 (poseidon2_merkle.cu:78-97). */
+/* mds_light16 (poseidon2_merkle.cu:78-97): the 4x4 block on each chunk, then
+ * the per-residue column sums added; one reduction per output. */
 static void mds_light16(uint64_t *st)
 {
-    for (int j = 0; j < 16; j += 4) mat4(st + j);
-    uint64_t sums[4] = {0, 0, 0, 0};
-    for (int j = 0; j < 16; j += 4)
-        for (int k = 0; k < 4; k++) sums[k] = orc_add(sums[k], st[j + k]);
-    for (int i = 0; i < 16; i++) st[i] = orc_add(st[i], sums[i & 3]);
+    u128 y[16];
+    for (int j = 0; j < 16; j += 4) mat4_acc(st + j, y + j);
+    u128 sums[4];
+    for (int k = 0; k < 4; k++) sums[k] = y[k] + y[4 + k] + y[8 + k] + y[12 + k];
+    for (int i = 0; i < 16; i++) st[i] = reduce128(y[i] + sums[i & 3]);
 }
 
 /* Internal diagonal V (matrix 1 + diag(V)), poseidon2_merkle.cu:111-142:
@@ -389,9 +420,11 @@ void orc_p2_permute(const orc_p2_consts *c, uint64_t st[16])
     }
     for (int r = 0; r < 22; r++) {
         st[0] = sbox7(orc_add(st[0], c->internal[r]));
-        uint64_t sum = 0;
-        for (int i = 0; i < 16; i++) sum = orc_add(sum, st[i]);
-        for (int i = 0; i < 16; i++) st[i] = orc_add(sum, orc_mul(V[i], st[i]));
+        u128 acc = 0;
+        for (int i = 0; i < 16; i++) acc += st[i];
+        const uint64_t sum = reduce128(acc);
+        /* sum + V_i st_i, reduced once (the product and the sum in 128 bits) */
+        for (int i = 0; i < 16; i++) st[i] = reduce128((u128)V[i] * st[i] + sum);
     }
     for (int r = 0; r < 4; r++) {
         for (int i = 0; i < 16; i++) st[i] = sbox7(orc_add(st[i], c->ext_final[r][i]));
