@@ -125,7 +125,14 @@ def cpu_commit_rate(lg_rows, w, lg_b, seed=7):
 def cpu_sample_rows(w, lg_b, target_s):
     rate, _ = cpu_commit_rate(8, w, lg_b)
     rows = max(1, int(target_s * rate * 1e6 / w))
-    return min(max(8, rows.bit_length() - 1), 18)
+    return min(max(8, rows.bit_length() - 1), 19)
+
+
+def cpu_lanes():
+    """SIMD lanes of the oracle's packed field loops on this host (8 with
+    AVX-512F, 4 with AVX2, 0 scalar)."""
+    from oracle import oracle as orc
+    return orc.set_lanes(-1)
 
 
 def cpu_baseline(w, lg_b, target_s=10.0):
@@ -133,7 +140,7 @@ def cpu_baseline(w, lg_b, target_s=10.0):
     rate, dt = cpu_commit_rate(lg_rows, w, lg_b)
     return {"value": round(rate, 3), "unit": UNIT, "cores": host_threads(), "kind": "port", "label": CPU_LABEL,
             "sample": f"oracle/zkie_oracle.c LDE + Merkle of {w} polys x 2^{lg_rows} coeffs (blowup {1 << lg_b}), "
-                      f"OpenMP over {host_threads()} host threads, {dt:.1f} s"}
+                      f"OpenMP over {host_threads()} host threads, {cpu_lanes()} SIMD lanes per field op, {dt:.1f} s"}
 
 
 def run_reference(args):
@@ -157,7 +164,8 @@ def run_reference(args):
         "data": "synthetic", "impl": "reference", "config": cfg,
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": host_threads(), "kind": "port", "label": CPU_LABEL,
                          "sample": f"{args.polys} polys x 2^{lg_rows} coeffs per step (bounded sample of the "
-                                   f"workload), oracle/zkie_oracle.c on all host threads"},
+                                   f"workload), oracle/zkie_oracle.c on all host threads, {cpu_lanes()} SIMD "
+                                   f"lanes per field op"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -18,8 +18,8 @@ OUT = os.path.join(HERE, "liboracle.so")
 
 def build(force: bool = False) -> str:
     if (not force and os.path.exists(OUT)
-            and os.path.getmtime(OUT) >= max(os.path.getmtime(SRC),
-                                             os.path.getmtime(os.path.join(HERE, "zkie_oracle.h")))):
+            and os.path.getmtime(OUT) >= max(os.path.getmtime(os.path.join(HERE, f))
+                                             for f in ("zkie_oracle.c", "zkie_oracle.h", "packed_field.h"))):
         return OUT
     # -fno-semantic-interposition: the exported field primitives (orc_add,
     # orc_mul, ...) are inlined into the library's own loops instead of being

@@ -67,6 +67,7 @@ def lib():
             "orc_p2_permute": (None, [C.POINTER(P2Consts), _pu64]),
             "orc_p2_hash_row": (None, [C.POINTER(P2Consts), _pu64, _u64, _pu64]),
             "orc_p2_compress": (None, [C.POINTER(P2Consts), _pu64, _pu64, _pu64]),
+            "orc_set_lanes": (C.c_int, [C.c_int]),
             "orc_padded_len": (_u64, [_u64, _u64]),
             "orc_merkle_num_layers": (_u32, [_u64]),
             "orc_merkle_total_digests": (_u64, [_u64]),
@@ -276,6 +277,12 @@ def p2_compress(consts, left, right):
     out = np.zeros(8, dtype=np.uint64)
     lib().orc_p2_compress(C.byref(consts), ptr(u64(left)), ptr(u64(right)), ptr(out))
     return out
+
+
+def set_lanes(lanes=-1):
+    """SIMD lanes of the packed DFT and Merkle loops (8 AVX-512F, 4 AVX2, 0
+    scalar only; -1 the widest the CPU has); returns the lanes now in use."""
+    return int(lib().orc_set_lanes(int(lanes)))
 
 
 def padded_len(raw, n=2): return lib().orc_padded_len(raw, n)

@@ -11,6 +11,9 @@
 
 #include <stdlib.h>
 #include <string.h>
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -239,6 +242,71 @@ uint64_t orc_transcript_field(orc_transcript *t)
 uint64_t orc_transcript_next_u64(orc_transcript *t) { return transcript_draw(t); }
 
 /* ============================================================================
+ * Packed lanes (oracle/packed_field.h): the DFT runs blocks of adjacent
+ * columns and the Merkle loops groups of rows / pairs one per SIMD lane, the
+ * lane count chosen once per process from what the CPU offers (8 with
+ * AVX-512F, 4 with AVX2, else 0: the scalar forms), the remainder through
+ * the scalar forms.
+ * ========================================================================== */
+#if defined(__x86_64__) && defined(__GNUC__)
+#define PW 8
+#define PTGT __attribute__((target("avx512f")))
+#define PMUL32(a, b) ((pv_x8)_mm512_mul_epu32((__m512i)(a), (__m512i)(b)))
+#define PSUF _x8
+#define PADD_IF_LT(x, a, b, c) \
+    ((pv_x8)_mm512_mask_add_epi64((__m512i)(x), _mm512_cmplt_epu64_mask((__m512i)(a), (__m512i)(b)), \
+                                  (__m512i)(x), (__m512i)(c)))
+#define PSUB_IF_LT(x, a, b, c) \
+    ((pv_x8)_mm512_mask_sub_epi64((__m512i)(x), _mm512_cmplt_epu64_mask((__m512i)(a), (__m512i)(b)), \
+                                  (__m512i)(x), (__m512i)(c)))
+#define PSUB_IF_GE(x, a, b, c) \
+    ((pv_x8)_mm512_mask_sub_epi64((__m512i)(x), _mm512_cmpge_epu64_mask((__m512i)(a), (__m512i)(b)), \
+                                  (__m512i)(x), (__m512i)(c)))
+#include "packed_field.h"
+#undef PW
+#undef PTGT
+#undef PMUL32
+#undef PSUF
+#undef PADD_IF_LT
+#undef PSUB_IF_LT
+#undef PSUB_IF_GE
+
+#define PW 4
+#define PTGT __attribute__((target("avx2")))
+#define PMUL32(a, b) ((pv_x4)_mm256_mul_epu32((__m256i)(a), (__m256i)(b)))
+#define PSUF _x4
+#include "packed_field.h"
+#undef PW
+#undef PTGT
+#undef PMUL32
+#undef PSUF
+#define ORC_HAVE_PACKED 1
+#endif
+
+static int g_lanes; /* 0 = scalar */
+
+static int best_lanes(void)
+{
+#ifdef ORC_HAVE_PACKED
+    __builtin_cpu_init();
+    if (__builtin_cpu_supports("avx512f")) return 8;
+    if (__builtin_cpu_supports("avx2")) return 4;
+#endif
+    return 0;
+}
+
+__attribute__((constructor)) static void init_lanes(void) { g_lanes = best_lanes(); }
+
+int orc_set_lanes(int lanes)
+{
+    const int best = best_lanes();
+    if (lanes < 0 || lanes > best) lanes = best;
+    if (lanes != 0 && lanes != 4 && lanes != 8) lanes = best;
+    g_lanes = lanes;
+    return lanes;
+}
+
+/* ============================================================================
  * DFT.  Contract of p3 `TwoAdicSubgroupDft::dft_batch`, restated at
  * crates/zkie-core/cuda/goldilocks_ntt.cu:1-23: out[i] = sum_j x[j] w^(ij),
  * w = TWO_ADIC_GENERATORS[lg h], natural order in and out, canonical output.
@@ -293,10 +361,29 @@ static void dft_column(uint64_t *v, uint32_t lg, const uint64_t *tw_all, const u
     }
 }
 
-/* Columns go through in blocks of eight (one 64-byte line of a row holds a
- * block's values), each gathered into contiguous buffers, transformed and
- * scattered back; the twiddles are built once. */
+/* Columns go through in blocks: with packed lanes, `lanes` adjacent columns
+ * per block as one vector per row (dft_block, one lane per column); the
+ * columns past the last full block, or all of them without lanes, in blocks
+ * of eight (one 64-byte line of a row holds a block's values), each column
+ * gathered into a contiguous buffer, transformed and scattered back.  The
+ * twiddles and the bit-reversal are built once. */
 #define DFT_BLOCK 8
+static void dft_packed_columns(int lanes, uint64_t *mat, uint64_t w, uint64_t c0, uint32_t lg,
+                               const uint64_t *tw, const uint32_t *rev, void *buf)
+{
+#ifdef ORC_HAVE_PACKED
+    if (lanes == 8) {
+        dft_columns_x8(mat, w, c0, lg, tw, rev, (pv_x8 *)buf);
+        return;
+    }
+    if (lanes == 4) {
+        dft_columns_x4(mat, w, c0, lg, tw, rev, (pv_x4 *)buf);
+        return;
+    }
+#endif
+    (void)lanes, (void)mat, (void)w, (void)c0, (void)lg, (void)tw, (void)rev, (void)buf;
+}
+
 void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w)
 {
     if (lg_h == 0 || w == 0) {
@@ -307,13 +394,23 @@ void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w)
     uint64_t *tw = dft_twiddles(lg_h);
     uint32_t *rev = (uint32_t *)malloc(sizeof(uint32_t) * h);
     for (uint64_t i = 0; i < h; i++) rev[i] = bitrev((uint32_t)i, lg_h);
-    int64_t blocks = (int64_t)((w + DFT_BLOCK - 1) / DFT_BLOCK);
+    const int lanes = g_lanes;
+    const int64_t packed = lanes ? (int64_t)(w / (uint64_t)lanes) : 0;
+    const uint64_t c_rest = (uint64_t)packed * (uint64_t)lanes;
+    int64_t blocks = (int64_t)((w - c_rest + DFT_BLOCK - 1) / DFT_BLOCK);
 #pragma omp parallel
     {
+        if (packed) {
+            void *buf = aligned_alloc(64, 64 * h);
+#pragma omp for schedule(dynamic, 1) nowait
+            for (int64_t blk = 0; blk < packed; blk++)
+                dft_packed_columns(lanes, mat, w, (uint64_t)blk * (uint64_t)lanes, lg_h, tw, rev, buf);
+            free(buf);
+        }
         uint64_t *col = (uint64_t *)malloc(sizeof(uint64_t) * h * DFT_BLOCK);
 #pragma omp for schedule(dynamic, 1)
         for (int64_t blk = 0; blk < blocks; blk++) {
-            uint64_t c0 = (uint64_t)blk * DFT_BLOCK, nc = w - c0 < DFT_BLOCK ? w - c0 : DFT_BLOCK;
+            uint64_t c0 = c_rest + (uint64_t)blk * DFT_BLOCK, nc = w - c0 < DFT_BLOCK ? w - c0 : DFT_BLOCK;
             for (uint64_t i = 0; i < h; i++)
                 for (uint64_t c = 0; c < nc; c++) col[c * h + i] = canon(mat[i * w + c0 + c]);
             for (uint64_t c = 0; c < nc; c++) dft_column(col + c * h, lg_h, tw, rev);
@@ -432,6 +529,46 @@ void orc_p2_permute(const orc_p2_consts *c, uint64_t st[16])
     }
 }
 
+static void p2_diag(const orc_p2_consts *c, uint64_t diag[16])
+{
+    memcpy(diag, V_BASE, sizeof V_BASE);
+    diag[15] = c->diag15;
+}
+
+/* rows [0, h) of a row-major h x w matrix hashed into digests; `lanes`
+ * states per group, the rows past the last full group one by one */
+static void p2_hash_group(int lanes, const orc_p2_consts *c, const uint64_t *diag, const uint64_t *rows,
+                          uint64_t w, uint64_t *digests)
+{
+#ifdef ORC_HAVE_PACKED
+    if (lanes == 8) {
+        p2_hash_rows_x8(c, diag, rows, w, digests);
+        return;
+    }
+    if (lanes == 4) {
+        p2_hash_rows_x4(c, diag, rows, w, digests);
+        return;
+    }
+#endif
+    (void)c, (void)diag, (void)rows, (void)w, (void)digests, (void)lanes;
+}
+
+static void p2_compress_group(int lanes, const orc_p2_consts *c, const uint64_t *diag, const uint64_t *prev,
+                              uint64_t *next)
+{
+#ifdef ORC_HAVE_PACKED
+    if (lanes == 8) {
+        p2_compress_pairs_x8(c, diag, prev, next);
+        return;
+    }
+    if (lanes == 4) {
+        p2_compress_pairs_x4(c, diag, prev, next);
+        return;
+    }
+#endif
+    (void)c, (void)diag, (void)prev, (void)next, (void)lanes;
+}
+
 /* --- round-constant derivation (pcs/merkle_cuda.rs:54-85) ------------------
  * rand 0.10 `SmallRng::seed_from_u64` is restated as xoshiro256++ whose state
  * is filled by SplitMix64 (the published algorithms); p3-goldilocks samples a
@@ -548,14 +685,35 @@ void orc_merkle_leaves(const orc_p2_consts *c, const uint64_t *mat, uint64_t h, 
 {
 #ifdef _OPENMP
     if (threads <= 0) threads = omp_get_max_threads();
-#pragma omp parallel for schedule(static) num_threads(threads)
 #endif
-    for (int64_t r = 0; r < (int64_t)h; r++) orc_p2_hash_row(c, mat + (uint64_t)r * w, w, digests + 8 * r);
+    const int lanes = g_lanes;
+    const uint64_t groups = lanes ? h / (uint64_t)lanes : 0, done = groups * (uint64_t)lanes;
+    uint64_t diag[16];
+    p2_diag(c, diag);
+#ifdef _OPENMP
+#pragma omp parallel num_threads(threads)
+#endif
+    {
+#ifdef _OPENMP
+#pragma omp for schedule(static) nowait
+#endif
+        for (int64_t g = 0; g < (int64_t)groups; g++) {
+            const uint64_t r = (uint64_t)g * (uint64_t)lanes;
+            p2_hash_group(lanes, c, diag, mat + r * w, w, digests + 8 * r);
+        }
+#ifdef _OPENMP
+#pragma omp for schedule(static)
+#endif
+        for (int64_t r = (int64_t)done; r < (int64_t)h; r++)
+            orc_p2_hash_row(c, mat + (uint64_t)r * w, w, digests + 8 * r);
+    }
     (void)threads;
 }
 
 static void build_layers(const orc_p2_consts *c, uint64_t *layers, uint64_t h, uint64_t root[8])
 {
+    uint64_t diag[16];
+    p2_diag(c, diag);
     uint64_t len = orc_padded_len(h, 2);
     for (uint64_t i = h; i < len; i++) memset(layers + 8 * i, 0, 64);
     uint64_t *prev = layers;
@@ -563,9 +721,14 @@ static void build_layers(const orc_p2_consts *c, uint64_t *layers, uint64_t h, u
         uint64_t raw = len / 2, next_len = orc_padded_len(raw, 2);
         uint64_t *next = prev + 8 * len;
         memset(next, 0, 64 * next_len);
-#pragma omp parallel for schedule(static) if (raw > 4096)
-        for (int64_t i = 0; i < (int64_t)raw; i++)
-            orc_p2_compress(c, prev + 16 * i, prev + 16 * i + 8, next + 8 * i);
+        const int lanes = g_lanes;
+        const uint64_t groups = lanes ? raw / (uint64_t)lanes : 0, done = groups * (uint64_t)lanes;
+#pragma omp parallel for schedule(static) if (groups > 512)
+        for (int64_t g = 0; g < (int64_t)groups; g++) {
+            const uint64_t i = (uint64_t)g * (uint64_t)lanes;
+            p2_compress_group(lanes, c, diag, prev + 16 * i, next + 8 * i);
+        }
+        for (uint64_t i = done; i < raw; i++) orc_p2_compress(c, prev + 16 * i, prev + 16 * i + 8, next + 8 * i);
         prev = next;
         len = next_len;
     }

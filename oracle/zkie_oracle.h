@@ -82,6 +82,12 @@ typedef struct {
  * with SmallRng taken as xoshiro256++ seeded through SplitMix64 (UNPINNED). */
 void orc_p2_derive_constants(uint64_t seed, orc_p2_consts *c);
 void orc_p2_permute(const orc_p2_consts *c, uint64_t st[16]);
+/* SIMD lanes of the packed loops (the DFT's column blocks, the Merkle leaf
+ * and tree loops' row / pair groups): 8 (AVX-512F), 4 (AVX2) or 0 (the
+ * scalar forms only).  A request above what the CPU offers, or negative,
+ * selects the widest available; returns the lanes now in use.  Results do
+ * not depend on it. */
+int orc_set_lanes(int lanes);
 /* PaddingFreeSponge<Perm,16,8,8> over one row (poseidon2_merkle.cu:161-184). */
 void orc_p2_hash_row(const orc_p2_consts *c, const uint64_t *row, uint64_t w, uint64_t out[8]);
 /* TruncatedPermutation<Perm,2,8,16> (poseidon2_merkle.cu:212-225). */

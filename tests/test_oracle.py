@@ -117,6 +117,29 @@ def test_dft_batch_matches_naive(orc, lg, w):
         assert [int(x) for x in orc.dft_batch(m)[:, 0]] == pyref.dft(col)
 
 
+@pytest.mark.parametrize("lg,w", [(1, 4), (3, 8), (5, 9), (6, 13), (8, 16), (9, 37), (10, 256)])
+def test_dft_batch_matches_naive_with_packed_columns(orc, lg, w):
+    """Widths that fill the packed column blocks (one SIMD lane per column)
+    and leave ragged columns for the scalar blocks."""
+    rng = orc.XorShift64(300 + lg)
+    m = np.array([[rng.field() for _ in range(w)] for _ in range(1 << lg)], dtype=np.uint64)
+    if lg <= 6:
+        assert np.array_equal(orc.dft_batch(m), orc.dft_naive(m))
+    m[0, 0] = np.uint64(P)                      # non-canonical inputs
+    m[-1, -1] = np.uint64(2 ** 64 - 1)
+    best = orc.set_lanes(-1)
+    try:
+        orc.set_lanes(0)
+        ref = orc.dft_batch(m)
+        for lanes in sorted({4, best} - {0}):
+            if lanes > best:
+                continue
+            assert orc.set_lanes(lanes) == lanes
+            assert np.array_equal(orc.dft_batch(m), ref)
+    finally:
+        orc.set_lanes(best)
+
+
 def test_lde_is_padded_dft(orc):
     rng = orc.XorShift64(9)
     m = np.array([[rng.field() for _ in range(3)] for _ in range(16)], dtype=np.uint64)
@@ -181,6 +204,34 @@ def test_merkle_root_matches_python(orc, consts, h):
     assert [int(x) for x in root] == pyref.merkle_root(rows, cp)
     assert [len(l) for l in layers][0] == pyref.padded_len(h)
     assert np.array_equal(orc.merkle_root_from_leaves(consts, orc.merkle_leaves(consts, np.array(rows, dtype=np.uint64))), root)
+
+
+@pytest.mark.parametrize("h,w", [(1, 8), (7, 3), (8, 0), (8, 8), (9, 9), (17, 16), (33, 1), (64, 256),
+                                 (69, 33), (300, 7)])
+def test_packed_merkle_matches_scalar(orc, consts, h, w):
+    """The SIMD leaf and tree loops (one state per lane, several rows at once)
+    give the scalar permutation's digests on every layer, including a partial
+    sponge tail, non-canonical inputs and rows past the last full group."""
+    rnd = np.random.default_rng(1000 * h + w)
+    mat = rnd.integers(0, 2 ** 63, size=(h, w), dtype=np.uint64) * np.uint64(2) + np.uint64(1)
+    if mat.size:
+        mat.flat[0] = np.uint64(P)             # non-canonical: >= p
+        mat.flat[-1] = np.uint64(2 ** 64 - 1)
+    best = orc.set_lanes(-1)
+    try:
+        orc.set_lanes(0)
+        ref_layers, ref_root = orc.merkle_tree(consts, mat)
+        ref_leaves = orc.merkle_leaves(consts, mat, threads=1)
+        for lanes in sorted({4, best} - {0}):
+            if lanes > best:
+                continue
+            assert orc.set_lanes(lanes) == lanes
+            layers, root = orc.merkle_tree(consts, mat)
+            assert np.array_equal(root, ref_root)
+            assert all(np.array_equal(a, b) for a, b in zip(layers, ref_layers))
+            assert np.array_equal(orc.merkle_leaves(consts, mat, threads=1), ref_leaves)
+    finally:
+        orc.set_lanes(best)
 
 
 def test_padded_len(orc):
