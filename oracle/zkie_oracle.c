@@ -407,7 +407,7 @@ void orc_dft_batch(uint64_t *mat, uint32_t lg_h, uint64_t w)
                 dft_packed_columns(lanes, mat, w, (uint64_t)blk * (uint64_t)lanes, lg_h, tw, rev, buf);
             free(buf);
         }
-        uint64_t *col = (uint64_t *)malloc(sizeof(uint64_t) * h * DFT_BLOCK);
+        uint64_t *col = blocks ? (uint64_t *)malloc(sizeof(uint64_t) * h * DFT_BLOCK) : NULL;
 #pragma omp for schedule(dynamic, 1)
         for (int64_t blk = 0; blk < blocks; blk++) {
             uint64_t c0 = c_rest + (uint64_t)blk * DFT_BLOCK, nc = w - c0 < DFT_BLOCK ? w - c0 : DFT_BLOCK;
