@@ -123,7 +123,9 @@ def cpu_commit_rate(lg_rows, w, lg_b, seed=7):
 
 
 def cpu_sample_rows(w, lg_b, target_s):
-    rate, _ = cpu_commit_rate(8, w, lg_b)
+    """Sample height (log2) for about target_s seconds, from the rate of a
+    2^12-row probe (large enough that the per-call setup does not set it)."""
+    rate, _ = cpu_commit_rate(12, w, lg_b)
     rows = max(1, int(target_s * rate * 1e6 / w))
     return min(max(8, rows.bit_length() - 1), 19)
 
