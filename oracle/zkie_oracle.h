@@ -10,15 +10,19 @@
  * the trustless-ai/zkIE project root).  All arithmetic is exact over the
  * Goldilocks field p = 2^64 - 2^32 + 1; values are kept canonical (< p).
  *
- * Parity status: the reference cannot be compiled in this environment (Rust
- * toolchain absent; its CUDA files need sppark headers that are absent), and
- * its tests hold no golden roots, digests or proof bytes.  The H2 restatement
- * (MLE / sumcheck / matmul / transcript) follows the reference source line by
- * line and is checked against the reference's own property tests, replayed
- * with the same seeds.  The H1 restatement (NTT + Poseidon2 Merkle) follows the
- * reference kernels; its constants (Poseidon2 round constants, internal
- * diagonal entry 15) come from third-party crates that are absent here, so
- * Merkle-root parity with the reference CPU path is UNPINNED.
+ * Parity status: the reference's Rust host code cannot be compiled here (no
+ * Rust toolchain), and its tests hold no golden roots, digests or proof
+ * bytes.  The H2 restatement (MLE / sumcheck / matmul / transcript) follows
+ * the reference source line by line and is checked against the reference's
+ * own property tests, replayed with the same seeds.  The H1 restatement (NTT
+ * + Poseidon2 Merkle) follows the reference kernels, and those kernels
+ * themselves are compiled from the reference tree by oracle/build_ref.py
+ * (against a stand-in for the three sppark names they include) so that the
+ * GPU tests compare the product with the reference's own DFT, leaf and
+ * compression code on the same inputs.  What stays unpinned is the constants
+ * both sides are given (Poseidon2 round constants from rand's SmallRng,
+ * internal diagonal entry 15), which come from third-party crates absent
+ * here: Merkle-root parity with the reference CPU path rests on them.
  */
 #ifndef ZKIE_ORACLE_H
 #define ZKIE_ORACLE_H
