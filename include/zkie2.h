@@ -587,7 +587,8 @@ int zkie2_perm_num_den(const uint64_t *d_v, uint64_t len, uint64_t total, uint64
 /* gather_forward (gather.rs:36-52): out[t] (h values) = the field sum over
  * the positions routed to t of weighted[pos] gate[pos]; s positions, m
  * tokens; scratch zkie2_op_gather_scratch_u32(s, m) u32 values.  A token id
- * at or past m sets bit 1 of *d_err. */
+ * at or past m sets bit 1 of *d_err.  s and m must be below 2^32 (the
+ * offsets are u32): larger sizes return cudaErrorInvalidValue. */
 uint64_t zkie2_op_gather_scratch_u32(uint64_t s, uint64_t m);
 int zkie2_op_gather(const uint64_t *d_weighted, const uint32_t *d_token_id, const uint64_t *d_gate, uint64_t s,
                     uint64_t m, uint64_t h, uint64_t *d_out, uint32_t *d_scratch_u32, uint32_t *d_err,

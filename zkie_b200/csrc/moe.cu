@@ -577,6 +577,8 @@ uint64_t zkie2_op_gather_scratch_u32(uint64_t s, uint64_t m) { return 3 * m + 1 
 int zkie2_op_gather(const uint64_t* d_weighted, const uint32_t* d_token_id, const uint64_t* d_gate, uint64_t s,
                     uint64_t m, uint64_t h, uint64_t* d_out, uint32_t* d_scratch_u32, uint32_t* d_err,
                     cudaStream_t stream) {
+    // the per-token offsets and the position lists are u32: s and m below 2^32
+    if (s >= (1ull << 32) || m >= (1ull << 32) - 1) return (int)cudaErrorInvalidValue;
     if (m == 0 || h == 0) return 0;
     if (!d_out || !d_scratch_u32 || !d_err || (s && (!d_weighted || !d_token_id || !d_gate)))
         return (int)cudaErrorInvalidValue;
