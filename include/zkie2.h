@@ -564,7 +564,9 @@ int zkie2_op_rope_columns(const uint64_t *d_x, const uint64_t *d_out, uint64_t n
                           const uint64_t *d_sin, uint64_t m, uint64_t d, uint32_t shift, uint64_t *const *d_cols,
                           zkie_stream_t stream);
 /* Ones of the m x n one-hot sel (field value 1) per token row (by_token, m
- * counts) or per expert column (n counts), u32. */
+ * counts) or per expert column (n counts), u32.  Here and in the two scatter
+ * entries below, m and n must be below 2^32 (ids and counts are u32): larger
+ * sizes return cudaErrorInvalidValue. */
 int zkie2_op_sel_counts(const uint64_t *d_sel, uint64_t m, uint64_t n, uint32_t by_token, uint32_t *d_cnt,
                         zkie_stream_t stream);
 /* scatter_forward (scatter.rs:12-25): for each expert in order, the tokens

@@ -113,15 +113,21 @@ def test_scratch_queries(zk):
     assert L.zkie2_matmul_fixed_scratch_elems(16, 65535 * 32, 16) > 1
 
 
-def test_gather_rejects_sizes_past_u32(zk):
-    """zkie2_op_gather keeps per-token offsets and position lists in u32, so
-    it refuses s or m of 2^32 and more before touching the device (the
-    pointers here are never dereferenced)."""
+def test_moe_index_entries_reject_sizes_past_u32(zk):
+    """zkie2_op_gather keeps per-token offsets and position lists in u32, and
+    the scatter entries u32 token / expert ids and counts, so they refuse
+    sizes of 2^32 and more before touching the device (the pointers here are
+    never dereferenced)."""
     invalid = 1  # cudaErrorInvalidValue
     fake = 0x1000
     L = zk.lib
     assert L.zkie2_op_gather(fake, fake, fake, 1 << 32, 4, 8, fake, fake, fake, None) == invalid
     assert L.zkie2_op_gather(fake, fake, fake, 4, (1 << 32) - 1, 8, fake, fake, fake, None) == invalid
+    # the scatter entries' token / expert ids and counts are u32 as well
+    assert L.zkie2_op_sel_counts(fake, 1 << 32, 4, 1, fake, None) == invalid
+    assert L.zkie2_op_scatter(fake, 4, 1 << 32, fake, fake, fake, fake, None) == invalid
+    assert L.zkie2_op_scatter_encodings(fake, 1 << 32, 4, fake, fake, fake, 4, fake, fake, fake, fake,
+                                        None) == invalid
 
 
 def test_device_count_without_gpu(zk):

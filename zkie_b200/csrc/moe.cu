@@ -522,6 +522,8 @@ int zkie2_op_rope_columns(const uint64_t* d_x, const uint64_t* d_out, uint64_t n
 
 int zkie2_op_sel_counts(const uint64_t* d_sel, uint64_t m, uint64_t n, uint32_t by_token, uint32_t* d_cnt,
                         cudaStream_t stream) {
+    // token and expert ids and the per-line counts are u32
+    if (m >= (1ull << 32) || n >= (1ull << 32)) return (int)cudaErrorInvalidValue;
     if (m == 0 || n == 0) return 0;
     if (!d_sel || !d_cnt) return (int)cudaErrorInvalidValue;
     if (by_token)
@@ -534,6 +536,8 @@ int zkie2_op_sel_counts(const uint64_t* d_sel, uint64_t m, uint64_t n, uint32_t 
 
 int zkie2_op_scatter(const uint64_t* d_sel, uint64_t m, uint64_t n, const uint32_t* d_expert_cnt,
                      uint32_t* d_token_id, uint32_t* d_expert_of, uint64_t* d_scratch, cudaStream_t stream) {
+    // token and expert ids and the per-line counts are u32
+    if (m >= (1ull << 32) || n >= (1ull << 32)) return (int)cudaErrorInvalidValue;
     if (m == 0 || n == 0) return 0;
     if (!d_sel || !d_expert_cnt || !d_token_id || !d_expert_of || !d_scratch) return (int)cudaErrorInvalidValue;
     k_line_offsets<<<1, 32, 0, stream>>>(d_expert_cnt, n, d_scratch, 0, nullptr);
@@ -547,6 +551,8 @@ int zkie2_op_scatter(const uint64_t* d_sel, uint64_t m, uint64_t n, const uint32
 int zkie2_op_scatter_encodings(const uint64_t* d_sel, uint64_t m, uint64_t n, const uint32_t* d_token_cnt,
                                const uint32_t* d_token_id, const uint32_t* d_expert_of, uint64_t s, uint64_t* d_a,
                                uint64_t* d_b, uint64_t* d_scratch, uint32_t* d_err, cudaStream_t stream) {
+    // token and expert ids and the per-line counts are u32
+    if (m >= (1ull << 32) || n >= (1ull << 32)) return (int)cudaErrorInvalidValue;
     if (m == 0 || n == 0) return 0;
     if (!d_sel || !d_token_cnt || !d_a || !d_b || !d_scratch || !d_err || (s && (!d_token_id || !d_expert_of)))
         return (int)cudaErrorInvalidValue;
